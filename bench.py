@@ -1,0 +1,353 @@
+"""Benchmark: MTP-verified decode tok/s (bs=1) on the 43-layer DeepSeek-V4-Flash
+shaped model's MoE path, plus the FP4 MoE layer's HBM roofline fraction.
+
+One step = one iteration of generate()'s MTP loop (engine.py:2809-2922): the
+main T=1 forward through 43 MoE layers, the M=2 MTP draft, the fused T=3
+verify forward through 43 MoE layers, lm_head and greedy acceptance. Weights
+are random-init in the reference's formats (FP4 e2m1 + UE8M0 routed experts,
+FP8 e4m3 shared experts, bf16 router/embed/head), all resident in HBM.
+Attention/MHC are the reference's PyTorch path and are not part of this
+build's step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0). N > 1 (torchrun) runs one full replica per GPU
+(the MoE path is replicated per sequence; value = all ranks' tokens / max
+time over ranks).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "MTP-verified decode tok/s (bs=1); FP4 MoE layer HBM TB/s vs ~8 TB/s peak"
+UNIT = "tok/s"
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_from_profile():
+    """dram bytes per MoE FFN call from the committed ncu summary, if any."""
+    f = REPO / "profiles" / "moe_ffn_cfg0_t3.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_call:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        if not self.out:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU
+def cpu_sample(threads: int | None = None):
+    """The reference algorithm's CPU path (oracle port of fused_moe.py:458-551 +
+    the FP8 shared expert + router), timed on a bounded sample: one T=3 verify
+    MoE layer and one T=1 decode MoE layer at config-0 shapes, plus one lm_head
+    GEMV. Returns (tok_per_s, detail)."""
+    import torch
+    from oracle import inputs as I
+    from oracle import moe as O
+    n = threads or os.cpu_count() or 1
+    torch.set_num_threads(n)
+    shape = I.CONFIG0
+    gate, bias = I.router_weights(256, 4096, seed=1)
+    sh = I.shared_fp8(4096, 2048, seed=2)
+    load = I.make_loader(shape)
+    h3, h1 = I.hidden(3, 4096, seed=0), I.hidden(1, 4096, seed=5)
+    i3, w3 = O.router(h3, gate, bias)
+    i1, w1 = O.router(h1, gate, bias)
+    for e in set(i3.flatten().tolist()) | set(i1.flatten().tolist()):
+        load(int(e))  # generate the sample's weights outside the timed region
+    head = (torch.randn(129280, 4096) * 0.02).to(torch.bfloat16)
+    t0 = time.perf_counter()
+    O.moe_layer(h3, i3, w3, load, sh)
+    t1 = time.perf_counter()
+    O.router(h1, gate, bias)
+    O.moe_layer(h1, i1, w1, load, sh)
+    t2 = time.perf_counter()
+    _ = h1 @ head.t()
+    t3 = time.perf_counter()
+    t_verify, t_main, t_head = t1 - t0, t2 - t1, t3 - t2
+    L = 43
+    t_iter = L * (t_main + t_verify) + 2 * t_main + 4 * t_head
+    return 1.0 / t_iter, {"t_layer_T3_s": t_verify, "t_layer_T1_s": t_main, "t_lm_head_s": t_head, "cores": n,
+                          "t_iter_s": t_iter}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    for _ in range(args.warmup):
+        cpu_sample()
+    vals, det = [], None
+    for _ in range(args.steps):
+        v, det = cpu_sample()
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * det["t_iter_s"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config1 MTP iteration, MoE path, extrapolated from one T=3 + one T=1 MoE layer "
+                               "and one lm_head GEMV per step", "model": "DeepSeek-V4-Flash-shape 43L",
+                   "global_batch": 1, "seq_len": 3, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": det["cores"], "kind": "port",
+                         "sample": "per step: 1 verify MoE layer (T=3) + 1 decode MoE layer (T=1) + 1 lm_head "
+                                   "GEMV at config-0 shapes; x43 layers + 2 draft layers + 4 heads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU
+def moe_roofline(model, reps: int = 43):
+    """Time hs_moe_ffn_fp4 at T=3 (the verify shape) over distinct layers with
+    CUDA events on the launching stream; algorithmic bytes per call are the
+    touched experts' FP4 bytes + the FP8 shared expert + activations."""
+    import torch
+    from home_seek_b200 import ops
+    s = model.shape
+    dev = model.device
+    g = torch.Generator(device=dev)
+    g.manual_seed(123)
+    L = s.num_layers
+    calls = []
+    for l in range(s.hash_layers, L):
+        h = (torch.randn(3, s.hidden, generator=g, device=dev)).to(torch.bfloat16)
+        lw = model.store.layers[l]
+        idx, w = ops.router_topk(h, lw.gate, lw.bias, s.top_k, s.routed_scaling)
+        calls.append((l, h, idx, w))
+    uniq = [len(set(c[2].flatten().tolist())) for c in calls]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in calls]
+    for _ in range(2):
+        for (l, h, idx, w) in calls:
+            ops.moe_ffn(model.store.desc(l), model.store.dims, h, idx, w, use_shared=True)
+    torch.cuda.synchronize()
+    for (l, h, idx, w), (a, b) in zip(calls, ev):
+        a.record()
+        ops.moe_ffn(model.store.desc(l), model.store.dims, h, idx, w, use_shared=True)
+        b.record()
+    torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in ev]
+    shared = 3 * s.shared_inter * s.hidden + 3 * (s.shared_inter // 128) * (s.hidden // 128)
+    act = 3 * s.hidden * 2 * 2 + 12 * 3 * 2
+    bytes_ = [u * s.bytes_per_expert + shared + act for u in uniq]
+    gbs = [b / (m * 1e-3) / 1e9 for b, m in zip(bytes_, ms)]
+    return {"avg_ms": statistics.mean(ms), "avg_bytes": statistics.mean(bytes_), "avg_gbs": statistics.mean(gbs),
+            "avg_unique_experts": statistics.mean(uniq)}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from home_seek_b200 import ops
+    from home_seek_b200.mtp import ModelShape, MoEPathModel, MTPDecoder
+    shape = ModelShape(num_layers=args.layers)
+    model = MoEPathModel(shape, device=dev, seed=rank)
+    dec = MTPDecoder(model, max_tokens=(args.steps + args.warmup + 8) * (shape.num_draft + 2))
+    dec.reset(token=1234 + rank)
+    before = ops.launches
+    dec.iteration()  # eager iteration: counts this library's kernels per iteration
+    launches_per_iter = ops.launches - before
+    dec.capture(warmup=1)
+    dec.reset(token=1234 + rank)
+    for _ in range(args.warmup):
+        dec.replay()
+    torch.cuda.synchronize()
+    dec.count.zero_()
+    dec.accepted.zero_()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local if not os.environ.get("CUDA_VISIBLE_DEVICES") else
+                      int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+                      if os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local].isdigit() else local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            dec.replay()
+        end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    tokens = int(dec.count.item())
+    accepted = int(dec.accepted.item())
+    t = torch.tensor([ms, float(tokens)], device=dev, dtype=torch.float64)
+    if world > 1:
+        tmax = t.clone()
+        dist.all_reduce(tmax[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
+        ms, tokens_all = float(tmax[0]), float(t[1])
+    else:
+        tokens_all = float(tokens)
+    value = tokens_all / (ms * 1e-3)
+
+    # e2e through the public loop with host buffers: H2D of the step's input
+    # token, D2H of the produced tokens and their count, every step
+    host_in = torch.empty(1, dtype=torch.int64, pin_memory=True)
+    host_tok = torch.empty(shape.num_draft + 2, dtype=torch.int64, pin_memory=True)
+    host_cnt = torch.empty(1, dtype=torch.int64, pin_memory=True)
+    host_in.fill_(4321 + rank)
+    dec.count.zero_()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_tokens = 0
+    e0.record()
+    for _ in range(args.steps):
+        dec.next_id.copy_(host_in, non_blocking=True)
+        dec.replay()
+        host_tok.copy_(dec.step_tokens, non_blocking=True)
+        host_cnt.copy_(dec.step_count, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        c = int(host_cnt[0])
+        e_tokens += c
+        host_in[0] = host_tok[c - 1]
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    et = torch.tensor([e_ms, float(e_tokens)], device=dev, dtype=torch.float64)
+    if world > 1:
+        emax = et.clone()
+        dist.all_reduce(emax[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(et[1:], op=dist.ReduceOp.SUM)
+        e_ms, e_tokens = float(emax[0]), float(et[1])
+    e2e = {"value": float(e_tokens) / (e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": 8,
+           "d2h_bytes_per_step": 8 * (shape.num_draft + 2) + 8}
+
+    roof = moe_roofline(model) if rank == 0 else None
+    status = ops.check_status(dev)
+    if world > 1:
+        dev_graph = dec.graph
+        dec.graph = None
+        del dev_graph
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    peak, peak_kind = _peaks()
+    achieved = roof["avg_gbs"]
+    cpu_v, cpu_d = cpu_sample() if not args.no_cpu else (None, {"cores": 0})
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config1: MTP decode iteration (main T=1 + M=2 draft + fused T=3 verify + greedy "
+                               "accept) over the 43-layer MoE path, bs=1",
+                   "model": "DeepSeek-V4-Flash-shape 43L+MTP, 256 FP4 experts top-6 + FP8 shared, random init",
+                   "global_batch": 1, "seq_len": 3, "parallelism": f"replica x{world}",
+                   "attention": "not in this build's step (reference PyTorch path)",
+                   "l2": "inputs larger than L2: ~16 GB of distinct expert weights streamed per iteration",
+                   "acceptance_rate": accepted / max(1, args.steps * shape.num_draft), "status_word": status},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": _traffic_from_profile(),
+                     "kernel": "hs_moe_ffn_fp4 at T=3 (plan+gateup+down+finalize launches)",
+                     "peak_kind": peak_kind, "avg_ms": roof["avg_ms"], "avg_bytes": roof["avg_bytes"],
+                     "avg_unique_experts": roof["avg_unique_experts"]},
+        "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_d["cores"], "kind": "port",
+                         "sample": "one T=3 + one T=1 MoE layer and one lm_head GEMV at config-0 shapes, "
+                                   "extrapolated to 43 layers + 2 draft layers + 4 heads"},
+        "e2e": e2e,
+        "gpu_launches": launches_per_iter * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=43)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,407 @@
+// Speculative-decode acceptance over 129280-wide logits, sm_100a.
+//
+// Reference being replaced: the greedy loop inside
+// HomeSeekInferenceEngine._mtp_verify_batched (inference_engine/engine.py:
+// 2485-2497) and the bonus token choice in generate() (engine.py:2908-2913).
+// The reference has no rejection sampling; hs_accept_rejection implements
+// standard speculative sampling (Leviathan et al. 2023, "Fast Inference from
+// Transformers via Speculative Decoding"; Chen et al. 2023).
+//
+// One thread-block cluster of 8 CTAs per sequence: each CTA streams one eighth
+// of every logits row of the sequence (16-byte loads, HBM-bound), reduces in
+// shared memory, and the cluster combines the 8 partial results through
+// distributed shared memory in rank order (deterministic). The only waits are
+// hardware cluster barriers.
+#include <cooperative_groups.h>
+
+#include "hs_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace hs {
+namespace accept {
+
+constexpr int kCluster = 8;
+constexpr int kThreads = 256;
+constexpr int kMaxRows = 16;
+
+// torch.argmax: first maximal index, NaN counts as maximal.
+__device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
+  const bool n1 = isnan(v1), n2 = isnan(v2);
+  if (n1 || n2) {
+    if (n1 && n2) return i1 < i2;
+    return n1;
+  }
+  return v1 > v2 || (v1 == v2 && i1 < i2);
+}
+
+__device__ __forceinline__ void slice_of(int V, int rank, int& lo, int& hi) {
+  const int per = ((V + kCluster * 8 - 1) / (kCluster * 8)) * 8;
+  lo = min(V, rank * per);
+  hi = min(V, lo + per);
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Block-wide arg-max of one row slice [lo, hi). Result valid in thread 0.
+__device__ void block_argmax(const __nv_bfloat16* __restrict__ row, int lo, int hi, float& bv, int& bi) {
+  float v = -INFINITY;
+  int ix = 0x7fffffff;
+  // 8 bf16 per 16-byte load; lo is a multiple of 8 and rows are 16-byte aligned
+  const int nvec = (hi - lo) / 8;
+  const uint4* p = reinterpret_cast<const uint4*>(row + lo);
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    const uint4 q = p[i];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    const int base = lo + 8 * i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16lo(w[j]), b = bf16hi(w[j]);
+      if (better(a, base + 2 * j, v, ix)) {
+        v = a;
+        ix = base + 2 * j;
+      }
+      if (better(b, base + 2 * j + 1, v, ix)) {
+        v = b;
+        ix = base + 2 * j + 1;
+      }
+    }
+  }
+  for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += blockDim.x) {
+    const float a = __bfloat162float(row[k]);
+    if (better(a, k, v, ix)) {
+      v = a;
+      ix = k;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, ix, o);
+    if (better(v2, i2, v, ix)) {
+      v = v2;
+      ix = i2;
+    }
+  }
+  __shared__ float sv[kThreads / 32];
+  __shared__ int si[kThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) {
+    sv[warp] = v;
+    si[warp] = ix;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w2 = 1; w2 < static_cast<int>(blockDim.x / 32); ++w2)
+      if (better(sv[w2], si[w2], v, ix)) {
+        v = sv[w2];
+        ix = si[w2];
+      }
+    bv = v;
+    bi = ix;
+  }
+}
+
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
+    greedy_kernel(const __nv_bfloat16* __restrict__ logits, int T, int V, const int64_t* __restrict__ draft_ids,
+                  int32_t* __restrict__ n_acc, int64_t* __restrict__ next_tok, int64_t* __restrict__ argmax_out) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int b = blockIdx.x / kCluster;
+  __shared__ float pv[kMaxRows];
+  __shared__ int pi[kMaxRows];
+  int lo, hi;
+  slice_of(V, rank, lo, hi);
+  for (int i = 0; i < T; ++i) {
+    float v;
+    int ix;
+    block_argmax(logits + (static_cast<int64_t>(b) * T + i) * V, lo, hi, v, ix);
+    if (threadIdx.x == 0) {
+      pv[i] = v;
+      pi[i] = ix;
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    int am[kMaxRows];
+    for (int i = 0; i < T; ++i) {
+      float v = -INFINITY;
+      int ix = 0x7fffffff;
+      for (int r = 0; r < kCluster; ++r) {
+        const float* rv = cluster.map_shared_rank(pv, r);
+        const int* ri = cluster.map_shared_rank(pi, r);
+        if (ri[i] != 0x7fffffff && better(rv[i], ri[i], v, ix)) {
+          v = rv[i];
+          ix = ri[i];
+        }
+      }
+      am[i] = ix;
+      if (argmax_out) argmax_out[static_cast<int64_t>(b) * T + i] = ix;
+    }
+    int n = 0;
+    while (n < T - 1 && static_cast<int64_t>(am[n]) == draft_ids[static_cast<int64_t>(b) * (T - 1) + n]) ++n;
+    n_acc[b] = n;
+    next_tok[b] = am[n];
+  }
+  cluster.sync();
+}
+
+// ---------------------------------------------------------------------------
+// rejection sampling
+// ---------------------------------------------------------------------------
+struct MS {
+  float m, s;
+};
+
+__device__ __forceinline__ MS ms_combine(MS a, MS b) {
+  if (a.m == -INFINITY) return b;
+  if (b.m == -INFINITY) return a;
+  const float m = fmaxf(a.m, b.m);
+  return MS{m, a.s * expf(a.m - m) + b.s * expf(b.m - m)};
+}
+
+// (max, sum exp(z - max)) of z = x / t over a slice; result valid in thread 0.
+// Each thread keeps a running max and rescales its sum only when the max
+// grows, so every element costs one expf.
+__device__ __forceinline__ void ms_push(MS& a, float z) {
+  if (z == -INFINITY) return;  // exp(-inf) contributes nothing
+  if (z > a.m) {
+    a.s = (a.m == -INFINITY ? 0.f : a.s * expf(a.m - z)) + 1.f;
+    a.m = z;
+  } else {
+    a.s += expf(z - a.m);
+  }
+}
+
+__device__ MS block_ms(const __nv_bfloat16* __restrict__ row, int lo, int hi, float t) {
+  MS acc{-INFINITY, 0.f};
+  const int nvec = (hi - lo) / 8;
+  const uint4* p = reinterpret_cast<const uint4*>(row + lo);
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    const uint4 q = p[i];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      ms_push(acc, bf16lo(w[j]) / t);
+      ms_push(acc, bf16hi(w[j]) / t);
+    }
+  }
+  for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += blockDim.x) ms_push(acc, __bfloat162float(row[k]) / t);
+  for (int o = 16; o > 0; o >>= 1) {
+    MS other{__shfl_xor_sync(0xffffffffu, acc.m, o), __shfl_xor_sync(0xffffffffu, acc.s, o)};
+    acc = ms_combine(acc, other);
+  }
+  __shared__ MS sm[kThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) sm[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int w = 1; w < static_cast<int>(blockDim.x / 32); ++w) acc = ms_combine(acc, sm[w]);
+  return acc;
+}
+
+struct Bcast {
+  int n_acc;
+  int row;       // target row sampled from
+  int residual;  // 1: max(0, p - q), 0: p
+  float mt, st, md, sd;
+};
+
+__device__ __forceinline__ float resid(const __nv_bfloat16* tr, const __nv_bfloat16* dr, int k, float t,
+                                       const Bcast& bc) {
+  const float p = expf(__bfloat162float(tr[k]) / t - bc.mt) / bc.st;
+  if (!bc.residual) return p;
+  const float q = expf(__bfloat162float(dr[k]) / t - bc.md) / bc.sd;
+  return fmaxf(0.f, p - q);
+}
+
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
+    rejection_kernel(const __nv_bfloat16* __restrict__ target, const __nv_bfloat16* __restrict__ draft, int M,
+                     int draft_rows, int V, const int64_t* __restrict__ draft_ids, const float* __restrict__ u,
+                     float t, int32_t* __restrict__ n_acc, int64_t* __restrict__ next_tok, int32_t* status) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int b = blockIdx.x / kCluster;
+  __shared__ MS tms[kMaxRows], dms[kMaxRows];
+  __shared__ float tz[kMaxRows], dz[kMaxRows];  // z at the draft id (if in slice)
+  __shared__ Bcast bc;
+  __shared__ float csum;  // this CTA's slice mass
+  __shared__ int clast;   // last index with positive mass in this slice
+  __shared__ float tsum[kThreads];
+  __shared__ int found;
+  int lo, hi;
+  slice_of(V, rank, lo, hi);
+  const __nv_bfloat16* trow0 = target + static_cast<int64_t>(b) * (M + 1) * V;
+  const __nv_bfloat16* drow0 = draft + static_cast<int64_t>(b) * draft_rows * V;
+
+  for (int i = 0; i <= M; ++i) {
+    const MS r = block_ms(trow0 + static_cast<int64_t>(i) * V, lo, hi, t);
+    if (threadIdx.x == 0) tms[i] = r;
+  }
+  for (int i = 0; i < M; ++i) {
+    const MS r = block_ms(drow0 + static_cast<int64_t>(i) * V, lo, hi, t);
+    if (threadIdx.x == 0) dms[i] = r;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < M; ++i) {
+      const int64_t d = draft_ids[static_cast<int64_t>(b) * M + i];
+      tz[i] = NAN;
+      dz[i] = NAN;
+      if (d >= lo && d < hi) {
+        tz[i] = __bfloat162float(trow0[static_cast<int64_t>(i) * V + d]) / t;
+        dz[i] = __bfloat162float(drow0[static_cast<int64_t>(i) * V + d]) / t;
+      }
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    MS T_[kMaxRows], D_[kMaxRows];
+    float zt[kMaxRows], zd[kMaxRows];
+    for (int i = 0; i <= M; ++i) {
+      T_[i] = MS{-INFINITY, 0.f};
+      D_[i] = MS{-INFINITY, 0.f};
+      zt[i] = NAN;
+      zd[i] = NAN;
+    }
+    for (int r = 0; r < kCluster; ++r) {
+      const MS* rt = cluster.map_shared_rank(tms, r);
+      const MS* rd = cluster.map_shared_rank(dms, r);
+      const float* rtz = cluster.map_shared_rank(tz, r);
+      const float* rdz = cluster.map_shared_rank(dz, r);
+      for (int i = 0; i <= M; ++i) T_[i] = ms_combine(T_[i], rt[i]);
+      for (int i = 0; i < M; ++i) {
+        D_[i] = ms_combine(D_[i], rd[i]);
+        if (!isnan(rtz[i])) {
+          zt[i] = rtz[i];
+          zd[i] = rdz[i];
+        }
+      }
+    }
+    int n = 0;
+    for (; n < M; ++n) {
+      const int64_t d = draft_ids[static_cast<int64_t>(b) * M + n];
+      if (d < 0 || d >= V) {
+        report(status, HS_DEV_BAD_DRAFT);
+        break;
+      }
+      const float p = expf(zt[n] - T_[n].m) / T_[n].s;
+      const float q = expf(zd[n] - D_[n].m) / D_[n].s;
+      const float uu = u[static_cast<int64_t>(b) * (M + 1) + n];
+      if (!(uu < p / q)) break;
+    }
+    bc.n_acc = n;
+    bc.row = n;
+    bc.residual = n < M ? 1 : 0;
+    bc.mt = T_[n].m;
+    bc.st = T_[n].s;
+    bc.md = n < M ? D_[n].m : 0.f;
+    bc.sd = n < M ? D_[n].s : 1.f;
+  }
+  cluster.sync();
+  const Bcast B = *cluster.map_shared_rank(&bc, 0);
+  const __nv_bfloat16* tr = trow0 + static_cast<int64_t>(B.row) * V;
+  const __nv_bfloat16* dr = drow0 + static_cast<int64_t>(B.row < draft_rows ? B.row : 0) * V;
+  // Thread i owns one contiguous chunk of the slice; chunk sums are combined
+  // by thread 0 in thread order, so the CTA total and the exclusive prefixes
+  // come from the same sequence of additions.
+  const int len = hi - lo;
+  const int chunk = (len + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+  const int k0 = min(hi, lo + static_cast<int>(threadIdx.x) * chunk), k1 = min(hi, k0 + chunk);
+  float ts = 0.f;
+  int tl = -1;
+  for (int k = k0; k < k1; ++k) {
+    const float r = resid(tr, dr, k, t, B);
+    ts += r;
+    if (r > 0.f) tl = k;
+  }
+  tsum[threadIdx.x] = ts;
+  for (int o = 16; o > 0; o >>= 1) tl = max(tl, __shfl_xor_sync(0xffffffffu, tl, o));
+  __shared__ int wl[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) wl[threadIdx.x >> 5] = tl;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float x = 0.f;
+    for (int i = 0; i < static_cast<int>(blockDim.x); ++i) {
+      const float y = tsum[i];
+      tsum[i] = x;  // exclusive prefix within the CTA
+      x += y;
+    }
+    csum = x;
+    int m = -1;
+    for (int i = 0; i < static_cast<int>(blockDim.x / 32); ++i) m = max(m, wl[i]);
+    clast = m;
+    found = 0x7fffffff;
+  }
+  cluster.sync();
+  // prefix over the cluster in rank order
+  float pre = 0.f, tot = 0.f;
+  int last = -1;
+  for (int r = 0; r < kCluster; ++r) {
+    const float s = *cluster.map_shared_rank(&csum, r);
+    if (r < rank) pre += s;
+    tot += s;
+    last = max(last, *cluster.map_shared_rank(&clast, r));
+  }
+  const float tau = u[static_cast<int64_t>(b) * (M + 1) + M] * tot;
+  if (tau >= pre && tau < pre + csum) {
+    float x = pre + tsum[threadIdx.x];
+    for (int k = k0; k < k1; ++k) {
+      const float r = resid(tr, dr, k, t, B);
+      x += r;
+      if (r > 0.f && x > tau) {
+        atomicMin(&found, k);
+        break;
+      }
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    int best = 0x7fffffff;
+    for (int r = 0; r < kCluster; ++r) best = min(best, *cluster.map_shared_rank(&found, r));
+    next_tok[b] = best != 0x7fffffff ? best : (last >= 0 ? last : 0);
+    n_acc[b] = B.n_acc;
+  }
+  cluster.sync();
+}
+
+}  // namespace accept
+}  // namespace hs
+
+using namespace hs;
+using namespace hs::accept;
+
+extern "C" int hs_accept_greedy(const void* logits, int64_t B, int64_t T, int64_t V, const int64_t* draft_ids,
+                                int32_t* n_accept, int64_t* next_token, int64_t* argmax_out, int32_t* dev_status,
+                                void* stream) {
+  (void)dev_status;
+  if (B < 0 || T < 1 || T > kMaxRows || V < 64 || (V * 2) % 16 != 0) return HS_ERR_BAD_SHAPE;
+  if (B == 0) return HS_OK;
+  if (B * kCluster > 0x7fffffff) return HS_ERR_BAD_SHAPE;
+  if (!logits || !n_accept || !next_token || (T > 1 && !draft_ids)) return HS_ERR_BAD_ARGUMENT;
+  if (!aligned16(logits)) return HS_ERR_ALIGN;
+  greedy_kernel<<<static_cast<unsigned>(B * kCluster), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(logits), static_cast<int>(T), static_cast<int>(V), draft_ids, n_accept,
+      next_token, argmax_out);
+  return check_launch();
+}
+
+extern "C" int hs_accept_rejection(const void* target_logits, const void* draft_logits, int64_t B, int64_t M,
+                                   int64_t draft_rows, int64_t V, const int64_t* draft_ids, const float* uniform,
+                                   float temperature, int32_t* n_accept, int64_t* next_token, int32_t* dev_status,
+                                   void* stream) {
+  if (B < 0 || M < 0 || M + 1 > kMaxRows || draft_rows < M || V < 64 || (V * 2) % 16 != 0) return HS_ERR_BAD_SHAPE;
+  if (B == 0) return HS_OK;
+  if (!target_logits || !n_accept || !next_token || (M > 0 && (!draft_logits || !draft_ids)))
+    return HS_ERR_BAD_ARGUMENT;
+  if (!(temperature > 0.f))
+    return hs_accept_greedy(target_logits, B, M + 1, V, draft_ids, n_accept, next_token, nullptr, dev_status, stream);
+  if (!uniform) return HS_ERR_BAD_ARGUMENT;
+  if (!aligned16(target_logits) || (draft_logits && !aligned16(draft_logits))) return HS_ERR_ALIGN;
+  rejection_kernel<<<static_cast<unsigned>(B * kCluster), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(target_logits), static_cast<const __nv_bfloat16*>(draft_logits),
+      static_cast<int>(M), static_cast<int>(draft_rows), static_cast<int>(V), draft_ids, uniform, temperature,
+      n_accept, next_token, dev_status);
+  return check_launch();
+}

@@ -1,0 +1,199 @@
+// Shared device helpers for the sm_100a kernels: bounded mbarrier waits,
+// TMA / bulk-copy issue, FP4/FP8 -> f16 conversion, legacy-layout MMA, and
+// bf16 rounding helpers. Everything here is hand-written inline PTX or plain
+// CUDA; no library kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/hs_ext.h"
+
+#define HS_DI __device__ __forceinline__
+
+namespace hs {
+
+// ---------------------------------------------------------------------------
+// Host-side error plumbing
+// ---------------------------------------------------------------------------
+void set_last_cuda_error(int e);
+
+#define HS_CUDA_CHECK(expr)                         \
+  do {                                              \
+    cudaError_t _e = (expr);                        \
+    if (_e != cudaSuccess) {                        \
+      ::hs::set_last_cuda_error(static_cast<int>(_e)); \
+      return HS_ERR_CUDA;                           \
+    }                                               \
+  } while (0)
+
+// Returns HS_ERR_CUDA if the most recent launch on this thread failed.
+int check_launch();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Device: time / status
+// ---------------------------------------------------------------------------
+HS_DI uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+HS_DI void report(int32_t* status, int32_t bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+// Bounded waits give up after this many nanoseconds (about two seconds), after
+// which the kernel reports HS_DEV_TIMEOUT and returns.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ---------------------------------------------------------------------------
+// Device: mbarrier
+// ---------------------------------------------------------------------------
+HS_DI uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+HS_DI void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+HS_DI void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+HS_DI void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+HS_DI void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+HS_DI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete; false after the limit.
+HS_DI bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Device: TMA (tensor) and bulk (1D) copies global -> shared, completing on an
+// mbarrier with transaction bytes. No multicast anywhere in this library.
+// ---------------------------------------------------------------------------
+HS_DI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+HS_DI void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+HS_DI void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Device: shared-memory loads
+// ---------------------------------------------------------------------------
+HS_DI uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+HS_DI uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+HS_DI uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+HS_DI uint32_t lds8(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Device: FP4 (e2m1) and FP8 (e4m3) -> f16x2. Both conversions are exact.
+// e2m1x2: one byte holds two values; the low nibble lands in the low half.
+// e4m3x2: two bytes; the low byte lands in the low half.
+// ---------------------------------------------------------------------------
+HS_DI void e2m1x8_to_f16x2x4(uint32_t w, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}\n"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(w));
+}
+
+HS_DI void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& r0, uint32_t& r1) {
+  asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %2;\n"
+      " cvt.rn.f16x2.e4m3x2 %0, lo;\n cvt.rn.f16x2.e4m3x2 %1, hi;\n}\n"
+      : "=r"(r0), "=r"(r1)
+      : "r"(w));
+}
+
+// ue8m0 -> f32 as torch converts float8_e8m0fnu: 0 -> 2^-127, 255 -> NaN.
+HS_DI float e8m0_to_f32_torch(uint32_t s) {
+  if (s == 0u) return __uint_as_float(0x00400000u);
+  if (s == 255u) return __uint_as_float(0x7fc00000u);
+  return __uint_as_float(s << 23);
+}
+// ue8m0 -> f32 by the bit shift of weight_loader.py:14-19 (0 -> 0, 255 -> inf).
+HS_DI float e8m0_to_f32_shift(uint32_t s) { return __uint_as_float(s << 23); }
+
+// ---------------------------------------------------------------------------
+// Device: legacy warp MMA m16n8k16, f16 inputs, f32 accumulate.
+// ---------------------------------------------------------------------------
+HS_DI void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+HS_DI void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------------------
+// Device: rounding helpers (round-to-nearest-even, like torch's .to(bf16)).
+// ---------------------------------------------------------------------------
+HS_DI float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// 2^e as f32 for e in [-126, 127].
+HS_DI float exp2i(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
+
+}  // namespace hs

@@ -1,0 +1,195 @@
+"""MTP speculative decode (M=2 draft, fused T=3 verify, greedy acceptance) over
+the MoE path of the DeepSeek-V4-Flash-shaped model, with every expert in HBM.
+
+Reference: HomeSeekInferenceEngine.generate's decode loop
+(inference_engine/engine.py:2809-2922), `_mtp_generate_draft`
+(engine.py:2251-2336) and `_mtp_verify_batched` (engine.py:2431-2540).
+
+What runs per layer here is the part of `_forward_layer` this build owns:
+rms_norm -> router (or hash routing for layers < num_hash_layers) -> routed FP4
+experts + FP8 shared expert (one fused kernel sequence) -> residual add.
+Attention and the MHC hyper-connections stay on the reference's PyTorch path
+and are not part of this module; the layer body is therefore
+h <- h + MoE(rms_norm(h)). The draft layer is the MTP block's projections
+(e_proj(enorm(embed(tok))) + h_proj(hnorm(h))) followed by its own MoE.
+
+Everything stays on the device between iterations: the accept/branch logic of
+generate() (append n_acc drafts and the bonus token if n_acc > 0, else keep
+the main-step token) is computed with tensor ops, so one iteration has no host
+synchronisation and is captured as a single CUDA graph.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import ops
+from ._lib import HS_DUP_LAST, HS_DUP_SUM
+from .expert_store import HBMExpertStore
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """utils.py:6-9: f32 RMS norm, cast back."""
+    xf = x.float()
+    var = xf.pow(2).mean(-1, keepdim=True)
+    return (w.float() * (xf * torch.rsqrt(var + eps))).to(x.dtype)
+
+
+@dataclass
+class ModelShape:
+    num_layers: int = 43
+    num_experts: int = 256
+    hidden: int = 4096
+    inter: int = 2048
+    shared_inter: int = 2048
+    vocab: int = 129280
+    top_k: int = 6
+    hash_layers: int = 3
+    routed_scaling: float = 1.5
+    num_draft: int = 2
+
+    @property
+    def bytes_per_expert(self) -> int:
+        return 3 * self.inter * self.hidden // 2 + 3 * self.inter * self.hidden // 32
+
+
+class MoEPathModel:
+    """Random-init weights of the full model shape on one GPU (layers 0..L-1 plus
+    the MTP layer at index L in the same expert store)."""
+
+    def __init__(self, shape: ModelShape, device: str | torch.device = "cuda", seed: int = 0):
+        self.shape = s = shape
+        self.device = dev = torch.device(device)
+        self.store = HBMExpertStore(s.num_layers + 1, s.num_experts, s.hidden, s.inter, s.shared_inter, device=dev,
+                                    with_router=True, hash_layers=s.hash_layers, vocab_size=s.vocab,
+                                    top_k=s.top_k)
+        self.store.fill_random(seed)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed + 17)
+
+        def randn(*shp, std):
+            return (torch.randn(*shp, generator=g, device=dev) * std).to(torch.bfloat16)
+
+        self.embed = randn(s.vocab, s.hidden, std=0.02)
+        self.lm_head = randn(s.vocab, s.hidden, std=0.02)
+        self.norm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
+        self.ln_w = (1.0 + randn(s.num_layers + 1, s.hidden, std=0.02).float()).to(torch.bfloat16)
+        self.e_proj = randn(s.hidden, s.hidden, std=0.02)
+        self.h_proj = randn(s.hidden, s.hidden, std=0.02)
+        self.enorm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
+        self.hnorm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
+        self.mtp_norm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
+        for layer in range(s.num_layers + 1):
+            self.store.desc(layer)  # encode TMA descriptors once
+
+    # --- one MoE layer (the part of _forward_layer / _forward_ffn this build owns)
+    def moe(self, x: torch.Tensor, layer: int, ids: torch.Tensor) -> torch.Tensor:
+        s = self.shape
+        lw = self.store.layers[layer]
+        if layer < s.hash_layers and lw.tid2eid is not None:
+            idx, w = ops.hash_route(ids, lw.tid2eid, s.top_k)
+        else:
+            idx, w = ops.router_topk(x, lw.gate, lw.bias, s.top_k, s.routed_scaling)
+        # T=1 decode follows the reference's M=1 path (duplicates summed,
+        # engine.py:1388-1393); T>1 follows _forward_legacy (last weight wins)
+        dup = HS_DUP_SUM if x.shape[0] == 1 else HS_DUP_LAST
+        return ops.moe_ffn(self.store.desc(layer), self.store.dims, x, idx, w, use_shared=True, dup_mode=dup)
+
+    def layer(self, h: torch.Tensor, layer: int, ids: torch.Tensor) -> torch.Tensor:
+        x = rms_norm(h, self.ln_w[layer])
+        return h + self.moe(x, layer, ids)
+
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        h = self.embed[ids]
+        for layer in range(self.shape.num_layers):
+            h = self.layer(h, layer, ids)
+        return h
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        return rms_norm(h, self.norm_w) @ self.lm_head.t()
+
+    def draft(self, h_last: torch.Tensor, tok: torch.Tensor) -> torch.Tensor:
+        """_mtp_generate_draft at t=0 (engine.py:2251-2336) on the MoE path: M steps."""
+        s = self.shape
+        L = s.num_layers
+        prev = h_last
+        out = []
+        t = tok
+        for _ in range(s.num_draft):
+            e = rms_norm(self.embed[t], self.enorm_w) @ self.e_proj.t()
+            hc = rms_norm(prev, self.hnorm_w) @ self.h_proj.t() + e
+            hm = hc + self.moe(rms_norm(hc, self.ln_w[L]), L, t)
+            lg = rms_norm(hm, self.mtp_norm_w) @ self.lm_head.t()
+            _, t = ops.accept_greedy(lg.view(1, 1, -1), torch.empty(1, 0, dtype=torch.int64, device=lg.device))
+            out.append(t)
+            prev = hm
+        return torch.cat(out)
+
+
+class MTPDecoder:
+    """Device-resident MTP decode loop. state: next_id [1], out buffer of tokens."""
+
+    def __init__(self, model: MoEPathModel, max_tokens: int = 4096):
+        self.m = model
+        dev = model.device
+        M = model.shape.num_draft
+        self.next_id = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.tokens = torch.zeros(max_tokens + M + 2, dtype=torch.int64, device=dev)
+        self.count = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.step_tokens = torch.zeros(M + 2, dtype=torch.int64, device=dev)
+        self.step_count = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.accepted = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self._ar = torch.arange(M + 2, device=dev)
+
+    def iteration(self) -> None:
+        """One generate() iteration: main T=1 step, M-token draft, fused T=1+M verify, accept."""
+        m = self.m
+        M = m.shape.num_draft
+        none = torch.empty(1, 0, dtype=torch.int64, device=self.next_id.device)
+        h = m.forward(self.next_id)                                   # main step, T=1
+        _, main_pred = ops.accept_greedy(m.logits(h).view(1, 1, -1), none)
+        d = m.draft(h, main_pred)                                     # M drafts
+        ids = torch.cat([main_pred, d])                               # combined_ids
+        hv = m.forward(ids)                                           # fused verify, T=1+M
+        n_acc, bonus = ops.accept_greedy(m.logits(hv).view(1, M + 1, -1), d.view(1, M))
+        n = n_acc.to(torch.int64)
+        # tokens of this iteration: main_pred, then d[:n], then bonus if n > 0
+        cand = torch.cat([main_pred, d, bonus])                       # [M + 2]
+        take = torch.where(self._ar <= n, cand, torch.zeros_like(cand))
+        # bonus sits right after the n accepted drafts
+        take = torch.where(self._ar == n + 1, bonus.expand(M + 2), take)
+        cnt = torch.where(n > 0, n + 2, torch.ones_like(n))
+        self.step_tokens.copy_(take)
+        self.step_count.copy_(cnt)
+        pos = self.count + self._ar
+        keep = self._ar < cnt
+        self.tokens.index_put_((pos.clamp(max=self.tokens.numel() - 1),), torch.where(keep, take, self.tokens[
+            pos.clamp(max=self.tokens.numel() - 1)]))
+        self.count.add_(cnt)
+        self.accepted.add_(n)
+        self.next_id.copy_(torch.where(n > 0, bonus, main_pred))
+
+    def capture(self, warmup: int = 1) -> None:
+        s = torch.cuda.Stream(self.next_id.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self.iteration()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.iteration()
+
+    def replay(self) -> None:
+        if self.graph is None:
+            self.iteration()
+        else:
+            self.graph.replay()
+
+    def reset(self, token: int) -> None:
+        self.next_id.fill_(token)
+        self.count.zero_()
+        self.accepted.zero_()

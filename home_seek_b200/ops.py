@@ -1,0 +1,241 @@
+"""Tensor-level wrappers over the C ABI: validate, fetch a workspace, launch on
+the current stream. Every op runs on the GPU through libhs_ext.so; there is
+no CPU fallback (a CPU tensor raises).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import HsError, call
+
+_workspaces: dict = {}
+_status: dict = {}
+
+# Number of this library's kernels each op launches; summed into `launches`
+# so a caller can count the kernels of one decode iteration.
+launches = 0
+_KERNELS = {"hs_router_topk": 2, "hs_hash_route": 1, "hs_moe_ffn_fp4": 4, "hs_moe_permute": 2,
+            "hs_moe_unpermute": 1, "hs_accept_greedy": 1, "hs_accept_rejection": 1, "hs_fill_bytes": 1}
+
+
+def _launch(name: str, *args) -> None:
+    global launches
+    call(name, *args)
+    launches += _KERNELS.get(name, 0)
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _check_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("home_seek_b200 ops need CUDA tensors (there is no CPU path)")
+        if not t.is_contiguous():
+            raise ValueError("home_seek_b200 ops need contiguous tensors")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+def workspace(device: torch.device, nbytes: int, tag: str) -> torch.Tensor:
+    """Grow-only scratch per (device, stream, tag). Calls on one stream are
+    ordered, so reusing the buffer across calls is race-free."""
+    key = (device.index, _stream(device), tag)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Device int32 that kernels OR HS_DEV_* bits into; read with check_status()."""
+    s = _status.get(device.index)
+    if s is None:
+        s = torch.zeros(1, dtype=torch.int32, device=device)
+        _status[device.index] = s
+    return s
+
+
+def check_status(device: torch.device, reset: bool = True) -> int:
+    s = status_word(device)
+    v = int(s.item())
+    if reset and v:
+        s.zero_()
+    return v
+
+
+# --- router / hash -------------------------------------------------------------
+
+def router_topk(hidden: torch.Tensor, gate: torch.Tensor, bias: Optional[torch.Tensor], top_k: int = 6,
+                routed_scaling: float = 1.5, return_logits: bool = False):
+    """compute_expert_affinity_with_bias (router.py:22-36) on the GPU."""
+    dev = _check_cuda(hidden, gate, bias)
+    if hidden.dtype != torch.bfloat16 or gate.dtype != torch.bfloat16:
+        hidden = hidden.to(torch.bfloat16).contiguous()
+        gate = gate.to(torch.bfloat16).contiguous()
+    if bias is not None and bias.dtype != torch.bfloat16:
+        bias = bias.to(torch.bfloat16).contiguous()
+    T, D = hidden.shape
+    E = gate.shape[0]
+    idx = torch.empty(T, top_k, dtype=torch.int64, device=dev)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    lg = torch.empty(T, E, dtype=torch.bfloat16, device=dev) if return_logits else None
+    lib = _lib.load()
+    nb = lib.hs_router_workspace_size(T, D, E)
+    ws = workspace(dev, nb, "router")
+    _launch("hs_router_topk", hidden.data_ptr(), gate.data_ptr(), _ptr(bias), T, D, E, top_k, float(routed_scaling),
+         idx.data_ptr(), w.data_ptr(), _ptr(lg), ws.data_ptr(), ws.numel(), _stream(dev))
+    if return_logits:
+        return idx, w, lg
+    return idx, w
+
+
+def hash_route(input_ids: torch.Tensor, tid2eid: torch.Tensor, top_k: int = 6):
+    """_compute_hash_experts (engine.py:1018-1023) on the GPU; keeps input_ids' shape."""
+    dev = _check_cuda(input_ids, tid2eid)
+    ids = input_ids.to(torch.int64).contiguous()
+    tid = tid2eid.to(torch.int64).contiguous()
+    T = ids.numel()
+    idx = torch.empty(*ids.shape, top_k, dtype=torch.int64, device=dev)
+    w = torch.empty(*ids.shape, top_k, dtype=torch.float32, device=dev)
+    _launch("hs_hash_route", ids.data_ptr(), T, tid.data_ptr(), tid.shape[0], top_k, idx.data_ptr(), w.data_ptr(),
+         status_word(dev).data_ptr(), _stream(dev))
+    return idx, w
+
+
+# --- MoE FFN -------------------------------------------------------------------
+
+def make_moe_desc(w13, s13, w2, s2, sh_w13=None, sh_s13=None, sh_w2=None, sh_s2=None) -> ctypes.Array:
+    """Encode the per-layer TMA descriptor blob (host memory) for hs_moe_ffn_fp4."""
+    E, two, I, Dh = w13.shape
+    assert two == 2
+    D = Dh * 2
+    I_sh = sh_w13.shape[1] if sh_w13 is not None else 0
+    wts = _lib.hs_moe_weights(w13.data_ptr(), s13.data_ptr(), w2.data_ptr(), s2.data_ptr(),
+                              _ptr(sh_w13), _ptr(sh_s13), _ptr(sh_w2), _ptr(sh_s2), E, D, I, I_sh)
+    buf = (ctypes.c_uint8 * _lib.HS_MOE_DESC_BYTES)()
+    with torch.cuda.device(w13.device):
+        call("hs_moe_make_desc", ctypes.byref(wts), buf, ctypes.sizeof(buf))
+    return buf
+
+
+def moe_ffn(desc: ctypes.Array, dims: tuple, hidden: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor,
+            use_shared: bool = True, dup_mode: int = _lib.HS_DUP_LAST, out: Optional[torch.Tensor] = None,
+            out_f32: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Routed FP4 FFN (+ FP8 shared expert) for hidden [T, D] bf16. dims = (E, D, I, I_sh)."""
+    dev = _check_cuda(hidden, topk_idx, topk_w, out, out_f32)
+    if hidden.dtype != torch.bfloat16:
+        raise TypeError("hidden must be bf16")
+    topk_idx = topk_idx.to(torch.int64).contiguous()
+    topk_w = topk_w.to(torch.float32).contiguous()
+    T, D = hidden.shape
+    K = topk_idx.shape[-1]
+    E, Dd, I, I_sh = dims
+    if D != Dd:
+        raise ValueError(f"hidden dim {D} != store dim {Dd}")
+    if out is None:
+        out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    nb = lib.hs_moe_workspace_size(T, K, D, I, I_sh)
+    ws = workspace(dev, nb, "moe")
+    _launch("hs_moe_ffn_fp4", ctypes.addressof(desc), hidden.data_ptr(), topk_idx.data_ptr(), topk_w.data_ptr(), T, K,
+         int(bool(use_shared)), int(dup_mode), out.data_ptr(), _ptr(out_f32), ws.data_ptr(), ws.numel(),
+         status_word(dev).data_ptr(), _stream(dev))
+    return out
+
+
+def moe_permute(topk_idx: torch.Tensor, num_experts: int, x: Optional[torch.Tensor] = None):
+    """Expert-major permutation (expand_to_fused, tests/_reference.py:108-121).
+
+    Returns (token_topk_to_pos int32 [T, k], pos_to_expert int32 [T*k],
+    expert_count int32 [E], num_pos int32 [1], x_expanded [T*k, D] or None).
+    """
+    dev = _check_cuda(topk_idx, x)
+    idx = topk_idx.to(torch.int64).contiguous()
+    T, K = idx.shape
+    pos = torch.empty(T, K, dtype=torch.int32, device=dev)
+    p2e = torch.empty(T * K, dtype=torch.int32, device=dev)
+    cnt = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    npos = torch.empty(1, dtype=torch.int32, device=dev)
+    xe = None
+    if x is not None:
+        xe = torch.empty(T * K, x.shape[1], dtype=x.dtype, device=dev)
+    lib = _lib.load()
+    ws = workspace(dev, lib.hs_moe_permute_workspace_size(T, K, num_experts), "permute")
+    _launch("hs_moe_permute", idx.data_ptr(), T, K, num_experts, _ptr(x), x.shape[1] if x is not None else 0,
+         pos.data_ptr(), p2e.data_ptr(), cnt.data_ptr(), npos.data_ptr(), _ptr(xe), ws.data_ptr(), ws.numel(),
+         status_word(dev).data_ptr(), _stream(dev))
+    return pos, p2e, cnt, npos, xe
+
+
+def moe_unpermute(x_expanded: torch.Tensor, token_topk_to_pos: torch.Tensor,
+                  topk_w: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """reduce_fused (tests/_reference.py:52-90): out[t] = sum_k w[t,k] * x[pos[t,k]] in f32, k order."""
+    dev = _check_cuda(x_expanded, token_topk_to_pos, topk_w)
+    pos = token_topk_to_pos.to(torch.int32).contiguous()
+    w = topk_w.to(torch.float32).contiguous() if topk_w is not None else None
+    T, K = pos.shape
+    out = torch.empty(T, x_expanded.shape[1], dtype=torch.bfloat16, device=dev)
+    _launch("hs_moe_unpermute", x_expanded.data_ptr(), x_expanded.shape[0], x_expanded.shape[1], pos.data_ptr(),
+         _ptr(w), T, K, out.data_ptr(), _stream(dev))
+    return out
+
+
+# --- acceptance ----------------------------------------------------------------
+
+def accept_greedy(logits: torch.Tensor, draft_ids: torch.Tensor, want_argmax: bool = False):
+    """logits [B, T, V] bf16, draft_ids [B, T-1] -> (n_accept int32 [B], next_token int64 [B][, argmax [B, T]])."""
+    dev = _check_cuda(logits, draft_ids)
+    if logits.dtype != torch.bfloat16:
+        raise TypeError("logits must be bf16")
+    B, T, V = logits.shape
+    ids = draft_ids.to(torch.int64).contiguous()
+    n = torch.empty(B, dtype=torch.int32, device=dev)
+    nxt = torch.empty(B, dtype=torch.int64, device=dev)
+    am = torch.empty(B, T, dtype=torch.int64, device=dev) if want_argmax else None
+    _launch("hs_accept_greedy", logits.data_ptr(), B, T, V, ids.data_ptr(), n.data_ptr(), nxt.data_ptr(), _ptr(am),
+         status_word(dev).data_ptr(), _stream(dev))
+    return (n, nxt, am) if want_argmax else (n, nxt)
+
+
+def accept_rejection(target: torch.Tensor, draft: torch.Tensor, draft_ids: torch.Tensor, uniform: torch.Tensor,
+                     temperature: float):
+    """Speculative sampling: target [B, M+1, V], draft [B, R>=M, V] bf16, draft_ids [B, M], uniform [B, M+1]."""
+    dev = _check_cuda(target, draft, draft_ids, uniform)
+    B, M1, V = target.shape
+    M = M1 - 1
+    ids = draft_ids.to(torch.int64).contiguous()
+    u = uniform.to(torch.float32).contiguous()
+    n = torch.empty(B, dtype=torch.int32, device=dev)
+    nxt = torch.empty(B, dtype=torch.int64, device=dev)
+    _launch("hs_accept_rejection", target.data_ptr(), draft.data_ptr(), B, M, draft.shape[1], V, ids.data_ptr(),
+         u.data_ptr(), float(temperature), n.data_ptr(), nxt.data_ptr(), status_word(dev).data_ptr(), _stream(dev))
+    return n, nxt
+
+
+def fill_bytes(t: torch.Tensor, seed: int, lo: int = 0, hi: int = 255) -> torch.Tensor:
+    """Counter-hash fill of a uint8 tensor with values in [lo, hi] (device side)."""
+    dev = _check_cuda(t)
+    _launch("hs_fill_bytes", t.data_ptr(), t.numel() * t.element_size(), int(seed) & 0xFFFFFFFFFFFFFFFF, lo, hi,
+         _stream(dev))
+    return t
+
+
+__all__ = ["HsError", "router_topk", "hash_route", "make_moe_desc", "moe_ffn", "moe_permute", "moe_unpermute",
+           "accept_greedy", "accept_rejection", "fill_bytes", "check_status", "status_word", "workspace"]

@@ -1,0 +1,206 @@
+/*
+ * hs_ext.h — C ABI of libhs_ext.so, the B200 (sm_100a) kernels behind the
+ * MTP speculative-decode MoE step of home-seek.
+ *
+ * Conventions (all entry points):
+ *   - Pointers are raw DEVICE pointers, borrowed; outputs are caller-allocated.
+ *   - Shapes are int64; `stream` is a cudaStream_t passed as void* (NULL = legacy
+ *     default stream). Every launch is asynchronous on that stream.
+ *   - The return value is an hs_status. Host-checkable errors (shape, alignment,
+ *     workspace size, launch failure) are returned immediately. Data-dependent
+ *     errors found on the device (expert id or token id out of range, a bounded
+ *     wait that gave up) are OR-ed into the optional `dev_status` word (device
+ *     int32, caller zeroes it) as HS_DEV_* bits; the host reads it when it syncs.
+ *   - No entry point allocates device memory. Kernels that need scratch take a
+ *     caller-provided `workspace`; its size comes from the matching
+ *     *_workspace_size() query and it must be zero-filled once after allocation
+ *     (the kernels leave every counter they use back at zero).
+ *   - No exceptions, no global mutable state: concurrent calls on different
+ *     streams are safe when they use different workspaces.
+ *
+ * The Python host layer (home_seek_b200/) binds this header with ctypes and
+ * turns non-zero statuses into Python exceptions, which keeps the reference
+ * engine's try/except fallback semantics.
+ */
+#ifndef HS_EXT_H
+#define HS_EXT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HS_ABI_VERSION 1
+
+typedef enum hs_status {
+  HS_OK = 0,
+  HS_ERR_BAD_SHAPE = 1,      /* a size or dimension the kernels do not support */
+  HS_ERR_BAD_ARGUMENT = 2,   /* a NULL pointer where one is required, bad enum */
+  HS_ERR_WORKSPACE = 3,      /* workspace smaller than *_workspace_size() */
+  HS_ERR_ALIGN = 4,          /* pointer or stride not 16-byte aligned as required */
+  HS_ERR_CUDA = 5,           /* a CUDA runtime/driver call failed */
+  HS_ERR_UNSUPPORTED = 6     /* device is not sm_100 or a driver entry point is missing */
+} hs_status;
+
+/* Bits OR-ed into the optional device status word. */
+#define HS_DEV_BAD_EXPERT 0x1  /* an expert id outside [-1, E) was skipped */
+#define HS_DEV_BAD_TOKEN 0x2   /* a token id outside [0, V) was skipped */
+#define HS_DEV_TIMEOUT 0x4     /* a bounded device-side wait gave up */
+#define HS_DEV_BAD_DRAFT 0x8   /* a draft id outside [0, V) */
+
+int hs_abi_version(void);
+const char* hs_status_string(int status);
+/* Last CUDA error code seen by the library on this thread (0 if none). */
+int hs_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* R1. Router: logits = bf16(h @ gate^T); logits = bf16(logits + bias);      */
+/*     s = sqrt(softplus(f32(logits))); idx = stable top-k of s (ties to the  */
+/*     lower expert id); w = s[idx] / max(sum, 1e-20) * routed_scaling.       */
+/* Replaces home_seek/router.py:22-36 (compute_expert_affinity_with_bias)     */
+/* and router.py:10-19 (compute_expert_affinity, bias == NULL), called from   */
+/* inference_engine/engine.py:1025-1031 (_compute_routing_experts).           */
+/* hidden [T][D] bf16, gate [E][D] bf16, bias [E] bf16 or NULL.               */
+/* topk_idx [T][top_k] int64, topk_w [T][top_k] f32.                          */
+/* logits_out [T][E] bf16 (post-bias) or NULL.                                */
+/* Limits: D % 512 == 0, E % 16 == 0, E <= 1024, 1 <= top_k <= 16, top_k <= E.*/
+size_t hs_router_workspace_size(int64_t T, int64_t D, int64_t E);
+int hs_router_topk(const void* hidden, const void* gate, const void* bias,
+                   int64_t T, int64_t D, int64_t E, int64_t top_k,
+                   float routed_scaling, int64_t* topk_idx, float* topk_w,
+                   void* logits_out, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* R2. Hash routing for layers < num_hash_layers: idx = tid2eid[input_ids],   */
+/*     w = 1/top_k. Replaces engine.py:1018-1023 (_compute_hash_experts).      */
+/* input_ids [T] int64, tid2eid [V][top_k] int64 -> topk_idx [T][top_k] int64, */
+/* topk_w [T][top_k] f32. Out-of-range ids give -1 and set HS_DEV_BAD_TOKEN.  */
+int hs_hash_route(const int64_t* input_ids, int64_t T, const int64_t* tid2eid,
+                  int64_t V, int64_t top_k, int64_t* topk_idx, float* topk_w,
+                  int32_t* dev_status, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* R3/R5. Routed FP4 expert FFN with the FP8 shared expert fused in.          */
+/*                                                                            */
+/* Weight layout (what HBMExpertStore holds in HBM):                          */
+/*   w13 [E][2][I][D/2]  u8  packed e2m1, low nibble = even column            */
+/*   s13 [E][2][I][D/32] u8  ue8m0 (one per 32 columns)                       */
+/*   w2  [E][D][I/2]     u8  packed e2m1                                      */
+/*   s2  [E][D][I/32]    u8  ue8m0                                            */
+/*   sh_w13 [2][I_sh][D] u8  e4m3 (w1 rows then w3 rows), or NULL            */
+/*   sh_s13 [2][I_sh/128][D/128] u8 ue8m0                                     */
+/*   sh_w2  [D][I_sh]    u8  e4m3                                             */
+/*   sh_s2  [D/128][I_sh/128] u8 ue8m0                                        */
+/* Limits: D, I multiples of 512 in [512, 8192]; I_sh a multiple of 256 in    */
+/* [256, 8192]; E <= 1024; all base pointers 16-byte aligned.                 */
+/* ------------------------------------------------------------------------ */
+typedef struct hs_moe_weights {
+  const void* w13;
+  const void* s13;
+  const void* w2;
+  const void* s2;
+  const void* sh_w13;
+  const void* sh_s13;
+  const void* sh_w2;
+  const void* sh_s2;
+  int64_t E;
+  int64_t D;
+  int64_t I;
+  int64_t I_sh;
+} hs_moe_weights;
+
+/* Opaque per-layer descriptor (TMA tensor maps over the weights), encoded    */
+/* once on the host by hs_moe_make_desc and passed by pointer to every call.  */
+#define HS_MOE_DESC_BYTES 1024
+int hs_moe_make_desc(const hs_moe_weights* weights, void* desc_out, size_t desc_bytes);
+
+/* Duplicate (token, expert) pairs in one top-k row: */
+#define HS_DUP_LAST 0 /* keep the last occurrence's weight (fused_moe.py:526-539) */
+#define HS_DUP_SUM 1  /* sum the weights (engine.py:1388-1393, the T=1 path)     */
+
+size_t hs_moe_workspace_size(int64_t T, int64_t top_k, int64_t D, int64_t I,
+                             int64_t I_sh);
+
+/* out[t] = bf16( bf16(sum_e w_te * FFN_e(h_t)) + bf16(FFN_shared(h_t)) )      */
+/* with FFN(h) = bf16(bf16(clamp(g)*sigmoid(g)*clamp(u)) ...) exactly as       */
+/* FusedMoEFFN._forward_legacy (fused_moe.py:458-551) plus                     */
+/* SharedExpertFFN.forward / fused_expert_ffn_pt (fused_moe.py:383-392,        */
+/* 573-598) and the bf16 add at engine.py:1530-1536.                           */
+/* Replaces FusedMoEFFN.forward (fused_moe.py:447-456) and                     */
+/* FusedMoEFFN.forward_m1_fp4 (fused_moe.py:553-563).                          */
+/* hidden [T][D] bf16; topk_idx [T][top_k] int64 (-1 = skip); topk_w [T][top_k]*/
+/* f32; out [T][D] bf16. out_f32 [T][D] f32 (optional, may be NULL) receives   */
+/* the routed sum before rounding (used by the expert-parallel combine).       */
+/* use_shared = 0 skips the shared expert even if the descriptor has one.      */
+int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx,
+                   const float* topk_w, int64_t T, int64_t top_k, int use_shared,
+                   int dup_mode, void* out, float* out_f32, void* workspace,
+                   size_t workspace_bytes, int32_t* dev_status, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* R10. Permute / unpermute, with the semantics of the reference's test       */
+/* oracles tests/_reference.py:93-121 (expand_to_fused) and                   */
+/* tests/_reference.py:52-90 (reduce_fused). Positions are expert-major       */
+/* (ascending expert id, then ascending token), deterministic.                */
+/* hs_moe_permute: topk_idx [T][k] -> token_topk_to_pos [T][k] int32 (-1 for  */
+/*   invalid), pos_to_expert [T*k] int32 (-1 past the end), expert_count [E]   */
+/*   int32, num_pos (device int32), and x_expanded [T*k][D] bf16 (may be NULL) */
+/*   gathered from x [T][D] bf16.                                              */
+/* hs_moe_unpermute: out[t] = cast(sum_k w[t][k] * x[pos[t][k]]) in f32, in    */
+/*   k order, over valid positions; weights may be NULL (= 1).                 */
+/* ------------------------------------------------------------------------ */
+size_t hs_moe_permute_workspace_size(int64_t T, int64_t top_k, int64_t E);
+int hs_moe_permute(const int64_t* topk_idx, int64_t T, int64_t top_k, int64_t E,
+                   const void* x, int64_t D, int32_t* token_topk_to_pos,
+                   int32_t* pos_to_expert, int32_t* expert_count, int32_t* num_pos,
+                   void* x_expanded, void* workspace, size_t workspace_bytes,
+                   int32_t* dev_status, void* stream);
+int hs_moe_unpermute(const void* x_expanded, int64_t num_expanded, int64_t D,
+                     const int32_t* token_topk_to_pos, const float* topk_w,
+                     int64_t T, int64_t top_k, void* out_bf16, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* R6. Acceptance.                                                            */
+/* hs_accept_greedy: logits [B][T][V] bf16 (row stride V); draft_ids [B][T-1] */
+/*   int64. For each row b: n_accept = number of leading positions i < T-1    */
+/*   with argmax(logits[b][i]) == draft_ids[b][i]; next_token =               */
+/*   argmax(logits[b][n_accept]). argmax takes the first maximal index and   */
+/*   treats NaN as maximal (torch.argmax). Replaces the loop at               */
+/*   engine.py:2485-2497 and the t=0 bonus at engine.py:2908-2913.            */
+/*   argmax_out [B][T] int64 may be NULL.                                     */
+/* hs_accept_rejection: standard speculative sampling (Leviathan et al. 2023) */
+/*   with p = softmax(target/t), q = softmax(draft/t) in f32: accept draft i  */
+/*   iff u[b][i] < p_i(d_i) / q_i(d_i); at the first rejection i sample from  */
+/*   normalise(max(0, p_i - q_i)), else (all accepted) from p_M, by inverse   */
+/*   CDF in ascending token order with u[b][M]. target [B][M+1][V],           */
+/*   draft [B][draft_rows][V] (draft_rows >= M), draft_ids [B][M],            */
+/*   uniform [B][M+1] f32. t <= 0 falls back to greedy.                       */
+/*   Outputs n_accept [B] int32 and next_token [B] int64.                     */
+/* Limits: V >= 64, V*2 % 16 == 0 (rows 16-byte aligned).                     */
+/* ------------------------------------------------------------------------ */
+int hs_accept_greedy(const void* logits, int64_t B, int64_t T, int64_t V,
+                     const int64_t* draft_ids, int32_t* n_accept,
+                     int64_t* next_token, int64_t* argmax_out,
+                     int32_t* dev_status, void* stream);
+int hs_accept_rejection(const void* target_logits, const void* draft_logits,
+                        int64_t B, int64_t M, int64_t draft_rows, int64_t V,
+                        const int64_t* draft_ids, const float* uniform,
+                        float temperature, int32_t* n_accept,
+                        int64_t* next_token, int32_t* dev_status, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Synthetic weight fill (device-side, counter-based hash; no allocation).    */
+/* Fills n bytes at dst with lo + (hash(seed, i) % (hi - lo + 1)). Used to    */
+/* build random-init expert stores of the full model shape in seconds.        */
+/* No counterpart in the reference (its weights come from safetensors).       */
+/* ------------------------------------------------------------------------ */
+int hs_fill_bytes(void* dst, int64_t n, uint64_t seed, int32_t lo, int32_t hi,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HS_EXT_H */

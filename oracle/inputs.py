@@ -1,0 +1,115 @@
+"""Seeded synthetic inputs for the parity tests, the golden fixtures and the
+CPU baseline (test infrastructure; the GPU bench builds its own full-size
+weights on the device).
+
+Shapes and value distributions follow the benchmark configurations:
+  routed experts: w1/w3 [I, D/2], w2 [D, I/2] bytes uniform over 0..255 (both
+  nibbles uniform over the 16 e2m1 codes); UE8M0 scales with exponent uniform
+  in [-9, -5] (bytes 118..122); per-expert sub-seed 1000 + eid so experts can
+  be generated lazily;
+  shared expert: e4m3 from N(0, 1) clipped to +-448, 128x128 scales 2^-6;
+  router gate bf16 ~ N(0, 0.02^2), bias bf16 ~ N(0, 0.01^2); hidden ~ N(0, 1).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from functools import lru_cache
+
+import numpy as np
+import torch
+
+
+@dataclass(frozen=True)
+class MoeShape:
+    D: int = 4096
+    I: int = 2048
+    E: int = 256
+    I_sh: int = 2048
+    K: int = 6
+
+
+CONFIG0 = MoeShape()
+SMALL = MoeShape(D=512, I=512, E=16, I_sh=512, K=6)
+
+
+def expert_fp4(eid: int, D: int, I: int, seed_base: int = 1000):
+    """(w1, s1, w3, s3, w2, s2) as uint8 numpy arrays for routed expert eid."""
+    g = torch.Generator().manual_seed(seed_base + int(eid))
+    w1 = torch.randint(0, 256, (I, D // 2), generator=g, dtype=torch.uint8)
+    s1 = torch.randint(118, 123, (I, D // 32), generator=g, dtype=torch.uint8)
+    w3 = torch.randint(0, 256, (I, D // 2), generator=g, dtype=torch.uint8)
+    s3 = torch.randint(118, 123, (I, D // 32), generator=g, dtype=torch.uint8)
+    w2 = torch.randint(0, 256, (D, I // 2), generator=g, dtype=torch.uint8)
+    s2 = torch.randint(118, 123, (D, I // 32), generator=g, dtype=torch.uint8)
+    return tuple(x.numpy() for x in (w1, s1, w3, s3, w2, s2))
+
+
+def make_loader(shape: MoeShape, seed_base: int = 1000):
+    @lru_cache(maxsize=None)
+    def load(eid: int):
+        return expert_fp4(eid, shape.D, shape.I, seed_base)
+    return load
+
+
+def shared_fp8(D: int, I_sh: int, seed: int = 7):
+    """(w13 [2, I_sh, D], s13 [2, I_sh/128, D/128], w2 [D, I_sh], s2 [D/128, I_sh/128]) uint8."""
+    g = torch.Generator().manual_seed(seed)
+    w13 = torch.randn(2, I_sh, D, generator=g).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+    w2 = torch.randn(D, I_sh, generator=g).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+    s13 = torch.full((2, I_sh // 128, D // 128), 121, dtype=torch.uint8)
+    s2 = torch.full((D // 128, I_sh // 128), 121, dtype=torch.uint8)
+    return w13.numpy(), s13.numpy(), w2.numpy(), s2.numpy()
+
+
+def hidden(T: int, D: int, seed: int = 0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(T, D, generator=g).to(torch.bfloat16)
+
+
+def router_weights(E: int, D: int, seed: int = 1):
+    g = torch.Generator().manual_seed(seed)
+    gate = (torch.randn(E, D, generator=g) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(E, generator=g) * 0.01).to(torch.bfloat16)
+    return gate, bias
+
+
+def tid2eid(V: int, E: int, K: int, seed: int = 3) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, E, (V, K), generator=g, dtype=torch.int64)
+
+
+def zipf_routing(T: int, E: int = 256, K: int = 6, s: float = 1.1, seed: int = 0):
+    """Config-2 routing: Zipf(s) over a fixed random permutation of the expert
+    ids, top-K without replacement (sequential renormalised draws), combine
+    weights = softmax of N(0, 1) logits over the K picks."""
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(E)
+    p = 1.0 / np.arange(1, E + 1) ** s
+    p = p / p.sum()
+    idx = np.zeros((T, K), dtype=np.int64)
+    for t in range(T):
+        avail = np.ones(E, dtype=bool)
+        for k in range(K):
+            q = np.where(avail, p, 0.0)
+            q = q / q.sum()
+            r = rng.choice(E, p=q)
+            avail[r] = False
+            idx[t, k] = perm[r]
+    z = rng.standard_normal((T, K)).astype(np.float32)
+    w = np.exp(z - z.max(axis=1, keepdims=True))
+    w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+    return torch.from_numpy(idx), torch.from_numpy(w)
+
+
+def accept_inputs(B: int = 64, M: int = 2, V: int = 129280, t: float = 0.7, seed: int = 1):
+    """Config-4 inputs: target/draft logits bf16 [B, M+1, V] ~ N(0, 3^2), uniform
+    [B, M+1] from torch.Generator().manual_seed(1), draft ids drawn from
+    q = softmax(draft / t) with a harness generator (seed + 1)."""
+    g = torch.Generator().manual_seed(seed + 100)
+    target = (torch.randn(B, M + 1, V, generator=g) * 3.0).to(torch.bfloat16)
+    draft = (torch.randn(B, M + 1, V, generator=g) * 3.0).to(torch.bfloat16)
+    u = torch.rand(B, M + 1, generator=torch.Generator().manual_seed(seed))
+    gd = torch.Generator().manual_seed(seed + 1)
+    q = torch.softmax(draft[:, :M].float() / t, dim=-1)
+    ids = torch.multinomial(q.reshape(B * M, V), 1, generator=gd).reshape(B, M)
+    return target, draft, ids, u

@@ -1,0 +1,230 @@
+"""Generate golden vectors by running the reference's own code on CPU.
+
+Run once in a container that has the reference source tree (it is read-only
+and not present on the GPU host):
+
+    HOME_SEEK_REF=/path/to/home-seek/src python tests/golden/make_golden.py
+
+Every input is regenerated from the seeds in oracle/inputs.py; the fixtures
+store the reference outputs (and the small inputs, for convenience) in
+tests/golden/*.npz. Reference entry points exercised:
+  home_seek.router.compute_expert_affinity_with_bias        (router.py:22-36)
+  HomeSeekInferenceEngine._compute_hash_experts              (engine.py:1018-1023)
+  home_seek.fused_moe.FusedMoEFFN.forward                    (fused_moe.py:447-551)
+  home_seek.fused_moe.SharedExpertFFN.forward + load_fp8_weight
+                                                             (fused_moe.py:573-598,
+                                                              weight_loader.py:22-32)
+  HomeSeekInferenceEngine._mtp_verify_batched (greedy loop)  (engine.py:2431-2540)
+  tests/_reference.py expand_to_fused / reduce_fused          (_reference.py:52-121)
+"""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+from unittest.mock import MagicMock
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+
+from oracle import inputs as I  # noqa: E402
+from oracle import moe as O  # noqa: E402
+
+
+def _ref_path() -> Path:
+    p = os.environ.get("HOME_SEEK_REF")
+    if p:
+        return Path(p)
+    raise SystemExit("set HOME_SEEK_REF to the reference's src directory")
+
+
+def _bf16_np(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _fp4_loader_ref(load):
+    """Wrap the oracle's seeded uint8 arrays in the reference's 6-tuple format:
+    int8 packed data and float8_e8m0fnu scales (what _make_raw_entry keeps)."""
+    def fn(layer, eid):
+        w1, s1, w3, s3, w2, s2 = load(int(eid))
+        c = lambda a: torch.from_numpy(a).view(torch.int8)  # noqa: E731
+        s = lambda a: torch.from_numpy(a).view(torch.float8_e8m0fnu)  # noqa: E731
+        return (c(w1), s(s1), c(w3), s(s3), c(w2), s(s2))
+    return fn
+
+
+def gen_router(out):
+    from home_seek.router import compute_expert_affinity_with_bias
+    cases = {
+        "small": (I.hidden(5, 512, seed=10), *I.router_weights(16, 512, seed=11)),
+        "cfg0": (I.hidden(3, 4096, seed=0), *I.router_weights(256, 4096, seed=1)),
+        "t24": (I.hidden(24, 4096, seed=12), *I.router_weights(256, 4096, seed=13)),
+    }
+    h, gate, bias = I.hidden(4, 512, seed=14), *I.router_weights(32, 512, seed=15)
+    gate = gate.clone()
+    gate[9] = gate[5]  # identical rows -> identical logits: stable order must pick 5 before 9
+    gate[20] = gate[5]
+    bias = bias.clone()
+    bias[9] = bias[5]
+    bias[20] = bias[5]
+    cases["ties"] = (h, gate, bias)
+    for name, (h, gate, bias) in cases.items():
+        idx, w = compute_expert_affinity_with_bias(h, gate, bias, top_k=6, routed_scaling_factor=1.5)
+        logits = torch.matmul(h, gate.t()) + bias
+        out[f"router_{name}_idx"] = idx.numpy()
+        out[f"router_{name}_w"] = w.numpy()
+        out[f"router_{name}_logits"] = _bf16_np(logits)
+
+
+def gen_hash(out):
+    from home_seek.inference_engine import HomeSeekInferenceEngine
+    from home_seek.model_config import DeepSeekV4FlashConfig
+    eng = HomeSeekInferenceEngine.__new__(HomeSeekInferenceEngine)
+    eng.config = DeepSeekV4FlashConfig(num_experts_per_tok=6, num_hash_layers=3)
+    tid = I.tid2eid(1000, 256, 6, seed=3)
+    ids = torch.tensor([[5, 10, 15, 999, 0]], dtype=torch.int64)
+    eids, w = eng._compute_hash_experts(ids, 0, tid)
+    out["hash_ids"] = ids.numpy()
+    out["hash_eids"] = eids.numpy()
+    out["hash_w"] = w.numpy()
+
+
+def gen_moe(out):
+    from home_seek.fused_moe import FusedMoEFFN, SharedExpertFFN
+    from home_seek.inference_engine.weight_loader import load_fp8_weight
+    from home_seek.router import compute_expert_affinity_with_bias
+
+    def run(shape, T, seed, name, hash_route=False):
+        h = I.hidden(T, shape.D, seed=seed)
+        if hash_route:
+            tid = I.tid2eid(97, shape.E, shape.K, seed=seed + 1)
+            ids = torch.arange(T, dtype=torch.int64) * 7 % 97
+            idx = tid[ids]
+            w = torch.full((T, shape.K), 1.0 / shape.K)
+        else:
+            gate, bias = I.router_weights(shape.E, shape.D, seed=seed + 1)
+            idx, w = compute_expert_affinity_with_bias(h, gate, bias, top_k=shape.K, routed_scaling_factor=1.5)
+        load = I.make_loader(shape)
+        ffn = FusedMoEFFN(num_experts=shape.E, intermediate_size=shape.I, hidden_size=shape.D)
+        assert not ffn.use_triton  # CPU: the _forward_legacy cuBLAS-branch math on ATen
+        routed = ffn.forward(h, idx, w, _fp4_loader_ref(load), 5)
+        w13, s13, w2, s2 = I.shared_fp8(shape.D, shape.I_sh, seed=seed + 2)
+        t8 = lambda a: torch.from_numpy(np.ascontiguousarray(a)).view(torch.float8_e4m3fn)  # noqa: E731
+        u8 = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+        sw1 = load_fp8_weight(t8(w13[0]), u8(s13[0]))
+        sw3 = load_fp8_weight(t8(w13[1]), u8(s13[1]))
+        sw2 = load_fp8_weight(t8(w2), u8(s2))
+        sh = SharedExpertFFN(hidden_size=shape.D, intermediate_size=shape.I_sh)
+        shared = sh.forward(h.unsqueeze(0), sw1, sw3, sw2, h.dtype)[0]
+        full = routed + shared
+        out[f"moe_{name}_idx"] = idx.numpy()
+        out[f"moe_{name}_w"] = w.numpy()
+        out[f"moe_{name}_routed"] = _bf16_np(routed)
+        out[f"moe_{name}_out"] = _bf16_np(full)
+        out[f"moe_{name}_meta"] = np.array([shape.D, shape.I, shape.E, shape.I_sh, shape.K, T, seed], dtype=np.int64)
+
+    for T in (1, 3, 5, 24):
+        run(I.SMALL, T, 20 + T, f"small_t{T}")
+    run(I.SMALL, 6, 40, "small_hash", hash_route=True)
+    run(I.CONFIG0, 3, 0, "cfg0")
+
+
+def gen_accept(out):
+    """Greedy acceptance through the reference's _mtp_verify_batched, with a
+    mocked forward whose output becomes the logits exactly (identity lm_head,
+    hc_mult=1, no norm, no hc head)."""
+    from home_seek.inference_engine import HomeSeekInferenceEngine
+    V = 256
+
+    def verify(logits_rows: torch.Tensor, ids: list[int]):
+        eng = HomeSeekInferenceEngine.__new__(HomeSeekInferenceEngine)
+        eng._log = lambda m: None
+        eng.config = MagicMock()
+        eng.config.num_hidden_layers = 1
+        eng.config.hc_mult = 1
+        eng.layer_states = {}
+        eng._compressors = {}
+        eng._global_pos = 0
+        eng.embed = torch.zeros(V, V, dtype=torch.bfloat16)
+        eng.lm_head = torch.eye(V, dtype=torch.bfloat16)
+        eng.norm_weight = None
+        eng.hc_head_fn = None
+        eng._get_layer_weights = lambda i: {}
+        eng._forward_layer = lambda h, lw, i, ids_: (logits_rows.view(1, -1, 1, V).to(torch.bfloat16), set())
+        main = torch.tensor([[ids[0]]], dtype=torch.int64)
+        drafts = torch.tensor([ids[1:]], dtype=torch.int64)
+        n, bonus = eng._mtp_verify_batched(drafts, 0.0, main_pred_id=main)
+        return n, int(bonus.argmax(dim=-1).item())
+
+    g = torch.Generator().manual_seed(5)
+    rows, ids_all, n_all, nxt_all = [], [], [], []
+    for case in range(12):
+        lg = (torch.randn(3, V, generator=g) * 3).to(torch.bfloat16)
+        am = lg.float().argmax(dim=-1).tolist()
+        # case % 4: 0 -> reject first, 1 -> accept one, 2 -> accept both, 3 -> tie at argmax
+        ids = [7, (am[0] + 1) % V, 11]
+        if case % 4 >= 1:
+            ids[1] = am[0]
+        if case % 4 == 2:
+            ids[2] = am[1]
+        if case % 4 == 3:
+            j = (am[0] + 17) % V
+            lg[0, j] = lg[0, am[0]]  # duplicate max later in the row... or earlier
+            lg[0, (am[0] + V - 3) % V] = lg[0, am[0]]
+            ids[1] = int(lg[0].float().argmax())
+        n, nxt = verify(lg, ids)
+        rows.append(lg)
+        ids_all.append(ids)
+        n_all.append(n)
+        nxt_all.append(nxt)
+    out["accept_logits"] = _bf16_np(torch.stack(rows))
+    out["accept_ids"] = np.array(ids_all, dtype=np.int64)
+    out["accept_n"] = np.array(n_all, dtype=np.int32)
+    out["accept_next"] = np.array(nxt_all, dtype=np.int64)
+
+
+def gen_permute(out):
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_hs_ref_tests", _ref_path().parent / "tests" / "_reference.py")
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    # The reference compiles elementwise_fma with Inductor, whose CPU build uses
+    # -ffp-contract=off: a separate multiply and add. Run the same arithmetic
+    # eagerly (Inductor's C++ toolchain is not available here).
+    ref.elementwise_fma = lambda a, b, c: a * b + c
+    g = torch.Generator().manual_seed(9)
+    T, K, E, D = 7, 4, 8, 64
+    idx = torch.randint(-1, E, (T, K), generator=g)
+    idx[2, 1] = idx[2, 0]  # a duplicate expert in one row
+    x = torch.randn(T, D, generator=g).to(torch.bfloat16)
+    w = torch.rand(T, K, generator=g)
+    pos, p2e, cnt, n = O.permute_plan(idx.numpy(), E)
+    xe = ref.expand_to_fused(x, torch.from_numpy(pos).long(), torch.from_numpy(p2e[: T * K]).long())
+    red = ref.reduce_fused(xe, w, torch.from_numpy(pos).long())
+    out["perm_idx"] = idx.numpy()
+    out["perm_x"] = _bf16_np(x)
+    out["perm_w"] = w.numpy()
+    out["perm_pos"] = pos
+    out["perm_xe"] = _bf16_np(xe)
+    out["perm_reduced"] = _bf16_np(red)
+
+
+def main():
+    sys.path.insert(0, str(_ref_path()))
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    out = {}
+    gen_router(out)
+    gen_hash(out)
+    gen_accept(out)
+    gen_permute(out)
+    gen_moe(out)
+    np.savez_compressed(HERE / "golden.npz", **out)
+    print("wrote", HERE / "golden.npz", len(out), "arrays")
+
+
+if __name__ == "__main__":
+    main()

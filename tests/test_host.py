@@ -1,0 +1,48 @@
+"""Host-side logic on the CPU: the expert store layout and its reference-format
+views, the loader protocol, and expert-id localisation for sharded stores."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import inputs as I
+
+
+def test_store_layout_and_reference_views():
+    from home_seek_b200.expert_store import HBMExpertStore
+    sh = I.SMALL
+    st = HBMExpertStore(2, sh.E, sh.D, sh.I, sh.I_sh, device="cpu", hash_layers=1, vocab_size=100)
+    w = I.expert_fp4(5, sh.D, sh.I)
+    st.set_expert(1, 5, *w)
+    raw = st._load_expert_fp4_raw(1, 5)
+    assert raw[0].dtype == torch.int8 and raw[1].dtype == torch.float8_e8m0fnu
+    assert raw[0].shape == (sh.I, sh.D // 2) and raw[4].shape == (sh.D, sh.I // 2)
+    for got, want in zip(raw, w):
+        assert np.array_equal(got.view(torch.uint8).numpy(), want)
+    # views, not copies: writing through the store changes what the view sees
+    assert raw[0].data_ptr() == st.layers[1].w13[5, 0].data_ptr()
+    trip = st._load_expert_weights(1, 5)
+    assert [e[2] for e in trip] == ["fp4_gpu"] * 3
+    assert st.layers[0].tid2eid is not None and st.layers[1].tid2eid is None
+    assert st.bytes_per_expert() == 3 * sh.I * sh.D // 2 + 3 * sh.I * sh.D // 32
+
+
+def test_config0_expert_bytes():
+    from home_seek_b200.mtp import ModelShape
+    # B_exp = 3 * I * D * (1/2 + 1/32), engine.py:152 (I*D*51/32)
+    assert ModelShape().bytes_per_expert == 13_369_344 == 2048 * 4096 * 51 // 32
+
+
+def test_loader_protocol_and_localise():
+    from home_seek_b200.expert_store import HBMExpertStore
+    from home_seek_b200.fused_moe import _localise, _e8m0_bytes
+    sh = I.SMALL
+    st = HBMExpertStore(1, sh.E, sh.D, sh.I, None, device="cpu", with_router=False, expert_offset=8,
+                        experts_held=8)
+    fn = st.loader()
+    assert fn.__hs_store__ is st
+    assert fn(0, 3) is None and fn(0, 9) is not None
+    idx = torch.tensor([[0, 8, 15, 16, -1]])
+    assert _localise(idx, 8, 8).tolist() == [[-1, 0, 7, -1, -1]]
+    s = torch.tensor([1.0, 2.0, 0.5, 2.0 ** -9], dtype=torch.float32)
+    assert _e8m0_bytes(s).tolist() == [127, 128, 126, 118]
