@@ -203,6 +203,47 @@ def moe_roofline(model, reps: int = 43):
             "avg_unique_experts": statistics.mean(uniq)}
 
 
+def run_moe_only(args):
+    """MoE FFN microbenchmark for profiling: one (or a few) random-init layers
+    of the config-0 shape, T tokens routed by the layer's own router,
+    hs_moe_ffn_fp4 timed with CUDA events (prints one JSON line)."""
+    import torch
+    from home_seek_b200 import ops
+    from home_seek_b200.expert_store import HBMExpertStore
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    store = HBMExpertStore(args.layers, 256, 4096, 2048, 2048, device=dev)
+    store.fill_random(7)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    calls = []
+    for l in range(args.layers):
+        for _ in range(max(1, args.reps // args.layers)):
+            h = torch.randn(args.T, 4096, generator=g, device=dev).to(torch.bfloat16)
+            idx, w = ops.router_topk(h, store.layers[l].gate, store.layers[l].bias, 6, 1.5)
+            calls.append((l, h, idx, w))
+    for (l, h, idx, w) in calls[:3]:
+        ops.moe_ffn(store.desc(l), store.dims, h, idx, w)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in calls]
+    for (l, h, idx, w), (a, b) in zip(calls, ev):
+        a.record()
+        ops.moe_ffn(store.desc(l), store.dims, h, idx, w)
+        b.record()
+    torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in ev]
+    uniq = [len(set(c[2].flatten().tolist())) for c in calls]
+    shared = 3 * 2048 * 4096 + 3 * 16 * 32
+    byts = [u * 13_369_344 + shared + args.T * 4096 * 4 + 24 * args.T for u in uniq]
+    peak, kind = _peaks()
+    gbs = statistics.mean(b / (m * 1e-3) / 1e9 for b, m in zip(byts, ms))
+    print(json.dumps({"mode": "moe", "T": args.T, "layers": args.layers, "calls": len(calls),
+                      "avg_us": 1000 * statistics.mean(ms), "min_us": 1000 * min(ms),
+                      "avg_unique_experts": statistics.mean(uniq), "avg_bytes": statistics.mean(byts),
+                      "gbs": gbs, "frac": gbs / peak, "peak": peak, "peak_kind": kind}), flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -341,11 +382,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=43)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--mode", default="decode", choices=["decode", "moe"],
+                    help="moe: MoE FFN microbenchmark only (profiling; not the driver's line)")
+    ap.add_argument("--T", type=int, default=3, help="tokens per MoE call in --mode moe")
+    ap.add_argument("--reps", type=int, default=20, help="MoE calls timed in --mode moe")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.mode == "moe":
+        return run_moe_only(args)
     return run_ours(args)
 
 

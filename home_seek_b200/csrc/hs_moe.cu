@@ -1,5 +1,5 @@
-// Routed FP4 expert FFN + fused FP8 shared expert for the decode / verify
-// regime (T <= a few dozen tokens), sm_100a.
+// Routed FP4 expert FFN + fused FP8 shared expert on the 5th-generation tensor
+// cores (tcgen05, TMEM accumulators, TMA), sm_100a.
 //
 // Reference being replaced: FusedMoEFFN._forward_legacy
 // (home_seek/fused_moe.py:458-551), which dequantises every touched expert to
@@ -8,58 +8,77 @@
 // (fused_moe.py:383-392, 573-598) for the shared expert; and the bf16 add of
 // the two at inference_engine/engine.py:1530-1536.
 //
-// Design (B200-first, HBM-bound):
-//   plan     one CTA builds the expert-major pair list (deterministic counting
-//            sort), T more CTAs convert each token's hidden row to f16 with a
-//            per-token power-of-two prescale (exact for bf16 inputs).
-//   gateup   one CTA per (chunk of <= 24 pairs of one expert, 64 rows of I).
-//            A producer warp streams the packed e2m1 rows of w1 and w3 with TMA
-//            (128B-swizzled boxes) plus the token rows with bulk copies through
-//            a 4-stage mbarrier ring; 4 consumer warps convert e2m1 -> f16 in
-//            registers (cvt.rn.f16x2.e2m1x2, exact) and run m16n8k16 MMAs with
-//            f32 accumulation, applying each 32-column E8M0 scale to the group's
-//            partial sum (an exact power-of-two multiply). The epilogue rounds
-//            gate/up to bf16, applies SwiGLU with clamp 10 in f32, rounds to
-//            bf16, multiplies by the bf16 routing weight and stores the result.
-//   down     one CTA per (chunk, 64 rows of D) streams w2 the same way and
-//            writes an f32 partial row per (token, expert) pair.
-//   finalize sums each token's pairs in ascending expert order (deterministic),
-//            rounds once to bf16, adds the bf16 shared-expert output.
-// The shared expert is one more chunk list with e4m3 weights and 128x128
-// block scales (cvt.rn.f16x2.e4m3x2, exact).
+// Design (B200-first):
+//   * Weights never pass through registers. TMA loads 128x128 tiles of packed
+//     e2m1 straight into 128B-swizzled shared memory (data type 16U4_ALIGN16B,
+//     the layout kind::mxf8f6f4 reads), the UE8M0 scales (stored by the expert
+//     store in the tcgen05 scale-factor atom layout, 512 B per 128 rows x 128
+//     columns) go to TMEM with one tcgen05.cp, and tcgen05.mma.kind::mxf8f6f4
+//     .block_scale multiplies them with the activations, accumulating f32 in
+//     TMEM. The FP8 shared expert runs through the same MMA with E4M3 weights.
+//   * Activations are bf16 in the reference. Each bf16 value v (8 significant
+//     bits) is split into two e4m3 values hi = e4m3(v * 2^e), lo = e4m3(v * 2^e
+//     - hi) that sum back to v * 2^e exactly (down to 2^-9 of the row maximum
+//     scaled to [128, 256)); the power-of-two prescale 2^e is undone by the
+//     MMA's B scale factor. The N dimension of one MMA carries the hi and lo
+//     rows of up to 8*NT tokens, so every weight is read once.
+//   * plan    one CTA builds the expert-major pair list (deterministic counting
+//             sort); T more CTAs convert their token's row to the hi/lo pair
+//             rows (one per (token, expert) pair and one for the shared expert).
+//   * gateup  one CTA per (chunk of <= 8*NT pairs of one expert, 128 rows of
+//             I): warp 4 issues TMA, warp 5 issues tcgen05.cp + tcgen05.mma,
+//             warps 0-3 read the TMEM accumulators (gate and up), apply the
+//             reference's roundings and SwiGLU, multiply by the bf16 routing
+//             weight and write the activation as hi/lo e4m3 rows.
+//   * down    one CTA per (chunk, 128 rows of D): same pipeline over w2; the
+//             f32 partial rows are reduced per token in ascending expert order
+//             by the last CTA to finish each 128-row slice of D (a ticket on a
+//             counter; no CTA waits for another), rounded once to bf16 and
+//             added to the bf16 shared-expert output.
 #include <algorithm>
 #include <atomic>
 #include <mutex>
 
+#include <cuda_fp8.h>
+
 #include "hs_common.cuh"
+#include "hs_tcgen05.cuh"
 
 namespace hs {
 namespace moe {
 
-constexpr int kRows = 64;          // weight rows per unit
-constexpr int kConsumerWarps = 4;  // 16 rows each
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 4;
-constexpr int kBoxBytes = kRows * 128;     // one TMA box: 64 rows x 128 B
-constexpr int kStageA = 2 * kBoxBytes;     // two boxes per stage
-constexpr int kMaxNT = 3;                  // n-tiles of 8 pairs per chunk
-constexpr uint32_t kDescMagic = 0x48534d31u;  // "HSM1"
+constexpr int kM = 128;                 // weight rows per unit (UMMA M)
+constexpr int kBoxBytes = kM * 128;     // one 128x128 weight tile in shared memory
+constexpr int kStages = 3;
+constexpr int kThreads = 192;           // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
+constexpr int kTmemCols = 256;
+constexpr int kAccUp = 64;              // TMEM column of the up accumulator
+constexpr int kSfaCol = 128;            // 8 columns per stage (2 boxes x 4)
+constexpr int kSfbCol = 192;
+constexpr int kMaxNT = 3;               // n-tiles of 8 pairs (N = 16 * NT)
 constexpr int kPlanThreads = 512;
+constexpr int kLocalPairs = 4096;       // T*K up to this: token CTAs place their own rows
+constexpr uint32_t kDescMagic = 0x48534d32u;  // "HSM2"
 
 struct __align__(64) Desc {
-  CUtensorMap tm_w13;  // [E*2*I rows][D/2 B], box 128 B x 64, swizzle 128B
-  CUtensorMap tm_s13;  // [E*2*I rows][D/32 B], box D/32 x 64
-  CUtensorMap tm_w2;   // [E*D rows][I/2 B],  box 128 B x 64, swizzle 128B
-  CUtensorMap tm_s2;   // [E*D rows][I/32 B], box I/32 x 64
-  CUtensorMap tm_sw13; // [2*I_sh rows][D B] e4m3, box 128 B x 64, swizzle 128B
-  CUtensorMap tm_sw2;  // [D rows][I_sh B] e4m3, box 128 B x 64, swizzle 128B
-  const uint8_t* sh_s13;
-  const uint8_t* sh_s2;
+  CUtensorMap tm_w13;   // e2m1 [E*2*I rows][D], 16U4_ALIGN16B, box 128 x 128, swizzle 128B
+  CUtensorMap tm_w2;    // e2m1 [E*D rows][I]
+  CUtensorMap tm_sw13;  // e4m3 [2*I_sh rows][D], uint8, box 128 x 128
+  CUtensorMap tm_sw2;   // e4m3 [D rows][I_sh]
+  const uint8_t* s13a;  // [E][2][I/128][D/128][512] scale-factor atoms
+  const uint8_t* s2a;   // [E][D/128][I/128][512]
+  const uint8_t* sh_s13a;  // [2][I_sh/128][D/128][512]
+  const uint8_t* sh_s2a;   // [D/128][I_sh/128][512]
   int32_t E, D, I, I_sh;
   int32_t has_shared;
   uint32_t magic;
 };
 static_assert(sizeof(Desc) <= HS_MOE_DESC_BYTES, "descriptor blob too small");
+
+struct CallMaps {
+  CUtensorMap tm_x8;    // [2*P_max rows][D] e4m3 hi rows then lo rows, box 128 x 8
+  CUtensorMap tm_act8;  // [2*P_max rows][I_act]
+};
 
 // Device views into the caller's workspace.
 struct Plan {
@@ -70,25 +89,26 @@ struct Plan {
   int32_t* pair_token;    // [P_max]
   float* pair_wb;         // [P_max] bf16-rounded routing weight
   int32_t* pair_q;        // [P_max] power-of-two prescale of the activation
+  uint8_t* sb1;           // [P_max] UE8M0 B scale of the gate/up MMA (undoes 2^e)
+  uint8_t* sb2;           // [P_max] UE8M0 B scale of the down MMA (undoes 2^q)
   int32_t* tok_e;         // [T] power-of-two prescale of the hidden row
   int32_t* tok_pos;       // [T][K] ascending routed pair positions, -1 padded
-  __half* hx;             // [T][D]
-  __half* act;            // [P_max][I_act]
+  uint32_t* dcount;       // [D/128] finalize tickets, reset by the plan kernel
+  uint8_t* x8;            // [2][P_max][D] e4m3 hi / lo
+  uint8_t* act8;          // [2][P_max][I_act] e4m3 hi / lo
   float* out_part;        // [P_max][D]
 };
 
 struct Geometry {
   int64_t T, K, D, I, I_sh, I_act, P_max, C_max;
-  size_t off_hdr, off_chunk, off_pair, off_tok, off_tokpos, off_hx, off_act, off_out, total;
+  size_t off_hdr, off_chunk, off_pair, off_sb, off_tok, off_tokpos, off_dcount, off_x8, off_act8, off_out, total;
 };
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-static int64_t chunk_rows(int64_t T) {
+static int64_t ntiles(int64_t T) {
   int64_t nt = (T + 7) / 8;
-  if (nt > kMaxNT) nt = kMaxNT;
-  if (nt < 1) nt = 1;
-  return nt;
+  return std::max<int64_t>(1, std::min<int64_t>(nt, kMaxNT));
 }
 
 static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_sh) {
@@ -99,7 +119,7 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   g.I = I;
   g.I_sh = I_sh;
   g.I_act = std::max(I, I_sh);
-  const int64_t CH = 8 * chunk_rows(T);
+  const int64_t CH = 8 * ntiles(T);
   const int64_t Pr = T * K;
   g.P_max = T + Pr;
   g.C_max = Pr / CH + std::min<int64_t>(Pr, 1024) + 1;
@@ -110,14 +130,18 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   o = align_up(o + 3 * g.C_max * sizeof(int32_t), 256);
   g.off_pair = o;
   o = align_up(o + 3 * g.P_max * sizeof(int32_t), 256);
+  g.off_sb = o;
+  o = align_up(o + 2 * g.P_max, 256);
   g.off_tok = o;
   o = align_up(o + T * sizeof(int32_t), 256);
   g.off_tokpos = o;
   o = align_up(o + T * K * sizeof(int32_t), 256);
-  g.off_hx = o;
-  o = align_up(o + T * D * sizeof(__half), 256);
-  g.off_act = o;
-  o = align_up(o + g.P_max * g.I_act * sizeof(__half), 256);
+  g.off_dcount = o;
+  o = align_up(o + (D / kM + 1) * sizeof(uint32_t), 256);
+  g.off_x8 = o;
+  o = align_up(o + 2 * g.P_max * D, 256);
+  g.off_act8 = o;
+  o = align_up(o + 2 * g.P_max * g.I_act, 256);
   g.off_out = o;
   o = align_up(o + g.P_max * D * sizeof(float), 256);
   g.total = o;
@@ -134,10 +158,13 @@ static Plan plan_views(const Geometry& g, void* ws) {
   p.pair_token = reinterpret_cast<int32_t*>(b + g.off_pair);
   p.pair_wb = reinterpret_cast<float*>(p.pair_token + g.P_max);
   p.pair_q = reinterpret_cast<int32_t*>(p.pair_wb + g.P_max);
+  p.sb1 = b + g.off_sb;
+  p.sb2 = p.sb1 + g.P_max;
   p.tok_e = reinterpret_cast<int32_t*>(b + g.off_tok);
   p.tok_pos = reinterpret_cast<int32_t*>(b + g.off_tokpos);
-  p.hx = reinterpret_cast<__half*>(b + g.off_hx);
-  p.act = reinterpret_cast<__half*>(b + g.off_act);
+  p.dcount = reinterpret_cast<uint32_t*>(b + g.off_dcount);
+  p.x8 = b + g.off_x8;
+  p.act8 = b + g.off_act8;
   p.out_part = reinterpret_cast<float*>(b + g.off_out);
   return p;
 }
@@ -145,129 +172,217 @@ static Plan plan_views(const Geometry& g, void* ws) {
 // ---------------------------------------------------------------------------
 // plan kernel
 // ---------------------------------------------------------------------------
-// Power-of-two prescale for an activation rounded from a*wb with |a| <= 100:
-// |a*wb| * 2^q < 2^15, so the f16 copy never overflows and stays exact.
-__device__ __forceinline__ int act_prescale(float wb) {
-  const float m = fabsf(wb);
-  if (!(m > 0.f) || !isfinite(m)) return 0;
-  int ex;
-  frexpf(m, &ex);
-  int q = 8 - ex;
-  return max(-100, min(100, q));
-}
-
 // Internal duplicate mode for the standalone permute: every valid (t, j) gets
 // its own position.
 constexpr int kDupKeepAll = 2;
+constexpr int32_t kBadId = 0x7fffffff;  // expert id >= E (skipped and reported)
 
-// Optional outputs of the standalone permute (hs_moe_permute).
 struct PermuteOut {
   int32_t* pos_to_expert;  // [T*K] or nullptr
   int32_t* expert_count;   // [E] or nullptr
   int32_t* num_pos;        // [1] or nullptr
 };
 
-// Block 0 builds the routing plan; blocks 1..T (when hidden != nullptr)
-// convert one token row each. pos_offset is T for the MoE call (shared-expert
-// pairs first) and 0 for the standalone permute; sort_tok sorts each token's
-// positions ascending (the MoE finalize order) instead of keeping k order.
-__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __restrict__ topk_idx,
-                                                            const float* __restrict__ topk_w, int T, int K, int E,
-                                                            int CH, int dup_mode, const __nv_bfloat16* __restrict__ hidden,
-                                                            int D, Plan P, int pos_offset, int sort_tok,
-                                                            PermuteOut po, int32_t* status) {
+struct PlanArgs {
+  const int64_t* topk_idx;
+  const float* topk_w;
+  const __nv_bfloat16* hidden;  // nullptr for the standalone permute
+  int T, K, E, D, CH, dup_mode, pos_offset, sort_tok, n_dcount;
+  int64_t P_max;
+  int local_rows;  // token CTAs write their routed pair rows themselves
+  PermuteOut po;
+  int32_t* status;
+};
+
+// Power-of-two prescale for an activation aw = bf16(a * wb), |a| <= 100:
+// |aw| * 2^q <= 256 so the e4m3 split never saturates.
+__device__ __forceinline__ int act_prescale(float wb) {
+  const float m = fabsf(wb);
+  if (!(m > 0.f) || !isfinite(m)) return 0;
+  int ex;
+  frexpf(m, &ex);
+  return max(-100, min(100, 1 - ex));
+}
+
+__device__ __forceinline__ int32_t clamp_id(int64_t v, int E) {
+  return v < 0 ? -1 : (v >= E ? kBadId : static_cast<int32_t>(v));
+}
+
+// Expert of pair l = t*K + j after the duplicate rule, or -1; *wsum receives
+// the weight the pair carries. `row` is token t's K ids (clamped). Every CTA
+// evaluates the same function, so positions computed anywhere agree.
+__device__ __forceinline__ int pair_expert(const int32_t* row, const float* wrow, int j, int K, int dup_mode,
+                                           float* wsum) {
+  const int e = row[j];
+  if (e < 0 || e == kBadId) return -1;
+  if (dup_mode == kDupKeepAll) {
+    if (wsum) *wsum = wrow ? wrow[j] : 1.f;
+  } else if (dup_mode == HS_DUP_SUM) {
+    for (int jj = 0; jj < j; ++jj)
+      if (row[jj] == e) return -1;
+    float s = 0.f;
+    for (int jj = j; jj < K; ++jj)
+      if (row[jj] == e) s += wrow ? wrow[jj] : 1.f;
+    if (wsum) *wsum = s;
+  } else {
+    for (int jj = j + 1; jj < K; ++jj)
+      if (row[jj] == e) return -1;
+    if (wsum) *wsum = wrow ? wrow[j] : 1.f;
+  }
+  return e;
+}
+
+// hi/lo e4m3 split of 16 consecutive bf16 values scaled by 2^e.
+__device__ __forceinline__ void split16(const __nv_bfloat16* src, float sc, uint4& hi, uint4& lo) {
+  const uint4 a = reinterpret_cast<const uint4*>(src)[0];
+  const uint4 b = reinterpret_cast<const uint4*>(src)[1];
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float v0 = __uint_as_float(w[i] << 16) * sc;
+    const float v1 = __uint_as_float(w[i] & 0xffff0000u) * sc;
+    const __nv_fp8x2_storage_t hp = __nv_cvt_float2_to_fp8x2(make_float2(v0, v1), __NV_SATFINITE, __NV_E4M3);
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(hp, __NV_E4M3);
+    const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    const __nv_fp8x2_storage_t lp =
+        __nv_cvt_float2_to_fp8x2(make_float2(v0 - hf.x, v1 - hf.y), __NV_SATFINITE, __NV_E4M3);
+    h[i >> 1] |= static_cast<uint32_t>(hp) << (16 * (i & 1));
+    l[i >> 1] |= static_cast<uint32_t>(lp) << (16 * (i & 1));
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Block 0 builds the routing plan; blocks 1..T (MoE call only) convert one
+// token row each into its shared-expert row and, when local_rows is set, its
+// routed pair rows (positions recomputed locally from the same counts).
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) {
+  extern __shared__ int32_t sm[];
   const int tid = threadIdx.x;
+  const int T = A.T, K = A.K, E = A.E;
+  const int npairs = T * K;
+  const bool cache_idx = npairs <= kLocalPairs;
+  int32_t* sidx = sm;  // [npairs] clamped ids (when cached)
+  int32_t* rest = sm + (cache_idx ? npairs : 0);
+  if (cache_idx) {
+    for (int l = tid; l < npairs; l += blockDim.x) sidx[l] = clamp_id(A.topk_idx[l], E);
+    __syncthreads();
+  }
+
   if (blockIdx.x > 0) {
-    // ---- token row conversion: hx[t] = f16(h[t] * 2^e), e from max|h[t]| ----
+    // ---- token row: prescale, hi/lo split, rows for its pairs ----
     const int t = blockIdx.x - 1;
-    const __nv_bfloat16* h = hidden + static_cast<int64_t>(t) * D;
+    const __nv_bfloat16* h = A.hidden + static_cast<int64_t>(t) * A.D;
     float mx = 0.f;
-    for (int k = tid; k < D; k += blockDim.x) mx = fmaxf(mx, fabsf(__bfloat162float(h[k])));
+    for (int k = tid; k < A.D; k += blockDim.x) mx = fmaxf(mx, fabsf(__bfloat162float(h[k])));
     __shared__ float red[kPlanThreads / 32];
+    __shared__ int rows[17];
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((tid & 31) == 0) red[tid >> 5] = mx;
-    __syncthreads();
-    if (tid < 32) {
-      float v = tid < (int)(blockDim.x / 32) ? red[tid] : 0.f;
-      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-      if (tid == 0) red[0] = v;
+    int nrows = 1;
+    if (A.local_rows && cache_idx) {
+      nrows = 1 + K;
+      if (tid < 32) {
+        // warp 0: for each of my K entries count the valid pairs with a smaller
+        // expert (its expert's base) and with the same expert on an earlier
+        // token (its rank): the position block 0 assigns.
+        for (int j = 0; j < K; ++j) {
+          const int e = pair_expert(sidx + t * K, nullptr, j, K, A.dup_mode, nullptr);
+          int base = 0, rank = 0;
+          if (e >= 0) {
+            for (int m = tid; m < npairs; m += 32) {
+              const int tm = m / K;
+              const int e2 = pair_expert(sidx + tm * K, nullptr, m - tm * K, K, A.dup_mode, nullptr);
+              if (e2 < 0) continue;
+              base += e2 < e;
+              rank += (e2 == e) && (tm < t);
+            }
+          }
+          for (int o = 16; o > 0; o >>= 1) {
+            base += __shfl_xor_sync(0xffffffffu, base, o);
+            rank += __shfl_xor_sync(0xffffffffu, rank, o);
+          }
+          if (tid == 0) rows[1 + j] = e >= 0 ? A.pos_offset + base + rank : -1;
+        }
+      }
     }
     __syncthreads();
-    const float m = red[0];
-    int e = 0;
-    if (m > 0.f && isfinite(m)) {
-      int ex;
-      frexpf(m, &ex);
-      e = max(-100, min(100, 15 - ex));
+    if (tid == 0) {
+      float v = 0.f;
+      for (int i = 0; i < static_cast<int>(blockDim.x / 32); ++i) v = fmaxf(v, red[i]);
+      int e = 0;
+      if (v > 0.f && isfinite(v)) {
+        int ex;
+        frexpf(v, &ex);
+        e = max(-100, min(100, 8 - ex));
+      }
+      P.tok_e[t] = e;
+      red[0] = static_cast<float>(e);
+      rows[0] = t;  // shared-expert row
     }
+    __syncthreads();
+    const int e = static_cast<int>(red[0]);
     const float sc = exp2i(e);
-    __half* dst = P.hx + static_cast<int64_t>(t) * D;
-    for (int k = tid; k < D; k += blockDim.x) dst[k] = __float2half_rn(__bfloat162float(h[k]) * sc);
-    if (tid == 0) P.tok_e[t] = e;
+    uint8_t* hi_plane = P.x8;
+    uint8_t* lo_plane = P.x8 + A.P_max * A.D;
+    for (int k16 = tid; k16 < A.D / 16; k16 += blockDim.x) {
+      uint4 hv, lv;
+      split16(h + 16 * k16, sc, hv, lv);
+      for (int r = 0; r < nrows; ++r) {
+        const int p = rows[r];
+        if (p < 0) continue;
+        reinterpret_cast<uint4*>(hi_plane + static_cast<int64_t>(p) * A.D)[k16] = hv;
+        reinterpret_cast<uint4*>(lo_plane + static_cast<int64_t>(p) * A.D)[k16] = lv;
+      }
+    }
+    if (tid < nrows && rows[tid] >= 0) P.sb1[rows[tid]] = static_cast<uint8_t>(127 - e);
     return;
   }
 
   // ---- routing plan (block 0) ----
-  extern __shared__ int32_t sm[];
-  int32_t* hist = sm;                // [E]
+  int32_t* hist = rest;              // [E]
   int32_t* base = hist + E;          // [E+1]
   int32_t* cursor = base + E + 1;    // [E]
   int32_t* cbase = cursor + E;       // [E+1]
   int32_t* wcnt = cbase + E + 1;     // [nwarps][E]
   const int nwarps = blockDim.x / 32;
   const int warp = tid >> 5, lane = tid & 31;
-  const int npairs = T * K;
+
+  // expert of pair l (ids from shared memory when cached, else global)
+  auto expert_of = [&](int l, float* wsum) -> int {
+    const int t = l / K, j = l - t * K;
+    const float* wrow = A.topk_w ? A.topk_w + static_cast<int64_t>(t) * K : nullptr;
+    int32_t rowbuf[16];
+    const int32_t* row;
+    if (cache_idx) {
+      row = sidx + t * K;
+    } else {
+      for (int jj = 0; jj < K; ++jj) rowbuf[jj] = clamp_id(A.topk_idx[static_cast<int64_t>(t) * K + jj], E);
+      row = rowbuf;
+    }
+    if (row[j] == kBadId) report(A.status, HS_DEV_BAD_EXPERT);
+    return pair_expert(row, wrow, j, K, A.dup_mode, wsum);
+  };
 
   for (int e = tid; e < E; e += blockDim.x) {
     hist[e] = 0;
     cursor[e] = 0;
   }
+  for (int i = tid; i < A.n_dcount; i += blockDim.x) P.dcount[i] = 0u;
   __syncthreads();
-
-  // validity of pair l = t*K + j: expert in range and (dedupe) the occurrence
-  // that carries the token's weight for that expert.
-  auto pair_expert = [&](int l, float* wsum) -> int {
-    const int t = l / K, j = l - t * K;
-    const int64_t e64 = topk_idx[l];
-    if (e64 < 0) return -1;
-    if (e64 >= E) {
-      report(status, HS_DEV_BAD_EXPERT);
-      return -1;
-    }
-    const int e = static_cast<int>(e64);
-    const int64_t* row = topk_idx + static_cast<int64_t>(t) * K;
-    const float* wrow = topk_w ? topk_w + static_cast<int64_t>(t) * K : nullptr;
-    if (dup_mode == kDupKeepAll) {
-      if (wsum) *wsum = wrow ? wrow[j] : 1.f;
-    } else if (dup_mode == HS_DUP_SUM) {
-      for (int jj = 0; jj < j; ++jj)
-        if (row[jj] == e64) return -1;
-      float s = 0.f;
-      for (int jj = j; jj < K; ++jj)
-        if (row[jj] == e64) s += wrow ? wrow[jj] : 1.f;
-      if (wsum) *wsum = s;
-    } else {
-      for (int jj = j + 1; jj < K; ++jj)
-        if (row[jj] == e64) return -1;
-      if (wsum) *wsum = wrow ? wrow[j] : 1.f;
-    }
-    return e;
-  };
-
-  // pass 1: histogram
   for (int l = tid; l < npairs; l += blockDim.x) {
-    const int e = pair_expert(l, nullptr);
+    const int e = expert_of(l, nullptr);
     if (e >= 0) atomicAdd(&hist[e], 1);
   }
   __syncthreads();
-  // exclusive scans (pairs and chunks) by warp 0
   if (warp == 0) {
     int run = 0, crun = 0;
     for (int e0 = 0; e0 < E; e0 += 32) {
       const int e = e0 + lane;
-      const int h = e < E ? hist[e] : 0;
-      const int c = (h + CH - 1) / CH;
-      int x = h, y = c;
+      const int hh = e < E ? hist[e] : 0;
+      const int c = (hh + A.CH - 1) / A.CH;
+      int x = hh, y = c;
       for (int o = 1; o < 32; o <<= 1) {
         const int xv = __shfl_up_sync(0xffffffffu, x, o);
         const int yv = __shfl_up_sync(0xffffffffu, y, o);
@@ -277,7 +392,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __res
         }
       }
       if (e < E) {
-        base[e] = run + x - h;
+        base[e] = run + x - hh;
         cbase[e] = crun + y - c;
       }
       run += __shfl_sync(0xffffffffu, x, 31);
@@ -289,45 +404,50 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __res
     }
   }
   __syncthreads();
-  // chunk list and header
+  int my_slots = 0;
   for (int e = tid; e < E; e += blockDim.x) {
-    const int h = hist[e];
+    const int hh = hist[e];
+    my_slots += hh > 0;
     int cb = cbase[e];
-    for (int c = 0; c * CH < h; ++c, ++cb) {
+    for (int c = 0; c * A.CH < hh; ++c, ++cb) {
       P.chunk_expert[cb] = e;
-      P.chunk_pair0[cb] = pos_offset + base[e] + c * CH;
-      P.chunk_np[cb] = min(CH, h - c * CH);
+      P.chunk_pair0[cb] = A.pos_offset + base[e] + c * A.CH;
+      P.chunk_np[cb] = min(A.CH, hh - c * A.CH);
     }
   }
+  for (int o = 16; o > 0; o >>= 1) my_slots += __shfl_xor_sync(0xffffffffu, my_slots, o);
+  if (lane == 0) wcnt[warp] = my_slots;
+  __syncthreads();
   if (tid == 0) {
     int slots = 0;
-    for (int e = 0; e < E; ++e) slots += hist[e] > 0;
+    for (int w = 0; w < nwarps; ++w) slots += wcnt[w];
     P.hdr[0] = cbase[E];
     P.hdr[1] = slots;
     P.hdr[2] = base[E];
-    if (po.num_pos) *po.num_pos = base[E];
+    if (A.po.num_pos) *A.po.num_pos = base[E];
   }
-  if (po.expert_count)
-    for (int e = tid; e < E; e += blockDim.x) po.expert_count[e] = hist[e];
-  if (po.pos_to_expert)
-    for (int p = base[E] + tid; p < T * K; p += blockDim.x) po.pos_to_expert[p] = -1;
-  // shared-expert pairs occupy positions [0, T)
-  for (int t = tid; t < pos_offset; t += blockDim.x) {
+  __syncthreads();
+  if (A.po.expert_count)
+    for (int e = tid; e < E; e += blockDim.x) A.po.expert_count[e] = hist[e];
+  if (A.po.pos_to_expert)
+    for (int p = base[E] + tid; p < npairs; p += blockDim.x) A.po.pos_to_expert[p] = -1;
+  for (int t = tid; t < A.pos_offset; t += blockDim.x) {  // shared-expert pairs
     P.pair_token[t] = t;
     P.pair_wb[t] = 1.f;
-    P.pair_q[t] = 7;
+    P.pair_q[t] = 0;
+    P.sb2[t] = 127;
   }
-  // pass 2: stable positions, tile by tile (warp-major = pair order)
+  // stable positions, tile by tile (warp-major = pair order)
   const int tile = blockDim.x;
   for (int l0 = 0; l0 < npairs; l0 += tile) {
     const int l = l0 + tid;
     float wsum = 0.f;
-    const int e = l < npairs ? pair_expert(l, &wsum) : -1;
-    const unsigned m = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(m & ((1u << lane) - 1u));
+    const int e = l < npairs ? expert_of(l, &wsum) : -1;
+    const unsigned msk = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(msk & ((1u << lane) - 1u));
     for (int x = lane; x < E; x += 32) wcnt[warp * E + x] = 0;
     __syncwarp();
-    if (e >= 0 && rank == 0) wcnt[warp * E + e] = __popc(m);
+    if (e >= 0 && rank == 0) wcnt[warp * E + e] = __popc(msk);
     __syncthreads();
     for (int x = tid; x < E; x += blockDim.x) {
       int run = cursor[x];
@@ -343,20 +463,20 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __res
       const int t = l / K;
       int pos = -1;
       if (e >= 0) {
-        pos = pos_offset + base[e] + wcnt[warp * E + e] + rank;
+        pos = A.pos_offset + base[e] + wcnt[warp * E + e] + rank;
         const float wb = round_bf16(wsum);
+        const int q = act_prescale(wb);
         P.pair_token[pos] = t;
         P.pair_wb[pos] = wb;
-        P.pair_q[pos] = act_prescale(wb);
-        if (po.pos_to_expert) po.pos_to_expert[pos] = e;
+        P.pair_q[pos] = q;
+        P.sb2[pos] = static_cast<uint8_t>(127 - q);
+        if (A.po.pos_to_expert) A.po.pos_to_expert[pos] = e;
       }
       P.tok_pos[l] = pos;
     }
     __syncthreads();
   }
-  __syncthreads();
-  // sort each token's positions ascending (= ascending expert id), -1 last
-  if (!sort_tok) return;
+  if (!A.sort_tok) return;
   for (int t = tid; t < T; t += blockDim.x) {
     int32_t* row = P.tok_pos + static_cast<int64_t>(t) * K;
     for (int a = 1; a < K; ++a) {
@@ -372,436 +492,318 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int64_t* __res
   }
 }
 
+// Routed pair rows when T*K is too large for per-token position recomputation:
+// one CTA per routed pair copies its token's hi/lo rows (written by the plan).
+__global__ void __launch_bounds__(256) gather_kernel(Plan P, int T, int64_t P_max, int D) {
+  const int64_t p = T + static_cast<int64_t>(blockIdx.x);
+  if (p >= T + P.hdr[2]) return;
+  const int t = P.pair_token[p];
+  const uint4* hs = reinterpret_cast<const uint4*>(P.x8 + static_cast<int64_t>(t) * D);
+  const uint4* ls = reinterpret_cast<const uint4*>(P.x8 + (P_max + t) * D);
+  uint4* hd = reinterpret_cast<uint4*>(P.x8 + p * D);
+  uint4* ld = reinterpret_cast<uint4*>(P.x8 + (P_max + p) * D);
+  for (int i = threadIdx.x; i < D / 16; i += blockDim.x) {
+    hd[i] = hs[i];
+    ld[i] = ls[i];
+  }
+  if (threadIdx.x == 0) P.sb1[p] = P.sb1[t];
+}
 
 // ---------------------------------------------------------------------------
-// streaming units (gate/up and down)
+// tcgen05 units
 // ---------------------------------------------------------------------------
 struct UnitArgs {
   Plan P;
-  int T, CH;
+  int T, K, CH;
+  int64_t P_max;
   int n_sh_chunks;  // shared-expert chunks (0 when the shared expert is off)
+  int use_shared;
+  __nv_bfloat16* out;
+  float* out_f32;
   int32_t* status;
 };
-
-struct Smem {
-  uint8_t* a;       // kStages x kStageA, 1024-aligned (128B swizzle)
-  uint8_t* b;       // kStages x b_stage
-  uint8_t* sc;      // per-unit scale rows
-  uint64_t* full;   // [kStages] producer -> consumers (TMA transaction bytes)
-  uint64_t* empty;  // [kStages] consumers -> producer (one arrive per warp)
-  uint64_t* sbar;   // scale rows landed
-  int b_stage;
-};
-
-constexpr int kPitchGU = 576;     // gate/up B row pitch: 512 B + 64 B pad
-constexpr int kPitchDN = 1088;    // down B row pitch: 1024 B + 64 B pad
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
 }
 
-__device__ __forceinline__ Smem carve(uint8_t* raw, int b_stage, int sc_bytes) {
-  Smem s;
-  uint8_t* base = align1024(raw);
-  s.a = base;
-  s.b = base + kStages * kStageA;
-  s.sc = s.b + kStages * b_stage;
-  uint8_t* bars = s.sc + ((sc_bytes + 127) & ~127);
-  s.full = reinterpret_cast<uint64_t*>(bars);
-  s.empty = s.full + kStages;
-  s.sbar = s.empty + kStages;
-  s.b_stage = b_stage;
-  return s;
-}
-
-__device__ __forceinline__ void init_barriers(const Smem& s) {
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], kConsumerWarps);
-    }
-    mbar_init(s.sbar, 1);
-    fence_mbar_init();
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
-  __syncthreads();
-}
-
-// One group of 32 k columns for 16 weight rows (lo = g, hi = g + 8) and up to
-// kMaxNT tiles of 8 pairs. wlo/whi: this thread's 4 (FP4) or 8 (FP8) bytes of
-// each row; K order inside the group is permuted identically on both operands
-// (thread c owns logical columns 8c..8c+7), so the dot products are exact sums
-// of the same terms. Accumulates (scale_lo, scale_hi) * partial into acc.
-template <bool kFP8>
-__device__ __forceinline__ void group_mma(uint32_t wlo0, uint32_t wlo1, uint32_t whi0, uint32_t whi1, uint32_t bbase,
-                                          int pitch, int nt_used, float slo, float shi, float (&acc)[kMaxNT][4]) {
-  uint32_t x0, x1, x2, x3, y0, y1, y2, y3;
-  if (kFP8) {
-    e4m3x4_to_f16x2x2(wlo0, x0, x1);
-    e4m3x4_to_f16x2x2(wlo1, x2, x3);
-    e4m3x4_to_f16x2x2(whi0, y0, y1);
-    e4m3x4_to_f16x2x2(whi1, y2, y3);
-  } else {
-    e2m1x8_to_f16x2x4(wlo0, x0, x1, x2, x3);
-    e2m1x8_to_f16x2x4(whi0, y0, y1, y2, y3);
-  }
-#pragma unroll
-  for (int nt = 0; nt < kMaxNT; ++nt) {
-    if (nt < nt_used) {
-      const uint4 bv = lds128(bbase + nt * 8 * pitch);
-      float t[4] = {0.f, 0.f, 0.f, 0.f};
-      mma_f16(t, x0, y0, x1, y1, bv.x, bv.y);
-      mma_f16(t, x2, y2, x3, y3, bv.z, bv.w);
-      acc[nt][0] = fmaf(t[0], slo, acc[nt][0]);
-      acc[nt][1] = fmaf(t[1], slo, acc[nt][1]);
-      acc[nt][2] = fmaf(t[2], shi, acc[nt][2]);
-      acc[nt][3] = fmaf(t[3], shi, acc[nt][3]);
-    }
-  }
-}
-
-// Producer: lane 0 of the last warp. Streams nk stages; each stage is two TMA
-// boxes (x0a/x0b at rows ya/yb) plus np bulk-copied B rows.
-struct StageSrc {
-  const CUtensorMap* map;
-  int ya, yb;          // box rows
-  int xa_mul, xb_add;  // box a x = kc*xa_mul, box b x = kc*xa_mul + xb_add
-  const __half* bsrc;  // B base for pair row 0 (row r: + r_off(r))
-  int brow_elems;      // B elements per row per stage
+template <int NT, int BOXES>
+struct SmemLayout {
+  static constexpr int kA = 2 * kBoxBytes;             // two weight boxes per stage
+  static constexpr int kB = BOXES * 2 * NT * 1024;     // hi and lo atoms per k-box
+  static constexpr int kSF = 2 * 512;                  // two scale atoms per stage
+  static constexpr int kStage = kA + kB + kSF;
+  // three stages when two CTAs still fit on an SM (2 x 113 KB), else two
+  static constexpr int kNumStages = (1024 + kStages * kStage + 768 <= 113 * 1024) ? kStages : 2;
+  static constexpr int kBytes = 1024 + kNumStages * kStage + 512 + 256;
 };
 
-// Consumer wait-or-abort helper: returns false (and reports) on timeout.
-__device__ __forceinline__ bool wait_full(const Smem& s, int kc, int32_t* status) {
-  if (mbar_wait(&s.full[kc % kStages], (kc / kStages) & 1)) return true;
-  report(status, HS_DEV_TIMEOUT);
-  return false;
-}
+struct Bars {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t accum;
+  uint32_t tmem;
+  int32_t last;
+};
 
-__device__ __forceinline__ void release(const Smem& s, int kc) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(&s.empty[kc % kStages]);
-}
-
-template <bool kFP8>
-__device__ __forceinline__ void gateup_unit(const Desc& d, const UnitArgs& a, const Smem& s, int e, int pair0, int np,
-                                            int rt) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int D = d.D;
-  constexpr int KS = kFP8 ? 128 : 256;  // k columns per stage (one 128-byte box)
-  const int nk = D / KS;
-  constexpr int rowb = KS * 2;          // B bytes per pair row per stage
-  const int SB = D / 32;                // FP4 scale bytes per weight row
-  const int y1 = kFP8 ? rt * kRows : (2 * e) * d.I + rt * kRows;
-  const int y3 = kFP8 ? d.I_sh + rt * kRows : (2 * e + 1) * d.I + rt * kRows;
-  const CUtensorMap* tw = kFP8 ? &d.tm_sw13 : &d.tm_w13;
-
-  if (warp == kConsumerWarps) {
-    if (lane == 0) {
-      if (!kFP8) {
-        mbar_arrive_expect_tx(s.sbar, 2 * kRows * SB);
-        tma_load_2d(s.sc, &d.tm_s13, s.sbar, 0, y1);
-        tma_load_2d(s.sc + kRows * SB, &d.tm_s13, s.sbar, 0, y3);
-      }
-      for (int kc = 0; kc < nk; ++kc) {
-        const int st = kc % kStages;
-        if (kc >= kStages && !mbar_wait(&s.empty[st], ((kc / kStages) - 1) & 1)) {
-          report(a.status, HS_DEV_TIMEOUT);
-          break;
-        }
-        uint8_t* A = s.a + st * kStageA;
-        uint8_t* B = s.b + st * s.b_stage;
-        mbar_arrive_expect_tx(&s.full[st], kStageA + np * rowb);
-        tma_load_2d(A, tw, &s.full[st], kc * 128, y1);
-        tma_load_2d(A + kBoxBytes, tw, &s.full[st], kc * 128, y3);
-        for (int r = 0; r < np; ++r) {
-          const int t = a.P.pair_token[pair0 + r];
-          bulk_load(B + r * kPitchGU, a.P.hx + static_cast<int64_t>(t) * D + kc * KS, rowb, &s.full[st]);
-        }
-      }
+// out[t][tile rows] = bf16( bf16(sum of the token's routed partial rows in
+// ascending expert order) + bf16(shared-expert row) ), for every token.
+__device__ __noinline__ void finalize_tile(const UnitArgs& a, int D, int tile) {
+  for (int i = threadIdx.x; i < a.T * kM; i += blockDim.x) {
+    const int t = i / kM;
+    const int dd = tile * kM + (i - t * kM);
+    const int32_t* pos = a.P.tok_pos + static_cast<int64_t>(t) * a.K;
+    float r = 0.f;
+    for (int j = 0; j < a.K; ++j) {
+      const int p = pos[j];
+      if (p < 0) break;
+      r += __ldcg(a.P.out_part + static_cast<int64_t>(p) * D + dd);
     }
-    return;
-  }
-
-  const int g = lane >> 2, c = lane & 3;
-  const int rlo = 16 * warp + g, rhi = rlo + 8;
-  const int nt_used = (np + 7) >> 3;
-  float gate[kMaxNT][4], up[kMaxNT][4];
-#pragma unroll
-  for (int i = 0; i < kMaxNT; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) gate[i][j] = up[i][j] = 0.f;
-
-  if (!kFP8 && !mbar_wait(s.sbar, 0)) {
-    report(a.status, HS_DEV_TIMEOUT);
-    return;
-  }
-  const uint32_t a0 = smem_u32(s.a), b0 = smem_u32(s.b), sc0 = smem_u32(s.sc);
-  for (int kc = 0; kc < nk; ++kc) {
-    if (!wait_full(s, kc, a.status)) return;
-    const int st = kc % kStages;
-    const uint32_t A = a0 + st * kStageA;
-    const uint32_t B = b0 + st * s.b_stage + g * kPitchGU + c * 16;
-    if (!kFP8) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint32_t sw = ((q ^ g) << 4) + 4 * c;
-        const uint32_t w1l = lds32(A + rlo * 128 + sw), w1h = lds32(A + rhi * 128 + sw);
-        const uint32_t w3l = lds32(A + kBoxBytes + rlo * 128 + sw), w3h = lds32(A + kBoxBytes + rhi * 128 + sw);
-        const int G = kc * 8 + q;
-        const float s1l = e8m0_to_f32_torch(lds8(sc0 + rlo * SB + G));
-        const float s1h = e8m0_to_f32_torch(lds8(sc0 + rhi * SB + G));
-        const float s3l = e8m0_to_f32_torch(lds8(sc0 + (kRows + rlo) * SB + G));
-        const float s3h = e8m0_to_f32_torch(lds8(sc0 + (kRows + rhi) * SB + G));
-        group_mma<false>(w1l, 0u, w1h, 0u, B + q * 64, kPitchGU, nt_used, s1l, s1h, gate);
-        group_mma<false>(w3l, 0u, w3h, 0u, B + q * 64, kPitchGU, nt_used, s3l, s3h, up);
-      }
-    } else {
-      const int nbc = D / 128;  // scale blocks along k
-      const int br = (rt * kRows) / 128;
-      const float s1 = e8m0_to_f32_shift(d.sh_s13[(br)*nbc + kc]);
-      const float s3 = e8m0_to_f32_shift(d.sh_s13[((d.I_sh / 128) + br) * nbc + kc]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t ch = 2 * q + (c >> 1);
-        const uint32_t sw = ((ch ^ g) << 4) + (c & 1) * 8;
-        const uint2 w1l = lds64(A + rlo * 128 + sw), w1h = lds64(A + rhi * 128 + sw);
-        const uint2 w3l = lds64(A + kBoxBytes + rlo * 128 + sw), w3h = lds64(A + kBoxBytes + rhi * 128 + sw);
-        group_mma<true>(w1l.x, w1l.y, w1h.x, w1h.y, B + q * 64, kPitchGU, nt_used, s1, s1, gate);
-        group_mma<true>(w3l.x, w3l.y, w3h.x, w3h.y, B + q * 64, kPitchGU, nt_used, s3, s3, up);
-      }
-    }
-    release(s, kc);
-  }
-
-  // epilogue: bf16(gate), bf16(up) -> SwiGLU(clamp 10) -> bf16 -> * bf16(w) -> bf16
-  const int Iu = kFP8 ? d.I_sh : d.I;
-  (void)Iu;
-  const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
-#pragma unroll
-  for (int nt = 0; nt < kMaxNT; ++nt) {
-    if (nt >= nt_used) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = nt * 8 + 2 * c + (j & 1);
-      if (n >= np) continue;
-      const int r = (j < 2) ? rlo : rhi;
-      const int p = pair0 + n;
-      const int t = a.P.pair_token[p];
-      const float inv = exp2i(-a.P.tok_e[t]);
-      const float gf = round_bf16(gate[nt][j] * inv);
-      const float uf = round_bf16(up[nt][j] * inv);
-      const float gc = gf > 10.f ? 10.f : gf;
-      const float uc = uf > 10.f ? 10.f : (uf < -10.f ? -10.f : uf);
-      const float sig = 1.f / (1.f + expf(-gc));
-      float av = round_bf16((gc * sig) * uc);
-      if (!kFP8) av = round_bf16(av * a.P.pair_wb[p]);
-      a.P.act[static_cast<int64_t>(p) * I_act + rt * kRows + r] = __float2half_rn(av * exp2i(a.P.pair_q[p]));
-    }
+    if (a.out_f32) a.out_f32[static_cast<int64_t>(t) * D + dd] = r;
+    float o = round_bf16(r);
+    if (a.use_shared) o += round_bf16(__ldcg(a.P.out_part + static_cast<int64_t>(t) * D + dd));
+    a.out[static_cast<int64_t>(t) * D + dd] = __float2bfloat16_rn(o);
   }
 }
 
-template <bool kFP8>
-__device__ __forceinline__ void down_unit(const Desc& d, const UnitArgs& a, const Smem& s, int e, int pair0, int np,
-                                          int dt) {
+// One unit on the tensor cores. kDown = false: gate/up (A boxes = w1 and w3,
+// one 128-column k-box per stage); kDown = true: down (A boxes = two k-boxes
+// of w2). kFP8 selects the shared expert's E4M3 weights.
+template <bool kDown, bool kFP8, int NT>
+__device__ __forceinline__ void run_unit(const Desc& d, const CallMaps& cm, const UnitArgs& a, int e, int pair0,
+                                         int np, int tile) {
+  constexpr int BOXES = kDown ? 2 : 1;
+  using L = SmemLayout<NT, BOXES>;
+  constexpr int S_ = L::kNumStages;
+  constexpr int N = 16 * NT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* stages = base;
+  uint8_t* sfb = base + S_ * L::kStage;
+  Bars* bars = reinterpret_cast<Bars*>(sfb + 512);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = d.D;
   const int Iu = kFP8 ? d.I_sh : d.I;
-  constexpr int KS = kFP8 ? 256 : 512;  // k columns per stage (two 128-byte boxes)
-  const int nk = Iu / KS;
-  constexpr int rowb = KS * 2;
-  const int SB = d.I / 32;  // FP4 scale bytes per row
-  const int y = kFP8 ? dt * kRows : e * D + dt * kRows;
-  const CUtensorMap* tw = kFP8 ? &d.tm_sw2 : &d.tm_w2;
-  const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
+  const int nk = kDown ? Iu / 256 : D / 128;
+  const uint32_t tx_box = kFP8 ? kBoxBytes : kBoxBytes / 2;  // packed e2m1 counts half
+  const uint32_t tx = 2 * tx_box + L::kB + L::kSF;
+  const uint8_t* sbv = kDown ? a.P.sb2 : a.P.sb1;
 
-  if (warp == kConsumerWarps) {
+  // ---- setup: barriers, TMEM, B scale factors ----
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S_; ++i) {
+      mbar_init(&bars->full[i], 1);
+      mbar_init(&bars->empty[i], 1);
+    }
+    mbar_init(&bars->accum, 1);
+    bars->last = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) tc5::tmem_alloc(&bars->tmem, kTmemCols);
+  if (threadIdx.x < 128) {
+    // SFB atom: word (m0, m1) = scale of B row n = m0 + 32*m1 in all 4 k-blocks
+    const int m0 = threadIdx.x >> 2, m1 = threadIdx.x & 3;
+    const int n = m0 + 32 * m1;
+    uint32_t b = 127u;
+    if (n < N) {
+      const int r = n % (8 * NT);
+      if (r < np) b = sbv[pair0 + r];
+    }
+    *reinterpret_cast<uint32_t*>(sfb + m0 * 16 + m1 * 4) = b * 0x01010101u;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t tmem = bars->tmem;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      if (!kFP8) {
-        mbar_arrive_expect_tx(s.sbar, kRows * SB);
-        tma_load_2d(s.sc, &d.tm_s2, s.sbar, 0, y);
+      const CUtensorMap* wm = kDown ? (kFP8 ? &d.tm_sw2 : &d.tm_w2) : (kFP8 ? &d.tm_sw13 : &d.tm_w13);
+      const CUtensorMap* bm = kDown ? &cm.tm_act8 : &cm.tm_x8;
+      int ya = 0, yb = 0;
+      if (!kDown) {
+        ya = kFP8 ? tile * kM : (2 * e) * d.I + tile * kM;
+        yb = kFP8 ? d.I_sh + tile * kM : (2 * e + 1) * d.I + tile * kM;
+      } else {
+        ya = yb = kFP8 ? tile * kM : e * D + tile * kM;
       }
       for (int kc = 0; kc < nk; ++kc) {
-        const int st = kc % kStages;
-        if (kc >= kStages && !mbar_wait(&s.empty[st], ((kc / kStages) - 1) & 1)) {
+        const int st = kc % S_;
+        if (kc >= S_ && !mbar_wait(&bars->empty[st], ((kc / S_) - 1) & 1)) {
           report(a.status, HS_DEV_TIMEOUT);
           break;
         }
-        uint8_t* A = s.a + st * kStageA;
-        uint8_t* B = s.b + st * s.b_stage;
-        mbar_arrive_expect_tx(&s.full[st], kStageA + np * rowb);
-        tma_load_2d(A, tw, &s.full[st], kc * 256, y);
-        tma_load_2d(A + kBoxBytes, tw, &s.full[st], kc * 256 + 128, y);
-        for (int r = 0; r < np; ++r)
-          bulk_load(B + r * kPitchDN, a.P.act + static_cast<int64_t>(pair0 + r) * I_act + kc * KS, rowb, &s.full[st]);
+        uint8_t* S = stages + st * L::kStage;
+        uint8_t* Bs = S + L::kA;
+        uint8_t* SF = Bs + L::kB;
+        mbar_arrive_expect_tx(&bars->full[st], tx);
+        const int xa = kDown ? kc * 256 : kc * 128;
+        tma_load_2d(S, wm, &bars->full[st], xa, ya);
+        tma_load_2d(S + kBoxBytes, wm, &bars->full[st], kDown ? xa + 128 : xa, yb);
+        for (int b = 0; b < BOXES; ++b)
+          for (int pl = 0; pl < 2; ++pl)
+            for (int nt = 0; nt < NT; ++nt)
+              tma_load_2d(Bs + ((b * 2 + pl) * NT + nt) * 1024, bm, &bars->full[st], xa + b * 128,
+                          static_cast<int>(pl * a.P_max) + pair0 + 8 * nt);
+        for (int i = 0; i < 2; ++i) {
+          const uint8_t* atom;
+          if (!kDown) {
+            atom = kFP8 ? d.sh_s13a + ((static_cast<int64_t>(i) * (d.I_sh / kM) + tile) * (D / kM) + kc) * 512
+                        : d.s13a + (((static_cast<int64_t>(e) * 2 + i) * (d.I / kM) + tile) * (D / kM) + kc) * 512;
+          } else {
+            atom = kFP8 ? d.sh_s2a + (static_cast<int64_t>(tile) * (d.I_sh / kM) + kc * 2 + i) * 512
+                        : d.s2a + ((static_cast<int64_t>(e) * (D / kM) + tile) * (d.I / kM) + kc * 2 + i) * 512;
+          }
+          bulk_load(SF + i * 512, atom, 512, &bars->full[st]);
+        }
       }
     }
-    return;
-  }
-
-  const int g = lane >> 2, c = lane & 3;
-  const int rlo = 16 * warp + g, rhi = rlo + 8;
-  const int nt_used = (np + 7) >> 3;
-  float acc[kMaxNT][4];
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      tc5::cp_sf_32x128b(tmem + kSfbCol, tc5::sdesc_sf(smem_u32(sfb)));
+      const uint32_t afmt = kFP8 ? 0u : 5u;
+      for (int kc = 0; kc < nk; ++kc) {
+        const int st = kc % S_;
+        if (!mbar_wait(&bars->full[st], (kc / S_) & 1)) {
+          report(a.status, HS_DEV_TIMEOUT);
+          break;
+        }
+        tc5::fence_after_sync();
+        uint8_t* S = stages + st * L::kStage;
+        const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
+        const uint32_t sfa0 = tmem + kSfaCol + st * 8;
+        tc5::cp_sf_32x128b(sfa0, tc5::sdesc_sf(sSF));
+        tc5::cp_sf_32x128b(sfa0 + 4, tc5::sdesc_sf(sSF + 512));
 #pragma unroll
-  for (int i = 0; i < kMaxNT; ++i)
+        for (int i = 0; i < 2; ++i) {
+          const uint64_t ad = tc5::sdesc_sw128(sA + i * kBoxBytes);
+          const uint64_t bd = tc5::sdesc_sw128(sB + (kDown ? i * 2 * NT * 1024 : 0));
+          const uint32_t dcol = tmem + (kDown ? 0 : (i ? kAccUp : 0));
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-
-  if (!kFP8 && !mbar_wait(s.sbar, 0)) {
-    report(a.status, HS_DEV_TIMEOUT);
-    return;
-  }
-  const uint32_t a0 = smem_u32(s.a), b0 = smem_u32(s.b), sc0 = smem_u32(s.sc);
-  for (int kc = 0; kc < nk; ++kc) {
-    if (!wait_full(s, kc, a.status)) return;
-    const int st = kc % kStages;
-    const uint32_t A = a0 + st * kStageA;
-    const uint32_t B = b0 + st * s.b_stage + g * kPitchDN + c * 16;
-    if (!kFP8) {
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t id = tc5::idesc_mxf8f6f4(afmt, N, j, j);
+            const uint32_t acc = (kc > 0 || j > 0 || (kDown && i > 0)) ? 1u : 0u;
+            tc5::mma_mxf8f6f4(dcol, ad + 2 * j, bd + 2 * j, id, acc, (sfa0 + 4 * i) | (static_cast<uint32_t>(j) << 30),
+                              (tmem + kSfbCol) | (static_cast<uint32_t>(j) << 30));
+          }
+        }
+        tc5::commit(&bars->empty[st]);
+      }
+      tc5::commit(&bars->accum);
+    }
+  } else {
+    // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31) ----------------
+    const int row = 32 * warp + lane;  // weight row within the tile
+    if (!mbar_wait(&bars->accum, 0)) report(a.status, HS_DEV_TIMEOUT);
+    tc5::fence_after_sync();
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    float c0[N];
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const uint32_t box = (q >> 3) * kBoxBytes;
-        const uint32_t sw = box + (((q & 7) ^ g) << 4) + 4 * c;
-        const uint32_t wl = lds32(A + rlo * 128 + sw), wh = lds32(A + rhi * 128 + sw);
-        const int G = kc * 16 + q;
-        const float sl = e8m0_to_f32_torch(lds8(sc0 + rlo * SB + G));
-        const float sh = e8m0_to_f32_torch(lds8(sc0 + rhi * SB + G));
-        group_mma<false>(wl, 0u, wh, 0u, B + q * 64, kPitchDN, nt_used, sl, sh, acc);
+    for (int q = 0; q < NT; ++q) {
+      float v[16];
+      tc5::ld_32x32b_x16(lane_base + q * 16, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) c0[q * 16 + i] = v[i];
+    }
+    if (!kDown) {
+      float c1[N];
+#pragma unroll
+      for (int q = 0; q < NT; ++q) {
+        float v[16];
+        tc5::ld_32x32b_x16(lane_base + kAccUp + q * 16, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c1[q * 16 + i] = v[i];
+      }
+      tc5::wait_ld();
+      const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
+      uint8_t* hi_plane = a.P.act8;
+      uint8_t* lo_plane = a.P.act8 + a.P_max * I_act;
+      const int col = tile * kM + row;
+#pragma unroll
+      for (int r = 0; r < 8 * NT; ++r) {
+        if (r < np) {
+          const int p = pair0 + r;
+          // reference: gate/up rounded to bf16, SwiGLU with clamp 10 in f32,
+          // rounded to bf16, times the bf16 routing weight, rounded to bf16
+          const float gf = round_bf16(c0[r] + c0[8 * NT + r]);
+          const float uf = round_bf16(c1[r] + c1[8 * NT + r]);
+          const float gc = gf > 10.f ? 10.f : gf;
+          const float uc = uf > 10.f ? 10.f : (uf < -10.f ? -10.f : uf);
+          const float sig = 1.f / (1.f + expf(-gc));
+          float av = round_bf16((gc * sig) * uc);
+          if (!kFP8) av = round_bf16(av * a.P.pair_wb[p]);
+          const float v = av * exp2i(a.P.pair_q[p]);
+          const __nv_fp8_storage_t hb = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+          const __half_raw hr = __nv_cvt_fp8_to_halfraw(hb, __NV_E4M3);
+          const float hf = __half2float(*reinterpret_cast<const __half*>(&hr));
+          const __nv_fp8_storage_t lb = __nv_cvt_float_to_fp8(v - hf, __NV_SATFINITE, __NV_E4M3);
+          hi_plane[static_cast<int64_t>(p) * I_act + col] = hb;
+          lo_plane[static_cast<int64_t>(p) * I_act + col] = lb;
+        }
       }
     } else {
-      const int nbc = d.I_sh / 128;
-      const int br = (dt * kRows) / 128;
+      tc5::wait_ld();
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint32_t box = (q >> 2) * kBoxBytes;
-        const uint32_t ch = 2 * (q & 3) + (c >> 1);
-        const uint32_t sw = box + ((ch ^ g) << 4) + (c & 1) * 8;
-        const uint2 wl = lds64(A + rlo * 128 + sw), wh = lds64(A + rhi * 128 + sw);
-        const float sv = e8m0_to_f32_shift(d.sh_s2[br * nbc + kc * 2 + (q >> 2)]);
-        group_mma<true>(wl.x, wl.y, wh.x, wh.y, B + q * 64, kPitchDN, nt_used, sv, sv, acc);
+      for (int r = 0; r < 8 * NT; ++r) {
+        if (r < np) {
+          const int p = pair0 + r;
+          a.P.out_part[static_cast<int64_t>(p) * D + tile * kM + row] = c0[r] + c0[8 * NT + r];
+        }
       }
     }
-    release(s, kc);
   }
 
-#pragma unroll
-  for (int nt = 0; nt < kMaxNT; ++nt) {
-    if (nt >= nt_used) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = nt * 8 + 2 * c + (j & 1);
-      if (n >= np) continue;
-      const int r = (j < 2) ? rlo : rhi;
-      const int p = pair0 + n;
-      a.P.out_part[static_cast<int64_t>(p) * D + dt * kRows + r] = acc[nt][j] * exp2i(-a.P.pair_q[p]);
+  // ---- teardown: every tcgen05 op has completed (accum barrier / ld waits) ----
+  tc5::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc5::fence_after_sync();
+    tc5::tmem_dealloc(tmem, kTmemCols);
+  }
+
+  if (kDown) {
+    // ---- finalize this 128-row slice of D if this CTA is the last one on it ----
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t total = static_cast<uint32_t>(a.n_sh_chunks + a.P.hdr[0]);
+      bars->last = atomicAdd(&a.P.dcount[tile], 1u) == total - 1u;
+    }
+    __syncthreads();
+    if (bars->last) {
+      __threadfence();
+      finalize_tile(a, D, tile);
     }
   }
 }
 
-__global__ void __launch_bounds__(kThreads) gateup_kernel(const __grid_constant__ Desc d, UnitArgs a) {
-  extern __shared__ uint8_t smem_raw[];
+template <bool kDown, int NT>
+__global__ void __launch_bounds__(kThreads) unit_kernel(const __grid_constant__ Desc d,
+                                                           const __grid_constant__ CallMaps cm, UnitArgs a) {
   int u = blockIdx.x;
-  const int sh_tiles = d.has_shared ? d.I_sh / kRows : 0;
-  const int n_sh_units = a.n_sh_chunks * sh_tiles;
-  bool shared;
-  int e = 0, pair0, np, rt;
+  const int tiles_sh = kDown ? d.D / kM : (d.has_shared ? d.I_sh / kM : 0);
+  const int tiles = kDown ? d.D / kM : d.I / kM;
+  const int n_sh_units = a.n_sh_chunks * tiles_sh;
   if (u < n_sh_units) {
-    shared = true;
-    const int c = u / sh_tiles;
-    rt = u - c * sh_tiles;
-    pair0 = c * a.CH;
-    np = min(a.CH, a.T - pair0);
-  } else {
-    shared = false;
-    u -= n_sh_units;
-    const int tiles = d.I / kRows;
-    const int c = u / tiles;
-    rt = u - c * tiles;
-    if (c >= a.P.hdr[0]) return;
-    e = a.P.chunk_expert[c];
-    pair0 = a.P.chunk_pair0[c];
-    np = a.P.chunk_np[c];
+    const int c = u / tiles_sh;
+    const int tile = u - c * tiles_sh;
+    const int pair0 = c * a.CH;
+    run_unit<kDown, true, NT>(d, cm, a, 0, pair0, min(a.CH, a.T - pair0), tile);
+    return;
   }
-  const int nt_max = (a.CH + 7) >> 3;
-  const Smem s = carve(smem_raw, nt_max * 8 * kPitchGU, 2 * kRows * (d.D / 32));
-  init_barriers(s);
-  if (threadIdx.x == kConsumerWarps * 32) {
-    prefetch_tensormap(shared ? &d.tm_sw13 : &d.tm_w13);
-    if (!shared) prefetch_tensormap(&d.tm_s13);
+  u -= n_sh_units;
+  const int c = u / tiles;
+  const int tile = u - c * tiles;
+  if (c >= a.P.hdr[0]) {
+    // no unit at all (every pair skipped, no shared expert): the first chunk
+    // slot of each tile writes the all-zero result
+    if (kDown && c == 0 && a.n_sh_chunks == 0) finalize_tile(a, d.D, tile);
+    return;
   }
-  if (shared)
-    gateup_unit<true>(d, a, s, e, pair0, np, rt);
-  else
-    gateup_unit<false>(d, a, s, e, pair0, np, rt);
-}
-
-__global__ void __launch_bounds__(kThreads) down_kernel(const __grid_constant__ Desc d, UnitArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  int u = blockIdx.x;
-  const int tiles = d.D / kRows;
-  const int n_sh_units = a.n_sh_chunks * tiles;
-  bool shared;
-  int e = 0, pair0, np, dt;
-  if (u < n_sh_units) {
-    shared = true;
-    const int c = u / tiles;
-    dt = u - c * tiles;
-    pair0 = c * a.CH;
-    np = min(a.CH, a.T - pair0);
-  } else {
-    shared = false;
-    u -= n_sh_units;
-    const int c = u / tiles;
-    dt = u - c * tiles;
-    if (c >= a.P.hdr[0]) return;
-    e = a.P.chunk_expert[c];
-    pair0 = a.P.chunk_pair0[c];
-    np = a.P.chunk_np[c];
-  }
-  const int nt_max = (a.CH + 7) >> 3;
-  const Smem s = carve(smem_raw, nt_max * 8 * kPitchDN, kRows * (d.I / 32));
-  init_barriers(s);
-  if (threadIdx.x == kConsumerWarps * 32) {
-    prefetch_tensormap(shared ? &d.tm_sw2 : &d.tm_w2);
-    if (!shared) prefetch_tensormap(&d.tm_s2);
-  }
-  if (shared)
-    down_unit<true>(d, a, s, e, pair0, np, dt);
-  else
-    down_unit<false>(d, a, s, e, pair0, np, dt);
-}
-
-// out[t] = bf16( bf16(sum of routed partials, ascending expert) + bf16(shared) )
-__global__ void __launch_bounds__(256) finalize_kernel(Plan P, int T, int K, int D, int use_shared,
-                                                       __nv_bfloat16* __restrict__ out, float* __restrict__ out_f32) {
-  const int t = blockIdx.y;
-  const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
-  if (d >= D) return;
-  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-  const int32_t* pos = P.tok_pos + static_cast<int64_t>(t) * K;
-  for (int j = 0; j < K; ++j) {
-    const int p = pos[j];
-    if (p < 0) break;
-    const float4 v = *reinterpret_cast<const float4*>(P.out_part + static_cast<int64_t>(p) * D + d);
-    r.x += v.x;
-    r.y += v.y;
-    r.z += v.z;
-    r.w += v.w;
-  }
-  if (out_f32) *reinterpret_cast<float4*>(out_f32 + static_cast<int64_t>(t) * D + d) = r;
-  float o[4] = {round_bf16(r.x), round_bf16(r.y), round_bf16(r.z), round_bf16(r.w)};
-  if (use_shared) {
-    const float4 sv = *reinterpret_cast<const float4*>(P.out_part + static_cast<int64_t>(t) * D + d);
-    o[0] += round_bf16(sv.x);
-    o[1] += round_bf16(sv.y);
-    o[2] += round_bf16(sv.z);
-    o[3] += round_bf16(sv.w);
-  }
-  __nv_bfloat16* dst = out + static_cast<int64_t>(t) * D + d;
-  dst[0] = __float2bfloat16_rn(o[0]);
-  dst[1] = __float2bfloat16_rn(o[1]);
-  dst[2] = __float2bfloat16_rn(o[2]);
-  dst[3] = __float2bfloat16_rn(o[3]);
+  run_unit<kDown, false, NT>(d, cm, a, a.P.chunk_expert[c], a.P.chunk_pair0[c], a.P.chunk_np[c], tile);
 }
 
 // ---------------------------------------------------------------------------
@@ -861,18 +863,17 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2D uint8 tensor map: rows x inner bytes, row pitch = inner bytes.
-static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner,
-                    uint32_t box_rows, bool swizzle) {
+// 2D map: `cols` elements per row, row pitch `pitch` bytes, box cols x rows, 128B swizzle.
+static int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
+                    uint64_t pitch, uint32_t box_cols, uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return HS_ERR_UNSUPPORTED;
-  cuuint64_t dims[2] = {inner, rows};
-  cuuint64_t strides[1] = {inner};
-  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_last_cuda_error(static_cast<int>(r));
     return HS_ERR_CUDA;
@@ -881,27 +882,54 @@ static int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t r
 }
 
 static bool dim_ok(int64_t v, int64_t mult, int64_t lo, int64_t hi) { return v % mult == 0 && v >= lo && v <= hi; }
+static bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
-// The largest dynamic shared memory any launch can ask for (NT = 3, D = I = 8192).
-constexpr int kMaxDynSmem = 200 * 1024;
-
-// Raise the kernels' dynamic shared-memory limit once per device (a host-side
-// function attribute; safe to call before or during stream capture).
-static int opt_in_smem() {
+template <bool kDown, int NT>
+static int launch_units(const Desc& d, const CallMaps& cm, const UnitArgs& a, int64_t units, cudaStream_t st) {
+  constexpr int bytes = SmemLayout<NT, kDown ? 2 : 1>::kBytes;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   HS_CUDA_CHECK(cudaGetDevice(&dev));
   const uint64_t bit = 1ull << (dev & 63);
-  if (done.load() & bit) return HS_OK;
-  HS_CUDA_CHECK(cudaFuncSetAttribute(gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem));
-  HS_CUDA_CHECK(cudaFuncSetAttribute(down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem));
-  HS_CUDA_CHECK(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024));
-  done.fetch_or(bit);
-  return HS_OK;
+  if (!(done.load() & bit)) {
+    HS_CUDA_CHECK(cudaFuncSetAttribute(unit_kernel<kDown, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.fetch_or(bit);
+  }
+  unit_kernel<kDown, NT><<<static_cast<unsigned>(units), kThreads, bytes, st>>>(d, cm, a);
+  return check_launch();
 }
 
-static int smem_gateup(int NT, int D) { return 1024 + kStages * kStageA + kStages * NT * 8 * kPitchGU + 2 * kRows * (D / 32) + 256; }
-static int smem_down(int NT, int I) { return 1024 + kStages * kStageA + kStages * NT * 8 * kPitchDN + kRows * (I / 32) + 256; }
+template <bool kDown>
+static int launch_nt(int NT, const Desc& d, const CallMaps& cm, const UnitArgs& a, int64_t units, cudaStream_t st) {
+  switch (NT) {
+    case 1:
+      return launch_units<kDown, 1>(d, cm, a, units, st);
+    case 2:
+      return launch_units<kDown, 2>(d, cm, a, units, st);
+    default:
+      return launch_units<kDown, 3>(d, cm, a, units, st);
+  }
+}
+
+static int plan_smem(int E, int npairs) {
+  return static_cast<int>(((npairs <= kLocalPairs ? npairs : 0) + 4 * E + 2 + (kPlanThreads / 32) * E) *
+                          sizeof(int32_t));
+}
+
+static int launch_plan(const PlanArgs& pa, const Plan& P, int grid, cudaStream_t st) {
+  const int smem = plan_smem(pa.E, pa.T * pa.K);
+  if (smem > 200 * 1024) return HS_ERR_BAD_SHAPE;
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  HS_CUDA_CHECK(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(done.load() & bit)) {
+    HS_CUDA_CHECK(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    done.fetch_or(bit);
+  }
+  plan_kernel<<<grid, kPlanThreads, smem, st>>>(pa, P);
+  return check_launch();
+}
 
 }  // namespace moe
 }  // namespace hs
@@ -915,7 +943,7 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
   if (!dim_ok(w->D, 512, 512, 8192) || !dim_ok(w->I, 512, 512, 8192) || w->E < 1 || w->E > 1024)
     return HS_ERR_BAD_SHAPE;
   if (!w->w13 || !w->s13 || !w->w2 || !w->s2) return HS_ERR_BAD_ARGUMENT;
-  if (!aligned16(w->w13) || !aligned16(w->s13) || !aligned16(w->w2) || !aligned16(w->s2)) return HS_ERR_ALIGN;
+  if (!aligned32(w->w13) || !aligned32(w->w2) || !aligned16(w->s13) || !aligned16(w->s2)) return HS_ERR_ALIGN;
   Desc d;
   memset(&d, 0, sizeof(d));
   d.E = static_cast<int32_t>(w->E);
@@ -924,20 +952,22 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
   d.has_shared = w->sh_w13 != nullptr;
   int st;
   const uint64_t E = w->E, D = w->D, I = w->I;
-  if ((st = make_map(&d.tm_w13, w->w13, D / 2, E * 2 * I, 128, kRows, true))) return st;
-  if ((st = make_map(&d.tm_s13, w->s13, D / 32, E * 2 * I, static_cast<uint32_t>(D / 32), kRows, false))) return st;
-  if ((st = make_map(&d.tm_w2, w->w2, I / 2, E * D, 128, kRows, true))) return st;
-  if ((st = make_map(&d.tm_s2, w->s2, I / 32, E * D, static_cast<uint32_t>(I / 32), kRows, false))) return st;
+  if ((st = make_map(&d.tm_w13, w->w13, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, D, E * 2 * I, D / 2, 128, kM)))
+    return st;
+  if ((st = make_map(&d.tm_w2, w->w2, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, I, E * D, I / 2, 128, kM))) return st;
+  d.s13a = static_cast<const uint8_t*>(w->s13);
+  d.s2a = static_cast<const uint8_t*>(w->s2);
   if (d.has_shared) {
     if (!dim_ok(w->I_sh, 256, 256, 8192)) return HS_ERR_BAD_SHAPE;
     if (!w->sh_s13 || !w->sh_w2 || !w->sh_s2) return HS_ERR_BAD_ARGUMENT;
-    if (!aligned16(w->sh_w13) || !aligned16(w->sh_w2)) return HS_ERR_ALIGN;
+    if (!aligned16(w->sh_w13) || !aligned16(w->sh_w2) || !aligned16(w->sh_s13) || !aligned16(w->sh_s2))
+      return HS_ERR_ALIGN;
     d.I_sh = static_cast<int32_t>(w->I_sh);
     const uint64_t Ish = w->I_sh;
-    if ((st = make_map(&d.tm_sw13, w->sh_w13, D, 2 * Ish, 128, kRows, true))) return st;
-    if ((st = make_map(&d.tm_sw2, w->sh_w2, Ish, D, 128, kRows, true))) return st;
-    d.sh_s13 = static_cast<const uint8_t*>(w->sh_s13);
-    d.sh_s2 = static_cast<const uint8_t*>(w->sh_s2);
+    if ((st = make_map(&d.tm_sw13, w->sh_w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, D, 2 * Ish, D, 128, kM))) return st;
+    if ((st = make_map(&d.tm_sw2, w->sh_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, Ish, D, Ish, 128, kM))) return st;
+    d.sh_s13a = static_cast<const uint8_t*>(w->sh_s13);
+    d.sh_s2a = static_cast<const uint8_t*>(w->sh_s2);
   }
   d.magic = kDescMagic;
   memset(desc_out, 0, desc_bytes);
@@ -948,20 +978,6 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
 extern "C" size_t hs_moe_workspace_size(int64_t T, int64_t top_k, int64_t D, int64_t I, int64_t I_sh) {
   if (T < 0 || top_k < 1) return 0;
   return geometry(T, top_k, D, I, I_sh).total;
-}
-
-static int launch_plan(const int64_t* topk_idx, const float* topk_w, int64_t T, int64_t K, int E, int CH, int dup,
-                       const void* hidden, int D, const Plan& P, int pos_offset, int sort_tok, PermuteOut po,
-                       int32_t* dev_status, cudaStream_t st) {
-  const int nwarps = kPlanThreads / 32;
-  const size_t smem = static_cast<size_t>(4 * E + 2 + nwarps * E) * sizeof(int32_t);
-  int rc0 = opt_in_smem();
-  if (rc0) return rc0;
-  const int grid = 1 + (hidden ? static_cast<int>(T) : 0);
-  plan_kernel<<<grid, kPlanThreads, smem, st>>>(topk_idx, topk_w, static_cast<int>(T), static_cast<int>(K), E, CH,
-                                                dup, static_cast<const __nv_bfloat16*>(hidden), D, P, pos_offset,
-                                                sort_tok, po, dev_status);
-  return check_launch();
 }
 
 extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx, const float* topk_w,
@@ -984,41 +1000,62 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   if (workspace_bytes < g.total) return HS_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Plan P = plan_views(g, workspace);
-  const int NT = static_cast<int>(chunk_rows(T));
+  const int NT = static_cast<int>(ntiles(T));
   const int CH = 8 * NT;
+  const int64_t npairs = T * top_k;
+  const bool local_rows = npairs <= kLocalPairs;
 
-  int rc = launch_plan(topk_idx, topk_w, T, top_k, d.E, CH, dup_mode, hidden, d.D, P, static_cast<int>(T), 1,
-                       PermuteOut{nullptr, nullptr, nullptr}, dev_status, st);
-  if (rc) return rc;
+  CallMaps cm;
+  int rc;
+  if ((rc = make_map(&cm.tm_x8, P.x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, d.D, 2 * g.P_max, d.D, 128, 8))) return rc;
+  if ((rc = make_map(&cm.tm_act8, P.act8, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.I_act, 2 * g.P_max, g.I_act, 128, 8)))
+    return rc;
+
+  PlanArgs pa;
+  pa.topk_idx = topk_idx;
+  pa.topk_w = topk_w;
+  pa.hidden = static_cast<const __nv_bfloat16*>(hidden);
+  pa.T = static_cast<int>(T);
+  pa.K = static_cast<int>(top_k);
+  pa.E = d.E;
+  pa.D = d.D;
+  pa.CH = CH;
+  pa.dup_mode = dup_mode;
+  pa.pos_offset = static_cast<int>(T);
+  pa.sort_tok = 1;
+  pa.n_dcount = d.D / kM;
+  pa.P_max = g.P_max;
+  pa.local_rows = local_rows ? 1 : 0;
+  pa.po = PermuteOut{nullptr, nullptr, nullptr};
+  pa.status = dev_status;
+  if ((rc = launch_plan(pa, P, 1 + static_cast<int>(T), st))) return rc;
+  if (!local_rows) {
+    gather_kernel<<<static_cast<unsigned>(npairs), 256, 0, st>>>(P, static_cast<int>(T), g.P_max, d.D);
+    if ((rc = check_launch())) return rc;
+  }
 
   UnitArgs a;
   a.P = P;
   a.T = static_cast<int>(T);
+  a.K = static_cast<int>(top_k);
   a.CH = CH;
+  a.P_max = g.P_max;
   a.n_sh_chunks = use_shared ? static_cast<int>((T + CH - 1) / CH) : 0;
+  a.use_shared = use_shared;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_f32 = out_f32;
   a.status = dev_status;
-  // grids cover the largest possible chunk list; CTAs past the device count exit
-  const int64_t gu_units = static_cast<int64_t>(a.n_sh_chunks) * (use_shared ? d.I_sh / kRows : 0) +
-                           g.C_max * (d.I / kRows);
-  const int64_t dn_units = (static_cast<int64_t>(a.n_sh_chunks) + g.C_max) * (d.D / kRows);
+  const int64_t gu_units = static_cast<int64_t>(a.n_sh_chunks) * (use_shared ? d.I_sh / kM : 0) +
+                           g.C_max * (d.I / kM);
+  const int64_t dn_units = (static_cast<int64_t>(a.n_sh_chunks) + g.C_max) * (d.D / kM);
   if (gu_units > 0x7fffffff || dn_units > 0x7fffffff) return HS_ERR_BAD_SHAPE;
-
-  const int sm_gu = smem_gateup(NT, d.D), sm_dn = smem_down(NT, d.I);
-  if ((rc = opt_in_smem())) return rc;
-  gateup_kernel<<<static_cast<unsigned>(gu_units), kThreads, sm_gu, st>>>(d, a);
-  if ((rc = check_launch())) return rc;
-  down_kernel<<<static_cast<unsigned>(dn_units), kThreads, sm_dn, st>>>(d, a);
-  if ((rc = check_launch())) return rc;
-  dim3 fg(static_cast<unsigned>((d.D / 4 + 255) / 256), static_cast<unsigned>(T));
-  finalize_kernel<<<fg, 256, 0, st>>>(P, static_cast<int>(T), static_cast<int>(top_k), d.D, use_shared,
-                                      static_cast<__nv_bfloat16*>(out), out_f32);
-  return check_launch();
+  if ((rc = launch_nt<false>(NT, d, cm, a, gu_units, st))) return rc;
+  return launch_nt<true>(NT, d, cm, a, dn_units, st);
 }
 
 extern "C" size_t hs_moe_permute_workspace_size(int64_t T, int64_t top_k, int64_t E) {
   (void)E;
   if (T < 0 || top_k < 1) return 0;
-  // plan views with D = I = I_sh = 0: header, chunk and pair arrays only
   return geometry(T, top_k, 0, 0, 0).total;
 }
 
@@ -1026,7 +1063,7 @@ extern "C" int hs_moe_permute(const int64_t* topk_idx, int64_t T, int64_t top_k,
                               int32_t* token_topk_to_pos, int32_t* pos_to_expert, int32_t* expert_count,
                               int32_t* num_pos, void* x_expanded, void* workspace, size_t workspace_bytes,
                               int32_t* dev_status, void* stream) {
-  if (T < 0 || top_k < 1 || top_k > 64 || E < 1 || E > 1024) return HS_ERR_BAD_SHAPE;
+  if (T < 0 || top_k < 1 || top_k > 16 || E < 1 || E > 1024) return HS_ERR_BAD_SHAPE;
   if (!topk_idx || !token_topk_to_pos || !num_pos || !workspace) return HS_ERR_BAD_ARGUMENT;
   if (x_expanded && (!x || D < 1)) return HS_ERR_BAD_ARGUMENT;
   const Geometry g = geometry(T, top_k, 0, 0, 0);
@@ -1039,8 +1076,24 @@ extern "C" int hs_moe_permute(const int64_t* topk_idx, int64_t T, int64_t top_k,
     if (expert_count) HS_CUDA_CHECK(cudaMemsetAsync(expert_count, 0, E * sizeof(int32_t), st));
     return HS_OK;
   }
-  int rc = launch_plan(topk_idx, nullptr, T, top_k, static_cast<int>(E), 1 << 30, kDupKeepAll, nullptr, 0, P, 0, 0,
-                       PermuteOut{pos_to_expert, expert_count, num_pos}, dev_status, st);
+  PlanArgs pa;
+  pa.topk_idx = topk_idx;
+  pa.topk_w = nullptr;
+  pa.hidden = nullptr;
+  pa.T = static_cast<int>(T);
+  pa.K = static_cast<int>(top_k);
+  pa.E = static_cast<int>(E);
+  pa.D = 0;
+  pa.CH = 1 << 30;
+  pa.dup_mode = kDupKeepAll;
+  pa.pos_offset = 0;
+  pa.sort_tok = 0;
+  pa.n_dcount = 0;
+  pa.P_max = g.P_max;
+  pa.local_rows = 0;
+  pa.po = PermuteOut{pos_to_expert, expert_count, num_pos};
+  pa.status = dev_status;
+  int rc = launch_plan(pa, P, 1, st);
   if (rc) return rc;
   if (x_expanded) {
     expand_kernel<<<static_cast<unsigned>(T * top_k), 256, 0, st>>>(

@@ -29,10 +29,25 @@ namespace router {
 
 constexpr int kKSplitCols = 512;  // columns per CTA along D
 constexpr int kWarps = 4;         // 128 columns per warp per CTA
+constexpr int kFusedTopkTokens = 64;  // T <= this: top-k runs in the last logits CTA
+
+struct TopkArgs {
+  const __nv_bfloat16* bias;
+  int K;
+  float scaling;
+  int64_t* idx_out;
+  float* w_out;
+  __nv_bfloat16* logits_out;
+  uint32_t* counter;  // nullptr: a separate top-k launch follows
+};
+
+__device__ __forceinline__ void topk_dispatch(const float* partial, int ksplit, int T, int E, int t,
+                                              const __nv_bfloat16* bias, int K, float scaling, int64_t* idx_out,
+                                              float* w_out, __nv_bfloat16* logits_out);
 
 __global__ void __launch_bounds__(kWarps * 32) logits_kernel(const __nv_bfloat16* __restrict__ h,
                                                              const __nv_bfloat16* __restrict__ gate, int T, int D,
-                                                             int E, float* __restrict__ partial) {
+                                                             int E, float* __restrict__ partial, TopkArgs ta) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int e0 = blockIdx.x * 16;
@@ -72,80 +87,117 @@ __global__ void __launch_bounds__(kWarps * 32) logits_kernel(const __nv_bfloat16
       if (t < T) partial[(static_cast<int64_t>(ks) * T + t) * E + e] = s[j];
     }
   }
+  if (ta.counter == nullptr) return;
+  // Last CTA to finish runs the top-k for every token (small T only). The
+  // ticket is an atomic on a workspace counter that the last CTA resets; no
+  // CTA ever waits for another.
+  __shared__ int last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
+    last = atomicAdd(ta.counter, 1u) == total - 1u;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int ksplit = gridDim.y;
+  for (int t = warp; t < T; t += kWarps)
+    topk_dispatch(partial, ksplit, T, E, t, ta.bias, ta.K, ta.scaling, ta.idx_out, ta.w_out, ta.logits_out);
+  if (threadIdx.x == 0) *ta.counter = 0u;
 }
 
-constexpr int kMaxPerLane = 32;  // E <= 1024
-
 __device__ __forceinline__ uint64_t score_key(float s, int e) {
-  uint32_t hi = isnan(s) ? 0xffffffffu : __float_as_uint(s);  // s >= 0 (or NaN)
+  const uint32_t hi = isnan(s) ? 0xffffffffu : __float_as_uint(s);  // s >= 0 (or NaN)
   return (static_cast<uint64_t>(hi) << 32) | static_cast<uint64_t>(0xffffffffu - static_cast<uint32_t>(e));
+}
+
+// One warp selects the top-K experts of one token. PER = experts per lane
+// (compile-time, so scores and keys stay in registers).
+template <int PER>
+__device__ __forceinline__ void topk_token(const float* __restrict__ partial, int ksplit, int T, int E, int t,
+                                           const __nv_bfloat16* __restrict__ bias, int K, float scaling,
+                                           int64_t* __restrict__ idx_out, float* __restrict__ w_out,
+                                           __nv_bfloat16* __restrict__ logits_out) {
+  const int lane = threadIdx.x & 31;
+  float sc[PER];
+  uint64_t key[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    key[i] = 0ull;
+    sc[i] = 0.f;
+    if (e < E) {
+      float l = 0.f;
+      for (int s = 0; s < ksplit; ++s) l += partial[(static_cast<int64_t>(s) * T + t) * E + e];
+      float lb = round_bf16(l);
+      if (bias) lb = round_bf16(lb + __bfloat162float(bias[e]));
+      if (logits_out) logits_out[static_cast<int64_t>(t) * E + e] = __float2bfloat16_rn(lb);
+      const float sp = lb > 20.f ? lb : log1pf(expf(lb));
+      sc[i] = sqrtf(sp);
+      key[i] = score_key(sc[i], e);
+    }
+  }
+  float wsum = 0.f;
+  float wsel = 0.f;  // lane r keeps the r-th selected score
+  int esel = 0;
+  for (int r = 0; r < K; ++r) {
+    uint64_t best = 0ull;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) best = key[i] > best ? key[i] : best;
+    uint64_t wb = best;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, wb, o);
+      wb = other > wb ? other : wb;
+    }
+    const int e = static_cast<int>(0xffffffffu - static_cast<uint32_t>(wb & 0xffffffffull));
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (key[i] == wb) {
+        s = sc[i];
+        key[i] = 0ull;
+      }
+    s = __shfl_sync(0xffffffffu, s, e & 31);
+    wsum += s;  // same order on every lane: selection order
+    if (lane == r) {
+      wsel = s;
+      esel = e;
+    }
+  }
+  const float denom = fmaxf(wsum, 1e-20f);
+  if (lane < K) {
+    idx_out[static_cast<int64_t>(t) * K + lane] = esel;
+    w_out[static_cast<int64_t>(t) * K + lane] = (wsel / denom) * scaling;
+  }
+}
+
+__device__ __forceinline__ void topk_dispatch(const float* partial, int ksplit, int T, int E, int t,
+                                              const __nv_bfloat16* bias, int K, float scaling, int64_t* idx_out,
+                                              float* w_out, __nv_bfloat16* logits_out) {
+  const int per = (E + 31) / 32;
+  if (per <= 1)
+    topk_token<1>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
+  else if (per <= 2)
+    topk_token<2>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
+  else if (per <= 4)
+    topk_token<4>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
+  else if (per <= 8)
+    topk_token<8>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
+  else if (per <= 16)
+    topk_token<16>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
+  else
+    topk_token<32>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
 }
 
 __global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ partial, int ksplit, int T, int E,
                                                    const __nv_bfloat16* __restrict__ bias, int K, float scaling,
                                                    int64_t* __restrict__ idx_out, float* __restrict__ w_out,
                                                    __nv_bfloat16* __restrict__ logits_out) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + warp;
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
   if (t >= T) return;
-  float sc[kMaxPerLane];
-  uint64_t key[kMaxPerLane];
-  const int per = (E + 31) / 32;
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
-    key[i] = 0ull;
-    sc[i] = 0.f;
-    if (i >= per) continue;
-    const int e = lane + 32 * i;
-    if (e >= E) continue;
-    float l = 0.f;
-    for (int s = 0; s < ksplit; ++s) l += partial[(static_cast<int64_t>(s) * T + t) * E + e];
-    float lb = round_bf16(l);
-    if (bias) lb = round_bf16(lb + __bfloat162float(bias[e]));
-    if (logits_out) logits_out[static_cast<int64_t>(t) * E + e] = __float2bfloat16_rn(lb);
-    const float sp = lb > 20.f ? lb : log1pf(expf(lb));
-    const float s = sqrtf(sp);
-    sc[i] = s;
-    key[i] = score_key(s, e);
-  }
-  float wsel[16];
-  int esel[16];
-  for (int r = 0; r < K; ++r) {
-    uint64_t best = 0ull;
-    int bi = -1;
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
-      if (key[i] > best) {
-        best = key[i];
-        bi = i;
-      }
-    uint64_t wb = best;
-    for (int o = 16; o > 0; o >>= 1) {
-      const uint64_t other = __shfl_xor_sync(0xffffffffu, wb, o);
-      wb = other > wb ? other : wb;
-    }
-    const int e = static_cast<int>(0xffffffffu - static_cast<uint32_t>(wb & 0xffffffffull));
-    const int owner = e & 31;
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
-      if (lane == owner && i == bi && best == wb) {
-        s = sc[i];
-        key[i] = 0ull;
-      }
-    s = __shfl_sync(0xffffffffu, s, owner);
-    wsel[r] = s;
-    esel[r] = e;
-  }
-  if (lane == 0) {
-    float sum = 0.f;
-    for (int r = 0; r < K; ++r) sum += wsel[r];
-    sum = fmaxf(sum, 1e-20f);
-    for (int r = 0; r < K; ++r) {
-      idx_out[static_cast<int64_t>(t) * K + r] = esel[r];
-      w_out[static_cast<int64_t>(t) * K + r] = (wsel[r] / sum) * scaling;
-    }
-  }
+  topk_dispatch(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
 }
 
 __global__ void hash_kernel(const int64_t* __restrict__ ids, int T, const int64_t* __restrict__ tid2eid, int64_t V,
@@ -171,7 +223,7 @@ using namespace hs::router;
 
 extern "C" size_t hs_router_workspace_size(int64_t T, int64_t D, int64_t E) {
   if (T < 0 || D < kKSplitCols || E < 1) return 0;
-  return static_cast<size_t>(D / kKSplitCols) * T * E * sizeof(float) + 256;
+  return static_cast<size_t>(D / kKSplitCols) * T * E * sizeof(float) + 512;
 }
 
 extern "C" int hs_router_topk(const void* hidden, const void* gate, const void* bias, int64_t T, int64_t D, int64_t E,
@@ -187,13 +239,18 @@ extern "C" int hs_router_topk(const void* hidden, const void* gate, const void* 
   if (workspace_bytes < hs_router_workspace_size(T, D, E)) return HS_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int ksplit = static_cast<int>(D / kKSplitCols);
-  float* partial = static_cast<float*>(workspace);
+  // workspace: [0, 256) counter (zero at rest), then the k-split partials
+  uint32_t* counter = static_cast<uint32_t*>(workspace);
+  float* partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+  const bool fused = T <= kFusedTopkTokens;
+  TopkArgs ta{static_cast<const __nv_bfloat16*>(bias), static_cast<int>(top_k), routed_scaling, topk_idx, topk_w,
+              static_cast<__nv_bfloat16*>(logits_out), fused ? counter : nullptr};
   dim3 g1(static_cast<unsigned>(E / 16), static_cast<unsigned>(ksplit), static_cast<unsigned>((T + 7) / 8));
   logits_kernel<<<g1, kWarps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(hidden),
                                             static_cast<const __nv_bfloat16*>(gate), static_cast<int>(T),
-                                            static_cast<int>(D), static_cast<int>(E), partial);
+                                            static_cast<int>(D), static_cast<int>(E), partial, ta);
   int rc = check_launch();
-  if (rc) return rc;
+  if (rc || fused) return rc;
   topk_kernel<<<static_cast<unsigned>((T + 3) / 4), 128, 0, st>>>(
       partial, ksplit, static_cast<int>(T), static_cast<int>(E), static_cast<const __nv_bfloat16*>(bias),
       static_cast<int>(top_k), routed_scaling, topk_idx, topk_w, static_cast<__nv_bfloat16*>(logits_out));

@@ -11,12 +11,14 @@ collapses into one allocation per layer and a lookup returns views.
 
 Layout per layer (what the kernels stream with TMA):
   w13 [E][2][I][D/2] u8 packed e2m1 (w1 rows then w3 rows of each expert)
-  s13 [E][2][I][D/32] u8 UE8M0
+  s13 [E][2][I/128][D/128][512] u8 UE8M0 in scale-factor atoms (layout.py)
   w2  [E][D][I/2]    u8 packed e2m1
-  s2  [E][D][I/32]   u8 UE8M0
-  sh_w13 [2][I_sh][D] e4m3, sh_s13 [2][I_sh/128][D/128], sh_w2 [D][I_sh],
-  sh_s2 [D/128][I_sh/128]
+  s2  [E][D/128][I/128][512] u8 UE8M0 atoms
+  sh_w13 [2][I_sh][D] e4m3, sh_s13 [2][I_sh/128][D/128][512] atoms of the
+  128x128 block scales, sh_w2 [D][I_sh], sh_s2 [D/128][I_sh/128][512]
   gate [E][D] bf16, bias [E] bf16, tid2eid [V][K] int64 (hash layers only)
+The packed weights are returned to reference callers as views; the scales
+are returned in the reference's row-major [rows][cols/32] form as copies.
 """
 from __future__ import annotations
 
@@ -28,6 +30,7 @@ import numpy as np
 import torch
 
 from . import ops
+from .layout import atoms_to_scales, block_scales_to_atoms, scales_to_atoms
 
 
 @dataclass
@@ -74,15 +77,15 @@ class HBMExpertStore:
         for layer in range(num_layers):
             lw = LayerWeights(
                 w13=torch.zeros(E, 2, I, D // 2, dtype=torch.uint8, device=dev),
-                s13=torch.zeros(E, 2, I, D // 32, dtype=torch.uint8, device=dev),
+                s13=torch.zeros(E, 2, I // 128, D // 128, 512, dtype=torch.uint8, device=dev),
                 w2=torch.zeros(E, D, I // 2, dtype=torch.uint8, device=dev),
-                s2=torch.zeros(E, D, I // 32, dtype=torch.uint8, device=dev),
+                s2=torch.zeros(E, D // 128, I // 128, 512, dtype=torch.uint8, device=dev),
             )
             if Ish:
                 lw.sh_w13 = torch.zeros(2, Ish, D, dtype=torch.uint8, device=dev)
-                lw.sh_s13 = torch.zeros(2, Ish // 128, D // 128, dtype=torch.uint8, device=dev)
+                lw.sh_s13 = torch.zeros(2, Ish // 128, D // 128, 512, dtype=torch.uint8, device=dev)
                 lw.sh_w2 = torch.zeros(D, Ish, dtype=torch.uint8, device=dev)
-                lw.sh_s2 = torch.zeros(D // 128, Ish // 128, dtype=torch.uint8, device=dev)
+                lw.sh_s2 = torch.zeros(D // 128, Ish // 128, 512, dtype=torch.uint8, device=dev)
             if with_router:
                 lw.gate = torch.zeros(num_experts, D, dtype=torch.bfloat16, device=dev)
                 lw.bias = torch.zeros(num_experts, dtype=torch.bfloat16, device=dev)
@@ -107,18 +110,25 @@ class HBMExpertStore:
             return t.contiguous().view(torch.uint8).to(self.device, non_blocking=True)
 
         lw.w13[le, 0].copy_(dev_u8(w1))
-        lw.s13[le, 0].copy_(dev_u8(s1))
+        lw.s13[le, 0].copy_(scales_to_atoms(dev_u8(s1)))
         lw.w13[le, 1].copy_(dev_u8(w3))
-        lw.s13[le, 1].copy_(dev_u8(s3))
+        lw.s13[le, 1].copy_(scales_to_atoms(dev_u8(s3)))
         lw.w2[le].copy_(dev_u8(w2))
-        lw.s2[le].copy_(dev_u8(s2))
+        lw.s2[le].copy_(scales_to_atoms(dev_u8(s2)))
         lw.desc = None
 
     def set_shared(self, layer: int, w13, s13, w2, s2) -> None:
+        """Shared expert: e4m3 weights, 128x128 block scales [2][I_sh/128][D/128] and [D/128][I_sh/128]."""
         lw = self.layers[layer]
-        for dst, src in ((lw.sh_w13, w13), (lw.sh_s13, s13), (lw.sh_w2, w2), (lw.sh_s2, s2)):
-            t = torch.from_numpy(np.ascontiguousarray(src)) if isinstance(src, np.ndarray) else src
-            dst.copy_(t.contiguous().view(torch.uint8).reshape(dst.shape).to(self.device))
+
+        def dev_u8(a):
+            t = torch.from_numpy(np.ascontiguousarray(a)) if isinstance(a, np.ndarray) else a
+            return t.contiguous().view(torch.uint8).to(self.device)
+
+        lw.sh_w13.copy_(dev_u8(w13).reshape(lw.sh_w13.shape))
+        lw.sh_w2.copy_(dev_u8(w2).reshape(lw.sh_w2.shape))
+        lw.sh_s13.copy_(block_scales_to_atoms(dev_u8(s13).reshape(lw.sh_s13.shape[:-1])))
+        lw.sh_s2.copy_(block_scales_to_atoms(dev_u8(s2).reshape(lw.sh_s2.shape[:-1])))
         lw.desc = None
 
     def set_router(self, layer: int, gate: torch.Tensor, bias: Optional[torch.Tensor]) -> None:
@@ -196,8 +206,9 @@ class HBMExpertStore:
         except KeyError:
             return None
         e8 = torch.float8_e8m0fnu
-        return (lw.w13[le, 0].view(torch.int8), lw.s13[le, 0].view(e8), lw.w13[le, 1].view(torch.int8),
-                lw.s13[le, 1].view(e8), lw.w2[le].view(torch.int8), lw.s2[le].view(e8))
+        return (lw.w13[le, 0].view(torch.int8), atoms_to_scales(lw.s13[le, 0]).view(e8),
+                lw.w13[le, 1].view(torch.int8), atoms_to_scales(lw.s13[le, 1]).view(e8),
+                lw.w2[le].view(torch.int8), atoms_to_scales(lw.s2[le]).view(e8))
 
     def _load_expert_weights(self, layer_idx: int, eid: int):
         """Reference triple format: ((data, scale, "fp4_gpu"), w3 entry, w2 entry)."""

@@ -18,14 +18,14 @@ _status: dict = {}
 # Number of this library's kernels each op launches; summed into `launches`
 # so a caller can count the kernels of one decode iteration.
 launches = 0
-_KERNELS = {"hs_router_topk": 2, "hs_hash_route": 1, "hs_moe_ffn_fp4": 4, "hs_moe_permute": 2,
+_KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_moe_permute": 2,
             "hs_moe_unpermute": 1, "hs_accept_greedy": 1, "hs_accept_rejection": 1, "hs_fill_bytes": 1}
 
 
-def _launch(name: str, *args) -> None:
+def _launch(name: str, *args, extra: int = 0) -> None:
     global launches
     call(name, *args)
-    launches += _KERNELS.get(name, 0)
+    launches += _KERNELS.get(name, 0) + extra
 
 
 def _stream(device: torch.device) -> int:
@@ -53,12 +53,13 @@ def _check_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
 
 
 def workspace(device: torch.device, nbytes: int, tag: str) -> torch.Tensor:
-    """Grow-only scratch per (device, stream, tag). Calls on one stream are
-    ordered, so reusing the buffer across calls is race-free."""
+    """Grow-only scratch per (device, stream, tag), zero-filled when allocated
+    (the kernels keep their counters at zero between calls). Calls on one
+    stream are ordered, so reusing the buffer across calls is race-free."""
     key = (device.index, _stream(device), tag)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        buf = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf
 
@@ -100,7 +101,8 @@ def router_topk(hidden: torch.Tensor, gate: torch.Tensor, bias: Optional[torch.T
     nb = lib.hs_router_workspace_size(T, D, E)
     ws = workspace(dev, nb, "router")
     _launch("hs_router_topk", hidden.data_ptr(), gate.data_ptr(), _ptr(bias), T, D, E, top_k, float(routed_scaling),
-         idx.data_ptr(), w.data_ptr(), _ptr(lg), ws.data_ptr(), ws.numel(), _stream(dev))
+            idx.data_ptr(), w.data_ptr(), _ptr(lg), ws.data_ptr(), ws.numel(), _stream(dev),
+            extra=0 if T <= 64 else 1)
     if return_logits:
         return idx, w, lg
     return idx, w
@@ -156,7 +158,7 @@ def moe_ffn(desc: ctypes.Array, dims: tuple, hidden: torch.Tensor, topk_idx: tor
     ws = workspace(dev, nb, "moe")
     _launch("hs_moe_ffn_fp4", ctypes.addressof(desc), hidden.data_ptr(), topk_idx.data_ptr(), topk_w.data_ptr(), T, K,
          int(bool(use_shared)), int(dup_mode), out.data_ptr(), _ptr(out_f32), ws.data_ptr(), ws.numel(),
-         status_word(dev).data_ptr(), _stream(dev))
+         status_word(dev).data_ptr(), _stream(dev), extra=0 if T * K <= 4096 else 1)
     return out
 
 

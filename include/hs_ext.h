@@ -14,7 +14,8 @@
  *   - No entry point allocates device memory. Kernels that need scratch take a
  *     caller-provided `workspace`; its size comes from the matching
  *     *_workspace_size() query and it must be zero-filled once after allocation
- *     (the kernels leave every counter they use back at zero).
+ *     (the router's counter is left at zero by every call; the MoE call resets
+ *     its own counters).
  *   - No exceptions, no global mutable state: concurrent calls on different
  *     streams are safe when they use different workspaces.
  *
@@ -86,15 +87,19 @@ int hs_hash_route(const int64_t* input_ids, int64_t T, const int64_t* tid2eid,
 /*                                                                            */
 /* Weight layout (what HBMExpertStore holds in HBM):                          */
 /*   w13 [E][2][I][D/2]  u8  packed e2m1, low nibble = even column            */
-/*   s13 [E][2][I][D/32] u8  ue8m0 (one per 32 columns)                       */
+/*   s13 [E][2][I/128][D/128][512] u8 ue8m0 scale-factor atoms (below)        */
 /*   w2  [E][D][I/2]     u8  packed e2m1                                      */
-/*   s2  [E][D][I/32]    u8  ue8m0                                            */
+/*   s2  [E][D/128][I/128][512]    u8 ue8m0 atoms                             */
 /*   sh_w13 [2][I_sh][D] u8  e4m3 (w1 rows then w3 rows), or NULL            */
-/*   sh_s13 [2][I_sh/128][D/128] u8 ue8m0                                     */
+/*   sh_s13 [2][I_sh/128][D/128][512] u8 atoms of the 128x128 block scales    */
 /*   sh_w2  [D][I_sh]    u8  e4m3                                             */
-/*   sh_s2  [D/128][I_sh/128] u8 ue8m0                                        */
+/*   sh_s2  [D/128][I_sh/128][512] u8 atoms                                   */
+/* A scale-factor atom covers 128 rows x 128 columns (4 blocks of 32): byte   */
+/* m0*16 + m1*4 + j holds the scale of row 32*m1 + m0, block j; the layout    */
+/* tcgen05 scale-factor memory takes with one 32x128b copy. Row-major scales  */
+/* s[R][C/32] convert with home_seek_b200/layout.py (scales_to_atoms).       */
 /* Limits: D, I multiples of 512 in [512, 8192]; I_sh a multiple of 256 in    */
-/* [256, 8192]; E <= 1024; all base pointers 16-byte aligned.                 */
+/* [256, 8192]; E <= 1024; w13/w2 32-byte aligned, other pointers 16-byte.    */
 /* ------------------------------------------------------------------------ */
 typedef struct hs_moe_weights {
   const void* w13;

@@ -46,3 +46,18 @@ def test_loader_protocol_and_localise():
     assert _localise(idx, 8, 8).tolist() == [[-1, 0, 7, -1, -1]]
     s = torch.tensor([1.0, 2.0, 0.5, 2.0 ** -9], dtype=torch.float32)
     assert _e8m0_bytes(s).tolist() == [127, 128, 126, 118]
+
+
+def test_scale_atom_layout_roundtrip_and_formula():
+    from home_seek_b200.layout import atoms_to_scales, block_scales_to_atoms, scales_to_atoms
+    g = torch.Generator().manual_seed(0)
+    s = torch.randint(0, 256, (256, 64), generator=g, dtype=torch.uint8)
+    a = scales_to_atoms(s)
+    assert a.shape == (2, 16, 512)
+    assert torch.equal(atoms_to_scales(a), s)
+    # byte m0*16 + m1*4 + j of atom (ra, ka) = s[128*ra + 32*m1 + m0][4*ka + j]
+    for ra, ka, m0, m1, j in [(0, 0, 0, 0, 0), (1, 3, 31, 3, 3), (0, 7, 5, 2, 1), (1, 15, 17, 1, 2)]:
+        assert a[ra, ka, m0 * 16 + m1 * 4 + j] == s[128 * ra + 32 * m1 + m0, 4 * ka + j]
+    b = torch.tensor([[121, 120]], dtype=torch.uint8)
+    ab = block_scales_to_atoms(b)
+    assert ab.shape == (1, 2, 512) and (ab[0, 0] == 121).all() and (ab[0, 1] == 120).all()
