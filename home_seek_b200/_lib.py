@@ -25,6 +25,7 @@ HS_DEV_BAD_TOKEN = 0x2
 HS_DEV_TIMEOUT = 0x4
 HS_DEV_BAD_DRAFT = 0x8
 HS_MOE_DESC_BYTES = 1024
+HS_MOE_NOALLOC_BYTES = 6 << 20
 HS_DUP_LAST = 0
 HS_DUP_SUM = 1
 
@@ -61,6 +62,8 @@ SIGNATURES = {
     "hs_moe_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64]),
     "hs_moe_ffn_fp4": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p,
                                c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hs_moe_ffn_fp4_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,
+                                       c_void_p, c_void_p, c_void_p, c_void_p]),
     "hs_moe_permute_workspace_size": (c_size_t, [c_int64, c_int64, c_int64]),
     "hs_moe_permute": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),

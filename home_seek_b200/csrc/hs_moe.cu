@@ -1117,3 +1117,60 @@ extern "C" int hs_moe_unpermute(const void* x_expanded, int64_t num_expanded, in
                                          static_cast<int>(top_k), static_cast<__nv_bfloat16*>(out_bf16));
   return check_launch();
 }
+
+// ---------------------------------------------------------------------------
+// No-allocation variant
+// ---------------------------------------------------------------------------
+// For callers that cannot allocate device memory when they call (plugin hosts
+// whose enqueue path forbids it, code inside a CUDA-graph stream capture where
+// cudaMalloc is not permitted, loops where cudaMalloc/cudaFree would
+// synchronise the device): the scratch lives in this file-scope device array.
+// Every GPU that loads the library holds it until the process exits, and
+// every call shares it, so calls that overlap on the GPU race. The plan kernel
+// clears the finalize counters at the start of each call; nothing else in the
+// scratch needs to start at zero.
+static __device__ __align__(256) uint8_t g_moe_noalloc_scratch[HS_MOE_NOALLOC_BYTES];
+
+// Device address of the scratch array per device, looked up once per device
+// with that device current (the array's name is only a host-side stand-in).
+static void* noalloc_scratch_ptr(int* status) {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_cuda_error(static_cast<int>(e));
+    *status = HS_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_last_cuda_error(static_cast<int>(e));
+      *status = HS_ERR_CUDA;
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *status = HS_OK;
+  return ptrs[dev];
+}
+
+extern "C" int hs_moe_ffn_fp4_noalloc(const void* desc, const void* hidden, const int64_t* topk_idx,
+                                      const float* topk_w, int64_t T, int64_t top_k, int use_shared, int dup_mode,
+                                      void* out, float* out_f32, int32_t* dev_status, void* stream) {
+  if (!desc) return HS_ERR_BAD_ARGUMENT;
+  Desc d;
+  memcpy(&d, desc, sizeof(d));
+  if (d.magic != kDescMagic) return HS_ERR_BAD_ARGUMENT;
+  if (T < 0 || top_k < 1 || top_k > 16) return HS_ERR_BAD_SHAPE;
+  if (hs_moe_workspace_size(T, top_k, d.D, d.I, d.has_shared ? d.I_sh : 0) > HS_MOE_NOALLOC_BYTES)
+    return HS_ERR_WORKSPACE;
+  int st = HS_OK;
+  void* scratch = noalloc_scratch_ptr(&st);
+  if (st != HS_OK) return st;
+  return hs_moe_ffn_fp4(desc, hidden, topk_idx, topk_w, T, top_k, use_shared, dup_mode, out, out_f32, scratch,
+                        HS_MOE_NOALLOC_BYTES, dev_status, stream);
+}

@@ -144,6 +144,27 @@ int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx
                    int dup_mode, void* out, float* out_f32, void* workspace,
                    size_t workspace_bytes, int32_t* dev_status, void* stream);
 
+/* hs_moe_ffn_fp4_noalloc: hs_moe_ffn_fp4 without the workspace argument.     */
+/* No counterpart in the reference. It is for callers that cannot allocate    */
+/* device memory at the moment they call: plugin hosts whose enqueue path     */
+/* forbids allocation, code running while a stream is being captured into a  */
+/* CUDA graph (where cudaMalloc is not permitted), and latency-critical loops  */
+/* in which cudaMalloc/cudaFree would synchronise the device. The scratch is  */
+/* a fixed array of HS_MOE_NOALLOC_BYTES inside the library; every GPU that   */
+/* loads the library holds it until the process exits. A call whose          */
+/* hs_moe_workspace_size(T, top_k, D, I, I_sh) exceeds it returns             */
+/* HS_ERR_WORKSPACE without launching (at D = 4096, I = I_sh = 2048, top_k = 6 */
+/* that allows T <= 31 tokens). The first call on a device looks up the       */
+/* array's device address (cudaGetSymbolAddress): make that first call        */
+/* before any stream capture. All calls share the one array, so calls that    */
+/* overlap on the GPU (two streams, two host threads) race; the kernels clear */
+/* the counters they need at the start of every call.                         */
+#define HS_MOE_NOALLOC_BYTES (6u << 20)
+int hs_moe_ffn_fp4_noalloc(const void* desc, const void* hidden, const int64_t* topk_idx,
+                           const float* topk_w, int64_t T, int64_t top_k, int use_shared,
+                           int dup_mode, void* out, float* out_f32, int32_t* dev_status,
+                           void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* R10. Permute / unpermute, with the semantics of the reference's test       */
 /* oracles tests/_reference.py:93-121 (expand_to_fused) and                   */
