@@ -24,8 +24,9 @@ HS_DEV_BAD_EXPERT = 0x1
 HS_DEV_BAD_TOKEN = 0x2
 HS_DEV_TIMEOUT = 0x4
 HS_DEV_BAD_DRAFT = 0x8
+HS_DEV_SMEM_ALIGN = 0x10
 HS_MOE_DESC_BYTES = 1024
-HS_MOE_NOALLOC_BYTES = 6 << 20
+HS_MOE_NOALLOC_BYTES = 16 << 20
 HS_DUP_LAST = 0
 HS_DUP_SUM = 1
 

@@ -9,11 +9,15 @@
 // the two at inference_engine/engine.py:1530-1536.
 //
 // Design (B200-first):
-//   * Weights never pass through registers. TMA loads 128x128 tiles of packed
-//     e2m1 straight into 128B-swizzled shared memory (data type 16U4_ALIGN16B,
-//     the layout kind::mxf8f6f4 reads), the UE8M0 scales (stored by the expert
-//     store in the tcgen05 scale-factor atom layout, 512 B per 128 rows x 128
-//     columns) go to TMEM with one tcgen05.cp, and tcgen05.mma.kind::mxf8f6f4
+//   * Weights never pass through registers. The expert store keeps every
+//     128x128 weight tile contiguous and the two tiles a pipeline stage needs
+//     (w1 and w3 of one k-step, or two consecutive k-steps of w2) adjacent, so
+//     one TMA per stage streams 16 KB of consecutive packed e2m1 straight into
+//     128B-swizzled shared memory (data type 16U4_ALIGN16B, the layout
+//     kind::mxf8f6f4 reads); the UE8M0 scales (stored in the tcgen05
+//     scale-factor atom layout, 512 B per 128 rows x 128 columns, the stage's
+//     two atoms adjacent) arrive with one 1 KB bulk copy and go to TMEM with
+//     tcgen05.cp, and tcgen05.mma.kind::mxf8f6f4
 //     .block_scale multiplies them with the activations, accumulating f32 in
 //     TMEM. The FP8 shared expert runs through the same MMA with E4M3 weights.
 //   * Activations are bf16 in the reference. Each bf16 value v (8 significant
@@ -49,25 +53,26 @@ namespace moe {
 
 constexpr int kM = 128;                 // weight rows per unit (UMMA M)
 constexpr int kBoxBytes = kM * 128;     // one 128x128 weight tile in shared memory
-constexpr int kStages = 3;
 constexpr int kThreads = 192;           // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
-constexpr int kTmemCols = 256;
-constexpr int kAccUp = 64;              // TMEM column of the up accumulator
-constexpr int kSfaCol = 128;            // 8 columns per stage (2 boxes x 4)
-constexpr int kSfbCol = 192;
+constexpr int kAccUp = 48;              // TMEM column of the up accumulator within a buffer (N <= 48)
 constexpr int kMaxNT = 3;               // n-tiles of 8 pairs (N = 16 * NT)
 constexpr int kPlanThreads = 512;
 constexpr int kLocalPairs = 4096;       // T*K up to this: token CTAs place their own rows
-constexpr uint32_t kDescMagic = 0x48534d32u;  // "HSM2"
+constexpr int kFastPlanPairs = 1024;    // T*K up to this: block 0 uses the direct-count plan
+constexpr uint32_t kDescMagic = 0x48534d33u;  // "HSM3" (tiled weights)
+constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two independent MMA streams)
+constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
 
 struct __align__(64) Desc {
-  CUtensorMap tm_w13;   // e2m1 [E*2*I rows][D], 16U4_ALIGN16B, box 128 x 128, swizzle 128B
-  CUtensorMap tm_w2;    // e2m1 [E*D rows][I]
-  CUtensorMap tm_sw13;  // e4m3 [2*I_sh rows][D], uint8, box 128 x 128
-  CUtensorMap tm_sw2;   // e4m3 [D rows][I_sh]
-  const uint8_t* s13a;  // [E][2][I/128][D/128][512] scale-factor atoms
+  // Weight tiles as rows of 128 values: [tiles * 128 rows][128], box 128 x 256
+  // (two adjacent tiles), 128B swizzle.
+  CUtensorMap tm_w13;   // e2m1 [E][I/128][D/128][w1, w3][128][128], 16U4_ALIGN16B
+  CUtensorMap tm_w2;    // e2m1 [E][D/128][I/128][128][128]
+  CUtensorMap tm_sw13;  // e4m3 [I_sh/128][D/128][w1, w3][128][128], uint8
+  CUtensorMap tm_sw2;   // e4m3 [D/128][I_sh/128][128][128]
+  const uint8_t* s13a;  // [E][I/128][D/128][2][512] scale-factor atoms
   const uint8_t* s2a;   // [E][D/128][I/128][512]
-  const uint8_t* sh_s13a;  // [2][I_sh/128][D/128][512]
+  const uint8_t* sh_s13a;  // [I_sh/128][D/128][2][512]
   const uint8_t* sh_s2a;   // [D/128][I_sh/128][512]
   int32_t E, D, I, I_sh;
   int32_t has_shared;
@@ -76,8 +81,8 @@ struct __align__(64) Desc {
 static_assert(sizeof(Desc) <= HS_MOE_DESC_BYTES, "descriptor blob too small");
 
 struct CallMaps {
-  CUtensorMap tm_x8;    // [2*P_max rows][D] e4m3 hi rows then lo rows, box 128 x 8
-  CUtensorMap tm_act8;  // [2*P_max rows][I_act]
+  CUtensorMap tm_x8;    // [2 (hi, lo)][P_max rows][D] e4m3, box 128 x 8*NT x 2
+  CUtensorMap tm_act8;  // [2][P_max rows][I_act]
 };
 
 // Device views into the caller's workspace.
@@ -101,7 +106,12 @@ struct Plan {
 
 struct Geometry {
   int64_t T, K, D, I, I_sh, I_act, P_max, C_max;
-  size_t off_hdr, off_chunk, off_pair, off_sb, off_tok, off_tokpos, off_dcount, off_x8, off_act8, off_out, total;
+  int64_t U_gu, U_dn;      // upper bounds on gate/up and down units
+  int G;                   // persistent CTAs
+  int aligned;             // unit-aligned schedule (no partial slots)
+  int64_t slot_floats;     // floats per partial slot (gate/up, the larger)
+  size_t off_hdr, off_chunk, off_pair, off_sb, off_tok, off_tokpos, off_dcount, off_x8, off_act8, off_out,
+      off_ucount, off_part, total;
 };
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -111,7 +121,7 @@ static int64_t ntiles(int64_t T) {
   return std::max<int64_t>(1, std::min<int64_t>(nt, kMaxNT));
 }
 
-static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_sh) {
+static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_sh, int G = 148) {
   Geometry g{};
   g.T = T;
   g.K = K;
@@ -144,6 +154,17 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   o = align_up(o + 2 * g.P_max * g.I_act, 256);
   g.off_out = o;
   o = align_up(o + g.P_max * D * sizeof(float), 256);
+  // stream-K state: per-unit tickets and partial accumulator slots
+  const int64_t n_sh = (T + CH - 1) / CH;
+  g.U_gu = g.C_max * (I / kM) + n_sh * (I_sh / kM);
+  g.U_dn = (g.C_max + n_sh) * (D / kM);
+  g.G = G;
+  g.aligned = 0;
+  g.slot_floats = 2 * kM * 8 * ntiles(T);
+  g.off_ucount = o;
+  o = align_up(o + (g.U_gu + g.U_dn) * sizeof(uint32_t), 256);
+  g.off_part = o;
+  o = align_up(o + 2 * static_cast<int64_t>(G) * g.slot_floats * sizeof(float), 256);
   g.total = o;
   return g;
 }
@@ -192,6 +213,8 @@ struct PlanArgs {
   int local_rows;  // token CTAs write their routed pair rows themselves
   PermuteOut po;
   int32_t* status;
+  uint32_t* ucount;  // stream-K unit tickets to clear (all plan CTAs share the work)
+  int64_t n_ucount;
 };
 
 // Power-of-two prescale for an activation aw = bf16(a * wb), |a| <= 100:
@@ -263,6 +286,9 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
   const int T = A.T, K = A.K, E = A.E;
   const int npairs = T * K;
   const bool cache_idx = npairs <= kLocalPairs;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid; i < A.n_ucount;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    A.ucount[i] = 0u;
   int32_t* sidx = sm;  // [npairs] clamped ids (when cached)
   int32_t* rest = sm + (cache_idx ? npairs : 0);
   if (cache_idx) {
@@ -270,41 +296,49 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
     __syncthreads();
   }
 
+  // expert of every pair after the duplicate rule (-1 = skipped), when cached
+  int32_t* sval = rest;                          // [npairs]
+  rest = rest + (cache_idx ? npairs : 0);
+  if (cache_idx) {
+    for (int l = tid; l < npairs; l += blockDim.x) {
+      const int t = l / K;
+      if (blockIdx.x == 0 && sidx[l] == kBadId) report(A.status, HS_DEV_BAD_EXPERT);
+      sval[l] = pair_expert(sidx + t * K, nullptr, l - t * K, K, A.dup_mode, nullptr);
+    }
+    __syncthreads();
+  }
+
   if (blockIdx.x > 0) {
     // ---- token row: prescale, hi/lo split, rows for its pairs ----
     const int t = blockIdx.x - 1;
+    const int warp = tid >> 5, lane = tid & 31;
     const __nv_bfloat16* h = A.hidden + static_cast<int64_t>(t) * A.D;
     float mx = 0.f;
     for (int k = tid; k < A.D; k += blockDim.x) mx = fmaxf(mx, fabsf(__bfloat162float(h[k])));
     __shared__ float red[kPlanThreads / 32];
     __shared__ int rows[17];
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    if (lane == 0) red[warp] = mx;
     int nrows = 1;
     if (A.local_rows && cache_idx) {
       nrows = 1 + K;
-      if (tid < 32) {
-        // warp 0: for each of my K entries count the valid pairs with a smaller
-        // expert (its expert's base) and with the same expert on an earlier
-        // token (its rank): the position block 0 assigns.
-        for (int j = 0; j < K; ++j) {
-          const int e = pair_expert(sidx + t * K, nullptr, j, K, A.dup_mode, nullptr);
-          int base = 0, rank = 0;
-          if (e >= 0) {
-            for (int m = tid; m < npairs; m += 32) {
-              const int tm = m / K;
-              const int e2 = pair_expert(sidx + tm * K, nullptr, m - tm * K, K, A.dup_mode, nullptr);
-              if (e2 < 0) continue;
-              base += e2 < e;
-              rank += (e2 == e) && (tm < t);
-            }
+      // warp j places this token's entry j: its position is the number of
+      // valid pairs with a smaller expert plus the number with the same
+      // expert on earlier tokens, exactly as block 0 assigns it
+      if (warp < K) {
+        const int e = sval[t * K + warp];
+        int base = 0, rank = 0;
+        if (e >= 0)
+          for (int m = lane; m < npairs; m += 32) {
+            const int e2 = sval[m];
+            base += (e2 >= 0) & (e2 < e);
+            rank += (e2 == e) & (m < t * K);
           }
-          for (int o = 16; o > 0; o >>= 1) {
-            base += __shfl_xor_sync(0xffffffffu, base, o);
-            rank += __shfl_xor_sync(0xffffffffu, rank, o);
-          }
-          if (tid == 0) rows[1 + j] = e >= 0 ? A.pos_offset + base + rank : -1;
+        for (int o = 16; o > 0; o >>= 1) {
+          base += __shfl_xor_sync(0xffffffffu, base, o);
+          rank += __shfl_xor_sync(0xffffffffu, rank, o);
         }
+        if (lane == 0) rows[1 + warp] = e >= 0 ? A.pos_offset + base + rank : -1;
       }
     }
     __syncthreads();
@@ -337,6 +371,110 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
       }
     }
     if (tid < nrows && rows[tid] >= 0) P.sb1[rows[tid]] = static_cast<uint8_t>(127 - e);
+    return;
+  }
+
+  // ---- routing plan, small pair counts: three phases of independent counts ----
+  if (cache_idx && npairs <= kFastPlanPairs) {
+    int32_t* spos = rest;            // [npairs] position (or -1)
+    int32_t* scnt = spos + npairs;   // [npairs] pair count of the expert (leaders only)
+    __shared__ int tot[4];           // chunks, slots, pairs
+    if (tid < 4) tot[tid] = 0;
+    for (int i = tid; i < A.n_dcount; i += blockDim.x) P.dcount[i] = 0u;
+    if (A.po.expert_count)
+      for (int x = tid; x < E; x += blockDim.x) A.po.expert_count[x] = 0;
+    for (int t = tid; t < A.pos_offset; t += blockDim.x) {  // shared-expert pairs
+      P.pair_token[t] = t;
+      P.pair_wb[t] = 1.f;
+      P.pair_q[t] = 0;
+      P.sb2[t] = 127;
+    }
+    __syncthreads();
+    for (int l = tid; l < npairs; l += blockDim.x) {
+      const int e = sval[l];
+      int pos = -1, cnt = 0;
+      if (e >= 0) {
+        int less = 0, before = 0;
+        for (int m = 0; m < npairs; ++m) {
+          const int e2 = sval[m];
+          less += (e2 >= 0) & (e2 < e);
+          before += (e2 == e) & (m < l);
+          cnt += (e2 == e);
+        }
+        pos = A.pos_offset + less + before;
+        const int t = l / K;
+        float wsum = 0.f;
+        pair_expert(sidx + t * K, A.topk_w ? A.topk_w + static_cast<int64_t>(t) * K : nullptr, l - t * K, K,
+                    A.dup_mode, &wsum);
+        const float wb = round_bf16(wsum);
+        const int q = act_prescale(wb);
+        P.pair_token[pos] = t;
+        P.pair_wb[pos] = wb;
+        P.pair_q[pos] = q;
+        P.sb2[pos] = static_cast<uint8_t>(127 - q);
+        if (A.po.pos_to_expert) A.po.pos_to_expert[pos - A.pos_offset] = e;
+        if (before == 0) {
+          atomicAdd(&tot[0], (cnt + A.CH - 1) / A.CH);
+          atomicAdd(&tot[1], 1);
+          if (A.po.expert_count) A.po.expert_count[e] = cnt;
+        }
+        atomicAdd(&tot[2], 1);
+      }
+      spos[l] = pos;
+      scnt[l] = 0;
+      if (e >= 0) {
+        int before = 0;
+        for (int m = 0; m < l; ++m) before += sval[m] == e;
+        scnt[l] = before == 0 ? cnt : 0;  // only the expert's first pair keeps the count
+      }
+    }
+    __syncthreads();
+    for (int l = tid; l < npairs; l += blockDim.x) {
+      const int e = sval[l];
+      const int pos = spos[l];
+      if (e >= 0) {
+        // the expert's first pair (the only one with a count) writes its chunks
+        if (scnt[l] > 0) {
+          int cb = 0;
+          for (int m = 0; m < npairs; ++m) {
+            const int e2 = sval[m];
+            if (scnt[m] > 0 && e2 < e) cb += (scnt[m] + A.CH - 1) / A.CH;
+          }
+          const int cnt = scnt[l];
+          const int first = pos;  // the leader holds the expert's first position
+          for (int ck = 0; ck * A.CH < cnt; ++ck, ++cb) {
+            P.chunk_expert[cb] = e;
+            P.chunk_pair0[cb] = first + ck * A.CH;
+            P.chunk_np[cb] = min(A.CH, cnt - ck * A.CH);
+          }
+        }
+      }
+      if (A.sort_tok) {
+        // rank among the token's valid pairs by position (= by expert id)
+        const int t = l / K;
+        int nvalid = 0, rank = 0;
+        for (int j = 0; j < K; ++j) {
+          const int p2 = spos[t * K + j];
+          nvalid += p2 >= 0;
+          rank += (p2 >= 0) & (pos >= 0) & (p2 < pos);
+        }
+        if (pos >= 0) P.tok_pos[t * K + rank] = pos;
+        const int j = l - t * K;
+        if (j >= nvalid) P.tok_pos[t * K + j] = -1;
+      } else {
+        P.tok_pos[l] = pos;
+      }
+    }
+    if (tid == 0) {
+      P.hdr[0] = tot[0];
+      P.hdr[1] = tot[1];
+      P.hdr[2] = tot[2];
+      if (A.po.num_pos) *A.po.num_pos = tot[2];
+    }
+    if (A.po.pos_to_expert) {
+      __syncthreads();
+      for (int p2 = tot[2] + tid; p2 < npairs; p2 += blockDim.x) A.po.pos_to_expert[p2] = -1;
+    }
     return;
   }
 
@@ -521,44 +659,149 @@ struct UnitArgs {
   __nv_bfloat16* out;
   float* out_f32;
   int32_t* status;
+  // stream-K schedule
+  int G;                 // persistent CTAs (kCtasPerSm per SM)
+  int aligned;           // 1: CTA boundaries on unit boundaries (many units), 0: split units
+  uint32_t* ucount;      // [U_max] per-unit tickets, cleared by the plan kernel
+  float* part;           // [(U_max + G)][slot] partial accumulators
 };
-
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
-}
 
 template <int NT, int BOXES>
 struct SmemLayout {
   static constexpr int kA = 2 * kBoxBytes;             // two weight boxes per stage
   static constexpr int kB = BOXES * 2 * NT * 1024;     // hi and lo atoms per k-box
-  static constexpr int kSF = 2 * 512;                  // two scale atoms per stage
+  static constexpr int kSF = 2 * 512 + 512;            // two A scale atoms + the unit's B scale atom
   static constexpr int kStage = kA + kB + kSF;
-  // three stages when two CTAs still fit on an SM (2 x 113 KB), else two
-  static constexpr int kNumStages = (1024 + kStages * kStage + 768 <= 113 * 1024) ? kStages : 2;
-  static constexpr int kBytes = 1024 + kNumStages * kStage + 512 + 256;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kFit = (kSmemPerCta - kBarBytes) / kStage;
+  static constexpr int kNumStages = kFit < 4 ? kFit : 4;
+  static constexpr int kBytes = kNumStages * kStage + kBarBytes;  // stages at the 1024-aligned base
 };
 
 struct Bars {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t accum;
+  uint64_t full[4];
+  uint64_t empty[4];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
   uint32_t tmem;
-  int32_t last;
+  int32_t flag;
+  int32_t issued, consumed;  // TMA stages issued by the producer / consumed by the MMA issuer
 };
 
+// Stream-K schedule over one phase. Units (chunk x 128-row tile) are laid end
+// to end as k-steps, shared-expert units first; a step of an FP8 unit weighs
+// 2 (twice the bytes of an FP4 step). CTA c owns steps [lo(c), lo(c+1)).
+struct Sched {
+  int64_t n_sh_units, n_rt_units, U;
+  int nk_sh, nk_rt, w_sh;
+  int64_t S_sh, S, W_sh, W;
+  int G, aligned;
+
+  __device__ __forceinline__ int64_t ustart(int64_t u) const {
+    return u < n_sh_units ? u * nk_sh : S_sh + (u - n_sh_units) * nk_rt;
+  }
+  __device__ __forceinline__ int unk(int64_t u) const { return u < n_sh_units ? nk_sh : nk_rt; }
+  __device__ __forceinline__ int64_t unit_of(int64_t s) const {
+    return s < S_sh ? s / nk_sh : n_sh_units + (s - S_sh) / nk_rt;
+  }
+  // first step at or after weight position w
+  __device__ __forceinline__ int64_t step_at(int64_t w) const {
+    if (w <= W_sh) return (w + w_sh - 1) / w_sh;
+    return S_sh + (w - W_sh);
+  }
+  // weight position where step s starts
+  __device__ __forceinline__ int64_t wpos(int64_t s) const {
+    return s < S_sh ? s * w_sh : W_sh + (s - S_sh);
+  }
+  __device__ __forceinline__ int64_t lo(int c) const {
+    if (c >= G) return S;
+    if (aligned) return ustart(udiv(U * c, G));
+    return step_at(udiv(W * c, G));
+  }
+  // The CTA whose range holds step s: the largest c with lo(c) <= s. With
+  // lo(c) = step_at(floor(W c / G)), lo(c) <= s <=> floor(W c / G) <= wpos(s)
+  // <=> c <= (G (wpos(s) + 1) - 1) / W (and likewise over units when aligned).
+  __device__ __forceinline__ int cta_of(int64_t s) const {
+    const int64_t c = aligned ? udiv(static_cast<int64_t>(G) * (unit_of(s) + 1) - 1, U)
+                              : udiv(static_cast<int64_t>(G) * (wpos(s) + 1) - 1, W);
+    return c < G - 1 ? static_cast<int>(c) : G - 1;
+  }
+  // non-negative division, 32-bit when both operands fit
+  __device__ __forceinline__ static int64_t udiv(int64_t a, int64_t b) {
+    if (((a | b) >> 32) == 0) return static_cast<uint32_t>(a) / static_cast<uint32_t>(b);
+    return a / b;
+  }
+};
+
+__device__ __forceinline__ int64_t min64(int64_t x, int64_t y) { return x < y ? x : y; }
+
+__device__ __forceinline__ Sched make_sched(const Desc& d, const UnitArgs& a, bool down) {
+  Sched s;
+  const int tiles_sh = down ? d.D / kM : (d.has_shared ? d.I_sh / kM : 0);
+  const int tiles_rt = down ? d.D / kM : d.I / kM;
+  s.n_sh_units = static_cast<int64_t>(a.n_sh_chunks) * tiles_sh;
+  s.n_rt_units = static_cast<int64_t>(a.P.hdr[0]) * tiles_rt;
+  s.U = s.n_sh_units + s.n_rt_units;
+  s.nk_sh = down ? (d.has_shared ? d.I_sh / 256 : 1) : d.D / 128;
+  s.nk_rt = down ? d.I / 256 : d.D / 128;
+  s.w_sh = 2;
+  s.S_sh = s.n_sh_units * s.nk_sh;
+  s.S = s.S_sh + s.n_rt_units * s.nk_rt;
+  s.W_sh = s.S_sh * s.w_sh;
+  s.W = s.W_sh + s.n_rt_units * s.nk_rt;
+  s.G = a.G;
+  s.aligned = a.aligned;
+  return s;
+}
+
+struct UnitInfo {
+  int shared, e, pair0, np, tile;
+};
+
+__device__ __forceinline__ UnitInfo unit_info(const Desc& d, const UnitArgs& a, const Sched& s, int64_t u, bool down) {
+  UnitInfo r;
+  const int tiles_sh = down ? d.D / kM : (d.has_shared ? d.I_sh / kM : 1);
+  const int tiles_rt = down ? d.D / kM : d.I / kM;
+  if (u < s.n_sh_units) {
+    const int c = static_cast<int>(u / tiles_sh);
+    r.shared = 1;
+    r.tile = static_cast<int>(u - static_cast<int64_t>(c) * tiles_sh);
+    r.e = 0;
+    r.pair0 = c * a.CH;
+    r.np = min(a.CH, a.T - r.pair0);
+  } else {
+    const int64_t uu = u - s.n_sh_units;
+    const int c = static_cast<int>(uu / tiles_rt);
+    r.shared = 0;
+    r.tile = static_cast<int>(uu - static_cast<int64_t>(c) * tiles_rt);
+    r.e = a.P.chunk_expert[c];
+    r.pair0 = a.P.chunk_pair0[c];
+    r.np = a.P.chunk_np[c];
+  }
+  return r;
+}
+
 // out[t][tile rows] = bf16( bf16(sum of the token's routed partial rows in
-// ascending expert order) + bf16(shared-expert row) ), for every token.
-__device__ __noinline__ void finalize_tile(const UnitArgs& a, int D, int tile) {
-  for (int i = threadIdx.x; i < a.T * kM; i += blockDim.x) {
+// ascending expert order) + bf16(shared-expert row) ), for every token; run
+// by the 128 epilogue threads.
+// Positions are ascending with -1 padding at the end; all K loads of a row
+// are issued before the in-order sum, so they overlap.
+__device__ __forceinline__ void finalize_tile(const UnitArgs& a, int D, int tile, int tid, int nthr) {
+  for (int i = tid; i < a.T * kM; i += nthr) {
     const int t = i / kM;
     const int dd = tile * kM + (i - t * kM);
     const int32_t* pos = a.P.tok_pos + static_cast<int64_t>(t) * a.K;
+    int p[16];
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) p[j] = j < a.K ? __ldcg(pos + j) : -1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = p[j] >= 0 ? __ldcg(a.P.out_part + static_cast<int64_t>(p[j]) * D + dd) : 0.f;
     float r = 0.f;
-    for (int j = 0; j < a.K; ++j) {
-      const int p = pos[j];
-      if (p < 0) break;
-      r += __ldcg(a.P.out_part + static_cast<int64_t>(p) * D + dd);
-    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (p[j] >= 0) r += v[j];
     if (a.out_f32) a.out_f32[static_cast<int64_t>(t) * D + dd] = r;
     float o = round_bf16(r);
     if (a.use_shared) o += round_bf16(__ldcg(a.P.out_part + static_cast<int64_t>(t) * D + dd));
@@ -566,244 +809,371 @@ __device__ __noinline__ void finalize_tile(const UnitArgs& a, int D, int tile) {
   }
 }
 
-// One unit on the tensor cores. kDown = false: gate/up (A boxes = w1 and w3,
-// one 128-column k-box per stage); kDown = true: down (A boxes = two k-boxes
-// of w2). kFP8 selects the shared expert's E4M3 weights.
-template <bool kDown, bool kFP8, int NT>
-__device__ __forceinline__ void run_unit(const Desc& d, const CallMaps& cm, const UnitArgs& a, int e, int pair0,
-                                         int np, int tile) {
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Gate/up epilogue of one 128-row unit from the summed accumulators.
+template <int NT, bool kFP8>
+__device__ __forceinline__ void gateup_finish(const Desc& d, const UnitArgs& a, const UnitInfo& ui, int row,
+                                              const float (&g)[8 * NT], const float (&u)[8 * NT]) {
+  const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
+  uint8_t* hi_plane = a.P.act8;
+  uint8_t* lo_plane = a.P.act8 + a.P_max * I_act;
+  const int col = ui.tile * kM + row;
+#pragma unroll
+  for (int r = 0; r < 8 * NT; ++r) {
+    if (r < ui.np) {
+      const int p = ui.pair0 + r;
+      // reference: gate/up rounded to bf16, SwiGLU with clamp 10 in f32,
+      // rounded to bf16, times the bf16 routing weight, rounded to bf16
+      const float gf = round_bf16(g[r]);
+      const float uf = round_bf16(u[r]);
+      const float gc = gf > 10.f ? 10.f : gf;
+      const float uc = uf > 10.f ? 10.f : (uf < -10.f ? -10.f : uf);
+      const float sig = 1.f / (1.f + expf(-gc));
+      float av = round_bf16((gc * sig) * uc);
+      if (!kFP8) av = round_bf16(av * a.P.pair_wb[p]);
+      const float v = av * exp2i(a.P.pair_q[p]);
+      const __nv_fp8_storage_t hb = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+      const __half_raw hr = __nv_cvt_fp8_to_halfraw(hb, __NV_E4M3);
+      const float hf = __half2float(*reinterpret_cast<const __half*>(&hr));
+      const __nv_fp8_storage_t lb = __nv_cvt_float_to_fp8(v - hf, __NV_SATFINITE, __NV_E4M3);
+      hi_plane[static_cast<int64_t>(p) * I_act + col] = hb;
+      lo_plane[static_cast<int64_t>(p) * I_act + col] = lb;
+    }
+  }
+}
+
+// Persistent stream-K kernel for one phase. kDown = false: gate/up (A boxes =
+// w1 and w3 tiles of one 128-column k-step); kDown = true: down (A boxes = two
+// k-boxes of w2). One CTA per SM: warp 4 streams TMA, warp 5 issues tcgen05
+// copies and MMAs, warps 0-3 drain the TMEM accumulators (double-buffered, so
+// the next unit's MMAs overlap this unit's epilogue). A unit split between
+// CTAs writes f32 partials; the last of them (atomic ticket, no waiting) sums
+// the partials in CTA order and finishes the unit.
+template <bool kDown, int NT>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_constant__ Desc d,
+                                                         const __grid_constant__ CallMaps cm, UnitArgs a) {
   constexpr int BOXES = kDown ? 2 : 1;
   using L = SmemLayout<NT, BOXES>;
   constexpr int S_ = L::kNumStages;
   constexpr int N = 16 * NT;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = align1024(smem_raw);
-  uint8_t* stages = base;
-  uint8_t* sfb = base + S_ * L::kStage;
-  Bars* bars = reinterpret_cast<Bars*>(sfb + 512);
+  static_assert(S_ >= 2 && S_ <= 4, "stage count");
+  static_assert(sizeof(Bars) <= L::kBarBytes, "barrier block");
+  // TMEM (256 columns per CTA, two CTAs per SM): accumulator buffers at 0 and
+  // 96 (gate at +0, up at +48), A scales at 192 + 8*stage, B scales at 224 + 4*buffer
+  constexpr uint32_t kAcc = 96;
+  constexpr uint32_t kSfa = 192;
+  constexpr uint32_t kSfb = 224;
+  constexpr int NP = 8 * NT;                        // pairs per unit (hi and lo columns summed)
+  constexpr int kSlot = (kDown ? 1 : 2) * kM * NP;  // floats per partial slot
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // the 128B-swizzled stages need a 1024-aligned base; no slack is reserved
+  // for realignment (two CTAs per SM leave none), so check it
+  if (smem_u32(smem_raw) & 1023u) {
+    if (threadIdx.x == 0) report(a.status, HS_DEV_SMEM_ALIGN);
+    return;
+  }
+  uint8_t* base = smem_raw;
+  Bars* bars = reinterpret_cast<Bars*>(base + S_ * L::kStage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = d.D;
-  const int Iu = kFP8 ? d.I_sh : d.I;
-  const int nk = kDown ? Iu / 256 : D / 128;
-  const uint32_t tx_box = kFP8 ? kBoxBytes : kBoxBytes / 2;  // packed e2m1 counts half
-  const uint32_t tx = 2 * tx_box + L::kB + L::kSF;
-  const uint8_t* sbv = kDown ? a.P.sb2 : a.P.sb1;
+  const Sched sc = make_sched(d, a, kDown);
+  const int c = blockIdx.x;
+  const int64_t s_begin = sc.lo(c), s_end = sc.lo(c + 1);
 
-  // ---- setup: barriers, TMEM, B scale factors ----
   if (threadIdx.x == 0) {
     for (int i = 0; i < S_; ++i) {
       mbar_init(&bars->full[i], 1);
       mbar_init(&bars->empty[i], 1);
     }
-    mbar_init(&bars->accum, 1);
-    bars->last = 0;
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->acc_full[i], 1);
+      mbar_init(&bars->acc_empty[i], 4);
+    }
+    mbar_init(&bars->mma_done, 1);
+    bars->issued = 0;
+    bars->consumed = 0;
     fence_mbar_init();
   }
-  if (warp == 0) tc5::tmem_alloc(&bars->tmem, kTmemCols);
-  if (threadIdx.x < 128) {
-    // SFB atom: word (m0, m1) = scale of B row n = m0 + 32*m1 in all 4 k-blocks
-    const int m0 = threadIdx.x >> 2, m1 = threadIdx.x & 3;
-    const int n = m0 + 32 * m1;
-    uint32_t b = 127u;
-    if (n < N) {
-      const int r = n % (8 * NT);
-      if (r < np) b = sbv[pair0 + r];
-    }
-    *reinterpret_cast<uint32_t*>(sfb + m0 * 16 + m1 * 4) = b * 0x01010101u;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
+  if (warp == 0) tc5::tmem_alloc(&bars->tmem, 256);
   tc5::fence_before_sync();
   __syncthreads();
   tc5::fence_after_sync();
   const uint32_t tmem = bars->tmem;
 
   if (warp == 4) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      const CUtensorMap* wm = kDown ? (kFP8 ? &d.tm_sw2 : &d.tm_w2) : (kFP8 ? &d.tm_sw13 : &d.tm_w13);
+    // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
+    int64_t step = 0;
+    bool ok = true;
+    for (int64_t s = s_begin; s < s_end && ok;) {
+      const int64_t u = sc.unit_of(s);
+      const UnitInfo ui = unit_info(d, a, sc, u, kDown);
+      const int64_t us = sc.ustart(u);
+      const int k0 = static_cast<int>(s - us);
+      const int k1 = static_cast<int>(min64(static_cast<int64_t>(sc.unk(u)), s_end - us));
+      const bool fp8 = ui.shared != 0;
+      const CUtensorMap* wm = kDown ? (fp8 ? &d.tm_sw2 : &d.tm_w2) : (fp8 ? &d.tm_sw13 : &d.tm_w13);
       const CUtensorMap* bm = kDown ? &cm.tm_act8 : &cm.tm_x8;
-      int ya = 0, yb = 0;
+      // first weight row of the unit's step 0 and the rows per step (two tiles
+      // of 128 rows per stage in both phases)
+      int64_t y0;
       if (!kDown) {
-        ya = kFP8 ? tile * kM : (2 * e) * d.I + tile * kM;
-        yb = kFP8 ? d.I_sh + tile * kM : (2 * e + 1) * d.I + tile * kM;
+        y0 = fp8 ? static_cast<int64_t>(ui.tile) * (D / kM) * 256
+                 : (static_cast<int64_t>(ui.e) * (d.I / kM) + ui.tile) * (D / kM) * 256;
       } else {
-        ya = yb = kFP8 ? tile * kM : e * D + tile * kM;
+        y0 = fp8 ? static_cast<int64_t>(ui.tile) * (d.I_sh / kM) * kM
+                 : (static_cast<int64_t>(ui.e) * (D / kM) + ui.tile) * (d.I / kM) * kM;
       }
-      for (int kc = 0; kc < nk; ++kc) {
-        const int st = kc % S_;
-        if (kc >= S_ && !mbar_wait(&bars->empty[st], ((kc / S_) - 1) & 1)) {
-          report(a.status, HS_DEV_TIMEOUT);
-          break;
+      const uint8_t* sf0;
+      if (!kDown) {
+        sf0 = fp8 ? d.sh_s13a + static_cast<int64_t>(ui.tile) * (D / kM) * 1024
+                  : d.s13a + (static_cast<int64_t>(ui.e) * (d.I / kM) + ui.tile) * (D / kM) * 1024;
+      } else {
+        sf0 = fp8 ? d.sh_s2a + static_cast<int64_t>(ui.tile) * (d.I_sh / kM) * 512
+                  : d.s2a + (static_cast<int64_t>(ui.e) * (D / kM) + ui.tile) * (d.I / kM) * 512;
+      }
+      const uint32_t tx = 2 * (fp8 ? kBoxBytes : kBoxBytes / 2) + L::kB + 2 * 512;
+      const uint8_t* sbv = kDown ? a.P.sb2 : a.P.sb1;
+      for (int k = k0; k < k1; ++k, ++step) {
+        const int st = static_cast<int>(step % S_);
+        if (step >= S_) {
+          bool w = true;
+          if (lane == 0) w = mbar_wait(&bars->empty[st], static_cast<uint32_t>(((step / S_) - 1) & 1));
+          w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+          if (!w) {
+            if (lane == 0) report(a.status, HS_DEV_TIMEOUT);
+            ok = false;
+            break;
+          }
         }
-        uint8_t* S = stages + st * L::kStage;
+        uint8_t* S = base + st * L::kStage;
         uint8_t* Bs = S + L::kA;
         uint8_t* SF = Bs + L::kB;
-        mbar_arrive_expect_tx(&bars->full[st], tx);
-        const int xa = kDown ? kc * 256 : kc * 128;
-        tma_load_2d(S, wm, &bars->full[st], xa, ya);
-        tma_load_2d(S + kBoxBytes, wm, &bars->full[st], kDown ? xa + 128 : xa, yb);
-        for (int b = 0; b < BOXES; ++b)
-          for (int pl = 0; pl < 2; ++pl)
-            for (int nt = 0; nt < NT; ++nt)
-              tma_load_2d(Bs + ((b * 2 + pl) * NT + nt) * 1024, bm, &bars->full[st], xa + b * 128,
-                          static_cast<int>(pl * a.P_max) + pair0 + 8 * nt);
-        for (int i = 0; i < 2; ++i) {
-          const uint8_t* atom;
-          if (!kDown) {
-            atom = kFP8 ? d.sh_s13a + ((static_cast<int64_t>(i) * (d.I_sh / kM) + tile) * (D / kM) + kc) * 512
-                        : d.s13a + (((static_cast<int64_t>(e) * 2 + i) * (d.I / kM) + tile) * (D / kM) + kc) * 512;
-          } else {
-            atom = kFP8 ? d.sh_s2a + (static_cast<int64_t>(tile) * (d.I_sh / kM) + kc * 2 + i) * 512
-                        : d.s2a + ((static_cast<int64_t>(e) * (D / kM) + tile) * (d.I / kM) + kc * 2 + i) * 512;
+        if (k == k0) {
+          // the unit's B scale atom: word (m0, m1) = scale of B row n = m0 + 32*m1
+          for (int wi = lane; wi < 128; wi += 32) {
+            const int m0 = wi >> 2, m1 = wi & 3;
+            const int n = m0 + 32 * m1;
+            uint32_t b = 127u;
+            if (n < N) {
+              const int r = n % (8 * NT);
+              if (r < ui.np) b = sbv[ui.pair0 + r];
+            }
+            *reinterpret_cast<uint32_t*>(SF + 1024 + m0 * 16 + m1 * 4) = b * 0x01010101u;
           }
-          bulk_load(SF + i * 512, atom, 512, &bars->full[st]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bars->full[st], tx);
+          const int xa = kDown ? k * 256 : k * 128;
+          tma_load_2d(S, wm, &bars->full[st], 0, static_cast<int>(y0 + static_cast<int64_t>(k) * 256));
+          for (int b = 0; b < BOXES; ++b)
+            tma_load_3d(Bs + b * 2 * NT * 1024, bm, &bars->full[st], xa + b * 128, ui.pair0, 0);
+          bulk_load(SF, sf0 + static_cast<int64_t>(k) * 1024, 1024, &bars->full[st]);
         }
       }
+      s = us + k1;
     }
+    if (lane == 0) bars->issued = static_cast<int32_t>(step);
   } else if (warp == 5) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer (lane 0) ----------------
     if (lane == 0) {
-      tc5::cp_sf_32x128b(tmem + kSfbCol, tc5::sdesc_sf(smem_u32(sfb)));
-      const uint32_t afmt = kFP8 ? 0u : 5u;
-      for (int kc = 0; kc < nk; ++kc) {
-        const int st = kc % S_;
-        if (!mbar_wait(&bars->full[st], (kc / S_) & 1)) {
+      int64_t step = 0;
+      int seg = 0;
+      bool ok = true;
+      for (int64_t s = s_begin; s < s_end && ok; ++seg) {
+        const int64_t u = sc.unit_of(s);
+        const int64_t us = sc.ustart(u);
+        const int k0 = static_cast<int>(s - us);
+        const int k1 = static_cast<int>(min64(static_cast<int64_t>(sc.unk(u)), s_end - us));
+        const uint32_t afmt = u < sc.n_sh_units ? 0u : 5u;
+        const int buf = seg & 1;
+        if (seg >= 2 && !mbar_wait(&bars->acc_empty[buf], static_cast<uint32_t>(((seg >> 1) - 1) & 1))) {
           report(a.status, HS_DEV_TIMEOUT);
           break;
         }
         tc5::fence_after_sync();
-        uint8_t* S = stages + st * L::kStage;
-        const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
-        const uint32_t sfa0 = tmem + kSfaCol + st * 8;
-        tc5::cp_sf_32x128b(sfa0, tc5::sdesc_sf(sSF));
-        tc5::cp_sf_32x128b(sfa0 + 4, tc5::sdesc_sf(sSF + 512));
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const uint64_t ad = tc5::sdesc_sw128(sA + i * kBoxBytes);
-          const uint64_t bd = tc5::sdesc_sw128(sB + (kDown ? i * 2 * NT * 1024 : 0));
-          const uint32_t dcol = tmem + (kDown ? 0 : (i ? kAccUp : 0));
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t id = tc5::idesc_mxf8f6f4(afmt, N, j, j);
-            const uint32_t acc = (kc > 0 || j > 0 || (kDown && i > 0)) ? 1u : 0u;
-            tc5::mma_mxf8f6f4(dcol, ad + 2 * j, bd + 2 * j, id, acc, (sfa0 + 4 * i) | (static_cast<uint32_t>(j) << 30),
-                              (tmem + kSfbCol) | (static_cast<uint32_t>(j) << 30));
+        const uint32_t acc = tmem + buf * kAcc;
+        const uint32_t sfb = tmem + kSfb + buf * 4;
+        for (int k = k0; k < k1; ++k, ++step) {
+          const int st = static_cast<int>(step % S_);
+          if (!mbar_wait(&bars->full[st], static_cast<uint32_t>((step / S_) & 1))) {
+            report(a.status, HS_DEV_TIMEOUT);
+            ok = false;
+            break;
           }
+          tc5::fence_after_sync();
+          uint8_t* S = base + st * L::kStage;
+          const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
+          if (k == k0) tc5::cp_sf_32x128b(sfb, tc5::sdesc_sf(sSF + 1024));
+          const uint32_t sfa0 = tmem + kSfa + st * 8;
+          tc5::cp_sf_32x128b(sfa0, tc5::sdesc_sf(sSF));
+          tc5::cp_sf_32x128b(sfa0 + 4, tc5::sdesc_sf(sSF + 512));
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint64_t ad = tc5::sdesc_sw128(sA + i * kBoxBytes);
+            const uint64_t bd = tc5::sdesc_sw128(sB + (kDown ? i * 2 * NT * 1024 : 0));
+            const uint32_t dcol = acc + (kDown ? 0u : (i ? static_cast<uint32_t>(kAccUp) : 0u));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t id = tc5::idesc_mxf8f6f4(afmt, N, j, j);
+              const uint32_t accum = (k > k0 || j > 0 || (kDown && i > 0)) ? 1u : 0u;
+              tc5::mma_mxf8f6f4(dcol, ad + 2 * j, bd + 2 * j, id, accum,
+                                (sfa0 + 4 * i) | (static_cast<uint32_t>(j) << 30),
+                                sfb | (static_cast<uint32_t>(j) << 30));
+            }
+          }
+          tc5::commit(&bars->empty[st]);
         }
-        tc5::commit(&bars->empty[st]);
+        tc5::commit(&bars->acc_full[buf]);
+        s = us + k1;
       }
-      tc5::commit(&bars->accum);
+      // every tcgen05 operation of this thread done before TMEM is freed
+      bars->consumed = static_cast<int32_t>(step);
+      tc5::commit(&bars->mma_done);
+      if (!mbar_wait(&bars->mma_done, 0)) report(a.status, HS_DEV_TIMEOUT);
     }
   } else {
     // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31) ----------------
-    const int row = 32 * warp + lane;  // weight row within the tile
-    if (!mbar_wait(&bars->accum, 0)) report(a.status, HS_DEV_TIMEOUT);
-    tc5::fence_after_sync();
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
-    float c0[N];
-#pragma unroll
-    for (int q = 0; q < NT; ++q) {
-      float v[16];
-      tc5::ld_32x32b_x16(lane_base + q * 16, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) c0[q * 16 + i] = v[i];
-    }
-    if (!kDown) {
-      float c1[N];
+    const int row = 32 * warp + lane;
+    const int etid = threadIdx.x;  // 0..127
+    const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+    int seg = 0;
+    for (int64_t s = s_begin; s < s_end; ++seg) {
+      const int64_t u = sc.unit_of(s);
+      const int64_t us = sc.ustart(u);
+      const int nk = sc.unk(u);
+      const int k1 = static_cast<int>(min64(static_cast<int64_t>(nk), s_end - us));
+      const UnitInfo ui = unit_info(d, a, sc, u, kDown);
+      const int buf = seg & 1;
+      if (!mbar_wait(&bars->acc_full[buf], static_cast<uint32_t>((seg >> 1) & 1))) {
+        if (etid == 0) report(a.status, HS_DEV_TIMEOUT);
+        break;
+      }
+      tc5::fence_after_sync();
+      float c0[N], c1[N];
+      const uint32_t acc = tmem + lane_off + buf * kAcc;
 #pragma unroll
       for (int q = 0; q < NT; ++q) {
         float v[16];
-        tc5::ld_32x32b_x16(lane_base + kAccUp + q * 16, v);
+        tc5::ld_32x32b_x16(acc + q * 16, v);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) c1[q * 16 + i] = v[i];
-      }
-      tc5::wait_ld();
-      const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
-      uint8_t* hi_plane = a.P.act8;
-      uint8_t* lo_plane = a.P.act8 + a.P_max * I_act;
-      const int col = tile * kM + row;
+        for (int i = 0; i < 16; ++i) c0[q * 16 + i] = v[i];
+        if (!kDown) {
+          tc5::ld_32x32b_x16(acc + kAccUp + q * 16, v);
 #pragma unroll
-      for (int r = 0; r < 8 * NT; ++r) {
-        if (r < np) {
-          const int p = pair0 + r;
-          // reference: gate/up rounded to bf16, SwiGLU with clamp 10 in f32,
-          // rounded to bf16, times the bf16 routing weight, rounded to bf16
-          const float gf = round_bf16(c0[r] + c0[8 * NT + r]);
-          const float uf = round_bf16(c1[r] + c1[8 * NT + r]);
-          const float gc = gf > 10.f ? 10.f : gf;
-          const float uc = uf > 10.f ? 10.f : (uf < -10.f ? -10.f : uf);
-          const float sig = 1.f / (1.f + expf(-gc));
-          float av = round_bf16((gc * sig) * uc);
-          if (!kFP8) av = round_bf16(av * a.P.pair_wb[p]);
-          const float v = av * exp2i(a.P.pair_q[p]);
-          const __nv_fp8_storage_t hb = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
-          const __half_raw hr = __nv_cvt_fp8_to_halfraw(hb, __NV_E4M3);
-          const float hf = __half2float(*reinterpret_cast<const __half*>(&hr));
-          const __nv_fp8_storage_t lb = __nv_cvt_float_to_fp8(v - hf, __NV_SATFINITE, __NV_E4M3);
-          hi_plane[static_cast<int64_t>(p) * I_act + col] = hb;
-          lo_plane[static_cast<int64_t>(p) * I_act + col] = lb;
+          for (int i = 0; i < 16; ++i) c1[q * 16 + i] = v[i];
         }
       }
-    } else {
       tc5::wait_ld();
+      tc5::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+      // hi + lo columns of each pair: the full dot product of this segment
+      float g[NP], v[NP];
 #pragma unroll
-      for (int r = 0; r < 8 * NT; ++r) {
-        if (r < np) {
-          const int p = pair0 + r;
-          a.P.out_part[static_cast<int64_t>(p) * D + tile * kM + row] = c0[r] + c0[8 * NT + r];
+      for (int r = 0; r < NP; ++r) {
+        g[r] = c0[r] + c0[NP + r];
+        v[r] = kDown ? 0.f : c1[r] + c1[NP + r];
+      }
+
+      // which CTAs share this unit
+      const int cf = sc.cta_of(us);
+      const int cl = sc.cta_of(us + nk - 1);
+      bool finish = (cf == cl);
+      const int k0 = static_cast<int>(s - us);
+      if (!finish) {
+        // a CTA splits at most its first and its last unit: slots 2c and 2c+1
+        float* slot = a.part + (2 * static_cast<int64_t>(c) + (u == sc.unit_of(s_begin) ? 0 : 1)) * kSlot;
+#pragma unroll
+        for (int n = 0; n < NP; ++n) {
+          __stcg(slot + n * kM + row, g[n]);
+          if (!kDown) __stcg(slot + (NP + n) * kM + row, v[n]);
+        }
+        __threadfence();
+        epi_bar();
+        if (etid == 0) {
+          // ticket counts the unit's steps: the segment that completes them is last
+          const uint32_t mine = static_cast<uint32_t>(k1 - k0);
+          bars->flag = atomicAdd(&a.ucount[u], mine) + mine == static_cast<uint32_t>(nk);
+        }
+        epi_bar();
+        finish = bars->flag != 0;
+        epi_bar();  // every thread has read the flag before it is reused
+        if (finish) {
+          __threadfence();
+          // sum every segment's partial in CTA order (this CTA's from registers)
+#pragma unroll
+          for (int n = 0; n < NP; ++n) {
+            g[n] = 0.f;
+            v[n] = 0.f;
+          }
+          int64_t lc = sc.lo(cf);
+          for (int cc = cf; cc <= cl; ++cc) {
+            const int64_t ln = sc.lo(cc + 1);
+            const bool empty_cta = !(lc < ln);
+            const bool first_of_cta = lc >= us;  // the unit is this CTA's first segment
+            lc = ln;
+            if (empty_cta) continue;
+            const float* sl = a.part + (2 * static_cast<int64_t>(cc) + (first_of_cta ? 0 : 1)) * kSlot;
+#pragma unroll
+            for (int n = 0; n < NP; ++n) {
+              g[n] += __ldcg(sl + n * kM + row);
+              if (!kDown) v[n] += __ldcg(sl + (NP + n) * kM + row);
+            }
+          }
         }
       }
+      if (finish) {
+        if (!kDown) {
+          if (ui.shared)
+            gateup_finish<NT, true>(d, a, ui, row, g, v);
+          else
+            gateup_finish<NT, false>(d, a, ui, row, g, v);
+        } else {
+#pragma unroll
+          for (int r = 0; r < NP; ++r)
+            if (r < ui.np) a.P.out_part[static_cast<int64_t>(ui.pair0 + r) * D + ui.tile * kM + row] = g[r];
+          // finalize the 128-row slice of D once every unit on it is done
+          __threadfence();
+          epi_bar();
+          if (etid == 0) {
+            const uint32_t total = static_cast<uint32_t>(a.n_sh_chunks + a.P.hdr[0]);
+            bars->flag = atomicAdd(&a.P.dcount[ui.tile], 1u) == total - 1u;
+          }
+          epi_bar();
+          const bool fin = bars->flag != 0;
+          epi_bar();
+          if (fin) {
+            __threadfence();
+            finalize_tile(a, D, ui.tile, etid, 128);
+          }
+        }
+      }
+      s = us + k1;
     }
+    // no unit at all (every pair skipped, no shared expert): write zeros
+    if (kDown && sc.U == 0)
+      for (int tile = c; tile < D / kM; tile += sc.G) finalize_tile(a, D, tile, etid, 128);
   }
 
-  // ---- teardown: every tcgen05 op has completed (accum barrier / ld waits) ----
   tc5::fence_before_sync();
+  __syncthreads();
+  // copies issued but never consumed (only after a timed-out wait): let them
+  // land before the CTA's shared memory is released
+  if (threadIdx.x == 128) {
+    for (int64_t k = bars->consumed; k < bars->issued; ++k)
+      if (!mbar_wait(&bars->full[k % S_], static_cast<uint32_t>((k / S_) & 1))) {
+        report(a.status, HS_DEV_TIMEOUT);
+        break;
+      }
+  }
   __syncthreads();
   if (warp == 0) {
     tc5::fence_after_sync();
-    tc5::tmem_dealloc(tmem, kTmemCols);
+    tc5::tmem_dealloc(tmem, 256);
   }
-
-  if (kDown) {
-    // ---- finalize this 128-row slice of D if this CTA is the last one on it ----
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const uint32_t total = static_cast<uint32_t>(a.n_sh_chunks + a.P.hdr[0]);
-      bars->last = atomicAdd(&a.P.dcount[tile], 1u) == total - 1u;
-    }
-    __syncthreads();
-    if (bars->last) {
-      __threadfence();
-      finalize_tile(a, D, tile);
-    }
-  }
-}
-
-template <bool kDown, int NT>
-__global__ void __launch_bounds__(kThreads) unit_kernel(const __grid_constant__ Desc d,
-                                                           const __grid_constant__ CallMaps cm, UnitArgs a) {
-  int u = blockIdx.x;
-  const int tiles_sh = kDown ? d.D / kM : (d.has_shared ? d.I_sh / kM : 0);
-  const int tiles = kDown ? d.D / kM : d.I / kM;
-  const int n_sh_units = a.n_sh_chunks * tiles_sh;
-  if (u < n_sh_units) {
-    const int c = u / tiles_sh;
-    const int tile = u - c * tiles_sh;
-    const int pair0 = c * a.CH;
-    run_unit<kDown, true, NT>(d, cm, a, 0, pair0, min(a.CH, a.T - pair0), tile);
-    return;
-  }
-  u -= n_sh_units;
-  const int c = u / tiles;
-  const int tile = u - c * tiles;
-  if (c >= a.P.hdr[0]) {
-    // no unit at all (every pair skipped, no shared expert): the first chunk
-    // slot of each tile writes the all-zero result
-    if (kDown && c == 0 && a.n_sh_chunks == 0) finalize_tile(a, d.D, tile);
-    return;
-  }
-  run_unit<kDown, false, NT>(d, cm, a, a.P.chunk_expert[c], a.P.chunk_pair0[c], a.P.chunk_np[c], tile);
 }
 
 // ---------------------------------------------------------------------------
@@ -881,39 +1251,73 @@ static int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, ui
   return HS_OK;
 }
 
+// 3D map [planes][rows][cols]: box cols x box_rows x planes, 128B swizzle.
+static int make_map_3d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t planes,
+                       uint64_t pitch, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return HS_ERR_UNSUPPORTED;
+  cuuint64_t dims[3] = {cols, rows, planes};
+  cuuint64_t strides[2] = {pitch, pitch * rows};
+  cuuint32_t box[3] = {128, box_rows, static_cast<cuuint32_t>(planes)};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_cuda_error(static_cast<int>(r));
+    return HS_ERR_CUDA;
+  }
+  return HS_OK;
+}
+
 static bool dim_ok(int64_t v, int64_t mult, int64_t lo, int64_t hi) { return v % mult == 0 && v >= lo && v <= hi; }
 static bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 template <bool kDown, int NT>
-static int launch_units(const Desc& d, const CallMaps& cm, const UnitArgs& a, int64_t units, cudaStream_t st) {
+static int launch_sk(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaStream_t st) {
   constexpr int bytes = SmemLayout<NT, kDown ? 2 : 1>::kBytes;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   HS_CUDA_CHECK(cudaGetDevice(&dev));
   const uint64_t bit = 1ull << (dev & 63);
   if (!(done.load() & bit)) {
-    HS_CUDA_CHECK(cudaFuncSetAttribute(unit_kernel<kDown, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    HS_CUDA_CHECK(cudaFuncSetAttribute(sk_kernel<kDown, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
     done.fetch_or(bit);
   }
-  unit_kernel<kDown, NT><<<static_cast<unsigned>(units), kThreads, bytes, st>>>(d, cm, a);
+  sk_kernel<kDown, NT><<<static_cast<unsigned>(a.G), kThreads, bytes, st>>>(d, cm, a);
   return check_launch();
 }
 
 template <bool kDown>
-static int launch_nt(int NT, const Desc& d, const CallMaps& cm, const UnitArgs& a, int64_t units, cudaStream_t st) {
+static int launch_nt(int NT, const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaStream_t st) {
   switch (NT) {
     case 1:
-      return launch_units<kDown, 1>(d, cm, a, units, st);
+      return launch_sk<kDown, 1>(d, cm, a, st);
     case 2:
-      return launch_units<kDown, 2>(d, cm, a, units, st);
+      return launch_sk<kDown, 2>(d, cm, a, st);
     default:
-      return launch_units<kDown, 3>(d, cm, a, units, st);
+      return launch_sk<kDown, 3>(d, cm, a, st);
   }
 }
 
+// Number of SMs of the current device, cached.
+static int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int v = cache[dev].load();
+  if (v <= 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev].store(v);
+  }
+  return v;
+}
+
 static int plan_smem(int E, int npairs) {
-  return static_cast<int>(((npairs <= kLocalPairs ? npairs : 0) + 4 * E + 2 + (kPlanThreads / 32) * E) *
-                          sizeof(int32_t));
+  const int cached = npairs <= kLocalPairs ? 2 * npairs : 0;  // ids and post-duplicate experts
+  const int general = 4 * E + 2 + (kPlanThreads / 32) * E;
+  const int fast = npairs <= kFastPlanPairs ? 2 * npairs : 0;
+  return static_cast<int>((cached + std::max(general, fast)) * sizeof(int32_t));
 }
 
 static int launch_plan(const PlanArgs& pa, const Plan& P, int grid, cudaStream_t st) {
@@ -952,9 +1356,12 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
   d.has_shared = w->sh_w13 != nullptr;
   int st;
   const uint64_t E = w->E, D = w->D, I = w->I;
-  if ((st = make_map(&d.tm_w13, w->w13, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, D, E * 2 * I, D / 2, 128, kM)))
+  // tiled weights: rows of 128 values (64 packed bytes), two tiles (256 rows) per box
+  if ((st = make_map(&d.tm_w13, w->w13, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 128, E * 2 * I * (D / 128), 64, 128,
+                     256)))
     return st;
-  if ((st = make_map(&d.tm_w2, w->w2, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, I, E * D, I / 2, 128, kM))) return st;
+  if ((st = make_map(&d.tm_w2, w->w2, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 128, E * D * (I / 128), 64, 128, 256)))
+    return st;
   d.s13a = static_cast<const uint8_t*>(w->s13);
   d.s2a = static_cast<const uint8_t*>(w->s2);
   if (d.has_shared) {
@@ -964,8 +1371,11 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
       return HS_ERR_ALIGN;
     d.I_sh = static_cast<int32_t>(w->I_sh);
     const uint64_t Ish = w->I_sh;
-    if ((st = make_map(&d.tm_sw13, w->sh_w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, D, 2 * Ish, D, 128, kM))) return st;
-    if ((st = make_map(&d.tm_sw2, w->sh_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, Ish, D, Ish, 128, kM))) return st;
+    if ((st = make_map(&d.tm_sw13, w->sh_w13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, 2 * Ish * (D / 128), 128, 128,
+                       256)))
+      return st;
+    if ((st = make_map(&d.tm_sw2, w->sh_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, D * (Ish / 128), 128, 128, 256)))
+      return st;
     d.sh_s13a = static_cast<const uint8_t*>(w->sh_s13);
     d.sh_s2a = static_cast<const uint8_t*>(w->sh_s2);
   }
@@ -977,7 +1387,7 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
 
 extern "C" size_t hs_moe_workspace_size(int64_t T, int64_t top_k, int64_t D, int64_t I, int64_t I_sh) {
   if (T < 0 || top_k < 1) return 0;
-  return geometry(T, top_k, D, I, I_sh).total;
+  return geometry(T, top_k, D, I, I_sh, kCtasPerSm * sm_count()).total;
 }
 
 extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx, const float* topk_w,
@@ -996,7 +1406,7 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
     return HS_ERR_ALIGN;
   use_shared = (use_shared && d.has_shared) ? 1 : 0;
   if (!d.has_shared) d.I_sh = 0;
-  const Geometry g = geometry(T, top_k, d.D, d.I, d.has_shared ? d.I_sh : 0);
+  const Geometry g = geometry(T, top_k, d.D, d.I, d.has_shared ? d.I_sh : 0, kCtasPerSm * sm_count());
   if (workspace_bytes < g.total) return HS_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Plan P = plan_views(g, workspace);
@@ -1007,8 +1417,8 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
 
   CallMaps cm;
   int rc;
-  if ((rc = make_map(&cm.tm_x8, P.x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, d.D, 2 * g.P_max, d.D, 128, 8))) return rc;
-  if ((rc = make_map(&cm.tm_act8, P.act8, CU_TENSOR_MAP_DATA_TYPE_UINT8, g.I_act, 2 * g.P_max, g.I_act, 128, 8)))
+  if ((rc = make_map_3d(&cm.tm_x8, P.x8, d.D, g.P_max, 2, d.D, 8 * NT))) return rc;
+  if ((rc = make_map_3d(&cm.tm_act8, P.act8, g.I_act, g.P_max, 2, g.I_act, 8 * NT)))
     return rc;
 
   PlanArgs pa;
@@ -1028,6 +1438,8 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   pa.local_rows = local_rows ? 1 : 0;
   pa.po = PermuteOut{nullptr, nullptr, nullptr};
   pa.status = dev_status;
+  pa.ucount = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + g.off_ucount);
+  pa.n_ucount = g.U_gu + g.U_dn;
   if ((rc = launch_plan(pa, P, 1 + static_cast<int>(T), st))) return rc;
   if (!local_rows) {
     gather_kernel<<<static_cast<unsigned>(npairs), 256, 0, st>>>(P, static_cast<int>(T), g.P_max, d.D);
@@ -1045,12 +1457,13 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   a.out = static_cast<__nv_bfloat16*>(out);
   a.out_f32 = out_f32;
   a.status = dev_status;
-  const int64_t gu_units = static_cast<int64_t>(a.n_sh_chunks) * (use_shared ? d.I_sh / kM : 0) +
-                           g.C_max * (d.I / kM);
-  const int64_t dn_units = (static_cast<int64_t>(a.n_sh_chunks) + g.C_max) * (d.D / kM);
-  if (gu_units > 0x7fffffff || dn_units > 0x7fffffff) return HS_ERR_BAD_SHAPE;
-  if ((rc = launch_nt<false>(NT, d, cm, a, gu_units, st))) return rc;
-  return launch_nt<true>(NT, d, cm, a, dn_units, st);
+  a.G = g.G;
+  a.aligned = g.aligned;
+  a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.off_part);
+  a.ucount = pa.ucount;
+  if ((rc = launch_nt<false>(NT, d, cm, a, st))) return rc;
+  a.ucount = pa.ucount + g.U_gu;
+  return launch_nt<true>(NT, d, cm, a, st);
 }
 
 extern "C" size_t hs_moe_permute_workspace_size(int64_t T, int64_t top_k, int64_t E) {
@@ -1093,6 +1506,8 @@ extern "C" int hs_moe_permute(const int64_t* topk_idx, int64_t T, int64_t top_k,
   pa.local_rows = 0;
   pa.po = PermuteOut{pos_to_expert, expert_count, num_pos};
   pa.status = dev_status;
+  pa.ucount = nullptr;
+  pa.n_ucount = 0;
   int rc = launch_plan(pa, P, 1, st);
   if (rc) return rc;
   if (x_expanded) {

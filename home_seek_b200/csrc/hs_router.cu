@@ -128,8 +128,14 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ partial, in
     key[i] = 0ull;
     sc[i] = 0.f;
     if (e < E) {
+      // all k-split partials are loaded before the in-order sum (independent loads)
+      float pv[16];
+#pragma unroll
+      for (int s = 0; s < 16; ++s) pv[s] = s < ksplit ? __ldcg(partial + (static_cast<int64_t>(s) * T + t) * E + e) : 0.f;
       float l = 0.f;
-      for (int s = 0; s < ksplit; ++s) l += partial[(static_cast<int64_t>(s) * T + t) * E + e];
+#pragma unroll
+      for (int s = 0; s < 16; ++s)
+        if (s < ksplit) l += pv[s];
       float lb = round_bf16(l);
       if (bias) lb = round_bf16(lb + __bfloat162float(bias[e]));
       if (logits_out) logits_out[static_cast<int64_t>(t) * E + e] = __float2bfloat16_rn(lb);
@@ -229,8 +235,8 @@ extern "C" size_t hs_router_workspace_size(int64_t T, int64_t D, int64_t E) {
 extern "C" int hs_router_topk(const void* hidden, const void* gate, const void* bias, int64_t T, int64_t D, int64_t E,
                               int64_t top_k, float routed_scaling, int64_t* topk_idx, float* topk_w, void* logits_out,
                               void* workspace, size_t workspace_bytes, void* stream) {
-  if (T < 0 || D % kKSplitCols != 0 || D < kKSplitCols || E % 16 != 0 || E < 16 || E > 1024 || top_k < 1 ||
-      top_k > 16 || top_k > E)
+  if (T < 0 || D % kKSplitCols != 0 || D < kKSplitCols || D > 16 * kKSplitCols || E % 16 != 0 || E < 16 ||
+      E > 1024 || top_k < 1 || top_k > 16 || top_k > E)
     return HS_ERR_BAD_SHAPE;
   if (T == 0) return HS_OK;
   if (T > 65535 * 8) return HS_ERR_BAD_SHAPE;

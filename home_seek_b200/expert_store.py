@@ -7,18 +7,21 @@ LRU / safetensors mmap; `_load_expert_weights` engine.py:1084-1129,
 expert_cache.py:7-121) and the GPU-resident FP8 shared experts
 (`_load_shared_experts_gpu` engine.py:1743-1777). On a B200 every expert of
 every layer fits in HBM (43 x 256 x 13,369,344 B = 147.2 GB), so the cache
-collapses into one allocation per layer and a lookup returns views.
+collapses into one allocation per layer, in the layout the kernels stream.
 
-Layout per layer (what the kernels stream with TMA):
-  w13 [E][2][I][D/2] u8 packed e2m1 (w1 rows then w3 rows of each expert)
-  s13 [E][2][I/128][D/128][512] u8 UE8M0 in scale-factor atoms (layout.py)
-  w2  [E][D][I/2]    u8 packed e2m1
+Layout per layer (what the kernels stream with TMA; see layout.py):
+  w13 [E][I/128][D/128][2][128][64] u8 packed e2m1 tiles (w1 tile, w3 tile)
+  s13 [E][I/128][D/128][2][512] u8 UE8M0 scale-factor atoms
+  w2  [E][D/128][I/128][128][64] u8 packed e2m1 tiles
   s2  [E][D/128][I/128][512] u8 UE8M0 atoms
-  sh_w13 [2][I_sh][D] e4m3, sh_s13 [2][I_sh/128][D/128][512] atoms of the
-  128x128 block scales, sh_w2 [D][I_sh], sh_s2 [D/128][I_sh/128][512]
+  sh_w13 [I_sh/128][D/128][2][128][128] e4m3 tiles, sh_s13 [I_sh/128][D/128][2][512]
+  atoms of the 128x128 block scales, sh_w2 [D/128][I_sh/128][128][128],
+  sh_s2 [D/128][I_sh/128][512]
   gate [E][D] bf16, bias [E] bf16, tid2eid [V][K] int64 (hash layers only)
-The packed weights are returned to reference callers as views; the scales
-are returned in the reference's row-major [rows][cols/32] form as copies.
+Every stage of the kernels reads one contiguous 16 KB block of packed weights
+(32 KB for the FP8 shared expert) and one contiguous 1 KB pair of scale atoms.
+Reference callers get the reference's row-major tensors back as copies
+(`_load_expert_fp4_raw`).
 """
 from __future__ import annotations
 
@@ -30,7 +33,7 @@ import numpy as np
 import torch
 
 from . import ops
-from .layout import atoms_to_scales, block_scales_to_atoms, scales_to_atoms
+from .layout import atoms_to_scales, block_scales_to_atoms, scales_to_atoms, tile_rows, untile_rows
 
 
 @dataclass
@@ -76,15 +79,15 @@ class HBMExpertStore:
         self.layers: list[LayerWeights] = []
         for layer in range(num_layers):
             lw = LayerWeights(
-                w13=torch.zeros(E, 2, I, D // 2, dtype=torch.uint8, device=dev),
-                s13=torch.zeros(E, 2, I // 128, D // 128, 512, dtype=torch.uint8, device=dev),
-                w2=torch.zeros(E, D, I // 2, dtype=torch.uint8, device=dev),
+                w13=torch.zeros(E, I // 128, D // 128, 2, 128, 64, dtype=torch.uint8, device=dev),
+                s13=torch.zeros(E, I // 128, D // 128, 2, 512, dtype=torch.uint8, device=dev),
+                w2=torch.zeros(E, D // 128, I // 128, 128, 64, dtype=torch.uint8, device=dev),
                 s2=torch.zeros(E, D // 128, I // 128, 512, dtype=torch.uint8, device=dev),
             )
             if Ish:
-                lw.sh_w13 = torch.zeros(2, Ish, D, dtype=torch.uint8, device=dev)
-                lw.sh_s13 = torch.zeros(2, Ish // 128, D // 128, 512, dtype=torch.uint8, device=dev)
-                lw.sh_w2 = torch.zeros(D, Ish, dtype=torch.uint8, device=dev)
+                lw.sh_w13 = torch.zeros(Ish // 128, D // 128, 2, 128, 128, dtype=torch.uint8, device=dev)
+                lw.sh_s13 = torch.zeros(Ish // 128, D // 128, 2, 512, dtype=torch.uint8, device=dev)
+                lw.sh_w2 = torch.zeros(D // 128, Ish // 128, 128, 128, dtype=torch.uint8, device=dev)
                 lw.sh_s2 = torch.zeros(D // 128, Ish // 128, 512, dtype=torch.uint8, device=dev)
             if with_router:
                 lw.gate = torch.zeros(num_experts, D, dtype=torch.bfloat16, device=dev)
@@ -109,11 +112,11 @@ class HBMExpertStore:
             t = torch.from_numpy(np.ascontiguousarray(a)) if isinstance(a, np.ndarray) else a
             return t.contiguous().view(torch.uint8).to(self.device, non_blocking=True)
 
-        lw.w13[le, 0].copy_(dev_u8(w1))
-        lw.s13[le, 0].copy_(scales_to_atoms(dev_u8(s1)))
-        lw.w13[le, 1].copy_(dev_u8(w3))
-        lw.s13[le, 1].copy_(scales_to_atoms(dev_u8(s3)))
-        lw.w2[le].copy_(dev_u8(w2))
+        lw.w13[le, :, :, 0].copy_(tile_rows(dev_u8(w1), 64))
+        lw.w13[le, :, :, 1].copy_(tile_rows(dev_u8(w3), 64))
+        lw.s13[le, :, :, 0].copy_(scales_to_atoms(dev_u8(s1)))
+        lw.s13[le, :, :, 1].copy_(scales_to_atoms(dev_u8(s3)))
+        lw.w2[le].copy_(tile_rows(dev_u8(w2), 64))
         lw.s2[le].copy_(scales_to_atoms(dev_u8(s2)))
         lw.desc = None
 
@@ -125,10 +128,13 @@ class HBMExpertStore:
             t = torch.from_numpy(np.ascontiguousarray(a)) if isinstance(a, np.ndarray) else a
             return t.contiguous().view(torch.uint8).to(self.device)
 
-        lw.sh_w13.copy_(dev_u8(w13).reshape(lw.sh_w13.shape))
-        lw.sh_w2.copy_(dev_u8(w2).reshape(lw.sh_w2.shape))
-        lw.sh_s13.copy_(block_scales_to_atoms(dev_u8(s13).reshape(lw.sh_s13.shape[:-1])))
-        lw.sh_s2.copy_(block_scales_to_atoms(dev_u8(s2).reshape(lw.sh_s2.shape[:-1])))
+        w13 = dev_u8(w13).reshape(2, self.I_sh, self.D)
+        lw.sh_w13[:, :, 0].copy_(tile_rows(w13[0], 128))
+        lw.sh_w13[:, :, 1].copy_(tile_rows(w13[1], 128))
+        lw.sh_w2.copy_(tile_rows(dev_u8(w2).reshape(self.D, self.I_sh), 128))
+        s13 = dev_u8(s13).reshape(2, self.I_sh // 128, self.D // 128)
+        lw.sh_s13.copy_(block_scales_to_atoms(s13.permute(1, 2, 0)))
+        lw.sh_s2.copy_(block_scales_to_atoms(dev_u8(s2).reshape(self.D // 128, self.I_sh // 128)))
         lw.desc = None
 
     def set_router(self, layer: int, gate: torch.Tensor, bias: Optional[torch.Tensor]) -> None:
@@ -197,18 +203,19 @@ class HBMExpertStore:
                     n += t.numel() * t.element_size()
         return n
 
-    # --- reference-facing views (engine.py:1084-1129, 1173-1285) ----------------
+    # --- reference-facing format (engine.py:1084-1129, 1173-1285) ---------------
     def _load_expert_fp4_raw(self, layer_idx: int, eid: int):
-        """(w1 int8 [I, D/2], s1 e8m0 [I, D/32], w3, s3, w2 int8 [D, I/2], s2 e8m0 [D, I/32]) views."""
+        """(w1 int8 [I, D/2], s1 e8m0 [I, D/32], w3, s3, w2 int8 [D, I/2], s2 e8m0 [D, I/32]),
+        row-major copies out of the tiled store (the kernel path never calls this)."""
         lw = self.layers[layer_idx]
         try:
             le = self._local(eid)
         except KeyError:
             return None
         e8 = torch.float8_e8m0fnu
-        return (lw.w13[le, 0].view(torch.int8), atoms_to_scales(lw.s13[le, 0]).view(e8),
-                lw.w13[le, 1].view(torch.int8), atoms_to_scales(lw.s13[le, 1]).view(e8),
-                lw.w2[le].view(torch.int8), atoms_to_scales(lw.s2[le]).view(e8))
+        return (untile_rows(lw.w13[le, :, :, 0]).view(torch.int8), atoms_to_scales(lw.s13[le, :, :, 0]).view(e8),
+                untile_rows(lw.w13[le, :, :, 1]).view(torch.int8), atoms_to_scales(lw.s13[le, :, :, 1]).view(e8),
+                untile_rows(lw.w2[le]).view(torch.int8), atoms_to_scales(lw.s2[le]).view(e8))
 
     def _load_expert_weights(self, layer_idx: int, eid: int):
         """Reference triple format: ((data, scale, "fp4_gpu"), w3 entry, w2 entry)."""

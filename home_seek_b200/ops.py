@@ -124,11 +124,14 @@ def hash_route(input_ids: torch.Tensor, tid2eid: torch.Tensor, top_k: int = 6):
 # --- MoE FFN -------------------------------------------------------------------
 
 def make_moe_desc(w13, s13, w2, s2, sh_w13=None, sh_s13=None, sh_w2=None, sh_s2=None) -> ctypes.Array:
-    """Encode the per-layer TMA descriptor blob (host memory) for hs_moe_ffn_fp4."""
-    E, two, I, Dh = w13.shape
-    assert two == 2
-    D = Dh * 2
-    I_sh = sh_w13.shape[1] if sh_w13 is not None else 0
+    """Encode the per-layer TMA descriptor blob (host memory) for hs_moe_ffn_fp4.
+    Tensors in the expert store's tiled layout (layout.py):
+    w13 [E][I/128][D/128][2][128][64], sh_w13 [I_sh/128][D/128][2][128][128]."""
+    E, it, kt, two, r, rb = w13.shape
+    if two != 2 or r != 128 or rb != 64:
+        raise ValueError(f"w13 {tuple(w13.shape)} is not in the tiled layout")
+    I, D = it * 128, kt * 128
+    I_sh = sh_w13.shape[0] * 128 if sh_w13 is not None else 0
     wts = _lib.hs_moe_weights(w13.data_ptr(), s13.data_ptr(), w2.data_ptr(), s2.data_ptr(),
                               _ptr(sh_w13), _ptr(sh_s13), _ptr(sh_w2), _ptr(sh_s2), E, D, I, I_sh)
     buf = (ctypes.c_uint8 * _lib.HS_MOE_DESC_BYTES)()

@@ -50,6 +50,7 @@ typedef enum hs_status {
 #define HS_DEV_BAD_TOKEN 0x2   /* a token id outside [0, V) was skipped */
 #define HS_DEV_TIMEOUT 0x4     /* a bounded device-side wait gave up */
 #define HS_DEV_BAD_DRAFT 0x8   /* a draft id outside [0, V) */
+#define HS_DEV_SMEM_ALIGN 0x10 /* dynamic shared memory not 1024-byte aligned; the MoE kernel did nothing */
 
 int hs_abi_version(void);
 const char* hs_status_string(int status);
@@ -66,7 +67,7 @@ int hs_last_cuda_error(void);
 /* hidden [T][D] bf16, gate [E][D] bf16, bias [E] bf16 or NULL.               */
 /* topk_idx [T][top_k] int64, topk_w [T][top_k] f32.                          */
 /* logits_out [T][E] bf16 (post-bias) or NULL.                                */
-/* Limits: D % 512 == 0, E % 16 == 0, E <= 1024, 1 <= top_k <= 16, top_k <= E.*/
+/* Limits: D % 512 == 0, D <= 8192, E % 16 == 0, E <= 1024, top_k in [1, 16].  */
 size_t hs_router_workspace_size(int64_t T, int64_t D, int64_t E);
 int hs_router_topk(const void* hidden, const void* gate, const void* bias,
                    int64_t T, int64_t D, int64_t E, int64_t top_k,
@@ -153,13 +154,14 @@ int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx
 /* a fixed array of HS_MOE_NOALLOC_BYTES inside the library; every GPU that   */
 /* loads the library holds it until the process exits. A call whose          */
 /* hs_moe_workspace_size(T, top_k, D, I, I_sh) exceeds it returns             */
-/* HS_ERR_WORKSPACE without launching (at D = 4096, I = I_sh = 2048, top_k = 6 */
-/* that allows T <= 31 tokens). The first call on a device looks up the       */
+/* HS_ERR_WORKSPACE without launching (on a 148-SM B200 at D = 4096,         */
+/* I = I_sh = 2048, top_k = 6 --- the size grows with the SM count ---       */
+/* that allows T <= 16 tokens). The first call on a device looks up the       */
 /* array's device address (cudaGetSymbolAddress): make that first call        */
 /* before any stream capture. All calls share the one array, so calls that    */
 /* overlap on the GPU (two streams, two host threads) race; the kernels clear */
 /* the counters they need at the start of every call.                         */
-#define HS_MOE_NOALLOC_BYTES (6u << 20)
+#define HS_MOE_NOALLOC_BYTES (16u << 20)
 int hs_moe_ffn_fp4_noalloc(const void* desc, const void* hidden, const int64_t* topk_idx,
                            const float* topk_w, int64_t T, int64_t top_k, int use_shared,
                            int dup_mode, void* out, float* out_f32, int32_t* dev_status,

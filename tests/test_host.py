@@ -1,5 +1,5 @@
-"""Host-side logic on the CPU: the expert store layout and its reference-format
-views, the loader protocol, and expert-id localisation for sharded stores."""
+"""Host-side logic on the CPU: the expert store's tiled layout and its
+reference-format copies, the loader protocol, and expert-id localisation for sharded stores."""
 from __future__ import annotations
 
 import numpy as np
@@ -8,7 +8,7 @@ import torch
 from oracle import inputs as I
 
 
-def test_store_layout_and_reference_views():
+def test_store_layout_and_reference_format():
     from home_seek_b200.expert_store import HBMExpertStore
     sh = I.SMALL
     st = HBMExpertStore(2, sh.E, sh.D, sh.I, sh.I_sh, device="cpu", hash_layers=1, vocab_size=100)
@@ -19,8 +19,10 @@ def test_store_layout_and_reference_views():
     assert raw[0].shape == (sh.I, sh.D // 2) and raw[4].shape == (sh.D, sh.I // 2)
     for got, want in zip(raw, w):
         assert np.array_equal(got.view(torch.uint8).numpy(), want)
-    # views, not copies: writing through the store changes what the view sees
-    assert raw[0].data_ptr() == st.layers[1].w13[5, 0].data_ptr()
+    # the store keeps tiles: tile (row tile 1, k chunk 2) of w3 is one contiguous block
+    tile = st.layers[1].w13[5, 1, 2, 1]
+    assert tile.is_contiguous() and tile.shape == (128, 64)
+    assert np.array_equal(tile.numpy(), w[2][128:256, 128:192])
     trip = st._load_expert_weights(1, 5)
     assert [e[2] for e in trip] == ["fp4_gpu"] * 3
     assert st.layers[0].tid2eid is not None and st.layers[1].tid2eid is None

@@ -61,10 +61,10 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
 
     lib = _lib.load()
     store = HBMExpertStore(1, 16, 4096, 2048, 2048, device="cuda", with_router=False)
-    # 32 tokens x top-6 at D = 4096 needs more than the fixed scratch holds
-    assert lib.hs_moe_workspace_size(32, 6, 4096, 2048, 2048) > _lib.HS_MOE_NOALLOC_BYTES
-    h = torch.zeros(32, 4096, dtype=torch.bfloat16, device="cuda")
-    idx = torch.zeros(32, 6, dtype=torch.int64, device="cuda")
-    w = torch.zeros(32, 6, dtype=torch.float32, device="cuda")
+    # 64 tokens x top-6 at D = 4096 needs more than the fixed scratch holds
+    assert lib.hs_moe_workspace_size(64, 6, 4096, 2048, 2048) > _lib.HS_MOE_NOALLOC_BYTES
+    h = torch.zeros(64, 4096, dtype=torch.bfloat16, device="cuda")
+    idx = torch.zeros(64, 6, dtype=torch.int64, device="cuda")
+    w = torch.zeros(64, 6, dtype=torch.float32, device="cuda")
     out = torch.empty_like(h)
     assert _noalloc(lib, store, h, idx, w, out) == 3  # HS_ERR_WORKSPACE, nothing launched
