@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/hs_ext.h"
 
 #define HS_DI __device__ __forceinline__
@@ -121,6 +123,13 @@ HS_DI void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
                : "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with launch_pdl() may start
+// while its predecessor in the stream is still running: it must call
+// pdl_wait() before it reads or writes any global memory the predecessor (or
+// anything earlier) touches. pdl_trigger() lets the successor launch early.
+HS_DI void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+HS_DI void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 HS_DI void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -205,3 +214,22 @@ HS_DI float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)
 HS_DI float exp2i(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
 
 }  // namespace hs
+
+// Host: launch `kernel` with programmatic stream serialization allowed (the
+// kernel must call pdl_wait() before touching global memory).
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+

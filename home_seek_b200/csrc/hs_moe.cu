@@ -286,6 +286,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
   const int T = A.T, K = A.K, E = A.E;
   const int npairs = T * K;
   const bool cache_idx = npairs <= kLocalPairs;
+  pdl_trigger();  // the MoE kernels may start their prologues
+  pdl_wait();     // router outputs (and everything earlier) are complete
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid; i < A.n_ucount;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     A.ucount[i] = 0u;
@@ -633,6 +635,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
 // Routed pair rows when T*K is too large for per-token position recomputation:
 // one CTA per routed pair copies its token's hi/lo rows (written by the plan).
 __global__ void __launch_bounds__(256) gather_kernel(Plan P, int T, int64_t P_max, int D) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t p = T + static_cast<int64_t>(blockIdx.x);
   if (p >= T + P.hdr[2]) return;
   const int t = P.pair_token[p];
@@ -870,6 +874,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   // the 128B-swizzled stages need a 1024-aligned base; no slack is reserved
   // for realignment (two CTAs per SM leave none), so check it
   if (smem_u32(smem_raw) & 1023u) {
+    pdl_wait();
     if (threadIdx.x == 0) report(a.status, HS_DEV_SMEM_ALIGN);
     return;
   }
@@ -877,9 +882,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   Bars* bars = reinterpret_cast<Bars*>(base + S_ * L::kStage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = d.D;
-  const Sched sc = make_sched(d, a, kDown);
   const int c = blockIdx.x;
-  const int64_t s_begin = sc.lo(c), s_end = sc.lo(c + 1);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S_; ++i) {
@@ -896,10 +899,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     fence_mbar_init();
   }
   if (warp == 0) tc5::tmem_alloc(&bars->tmem, 256);
+  if (warp == 4 && lane == 0) {
+    prefetch_tensormap(kDown ? &d.tm_w2 : &d.tm_w13);
+    prefetch_tensormap(kDown ? &d.tm_sw2 : &d.tm_sw13);
+    prefetch_tensormap(kDown ? &cm.tm_act8 : &cm.tm_x8);
+  }
+  // everything above overlaps the previous kernel; from here on the plan (and,
+  // for the down phase, the gate/up phase) is complete and visible
+  pdl_wait();
+  pdl_trigger();
   tc5::fence_before_sync();
   __syncthreads();
   tc5::fence_after_sync();
   const uint32_t tmem = bars->tmem;
+  const Sched sc = make_sched(d, a, kDown);
+  const int64_t s_begin = sc.lo(c), s_end = sc.lo(c + 1);
 
   if (warp == 4) {
     // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
@@ -1284,7 +1298,7 @@ static int launch_sk(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaS
     HS_CUDA_CHECK(cudaFuncSetAttribute(sk_kernel<kDown, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
     done.fetch_or(bit);
   }
-  sk_kernel<kDown, NT><<<static_cast<unsigned>(a.G), kThreads, bytes, st>>>(d, cm, a);
+  HS_CUDA_CHECK(launch_pdl(sk_kernel<kDown, NT>, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes, st, d, cm, a));
   return check_launch();
 }
 
@@ -1331,7 +1345,7 @@ static int launch_plan(const PlanArgs& pa, const Plan& P, int grid, cudaStream_t
     HS_CUDA_CHECK(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     done.fetch_or(bit);
   }
-  plan_kernel<<<grid, kPlanThreads, smem, st>>>(pa, P);
+  HS_CUDA_CHECK(launch_pdl(plan_kernel, dim3(grid), dim3(kPlanThreads), smem, st, pa, P));
   return check_launch();
 }
 
@@ -1442,7 +1456,8 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   pa.n_ucount = g.U_gu + g.U_dn;
   if ((rc = launch_plan(pa, P, 1 + static_cast<int>(T), st))) return rc;
   if (!local_rows) {
-    gather_kernel<<<static_cast<unsigned>(npairs), 256, 0, st>>>(P, static_cast<int>(T), g.P_max, d.D);
+    HS_CUDA_CHECK(launch_pdl(gather_kernel, dim3(static_cast<unsigned>(npairs)), dim3(256), 0, st, P,
+                             static_cast<int>(T), g.P_max, d.D));
     if ((rc = check_launch())) return rc;
   }
 
