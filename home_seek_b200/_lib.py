@@ -74,6 +74,9 @@ SIGNATURES = {
                                  c_void_p, c_void_p]),
     "hs_accept_rejection": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                     c_float, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "hs_rms_norm": (c_int, [c_void_p, c_void_p, c_float, c_int64, c_int64, c_void_p, c_void_p]),
+    "hs_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_int64, c_int64, c_void_p, c_void_p,
+                                c_void_p]),
     "hs_fill_bytes": (c_int, [c_void_p, c_int64, c_uint64, c_int32, c_int32, c_void_p]),
 }
 

@@ -1,0 +1,132 @@
+// RMSNorm, and the residual add fused with the next RMSNorm, sm_100a.
+//
+// Reference being replaced: home_seek/utils.py:6-9 (rms_norm, applied before
+// every FFN at inference_engine/engine.py:2679 and before the logits at
+// engine.py:2482) and the residual add that closes each layer
+// (engine.py:2685). In the decode loop the residual add of layer l and the
+// norm that opens layer l+1 touch the same row, so one launch does both.
+//
+// Numerics follow the reference operation by operation, in f32:
+//   h' = bf16(h + y)                      (bf16 + bf16 computed in f32)
+//   var = sum(f32(x)^2) / D               (each square rounded, then summed)
+//   out = bf16(f32(w) * (f32(x) * (1 / sqrt(var + eps))))
+// The sum runs in a fixed order (per-thread, then a fixed shuffle tree, then
+// warps in order), so results are deterministic; the reference's reduction
+// order differs, which can move var by an ulp.
+#include "hs_common.cuh"
+
+namespace hs {
+namespace norm {
+
+constexpr int kThreads = 256;
+constexpr int kMaxVec = 4;  // 8 bf16 per vector: D <= kThreads * 8 * kMaxVec = 8192
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i]));
+    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1]));
+    w[i] = lo | (hi << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// One CTA per row. kAdd: h_out = bf16(h + y) is normalised (h_out may alias h:
+// every element is read and written by the same thread).
+template <bool kAdd>
+__global__ void __launch_bounds__(kThreads) add_norm_kernel(const __nv_bfloat16* h, const __nv_bfloat16* y,
+                                                            const __nv_bfloat16* __restrict__ w, float eps, int D,
+                                                            __nv_bfloat16* h_out, __nv_bfloat16* __restrict__ x_out) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * D;
+  const int nv = D / 8;
+  const uint4* hr = reinterpret_cast<const uint4*>(h + row);
+  float v[kMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int j = threadIdx.x + i * kThreads;
+    if (j < nv) {
+      unpack8(hr[j], v[i]);
+      if (kAdd) {
+        float g[8];
+        unpack8(reinterpret_cast<const uint4*>(y + row)[j], g);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[i][k] = round_bf16(__fadd_rn(v[i][k], g[k]));
+        reinterpret_cast<uint4*>(h_out + row)[j] = pack8(v[i]);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss = __fadd_rn(ss, __fmul_rn(v[i][k], v[i][k]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+  __shared__ float part[kThreads / 32];
+  __shared__ float rinv;
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int i = 0; i < kThreads / 32; ++i) tot = __fadd_rn(tot, part[i]);
+    const float var = __fdiv_rn(tot, static_cast<float>(D));
+    rinv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, eps)));
+  }
+  __syncthreads();
+  const float r = rinv;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int j = threadIdx.x + i * kThreads;
+    if (j < nv) {
+      float wf[8], o[8];
+      unpack8(wr[j], wf);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(wf[k], __fmul_rn(v[i][k], r));
+      reinterpret_cast<uint4*>(x_out + row)[j] = pack8(o);
+    }
+  }
+}
+
+static int launch(bool add, const void* h, const void* y, const void* w, float eps, int64_t T, int64_t D, void* h_out,
+                  void* x_out, void* stream) {
+  if (T < 0 || D < 8 || D % 8 != 0 || D > kThreads * 8 * kMaxVec || T > (1 << 24)) return HS_ERR_BAD_SHAPE;
+  if (T == 0) return HS_OK;
+  if (!h || !w || !x_out || (add && (!y || !h_out))) return HS_ERR_BAD_ARGUMENT;
+  if (!aligned16(h) || !aligned16(w) || !aligned16(x_out) || (add && (!aligned16(y) || !aligned16(h_out))))
+    return HS_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const auto* hb = static_cast<const __nv_bfloat16*>(h);
+  const auto* yb = static_cast<const __nv_bfloat16*>(y);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  auto* ho = static_cast<__nv_bfloat16*>(h_out);
+  auto* xo = static_cast<__nv_bfloat16*>(x_out);
+  const dim3 grid(static_cast<unsigned>(T)), block(kThreads);
+  if (add)
+    HS_CUDA_CHECK(launch_pdl(add_norm_kernel<true>, grid, block, 0, st, hb, yb, wb, eps, static_cast<int>(D), ho, xo));
+  else
+    HS_CUDA_CHECK(launch_pdl(add_norm_kernel<false>, grid, block, 0, st, hb, yb, wb, eps, static_cast<int>(D), ho, xo));
+  return check_launch();
+}
+
+}  // namespace norm
+}  // namespace hs
+
+extern "C" int hs_rms_norm(const void* x, const void* w, float eps, int64_t T, int64_t D, void* out, void* stream) {
+  return hs::norm::launch(false, x, nullptr, w, eps, T, D, nullptr, out, stream);
+}
+
+extern "C" int hs_add_rms_norm(const void* h, const void* y, const void* w, float eps, int64_t T, int64_t D,
+                               void* h_out, void* x_out, void* stream) {
+  return hs::norm::launch(true, h, y, w, eps, T, D, h_out, x_out, stream);
+}

@@ -48,6 +48,8 @@ __device__ __forceinline__ void topk_dispatch(const float* partial, int ksplit, 
 __global__ void __launch_bounds__(kWarps * 32) logits_kernel(const __nv_bfloat16* __restrict__ h,
                                                              const __nv_bfloat16* __restrict__ gate, int T, int D,
                                                              int E, float* __restrict__ partial, TopkArgs ta) {
+  pdl_trigger();  // the plan kernel may start its prologue
+  pdl_wait();     // the hidden rows (and everything earlier) are complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int e0 = blockIdx.x * 16;
@@ -201,6 +203,8 @@ __global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ par
                                                    const __nv_bfloat16* __restrict__ bias, int K, float scaling,
                                                    int64_t* __restrict__ idx_out, float* __restrict__ w_out,
                                                    __nv_bfloat16* __restrict__ logits_out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
   if (t >= T) return;
   topk_dispatch(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
@@ -208,6 +212,8 @@ __global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ par
 
 __global__ void hash_kernel(const int64_t* __restrict__ ids, int T, const int64_t* __restrict__ tid2eid, int64_t V,
                             int K, float w, int64_t* __restrict__ idx_out, float* __restrict__ w_out, int32_t* status) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T * K) return;
   const int t = i / K, j = i - t * K;
@@ -252,14 +258,15 @@ extern "C" int hs_router_topk(const void* hidden, const void* gate, const void* 
   TopkArgs ta{static_cast<const __nv_bfloat16*>(bias), static_cast<int>(top_k), routed_scaling, topk_idx, topk_w,
               static_cast<__nv_bfloat16*>(logits_out), fused ? counter : nullptr};
   dim3 g1(static_cast<unsigned>(E / 16), static_cast<unsigned>(ksplit), static_cast<unsigned>((T + 7) / 8));
-  logits_kernel<<<g1, kWarps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(hidden),
-                                            static_cast<const __nv_bfloat16*>(gate), static_cast<int>(T),
-                                            static_cast<int>(D), static_cast<int>(E), partial, ta);
+  HS_CUDA_CHECK(launch_pdl(logits_kernel, g1, dim3(kWarps * 32), 0, st, static_cast<const __nv_bfloat16*>(hidden),
+                           static_cast<const __nv_bfloat16*>(gate), static_cast<int>(T), static_cast<int>(D),
+                           static_cast<int>(E), partial, ta));
   int rc = check_launch();
   if (rc || fused) return rc;
-  topk_kernel<<<static_cast<unsigned>((T + 3) / 4), 128, 0, st>>>(
-      partial, ksplit, static_cast<int>(T), static_cast<int>(E), static_cast<const __nv_bfloat16*>(bias),
-      static_cast<int>(top_k), routed_scaling, topk_idx, topk_w, static_cast<__nv_bfloat16*>(logits_out));
+  HS_CUDA_CHECK(launch_pdl(topk_kernel, dim3(static_cast<unsigned>((T + 3) / 4)), dim3(128), 0, st,
+                           static_cast<const float*>(partial), ksplit, static_cast<int>(T), static_cast<int>(E),
+                           static_cast<const __nv_bfloat16*>(bias), static_cast<int>(top_k), routed_scaling, topk_idx,
+                           topk_w, static_cast<__nv_bfloat16*>(logits_out)));
   return check_launch();
 }
 
@@ -272,7 +279,7 @@ extern "C" int hs_hash_route(const int64_t* input_ids, int64_t T, const int64_t*
   const int n = static_cast<int>(T * top_k);
   // torch.full(..., 1.0 / k) with a float32 default dtype
   const float w = static_cast<float>(1.0 / static_cast<double>(top_k));
-  hash_kernel<<<(n + 255) / 256, 256, 0, st>>>(input_ids, static_cast<int>(T), tid2eid, V, static_cast<int>(top_k), w,
-                                                topk_idx, topk_w, dev_status);
+  HS_CUDA_CHECK(launch_pdl(hash_kernel, dim3((n + 255) / 256), dim3(256), 0, st, input_ids, static_cast<int>(T),
+                           tid2eid, V, static_cast<int>(top_k), w, topk_idx, topk_w, dev_status));
   return check_launch();
 }

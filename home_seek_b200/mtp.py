@@ -7,7 +7,8 @@ Reference: HomeSeekInferenceEngine.generate's decode loop
 
 What runs per layer here is the part of `_forward_layer` this build owns:
 rms_norm -> router (or hash routing for layers < num_hash_layers) -> routed FP4
-experts + FP8 shared expert (one fused kernel sequence) -> residual add.
+experts + FP8 shared expert (one fused kernel sequence) -> residual add, the
+add fused with the next layer's norm (hs_add_rms_norm).
 Attention and the MHC hyper-connections stay on the reference's PyTorch path
 and are not part of this module; the layer body is therefore
 h <- h + MoE(rms_norm(h)). The draft layer is the MTP block's projections
@@ -28,13 +29,6 @@ import torch
 from . import ops
 from ._lib import HS_DUP_LAST, HS_DUP_SUM
 from .expert_store import HBMExpertStore
-
-
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
-    """utils.py:6-9: f32 RMS norm, cast back."""
-    xf = x.float()
-    var = xf.pow(2).mean(-1, keepdim=True)
-    return (w.float() * (xf * torch.rsqrt(var + eps))).to(x.dtype)
 
 
 @dataclass
@@ -97,18 +91,22 @@ class MoEPathModel:
         dup = HS_DUP_SUM if x.shape[0] == 1 else HS_DUP_LAST
         return ops.moe_ffn(self.store.desc(layer), self.store.dims, x, idx, w, use_shared=True, dup_mode=dup)
 
-    def layer(self, h: torch.Tensor, layer: int, ids: torch.Tensor) -> torch.Tensor:
-        x = rms_norm(h, self.ln_w[layer])
-        return h + self.moe(x, layer, ids)
-
-    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+    def forward(self, ids: torch.Tensor):
+        """All layers for tokens `ids`: returns (h, x) with h the residual stream
+        after the last layer and x = rms_norm(h, final norm). Each layer's
+        residual add is fused with the next layer's input norm (one launch)."""
+        L = self.shape.num_layers
         h = self.embed[ids]
-        for layer in range(self.shape.num_layers):
-            h = self.layer(h, layer, ids)
-        return h
+        x = ops.rms_norm(h, self.ln_w[0])
+        for layer in range(L):
+            y = self.moe(x, layer, ids)
+            w_next = self.ln_w[layer + 1] if layer + 1 < L else self.norm_w
+            h, x = ops.add_rms_norm(h, y, w_next, h_out=h, x_out=x)
+        return h, x
 
-    def logits(self, h: torch.Tensor) -> torch.Tensor:
-        return rms_norm(h, self.norm_w) @ self.lm_head.t()
+    def logits(self, x_normed: torch.Tensor) -> torch.Tensor:
+        """lm_head over rows that already carry the final norm (forward's x)."""
+        return x_normed @ self.lm_head.t()
 
     def draft(self, h_last: torch.Tensor, tok: torch.Tensor) -> torch.Tensor:
         """_mtp_generate_draft at t=0 (engine.py:2251-2336) on the MoE path: M steps."""
@@ -118,10 +116,11 @@ class MoEPathModel:
         out = []
         t = tok
         for _ in range(s.num_draft):
-            e = rms_norm(self.embed[t], self.enorm_w) @ self.e_proj.t()
-            hc = rms_norm(prev, self.hnorm_w) @ self.h_proj.t() + e
-            hm = hc + self.moe(rms_norm(hc, self.ln_w[L]), L, t)
-            lg = rms_norm(hm, self.mtp_norm_w) @ self.lm_head.t()
+            e = ops.rms_norm(self.embed[t], self.enorm_w) @ self.e_proj.t()
+            hc = ops.rms_norm(prev, self.hnorm_w) @ self.h_proj.t() + e
+            y = self.moe(ops.rms_norm(hc, self.ln_w[L]), L, t)
+            hm, xm = ops.add_rms_norm(hc, y, self.mtp_norm_w)
+            lg = xm @ self.lm_head.t()
             _, t = ops.accept_greedy(lg.view(1, 1, -1), torch.empty(1, 0, dtype=torch.int64, device=lg.device))
             out.append(t)
             prev = hm
@@ -149,12 +148,12 @@ class MTPDecoder:
         m = self.m
         M = m.shape.num_draft
         none = torch.empty(1, 0, dtype=torch.int64, device=self.next_id.device)
-        h = m.forward(self.next_id)                                   # main step, T=1
-        _, main_pred = ops.accept_greedy(m.logits(h).view(1, 1, -1), none)
+        h, x = m.forward(self.next_id)                                # main step, T=1
+        _, main_pred = ops.accept_greedy(m.logits(x).view(1, 1, -1), none)
         d = m.draft(h, main_pred)                                     # M drafts
         ids = torch.cat([main_pred, d])                               # combined_ids
-        hv = m.forward(ids)                                           # fused verify, T=1+M
-        n_acc, bonus = ops.accept_greedy(m.logits(hv).view(1, M + 1, -1), d.view(1, M))
+        _, xv = m.forward(ids)                                        # fused verify, T=1+M
+        n_acc, bonus = ops.accept_greedy(m.logits(xv).view(1, M + 1, -1), d.view(1, M))
         n = n_acc.to(torch.int64)
         # tokens of this iteration: main_pred, then d[:n], then bonus if n > 0
         cand = torch.cat([main_pred, d, bonus])                       # [M + 2]

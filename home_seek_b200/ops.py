@@ -19,7 +19,8 @@ _status: dict = {}
 # so a caller can count the kernels of one decode iteration.
 launches = 0
 _KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_moe_permute": 2,
-            "hs_moe_unpermute": 1, "hs_accept_greedy": 1, "hs_accept_rejection": 1, "hs_fill_bytes": 1}
+            "hs_moe_unpermute": 1, "hs_accept_greedy": 1, "hs_accept_rejection": 1, "hs_fill_bytes": 1,
+            "hs_rms_norm": 1, "hs_add_rms_norm": 1}
 
 
 def _launch(name: str, *args, extra: int = 0) -> None:
@@ -234,6 +235,48 @@ def accept_rejection(target: torch.Tensor, draft: torch.Tensor, draft_ids: torch
     return n, nxt
 
 
+# --- RMSNorm / residual add + RMSNorm ---------------------------------------------
+
+def _rows(x: torch.Tensor, name: str) -> torch.Tensor:
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"{name} must be bf16")
+    return x.contiguous()
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """utils.py:6-9 in one launch: bf16(f32(w) * (f32(x) * rsqrt(mean(f32(x)^2) + eps))) over the last dim."""
+    dev = _check_cuda(x, w, out)
+    x = _rows(x, "x")
+    w = _rows(w, "w")
+    D = x.shape[-1]
+    if w.numel() != D:
+        raise ValueError(f"weight has {w.numel()} elements, rows have {D}")
+    if out is None:
+        out = torch.empty_like(x)
+    _launch("hs_rms_norm", x.data_ptr(), w.data_ptr(), float(eps), x.numel() // D, D, out.data_ptr(), _stream(dev))
+    return out
+
+
+def add_rms_norm(h: torch.Tensor, y: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
+                 h_out: Optional[torch.Tensor] = None, x_out: Optional[torch.Tensor] = None):
+    """Residual add then RMSNorm in one launch: returns (bf16(h + y), rms_norm(bf16(h + y), w)).
+    h_out may be h itself (in-place residual stream)."""
+    dev = _check_cuda(h, y, w, h_out, x_out)
+    h = _rows(h, "h")
+    y = _rows(y, "y")
+    w = _rows(w, "w")
+    D = h.shape[-1]
+    if y.shape != h.shape or w.numel() != D:
+        raise ValueError(f"shapes h {tuple(h.shape)}, y {tuple(y.shape)}, w {tuple(w.shape)} do not match")
+    if h_out is None:
+        h_out = torch.empty_like(h)
+    if x_out is None:
+        x_out = torch.empty_like(h)
+    _launch("hs_add_rms_norm", h.data_ptr(), y.data_ptr(), w.data_ptr(), float(eps), h.numel() // D, D,
+            h_out.data_ptr(), x_out.data_ptr(), _stream(dev))
+    return h_out, x_out
+
+
 def fill_bytes(t: torch.Tensor, seed: int, lo: int = 0, hi: int = 255) -> torch.Tensor:
     """Counter-hash fill of a uint8 tensor with values in [lo, hi] (device side)."""
     dev = _check_cuda(t)
@@ -243,4 +286,5 @@ def fill_bytes(t: torch.Tensor, seed: int, lo: int = 0, hi: int = 255) -> torch.
 
 
 __all__ = ["HsError", "router_topk", "hash_route", "make_moe_desc", "moe_ffn", "moe_permute", "moe_unpermute",
-           "accept_greedy", "accept_rejection", "fill_bytes", "check_status", "status_word", "workspace"]
+           "accept_greedy", "accept_rejection", "fill_bytes", "rms_norm", "add_rms_norm", "check_status",
+           "status_word", "workspace"]

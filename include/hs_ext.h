@@ -219,6 +219,24 @@ int hs_accept_rejection(const void* target_logits, const void* draft_logits,
                         int64_t* next_token, int32_t* dev_status, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* RMSNorm and residual add + RMSNorm (the layer loop around the MoE FFN).    */
+/* hs_rms_norm replaces home_seek/utils.py:6-9 (rms_norm; called before every */
+/*   FFN at inference_engine/engine.py:2679 and before the logits at          */
+/*   engine.py:2482): out = bf16(f32(w) * (f32(x) * 1/sqrt(mean(x^2) + eps))). */
+/* hs_add_rms_norm fuses the residual add that closes a layer                 */
+/*   (engine.py:2685, h = h + ffn_out) with the norm that opens the next:     */
+/*   h_out = bf16(h + y), x_out = rms_norm(h_out, w). h_out may alias h.       */
+/* x, h, y, w, out: bf16, rows of D; T rows. Limits: D % 8 == 0, D <= 8192,    */
+/* 16-byte aligned pointers. The sum of squares runs in a fixed order         */
+/* (deterministic; it may differ from torch's by an ulp of the variance).     */
+/* ------------------------------------------------------------------------ */
+int hs_rms_norm(const void* x, const void* w, float eps, int64_t T, int64_t D,
+                void* out, void* stream);
+int hs_add_rms_norm(const void* h, const void* y, const void* w, float eps,
+                    int64_t T, int64_t D, void* h_out, void* x_out,
+                    void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Synthetic weight fill (device-side, counter-based hash; no allocation).    */
 /* Fills n bytes at dst with lo + (hash(seed, i) % (hi - lo + 1)). Used to    */
 /* build random-init expert stores of the full model shape in seconds.        */
