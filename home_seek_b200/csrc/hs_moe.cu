@@ -255,10 +255,8 @@ __device__ __forceinline__ int pair_expert(const int32_t* row, const float* wrow
   return e;
 }
 
-// hi/lo e4m3 split of 16 consecutive bf16 values scaled by 2^e.
-__device__ __forceinline__ void split16(const __nv_bfloat16* src, float sc, uint4& hi, uint4& lo) {
-  const uint4 a = reinterpret_cast<const uint4*>(src)[0];
-  const uint4 b = reinterpret_cast<const uint4*>(src)[1];
+// hi/lo e4m3 split of 16 consecutive bf16 values (two uint4) scaled by 2^e.
+__device__ __forceinline__ void split16(const uint4& a, const uint4& b, float sc, uint4& hi, uint4& lo) {
   const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
   uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -288,6 +286,16 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
   const bool cache_idx = npairs <= kLocalPairs;
   pdl_trigger();  // the MoE kernels may start their prologues
   pdl_wait();     // router outputs (and everything earlier) are complete
+  // token CTAs: thread k16 holds values 16*k16 .. 16*k16+15 of the row in
+  // registers (D <= 16 * kPlanThreads), loaded first so the load overlaps the
+  // routing reads below; then the max and the split run from registers
+  const bool holds = blockIdx.x > 0 && tid < A.D / 16;
+  uint4 va = make_uint4(0u, 0u, 0u, 0u), vb = va;
+  if (holds) {
+    const uint4* hrow = reinterpret_cast<const uint4*>(A.hidden + static_cast<int64_t>(blockIdx.x - 1) * A.D);
+    va = hrow[2 * tid];
+    vb = hrow[2 * tid + 1];
+  }
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid; i < A.n_ucount;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     A.ucount[i] = 0u;
@@ -314,9 +322,13 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
     // ---- token row: prescale, hi/lo split, rows for its pairs ----
     const int t = blockIdx.x - 1;
     const int warp = tid >> 5, lane = tid & 31;
-    const __nv_bfloat16* h = A.hidden + static_cast<int64_t>(t) * A.D;
     float mx = 0.f;
-    for (int k = tid; k < A.D; k += blockDim.x) mx = fmaxf(mx, fabsf(__bfloat162float(h[k])));
+    {
+      const uint32_t w[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(w[i] << 16)), fabsf(__uint_as_float(w[i] & 0xffff0000u))));
+    }
     __shared__ float red[kPlanThreads / 32];
     __shared__ int rows[17];
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -362,14 +374,14 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
     const float sc = exp2i(e);
     uint8_t* hi_plane = P.x8;
     uint8_t* lo_plane = P.x8 + A.P_max * A.D;
-    for (int k16 = tid; k16 < A.D / 16; k16 += blockDim.x) {
+    if (holds) {
       uint4 hv, lv;
-      split16(h + 16 * k16, sc, hv, lv);
+      split16(va, vb, sc, hv, lv);
       for (int r = 0; r < nrows; ++r) {
         const int p = rows[r];
         if (p < 0) continue;
-        reinterpret_cast<uint4*>(hi_plane + static_cast<int64_t>(p) * A.D)[k16] = hv;
-        reinterpret_cast<uint4*>(lo_plane + static_cast<int64_t>(p) * A.D)[k16] = lv;
+        reinterpret_cast<uint4*>(hi_plane + static_cast<int64_t>(p) * A.D)[tid] = hv;
+        reinterpret_cast<uint4*>(lo_plane + static_cast<int64_t>(p) * A.D)[tid] = lv;
       }
     }
     if (tid < nrows && rows[tid] >= 0) P.sb1[rows[tid]] = static_cast<uint8_t>(127 - e);
