@@ -23,6 +23,7 @@ import os
 import re
 import statistics
 import subprocess
+import threading
 import sys
 import time
 from pathlib import Path
@@ -61,32 +62,52 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.out = None
+        self.lines = []          # (monotonic time, csv line)
+        self.t0 = self.t1 = None
+        self.reader = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.monotonic(), line))
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "50", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            deadline = time.monotonic() + 5.0
+            while not self.lines and time.monotonic() < deadline:  # sampler is up before timing starts
+                time.sleep(0.01)
         except Exception:
             self.proc = None
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *a):
+        self.t1 = time.monotonic()
         if self.proc is not None:
+            time.sleep(0.06)
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                self.out = ""
+            if self.reader is not None:
+                self.reader.join(timeout=2)
 
     def summary(self):
-        if not self.out:
+        if not self.lines:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        # samples taken while the timed region ran (widened to the nearest
+        # samples around it when the region is shorter than the interval)
+        inside = [l for t, l in self.lines if self.t0 <= t <= self.t1]
+        if len(inside) < 3:
+            inside = [l for t, l in self.lines if self.t0 - 0.1 <= t <= self.t1 + 0.1] or [self.lines[-1][1]]
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.out.strip().splitlines():
+        for line in inside:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -166,6 +187,34 @@ def run_reference(args):
 
 
 # --------------------------------------------------------------------------- GPU
+def _graph_time_per_call(enqueue, n_calls: int, replays: int = 5) -> float:
+    """Capture `enqueue()` (n_calls MoE calls back to back, as in a layer loop)
+    in one CUDA graph and time its replays with CUDA events: ms per call with
+    no host launch cost in the timed region."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        enqueue()  # warm-up: workspaces, descriptors, function attributes
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        enqueue()
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(replays):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / (replays * n_calls)
+    del graph
+    return ms
+
+
 def moe_roofline(model, reps: int = 43):
     """Time hs_moe_ffn_fp4 at T=3 (the verify shape) over distinct layers with
     CUDA events on the launching stream; algorithmic bytes per call are the
@@ -184,17 +233,10 @@ def moe_roofline(model, reps: int = 43):
         idx, w = ops.router_topk(h, lw.gate, lw.bias, s.top_k, s.routed_scaling)
         calls.append((l, h, idx, w))
     uniq = [len(set(c[2].flatten().tolist())) for c in calls]
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in calls]
-    for _ in range(2):
-        for (l, h, idx, w) in calls:
-            ops.moe_ffn(model.store.desc(l), model.store.dims, h, idx, w, use_shared=True)
-    torch.cuda.synchronize()
-    for (l, h, idx, w), (a, b) in zip(calls, ev):
-        a.record()
-        ops.moe_ffn(model.store.desc(l), model.store.dims, h, idx, w, use_shared=True)
-        b.record()
-    torch.cuda.synchronize()
-    ms = [a.elapsed_time(b) for a, b in ev]
+    per_call = _graph_time_per_call(
+        lambda: [ops.moe_ffn(model.store.desc(l), model.store.dims, h, idx, w, use_shared=True)
+                 for (l, h, idx, w) in calls], len(calls))
+    ms = [per_call] * len(calls)
     shared = 3 * s.shared_inter * s.hidden + 3 * (s.shared_inter // 128) * (s.hidden // 128)
     act = 3 * s.hidden * 2 * 2 + 12 * 3 * 2
     bytes_ = [u * s.bytes_per_expert + shared + act for u in uniq]
@@ -232,13 +274,19 @@ def run_moe_only(args):
         b.record()
     torch.cuda.synchronize()
     ms = [a.elapsed_time(b) for a, b in ev]
+    # the same calls replayed from one CUDA graph (no host launch cost; with
+    # layers > 1 consecutive calls stream different weights, as in the model)
+    graph_ms = _graph_time_per_call(lambda: [ops.moe_ffn(store.desc(l), store.dims, h, idx, w)
+                                             for (l, h, idx, w) in calls], len(calls))
     uniq = [len(set(c[2].flatten().tolist())) for c in calls]
     shared = 3 * 2048 * 4096 + 3 * 16 * 32
     byts = [u * 13_369_344 + shared + args.T * 4096 * 4 + 24 * args.T for u in uniq]
     peak, kind = _peaks()
     gbs = statistics.mean(b / (m * 1e-3) / 1e9 for b, m in zip(byts, ms))
+    graph_gbs = statistics.mean(byts) / (graph_ms * 1e-3) / 1e9
     print(json.dumps({"mode": "moe", "T": args.T, "layers": args.layers, "calls": len(calls),
                       "avg_us": 1000 * statistics.mean(ms), "min_us": 1000 * min(ms),
+                      "graph_us": 1000 * graph_ms, "graph_frac": graph_gbs / peak,
                       "avg_unique_experts": statistics.mean(uniq), "avg_bytes": statistics.mean(byts),
                       "gbs": gbs, "frac": gbs / peak, "peak": peak, "peak_kind": kind}), flush=True)
     return 0

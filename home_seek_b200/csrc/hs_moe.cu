@@ -60,6 +60,8 @@ constexpr int kPlanThreads = 512;
 constexpr int kLocalPairs = 4096;       // T*K up to this: token CTAs place their own rows
 constexpr int kFastPlanPairs = 1024;    // T*K up to this: block 0 uses the direct-count plan
 constexpr uint32_t kDescMagic = 0x48534d33u;  // "HSM3" (tiled weights)
+constexpr int kTokMax = 8;              // T <= this: token mode (activation rows per token, not per pair)
+constexpr int kTokChunks = 128;         // token mode: at most T*K <= 8*16 routed chunks
 constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two independent MMA streams)
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
 
@@ -100,8 +102,10 @@ struct Plan {
   int32_t* tok_pos;       // [T][K] ascending routed pair positions, -1 padded
   uint32_t* dcount;       // [D/128] finalize tickets, reset by the plan kernel
   uint8_t* x8;            // [2][P_max][D] e4m3 hi / lo
-  uint8_t* act8;          // [2][P_max][I_act] e4m3 hi / lo
+  uint8_t* act8;          // [2][P_max][I_act] e4m3 hi / lo; token mode [2][(1 + C_max) * 8][I_act]
   float* out_part;        // [P_max][D]
+  float* ctab_wb;         // token mode: [C_max][8] routing weight of (chunk, token), 0 if not routed
+  uint8_t* ctab_sb;       // token mode: [C_max][8] UE8M0 down-MMA B scale 127 - q of (chunk, token)
 };
 
 struct Geometry {
@@ -110,8 +114,9 @@ struct Geometry {
   int G;                   // persistent CTAs
   int aligned;             // unit-aligned schedule (no partial slots)
   int64_t slot_floats;     // floats per partial slot (gate/up, the larger)
+  int64_t act_rows;        // rows per activation plane
   size_t off_hdr, off_chunk, off_pair, off_sb, off_tok, off_tokpos, off_dcount, off_x8, off_act8, off_out,
-      off_ucount, off_part, total;
+      off_ucount, off_part, off_ctab, total;
 };
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -150,8 +155,9 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   o = align_up(o + (D / kM + 1) * sizeof(uint32_t), 256);
   g.off_x8 = o;
   o = align_up(o + 2 * g.P_max * D, 256);
+  g.act_rows = T <= kTokMax ? std::max<int64_t>(g.P_max, 8 * (1 + g.C_max)) : g.P_max;
   g.off_act8 = o;
-  o = align_up(o + 2 * g.P_max * g.I_act, 256);
+  o = align_up(o + 2 * g.act_rows * g.I_act, 256);
   g.off_out = o;
   o = align_up(o + g.P_max * D * sizeof(float), 256);
   // stream-K state: per-unit tickets and partial accumulator slots
@@ -165,6 +171,8 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   o = align_up(o + (g.U_gu + g.U_dn) * sizeof(uint32_t), 256);
   g.off_part = o;
   o = align_up(o + 2 * static_cast<int64_t>(G) * g.slot_floats * sizeof(float), 256);
+  g.off_ctab = o;
+  o = align_up(o + g.C_max * 8 * (sizeof(float) + 1), 256);
   g.total = o;
   return g;
 }
@@ -187,6 +195,8 @@ static Plan plan_views(const Geometry& g, void* ws) {
   p.x8 = b + g.off_x8;
   p.act8 = b + g.off_act8;
   p.out_part = reinterpret_cast<float*>(b + g.off_out);
+  p.ctab_wb = reinterpret_cast<float*>(b + g.off_ctab);
+  p.ctab_sb = reinterpret_cast<uint8_t*>(p.ctab_wb + g.C_max * 8);
   return p;
 }
 
@@ -211,6 +221,8 @@ struct PlanArgs {
   int T, K, E, D, CH, dup_mode, pos_offset, sort_tok, n_dcount;
   int64_t P_max;
   int local_rows;  // token CTAs write their routed pair rows themselves
+  int tok_mode;    // T <= kTokMax: per-(chunk, token) tables instead of per-pair rows
+  int64_t n_ctab;  // token mode: table entries to clear (C_max * 8)
   PermuteOut po;
   int32_t* status;
   uint32_t* ucount;  // stream-K unit tickets to clear (all plan CTAs share the work)
@@ -334,7 +346,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) red[warp] = mx;
     int nrows = 1;
-    if (A.local_rows && cache_idx) {
+    if (A.local_rows && cache_idx && !A.tok_mode) {
       nrows = 1 + K;
       // warp j places this token's entry j: its position is the number of
       // valid pairs with a smaller expert plus the number with the same
@@ -392,9 +404,15 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
   if (cache_idx && npairs <= kFastPlanPairs) {
     int32_t* spos = rest;            // [npairs] position (or -1)
     int32_t* scnt = spos + npairs;   // [npairs] pair count of the expert (leaders only)
+    float* swb = reinterpret_cast<float*>(scnt + npairs);  // [npairs] bf16 routing weight
+    int32_t* sq = reinterpret_cast<int32_t*>(swb + npairs);  // [npairs] activation prescale
     __shared__ int tot[4];           // chunks, slots, pairs
     if (tid < 4) tot[tid] = 0;
     for (int i = tid; i < A.n_dcount; i += blockDim.x) P.dcount[i] = 0u;
+    for (int64_t i = tid; i < A.n_ctab; i += blockDim.x) {
+      P.ctab_wb[i] = 0.f;
+      P.ctab_sb[i] = 127;
+    }
     if (A.po.expert_count)
       for (int x = tid; x < E; x += blockDim.x) A.po.expert_count[x] = 0;
     for (int t = tid; t < A.pos_offset; t += blockDim.x) {  // shared-expert pairs
@@ -426,6 +444,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
         P.pair_wb[pos] = wb;
         P.pair_q[pos] = q;
         P.sb2[pos] = static_cast<uint8_t>(127 - q);
+        swb[l] = wb;
+        sq[l] = q;
         if (A.po.pos_to_expert) A.po.pos_to_expert[pos - A.pos_offset] = e;
         if (before == 0) {
           atomicAdd(&tot[0], (cnt + A.CH - 1) / A.CH);
@@ -461,6 +481,15 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
             P.chunk_pair0[cb] = first + ck * A.CH;
             P.chunk_np[cb] = min(A.CH, cnt - ck * A.CH);
           }
+        }
+        if (A.tok_mode) {
+          // one chunk per expert (at most T <= 8 pairs): its index is the
+          // number of distinct experts below e; record (weight, scale) of this token
+          int cb = 0;
+          for (int m = 0; m < npairs; ++m) cb += (scnt[m] > 0) & (sval[m] < e);
+          const int t = l / K;
+          P.ctab_wb[cb * 8 + t] = swb[l];
+          P.ctab_sb[cb * 8 + t] = static_cast<uint8_t>(127 - sq[l]);
         }
       }
       if (A.sort_tok) {
@@ -680,6 +709,7 @@ struct UnitArgs {
   int aligned;           // 1: CTA boundaries on unit boundaries (many units), 0: split units
   uint32_t* ucount;      // [U_max] per-unit tickets, cleared by the plan kernel
   float* part;           // [(U_max + G)][slot] partial accumulators
+  int64_t act_rows;      // rows per activation plane (P_max, or (1 + C_max) * 8 in token mode)
 };
 
 template <int NT, int BOXES>
@@ -772,7 +802,7 @@ __device__ __forceinline__ Sched make_sched(const Desc& d, const UnitArgs& a, bo
 }
 
 struct UnitInfo {
-  int shared, e, pair0, np, tile;
+  int shared, e, pair0, np, tile, chunk;
 };
 
 __device__ __forceinline__ UnitInfo unit_info(const Desc& d, const UnitArgs& a, const Sched& s, int64_t u, bool down) {
@@ -782,6 +812,7 @@ __device__ __forceinline__ UnitInfo unit_info(const Desc& d, const UnitArgs& a, 
   if (u < s.n_sh_units) {
     const int c = static_cast<int>(u / tiles_sh);
     r.shared = 1;
+    r.chunk = c;
     r.tile = static_cast<int>(u - static_cast<int64_t>(c) * tiles_sh);
     r.e = 0;
     r.pair0 = c * a.CH;
@@ -790,6 +821,7 @@ __device__ __forceinline__ UnitInfo unit_info(const Desc& d, const UnitArgs& a, 
     const int64_t uu = u - s.n_sh_units;
     const int c = static_cast<int>(uu / tiles_rt);
     r.shared = 0;
+    r.chunk = c;
     r.tile = static_cast<int>(uu - static_cast<int64_t>(c) * tiles_rt);
     r.e = a.P.chunk_expert[c];
     r.pair0 = a.P.chunk_pair0[c];
@@ -833,7 +865,7 @@ __device__ __forceinline__ void gateup_finish(const Desc& d, const UnitArgs& a, 
                                               const float (&g)[8 * NT], const float (&u)[8 * NT]) {
   const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
   uint8_t* hi_plane = a.P.act8;
-  uint8_t* lo_plane = a.P.act8 + a.P_max * I_act;
+  uint8_t* lo_plane = a.P.act8 + a.act_rows * I_act;
   const int col = ui.tile * kM + row;
 #pragma unroll
   for (int r = 0; r < 8 * NT; ++r) {
@@ -859,6 +891,88 @@ __device__ __forceinline__ void gateup_finish(const Desc& d, const UnitArgs& a, 
   }
 }
 
+// The unit's finishing CTA: sum the partial slots of CTAs cf..cl (one row, NV
+// values each) in CTA order. Slots are read four CTAs at a time so their
+// loads overlap; empty CTAs are skipped; a CTA's slot is 2c when the unit is
+// its first segment, else 2c+1.
+template <int NV, typename SchedT>
+__device__ __forceinline__ void sum_slots(const SchedT& sc, int cf, int cl, int64_t us, const float* part, int slot_floats,
+                                          int row, float (&acc)[NV]) {
+  constexpr int NB = NV <= 16 ? 4 : (NV <= 32 ? 2 : 1);  // slots in flight (register budget)
+#pragma unroll
+  for (int t = 0; t < NV; ++t) acc[t] = 0.f;
+  int64_t lc = sc.lo(cf);
+  for (int c0 = cf; c0 <= cl; c0 += NB) {
+    const float* sl[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      const int cc = c0 + b;
+      sl[b] = nullptr;
+      if (cc <= cl) {
+        const int64_t ln = sc.lo(cc + 1);
+        if (lc < ln) sl[b] = part + (2 * static_cast<int64_t>(cc) + (lc >= us ? 0 : 1)) * slot_floats;
+        lc = ln;
+      }
+    }
+    float v[NB][NV];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < NV; ++t) v[b][t] = sl[b] ? __ldcg(sl[b] + t * kM + row) : 0.f;
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if (sl[b])
+#pragma unroll
+        for (int t = 0; t < NV; ++t) acc[t] += v[b][t];
+  }
+}
+
+// Token-mode gate/up epilogue: the accumulator columns are the (up to 8)
+// tokens; every (chunk, token) activation row is written, as zeros where the
+// token is not routed to the chunk's expert (or t >= T), so the down phase can
+// run each unit over all experts with the same 8 token columns.
+template <bool kFP8>
+__device__ __forceinline__ void gateup_finish_tok(const Desc& d, const UnitArgs& a, const UnitInfo& ui, int row,
+                                                  const float (&g)[8], const float (&u)[8]) {
+  const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
+  uint8_t* hi_plane = a.P.act8;
+  uint8_t* lo_plane = a.P.act8 + a.act_rows * I_act;
+  const int col = ui.tile * kM + row;
+  const int64_t slot = kFP8 ? 0 : 1 + ui.chunk;
+  float wbv[8];
+  int qv[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    wbv[r] = 0.f;
+    qv[r] = 0;
+    if (r < a.T) {
+      wbv[r] = kFP8 ? 1.f : __ldg(a.P.ctab_wb + ui.chunk * 8 + r);
+      qv[r] = kFP8 ? 0 : 127 - static_cast<int>(__ldg(a.P.ctab_sb + ui.chunk * 8 + r));
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    __nv_fp8_storage_t hb = 0, lb = 0;
+    if (wbv[r] != 0.f) {
+      // reference roundings as in gateup_finish
+      const float gf = round_bf16(g[r]);
+      const float uf = round_bf16(u[r]);
+      const float gc = gf > 10.f ? 10.f : gf;
+      const float uc = uf > 10.f ? 10.f : (uf < -10.f ? -10.f : uf);
+      const float sig = 1.f / (1.f + expf(-gc));
+      float av = round_bf16((gc * sig) * uc);
+      if (!kFP8) av = round_bf16(av * wbv[r]);
+      const float v = av * exp2i(qv[r]);
+      hb = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+      const __half_raw hr = __nv_cvt_fp8_to_halfraw(hb, __NV_E4M3);
+      const float hf = __half2float(*reinterpret_cast<const __half*>(&hr));
+      lb = __nv_cvt_float_to_fp8(v - hf, __NV_SATFINITE, __NV_E4M3);
+    }
+    hi_plane[(slot * 8 + r) * I_act + col] = hb;
+    lo_plane[(slot * 8 + r) * I_act + col] = lb;
+  }
+}
+
 // Persistent stream-K kernel for one phase. kDown = false: gate/up (A boxes =
 // w1 and w3 tiles of one 128-column k-step); kDown = true: down (A boxes = two
 // k-boxes of w2). One CTA per SM: warp 4 streams TMA, warp 5 issues tcgen05
@@ -866,7 +980,7 @@ __device__ __forceinline__ void gateup_finish(const Desc& d, const UnitArgs& a, 
 // the next unit's MMAs overlap this unit's epilogue). A unit split between
 // CTAs writes f32 partials; the last of them (atomic ticket, no waiting) sums
 // the partials in CTA order and finishes the unit.
-template <bool kDown, int NT>
+template <bool kDown, int NT, bool kTok = false>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_constant__ Desc d,
                                                          const __grid_constant__ CallMaps cm, UnitArgs a) {
   constexpr int BOXES = kDown ? 2 : 1;
@@ -929,6 +1043,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
 
   if (warp == 4) {
     // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
+    const uint64_t pol = l2_evict_first_policy();
     int64_t step = 0;
     bool ok = true;
     for (int64_t s = s_begin; s < s_end && ok;) {
@@ -975,6 +1090,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
         uint8_t* S = base + st * L::kStage;
         uint8_t* Bs = S + L::kA;
         uint8_t* SF = Bs + L::kB;
+        // copies first (their latency overlaps the scale-atom work below): on a
+        // segment's first step the barrier gets its bytes now and its arrival
+        // once the warp has written the unit's B scale atom
+        if (lane == 0) {
+          if (k == k0)
+            mbar_expect_tx(&bars->full[st], tx);
+          else
+            mbar_arrive_expect_tx(&bars->full[st], tx);
+          const int xa = kDown ? k * 256 : k * 128;
+          tma_load_2d_hint(S, wm, &bars->full[st], 0, static_cast<int>(y0 + static_cast<int64_t>(k) * 256), pol);
+          for (int b = 0; b < BOXES; ++b)
+            tma_load_3d(Bs + b * 2 * NT * 1024, bm, &bars->full[st], xa + b * 128, kTok ? 0 : ui.pair0, 0);
+          bulk_load_hint(SF, sf0 + static_cast<int64_t>(k) * 1024, 1024, &bars->full[st], pol);
+        }
         if (k == k0) {
           // the unit's B scale atom: word (m0, m1) = scale of B row n = m0 + 32*m1
           for (int wi = lane; wi < 128; wi += 32) {
@@ -983,21 +1112,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
             uint32_t b = 127u;
             if (n < N) {
               const int r = n % (8 * NT);
-              if (r < ui.np) b = sbv[ui.pair0 + r];
+              if (kTok) {
+                if (r < a.T) b = a.P.sb1[r];  // token rows: the shared rows 0..T-1
+              } else if (r < ui.np) {
+                b = sbv[ui.pair0 + r];
+              }
             }
             *reinterpret_cast<uint32_t*>(SF + 1024 + m0 * 16 + m1 * 4) = b * 0x01010101u;
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->full[st]);
         }
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&bars->full[st], tx);
-          const int xa = kDown ? k * 256 : k * 128;
-          tma_load_2d(S, wm, &bars->full[st], 0, static_cast<int>(y0 + static_cast<int64_t>(k) * 256));
-          for (int b = 0; b < BOXES; ++b)
-            tma_load_3d(Bs + b * 2 * NT * 1024, bm, &bars->full[st], xa + b * 128, ui.pair0, 0);
-          bulk_load(SF, sf0 + static_cast<int64_t>(k) * 1024, 1024, &bars->full[st]);
-        }
       }
       s = us + k1;
     }
@@ -1129,30 +1256,27 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
         epi_bar();  // every thread has read the flag before it is reused
         if (finish) {
           __threadfence();
-          // sum every segment's partial in CTA order (this CTA's from registers)
-#pragma unroll
-          for (int n = 0; n < NP; ++n) {
-            g[n] = 0.f;
-            v[n] = 0.f;
-          }
-          int64_t lc = sc.lo(cf);
-          for (int cc = cf; cc <= cl; ++cc) {
-            const int64_t ln = sc.lo(cc + 1);
-            const bool empty_cta = !(lc < ln);
-            const bool first_of_cta = lc >= us;  // the unit is this CTA's first segment
-            lc = ln;
-            if (empty_cta) continue;
-            const float* sl = a.part + (2 * static_cast<int64_t>(cc) + (first_of_cta ? 0 : 1)) * kSlot;
+          // sum every segment's partial in CTA order (this CTA's included)
+          if constexpr (kDown) {
+            sum_slots<NP>(sc, cf, cl, us, a.part, kSlot, row, g);
+          } else {
+            float gv[2 * NP];
+            sum_slots<2 * NP>(sc, cf, cl, us, a.part, kSlot, row, gv);
 #pragma unroll
             for (int n = 0; n < NP; ++n) {
-              g[n] += __ldcg(sl + n * kM + row);
-              if (!kDown) v[n] += __ldcg(sl + (NP + n) * kM + row);
+              g[n] = gv[n];
+              v[n] = gv[NP + n];
             }
           }
         }
       }
       if (finish) {
-        if (!kDown) {
+        if constexpr (kTok) {
+          if (ui.shared)
+            gateup_finish_tok<true>(d, a, ui, row, g, v);
+          else
+            gateup_finish_tok<false>(d, a, ui, row, g, v);
+        } else if (!kDown) {
           if (ui.shared)
             gateup_finish<NT, true>(d, a, ui, row, g, v);
           else
@@ -1188,6 +1312,370 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   __syncthreads();
   // copies issued but never consumed (only after a timed-out wait): let them
   // land before the CTA's shared memory is released
+  if (threadIdx.x == 128) {
+    for (int64_t k = bars->consumed; k < bars->issued; ++k)
+      if (!mbar_wait(&bars->full[k % S_], static_cast<uint32_t>((k / S_) & 1))) {
+        report(a.status, HS_DEV_TIMEOUT);
+        break;
+      }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc5::fence_after_sync();
+    tc5::tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Token-mode down phase (T <= 8)
+// ---------------------------------------------------------------------------
+// A unit is one 128-row tile of D. Its k-steps are the shared expert's I_sh/256
+// steps (FP8, twice the bytes, weight 2) followed by I/256 steps of every
+// routed chunk (one expert each) in ascending expert order. B is the chunk's 8
+// token rows of act8, so the accumulator columns are tokens and TMEM sums every
+// expert's contribution: routed experts into columns [0, 16) of a buffer, the
+// shared expert into [48, 64), kept apart so the two sums round to bf16
+// separately as the reference's routed + shared add does. The CTA that
+// completes a unit writes the output rows; no per-pair rows, no finalize pass.
+struct TokSched {
+  int U, nsh, nrt, C, Su, G;
+  int64_t Wu, W;
+
+  __device__ __forceinline__ static int64_t udiv(int64_t a, int64_t b) {
+    if (((a | b) >> 32) == 0) return static_cast<uint32_t>(a) / static_cast<uint32_t>(b);
+    return a / b;
+  }
+  __device__ __forceinline__ int64_t unit_of(int64_t s) const { return udiv(s, Su); }
+  __device__ __forceinline__ int64_t ustart(int64_t u) const { return u * Su; }
+  // weight position where step s starts
+  __device__ __forceinline__ int64_t wpos(int64_t s) const {
+    const int64_t u = unit_of(s);
+    const int64_t k = s - u * Su;
+    return u * Wu + (k < nsh ? 2 * k : 2 * nsh + (k - nsh));
+  }
+  // first step at or after weight position w
+  __device__ __forceinline__ int64_t step_at(int64_t w) const {
+    const int64_t u = udiv(w, Wu);
+    const int64_t r = w - u * Wu;
+    return u * Su + (r <= 2 * nsh ? (r + 1) / 2 : nsh + (r - 2 * nsh));
+  }
+  __device__ __forceinline__ int64_t lo(int c) const {
+    if (c >= G) return static_cast<int64_t>(U) * Su;
+    return step_at(udiv(W * c, G));
+  }
+  // largest c with lo(c) <= s (lo(c) <= s <=> floor(W c / G) <= wpos(s))
+  __device__ __forceinline__ int cta_of(int64_t s) const {
+    const int64_t c = udiv(static_cast<int64_t>(G) * (wpos(s) + 1) - 1, W);
+    return c < G - 1 ? static_cast<int>(c) : G - 1;
+  }
+};
+
+__device__ __forceinline__ TokSched make_tok_sched(const Desc& d, const UnitArgs& a) {
+  TokSched s;
+  s.U = d.D / kM;
+  s.nsh = a.use_shared ? d.I_sh / 256 : 0;
+  s.nrt = d.I / 256;
+  s.C = a.P.hdr[0];
+  s.Su = s.nsh + s.C * s.nrt;
+  s.Wu = 2 * s.nsh + static_cast<int64_t>(s.C) * s.nrt;
+  s.W = s.Wu * s.U;
+  s.G = a.G;
+  return s;
+}
+
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __grid_constant__ Desc d,
+                                                                        const __grid_constant__ CallMaps cm,
+                                                                        UnitArgs a) {
+  using L = SmemLayout<1, 2>;
+  constexpr int S_ = L::kNumStages;
+  static_assert(S_ >= 2 && S_ <= 4, "stage count");
+  static_assert(sizeof(Bars) <= L::kBarBytes, "barrier block");
+  constexpr int N = 16;
+  // TMEM (256 columns): accumulator buffers at 0 and 96 (routed at +0, shared
+  // at +48), A scales at 192 + 8*stage, B scales at 224 + 4*stage
+  constexpr uint32_t kAcc = 96;
+  constexpr uint32_t kAccSh = 48;
+  constexpr uint32_t kSfa = 192;
+  constexpr uint32_t kSfb = 224;
+  constexpr int kSlot = 2 * kM * 8;  // routed and shared sums of 8 tokens
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {
+    pdl_wait();
+    if (threadIdx.x == 0) report(a.status, HS_DEV_SMEM_ALIGN);
+    return;
+  }
+  uint8_t* base = smem_raw;
+  Bars* bars = reinterpret_cast<Bars*>(base + S_ * L::kStage);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = d.D;
+  const int c = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S_; ++i) {
+      mbar_init(&bars->full[i], 1);
+      mbar_init(&bars->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->acc_full[i], 1);
+      mbar_init(&bars->acc_empty[i], 4);
+    }
+    mbar_init(&bars->mma_done, 1);
+    bars->issued = 0;
+    bars->consumed = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) tc5::tmem_alloc(&bars->tmem, 256);
+  if (warp == 4 && lane == 0) {
+    prefetch_tensormap(&d.tm_w2);
+    prefetch_tensormap(&d.tm_sw2);
+    prefetch_tensormap(&cm.tm_act8);
+  }
+  pdl_wait();  // the gate/up phase (and the plan before it) is complete
+  pdl_trigger();
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t tmem = bars->tmem;
+  const TokSched sc = make_tok_sched(d, a);
+  const bool any = sc.W > 0;
+  const int64_t s_begin = any ? sc.lo(c) : 0, s_end = any ? sc.lo(c + 1) : 0;
+
+  if (warp == 4) {
+    // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
+    // chunk table in registers: lane j keeps chunks j, j+32, j+64, j+96 (expert
+    // id and the 8 per-token B-scale bytes as two words)
+    static_assert(kTokChunks <= 4 * 32, "token-mode chunk table");
+    const uint64_t pol = l2_evict_first_policy();
+    int ex[4];
+    uint32_t sw0[4], sw1[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int cc = lane + 32 * i;
+      ex[i] = 0;
+      sw0[i] = sw1[i] = 0x7f7f7f7fu;
+      if (cc < sc.C) {
+        ex[i] = a.P.chunk_expert[cc];
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(a.P.ctab_sb + cc * 8);
+        sw0[i] = w[0];
+        sw1[i] = w[1];
+      }
+    }
+    int64_t step = 0;
+    for (int64_t s = s_begin; s < s_end; ++s, ++step) {
+      const int64_t u = sc.unit_of(s);
+      const int k = static_cast<int>(s - u * sc.Su);
+      const bool shared = k < sc.nsh;
+      const int kr = k - sc.nsh;
+      const int ch = shared ? 0 : kr / sc.nrt;
+      const int kk = shared ? k : kr - ch * sc.nrt;
+      int e_sel = 0;
+      uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (i == (ch >> 5)) {
+          e_sel = ex[i];
+          w0 = sw0[i];
+          w1 = sw1[i];
+        }
+      const int e = __shfl_sync(0xffffffffu, e_sel, ch & 31);
+      w0 = __shfl_sync(0xffffffffu, w0, ch & 31);
+      w1 = __shfl_sync(0xffffffffu, w1, ch & 31);
+      const int st = static_cast<int>(step % S_);
+      if (step >= S_) {
+        bool w = true;
+        if (lane == 0) w = mbar_wait(&bars->empty[st], static_cast<uint32_t>(((step / S_) - 1) & 1));
+        w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+        if (!w) {
+          if (lane == 0) report(a.status, HS_DEV_TIMEOUT);
+          break;
+        }
+      }
+      uint8_t* S = base + st * L::kStage;
+      uint8_t* Bs = S + L::kA;
+      uint8_t* SF = Bs + L::kB;
+      // this step's B scale atom: word (m0, m1) = scale of B row n = m0 + 32*m1;
+      // rows 0..7 are the tokens' hi rows, 8..15 their lo rows
+      for (int wi = lane; wi < 128; wi += 32) {
+        const int m0 = wi >> 2, m1 = wi & 3;
+        const int n = m0 + 32 * m1;
+        uint32_t b = 127u;
+        if (n < N && !shared) {
+          const int t = n & 7;
+          b = ((t < 4 ? w0 : w1) >> (8 * (t & 3))) & 0xffu;
+        }
+        *reinterpret_cast<uint32_t*>(SF + 1024 + m0 * 16 + m1 * 4) = b * 0x01010101u;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        const int tile = static_cast<int>(u);
+        const uint32_t tx = (shared ? 2 * kBoxBytes : kBoxBytes) + L::kB + 1024;
+        mbar_arrive_expect_tx(&bars->full[st], tx);
+        int64_t ya;
+        const uint8_t* sfp;
+        if (shared) {
+          ya = (static_cast<int64_t>(tile) * (d.I_sh / kM) + 2 * kk) * kM;
+          sfp = d.sh_s2a + (static_cast<int64_t>(tile) * (d.I_sh / kM) + 2 * kk) * 512;
+        } else {
+          ya = ((static_cast<int64_t>(e) * (D / kM) + tile) * (d.I / kM) + 2 * kk) * kM;
+          sfp = d.s2a + ((static_cast<int64_t>(e) * (D / kM) + tile) * (d.I / kM) + 2 * kk) * 512;
+        }
+        tma_load_2d_hint(S, shared ? &d.tm_sw2 : &d.tm_w2, &bars->full[st], 0, static_cast<int>(ya), pol);
+        const int brow = (shared ? 0 : 1 + ch) * 8;
+        for (int b = 0; b < 2; ++b)
+          tma_load_3d(Bs + b * 2048, &cm.tm_act8, &bars->full[st], kk * 256 + b * 128, brow, 0);
+        bulk_load_hint(SF, sfp, 1024, &bars->full[st], pol);
+      }
+    }
+    if (lane == 0) bars->issued = static_cast<int32_t>(step);
+  } else if (warp == 5) {
+    // ---------------- MMA issuer (lane 0) ----------------
+    if (lane == 0) {
+      int64_t step = 0;
+      int seg = 0;
+      bool ok = true;
+      for (int64_t s = s_begin; s < s_end && ok; ++seg) {
+        const int64_t u = sc.unit_of(s);
+        const int64_t us = sc.ustart(u);
+        const int k0 = static_cast<int>(s - us);
+        const int k1 = static_cast<int>(min64(static_cast<int64_t>(sc.Su), s_end - us));
+        const int buf = seg & 1;
+        if (seg >= 2 && !mbar_wait(&bars->acc_empty[buf], static_cast<uint32_t>(((seg >> 1) - 1) & 1))) {
+          report(a.status, HS_DEV_TIMEOUT);
+          break;
+        }
+        tc5::fence_after_sync();
+        const uint32_t acc = tmem + buf * kAcc;
+        const int first_rt = k0 > sc.nsh ? k0 : sc.nsh;  // first routed step of the segment
+        for (int k = k0; k < k1; ++k, ++step) {
+          const int st = static_cast<int>(step % S_);
+          if (!mbar_wait(&bars->full[st], static_cast<uint32_t>((step / S_) & 1))) {
+            report(a.status, HS_DEV_TIMEOUT);
+            ok = false;
+            break;
+          }
+          tc5::fence_after_sync();
+          uint8_t* S = base + st * L::kStage;
+          const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
+          const uint32_t sfa0 = tmem + kSfa + st * 8;
+          const uint32_t sfb = tmem + kSfb + st * 4;
+          tc5::cp_sf_32x128b(sfb, tc5::sdesc_sf(sSF + 1024));
+          tc5::cp_sf_32x128b(sfa0, tc5::sdesc_sf(sSF));
+          tc5::cp_sf_32x128b(sfa0 + 4, tc5::sdesc_sf(sSF + 512));
+          const bool shared = k < sc.nsh;
+          const uint32_t afmt = shared ? 0u : 5u;
+          const uint32_t dcol = acc + (shared ? kAccSh : 0u);
+          const bool first = shared ? (k == k0) : (k == first_rt);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint64_t ad = tc5::sdesc_sw128(sA + i * kBoxBytes);
+            const uint64_t bd = tc5::sdesc_sw128(sB + i * 2048);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t id = tc5::idesc_mxf8f6f4(afmt, N, j, j);
+              const uint32_t accum = (first && i == 0 && j == 0) ? 0u : 1u;
+              tc5::mma_mxf8f6f4(dcol, ad + 2 * j, bd + 2 * j, id, accum,
+                                (sfa0 + 4 * i) | (static_cast<uint32_t>(j) << 30),
+                                sfb | (static_cast<uint32_t>(j) << 30));
+            }
+          }
+          tc5::commit(&bars->empty[st]);
+        }
+        tc5::commit(&bars->acc_full[buf]);
+        s = us + k1;
+      }
+      bars->consumed = static_cast<int32_t>(step);
+      tc5::commit(&bars->mma_done);
+      if (!mbar_wait(&bars->mma_done, 0)) report(a.status, HS_DEV_TIMEOUT);
+    }
+  } else {
+    // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31) ----------------
+    const int row = 32 * warp + lane;
+    const int etid = threadIdx.x;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+    int seg = 0;
+    for (int64_t s = s_begin; s < s_end; ++seg) {
+      const int64_t u = sc.unit_of(s);
+      const int64_t us = sc.ustart(u);
+      const int nk = sc.Su;
+      const int k0 = static_cast<int>(s - us);
+      const int k1 = static_cast<int>(min64(static_cast<int64_t>(nk), s_end - us));
+      const int buf = seg & 1;
+      if (!mbar_wait(&bars->acc_full[buf], static_cast<uint32_t>((seg >> 1) & 1))) {
+        if (etid == 0) report(a.status, HS_DEV_TIMEOUT);
+        break;
+      }
+      tc5::fence_after_sync();
+      float c0[16], c1[16];
+      const uint32_t acc = tmem + lane_off + buf * kAcc;
+      tc5::ld_32x32b_x16(acc, c0);
+      tc5::ld_32x32b_x16(acc + kAccSh, c1);
+      tc5::wait_ld();
+      tc5::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+      const bool had_sh = k0 < sc.nsh, had_rt = k1 > sc.nsh;
+      float r[8], h[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        r[t] = had_rt ? c0[t] + c0[8 + t] : 0.f;
+        h[t] = had_sh ? c1[t] + c1[8 + t] : 0.f;
+      }
+      const int cf = sc.cta_of(us);
+      const int cl = sc.cta_of(us + nk - 1);
+      bool finish = (cf == cl);
+      if (!finish) {
+        float* slot = a.part + (2 * static_cast<int64_t>(c) + (u == sc.unit_of(s_begin) ? 0 : 1)) * kSlot;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          __stcg(slot + t * kM + row, r[t]);
+          __stcg(slot + (8 + t) * kM + row, h[t]);
+        }
+        __threadfence();
+        epi_bar();
+        if (etid == 0) {
+          const uint32_t mine = static_cast<uint32_t>(k1 - k0);
+          bars->flag = atomicAdd(&a.ucount[u], mine) + mine == static_cast<uint32_t>(nk);
+        }
+        epi_bar();
+        finish = bars->flag != 0;
+        epi_bar();
+        if (finish) {
+          __threadfence();
+          float rh[16];
+          sum_slots<16>(sc, cf, cl, us, a.part, kSlot, row, rh);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            r[t] = rh[t];
+            h[t] = rh[8 + t];
+          }
+        }
+      }
+      if (finish) {
+        const int64_t dd = u * kM + row;
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          if (t < a.T) {
+            if (a.out_f32) a.out_f32[t * static_cast<int64_t>(D) + dd] = r[t];
+            float o = round_bf16(r[t]);
+            if (a.use_shared) o += round_bf16(h[t]);
+            a.out[t * static_cast<int64_t>(D) + dd] = __float2bfloat16_rn(o);
+          }
+      }
+      s = us + k1;
+    }
+    // nothing to compute (every pair skipped, no shared expert): zeros
+    if (!any)
+      for (int tile = c; tile < D / kM; tile += sc.G)
+        for (int t = 0; t < a.T; ++t) {
+          const int64_t o = t * static_cast<int64_t>(D) + tile * kM + etid;
+          if (a.out_f32) a.out_f32[o] = 0.f;
+          a.out[o] = __float2bfloat16_rn(0.f);
+        }
+  }
+
+  tc5::fence_before_sync();
+  __syncthreads();
   if (threadIdx.x == 128) {
     for (int64_t k = bars->consumed; k < bars->issued; ++k)
       if (!mbar_wait(&bars->full[k % S_], static_cast<uint32_t>((k / S_) & 1))) {
@@ -1277,13 +1765,15 @@ static int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, ui
   return HS_OK;
 }
 
-// 3D map [planes][rows][cols]: box cols x box_rows x planes, 128B swizzle.
+// 3D map [planes][rows][cols] with planes plane_rows rows apart (rows <=
+// plane_rows visible; rows beyond read as zero): box cols x box_rows x planes,
+// 128B swizzle.
 static int make_map_3d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t planes,
-                       uint64_t pitch, uint32_t box_rows) {
+                       uint64_t pitch, uint32_t box_rows, uint64_t plane_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return HS_ERR_UNSUPPORTED;
   cuuint64_t dims[3] = {cols, rows, planes};
-  cuuint64_t strides[2] = {pitch, pitch * rows};
+  cuuint64_t strides[2] = {pitch, pitch * plane_rows};
   cuuint32_t box[3] = {128, box_rows, static_cast<cuuint32_t>(planes)};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
@@ -1299,7 +1789,7 @@ static int make_map_3d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t
 static bool dim_ok(int64_t v, int64_t mult, int64_t lo, int64_t hi) { return v % mult == 0 && v >= lo && v <= hi; }
 static bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
-template <bool kDown, int NT>
+template <bool kDown, int NT, bool kTok = false>
 static int launch_sk(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaStream_t st) {
   constexpr int bytes = SmemLayout<NT, kDown ? 2 : 1>::kBytes;
   static std::atomic<uint64_t> done{0};
@@ -1307,10 +1797,27 @@ static int launch_sk(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaS
   HS_CUDA_CHECK(cudaGetDevice(&dev));
   const uint64_t bit = 1ull << (dev & 63);
   if (!(done.load() & bit)) {
-    HS_CUDA_CHECK(cudaFuncSetAttribute(sk_kernel<kDown, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    HS_CUDA_CHECK(
+        cudaFuncSetAttribute(sk_kernel<kDown, NT, kTok>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
     done.fetch_or(bit);
   }
-  HS_CUDA_CHECK(launch_pdl(sk_kernel<kDown, NT>, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes, st, d, cm, a));
+  HS_CUDA_CHECK(launch_pdl(sk_kernel<kDown, NT, kTok>, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes, st,
+                           d, cm, a));
+  return check_launch();
+}
+
+static int launch_tok_down(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaStream_t st) {
+  constexpr int bytes = SmemLayout<1, 2>::kBytes;
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  HS_CUDA_CHECK(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(done.load() & bit)) {
+    HS_CUDA_CHECK(cudaFuncSetAttribute(tok_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.fetch_or(bit);
+  }
+  HS_CUDA_CHECK(
+      launch_pdl(tok_down_kernel, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes, st, d, cm, a));
   return check_launch();
 }
 
@@ -1342,7 +1849,7 @@ static int sm_count() {
 static int plan_smem(int E, int npairs) {
   const int cached = npairs <= kLocalPairs ? 2 * npairs : 0;  // ids and post-duplicate experts
   const int general = 4 * E + 2 + (kPlanThreads / 32) * E;
-  const int fast = npairs <= kFastPlanPairs ? 2 * npairs : 0;
+  const int fast = npairs <= kFastPlanPairs ? 4 * npairs : 0;
   return static_cast<int>((cached + std::max(general, fast)) * sizeof(int32_t));
 }
 
@@ -1443,8 +1950,10 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
 
   CallMaps cm;
   int rc;
-  if ((rc = make_map_3d(&cm.tm_x8, P.x8, d.D, g.P_max, 2, d.D, 8 * NT))) return rc;
-  if ((rc = make_map_3d(&cm.tm_act8, P.act8, g.I_act, g.P_max, 2, g.I_act, 8 * NT)))
+  const bool tok = T <= kTokMax;
+  // token mode reads the T token rows (rows T..7 of the box read as zero)
+  if ((rc = make_map_3d(&cm.tm_x8, P.x8, d.D, tok ? T : g.P_max, 2, d.D, 8 * NT, g.P_max))) return rc;
+  if ((rc = make_map_3d(&cm.tm_act8, P.act8, g.I_act, g.act_rows, 2, g.I_act, 8 * NT, g.act_rows)))
     return rc;
 
   PlanArgs pa;
@@ -1462,12 +1971,14 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   pa.n_dcount = d.D / kM;
   pa.P_max = g.P_max;
   pa.local_rows = local_rows ? 1 : 0;
+  pa.tok_mode = tok ? 1 : 0;
+  pa.n_ctab = tok ? g.C_max * 8 : 0;
   pa.po = PermuteOut{nullptr, nullptr, nullptr};
   pa.status = dev_status;
   pa.ucount = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + g.off_ucount);
   pa.n_ucount = g.U_gu + g.U_dn;
   if ((rc = launch_plan(pa, P, 1 + static_cast<int>(T), st))) return rc;
-  if (!local_rows) {
+  if (!local_rows && !tok) {
     HS_CUDA_CHECK(launch_pdl(gather_kernel, dim3(static_cast<unsigned>(npairs)), dim3(256), 0, st, P,
                              static_cast<int>(T), g.P_max, d.D));
     if ((rc = check_launch())) return rc;
@@ -1487,7 +1998,13 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   a.G = g.G;
   a.aligned = g.aligned;
   a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + g.off_part);
+  a.act_rows = g.act_rows;
   a.ucount = pa.ucount;
+  if (tok) {
+    if ((rc = launch_sk<false, 1, true>(d, cm, a, st))) return rc;
+    a.ucount = pa.ucount + g.U_gu;
+    return launch_tok_down(d, cm, a, st);
+  }
   if ((rc = launch_nt<false>(NT, d, cm, a, st))) return rc;
   a.ucount = pa.ucount + g.U_gu;
   return launch_nt<true>(NT, d, cm, a, st);
@@ -1531,6 +2048,8 @@ extern "C" int hs_moe_permute(const int64_t* topk_idx, int64_t T, int64_t top_k,
   pa.n_dcount = 0;
   pa.P_max = g.P_max;
   pa.local_rows = 0;
+  pa.tok_mode = 0;
+  pa.n_ctab = 0;
   pa.po = PermuteOut{pos_to_expert, expert_count, num_pos};
   pa.status = dev_status;
   pa.ucount = nullptr;
