@@ -216,9 +216,10 @@ def _graph_time_per_call(enqueue, n_calls: int, replays: int = 5) -> float:
 
 
 def moe_roofline(model, reps: int = 43):
-    """Time hs_moe_ffn_fp4 at T=3 (the verify shape) over distinct layers with
-    CUDA events on the launching stream; algorithmic bytes per call are the
-    touched experts' FP4 bytes + the FP8 shared expert + activations."""
+    """Time hs_moe_ffn_fp4 at T=3 (the verify shape) over distinct layers,
+    replayed from a CUDA graph; algorithmic bytes per call are the touched
+    experts' FP4 bytes + the FP8 shared expert + activations (under expert
+    parallelism: this rank's experts and shared rows, partials + all-reduce)."""
     import torch
     from home_seek_b200 import ops
     s = model.shape
@@ -232,12 +233,21 @@ def moe_roofline(model, reps: int = 43):
         lw = model.store.layers[l]
         idx, w = ops.router_topk(h, lw.gate, lw.bias, s.top_k, s.routed_scaling)
         calls.append((l, h, idx, w))
-    uniq = [len(set(c[2].flatten().tolist())) for c in calls]
-    per_call = _graph_time_per_call(
-        lambda: [ops.moe_ffn(model.store.desc(l), model.store.dims, h, idx, w, use_shared=True)
-                 for (l, h, idx, w) in calls], len(calls))
+    st = model.store
+    if model.ep is None:
+        uniq = [len(set(c[2].flatten().tolist())) for c in calls]
+        per_call = _graph_time_per_call(
+            lambda: [ops.moe_ffn(st.desc(l), st.dims, h, idx, w, use_shared=True) for (l, h, idx, w) in calls],
+            len(calls))
+    else:
+        # this rank's share: its touched experts, its shared-expert rows, the
+        # partials kernel plus the all-reduce (every rank replays the graph)
+        lo, hi = st.expert_offset, st.expert_offset + st.E_local
+        uniq = [len({e for e in c[2].flatten().tolist() if lo <= e < hi}) for c in calls]
+        per_call = _graph_time_per_call(
+            lambda: [model.ep.partials(st, l, h, idx, w, 0) for (l, h, idx, w) in calls], len(calls))
     ms = [per_call] * len(calls)
-    shared = 3 * s.shared_inter * s.hidden + 3 * (s.shared_inter // 128) * (s.hidden // 128)
+    shared = 3 * st.I_sh * s.hidden + 3 * (st.I_sh // 128) * (s.hidden // 128)
     act = 3 * s.hidden * 2 * 2 + 12 * 3 * 2
     bytes_ = [u * s.bytes_per_expert + shared + act for u in uniq]
     gbs = [b / (m * 1e-3) / 1e9 for b, m in zip(bytes_, ms)]
@@ -307,14 +317,20 @@ def run_ours(args):
     from home_seek_b200 import ops
     from home_seek_b200.mtp import ModelShape, MoEPathModel, MTPDecoder
     shape = ModelShape(num_layers=args.layers)
-    model = MoEPathModel(shape, device=dev, seed=rank)
+    ep = None
+    if world > 1:
+        # one decode stream over an expert-parallel group: every rank holds
+        # 1/world of the routed experts and of the shared expert (ep.py)
+        from home_seek_b200.ep import ExpertParallel
+        ep = ExpertParallel(rank, world)
+    model = MoEPathModel(shape, device=dev, seed=0, ep=ep)
     dec = MTPDecoder(model, max_tokens=(args.steps + args.warmup + 8) * (shape.num_draft + 2))
-    dec.reset(token=1234 + rank)
+    dec.reset(token=1234)
     before = ops.launches
     dec.iteration()  # eager iteration: counts this library's kernels per iteration
     launches_per_iter = ops.launches - before
     dec.capture(warmup=1)
-    dec.reset(token=1234 + rank)
+    dec.reset(token=1234)
     for _ in range(args.warmup):
         dec.replay()
     torch.cuda.synchronize()
@@ -339,13 +355,11 @@ def run_ours(args):
     tokens = int(dec.count.item())
     accepted = int(dec.accepted.item())
     t = torch.tensor([ms, float(tokens)], device=dev, dtype=torch.float64)
-    if world > 1:
+    if world > 1:  # one stream: every rank produced the same tokens; time = slowest rank
         tmax = t.clone()
         dist.all_reduce(tmax[:1], op=dist.ReduceOp.MAX)
-        dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
-        ms, tokens_all = float(tmax[0]), float(t[1])
-    else:
-        tokens_all = float(tokens)
+        ms = float(tmax[0])
+    tokens_all = float(tokens)
     value = tokens_all / (ms * 1e-3)
 
     # e2e through the public loop with host buffers: H2D of the step's input
@@ -353,7 +367,7 @@ def run_ours(args):
     host_in = torch.empty(1, dtype=torch.int64, pin_memory=True)
     host_tok = torch.empty(shape.num_draft + 2, dtype=torch.int64, pin_memory=True)
     host_cnt = torch.empty(1, dtype=torch.int64, pin_memory=True)
-    host_in.fill_(4321 + rank)
+    host_in.fill_(4321)
     dec.count.zero_()
     if world > 1:
         dist.barrier()
@@ -377,12 +391,11 @@ def run_ours(args):
     if world > 1:
         emax = et.clone()
         dist.all_reduce(emax[:1], op=dist.ReduceOp.MAX)
-        dist.all_reduce(et[1:], op=dist.ReduceOp.SUM)
-        e_ms, e_tokens = float(emax[0]), float(et[1])
+        e_ms = float(emax[0])
     e2e = {"value": float(e_tokens) / (e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": 8,
            "d2h_bytes_per_step": 8 * (shape.num_draft + 2) + 8}
 
-    roof = moe_roofline(model) if rank == 0 else None
+    roof = moe_roofline(model)  # every rank (expert parallelism runs collectives)
     status = ops.check_status(dev)
     if world > 1:
         dev_graph = dec.graph
@@ -397,12 +410,15 @@ def run_ours(args):
     cpu_v, cpu_d = cpu_sample() if not args.no_cpu else (None, {"cores": 0})
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "config1: MTP decode iteration (main T=1 + M=2 draft + fused T=3 verify + greedy "
                                "accept) over the 43-layer MoE path, bs=1",
                    "model": "DeepSeek-V4-Flash-shape 43L+MTP, 256 FP4 experts top-6 + FP8 shared, random init",
-                   "global_batch": 1, "seq_len": 3, "parallelism": f"replica x{world}",
+                   "global_batch": 1, "seq_len": 3,
+                   "parallelism": f"expert-parallel x{world} (1/{world} of the routed and shared experts per GPU, "
+                                  f"f32 partials all-reduced over NCCL)" if world > 1 else "single GPU",
                    "attention": "not in this build's step (reference PyTorch path)",
                    "l2": "inputs larger than L2: ~16 GB of distinct expert weights streamed per iteration",
                    "acceptance_rate": accepted / max(1, args.steps * shape.num_draft), "status_word": status},

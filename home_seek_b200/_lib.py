@@ -77,6 +77,11 @@ SIGNATURES = {
     "hs_rms_norm": (c_int, [c_void_p, c_void_p, c_float, c_int64, c_int64, c_void_p, c_void_p]),
     "hs_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_int64, c_int64, c_void_p, c_void_p,
                                 c_void_p]),
+    "hs_moe_ffn_fp4_partials": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,
+                                        c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hs_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]),
+    "hs_moe_combine_add_rms_norm": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_float, c_int64, c_int64,
+                                            c_void_p, c_void_p, c_void_p]),
     "hs_fill_bytes": (c_int, [c_void_p, c_int64, c_uint64, c_int32, c_int32, c_void_p]),
 }
 

@@ -103,7 +103,7 @@ HS_DI bool mbar_wait(uint64_t* bar, uint32_t parity) {
 
 // ---------------------------------------------------------------------------
 // Device: TMA (tensor) and bulk (1D) copies global -> shared, completing on an
-// mbarrier with transaction bytes. No multicast anywhere in this library.
+// mbarrier with transaction bytes. Every copy here targets the issuing CTA only.
 // ---------------------------------------------------------------------------
 HS_DI void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y) {
   asm volatile(

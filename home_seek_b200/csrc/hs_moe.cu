@@ -703,6 +703,8 @@ struct UnitArgs {
   int use_shared;
   __nv_bfloat16* out;
   float* out_f32;
+  float* shared_f32;     // partials mode: the shared expert's f32 output (or nullptr)
+  int partials;          // 1: write un-rounded f32 routed / shared sums only (no bf16 out)
   int32_t* status;
   // stream-K schedule
   int G;                 // persistent CTAs (kCtasPerSm per SM)
@@ -850,10 +852,16 @@ __device__ __forceinline__ void finalize_tile(const UnitArgs& a, int D, int tile
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (p[j] >= 0) r += v[j];
-    if (a.out_f32) a.out_f32[static_cast<int64_t>(t) * D + dd] = r;
+    const int64_t o_i = static_cast<int64_t>(t) * D + dd;
+    const float sh = a.use_shared ? __ldcg(a.P.out_part + o_i) : 0.f;  // the shared pair row of token t
+    if (a.out_f32) a.out_f32[o_i] = r;
+    if (a.partials) {
+      if (a.shared_f32) a.shared_f32[o_i] = sh;
+      continue;
+    }
     float o = round_bf16(r);
-    if (a.use_shared) o += round_bf16(__ldcg(a.P.out_part + static_cast<int64_t>(t) * D + dd));
-    a.out[static_cast<int64_t>(t) * D + dd] = __float2bfloat16_rn(o);
+    if (a.use_shared) o += round_bf16(sh);
+    a.out[o_i] = __float2bfloat16_rn(o);
   }
 }
 
@@ -1656,10 +1664,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
 #pragma unroll
         for (int t = 0; t < 8; ++t)
           if (t < a.T) {
-            if (a.out_f32) a.out_f32[t * static_cast<int64_t>(D) + dd] = r[t];
+            const int64_t o_i = t * static_cast<int64_t>(D) + dd;
+            if (a.out_f32) a.out_f32[o_i] = r[t];
+            if (a.partials) {
+              if (a.shared_f32) a.shared_f32[o_i] = h[t];
+              continue;
+            }
             float o = round_bf16(r[t]);
             if (a.use_shared) o += round_bf16(h[t]);
-            a.out[t * static_cast<int64_t>(D) + dd] = __float2bfloat16_rn(o);
+            a.out[o_i] = __float2bfloat16_rn(o);
           }
       }
       s = us + k1;
@@ -1670,7 +1683,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
         for (int t = 0; t < a.T; ++t) {
           const int64_t o = t * static_cast<int64_t>(D) + tile * kM + etid;
           if (a.out_f32) a.out_f32[o] = 0.f;
-          a.out[o] = __float2bfloat16_rn(0.f);
+          if (a.shared_f32) a.shared_f32[o] = 0.f;
+          if (!a.partials) a.out[o] = __float2bfloat16_rn(0.f);
         }
   }
 
@@ -1923,9 +1937,12 @@ extern "C" size_t hs_moe_workspace_size(int64_t T, int64_t top_k, int64_t D, int
   return geometry(T, top_k, D, I, I_sh, kCtasPerSm * sm_count()).total;
 }
 
-extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx, const float* topk_w,
-                              int64_t T, int64_t top_k, int use_shared, int dup_mode, void* out, float* out_f32,
-                              void* workspace, size_t workspace_bytes, int32_t* dev_status, void* stream) {
+// Both MoE entry points: `partials` = 0 writes the bf16 output (and optionally
+// the routed f32 sum); 1 writes the un-rounded f32 routed and shared sums only.
+static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* topk_idx, const float* topk_w,
+                        int64_t T, int64_t top_k, int use_shared, int dup_mode, void* out, float* out_f32,
+                        float* shared_f32, int partials, void* workspace, size_t workspace_bytes,
+                        int32_t* dev_status, void* stream) {
   if (!desc) return HS_ERR_BAD_ARGUMENT;
   Desc d;
   memcpy(&d, desc, sizeof(d));
@@ -1933,11 +1950,14 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   if (T < 0 || top_k < 1 || top_k > 16) return HS_ERR_BAD_SHAPE;
   if (T == 0) return HS_OK;
   if (T > (1 << 20)) return HS_ERR_BAD_SHAPE;
-  if (!hidden || !topk_idx || !topk_w || !out || !workspace) return HS_ERR_BAD_ARGUMENT;
+  if (!hidden || !topk_idx || !topk_w || !workspace) return HS_ERR_BAD_ARGUMENT;
+  if (partials ? !out_f32 : !out) return HS_ERR_BAD_ARGUMENT;
   if (dup_mode != HS_DUP_LAST && dup_mode != HS_DUP_SUM) return HS_ERR_BAD_ARGUMENT;
-  if (!aligned16(hidden) || !aligned16(out) || !aligned16(workspace) || (out_f32 && !aligned16(out_f32)))
+  if (!aligned16(hidden) || (out && !aligned16(out)) || !aligned16(workspace) || (out_f32 && !aligned16(out_f32)) ||
+      (shared_f32 && !aligned16(shared_f32)))
     return HS_ERR_ALIGN;
   use_shared = (use_shared && d.has_shared) ? 1 : 0;
+  if (partials && use_shared && !shared_f32) return HS_ERR_BAD_ARGUMENT;
   if (!d.has_shared) d.I_sh = 0;
   const Geometry g = geometry(T, top_k, d.D, d.I, d.has_shared ? d.I_sh : 0, kCtasPerSm * sm_count());
   if (workspace_bytes < g.total) return HS_ERR_WORKSPACE;
@@ -1994,6 +2014,8 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   a.use_shared = use_shared;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.out_f32 = out_f32;
+  a.shared_f32 = partials && use_shared ? shared_f32 : nullptr;
+  a.partials = partials;
   a.status = dev_status;
   a.G = g.G;
   a.aligned = g.aligned;
@@ -2008,6 +2030,21 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
   if ((rc = launch_nt<false>(NT, d, cm, a, st))) return rc;
   a.ucount = pa.ucount + g.U_gu;
   return launch_nt<true>(NT, d, cm, a, st);
+}
+
+extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx, const float* topk_w,
+                              int64_t T, int64_t top_k, int use_shared, int dup_mode, void* out, float* out_f32,
+                              void* workspace, size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  return moe_ffn_impl(desc, hidden, topk_idx, topk_w, T, top_k, use_shared, dup_mode, out, out_f32, nullptr, 0,
+                      workspace, workspace_bytes, dev_status, stream);
+}
+
+extern "C" int hs_moe_ffn_fp4_partials(const void* desc, const void* hidden, const int64_t* topk_idx,
+                                       const float* topk_w, int64_t T, int64_t top_k, int use_shared, int dup_mode,
+                                       float* routed_f32, float* shared_f32, void* workspace, size_t workspace_bytes,
+                                       int32_t* dev_status, void* stream) {
+  return moe_ffn_impl(desc, hidden, topk_idx, topk_w, T, top_k, use_shared, dup_mode, nullptr, routed_f32,
+                      shared_f32, 1, workspace, workspace_bytes, dev_status, stream);
 }
 
 extern "C" size_t hs_moe_permute_workspace_size(int64_t T, int64_t top_k, int64_t E) {

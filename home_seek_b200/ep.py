@@ -1,0 +1,130 @@
+"""Expert parallelism for the MoE layer.
+
+Reference being replaced: `_forward_ffn_ep` (inference_engine/engine.py:1575-1709)
+with its worker thread `_EPWorker` (inference_engine/parallel.py:189-290). The
+reference keeps every token on every GPU, splits the routed experts of the layer
+over the GPUs, runs each GPU on all tokens and adds the GPUs' bf16 outputs and
+the shared expert on GPU 0.
+
+Here one process per GPU (torch.distributed, NCCL over NVLink): rank r of n holds
+the routed experts [r E/n, (r+1) E/n) of every layer and rows
+[r I_sh/n, (r+1) I_sh/n) of the shared expert's intermediate dimension (an
+exact split: each intermediate unit's SwiGLU lives on one rank, the down
+projection is a sum over units). Every rank routes identically (replicated
+router, deterministic kernels), runs `hs_moe_ffn_fp4_partials` on its experts,
+which writes the UN-ROUNDED f32 routed and shared sums, and one all-reduce adds
+the ranks' partials in f32; the combine then rounds exactly where the
+single-GPU call rounds (bf16(bf16(routed) + bf16(shared))), fused with the
+layer's residual add and the next norm. There is no token dispatch at decode
+sizes: the tokens are already on every rank, so the only exchange is the
+[2, T, D] f32 combine.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+
+from . import ops
+from .expert_store import HBMExpertStore
+
+
+def expert_range(num_experts: int, rank: int, world: int) -> tuple[int, int]:
+    """(offset, count) of the routed experts rank `rank` holds."""
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not split over {world} ranks")
+    n = num_experts // world
+    return rank * n, n
+
+
+def shared_slice(shared_inter: int, rank: int, world: int) -> tuple[int, int]:
+    """[lo, hi) of the shared expert's intermediate rows rank `rank` holds
+    (a multiple of 256 wide: the kernels' shared-expert granularity)."""
+    if shared_inter % (256 * world):
+        raise ValueError(f"shared intermediate size {shared_inter} does not split into {world} x 256k")
+    n = shared_inter // world
+    return rank * n, (rank + 1) * n
+
+
+def localize(topk_idx: torch.Tensor, offset: int, held: int) -> torch.Tensor:
+    """Global expert ids -> this rank's local ids; experts held elsewhere -> -1
+    (skipped by the kernels), as the reference's per-GPU `topk_per_gpu`
+    (engine.py:1617-1622)."""
+    inside = (topk_idx >= offset) & (topk_idx < offset + held)
+    return torch.where(inside, topk_idx - offset, torch.full_like(topk_idx, -1))
+
+
+@dataclass
+class ExpertParallel:
+    """One rank's view of the expert-parallel group. `all_reduce` sums a tensor
+    over the group in place (default: torch.distributed on `group`)."""
+    rank: int
+    world: int
+    group: Optional[object] = None
+    all_reduce: Optional[Callable[[torch.Tensor], None]] = None
+
+    def __post_init__(self):
+        if self.all_reduce is None:
+            import torch.distributed as dist
+            grp = self.group
+
+            def _ar(t: torch.Tensor) -> None:
+                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=grp)
+
+            self.all_reduce = _ar
+
+    def partials(self, store: HBMExpertStore, layer: int, x: torch.Tensor, topk_idx: torch.Tensor,
+                 topk_w: torch.Tensor, dup_mode: int, use_shared: bool = True,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """This rank's f32 partial sums [2, T, D] for normed rows x, summed over
+        the group on return."""
+        idx = localize(topk_idx, store.expert_offset, store.E_local)
+        buf = ops.moe_ffn_partials(store.desc(layer), store.dims, x, idx, topk_w, use_shared=use_shared,
+                                   dup_mode=dup_mode, out=out)
+        self.all_reduce(buf)
+        return buf
+
+    def moe(self, store: HBMExpertStore, layer: int, x: torch.Tensor, topk_idx: torch.Tensor,
+            topk_w: torch.Tensor, dup_mode: int, use_shared: bool = True) -> torch.Tensor:
+        """The layer's MoE output [T, D] bf16 (same on every rank)."""
+        buf = self.partials(store, layer, x, topk_idx, topk_w, dup_mode, use_shared)
+        return ops.moe_combine(buf, use_shared=use_shared and store.I_sh > 0)
+
+
+def shard_store(full: HBMExpertStore, rank: int, world: int, device=None) -> HBMExpertStore:
+    """Rank `rank`'s slice of a full store: its routed experts, its rows of the
+    shared expert, and the replicated router (for tests and for loading one
+    set of weights onto an expert-parallel group)."""
+    from .layout import untile_rows
+    dev = torch.device(device) if device is not None else full.device
+    off, held = expert_range(full.E, rank, world)
+    lo, hi = shared_slice(full.I_sh, rank, world) if full.I_sh else (0, 0)
+    hash_layers = sum(1 for lw in full.layers if lw.tid2eid is not None)
+    vocab = full.layers[0].tid2eid.shape[0] if hash_layers else 129280
+    out = HBMExpertStore(full.num_layers, full.E, full.D, full.I, hi - lo if full.I_sh else None, device=dev,
+                         with_router=full.layers[0].gate is not None, hash_layers=hash_layers, vocab_size=vocab,
+                         top_k=full.K, expert_offset=off, experts_held=held)
+    for l, (src, dst) in enumerate(zip(full.layers, out.layers)):
+        s0 = full._local(off)
+        for t_src, t_dst in ((src.w13, dst.w13), (src.s13, dst.s13), (src.w2, dst.w2), (src.s2, dst.s2)):
+            t_dst.copy_(t_src[s0:s0 + held])
+        if full.I_sh:
+            # rows lo..hi of w1 / w3 (row tiles lo/128..), the same columns of w2
+            w13 = untile_rows(src.sh_w13[:, :, 0]), untile_rows(src.sh_w13[:, :, 1])
+            s13 = src.sh_s13[..., 0]                        # [I_sh/128][D/128][2] block scales
+            w2 = untile_rows(src.sh_w2)                      # [D][I_sh]
+            s2 = src.sh_s2[..., 0]                          # [D/128][I_sh/128]
+            out.set_shared(l, torch.stack([w13[0][lo:hi], w13[1][lo:hi]]),
+                           s13[lo // 128:hi // 128].permute(2, 0, 1), w2[:, lo:hi].contiguous(),
+                           s2[:, lo // 128:hi // 128])
+        if src.gate is not None:
+            dst.gate.copy_(src.gate)
+            if src.bias is not None:
+                dst.bias.copy_(src.bias)
+            else:
+                dst.bias = None
+        if src.tid2eid is not None:
+            dst.tid2eid.copy_(src.tid2eid)
+        dst.desc = None
+    return out

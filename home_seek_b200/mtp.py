@@ -22,13 +22,16 @@ synchronisation and is captured as a single CUDA graph.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Optional
+from typing import TYPE_CHECKING, Optional
 
 import torch
 
 from . import ops
 from ._lib import HS_DUP_LAST, HS_DUP_SUM
 from .expert_store import HBMExpertStore
+
+if TYPE_CHECKING:
+    from .ep import ExpertParallel
 
 
 @dataclass
@@ -53,12 +56,23 @@ class MoEPathModel:
     """Random-init weights of the full model shape on one GPU (layers 0..L-1 plus
     the MTP layer at index L in the same expert store)."""
 
-    def __init__(self, shape: ModelShape, device: str | torch.device = "cuda", seed: int = 0):
+    def __init__(self, shape: ModelShape, device: str | torch.device = "cuda", seed: int = 0,
+                 ep: Optional["ExpertParallel"] = None):
+        """ep: expert parallelism (ep.py): this rank holds its block of routed
+        experts and its rows of the shared expert; everything else (router,
+        embeddings, norms, lm_head) is replicated and identical on every rank."""
         self.shape = s = shape
         self.device = dev = torch.device(device)
-        self.store = HBMExpertStore(s.num_layers + 1, s.num_experts, s.hidden, s.inter, s.shared_inter, device=dev,
+        self.ep = ep
+        off, held, sh = 0, None, s.shared_inter
+        if ep is not None:
+            from .ep import expert_range, shared_slice
+            off, held = expert_range(s.num_experts, ep.rank, ep.world)
+            lo, hi = shared_slice(s.shared_inter, ep.rank, ep.world)
+            sh = hi - lo
+        self.store = HBMExpertStore(s.num_layers + 1, s.num_experts, s.hidden, s.inter, sh, device=dev,
                                     with_router=True, hash_layers=s.hash_layers, vocab_size=s.vocab,
-                                    top_k=s.top_k)
+                                    top_k=s.top_k, expert_offset=off, experts_held=held)
         self.store.fill_random(seed)
         g = torch.Generator(device=dev)
         g.manual_seed(seed + 17)
@@ -89,7 +103,21 @@ class MoEPathModel:
         # T=1 decode follows the reference's M=1 path (duplicates summed,
         # engine.py:1388-1393); T>1 follows _forward_legacy (last weight wins)
         dup = HS_DUP_SUM if x.shape[0] == 1 else HS_DUP_LAST
+        if self.ep is not None:  # f32 partial sums, already summed over the ranks
+            return self.ep.partials(self.store, layer, x, idx, w, dup)
         return ops.moe_ffn(self.store.desc(layer), self.store.dims, x, idx, w, use_shared=True, dup_mode=dup)
+
+    def _add_norm(self, h: torch.Tensor, y: torch.Tensor, w: torch.Tensor, in_place: bool,
+                  x_out: Optional[torch.Tensor] = None):
+        """Residual add of the MoE output y (bf16, or [2, T, D] f32 partials under
+        expert parallelism) fused with the next norm (h updated in place when
+        in_place; the norm written into x_out when given)."""
+        kw = {"h_out": h} if in_place else {}
+        if x_out is not None:
+            kw["x_out"] = x_out
+        if self.ep is not None:
+            return ops.moe_combine_add_rms_norm(y, h, w, **kw)
+        return ops.add_rms_norm(h, y, w, **kw)
 
     def forward(self, ids: torch.Tensor):
         """All layers for tokens `ids`: returns (h, x) with h the residual stream
@@ -101,7 +129,7 @@ class MoEPathModel:
         for layer in range(L):
             y = self.moe(x, layer, ids)
             w_next = self.ln_w[layer + 1] if layer + 1 < L else self.norm_w
-            h, x = ops.add_rms_norm(h, y, w_next, h_out=h, x_out=x)
+            h, x = self._add_norm(h, y, w_next, in_place=True, x_out=x)
         return h, x
 
     def logits(self, x_normed: torch.Tensor) -> torch.Tensor:
@@ -119,7 +147,7 @@ class MoEPathModel:
             e = ops.rms_norm(self.embed[t], self.enorm_w) @ self.e_proj.t()
             hc = ops.rms_norm(prev, self.hnorm_w) @ self.h_proj.t() + e
             y = self.moe(ops.rms_norm(hc, self.ln_w[L]), L, t)
-            hm, xm = ops.add_rms_norm(hc, y, self.mtp_norm_w)
+            hm, xm = self._add_norm(hc, y, self.mtp_norm_w, in_place=False)
             lg = xm @ self.lm_head.t()
             _, t = ops.accept_greedy(lg.view(1, 1, -1), torch.empty(1, 0, dtype=torch.int64, device=lg.device))
             out.append(t)

@@ -20,7 +20,8 @@ _status: dict = {}
 launches = 0
 _KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_moe_permute": 2,
             "hs_moe_unpermute": 1, "hs_accept_greedy": 1, "hs_accept_rejection": 1, "hs_fill_bytes": 1,
-            "hs_rms_norm": 1, "hs_add_rms_norm": 1}
+            "hs_rms_norm": 1, "hs_add_rms_norm": 1, "hs_moe_ffn_fp4_partials": 3, "hs_moe_combine": 1,
+            "hs_moe_combine_add_rms_norm": 1}
 
 
 def _launch(name: str, *args, extra: int = 0) -> None:
@@ -166,6 +167,69 @@ def moe_ffn(desc: ctypes.Array, dims: tuple, hidden: torch.Tensor, topk_idx: tor
     return out
 
 
+def moe_ffn_partials(desc: ctypes.Array, dims: tuple, hidden: torch.Tensor, topk_idx: torch.Tensor,
+                     topk_w: torch.Tensor, use_shared: bool = True, dup_mode: int = _lib.HS_DUP_LAST,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The un-rounded f32 sums of one expert-parallel rank: returns [2, T, D] f32
+    (routed over this store's experts, shared over its slice of the shared
+    expert; ids outside the store must already be -1). Sum over ranks, then
+    moe_combine / moe_combine_add_rms_norm."""
+    dev = _check_cuda(hidden, topk_idx, topk_w, out)
+    if hidden.dtype != torch.bfloat16:
+        raise TypeError("hidden must be bf16")
+    topk_idx = topk_idx.to(torch.int64).contiguous()
+    topk_w = topk_w.to(torch.float32).contiguous()
+    T, D = hidden.shape
+    K = topk_idx.shape[-1]
+    E, Dd, I, I_sh = dims
+    if D != Dd:
+        raise ValueError(f"hidden dim {D} != store dim {Dd}")
+    if out is None:
+        out = torch.empty(2, T, D, dtype=torch.float32, device=dev)
+    if tuple(out.shape) != (2, T, D) or out.dtype != torch.float32:
+        raise ValueError("out must be [2, T, D] float32")
+    use_shared = bool(use_shared) and bool(I_sh)
+    if not use_shared:
+        out[1].zero_()
+    lib = _lib.load()
+    nb = lib.hs_moe_workspace_size(T, K, D, I, I_sh)
+    ws = workspace(dev, nb, "moe")
+    _launch("hs_moe_ffn_fp4_partials", ctypes.addressof(desc), hidden.data_ptr(), topk_idx.data_ptr(),
+            topk_w.data_ptr(), T, K, int(use_shared), int(dup_mode), out[0].data_ptr(),
+            out[1].data_ptr() if use_shared else None, ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(),
+            _stream(dev), extra=0 if T * K <= 4096 else 1)
+    return out
+
+
+def moe_combine(partials: torch.Tensor, use_shared: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16(bf16(routed) + bf16(shared)) from summed f32 partials [2, T, D]."""
+    dev = _check_cuda(partials, out)
+    _, T, D = partials.shape
+    if out is None:
+        out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    _launch("hs_moe_combine", partials[0].data_ptr(), partials[1].data_ptr(), int(bool(use_shared)), T, D,
+            out.data_ptr(), _stream(dev))
+    return out
+
+
+def moe_combine_add_rms_norm(partials: torch.Tensor, h: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
+                             use_shared: bool = True, h_out: Optional[torch.Tensor] = None,
+                             x_out: Optional[torch.Tensor] = None):
+    """Combine f32 partials [2, T, D], add to the residual stream h and normalise:
+    returns (h + combine, rms_norm(h + combine, w)). h_out may be h."""
+    dev = _check_cuda(partials, h, w, h_out, x_out)
+    h = _rows(h, "h")
+    w = _rows(w, "w")
+    _, T, D = partials.shape
+    if h_out is None:
+        h_out = torch.empty_like(h)
+    if x_out is None:
+        x_out = torch.empty_like(h)
+    _launch("hs_moe_combine_add_rms_norm", partials[0].data_ptr(), partials[1].data_ptr(), int(bool(use_shared)),
+            h.data_ptr(), w.data_ptr(), float(eps), T, D, h_out.data_ptr(), x_out.data_ptr(), _stream(dev))
+    return h_out, x_out
+
+
 def moe_permute(topk_idx: torch.Tensor, num_experts: int, x: Optional[torch.Tensor] = None):
     """Expert-major permutation (expand_to_fused, tests/_reference.py:108-121).
 
@@ -286,5 +350,6 @@ def fill_bytes(t: torch.Tensor, seed: int, lo: int = 0, hi: int = 255) -> torch.
 
 
 __all__ = ["HsError", "router_topk", "hash_route", "make_moe_desc", "moe_ffn", "moe_permute", "moe_unpermute",
-           "accept_greedy", "accept_rejection", "fill_bytes", "rms_norm", "add_rms_norm", "check_status",
+           "accept_greedy", "accept_rejection", "fill_bytes", "rms_norm", "add_rms_norm", "moe_ffn_partials",
+           "moe_combine", "moe_combine_add_rms_norm", "check_status",
            "status_word", "workspace"]

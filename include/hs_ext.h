@@ -237,6 +237,36 @@ int hs_add_rms_norm(const void* h, const void* y, const void* w, float eps,
                     void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Expert parallelism: partial sums and their combine.                        */
+/* The reference splits the experts of a layer across GPUs, runs every GPU    */
+/* on all tokens and adds the outputs (engine.py:1575-1709 _forward_ffn_ep,   */
+/* parallel.py:203-290 _EPWorker). Here each rank runs                        */
+/* hs_moe_ffn_fp4_partials on its experts (ids outside them set to -1) and    */
+/* its slice of the shared expert's intermediate dimension, writing the       */
+/* UN-ROUNDED f32 sums routed_f32 [T][D] and shared_f32 [T][D]; the caller    */
+/* sums those over ranks (one NCCL all-reduce) and hs_moe_combine rounds them */
+/* exactly as the single-GPU call does: out = bf16(bf16(routed) +             */
+/* bf16(shared)). hs_moe_combine_add_rms_norm fuses the combine with the      */
+/* layer's residual add and the next norm (as hs_add_rms_norm).               */
+/* shared_f32 is required when use_shared (and the descriptor has a shared    */
+/* expert); pointers 16-byte aligned.                                         */
+/* ------------------------------------------------------------------------ */
+int hs_moe_ffn_fp4_partials(const void* desc, const void* hidden,
+                            const int64_t* topk_idx, const float* topk_w,
+                            int64_t T, int64_t top_k, int use_shared,
+                            int dup_mode, float* routed_f32, float* shared_f32,
+                            void* workspace, size_t workspace_bytes,
+                            int32_t* dev_status, void* stream);
+int hs_moe_combine(const float* routed_f32, const float* shared_f32,
+                   int use_shared, int64_t T, int64_t D, void* out,
+                   void* stream);
+int hs_moe_combine_add_rms_norm(const float* routed_f32,
+                                const float* shared_f32, int use_shared,
+                                const void* h, const void* w, float eps,
+                                int64_t T, int64_t D, void* h_out, void* x_out,
+                                void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Synthetic weight fill (device-side, counter-based hash; no allocation).    */
 /* Fills n bytes at dst with lo + (hash(seed, i) % (hi - lo + 1)). Used to    */
 /* build random-init expert stores of the full model shape in seconds.        */

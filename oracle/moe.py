@@ -123,6 +123,30 @@ def shared_expert(hidden: torch.Tensor, sh: tuple) -> torch.Tensor:
     return _ffn_cat(hidden, w1, w3, w2b)
 
 
+def shared_expert_f32(hidden: torch.Tensor, sh: tuple) -> torch.Tensor:
+    """The shared expert's output before its bf16 rounding (f32), for the
+    expert-parallel combine: a slice of its intermediate rows gives a partial
+    sum, and the slices' sum is the full output."""
+    w13, s13, w2, s2 = sh
+    w1 = dequant_fp8_block(w13[0], s13[0])
+    w3 = dequant_fp8_block(w13[1], s13[1])
+    w2b = dequant_fp8_block(w2, s2)
+    gate = hidden @ w1.T
+    up = hidden @ w3.T
+    g = gate.float().clamp(max=SWIGLU_LIMIT)
+    u = up.float().clamp(min=-SWIGLU_LIMIT, max=SWIGLU_LIMIT)
+    act = (g * g.sigmoid() * u).to(torch.bfloat16)
+    return act.float() @ w2b.float().T
+
+
+def ep_combine(routed_f32: torch.Tensor, shared_f32: Optional[torch.Tensor]) -> torch.Tensor:
+    """engine.py:1530-1536 applied to f32 sums: bf16(bf16(routed) + bf16(shared))."""
+    out = routed_f32.to(torch.bfloat16)
+    if shared_f32 is not None:
+        out = out + shared_f32.to(torch.bfloat16)
+    return out
+
+
 def moe_layer(hidden, topk_idx, topk_w, load_fp4, sh=None, dup_mode="last"):
     """engine.py:1480-1536: routed output (bf16) + shared output (bf16), bf16 add."""
     out = moe_routed(hidden, topk_idx, topk_w, load_fp4, dup_mode)

@@ -1,0 +1,85 @@
+"""Expert parallelism on the CPU with two gloo ranks: the expert / shared-row
+split (ep.expert_range, ep.shared_slice), id localisation (ep.localize) and the
+group plumbing (ExpertParallel.all_reduce over torch.distributed) reproduce the
+single-process layer. Each rank's partial sums come from the oracle (the CUDA
+kernels need a GPU; tests/test_gpu_ep.py checks them), summed over the two
+ranks, combined, and compared with oracle.moe.moe_layer on the full weights."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import inputs as I
+from oracle import moe as O
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, T: int, out_q) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from home_seek_b200.ep import ExpertParallel, expert_range, localize, shared_slice
+        shape = I.SMALL
+        load = I.make_loader(shape)
+        gate, bias = I.router_weights(shape.E, shape.D, seed=1)
+        sh = I.shared_fp8(shape.D, shape.I_sh, seed=2)
+        h = I.hidden(T, shape.D, seed=3 + T)
+        idx, w = O.router(h, gate, bias)                       # identical on every rank
+        off, held = expert_range(shape.E, rank, world)
+        lo, hi = shared_slice(shape.I_sh, rank, world)
+        loc = localize(idx, off, held)
+        # this rank's partials: its experts (local ids -> global for the loader)
+        routed = O.moe_routed_f32(h, torch.where(loc >= 0, loc + off, loc), w, load)
+        w13, s13, w2, s2 = sh
+        shared = O.shared_expert_f32(h, (w13[:, lo:hi], s13[:, lo // 128:hi // 128], w2[:, lo:hi],
+                                         s2[:, lo // 128:hi // 128]))
+        buf = torch.stack([routed, shared]).contiguous()
+        ExpertParallel(rank, world).all_reduce(buf)
+        out = O.ep_combine(buf[0], buf[1])
+        ref = O.moe_layer(h, idx, w, load, sh)
+        out_q.put((rank, out.float().numpy(), ref.float().numpy(), int((loc >= 0).sum())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_two_rank_expert_parallel_layer_matches_single_process(T):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, T, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    res.sort()
+    (_, out0, ref, n0), (_, out1, _, n1) = res
+    assert n0 + n1 == T * 6                 # every routed pair lands on exactly one rank
+    assert np.array_equal(out0, out1)       # the group agrees
+    rel = float(np.abs(out0 - ref).max() / max(np.abs(ref).max(), 1e-30))
+    assert rel <= 1e-2, rel
+
+
+def test_expert_and_shared_splits():
+    from home_seek_b200.ep import expert_range, localize, shared_slice
+    assert [expert_range(256, r, 8) for r in (0, 7)] == [(0, 32), (224, 32)]
+    assert shared_slice(2048, 3, 8) == (768, 1024)
+    with pytest.raises(ValueError):
+        shared_slice(2048, 0, 16)           # 128-row slices: below the kernels' 256-row granularity
+    idx = torch.tensor([[0, 31, 32, 255, -1, 64]])
+    assert localize(idx, 32, 32).tolist() == [[-1, -1, 0, -1, -1, -1]]
+    assert localize(idx, 0, 32).tolist() == [[0, 31, -1, -1, -1, -1]]

@@ -1,0 +1,117 @@
+"""Expert parallelism on the GPU. On one GPU the group is emulated: the full
+store is split with ep.shard_store, each shard's hs_moe_ffn_fp4_partials runs
+on its localised ids, the shards' f32 partials are added (what the all-reduce
+does) and hs_moe_combine must give the single-call output. With two or more
+GPUs the same check runs over a real NCCL group (one process per GPU)."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+from oracle import inputs as I
+
+pytestmark = pytest.mark.gpu
+
+MOE_TOL = 1e-2
+
+
+def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp(min=1e-30))
+
+
+def _full_store(device="cuda"):
+    from home_seek_b200.expert_store import HBMExpertStore
+    shape = I.SMALL
+    st = HBMExpertStore(1, shape.E, shape.D, shape.I, shape.I_sh, device=device, with_router=False)
+    load = I.make_loader(shape)
+    for e in range(shape.E):
+        st.set_expert(0, e, *load(e))
+    st.set_shared(0, *I.shared_fp8(shape.D, shape.I_sh, seed=2))
+    return st
+
+
+@pytest.mark.parametrize("T", [1, 3, 24])
+def test_emulated_two_rank_partials_combine_to_the_single_call(T):
+    from home_seek_b200 import ops
+    from home_seek_b200.ep import localize, shard_store
+    shape = I.SMALL
+    full = _full_store()
+    gate, bias = I.router_weights(shape.E, shape.D, seed=1)
+    h = I.hidden(T, shape.D, seed=5 + T).cuda()
+    idx, w = ops.router_topk(h, gate.cuda(), bias.cuda(), shape.K, 1.5)
+    dup = 1 if T == 1 else 0
+    ref = ops.moe_ffn(full.desc(0), full.dims, h, idx, w, use_shared=True, dup_mode=dup)
+    ref_f32 = torch.empty(T, shape.D, dtype=torch.float32, device="cuda")
+    ops.moe_ffn(full.desc(0), full.dims, h, idx, w, use_shared=False, dup_mode=dup, out_f32=ref_f32)
+    total = torch.zeros(2, T, shape.D, dtype=torch.float32, device="cuda")
+    for r in range(2):
+        sh = shard_store(full, r, 2)
+        part = ops.moe_ffn_partials(sh.desc(0), sh.dims, h, localize(idx, sh.expert_offset, sh.E_local), w,
+                                    use_shared=True, dup_mode=dup)
+        total += part
+    out = ops.moe_combine(total)
+    assert ops.check_status(torch.device("cuda")) == 0
+    assert _rel(out, ref) <= MOE_TOL, _rel(out, ref)
+    assert _rel(total[0], ref_f32) <= 1e-3, _rel(total[0], ref_f32)   # routed f32 sums, before rounding
+    # fused combine + residual add + norm equals the two-step form
+    from oracle import mtp as OM
+    res = torch.randn(T, shape.D, device="cuda").to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(shape.D, device="cuda")).to(torch.bfloat16)
+    h2, x2 = ops.moe_combine_add_rms_norm(total, res, nw)
+    h3, x3 = ops.add_rms_norm(res, out, nw)
+    assert torch.equal(h2, h3) and torch.equal(x2, x3)
+    assert _rel(x2, OM.rms_norm((res.cpu() + out.cpu()), nw.cpu())) <= 2e-2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank: int, world: int, port: int, q) -> None:
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from home_seek_b200 import ops
+        from home_seek_b200.ep import ExpertParallel, shard_store
+        shape = I.SMALL
+        full = _full_store(dev)
+        gate, bias = I.router_weights(shape.E, shape.D, seed=1)
+        h = I.hidden(3, shape.D, seed=9).to(dev)
+        idx, w = ops.router_topk(h, gate.to(dev), bias.to(dev), shape.K, 1.5)
+        ref = ops.moe_ffn(full.desc(0), full.dims, h, idx, w, use_shared=True)
+        ep = ExpertParallel(rank, world)
+        out = ep.moe(shard_store(full, rank, world), 0, h, idx, w, 0)
+        torch.cuda.synchronize()
+        q.put((rank, _rel(out, ref)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_expert_parallel_matches_single_gpu():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, rel in res:
+        assert rel <= MOE_TOL, (rank, rel)
