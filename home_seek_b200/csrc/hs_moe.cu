@@ -1383,7 +1383,7 @@ __device__ __forceinline__ TokSched make_tok_sched(const Desc& d, const UnitArgs
   s.U = d.D / kM;
   s.nsh = a.use_shared ? d.I_sh / 256 : 0;
   s.nrt = d.I / 256;
-  s.C = a.P.hdr[0];
+  s.C = __ldcg(a.P.hdr);
   s.Su = s.nsh + s.C * s.nrt;
   s.Wu = 2 * s.nsh + static_cast<int64_t>(s.C) * s.nrt;
   s.W = s.Wu * s.U;
@@ -1438,56 +1438,142 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     prefetch_tensormap(&d.tm_sw2);
     prefetch_tensormap(&cm.tm_act8);
   }
-  pdl_wait();  // the gate/up phase (and the plan before it) is complete
-  pdl_trigger();
   tc5::fence_before_sync();
   __syncthreads();
   tc5::fence_after_sync();
   const uint32_t tmem = bars->tmem;
+  // The plan is complete before this grid starts (every gate/up CTA waited for
+  // it before letting this grid launch), so the schedule and the chunk table
+  // are read now, through L2, and the first stages' weights start streaming
+  // while the gate/up phase finishes; only the activation loads wait.
   const TokSched sc = make_tok_sched(d, a);
   const bool any = sc.W > 0;
   const int64_t s_begin = any ? sc.lo(c) : 0, s_end = any ? sc.lo(c + 1) : 0;
+  const int64_t npre = min64(static_cast<int64_t>(S_), s_end - s_begin);
 
+  // producer state (warp 4): chunk table in registers, lane j keeps chunks j,
+  // j+32, j+64, j+96 (expert id and the 8 per-token B-scale bytes as two words)
+  static_assert(kTokChunks <= 4 * 32, "token-mode chunk table");
+  uint64_t pol = 0;
+  int ex[4];
+  uint32_t sw0[4], sw1[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    ex[i] = 0;
+    sw0[i] = sw1[i] = 0x7f7f7f7fu;
+  }
   if (warp == 4) {
-    // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
-    // chunk table in registers: lane j keeps chunks j, j+32, j+64, j+96 (expert
-    // id and the 8 per-token B-scale bytes as two words)
-    static_assert(kTokChunks <= 4 * 32, "token-mode chunk table");
-    const uint64_t pol = l2_evict_first_policy();
-    int ex[4];
-    uint32_t sw0[4], sw1[4];
+    pol = l2_evict_first_policy();
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int cc = lane + 32 * i;
-      ex[i] = 0;
-      sw0[i] = sw1[i] = 0x7f7f7f7fu;
       if (cc < sc.C) {
-        ex[i] = a.P.chunk_expert[cc];
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(a.P.ctab_sb + cc * 8);
-        sw0[i] = w[0];
-        sw1[i] = w[1];
+        ex[i] = __ldcg(a.P.chunk_expert + cc);
+        const uint2 w = __ldcg(reinterpret_cast<const uint2*>(a.P.ctab_sb + cc * 8));
+        sw0[i] = w.x;
+        sw1[i] = w.y;
       }
     }
-    int64_t step = 0;
-    for (int64_t s = s_begin; s < s_end; ++s, ++step) {
-      const int64_t u = sc.unit_of(s);
-      const int k = static_cast<int>(s - u * sc.Su);
-      const bool shared = k < sc.nsh;
-      const int kr = k - sc.nsh;
-      const int ch = shared ? 0 : kr / sc.nrt;
-      const int kk = shared ? k : kr - ch * sc.nrt;
-      int e_sel = 0;
-      uint32_t w0 = 0, w1 = 0;
+  }
+  // step s -> (tile, shared?, chunk, k within the expert, expert, B-scale words)
+  struct Step {
+    int tile, ch, kk, e;
+    bool shared;
+    uint32_t w0, w1;
+  };
+  auto decode = [&](int64_t s) {
+    Step r;
+    const int64_t u = sc.unit_of(s);
+    const int k = static_cast<int>(s - u * sc.Su);
+    r.tile = static_cast<int>(u);
+    r.shared = k < sc.nsh;
+    const int kr = k - sc.nsh;
+    r.ch = r.shared ? 0 : kr / sc.nrt;
+    r.kk = r.shared ? k : kr - r.ch * sc.nrt;
+    int e_sel = 0;
+    uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (i == (ch >> 5)) {
-          e_sel = ex[i];
-          w0 = sw0[i];
-          w1 = sw1[i];
-        }
-      const int e = __shfl_sync(0xffffffffu, e_sel, ch & 31);
-      w0 = __shfl_sync(0xffffffffu, w0, ch & 31);
-      w1 = __shfl_sync(0xffffffffu, w1, ch & 31);
+    for (int i = 0; i < 4; ++i)
+      if (i == (r.ch >> 5)) {
+        e_sel = ex[i];
+        w0 = sw0[i];
+        w1 = sw1[i];
+      }
+    r.e = __shfl_sync(0xffffffffu, e_sel, r.ch & 31);
+    r.w0 = __shfl_sync(0xffffffffu, w0, r.ch & 31);
+    r.w1 = __shfl_sync(0xffffffffu, w1, r.ch & 31);
+    return r;
+  };
+  // whole warp: this step's B scale atom; word (m0, m1) = scale of B row
+  // n = m0 + 32*m1; rows 0..7 are the tokens' hi rows, 8..15 their lo rows
+  auto write_atom = [&](uint8_t* SF, const Step& q) {
+    for (int wi = lane; wi < 128; wi += 32) {
+      const int m0 = wi >> 2, m1 = wi & 3;
+      const int n = m0 + 32 * m1;
+      uint32_t b = 127u;
+      if (n < N && !q.shared) {
+        const int t = n & 7;
+        b = ((t < 4 ? q.w0 : q.w1) >> (8 * (t & 3))) & 0xffu;
+      }
+      *reinterpret_cast<uint32_t*>(SF + 1024 + m0 * 16 + m1 * 4) = b * 0x01010101u;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+  };
+  // lane 0: weights and their scale atoms (independent of the gate/up phase)
+  auto issue_weights = [&](int st, const Step& q) {
+    uint8_t* S = base + st * L::kStage;
+    uint8_t* SF = S + L::kA + L::kB;
+    int64_t ya;
+    const uint8_t* sfp;
+    if (q.shared) {
+      ya = (static_cast<int64_t>(q.tile) * (d.I_sh / kM) + 2 * q.kk) * kM;
+      sfp = d.sh_s2a + (static_cast<int64_t>(q.tile) * (d.I_sh / kM) + 2 * q.kk) * 512;
+    } else {
+      ya = ((static_cast<int64_t>(q.e) * (D / kM) + q.tile) * (d.I / kM) + 2 * q.kk) * kM;
+      sfp = d.s2a + ((static_cast<int64_t>(q.e) * (D / kM) + q.tile) * (d.I / kM) + 2 * q.kk) * 512;
+    }
+    tma_load_2d_hint(S, q.shared ? &d.tm_sw2 : &d.tm_w2, &bars->full[st], 0, static_cast<int>(ya), pol);
+    bulk_load_hint(SF, sfp, 1024, &bars->full[st], pol);
+  };
+  // lane 0: the activation rows (written by the gate/up phase)
+  auto issue_act = [&](int st, const Step& q) {
+    uint8_t* Bs = base + st * L::kStage + L::kA;
+    const int brow = (q.shared ? 0 : 1 + q.ch) * 8;
+    for (int b = 0; b < 2; ++b)
+      tma_load_3d(Bs + b * 2048, &cm.tm_act8, &bars->full[st], q.kk * 256 + b * 128, brow, 0);
+  };
+  auto tx_of = [&](const Step& q) {
+    return static_cast<uint32_t>((q.shared ? 2 * kBoxBytes : kBoxBytes) + L::kB + 1024);
+  };
+
+  if (warp == 4) {
+    for (int64_t step = 0; step < npre; ++step) {  // stages are free: no empty waits yet
+      const Step q = decode(s_begin + step);
+      const int st = static_cast<int>(step);
+      write_atom(base + st * L::kStage + L::kA + L::kB, q);
+      if (lane == 0) {
+        mbar_expect_tx(&bars->full[st], tx_of(q));  // bytes now, the arrival after the activations
+        issue_weights(st, q);
+      }
+    }
+  }
+  pdl_wait();  // the gate/up phase's activations are complete
+  pdl_trigger();
+
+  if (warp == 4) {
+    // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
+    int64_t step = 0;
+    for (; step < npre; ++step) {
+      const Step q = decode(s_begin + step);
+      if (lane == 0) {
+        issue_act(static_cast<int>(step), q);
+        mbar_arrive(&bars->full[step]);
+      }
+      __syncwarp();
+    }
+    for (int64_t s = s_begin + npre; s < s_end; ++s, ++step) {
+      const Step q = decode(s);
       const int st = static_cast<int>(step % S_);
       if (step >= S_) {
         bool w = true;
@@ -1498,42 +1584,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
           break;
         }
       }
-      uint8_t* S = base + st * L::kStage;
-      uint8_t* Bs = S + L::kA;
-      uint8_t* SF = Bs + L::kB;
-      // this step's B scale atom: word (m0, m1) = scale of B row n = m0 + 32*m1;
-      // rows 0..7 are the tokens' hi rows, 8..15 their lo rows
-      for (int wi = lane; wi < 128; wi += 32) {
-        const int m0 = wi >> 2, m1 = wi & 3;
-        const int n = m0 + 32 * m1;
-        uint32_t b = 127u;
-        if (n < N && !shared) {
-          const int t = n & 7;
-          b = ((t < 4 ? w0 : w1) >> (8 * (t & 3))) & 0xffu;
-        }
-        *reinterpret_cast<uint32_t*>(SF + 1024 + m0 * 16 + m1 * 4) = b * 0x01010101u;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
+      write_atom(base + st * L::kStage + L::kA + L::kB, q);
       if (lane == 0) {
-        const int tile = static_cast<int>(u);
-        const uint32_t tx = (shared ? 2 * kBoxBytes : kBoxBytes) + L::kB + 1024;
-        mbar_arrive_expect_tx(&bars->full[st], tx);
-        int64_t ya;
-        const uint8_t* sfp;
-        if (shared) {
-          ya = (static_cast<int64_t>(tile) * (d.I_sh / kM) + 2 * kk) * kM;
-          sfp = d.sh_s2a + (static_cast<int64_t>(tile) * (d.I_sh / kM) + 2 * kk) * 512;
-        } else {
-          ya = ((static_cast<int64_t>(e) * (D / kM) + tile) * (d.I / kM) + 2 * kk) * kM;
-          sfp = d.s2a + ((static_cast<int64_t>(e) * (D / kM) + tile) * (d.I / kM) + 2 * kk) * 512;
-        }
-        tma_load_2d_hint(S, shared ? &d.tm_sw2 : &d.tm_w2, &bars->full[st], 0, static_cast<int>(ya), pol);
-        const int brow = (shared ? 0 : 1 + ch) * 8;
-        for (int b = 0; b < 2; ++b)
-          tma_load_3d(Bs + b * 2048, &cm.tm_act8, &bars->full[st], kk * 256 + b * 128, brow, 0);
-        bulk_load_hint(SF, sfp, 1024, &bars->full[st], pol);
+        mbar_arrive_expect_tx(&bars->full[st], tx_of(q));
+        issue_weights(st, q);
+        issue_act(st, q);
       }
+      __syncwarp();
     }
     if (lane == 0) bars->issued = static_cast<int32_t>(step);
   } else if (warp == 5) {
