@@ -43,10 +43,13 @@
 #include <atomic>
 #include <mutex>
 
+#include <cooperative_groups.h>
 #include <cuda_fp8.h>
 
 #include "hs_common.cuh"
 #include "hs_tcgen05.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace hs {
 namespace moe {
@@ -1004,7 +1007,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   constexpr uint32_t kSfb = 224;
   constexpr int NP = 8 * NT;                        // pairs per unit (hi and lo columns summed)
   constexpr int kSlot = (kDown ? 1 : 2) * kM * NP;  // floats per partial slot
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  extern __shared__ uint8_t smem_raw[];  // 1024-aligned at offset 0 (checked below)
   // the 128B-swizzled stages need a 1024-aligned base; no slack is reserved
   // for realignment (two CTAs per SM leave none), so check it
   if (smem_u32(smem_raw) & 1023u) {
@@ -1391,6 +1394,11 @@ __device__ __forceinline__ TokSched make_tok_sched(const Desc& d, const UnitArgs
   return s;
 }
 
+// kCl = false: stream-K over all tiles (one CTA per SM slot). kCl = true: one
+// 8-CTA thread-block cluster per 128-row tile of D; the tile's k-steps are cut
+// into 8 equal-weight slices and the 8 partial accumulators are summed through
+// distributed shared memory (no partial slots in global memory, no tickets).
+template <bool kCl>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __grid_constant__ Desc d,
                                                                         const __grid_constant__ CallMaps cm,
                                                                         UnitArgs a) {
@@ -1406,7 +1414,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   constexpr uint32_t kSfa = 192;
   constexpr uint32_t kSfb = 224;
   constexpr int kSlot = 2 * kM * 8;  // routed and shared sums of 8 tokens
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  extern __shared__ uint8_t smem_raw[];  // 1024-aligned at offset 0 (checked below)
   if (smem_u32(smem_raw) & 1023u) {
     pdl_wait();
     if (threadIdx.x == 0) report(a.status, HS_DEV_SMEM_ALIGN);
@@ -1448,32 +1456,43 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   // while the gate/up phase finishes; only the activation loads wait.
   const TokSched sc = make_tok_sched(d, a);
   const bool any = sc.W > 0;
-  const int64_t s_begin = any ? sc.lo(c) : 0, s_end = any ? sc.lo(c + 1) : 0;
+  int64_t s_begin = 0, s_end = 0;
+  if (any) {
+    if constexpr (kCl) {
+      // cluster u = tile u; rank j takes the weight slice [Wu j/8, Wu (j+1)/8)
+      const int64_t u = c / 8, j = c % 8;
+      auto kb = [&](int64_t jj) {
+        const int64_t w = TokSched::udiv(sc.Wu * jj, 8);
+        return w <= 2 * sc.nsh ? (w + 1) / 2 : sc.nsh + (w - 2 * sc.nsh);
+      };
+      s_begin = u * sc.Su + kb(j);
+      s_end = u * sc.Su + kb(j + 1);
+    } else {
+      s_begin = sc.lo(c);
+      s_end = sc.lo(c + 1);
+    }
+  }
   const int64_t npre = min64(static_cast<int64_t>(S_), s_end - s_begin);
 
   // producer state (warp 4): chunk table in registers, lane j keeps chunks j,
   // j+32, j+64, j+96 (expert id and the 8 per-token B-scale bytes as two words)
   static_assert(kTokChunks <= 4 * 32, "token-mode chunk table");
   uint64_t pol = 0;
-  int ex[4];
-  uint32_t sw0[4], sw1[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    ex[i] = 0;
-    sw0[i] = sw1[i] = 0x7f7f7f7fu;
-  }
+  // (scalars, not arrays: the lambdas below capture them by reference)
+  int ex0 = 0, ex1 = 0, ex2 = 0, ex3 = 0;
+  uint2 sb0 = make_uint2(0x7f7f7f7fu, 0x7f7f7f7fu), sb1 = sb0, sb2 = sb0, sb3 = sb0;
   if (warp == 4) {
     pol = l2_evict_first_policy();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int cc = lane + 32 * i;
+    auto load = [&](int cc, int& e, uint2& sb) {
       if (cc < sc.C) {
-        ex[i] = __ldcg(a.P.chunk_expert + cc);
-        const uint2 w = __ldcg(reinterpret_cast<const uint2*>(a.P.ctab_sb + cc * 8));
-        sw0[i] = w.x;
-        sw1[i] = w.y;
+        e = __ldcg(a.P.chunk_expert + cc);
+        sb = __ldcg(reinterpret_cast<const uint2*>(a.P.ctab_sb + cc * 8));
       }
-    }
+    };
+    load(lane, ex0, sb0);
+    load(lane + 32, ex1, sb1);
+    load(lane + 64, ex2, sb2);
+    load(lane + 96, ex3, sb3);
   }
   // step s -> (tile, shared?, chunk, k within the expert, expert, B-scale words)
   struct Step {
@@ -1490,18 +1509,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     const int kr = k - sc.nsh;
     r.ch = r.shared ? 0 : kr / sc.nrt;
     r.kk = r.shared ? k : kr - r.ch * sc.nrt;
-    int e_sel = 0;
-    uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (i == (r.ch >> 5)) {
-        e_sel = ex[i];
-        w0 = sw0[i];
-        w1 = sw1[i];
-      }
+    const int grp = r.ch >> 5;
+    const int e_sel = grp == 0 ? ex0 : grp == 1 ? ex1 : grp == 2 ? ex2 : ex3;
+    const uint2 sb = grp == 0 ? sb0 : grp == 1 ? sb1 : grp == 2 ? sb2 : sb3;
     r.e = __shfl_sync(0xffffffffu, e_sel, r.ch & 31);
-    r.w0 = __shfl_sync(0xffffffffu, w0, r.ch & 31);
-    r.w1 = __shfl_sync(0xffffffffu, w1, r.ch & 31);
+    r.w0 = __shfl_sync(0xffffffffu, sb.x, r.ch & 31);
+    r.w1 = __shfl_sync(0xffffffffu, sb.y, r.ch & 31);
     return r;
   };
   // whole warp: this step's B scale atom; word (m0, m1) = scale of B row
@@ -1653,6 +1666,43 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
       tc5::commit(&bars->mma_done);
       if (!mbar_wait(&bars->mma_done, 0)) report(a.status, HS_DEV_TIMEOUT);
     }
+  } else if constexpr (kCl) {
+    // ---------------- epilogue, cluster mode (one segment) ----------------
+    const int row = 32 * warp + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+    float r[8], h[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) r[t] = h[t] = 0.f;
+    if (s_begin < s_end) {
+      const int64_t us = sc.ustart(sc.unit_of(s_begin));
+      const int k0 = static_cast<int>(s_begin - us), k1 = static_cast<int>(s_end - us);
+      if (mbar_wait(&bars->acc_full[0], 0)) {
+        tc5::fence_after_sync();
+        float c0[16], c1[16];
+        tc5::ld_32x32b_x16(tmem + lane_off, c0);
+        tc5::ld_32x32b_x16(tmem + lane_off + kAccSh, c1);
+        tc5::wait_ld();
+        tc5::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->acc_empty[0]);
+        const bool had_sh = k0 < sc.nsh, had_rt = k1 > sc.nsh;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          r[t] = had_rt ? c0[t] + c0[8 + t] : 0.f;
+          h[t] = had_sh ? c1[t] + c1[8 + t] : 0.f;
+        }
+      } else if (threadIdx.x == 0) {
+        report(a.status, HS_DEV_TIMEOUT);
+      }
+    }
+    // park this CTA's partial rows in stage 0 (every stage is consumed once
+    // the accumulator is complete): [routed t][row], [shared t][row]
+    float* red = reinterpret_cast<float*>(base);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      red[t * kM + row] = r[t];
+      red[(8 + t) * kM + row] = h[t];
+    }
   } else {
     // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31) ----------------
     const int row = 32 * warp + lane;
@@ -1743,6 +1793,44 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
           if (a.shared_f32) a.shared_f32[o] = 0.f;
           if (!a.partials) a.out[o] = __float2bfloat16_rn(0.f);
         }
+  }
+
+  if constexpr (kCl) {
+    // the tile's 8 partial accumulators, summed in rank order: rank j reduces
+    // rows 16j..16j+15, thread (row, token) reads its two values from all 8
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (warp < 4) {
+      const int rank = static_cast<int>(cluster.block_rank());
+      const int rl = threadIdx.x >> 3, t = threadIdx.x & 7;
+      const int rowc = rank * 16 + rl;
+      float* red = reinterpret_cast<float*>(base);
+      float vr[8], vh[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float* pr = cluster.map_shared_rank(red, q);
+        vr[q] = pr[t * kM + rowc];
+        vh[q] = pr[(8 + t) * kM + rowc];
+      }
+      float rs = 0.f, hs = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        rs += vr[q];
+        hs += vh[q];
+      }
+      if (t < a.T) {
+        const int64_t o_i = t * static_cast<int64_t>(D) + (c / 8) * kM + rowc;
+        if (a.out_f32) a.out_f32[o_i] = rs;
+        if (a.partials) {
+          if (a.shared_f32) a.shared_f32[o_i] = hs;
+        } else {
+          float o = round_bf16(rs);
+          if (a.use_shared) o += round_bf16(hs);
+          a.out[o_i] = __float2bfloat16_rn(o);
+        }
+      }
+    }
+    cluster.sync();  // peers have read this CTA's shared memory
   }
 
   tc5::fence_before_sync();
@@ -1860,6 +1948,19 @@ static int make_map_3d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t
 static bool dim_ok(int64_t v, int64_t mult, int64_t lo, int64_t hi) { return v % mult == 0 && v >= lo && v <= hi; }
 static bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
+// Number of SMs of the current device, cached.
+static int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int v = cache[dev].load();
+  if (v <= 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev].store(v);
+  }
+  return v;
+}
+
 template <bool kDown, int NT, bool kTok = false>
 static int launch_sk(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaStream_t st) {
   constexpr int bytes = SmemLayout<NT, kDown ? 2 : 1>::kBytes;
@@ -1877,18 +1978,31 @@ static int launch_sk(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaS
   return check_launch();
 }
 
-static int launch_tok_down(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaStream_t st) {
+static int launch_tok_down(const Desc& d, const CallMaps& cm, UnitArgs a, cudaStream_t st) {
   constexpr int bytes = SmemLayout<1, 2>::kBytes;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   HS_CUDA_CHECK(cudaGetDevice(&dev));
   const uint64_t bit = 1ull << (dev & 63);
   if (!(done.load() & bit)) {
-    HS_CUDA_CHECK(cudaFuncSetAttribute(tok_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    HS_CUDA_CHECK(cudaFuncSetAttribute(tok_down_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    HS_CUDA_CHECK(cudaFuncSetAttribute(tok_down_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
     done.fetch_or(bit);
   }
+  const int tiles = d.D / kM;
+  // One 8-CTA cluster per tile when all tiles' clusters fit the two-CTAs-per-SM
+  // budget (D = 4096: 32 clusters, 256 CTAs). cudaOccupancyMaxActiveClusters
+  // reports one CTA per SM for these kernels, but 32 clusters do run at once on
+  // a B200 (measured); clusters never wait on one another, so a device that
+  // fits fewer runs the rest in a second wave.
+  if (8 * tiles <= kCtasPerSm * sm_count()) {
+    a.G = 8 * tiles;
+    HS_CUDA_CHECK(launch_pdl_cluster(tok_down_kernel<true>, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes,
+                                     st, 8u, d, cm, a));
+    return check_launch();
+  }
   HS_CUDA_CHECK(
-      launch_pdl(tok_down_kernel, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes, st, d, cm, a));
+      launch_pdl(tok_down_kernel<false>, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes, st, d, cm, a));
   return check_launch();
 }
 
@@ -1904,18 +2018,6 @@ static int launch_nt(int NT, const Desc& d, const CallMaps& cm, const UnitArgs& 
   }
 }
 
-// Number of SMs of the current device, cached.
-static int sm_count() {
-  static std::atomic<int> cache[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  int v = cache[dev].load();
-  if (v <= 0) {
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
-    cache[dev].store(v);
-  }
-  return v;
-}
 
 static int plan_smem(int E, int npairs) {
   const int cached = npairs <= kLocalPairs ? 2 * npairs : 0;  // ids and post-duplicate experts
