@@ -48,6 +48,7 @@
 
 #include "hs_common.cuh"
 #include "hs_tcgen05.cuh"
+#include "hs_topk.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -693,6 +694,206 @@ __global__ void __launch_bounds__(256) gather_kernel(Plan P, int T, int64_t P_ma
     ld[i] = ls[i];
   }
   if (threadIdx.x == 0) P.sb1[p] = P.sb1[t];
+}
+
+// ---------------------------------------------------------------------------
+// Fused route + plan (token mode, T <= 8): one thread-block cluster of E/16
+// CTAs replaces the router's two phases and the plan kernel. CTA r stages the
+// gate rows of experts [16r, 16r+16) with bulk copies (before the PDL wait:
+// they do not depend on the previous kernel) and the T normed rows, computes
+// the logits with the router's own arithmetic (logit_chunk, the same k-split
+// order), and sends them to CTA 0 through distributed shared memory; CTA 0
+// runs the router's top-k (identical selections and weights) and builds the
+// token-mode plan; every CTA writes its slice of the token rows' hi/lo split.
+// Reference: router.py:22-36 (routing), fused_moe.py:458-517 (the union of
+// experts the FFN runs).
+// ---------------------------------------------------------------------------
+constexpr int kRouteThreads = 256;
+constexpr int kRouteMaxD = 4096;  // 16 gate rows + 8 token rows of D in shared memory
+
+struct RouteArgs {
+  const __nv_bfloat16* x;     // [T][D] normed rows
+  const __nv_bfloat16* gate;  // [E_router][D]
+  const __nv_bfloat16* bias;  // [E_router] or nullptr
+  int T, D, E, K;             // E = router experts (E/16 CTAs)
+  float scaling;
+  int dup_mode;
+  int offset, held;           // this store holds routed experts [offset, offset + held)
+  int64_t* idx_out;           // [T][K] global expert ids
+  float* w_out;               // [T][K]
+  uint32_t* ucount;           // tickets to clear
+  int64_t n_ucount;
+  int64_t n_ctab;             // token tables to clear (C_max * 8)
+  int64_t P_max;              // x8 plane stride in rows
+};
+
+struct RouteSmem {
+  static constexpr size_t gw(int D) { return 0; }
+  static constexpr size_t xs(int D) { return static_cast<size_t>(16) * D * 2; }
+  static constexpr size_t red(int D) { return xs(D) + static_cast<size_t>(8) * D * 2; }
+  static constexpr size_t lg(int D) { return red(D) + 8 * 4 * 32 * 4 * 4; }  // [split <= 8][q 4][lane][4] f32
+  static constexpr size_t top(int D) { return lg(D) + 8 * 256 * 4; }          // CTA 0: [token][expert] logits
+  static constexpr size_t bar(int D) { return top(D) + 8 * 16 * (8 + 4) + 256 + 32; }
+  static constexpr size_t bytes(int D) { return bar(D) + 64; }
+};
+
+__global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs A, Plan P) {
+  extern __shared__ __align__(128) uint8_t rs[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int ncta = static_cast<int>(cluster.num_blocks());
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = A.T, D = A.D, E = A.E, K = A.K;
+  __nv_bfloat16* gw = reinterpret_cast<__nv_bfloat16*>(rs + RouteSmem::gw(D));
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rs + RouteSmem::xs(D));
+  float* red = reinterpret_cast<float*>(rs + RouteSmem::red(D));
+  float* lg = reinterpret_cast<float*>(rs + RouteSmem::lg(D));
+  int64_t* sI = reinterpret_cast<int64_t*>(rs + RouteSmem::top(D));  // [T][K] selections
+  float* sW = reinterpret_cast<float*>(sI + 8 * 16);                 // [T][K] weights
+  uint32_t* emask = reinterpret_cast<uint32_t*>(sW + 8 * 16);         // 256-bit expert bitmap (CTA 0)
+  int* rowe = reinterpret_cast<int*>(emask + 8);                      // [8] row prescale exponents
+  uint64_t* bar = reinterpret_cast<uint64_t*>(rs + RouteSmem::bar(D));
+  const int e0 = rank * 16;
+  const size_t gbytes = static_cast<size_t>(16) * D * 2, xbytes = static_cast<size_t>(T) * D * 2;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {  // the gate slice does not depend on the previous kernel: start it now
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(gbytes + xbytes));
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(A.gate + static_cast<int64_t>(e0) * D);
+    for (size_t o = 0; o < gbytes; o += 16384)
+      bulk_load(reinterpret_cast<uint8_t*>(gw) + o, src + o,
+                static_cast<uint32_t>(gbytes - o < 16384 ? gbytes - o : 16384), bar);
+  }
+  pdl_trigger();
+  pdl_wait();  // the normed rows (and everything earlier) are complete
+  if (tid == 0)
+    for (size_t o = 0; o < xbytes; o += 16384)
+      bulk_load(reinterpret_cast<uint8_t*>(xs) + o, reinterpret_cast<const uint8_t*>(A.x) + o,
+                static_cast<uint32_t>(xbytes - o < 16384 ? xbytes - o : 16384), bar);
+  // clear this kernel's share of the tickets and token tables meanwhile
+  for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ucount;
+       i += static_cast<int64_t>(ncta) * kRouteThreads)
+    A.ucount[i] = 0u;
+  for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ctab;
+       i += static_cast<int64_t>(ncta) * kRouteThreads) {
+    P.ctab_wb[i] = 0.f;
+    P.ctab_sb[i] = 127;
+  }
+  if (rank == 0 && tid < 8) emask[tid] = 0u;
+  const bool ok = mbar_wait(bar, 0);
+
+  // ---- logits: chunk (split s, quarter q) of 128 columns per warp iteration ----
+  const int nsplit = D / router::kKSplitCols;
+  const int g = lane >> 2;
+  if (ok) {
+    for (int ch = warp; ch < 4 * nsplit; ch += kRouteThreads / 32) {
+      const int sp = ch >> 2, q = ch & 3;
+      float acc[4];
+      router::logit_chunk(gw + static_cast<int64_t>(g) * D, gw + static_cast<int64_t>(g + 8) * D,
+                          xs + static_cast<int64_t>(g < T ? g : 0) * D, g < T, sp * router::kKSplitCols + q * 128,
+                          acc);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red[((sp * 4 + q) * 32 + lane) * 4 + j] = acc[j];
+    }
+  }
+  // row prescale of every token (each CTA needs it for its x8 slice)
+  for (int t = warp; t < T; t += kRouteThreads / 32) {
+    float mx = 0.f;
+    for (int k = lane; k < D; k += 32) mx = fmaxf(mx, fabsf(__bfloat162float(xs[static_cast<int64_t>(t) * D + k])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) {
+      int ex = 0;
+      if (mx > 0.f && isfinite(mx)) {
+        frexpf(mx, &ex);
+        ex = max(-100, min(100, 8 - ex));
+      } else {
+        ex = 0;
+      }
+      rowe[t] = ex;
+    }
+  }
+  __syncthreads();
+  // logit of (expert, token) for the 16 x 8 fragment positions: quarters in
+  // order, then k-splits in order (the router's order), to CTA 0
+  if (tid < 128) {
+    const int ln = tid & 31, j = tid >> 5;
+    const int el = (ln >> 2) + ((j & 2) ? 8 : 0), t = 2 * (ln & 3) + (j & 1);
+    float l = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float* r = red + (sp * 4 * 32 + ln) * 4 + j;
+      l += ((r[0] + r[32 * 4]) + r[2 * 32 * 4]) + r[3 * 32 * 4];
+    }
+    if (t < T) cluster.map_shared_rank(lg, 0)[t * E + e0 + el] = l;
+  }
+  // this CTA's columns of the token rows' hi/lo e4m3 split
+  {
+    const int cols = D / ncta, c0 = rank * cols;
+    for (int i = tid; i < T * (cols / 16); i += kRouteThreads) {
+      const int t = i / (cols / 16), k16 = c0 / 16 + (i - t * (cols / 16));
+      const uint4* src = reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(t) * D);
+      uint4 hv, lv;
+      split16(src[2 * k16], src[2 * k16 + 1], exp2i(rowe[t]), hv, lv);
+      reinterpret_cast<uint4*>(P.x8 + static_cast<int64_t>(t) * D)[k16] = hv;
+      reinterpret_cast<uint4*>(P.x8 + (A.P_max + t) * D)[k16] = lv;
+    }
+  }
+  cluster.sync();
+  if (rank != 0) return;
+
+  // ---- CTA 0: top-k (the router's selection), then the token-mode plan ----
+  if (warp < T) router::topk_dispatch<true>(lg, 1, 1, E, warp, A.bias, K, A.scaling, sI, sW, nullptr);
+  __syncthreads();
+  for (int i = tid; i < T * K; i += kRouteThreads) {
+    A.idx_out[i] = sI[i];
+    A.w_out[i] = sW[i];
+  }
+  if (tid < T) {
+    P.sb1[tid] = static_cast<uint8_t>(127 - rowe[tid]);
+    P.tok_e[tid] = rowe[tid];
+  }
+  // local expert of pair (t, j) after the duplicate rule, -1 if skipped or held elsewhere
+  auto pair_local = [&](int t, int j, float* wsum) {
+    int32_t row[16];
+    for (int jj = 0; jj < K; ++jj) {
+      const int64_t e = sI[t * K + jj] - A.offset;
+      row[jj] = (e < 0 || e >= A.held) ? -1 : static_cast<int32_t>(e);
+    }
+    return pair_expert(row, sW + t * K, j, K, A.dup_mode, wsum);
+  };
+  const int npairs = T * K;
+  if (tid < npairs) {
+    float ws = 0.f;
+    const int e = pair_local(tid / K, tid % K, &ws);
+    if (e >= 0) atomicOr(&emask[e >> 5], 1u << (e & 31));
+  }
+  __syncthreads();
+  if (tid < npairs) {
+    const int t = tid / K;
+    float ws = 0.f;
+    const int e = pair_local(t, tid % K, &ws);
+    if (e >= 0) {
+      int cb = __popc(emask[e >> 5] & ((1u << (e & 31)) - 1u));
+      for (int w = 0; w < (e >> 5); ++w) cb += __popc(emask[w]);
+      const float wb = round_bf16(ws);
+      P.ctab_wb[cb * 8 + t] = wb;
+      P.ctab_sb[cb * 8 + t] = static_cast<uint8_t>(127 - act_prescale(wb));
+      P.chunk_expert[cb] = e;
+      P.chunk_pair0[cb] = 0;
+      P.chunk_np[cb] = 0;
+    }
+  }
+  if (tid == 0) {
+    int C = 0;
+    for (int w = 0; w < 8; ++w) C += __popc(emask[w]);
+    P.hdr[0] = C;
+    P.hdr[1] = C;
+    P.hdr[2] = 0;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -2098,10 +2299,38 @@ extern "C" size_t hs_moe_workspace_size(int64_t T, int64_t top_k, int64_t D, int
 
 // Both MoE entry points: `partials` = 0 writes the bf16 output (and optionally
 // the routed f32 sum); 1 writes the un-rounded f32 routed and shared sums only.
+// Routing folded into the MoE call (token mode): the router's inputs and outputs.
+struct RouteIn {
+  const void* gate;
+  const void* bias;
+  int64_t num_experts, expert_offset;
+  float scaling;
+  int64_t* idx_out;
+  float* w_out;
+};
+
+static int launch_route(const RouteArgs& ra, const Plan& P, cudaStream_t st) {
+  const int ncta = ra.E / 16;
+  const size_t bytes = RouteSmem::bytes(ra.D);
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  HS_CUDA_CHECK(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(done.load() & bit)) {
+    HS_CUDA_CHECK(cudaFuncSetAttribute(route_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(RouteSmem::bytes(kRouteMaxD))));
+    HS_CUDA_CHECK(cudaFuncSetAttribute(route_plan_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    done.fetch_or(bit);
+  }
+  HS_CUDA_CHECK(launch_pdl_cluster(route_plan_kernel, dim3(static_cast<unsigned>(ncta)), dim3(kRouteThreads), bytes,
+                                   st, static_cast<unsigned>(ncta), ra, P));
+  return check_launch();
+}
+
 static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* topk_idx, const float* topk_w,
                         int64_t T, int64_t top_k, int use_shared, int dup_mode, void* out, float* out_f32,
                         float* shared_f32, int partials, void* workspace, size_t workspace_bytes,
-                        int32_t* dev_status, void* stream) {
+                        int32_t* dev_status, void* stream, const RouteIn* route = nullptr) {
   if (!desc) return HS_ERR_BAD_ARGUMENT;
   Desc d;
   memcpy(&d, desc, sizeof(d));
@@ -2109,7 +2338,16 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   if (T < 0 || top_k < 1 || top_k > 16) return HS_ERR_BAD_SHAPE;
   if (T == 0) return HS_OK;
   if (T > (1 << 20)) return HS_ERR_BAD_SHAPE;
-  if (!hidden || !topk_idx || !topk_w || !workspace) return HS_ERR_BAD_ARGUMENT;
+  if (!hidden || !workspace) return HS_ERR_BAD_ARGUMENT;
+  if (!route && (!topk_idx || !topk_w)) return HS_ERR_BAD_ARGUMENT;
+  if (route) {
+    const int64_t Er = route->num_experts;
+    if (T > kTokMax || Er < 16 || Er > 256 || Er % 16 || d.D > kRouteMaxD || d.D % (Er / 16 * 16) ||
+        route->expert_offset < 0 || route->expert_offset + d.E > Er)
+      return HS_ERR_UNSUPPORTED;
+    if (!route->gate || !route->idx_out || !route->w_out) return HS_ERR_BAD_ARGUMENT;
+    if (!aligned16(route->gate)) return HS_ERR_ALIGN;
+  }
   if (partials ? !out_f32 : !out) return HS_ERR_BAD_ARGUMENT;
   if (dup_mode != HS_DUP_LAST && dup_mode != HS_DUP_SUM) return HS_ERR_BAD_ARGUMENT;
   if (!aligned16(hidden) || (out && !aligned16(out)) || !aligned16(workspace) || (out_f32 && !aligned16(out_f32)) ||
@@ -2156,8 +2394,30 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   pa.status = dev_status;
   pa.ucount = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + g.off_ucount);
   pa.n_ucount = g.U_gu + g.U_dn;
-  if ((rc = launch_plan(pa, P, 1 + static_cast<int>(T), st))) return rc;
-  if (!local_rows && !tok) {
+  if (route) {
+    RouteArgs ra;
+    ra.x = static_cast<const __nv_bfloat16*>(hidden);
+    ra.gate = static_cast<const __nv_bfloat16*>(route->gate);
+    ra.bias = static_cast<const __nv_bfloat16*>(route->bias);
+    ra.T = static_cast<int>(T);
+    ra.D = d.D;
+    ra.E = static_cast<int>(route->num_experts);
+    ra.K = static_cast<int>(top_k);
+    ra.scaling = route->scaling;
+    ra.dup_mode = dup_mode;
+    ra.offset = static_cast<int>(route->expert_offset);
+    ra.held = d.E;
+    ra.idx_out = route->idx_out;
+    ra.w_out = route->w_out;
+    ra.ucount = pa.ucount;
+    ra.n_ucount = pa.n_ucount;
+    ra.n_ctab = g.C_max * 8;
+    ra.P_max = g.P_max;
+    if ((rc = launch_route(ra, P, st))) return rc;
+  } else if ((rc = launch_plan(pa, P, 1 + static_cast<int>(T), st))) {
+    return rc;
+  }
+  if (!route && !local_rows && !tok) {
     HS_CUDA_CHECK(launch_pdl(gather_kernel, dim3(static_cast<unsigned>(npairs)), dim3(256), 0, st, P,
                              static_cast<int>(T), g.P_max, d.D));
     if ((rc = check_launch())) return rc;
@@ -2196,6 +2456,27 @@ extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_
                               void* workspace, size_t workspace_bytes, int32_t* dev_status, void* stream) {
   return moe_ffn_impl(desc, hidden, topk_idx, topk_w, T, top_k, use_shared, dup_mode, out, out_f32, nullptr, 0,
                       workspace, workspace_bytes, dev_status, stream);
+}
+
+extern "C" int hs_moe_route_ffn_fp4(const void* desc, const void* hidden, const void* gate, const void* bias,
+                                    int64_t num_experts, int64_t expert_offset, int64_t T, int64_t top_k,
+                                    float routed_scaling, int use_shared, int dup_mode, int64_t* topk_idx,
+                                    float* topk_w, void* out, float* out_f32, void* workspace,
+                                    size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  const RouteIn r{gate, bias, num_experts, expert_offset, routed_scaling, topk_idx, topk_w};
+  return moe_ffn_impl(desc, hidden, nullptr, nullptr, T, top_k, use_shared, dup_mode, out, out_f32, nullptr, 0,
+                      workspace, workspace_bytes, dev_status, stream, &r);
+}
+
+extern "C" int hs_moe_route_ffn_fp4_partials(const void* desc, const void* hidden, const void* gate,
+                                             const void* bias, int64_t num_experts, int64_t expert_offset, int64_t T,
+                                             int64_t top_k, float routed_scaling, int use_shared, int dup_mode,
+                                             int64_t* topk_idx, float* topk_w, float* routed_f32,
+                                             float* shared_f32, void* workspace, size_t workspace_bytes,
+                                             int32_t* dev_status, void* stream) {
+  const RouteIn r{gate, bias, num_experts, expert_offset, routed_scaling, topk_idx, topk_w};
+  return moe_ffn_impl(desc, hidden, nullptr, nullptr, T, top_k, use_shared, dup_mode, nullptr, routed_f32,
+                      shared_f32, 1, workspace, workspace_bytes, dev_status, stream, &r);
 }
 
 extern "C" int hs_moe_ffn_fp4_partials(const void* desc, const void* hidden, const int64_t* topk_idx,

@@ -23,12 +23,11 @@
 // Kernel 2 (top-k): one warp per token sums the k-split partials in order,
 // applies the roundings/transcendentals and selects by warp-shuffle arg-max.
 #include "hs_common.cuh"
+#include "hs_topk.cuh"
 
 namespace hs {
 namespace router {
 
-constexpr int kKSplitCols = 512;  // columns per CTA along D
-constexpr int kWarps = 4;         // 128 columns per warp per CTA
 constexpr int kFusedTopkTokens = 64;  // T <= this: top-k runs in the last logits CTA
 
 struct TopkArgs {
@@ -41,10 +40,6 @@ struct TopkArgs {
   uint32_t* counter;  // nullptr: a separate top-k launch follows
 };
 
-__device__ __forceinline__ void topk_dispatch(const float* partial, int ksplit, int T, int E, int t,
-                                              const __nv_bfloat16* bias, int K, float scaling, int64_t* idx_out,
-                                              float* w_out, __nv_bfloat16* logits_out);
-
 __global__ void __launch_bounds__(kWarps * 32) logits_kernel(const __nv_bfloat16* __restrict__ h,
                                                              const __nv_bfloat16* __restrict__ gate, int T, int D,
                                                              int E, float* __restrict__ partial, TopkArgs ta) {
@@ -56,23 +51,10 @@ __global__ void __launch_bounds__(kWarps * 32) logits_kernel(const __nv_bfloat16
   const int ks = blockIdx.y;
   const int t0 = blockIdx.z * 8;
   const int kw = ks * kKSplitCols + warp * (kKSplitCols / kWarps);
-  const __nv_bfloat16* alo = gate + static_cast<int64_t>(e0 + g) * D;
-  const __nv_bfloat16* ahi = gate + static_cast<int64_t>(e0 + g + 8) * D;
   const bool tv = (t0 + g) < T;
-  const __nv_bfloat16* brow = h + static_cast<int64_t>(tv ? t0 + g : 0) * D;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int k = 0; k < kKSplitCols / kWarps; k += 32) {
-    // thread c owns logical columns 8c..8c+7 of this 32-column group on both
-    // operands, so the MMA sums exactly the same products.
-    const int kk = kw + k + 8 * c;
-    const uint4 al = *reinterpret_cast<const uint4*>(alo + kk);
-    const uint4 ah = *reinterpret_cast<const uint4*>(ahi + kk);
-    uint4 bv = make_uint4(0u, 0u, 0u, 0u);
-    if (tv) bv = *reinterpret_cast<const uint4*>(brow + kk);
-    mma_bf16(acc, al.x, ah.x, al.y, ah.y, bv.x, bv.y);
-    mma_bf16(acc, al.z, ah.z, al.w, ah.w, bv.z, bv.w);
-  }
+  float acc[4];
+  logit_chunk(gate + static_cast<int64_t>(e0 + g) * D, gate + static_cast<int64_t>(e0 + g + 8) * D,
+              h + static_cast<int64_t>(tv ? t0 + g : 0) * D, tv, kw, acc);
   __shared__ float red[kWarps][32][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) red[warp][lane][j] = acc[j];
@@ -107,96 +89,6 @@ __global__ void __launch_bounds__(kWarps * 32) logits_kernel(const __nv_bfloat16
   for (int t = warp; t < T; t += kWarps)
     topk_dispatch(partial, ksplit, T, E, t, ta.bias, ta.K, ta.scaling, ta.idx_out, ta.w_out, ta.logits_out);
   if (threadIdx.x == 0) *ta.counter = 0u;
-}
-
-__device__ __forceinline__ uint64_t score_key(float s, int e) {
-  const uint32_t hi = isnan(s) ? 0xffffffffu : __float_as_uint(s);  // s >= 0 (or NaN)
-  return (static_cast<uint64_t>(hi) << 32) | static_cast<uint64_t>(0xffffffffu - static_cast<uint32_t>(e));
-}
-
-// One warp selects the top-K experts of one token. PER = experts per lane
-// (compile-time, so scores and keys stay in registers).
-template <int PER>
-__device__ __forceinline__ void topk_token(const float* __restrict__ partial, int ksplit, int T, int E, int t,
-                                           const __nv_bfloat16* __restrict__ bias, int K, float scaling,
-                                           int64_t* __restrict__ idx_out, float* __restrict__ w_out,
-                                           __nv_bfloat16* __restrict__ logits_out) {
-  const int lane = threadIdx.x & 31;
-  float sc[PER];
-  uint64_t key[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int e = lane + 32 * i;
-    key[i] = 0ull;
-    sc[i] = 0.f;
-    if (e < E) {
-      // all k-split partials are loaded before the in-order sum (independent loads)
-      float pv[16];
-#pragma unroll
-      for (int s = 0; s < 16; ++s) pv[s] = s < ksplit ? __ldcg(partial + (static_cast<int64_t>(s) * T + t) * E + e) : 0.f;
-      float l = 0.f;
-#pragma unroll
-      for (int s = 0; s < 16; ++s)
-        if (s < ksplit) l += pv[s];
-      float lb = round_bf16(l);
-      if (bias) lb = round_bf16(lb + __bfloat162float(bias[e]));
-      if (logits_out) logits_out[static_cast<int64_t>(t) * E + e] = __float2bfloat16_rn(lb);
-      const float sp = lb > 20.f ? lb : log1pf(expf(lb));
-      sc[i] = sqrtf(sp);
-      key[i] = score_key(sc[i], e);
-    }
-  }
-  float wsum = 0.f;
-  float wsel = 0.f;  // lane r keeps the r-th selected score
-  int esel = 0;
-  for (int r = 0; r < K; ++r) {
-    uint64_t best = 0ull;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) best = key[i] > best ? key[i] : best;
-    uint64_t wb = best;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const uint64_t other = __shfl_xor_sync(0xffffffffu, wb, o);
-      wb = other > wb ? other : wb;
-    }
-    const int e = static_cast<int>(0xffffffffu - static_cast<uint32_t>(wb & 0xffffffffull));
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < PER; ++i)
-      if (key[i] == wb) {
-        s = sc[i];
-        key[i] = 0ull;
-      }
-    s = __shfl_sync(0xffffffffu, s, e & 31);
-    wsum += s;  // same order on every lane: selection order
-    if (lane == r) {
-      wsel = s;
-      esel = e;
-    }
-  }
-  const float denom = fmaxf(wsum, 1e-20f);
-  if (lane < K) {
-    idx_out[static_cast<int64_t>(t) * K + lane] = esel;
-    w_out[static_cast<int64_t>(t) * K + lane] = (wsel / denom) * scaling;
-  }
-}
-
-__device__ __forceinline__ void topk_dispatch(const float* partial, int ksplit, int T, int E, int t,
-                                              const __nv_bfloat16* bias, int K, float scaling, int64_t* idx_out,
-                                              float* w_out, __nv_bfloat16* logits_out) {
-  const int per = (E + 31) / 32;
-  if (per <= 1)
-    topk_token<1>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
-  else if (per <= 2)
-    topk_token<2>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
-  else if (per <= 4)
-    topk_token<4>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
-  else if (per <= 8)
-    topk_token<8>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
-  else if (per <= 16)
-    topk_token<16>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
-  else
-    topk_token<32>(partial, ksplit, T, E, t, bias, K, scaling, idx_out, w_out, logits_out);
 }
 
 __global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ partial, int ksplit, int T, int E,

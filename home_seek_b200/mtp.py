@@ -95,17 +95,29 @@ class MoEPathModel:
     # --- one MoE layer (the part of _forward_layer / _forward_ffn this build owns)
     def moe(self, x: torch.Tensor, layer: int, ids: torch.Tensor) -> torch.Tensor:
         s = self.shape
-        lw = self.store.layers[layer]
-        if layer < s.hash_layers and lw.tid2eid is not None:
-            idx, w = ops.hash_route(ids, lw.tid2eid, s.top_k)
-        else:
-            idx, w = ops.router_topk(x, lw.gate, lw.bias, s.top_k, s.routed_scaling)
+        st = self.store
+        lw = st.layers[layer]
         # T=1 decode follows the reference's M=1 path (duplicates summed,
         # engine.py:1388-1393); T>1 follows _forward_legacy (last weight wins)
         dup = HS_DUP_SUM if x.shape[0] == 1 else HS_DUP_LAST
+        if layer < s.hash_layers and lw.tid2eid is not None:
+            idx, w = ops.hash_route(ids, lw.tid2eid, s.top_k)
+        elif x.shape[0] <= 8:
+            # decode sizes: router + FFN in one call (routing and plan in one cluster)
+            if self.ep is not None:  # f32 partial sums, summed over the ranks
+                buf, _, _ = ops.moe_route_ffn(st.desc(layer), st.dims, x, lw.gate, lw.bias, s.top_k,
+                                              s.routed_scaling, dup_mode=dup, expert_offset=st.expert_offset,
+                                              partials=True)
+                self.ep.all_reduce(buf)
+                return buf
+            out, _, _ = ops.moe_route_ffn(st.desc(layer), st.dims, x, lw.gate, lw.bias, s.top_k, s.routed_scaling,
+                                          dup_mode=dup)
+            return out
+        else:
+            idx, w = ops.router_topk(x, lw.gate, lw.bias, s.top_k, s.routed_scaling)
         if self.ep is not None:  # f32 partial sums, already summed over the ranks
-            return self.ep.partials(self.store, layer, x, idx, w, dup)
-        return ops.moe_ffn(self.store.desc(layer), self.store.dims, x, idx, w, use_shared=True, dup_mode=dup)
+            return self.ep.partials(st, layer, x, idx, w, dup)
+        return ops.moe_ffn(st.desc(layer), st.dims, x, idx, w, use_shared=True, dup_mode=dup)
 
     def _add_norm(self, h: torch.Tensor, y: torch.Tensor, w: torch.Tensor, in_place: bool,
                   x_out: Optional[torch.Tensor] = None):

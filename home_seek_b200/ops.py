@@ -21,6 +21,7 @@ launches = 0
 _KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_moe_permute": 2,
             "hs_moe_unpermute": 1, "hs_accept_greedy": 1, "hs_accept_rejection": 1, "hs_fill_bytes": 1,
             "hs_rms_norm": 1, "hs_add_rms_norm": 1, "hs_moe_ffn_fp4_partials": 3, "hs_moe_combine": 1,
+            "hs_moe_route_ffn_fp4": 3, "hs_moe_route_ffn_fp4_partials": 3,
             "hs_moe_combine_add_rms_norm": 1}
 
 
@@ -201,6 +202,46 @@ def moe_ffn_partials(desc: ctypes.Array, dims: tuple, hidden: torch.Tensor, topk
     return out
 
 
+def moe_route_ffn(desc: ctypes.Array, dims: tuple, hidden: torch.Tensor, gate: torch.Tensor,
+                  bias: Optional[torch.Tensor], top_k: int, routed_scaling: float, use_shared: bool = True,
+                  dup_mode: int = _lib.HS_DUP_LAST, expert_offset: int = 0, partials: bool = False,
+                  out: Optional[torch.Tensor] = None):
+    """Router + MoE FFN in one call for T <= 8 (hs_moe_route_ffn_fp4): returns
+    (out, topk_idx, topk_w) with out [T, D] bf16, or [2, T, D] f32 partial sums
+    when partials (expert parallelism: sum over ranks, then moe_combine)."""
+    dev = _check_cuda(hidden, gate, bias, out)
+    if hidden.dtype != torch.bfloat16 or gate.dtype != torch.bfloat16:
+        raise TypeError("hidden and gate must be bf16")
+    T, D = hidden.shape
+    E, Dd, I, I_sh = dims
+    if D != Dd:
+        raise ValueError(f"hidden dim {D} != store dim {Dd}")
+    n_exp = gate.shape[0]
+    idx = torch.empty(T, top_k, dtype=torch.int64, device=dev)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws = workspace(dev, lib.hs_moe_workspace_size(T, top_k, D, I, I_sh), "moe")
+    use_shared = bool(use_shared) and bool(I_sh)
+    if partials:
+        if out is None:
+            out = torch.empty(2, T, D, dtype=torch.float32, device=dev)
+        if not use_shared:
+            out[1].zero_()
+        _launch("hs_moe_route_ffn_fp4_partials", ctypes.addressof(desc), hidden.data_ptr(), gate.data_ptr(),
+                _ptr(bias), n_exp, int(expert_offset), T, top_k, float(routed_scaling), int(use_shared),
+                int(dup_mode), idx.data_ptr(), w.data_ptr(), out[0].data_ptr(),
+                out[1].data_ptr() if use_shared else None, ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(),
+                _stream(dev))
+    else:
+        if out is None:
+            out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+        _launch("hs_moe_route_ffn_fp4", ctypes.addressof(desc), hidden.data_ptr(), gate.data_ptr(), _ptr(bias),
+                n_exp, int(expert_offset), T, top_k, float(routed_scaling), int(use_shared), int(dup_mode),
+                idx.data_ptr(), w.data_ptr(), out.data_ptr(), None, ws.data_ptr(), ws.numel(),
+                status_word(dev).data_ptr(), _stream(dev))
+    return out, idx, w
+
+
 def moe_combine(partials: torch.Tensor, use_shared: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """bf16(bf16(routed) + bf16(shared)) from summed f32 partials [2, T, D]."""
     dev = _check_cuda(partials, out)
@@ -351,5 +392,6 @@ def fill_bytes(t: torch.Tensor, seed: int, lo: int = 0, hi: int = 255) -> torch.
 
 __all__ = ["HsError", "router_topk", "hash_route", "make_moe_desc", "moe_ffn", "moe_permute", "moe_unpermute",
            "accept_greedy", "accept_rejection", "fill_bytes", "rms_norm", "add_rms_norm", "moe_ffn_partials",
+           "moe_route_ffn",
            "moe_combine", "moe_combine_add_rms_norm", "check_status",
            "status_word", "workspace"]

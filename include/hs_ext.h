@@ -257,6 +257,39 @@ int hs_moe_ffn_fp4_partials(const void* desc, const void* hidden,
                             int dup_mode, float* routed_f32, float* shared_f32,
                             void* workspace, size_t workspace_bytes,
                             int32_t* dev_status, void* stream);
+/* ------------------------------------------------------------------------ */
+/* Routing folded into the MoE call (decode sizes).                          */
+/* One call = hs_router_topk + hs_moe_ffn_fp4 (or its partials form) for     */
+/* T <= 8 tokens: the router (router.py:22-36, same arithmetic and           */
+/* selections as hs_router_topk) runs in one thread-block cluster that also  */
+/* builds the FFN's plan, so the layer is three launches instead of five.    */
+/* hidden [T][D] bf16 (normed rows), gate [num_experts][D] bf16, bias         */
+/* [num_experts] bf16 or NULL; topk_idx [T][top_k] int64 (global ids) and    */
+/* topk_w [T][top_k] f32 receive the routing. The descriptor's store holds    */
+/* routed experts [expert_offset, expert_offset + E) (expert parallelism;     */
+/* 0 and num_experts for a full store); selections outside it are skipped.    */
+/* Limits: T <= 8, 16 <= num_experts <= 256 (a multiple of 16), D <= 4096;   */
+/* otherwise HS_ERR_UNSUPPORTED (use hs_router_topk + hs_moe_ffn_fp4). The    */
+/* workspace is hs_moe_workspace_size(T, top_k, D, I, I_sh).                  */
+/* ------------------------------------------------------------------------ */
+int hs_moe_route_ffn_fp4(const void* desc, const void* hidden,
+                         const void* gate, const void* bias,
+                         int64_t num_experts, int64_t expert_offset,
+                         int64_t T, int64_t top_k, float routed_scaling,
+                         int use_shared, int dup_mode, int64_t* topk_idx,
+                         float* topk_w, void* out, float* out_f32,
+                         void* workspace, size_t workspace_bytes,
+                         int32_t* dev_status, void* stream);
+int hs_moe_route_ffn_fp4_partials(const void* desc, const void* hidden,
+                                  const void* gate, const void* bias,
+                                  int64_t num_experts, int64_t expert_offset,
+                                  int64_t T, int64_t top_k,
+                                  float routed_scaling, int use_shared,
+                                  int dup_mode, int64_t* topk_idx,
+                                  float* topk_w, float* routed_f32,
+                                  float* shared_f32, void* workspace,
+                                  size_t workspace_bytes, int32_t* dev_status,
+                                  void* stream);
 int hs_moe_combine(const float* routed_f32, const float* shared_f32,
                    int use_shared, int64_t T, int64_t D, void* out,
                    void* stream);

@@ -325,3 +325,31 @@ def test_rejection_accepts_when_p_equals_q():
     assert (n.cpu() == 2).all()
     _, tok_ref = A.rejection(target.float().numpy(), target.float().numpy(), ids.numpy(), u.numpy(), 0.7)
     assert np.array_equal(nxt.cpu().numpy(), tok_ref)
+
+
+@pytest.mark.parametrize("T", [1, 3, 8])
+def test_fused_route_ffn_equals_router_then_ffn(T):
+    """hs_moe_route_ffn_fp4 (router + plan in one cluster) gives the routing of
+    hs_router_topk bit for bit and the output of hs_moe_ffn_fp4 on it."""
+    from home_seek_b200 import ops
+    from home_seek_b200.expert_store import HBMExpertStore
+    st = HBMExpertStore(1, 256, 4096, 2048, 2048, device="cuda")
+    st.fill_random(11)
+    lw = st.layers[0]
+    g = torch.Generator(device="cuda").manual_seed(T)
+    h = torch.randn(T, 4096, generator=g, device="cuda").to(torch.bfloat16)
+    dup = 1 if T == 1 else 0
+    idx, w = ops.router_topk(h, lw.gate, lw.bias, 6, 1.5)
+    ref = ops.moe_ffn(st.desc(0), st.dims, h, idx, w, dup_mode=dup)
+    out, idx2, w2 = ops.moe_route_ffn(st.desc(0), st.dims, h, lw.gate, lw.bias, 6, 1.5, dup_mode=dup)
+    assert ops.check_status(torch.device("cuda")) == 0
+    assert torch.equal(idx2, idx) and torch.equal(w2, w)
+    assert torch.equal(out, ref)
+    # expert-parallel half: partial sums over experts [128, 256) equal the unfused partials
+    from home_seek_b200.ep import localize, shard_store
+    half = shard_store(st, 1, 2)
+    p_ref = ops.moe_ffn_partials(half.desc(0), half.dims, h, localize(idx, 128, 128), w, dup_mode=dup)
+    p, idx3, _ = ops.moe_route_ffn(half.desc(0), half.dims, h, lw.gate, lw.bias, 6, 1.5, dup_mode=dup,
+                                   expert_offset=128, partials=True)
+    assert torch.equal(idx3, idx)
+    assert torch.equal(p, p_ref)
