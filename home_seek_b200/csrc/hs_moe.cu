@@ -727,15 +727,20 @@ struct RouteArgs {
   int64_t P_max;              // x8 plane stride in rows
 };
 
+// Shared memory of the route kernel. Gate and token rows are stored with a
+// 16-byte pad per row so the MMA fragment loads (8 rows at one column offset)
+// fall in different banks.
 struct RouteSmem {
-  static constexpr size_t gw(int D) { return 0; }
-  static constexpr size_t xs(int D) { return static_cast<size_t>(16) * D * 2; }
-  static constexpr size_t red(int D) { return xs(D) + static_cast<size_t>(8) * D * 2; }
-  static constexpr size_t lg(int D) { return red(D) + 8 * 4 * 32 * 4 * 4; }  // [split <= 8][q 4][lane][4] f32
-  static constexpr size_t top(int D) { return lg(D) + 8 * 256 * 4; }          // CTA 0: [token][expert] logits
-  static constexpr size_t bar(int D) { return top(D) + 8 * 16 * (8 + 4) + 256 + 32; }
-  static constexpr size_t bytes(int D) { return bar(D) + 64; }
+  static constexpr int stride(int D) { return D + 8; }  // bf16 elements per stored row
+  static constexpr size_t gw(int) { return 0; }
+  static constexpr size_t xs(int D) { return static_cast<size_t>(16) * stride(D) * 2; }
+  static constexpr size_t red(int D) { return xs(D) + static_cast<size_t>(8) * stride(D) * 2; }
+  static constexpr size_t keys(int D) { return red(D) + 8 * 4 * 32 * 4 * 4; }  // [split <= 8][q][lane][4] f32
+  static constexpr size_t top(int D) { return keys(D) + 8 * 256 * 8; }         // CTA 0: [token][expert] keys
+  static constexpr size_t bar(int D) { return top(D) + 8 * 16 * (8 + 4) + 32 + 32 + 64; }
+  static constexpr size_t bytes(int D) { return bar(D) + 16; }
 };
+static_assert(RouteSmem::bytes(kRouteMaxD) <= 232448, "route kernel shared memory");
 
 __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs A, Plan P) {
   extern __shared__ __align__(128) uint8_t rs[];
@@ -744,17 +749,19 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   const int ncta = static_cast<int>(cluster.num_blocks());
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = A.T, D = A.D, E = A.E, K = A.K;
+  const int RS = RouteSmem::stride(D);
   __nv_bfloat16* gw = reinterpret_cast<__nv_bfloat16*>(rs + RouteSmem::gw(D));
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rs + RouteSmem::xs(D));
   float* red = reinterpret_cast<float*>(rs + RouteSmem::red(D));
-  float* lg = reinterpret_cast<float*>(rs + RouteSmem::lg(D));
+  uint64_t* keys = reinterpret_cast<uint64_t*>(rs + RouteSmem::keys(D));
   int64_t* sI = reinterpret_cast<int64_t*>(rs + RouteSmem::top(D));  // [T][K] selections
   float* sW = reinterpret_cast<float*>(sI + 8 * 16);                 // [T][K] weights
   uint32_t* emask = reinterpret_cast<uint32_t*>(sW + 8 * 16);         // 256-bit expert bitmap (CTA 0)
   int* rowe = reinterpret_cast<int*>(emask + 8);                      // [8] row prescale exponents
+  float* biasv = reinterpret_cast<float*>(rowe + 8);                  // [16] this CTA's biases
   uint64_t* bar = reinterpret_cast<uint64_t*>(rs + RouteSmem::bar(D));
   const int e0 = rank * 16;
-  const size_t gbytes = static_cast<size_t>(16) * D * 2, xbytes = static_cast<size_t>(T) * D * 2;
+  const uint32_t rowb = static_cast<uint32_t>(D) * 2;
 
   if (tid == 0) {
     mbar_init(bar, 1);
@@ -762,18 +769,15 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   }
   __syncthreads();
   if (tid == 0) {  // the gate slice does not depend on the previous kernel: start it now
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(gbytes + xbytes));
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(A.gate + static_cast<int64_t>(e0) * D);
-    for (size_t o = 0; o < gbytes; o += 16384)
-      bulk_load(reinterpret_cast<uint8_t*>(gw) + o, src + o,
-                static_cast<uint32_t>(gbytes - o < 16384 ? gbytes - o : 16384), bar);
+    mbar_arrive_expect_tx(bar, rowb * (16 + T));
+    for (int r = 0; r < 16; ++r)
+      bulk_load(gw + r * RS, A.gate + static_cast<int64_t>(e0 + r) * D, rowb, bar);
   }
+  if (tid < 16) biasv[tid] = A.bias ? __bfloat162float(A.bias[e0 + tid]) : 0.f;
   pdl_trigger();
   pdl_wait();  // the normed rows (and everything earlier) are complete
   if (tid == 0)
-    for (size_t o = 0; o < xbytes; o += 16384)
-      bulk_load(reinterpret_cast<uint8_t*>(xs) + o, reinterpret_cast<const uint8_t*>(A.x) + o,
-                static_cast<uint32_t>(xbytes - o < 16384 ? xbytes - o : 16384), bar);
+    for (int t = 0; t < T; ++t) bulk_load(xs + t * RS, A.x + static_cast<int64_t>(t) * D, rowb, bar);
   // clear this kernel's share of the tickets and token tables meanwhile
   for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ucount;
        i += static_cast<int64_t>(ncta) * kRouteThreads)
@@ -793,17 +797,23 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     for (int ch = warp; ch < 4 * nsplit; ch += kRouteThreads / 32) {
       const int sp = ch >> 2, q = ch & 3;
       float acc[4];
-      router::logit_chunk(gw + static_cast<int64_t>(g) * D, gw + static_cast<int64_t>(g + 8) * D,
-                          xs + static_cast<int64_t>(g < T ? g : 0) * D, g < T, sp * router::kKSplitCols + q * 128,
-                          acc);
+      router::logit_chunk(gw + g * RS, gw + (g + 8) * RS, xs + (g < T ? g : 0) * RS, g < T,
+                          sp * router::kKSplitCols + q * 128, acc);
 #pragma unroll
       for (int j = 0; j < 4; ++j) red[((sp * 4 + q) * 32 + lane) * 4 + j] = acc[j];
     }
   }
-  // row prescale of every token (each CTA needs it for its x8 slice)
-  for (int t = warp; t < T; t += kRouteThreads / 32) {
+  // row prescale of every token, one warp per token (each CTA needs it for its x8 slice)
+  if (warp < T) {
+    const uint4* row = reinterpret_cast<const uint4*>(xs + warp * RS);
     float mx = 0.f;
-    for (int k = lane; k < D; k += 32) mx = fmaxf(mx, fabsf(__bfloat162float(xs[static_cast<int64_t>(t) * D + k])));
+    for (int v = lane; v < D / 8; v += 32) {
+      const uint4 u = row[v];
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(w4[i] << 16)), fabsf(__uint_as_float(w4[i] & 0xffff0000u))));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) {
@@ -814,12 +824,13 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       } else {
         ex = 0;
       }
-      rowe[t] = ex;
+      rowe[warp] = ex;
     }
   }
   __syncthreads();
-  // logit of (expert, token) for the 16 x 8 fragment positions: quarters in
-  // order, then k-splits in order (the router's order), to CTA 0
+  // (expert, token) of the 16 x 8 fragment: the logit (quarters in order, then
+  // k-splits in order: the router's order), its score sqrt(softplus(bf16(bf16(l)
+  // + bias))) and selection key, to CTA 0
   if (tid < 128) {
     const int ln = tid & 31, j = tid >> 5;
     const int el = (ln >> 2) + ((j & 2) ? 8 : 0), t = 2 * (ln & 3) + (j & 1);
@@ -828,14 +839,18 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       const float* r = red + (sp * 4 * 32 + ln) * 4 + j;
       l += ((r[0] + r[32 * 4]) + r[2 * 32 * 4]) + r[3 * 32 * 4];
     }
-    if (t < T) cluster.map_shared_rank(lg, 0)[t * E + e0 + el] = l;
+    float lb = round_bf16(l);
+    if (A.bias) lb = round_bf16(lb + biasv[el]);
+    const float sp = lb > 20.f ? lb : log1pf(expf(lb));
+    const float sc = sqrtf(sp);
+    if (t < T) cluster.map_shared_rank(keys, 0)[t * 256 + e0 + el] = router::score_key(sc, e0 + el);
   }
   // this CTA's columns of the token rows' hi/lo e4m3 split
   {
     const int cols = D / ncta, c0 = rank * cols;
     for (int i = tid; i < T * (cols / 16); i += kRouteThreads) {
       const int t = i / (cols / 16), k16 = c0 / 16 + (i - t * (cols / 16));
-      const uint4* src = reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(t) * D);
+      const uint4* src = reinterpret_cast<const uint4*>(xs + t * RS);
       uint4 hv, lv;
       split16(src[2 * k16], src[2 * k16 + 1], exp2i(rowe[t]), hv, lv);
       reinterpret_cast<uint4*>(P.x8 + static_cast<int64_t>(t) * D)[k16] = hv;
@@ -845,47 +860,90 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   cluster.sync();
   if (rank != 0) return;
 
-  // ---- CTA 0: top-k (the router's selection), then the token-mode plan ----
-  if (warp < T) router::topk_dispatch<true>(lg, 1, 1, E, warp, A.bias, K, A.scaling, sI, sW, nullptr);
-  __syncthreads();
-  for (int i = tid; i < T * K; i += kRouteThreads) {
-    A.idx_out[i] = sI[i];
-    A.w_out[i] = sW[i];
-  }
-  if (tid < T) {
-    P.sb1[tid] = static_cast<uint8_t>(127 - rowe[tid]);
-    P.tok_e[tid] = rowe[tid];
-  }
-  // local expert of pair (t, j) after the duplicate rule, -1 if skipped or held elsewhere
-  auto pair_local = [&](int t, int j, float* wsum) {
-    int32_t row[16];
-    for (int jj = 0; jj < K; ++jj) {
-      const int64_t e = sI[t * K + jj] - A.offset;
-      row[jj] = (e < 0 || e >= A.held) ? -1 : static_cast<int32_t>(e);
+  // ---- CTA 0: the router's top-k selection from the gathered keys ----
+  if (warp < T) {
+    const int t = warp;
+    uint64_t key[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      key[i] = e < E ? keys[t * 256 + e] : 0ull;
     }
-    return pair_expert(row, sW + t * K, j, K, A.dup_mode, wsum);
-  };
+    float wsum = 0.f, wsel = 0.f;
+    int esel = 0;
+    for (int r = 0; r < K; ++r) {
+      uint64_t best = 0ull;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) best = key[i] > best ? key[i] : best;
+      uint64_t wb = best;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t other = __shfl_xor_sync(0xffffffffu, wb, o);
+        wb = other > wb ? other : wb;
+      }
+      const int e = static_cast<int>(0xffffffffu - static_cast<uint32_t>(wb & 0xffffffffull));
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (key[i] == wb) key[i] = 0ull;
+      const float s = __uint_as_float(static_cast<uint32_t>(wb >> 32));
+      wsum += s;  // selection order, as the router
+      if (lane == r) {
+        wsel = s;
+        esel = e;
+      }
+    }
+    const float denom = fmaxf(wsum, 1e-20f);
+    if (lane < K) {
+      const float wv = (wsel / denom) * A.scaling;
+      sI[t * K + lane] = esel;
+      sW[t * K + lane] = wv;
+      A.idx_out[t * K + lane] = esel;
+      A.w_out[t * K + lane] = wv;
+    }
+    if (lane == 0) {
+      P.sb1[t] = static_cast<uint8_t>(127 - rowe[t]);
+      P.tok_e[t] = rowe[t];
+    }
+  }
+  __syncthreads();
+
+  // ---- CTA 0: the token-mode plan, one thread per (token, slot) pair ----
   const int npairs = T * K;
+  int le = -1;
+  float ws = 0.f;
   if (tid < npairs) {
-    float ws = 0.f;
-    const int e = pair_local(tid / K, tid % K, &ws);
-    if (e >= 0) atomicOr(&emask[e >> 5], 1u << (e & 31));
+    const int t = tid / K, j = tid - t * K;
+    auto local = [&](int jj) {
+      const int64_t e = sI[t * K + jj] - A.offset;
+      return (e < 0 || e >= A.held) ? -1 : static_cast<int>(e);
+    };
+    le = local(j);
+    if (le >= 0) {
+      if (A.dup_mode == HS_DUP_SUM) {  // the first slot of an expert carries the summed weight
+        for (int jj = 0; jj < j; ++jj)
+          if (local(jj) == le) le = -1;
+        if (le >= 0)
+          for (int jj = j; jj < K; ++jj)
+            if (local(jj) == le) ws += sW[t * K + jj];
+      } else {  // the last slot of an expert wins
+        for (int jj = j + 1; jj < K; ++jj)
+          if (local(jj) == le) le = -1;
+        ws = sW[t * K + j];
+      }
+    }
+    if (le >= 0) atomicOr(&emask[le >> 5], 1u << (le & 31));
   }
   __syncthreads();
-  if (tid < npairs) {
+  if (tid < npairs && le >= 0) {
     const int t = tid / K;
-    float ws = 0.f;
-    const int e = pair_local(t, tid % K, &ws);
-    if (e >= 0) {
-      int cb = __popc(emask[e >> 5] & ((1u << (e & 31)) - 1u));
-      for (int w = 0; w < (e >> 5); ++w) cb += __popc(emask[w]);
-      const float wb = round_bf16(ws);
-      P.ctab_wb[cb * 8 + t] = wb;
-      P.ctab_sb[cb * 8 + t] = static_cast<uint8_t>(127 - act_prescale(wb));
-      P.chunk_expert[cb] = e;
-      P.chunk_pair0[cb] = 0;
-      P.chunk_np[cb] = 0;
-    }
+    int cb = __popc(emask[le >> 5] & ((1u << (le & 31)) - 1u));
+    for (int w = 0; w < (le >> 5); ++w) cb += __popc(emask[w]);
+    const float wb = round_bf16(ws);
+    P.ctab_wb[cb * 8 + t] = wb;
+    P.ctab_sb[cb * 8 + t] = static_cast<uint8_t>(127 - act_prescale(wb));
+    P.chunk_expert[cb] = le;
+    P.chunk_pair0[cb] = 0;
+    P.chunk_np[cb] = 0;
   }
   if (tid == 0) {
     int C = 0;
