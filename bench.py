@@ -234,21 +234,27 @@ def moe_roofline(model, reps: int = 43):
         idx, w = ops.router_topk(h, lw.gate, lw.bias, s.top_k, s.routed_scaling)
         calls.append((l, h, idx, w))
     st = model.store
+    # the call the model step runs at T = 3: router folded into the MoE call
     if model.ep is None:
         uniq = [len(set(c[2].flatten().tolist())) for c in calls]
         per_call = _graph_time_per_call(
-            lambda: [ops.moe_ffn(st.desc(l), st.dims, h, idx, w, use_shared=True) for (l, h, idx, w) in calls],
-            len(calls))
+            lambda: [ops.moe_route_ffn(st.desc(l), st.dims, h, st.layers[l].gate, st.layers[l].bias, s.top_k,
+                                       s.routed_scaling) for (l, h, idx, w) in calls], len(calls))
     else:
         # this rank's share: its touched experts, its shared-expert rows, the
-        # partials kernel plus the all-reduce (every rank replays the graph)
+        # partials call plus the all-reduce (every rank replays the graph)
         lo, hi = st.expert_offset, st.expert_offset + st.E_local
+
+        def ep_call(l, h):
+            buf = ops.moe_route_ffn(st.desc(l), st.dims, h, st.layers[l].gate, st.layers[l].bias, s.top_k,
+                                    s.routed_scaling, expert_offset=lo, partials=True)[0]
+            model.ep.all_reduce(buf)
+
         uniq = [len({e for e in c[2].flatten().tolist() if lo <= e < hi}) for c in calls]
-        per_call = _graph_time_per_call(
-            lambda: [model.ep.partials(st, l, h, idx, w, 0) for (l, h, idx, w) in calls], len(calls))
+        per_call = _graph_time_per_call(lambda: [ep_call(l, h) for (l, h, idx, w) in calls], len(calls))
     ms = [per_call] * len(calls)
     shared = 3 * st.I_sh * s.hidden + 3 * (st.I_sh // 128) * (s.hidden // 128)
-    act = 3 * s.hidden * 2 * 2 + 12 * 3 * 2
+    act = 3 * s.hidden * 2 * 2 + 12 * 3 * 2 + s.num_experts * s.hidden * 2 + 512  # + the router gate
     bytes_ = [u * s.bytes_per_expert + shared + act for u in uniq]
     gbs = [b / (m * 1e-3) / 1e9 for b, m in zip(bytes_, ms)]
     return {"avg_ms": statistics.mean(ms), "avg_bytes": statistics.mean(bytes_), "avg_gbs": statistics.mean(gbs),
@@ -274,27 +280,36 @@ def run_moe_only(args):
             h = torch.randn(args.T, 4096, generator=g, device=dev).to(torch.bfloat16)
             idx, w = ops.router_topk(h, store.layers[l].gate, store.layers[l].bias, 6, 1.5)
             calls.append((l, h, idx, w))
-    for (l, h, idx, w) in calls[:3]:
-        ops.moe_ffn(store.desc(l), store.dims, h, idx, w)
+    dup = 1 if args.T == 1 else 0
+
+    def call(l, h, idx, w):
+        if args.fused:  # router folded into the call (what the model step runs at T <= 8)
+            lw = store.layers[l]
+            return ops.moe_route_ffn(store.desc(l), store.dims, h, lw.gate, lw.bias, 6, 1.5, dup_mode=dup)[0]
+        return ops.moe_ffn(store.desc(l), store.dims, h, idx, w, dup_mode=dup)
+
+    for c in calls[:3]:
+        call(*c)
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in calls]
-    for (l, h, idx, w), (a, b) in zip(calls, ev):
+    for c, (a, b) in zip(calls, ev):
         a.record()
-        ops.moe_ffn(store.desc(l), store.dims, h, idx, w)
+        call(*c)
         b.record()
     torch.cuda.synchronize()
     ms = [a.elapsed_time(b) for a, b in ev]
     # the same calls replayed from one CUDA graph (no host launch cost; with
     # layers > 1 consecutive calls stream different weights, as in the model)
-    graph_ms = _graph_time_per_call(lambda: [ops.moe_ffn(store.desc(l), store.dims, h, idx, w)
-                                             for (l, h, idx, w) in calls], len(calls))
+    graph_ms = _graph_time_per_call(lambda: [call(*c) for c in calls], len(calls))
     uniq = [len(set(c[2].flatten().tolist())) for c in calls]
     shared = 3 * 2048 * 4096 + 3 * 16 * 32
-    byts = [u * 13_369_344 + shared + args.T * 4096 * 4 + 24 * args.T for u in uniq]
+    byts = [u * 13_369_344 + shared + args.T * 4096 * 4 + 24 * args.T + (256 * 4096 * 2 + 512 if args.fused else 0)
+            for u in uniq]
     peak, kind = _peaks()
     gbs = statistics.mean(b / (m * 1e-3) / 1e9 for b, m in zip(byts, ms))
     graph_gbs = statistics.mean(byts) / (graph_ms * 1e-3) / 1e9
-    print(json.dumps({"mode": "moe", "T": args.T, "layers": args.layers, "calls": len(calls),
+    print(json.dumps({"mode": "moe", "fused_router": bool(args.fused), "T": args.T, "layers": args.layers,
+                      "calls": len(calls),
                       "avg_us": 1000 * statistics.mean(ms), "min_us": 1000 * min(ms),
                       "graph_us": 1000 * graph_ms, "graph_frac": graph_gbs / peak,
                       "avg_unique_experts": statistics.mean(uniq), "avg_bytes": statistics.mean(byts),
@@ -424,7 +439,7 @@ def run_ours(args):
                    "acceptance_rate": accepted / max(1, args.steps * shape.num_draft), "status_word": status},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": _traffic_from_profile(),
-                     "kernel": "hs_moe_ffn_fp4 at T=3 (plan+gateup+down+finalize launches)",
+                     "kernel": "hs_moe_route_ffn_fp4 at T=3 (route+plan, gate/up, down launches)",
                      "peak_kind": peak_kind, "avg_ms": roof["avg_ms"], "avg_bytes": roof["avg_bytes"],
                      "avg_unique_experts": roof["avg_unique_experts"]},
         "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_d["cores"], "kind": "port",
@@ -450,6 +465,7 @@ def main():
                     help="moe: MoE FFN microbenchmark only (profiling; not the driver's line)")
     ap.add_argument("--T", type=int, default=3, help="tokens per MoE call in --mode moe")
     ap.add_argument("--reps", type=int, default=20, help="MoE calls timed in --mode moe")
+    ap.add_argument("--fused", action="store_true", help="--mode moe: router folded into the call (T <= 8)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
