@@ -216,10 +216,12 @@ def _graph_time_per_call(enqueue, n_calls: int, replays: int = 5) -> float:
 
 
 def moe_roofline(model, reps: int = 43):
-    """Time hs_moe_ffn_fp4 at T=3 (the verify shape) over distinct layers,
-    replayed from a CUDA graph; algorithmic bytes per call are the touched
-    experts' FP4 bytes + the FP8 shared expert + activations (under expert
-    parallelism: this rank's experts and shared rows, partials + all-reduce)."""
+    """Time the MoE half of a routed layer at T=3 (the verify shape) as the
+    model step runs it, hs_moe_layer_fp4 (norm + routing + FFN + residual add),
+    over distinct layers replayed from a CUDA graph. Algorithmic bytes per call:
+    the touched experts' FP4 bytes + the FP8 shared expert + the router gate +
+    activations (under expert parallelism: this rank's experts and shared rows,
+    the partials call, the all-reduce and the combine)."""
     import torch
     from home_seek_b200 import ops
     s = model.shape
@@ -231,30 +233,28 @@ def moe_roofline(model, reps: int = 43):
     for l in range(s.hash_layers, L):
         h = (torch.randn(3, s.hidden, generator=g, device=dev)).to(torch.bfloat16)
         lw = model.store.layers[l]
-        idx, w = ops.router_topk(h, lw.gate, lw.bias, s.top_k, s.routed_scaling)
-        calls.append((l, h, idx, w))
+        idx, w = ops.router_topk(ops.rms_norm(h, model.ln_w[l]), lw.gate, lw.bias, s.top_k, s.routed_scaling)
+        calls.append((l, h, idx, torch.empty_like(h)))
     st = model.store
-    # the call the model step runs at T = 3: router folded into the MoE call
-    if model.ep is None:
-        uniq = [len(set(c[2].flatten().tolist())) for c in calls]
-        per_call = _graph_time_per_call(
-            lambda: [ops.moe_route_ffn(st.desc(l), st.dims, h, st.layers[l].gate, st.layers[l].bias, s.top_k,
-                                       s.routed_scaling) for (l, h, idx, w) in calls], len(calls))
-    else:
-        # this rank's share: its touched experts, its shared-expert rows, the
-        # partials call plus the all-reduce (every rank replays the graph)
-        lo, hi = st.expert_offset, st.expert_offset + st.E_local
 
-        def ep_call(l, h):
-            buf = ops.moe_route_ffn(st.desc(l), st.dims, h, st.layers[l].gate, st.layers[l].bias, s.top_k,
-                                    s.routed_scaling, expert_offset=lo, partials=True)[0]
-            model.ep.all_reduce(buf)
+    def layer_call(l, h, h_out):
+        lw = st.layers[l]
+        if model.ep is None:
+            ops.moe_layer(st.desc(l), st.dims, h, model.ln_w[l], lw.gate, lw.bias, s.top_k, s.routed_scaling,
+                          h_out=h_out)
+            return
+        buf = ops.moe_layer(st.desc(l), st.dims, h, model.ln_w[l], lw.gate, lw.bias, s.top_k, s.routed_scaling,
+                            num_experts=s.num_experts, expert_offset=st.expert_offset, partials=True)[0]
+        model.ep.all_reduce(buf)
+        ops.moe_combine_add_rms_norm(buf, h, None, h_out=h_out)
 
-        uniq = [len({e for e in c[2].flatten().tolist() if lo <= e < hi}) for c in calls]
-        per_call = _graph_time_per_call(lambda: [ep_call(l, h) for (l, h, idx, w) in calls], len(calls))
+    lo, hi = st.expert_offset, st.expert_offset + st.E_local
+    uniq = [len({e for e in c[2].flatten().tolist() if lo <= e < hi}) for c in calls]
+    per_call = _graph_time_per_call(lambda: [layer_call(l, h, ho) for (l, h, idx, ho) in calls], len(calls))
     ms = [per_call] * len(calls)
     shared = 3 * st.I_sh * s.hidden + 3 * (st.I_sh // 128) * (s.hidden // 128)
-    act = 3 * s.hidden * 2 * 2 + 12 * 3 * 2 + s.num_experts * s.hidden * 2 + 512  # + the router gate
+    # h in, normed rows (x8) and activations, h out, idx/w, norm weight, router gate and bias
+    act = 3 * s.hidden * 2 * 3 + 12 * 3 * 2 + s.hidden * 2 + s.num_experts * s.hidden * 2 + 512
     bytes_ = [u * s.bytes_per_expert + shared + act for u in uniq]
     gbs = [b / (m * 1e-3) / 1e9 for b, m in zip(bytes_, ms)]
     return {"avg_ms": statistics.mean(ms), "avg_bytes": statistics.mean(bytes_), "avg_gbs": statistics.mean(gbs),
@@ -282,9 +282,15 @@ def run_moe_only(args):
             calls.append((l, h, idx, w))
     dup = 1 if args.T == 1 else 0
 
+    nw = (1 + 0.02 * torch.randn(args.layers, 4096, generator=g, device=dev)).to(torch.bfloat16)
+    h_out = torch.empty(args.T, 4096, dtype=torch.bfloat16, device=dev)
+
     def call(l, h, idx, w):
-        if args.fused:  # router folded into the call (what the model step runs at T <= 8)
-            lw = store.layers[l]
+        lw = store.layers[l]
+        if args.layer:  # norm + router + FFN + residual add (what the model step runs at T <= 8)
+            return ops.moe_layer(store.desc(l), store.dims, h, nw[l], lw.gate, lw.bias, 6, 1.5, dup_mode=dup,
+                                 h_out=h_out)[0]
+        if args.fused:  # router folded into the call
             return ops.moe_route_ffn(store.desc(l), store.dims, h, lw.gate, lw.bias, 6, 1.5, dup_mode=dup)[0]
         return ops.moe_ffn(store.desc(l), store.dims, h, idx, w, dup_mode=dup)
 
@@ -303,12 +309,14 @@ def run_moe_only(args):
     graph_ms = _graph_time_per_call(lambda: [call(*c) for c in calls], len(calls))
     uniq = [len(set(c[2].flatten().tolist())) for c in calls]
     shared = 3 * 2048 * 4096 + 3 * 16 * 32
-    byts = [u * 13_369_344 + shared + args.T * 4096 * 4 + 24 * args.T + (256 * 4096 * 2 + 512 if args.fused else 0)
-            for u in uniq]
+    routed_in = args.fused or args.layer
+    byts = [u * 13_369_344 + shared + args.T * 4096 * 4 + 24 * args.T + (256 * 4096 * 2 + 512 if routed_in else 0)
+            + (args.T * 4096 * 2 + 4096 * 2 if args.layer else 0) for u in uniq]
     peak, kind = _peaks()
     gbs = statistics.mean(b / (m * 1e-3) / 1e9 for b, m in zip(byts, ms))
     graph_gbs = statistics.mean(byts) / (graph_ms * 1e-3) / 1e9
-    print(json.dumps({"mode": "moe", "fused_router": bool(args.fused), "T": args.T, "layers": args.layers,
+    print(json.dumps({"mode": "moe", "fused_router": bool(routed_in), "layer_call": bool(args.layer), "T": args.T,
+                      "layers": args.layers,
                       "calls": len(calls),
                       "avg_us": 1000 * statistics.mean(ms), "min_us": 1000 * min(ms),
                       "graph_us": 1000 * graph_ms, "graph_frac": graph_gbs / peak,
@@ -439,7 +447,7 @@ def run_ours(args):
                    "acceptance_rate": accepted / max(1, args.steps * shape.num_draft), "status_word": status},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": _traffic_from_profile(),
-                     "kernel": "hs_moe_route_ffn_fp4 at T=3 (route+plan, gate/up, down launches)",
+                     "kernel": "hs_moe_layer_fp4 at T=3 (norm+route+plan, gate/up, down+residual launches)",
                      "peak_kind": peak_kind, "avg_ms": roof["avg_ms"], "avg_bytes": roof["avg_bytes"],
                      "avg_unique_experts": roof["avg_unique_experts"]},
         "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_d["cores"], "kind": "port",
@@ -466,6 +474,8 @@ def main():
     ap.add_argument("--T", type=int, default=3, help="tokens per MoE call in --mode moe")
     ap.add_argument("--reps", type=int, default=20, help="MoE calls timed in --mode moe")
     ap.add_argument("--fused", action="store_true", help="--mode moe: router folded into the call (T <= 8)")
+    ap.add_argument("--layer", action="store_true",
+                    help="--mode moe: the layer call, norm + router + FFN + residual add (T <= 8)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

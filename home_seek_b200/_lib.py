@@ -85,6 +85,13 @@ SIGNATURES = {
     "hs_moe_route_ffn_fp4_partials": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                               c_int64, c_float, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                               c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hs_moe_layer_fp4": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p,
+                                 c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int, c_int, c_void_p,
+                                 c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hs_moe_layer_fp4_partials": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int,
+                                          c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_size_t, c_void_p, c_void_p]),
     "hs_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]),
     "hs_moe_combine_add_rms_norm": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_float, c_int64, c_int64,
                                             c_void_p, c_void_p, c_void_p]),

@@ -242,6 +242,35 @@ HS_DI float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)
 // 2^e as f32 for e in [-126, 127].
 HS_DI float exp2i(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
 
+// Eight bf16 (one 16-byte vector) <-> f32, element i of the vector at f[i].
+HS_DI void bf16x8_unpack(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+HS_DI uint4 bf16x8_pack(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i]));
+    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1]));
+    w[i] = lo | (hi << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// RMSNorm constants shared by every kernel that normalises rows, so all of
+// them sum in the same order: a row of D bf16 values is read as D/8 vectors;
+// thread j of kNormThreads takes vectors j, j + kNormThreads, ... and sums the
+// squares in element order, the warp sums with a fixed xor tree, and the warp
+// sums are added in warp order.
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxVec = 4;  // D <= kNormThreads * 8 * kNormMaxVec = 8192
+
 }  // namespace hs
 
 // Host: launch `kernel` with programmatic stream serialization allowed (the

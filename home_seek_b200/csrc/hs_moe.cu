@@ -697,50 +697,75 @@ __global__ void __launch_bounds__(256) gather_kernel(Plan P, int T, int64_t P_ma
 }
 
 // ---------------------------------------------------------------------------
-// Fused route + plan (token mode, T <= 8): one thread-block cluster of E/16
-// CTAs replaces the router's two phases and the plan kernel. CTA r stages the
-// gate rows of experts [16r, 16r+16) with bulk copies (before the PDL wait:
-// they do not depend on the previous kernel) and the T normed rows, computes
-// the logits with the router's own arithmetic (logit_chunk, the same k-split
-// order), and sends them to CTA 0 through distributed shared memory; CTA 0
-// runs the router's top-k (identical selections and weights) and builds the
-// token-mode plan; every CTA writes its slice of the token rows' hi/lo split.
+// Fused norm + route + plan (token mode, T <= 8): one thread-block cluster of
+// E/16 CTAs replaces the layer's RMSNorm, the router's two phases (or the hash
+// lookup) and the plan kernel. CTA r stages the gate rows of experts
+// [16r, 16r+16) and the norm weight with bulk copies (before the PDL wait:
+// they do not depend on the previous kernel), then the T rows. When a norm
+// weight is given the rows are the residual stream h and every CTA normalises
+// them (utils.py:6-9, the sums in the order of the standalone norm kernel, so
+// both give identical rows); otherwise they arrive normed. CTA r computes the
+// logits of its 16 experts with the router's own arithmetic (logit_chunk, the
+// same k-split order), their scores and selection keys, and sends the keys to
+// CTA 0 through distributed shared memory; CTA 0 runs the router's top-k
+// (identical selections and weights) or reads the hash table
+// (engine.py:1018-1023), and builds the token-mode plan; every CTA writes its
+// slice of the normed rows and of their hi/lo split.
 // Reference: router.py:22-36 (routing), fused_moe.py:458-517 (the union of
 // experts the FFN runs).
 // ---------------------------------------------------------------------------
-constexpr int kRouteThreads = 256;
+constexpr int kRouteThreads = kNormThreads;  // the norm's thread layout (256)
 constexpr int kRouteMaxD = 4096;  // 16 gate rows + 8 token rows of D in shared memory
 
 struct RouteArgs {
-  const __nv_bfloat16* x;     // [T][D] normed rows
-  const __nv_bfloat16* gate;  // [E_router][D]
-  const __nv_bfloat16* bias;  // [E_router] or nullptr
-  int T, D, E, K;             // E = router experts (E/16 CTAs)
-  float scaling;
+  const __nv_bfloat16* x;       // [T][D] rows: the residual stream (norm_w given) or normed rows
+  const __nv_bfloat16* norm_w;  // [D] RMSNorm weight, or nullptr (rows already normed)
+  float eps;
+  __nv_bfloat16* x_out;         // [T][D] normed rows, or nullptr
+  const __nv_bfloat16* gate;    // [E_router][D] (router mode)
+  const __nv_bfloat16* bias;    // [E_router] or nullptr
+  const int64_t* ids;           // [T] token ids (hash mode)
+  const int64_t* tid2eid;       // [V][K]: hash mode when not nullptr
+  int64_t V;
+  int T, D, E, K;               // E = router experts (E/16 CTAs)
+  float scaling;                // routed scaling factor (router mode) or the weight 1/K (hash mode)
   int dup_mode;
-  int offset, held;           // this store holds routed experts [offset, offset + held)
-  int64_t* idx_out;           // [T][K] global expert ids
-  float* w_out;               // [T][K]
-  uint32_t* ucount;           // tickets to clear
+  int offset, held;             // this store holds routed experts [offset, offset + held)
+  int64_t* idx_out;             // [T][K] global expert ids
+  float* w_out;                 // [T][K]
+  uint32_t* ucount;             // tickets to clear
   int64_t n_ucount;
-  int64_t n_ctab;             // token tables to clear (C_max * 8)
-  int64_t P_max;              // x8 plane stride in rows
+  int64_t n_ctab;               // token tables to clear (C_max * 8)
+  int64_t P_max;                // x8 plane stride in rows
+  int32_t* status;
 };
 
 // Shared memory of the route kernel. Gate and token rows are stored with a
-// 16-byte pad per row so the MMA fragment loads (8 rows at one column offset)
-// fall in different banks.
+// 64-byte pad per row, so consecutive rows start in opposite halves of the
+// banks and the MMA fragment loads (8 rows x 16 bytes per quarter warp) are
+// conflict-free.
 struct RouteSmem {
-  static constexpr int stride(int D) { return D + 8; }  // bf16 elements per stored row
+  static constexpr int stride(int D) { return D + 32; }  // bf16 elements per stored row
   static constexpr size_t gw(int) { return 0; }
   static constexpr size_t xs(int D) { return static_cast<size_t>(16) * stride(D) * 2; }
-  static constexpr size_t red(int D) { return xs(D) + static_cast<size_t>(8) * stride(D) * 2; }
-  static constexpr size_t keys(int D) { return red(D) + 8 * 4 * 32 * 4 * 4; }  // [split <= 8][q][lane][4] f32
-  static constexpr size_t top(int D) { return keys(D) + 8 * 256 * 8; }         // CTA 0: [token][expert] keys
-  static constexpr size_t bar(int D) { return top(D) + 8 * 16 * (8 + 4) + 32 + 32 + 64; }
+  static constexpr size_t nw(int D) { return xs(D) + static_cast<size_t>(8) * stride(D) * 2; }
+  static constexpr size_t red(int D) { return nw(D) + static_cast<size_t>(D) * 2; }  // [split <= 8][lane][4] f32
+  static constexpr size_t keys(int D) { return red(D) + 8 * 32 * 4 * 4; }            // CTA 0: [token][expert] u32
+  static constexpr size_t top(int D) { return keys(D) + 8 * 256 * 4; }
+  static constexpr size_t bar(int D) { return top(D) + 8 * 16 * (8 + 4) + 32 + 32 + 64 + 32 + 256; }
   static constexpr size_t bytes(int D) { return bar(D) + 16; }
 };
 static_assert(RouteSmem::bytes(kRouteMaxD) <= 232448, "route kernel shared memory");
+
+// Selection key of a score: the score's bits plus one (scores are >= 0, so
+// bit order is value order; 0 marks a taken or absent expert), NaN above all.
+// Ties go to the lower expert id, as the router's 64-bit keys order them.
+__device__ __forceinline__ uint32_t score_key32(float s) {
+  return isnan(s) ? 0xffffffffu : __float_as_uint(s) + 1u;
+}
+__device__ __forceinline__ float key32_score(uint32_t k) {
+  return __uint_as_float(k == 0xffffffffu ? k : k - 1u);
+}
 
 __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs A, Plan P) {
   extern __shared__ __align__(128) uint8_t rs[];
@@ -749,33 +774,40 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   const int ncta = static_cast<int>(cluster.num_blocks());
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = A.T, D = A.D, E = A.E, K = A.K;
+  const bool hash = A.tid2eid != nullptr;
+  const bool norm = A.norm_w != nullptr;
   const int RS = RouteSmem::stride(D);
   __nv_bfloat16* gw = reinterpret_cast<__nv_bfloat16*>(rs + RouteSmem::gw(D));
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rs + RouteSmem::xs(D));
+  __nv_bfloat16* nw = reinterpret_cast<__nv_bfloat16*>(rs + RouteSmem::nw(D));
   float* red = reinterpret_cast<float*>(rs + RouteSmem::red(D));
-  uint64_t* keys = reinterpret_cast<uint64_t*>(rs + RouteSmem::keys(D));
+  uint32_t* keys = reinterpret_cast<uint32_t*>(rs + RouteSmem::keys(D));
   int64_t* sI = reinterpret_cast<int64_t*>(rs + RouteSmem::top(D));  // [T][K] selections
   float* sW = reinterpret_cast<float*>(sI + 8 * 16);                 // [T][K] weights
   uint32_t* emask = reinterpret_cast<uint32_t*>(sW + 8 * 16);         // 256-bit expert bitmap (CTA 0)
   int* rowe = reinterpret_cast<int*>(emask + 8);                      // [8] row prescale exponents
   float* biasv = reinterpret_cast<float*>(rowe + 8);                  // [16] this CTA's biases
+  float* rinv = biasv + 16;                                           // [8] 1 / rms of each row
+  float* wpart = rinv + 8;                                            // [8 warps][8 rows] sums of squares
   uint64_t* bar = reinterpret_cast<uint64_t*>(rs + RouteSmem::bar(D));
   const int e0 = rank * 16;
   const uint32_t rowb = static_cast<uint32_t>(D) * 2;
+  const int nv = D / 8;  // 16-byte vectors per row
 
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0) {  // the gate slice does not depend on the previous kernel: start it now
-    mbar_arrive_expect_tx(bar, rowb * (16 + T));
-    for (int r = 0; r < 16; ++r)
-      bulk_load(gw + r * RS, A.gate + static_cast<int64_t>(e0 + r) * D, rowb, bar);
+  if (tid == 0) {  // parameters do not depend on the previous kernel: start them now
+    mbar_arrive_expect_tx(bar, rowb * ((hash ? 0 : 16) + (norm ? 1 : 0) + T));
+    if (!hash)
+      for (int r = 0; r < 16; ++r) bulk_load(gw + r * RS, A.gate + static_cast<int64_t>(e0 + r) * D, rowb, bar);
+    if (norm) bulk_load(nw, A.norm_w, rowb, bar);
   }
-  if (tid < 16) biasv[tid] = A.bias ? __bfloat162float(A.bias[e0 + tid]) : 0.f;
+  if (tid < 16) biasv[tid] = (!hash && A.bias) ? __bfloat162float(A.bias[e0 + tid]) : 0.f;
   pdl_trigger();
-  pdl_wait();  // the normed rows (and everything earlier) are complete
+  pdl_wait();  // the rows (and everything earlier) are complete
   if (tid == 0)
     for (int t = 0; t < T; ++t) bulk_load(xs + t * RS, A.x + static_cast<int64_t>(t) * D, rowb, bar);
   // clear this kernel's share of the tickets and token tables meanwhile
@@ -787,32 +819,112 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     P.ctab_wb[i] = 0.f;
     P.ctab_sb[i] = 127;
   }
-  if (rank == 0 && tid < 8) emask[tid] = 0u;
-  const bool ok = mbar_wait(bar, 0);
+  if (rank == 0) {
+    if (tid < 8) emask[tid] = 0u;
+    if (hash && tid < T * K) {  // hash routing: tid2eid[id], weight 1/K (engine.py:1018-1023)
+      const int t = tid / K, j = tid - t * K;
+      const int64_t id = A.ids[t];
+      int64_t e = -1;
+      if (id < 0 || id >= A.V)
+        report(A.status, HS_DEV_BAD_TOKEN);
+      else
+        e = A.tid2eid[id * K + j];
+      const float hw = A.scaling;  // hash mode: the host passes 1/K
+      A.idx_out[tid] = e;
+      A.w_out[tid] = hw;
+      if (e >= E) {
+        report(A.status, HS_DEV_BAD_EXPERT);
+        e = -1;
+      }
+      sI[tid] = e;
+      sW[tid] = hw;
+    }
+  }
+  bool ok = mbar_wait(bar, 0);
+  if (!ok) {  // report, and let the copies land before the shared memory is reused or released
+    report(A.status, HS_DEV_TIMEOUT);
+    (void)mbar_wait(bar, 0);
+  }
+  ok = __syncthreads_and(ok) != 0;  // uniform over the CTA (barriers follow)
 
-  // ---- logits: chunk (split s, quarter q) of 128 columns per warp iteration ----
+  // ---- RMSNorm of every row, the standalone norm kernel's summation order ----
+  if (norm && ok) {
+    float ss[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) ss[t] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; ++i) {
+      const int j = tid + i * kRouteThreads;
+      if (j < nv)
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          if (t < T) {
+            float v[8];
+            bf16x8_unpack(reinterpret_cast<const uint4*>(xs + t * RS)[j], v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ss[t] = __fadd_rn(ss[t], __fmul_rn(v[k], v[k]));
+          }
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss[t] = __fadd_rn(ss[t], __shfl_xor_sync(0xffffffffu, ss[t], o));
+    if (lane == 0)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) wpart[warp * 8 + t] = ss[t];
+    __syncthreads();
+    if (tid < T) {
+      float tot = 0.f;
+      for (int w = 0; w < kRouteThreads / 32; ++w) tot = __fadd_rn(tot, wpart[w * 8 + tid]);
+      const float var = __fdiv_rn(tot, static_cast<float>(D));
+      rinv[tid] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, A.eps)));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; ++i) {
+      const int j = tid + i * kRouteThreads;
+      if (j < nv) {
+        float wf[8];
+        bf16x8_unpack(reinterpret_cast<const uint4*>(nw)[j], wf);
+        for (int t = 0; t < T; ++t) {
+          uint4* p = reinterpret_cast<uint4*>(xs + t * RS) + j;
+          float v[8], o[8];
+          bf16x8_unpack(*p, v);
+          const float ri = rinv[t];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(wf[k], __fmul_rn(v[k], ri));
+          *p = bf16x8_pack(o);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- logits: warp s sums the four 128-column quarters of k-split s in order ----
   const int nsplit = D / router::kKSplitCols;
-  const int g = lane >> 2;
-  if (ok) {
-    for (int ch = warp; ch < 4 * nsplit; ch += kRouteThreads / 32) {
-      const int sp = ch >> 2, q = ch & 3;
+  if (!hash && ok && warp < nsplit) {
+    const int g = lane >> 2;
+    float s4[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
       float acc[4];
       router::logit_chunk(gw + g * RS, gw + (g + 8) * RS, xs + (g < T ? g : 0) * RS, g < T,
-                          sp * router::kKSplitCols + q * 128, acc);
+                          warp * router::kKSplitCols + q * 128, acc);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) red[((sp * 4 + q) * 32 + lane) * 4 + j] = acc[j];
+      for (int j = 0; j < 4; ++j) s4[j] = q == 0 ? acc[j] : s4[j] + acc[j];
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red[(warp * 32 + lane) * 4 + j] = s4[j];
   }
   // row prescale of every token, one warp per token (each CTA needs it for its x8 slice)
   if (warp < T) {
     const uint4* row = reinterpret_cast<const uint4*>(xs + warp * RS);
     float mx = 0.f;
-    for (int v = lane; v < D / 8; v += 32) {
-      const uint4 u = row[v];
-      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+    for (int v = lane; v < nv; v += 32) {
+      float f[8];
+      bf16x8_unpack(row[v], f);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(w4[i] << 16)), fabsf(__uint_as_float(w4[i] & 0xffff0000u))));
+      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(f[i]));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -828,24 +940,20 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     }
   }
   __syncthreads();
-  // (expert, token) of the 16 x 8 fragment: the logit (quarters in order, then
-  // k-splits in order: the router's order), its score sqrt(softplus(bf16(bf16(l)
-  // + bias))) and selection key, to CTA 0
-  if (tid < 128) {
+  // (expert, token) of the 16 x 8 fragment: the logit (k-splits in order), its
+  // score sqrt(softplus(bf16(bf16(l) + bias))) and selection key, to CTA 0
+  if (!hash && tid < 128) {
     const int ln = tid & 31, j = tid >> 5;
     const int el = (ln >> 2) + ((j & 2) ? 8 : 0), t = 2 * (ln & 3) + (j & 1);
     float l = 0.f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float* r = red + (sp * 4 * 32 + ln) * 4 + j;
-      l += ((r[0] + r[32 * 4]) + r[2 * 32 * 4]) + r[3 * 32 * 4];
-    }
+    for (int sp = 0; sp < nsplit; ++sp) l += red[(sp * 32 + ln) * 4 + j];
     float lb = round_bf16(l);
     if (A.bias) lb = round_bf16(lb + biasv[el]);
     const float sp = lb > 20.f ? lb : log1pf(expf(lb));
     const float sc = sqrtf(sp);
-    if (t < T) cluster.map_shared_rank(keys, 0)[t * 256 + e0 + el] = router::score_key(sc, e0 + el);
+    if (t < T) cluster.map_shared_rank(keys, 0)[t * 256 + e0 + el] = score_key32(sc);
   }
-  // this CTA's columns of the token rows' hi/lo e4m3 split
+  // this CTA's columns of the normed rows and of their hi/lo e4m3 split
   {
     const int cols = D / ncta, c0 = rank * cols;
     for (int i = tid; i < T * (cols / 16); i += kRouteThreads) {
@@ -855,37 +963,43 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       split16(src[2 * k16], src[2 * k16 + 1], exp2i(rowe[t]), hv, lv);
       reinterpret_cast<uint4*>(P.x8 + static_cast<int64_t>(t) * D)[k16] = hv;
       reinterpret_cast<uint4*>(P.x8 + (A.P_max + t) * D)[k16] = lv;
+      if (A.x_out) {
+        uint4* xo = reinterpret_cast<uint4*>(A.x_out + static_cast<int64_t>(t) * D);
+        xo[2 * k16] = src[2 * k16];
+        xo[2 * k16 + 1] = src[2 * k16 + 1];
+      }
     }
   }
   cluster.sync();
   if (rank != 0) return;
 
   // ---- CTA 0: the router's top-k selection from the gathered keys ----
-  if (warp < T) {
+  if (!hash && warp < T) {
     const int t = warp;
-    uint64_t key[8];
+    uint32_t key[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int e = lane + 32 * i;
-      key[i] = e < E ? keys[t * 256 + e] : 0ull;
+      key[i] = e < E ? keys[t * 256 + e] : 0u;
     }
     float wsum = 0.f, wsel = 0.f;
     int esel = 0;
     for (int r = 0; r < K; ++r) {
-      uint64_t best = 0ull;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) best = key[i] > best ? key[i] : best;
-      uint64_t wb = best;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const uint64_t other = __shfl_xor_sync(0xffffffffu, wb, o);
-        wb = other > wb ? other : wb;
-      }
-      const int e = static_cast<int>(0xffffffffu - static_cast<uint32_t>(wb & 0xffffffffull));
+      // this lane's best (the lowest id among equal keys), then the warp's
+      uint32_t best = 0u;
+      int be = 0x7fffffff;
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (key[i] == wb) key[i] = 0ull;
-      const float s = __uint_as_float(static_cast<uint32_t>(wb >> 32));
+        if (key[i] > best) {
+          best = key[i];
+          be = lane + 32 * i;
+        }
+      const uint32_t m = __reduce_max_sync(0xffffffffu, best);
+      const int e = __reduce_min_sync(0xffffffffu, (best == m && m != 0u) ? be : 0x7fffffff);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (lane + 32 * i == e) key[i] = 0u;
+      const float s = key32_score(m);
       wsum += s;  // selection order, as the router
       if (lane == r) {
         wsel = s;
@@ -900,10 +1014,10 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       A.idx_out[t * K + lane] = esel;
       A.w_out[t * K + lane] = wv;
     }
-    if (lane == 0) {
-      P.sb1[t] = static_cast<uint8_t>(127 - rowe[t]);
-      P.tok_e[t] = rowe[t];
-    }
+  }
+  if (tid < T) {
+    P.sb1[tid] = static_cast<uint8_t>(127 - rowe[tid]);
+    P.tok_e[tid] = rowe[tid];
   }
   __syncthreads();
 
@@ -967,6 +1081,10 @@ struct UnitArgs {
   float* out_f32;
   float* shared_f32;     // partials mode: the shared expert's f32 output (or nullptr)
   int partials;          // 1: write un-rounded f32 routed / shared sums only (no bf16 out)
+  // token-mode down phase: the layer's residual add, resid_out = bf16(resid +
+  // out) (engine.py:2685; resid_out may alias resid); out may then be nullptr
+  const __nv_bfloat16* resid;
+  __nv_bfloat16* resid_out;
   int32_t* status;
   // stream-K schedule
   int G;                 // persistent CTAs (kCtasPerSm per SM)
@@ -1128,6 +1246,22 @@ __device__ __forceinline__ void finalize_tile(const UnitArgs& a, int D, int tile
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// One element of the MoE output from its routed and shared f32 sums:
+// bf16(bf16(routed) + bf16(shared)) (engine.py:1530-1536), and the residual
+// add when the call carries one.
+__device__ __forceinline__ void store_out(const UnitArgs& a, int64_t o_i, float r, float h) {
+  if (a.out_f32) a.out_f32[o_i] = r;
+  if (a.partials) {
+    if (a.shared_f32) a.shared_f32[o_i] = h;
+    return;
+  }
+  float o = round_bf16(r);
+  if (a.use_shared) o += round_bf16(h);
+  const __nv_bfloat16 y = __float2bfloat16_rn(o);
+  if (a.out) a.out[o_i] = y;
+  if (a.resid_out) a.resid_out[o_i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(a.resid[o_i]), __bfloat162float(y)));
+}
 
 // Gate/up epilogue of one 128-row unit from the summed accumulators.
 template <int NT, bool kFP8>
@@ -2029,29 +2163,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
         const int64_t dd = u * kM + row;
 #pragma unroll
         for (int t = 0; t < 8; ++t)
-          if (t < a.T) {
-            const int64_t o_i = t * static_cast<int64_t>(D) + dd;
-            if (a.out_f32) a.out_f32[o_i] = r[t];
-            if (a.partials) {
-              if (a.shared_f32) a.shared_f32[o_i] = h[t];
-              continue;
-            }
-            float o = round_bf16(r[t]);
-            if (a.use_shared) o += round_bf16(h[t]);
-            a.out[o_i] = __float2bfloat16_rn(o);
-          }
+          if (t < a.T) store_out(a, t * static_cast<int64_t>(D) + dd, r[t], h[t]);
       }
       s = us + k1;
     }
     // nothing to compute (every pair skipped, no shared expert): zeros
     if (!any)
       for (int tile = c; tile < D / kM; tile += sc.G)
-        for (int t = 0; t < a.T; ++t) {
-          const int64_t o = t * static_cast<int64_t>(D) + tile * kM + etid;
-          if (a.out_f32) a.out_f32[o] = 0.f;
-          if (a.shared_f32) a.shared_f32[o] = 0.f;
-          if (!a.partials) a.out[o] = __float2bfloat16_rn(0.f);
-        }
+        for (int t = 0; t < a.T; ++t) store_out(a, t * static_cast<int64_t>(D) + tile * kM + etid, 0.f, 0.f);
   }
 
   if constexpr (kCl) {
@@ -2077,17 +2196,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
         rs += vr[q];
         hs += vh[q];
       }
-      if (t < a.T) {
-        const int64_t o_i = t * static_cast<int64_t>(D) + (c / 8) * kM + rowc;
-        if (a.out_f32) a.out_f32[o_i] = rs;
-        if (a.partials) {
-          if (a.shared_f32) a.shared_f32[o_i] = hs;
-        } else {
-          float o = round_bf16(rs);
-          if (a.use_shared) o += round_bf16(hs);
-          a.out[o_i] = __float2bfloat16_rn(o);
-        }
-      }
+      if (t < a.T) store_out(a, t * static_cast<int64_t>(D) + (c / 8) * kM + rowc, rs, hs);
     }
     cluster.sync();  // peers have read this CTA's shared memory
   }
@@ -2365,6 +2474,15 @@ struct RouteIn {
   float scaling;
   int64_t* idx_out;
   float* w_out;
+  // the layer form: rows are the residual stream, normed in the route kernel,
+  // and the down phase adds the MoE output back (norm_w == nullptr: normed rows)
+  const void* norm_w = nullptr;
+  float eps = 0.f;
+  void* x_out = nullptr;
+  void* h_out = nullptr;
+  const int64_t* ids = nullptr;      // hash routing when tid2eid is set
+  const int64_t* tid2eid = nullptr;
+  int64_t vocab = 0;
 };
 
 static int launch_route(const RouteArgs& ra, const Plan& P, cudaStream_t st) {
@@ -2398,15 +2516,22 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   if (T > (1 << 20)) return HS_ERR_BAD_SHAPE;
   if (!hidden || !workspace) return HS_ERR_BAD_ARGUMENT;
   if (!route && (!topk_idx || !topk_w)) return HS_ERR_BAD_ARGUMENT;
+  const bool layer = route && route->norm_w;
   if (route) {
     const int64_t Er = route->num_experts;
+    const bool hash = route->tid2eid != nullptr;
     if (T > kTokMax || Er < 16 || Er > 256 || Er % 16 || d.D > kRouteMaxD || d.D % (Er / 16 * 16) ||
-        route->expert_offset < 0 || route->expert_offset + d.E > Er)
+        (!hash && d.D % router::kKSplitCols) || top_k > Er || route->expert_offset < 0 ||
+        route->expert_offset + d.E > Er)
       return HS_ERR_UNSUPPORTED;
-    if (!route->gate || !route->idx_out || !route->w_out) return HS_ERR_BAD_ARGUMENT;
-    if (!aligned16(route->gate)) return HS_ERR_ALIGN;
+    if ((!hash && !route->gate) || (hash && (!route->ids || route->vocab < 1)) || !route->idx_out || !route->w_out)
+      return HS_ERR_BAD_ARGUMENT;
+    if ((route->gate && !aligned16(route->gate)) || (route->norm_w && !aligned16(route->norm_w)) ||
+        (route->x_out && !aligned16(route->x_out)))
+      return HS_ERR_ALIGN;
+    if (layer && !partials && !route->h_out) return HS_ERR_BAD_ARGUMENT;
   }
-  if (partials ? !out_f32 : !out) return HS_ERR_BAD_ARGUMENT;
+  if (partials ? !out_f32 : (!out && !(layer && route->h_out))) return HS_ERR_BAD_ARGUMENT;
   if (dup_mode != HS_DUP_LAST && dup_mode != HS_DUP_SUM) return HS_ERR_BAD_ARGUMENT;
   if (!aligned16(hidden) || (out && !aligned16(out)) || !aligned16(workspace) || (out_f32 && !aligned16(out_f32)) ||
       (shared_f32 && !aligned16(shared_f32)))
@@ -2454,14 +2579,23 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   pa.n_ucount = g.U_gu + g.U_dn;
   if (route) {
     RouteArgs ra;
+    const bool hash = route->tid2eid != nullptr;
     ra.x = static_cast<const __nv_bfloat16*>(hidden);
-    ra.gate = static_cast<const __nv_bfloat16*>(route->gate);
-    ra.bias = static_cast<const __nv_bfloat16*>(route->bias);
+    ra.norm_w = static_cast<const __nv_bfloat16*>(route->norm_w);
+    ra.eps = route->eps;
+    ra.x_out = static_cast<__nv_bfloat16*>(route->x_out);
+    ra.gate = hash ? nullptr : static_cast<const __nv_bfloat16*>(route->gate);
+    ra.bias = hash ? nullptr : static_cast<const __nv_bfloat16*>(route->bias);
+    ra.ids = route->ids;
+    ra.tid2eid = route->tid2eid;
+    ra.V = route->vocab;
     ra.T = static_cast<int>(T);
     ra.D = d.D;
     ra.E = static_cast<int>(route->num_experts);
     ra.K = static_cast<int>(top_k);
-    ra.scaling = route->scaling;
+    // hash weights: torch.full(..., 1.0 / k) with a float32 default dtype
+    ra.scaling = hash ? static_cast<float>(1.0 / static_cast<double>(top_k)) : route->scaling;
+    ra.status = dev_status;
     ra.dup_mode = dup_mode;
     ra.offset = static_cast<int>(route->expert_offset);
     ra.held = d.E;
@@ -2493,6 +2627,8 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   a.out_f32 = out_f32;
   a.shared_f32 = partials && use_shared ? shared_f32 : nullptr;
   a.partials = partials;
+  a.resid = layer && !partials ? static_cast<const __nv_bfloat16*>(hidden) : nullptr;
+  a.resid_out = layer && !partials ? static_cast<__nv_bfloat16*>(route->h_out) : nullptr;
   a.status = dev_status;
   a.G = g.G;
   a.aligned = g.aligned;
@@ -2535,6 +2671,44 @@ extern "C" int hs_moe_route_ffn_fp4_partials(const void* desc, const void* hidde
   const RouteIn r{gate, bias, num_experts, expert_offset, routed_scaling, topk_idx, topk_w};
   return moe_ffn_impl(desc, hidden, nullptr, nullptr, T, top_k, use_shared, dup_mode, nullptr, routed_f32,
                       shared_f32, 1, workspace, workspace_bytes, dev_status, stream, &r);
+}
+
+extern "C" int hs_moe_layer_fp4(const void* desc, const void* h, const void* norm_w, float eps, const void* gate,
+                                const void* bias, const int64_t* input_ids, const int64_t* tid2eid, int64_t vocab,
+                                int64_t num_experts, int64_t expert_offset, int64_t T, int64_t top_k,
+                                float routed_scaling, int use_shared, int dup_mode, int64_t* topk_idx, float* topk_w,
+                                void* x_out, void* h_out, void* workspace, size_t workspace_bytes,
+                                int32_t* dev_status, void* stream) {
+  if (!norm_w || !h_out) return HS_ERR_BAD_ARGUMENT;
+  RouteIn r{gate, bias, num_experts, expert_offset, routed_scaling, topk_idx, topk_w};
+  r.norm_w = norm_w;
+  r.eps = eps;
+  r.x_out = x_out;
+  r.h_out = h_out;
+  r.ids = input_ids;
+  r.tid2eid = tid2eid;
+  r.vocab = vocab;
+  return moe_ffn_impl(desc, h, nullptr, nullptr, T, top_k, use_shared, dup_mode, nullptr, nullptr, nullptr, 0,
+                      workspace, workspace_bytes, dev_status, stream, &r);
+}
+
+extern "C" int hs_moe_layer_fp4_partials(const void* desc, const void* h, const void* norm_w, float eps,
+                                         const void* gate, const void* bias, const int64_t* input_ids,
+                                         const int64_t* tid2eid, int64_t vocab, int64_t num_experts,
+                                         int64_t expert_offset, int64_t T, int64_t top_k, float routed_scaling,
+                                         int use_shared, int dup_mode, int64_t* topk_idx, float* topk_w,
+                                         void* x_out, float* routed_f32, float* shared_f32, void* workspace,
+                                         size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  if (!norm_w) return HS_ERR_BAD_ARGUMENT;
+  RouteIn r{gate, bias, num_experts, expert_offset, routed_scaling, topk_idx, topk_w};
+  r.norm_w = norm_w;
+  r.eps = eps;
+  r.x_out = x_out;
+  r.ids = input_ids;
+  r.tid2eid = tid2eid;
+  r.vocab = vocab;
+  return moe_ffn_impl(desc, h, nullptr, nullptr, T, top_k, use_shared, dup_mode, nullptr, routed_f32, shared_f32, 1,
+                      workspace, workspace_bytes, dev_status, stream, &r);
 }
 
 extern "C" int hs_moe_ffn_fp4_partials(const void* desc, const void* hidden, const int64_t* topk_idx,

@@ -21,28 +21,8 @@
 namespace hs {
 namespace norm {
 
-constexpr int kThreads = 256;
-constexpr int kMaxVec = 4;  // 8 bf16 per vector: D <= kThreads * 8 * kMaxVec = 8192
-
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
-}
-
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i]));
-    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1]));
-    w[i] = lo | (hi << 16);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
+constexpr int kThreads = kNormThreads;
+constexpr int kMaxVec = kNormMaxVec;  // 8 bf16 per vector: D <= kThreads * 8 * kMaxVec = 8192
 
 // The MoE output from un-rounded f32 partial sums (already summed over
 // expert-parallel ranks): bf16(bf16(routed) + bf16(shared)), the rounding the
@@ -79,21 +59,22 @@ __global__ void __launch_bounds__(kThreads) add_norm_kernel(const __nv_bfloat16*
   for (int i = 0; i < kMaxVec; ++i) {
     const int j = threadIdx.x + i * kThreads;
     if (j < nv) {
-      unpack8(hr[j], v[i]);
+      bf16x8_unpack(hr[j], v[i]);
       if (kMode != 0) {
         float g[8];
         if (kMode == 1)
-          unpack8(reinterpret_cast<const uint4*>(y + row)[j], g);
+          bf16x8_unpack(reinterpret_cast<const uint4*>(y + row)[j], g);
         else
           combine8(r, sh, row + 8 * static_cast<int64_t>(j), use_shared != 0, g);
 #pragma unroll
         for (int k = 0; k < 8; ++k) v[i][k] = round_bf16(__fadd_rn(v[i][k], g[k]));
-        reinterpret_cast<uint4*>(h_out + row)[j] = pack8(v[i]);
+        reinterpret_cast<uint4*>(h_out + row)[j] = bf16x8_pack(v[i]);
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k) ss = __fadd_rn(ss, __fmul_rn(v[i][k], v[i][k]));
     }
   }
+  if (kMode != 0 && x_out == nullptr) return;  // the residual add alone (uniform over the CTA)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
   __shared__ float part[kThreads / 32];
@@ -114,10 +95,10 @@ __global__ void __launch_bounds__(kThreads) add_norm_kernel(const __nv_bfloat16*
     const int j = threadIdx.x + i * kThreads;
     if (j < nv) {
       float wf[8], o[8];
-      unpack8(wr[j], wf);
+      bf16x8_unpack(wr[j], wf);
 #pragma unroll
       for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(wf[k], __fmul_rn(v[i][k], ri));
-      reinterpret_cast<uint4*>(x_out + row)[j] = pack8(o);
+      reinterpret_cast<uint4*>(x_out + row)[j] = bf16x8_pack(o);
     }
   }
 }
@@ -126,9 +107,12 @@ static int launch(int mode, const void* h, const void* y, const float* r, const 
                   const void* w, float eps, int64_t T, int64_t D, void* h_out, void* x_out, void* stream) {
   if (T < 0 || D < 8 || D % 8 != 0 || D > kThreads * 8 * kMaxVec || T > (1 << 24)) return HS_ERR_BAD_SHAPE;
   if (T == 0) return HS_OK;
-  if (!h || !w || !x_out || (mode != 0 && !h_out) || (mode == 1 && !y) || (mode == 2 && (!r || (use_shared && !sh))))
+  // modes 1 and 2 may leave out the norm (w and x_out both NULL): the add alone
+  const bool no_norm = mode != 0 && !w && !x_out;
+  if (!h || (!no_norm && (!w || !x_out)) || (mode != 0 && !h_out) || (mode == 1 && !y) ||
+      (mode == 2 && (!r || (use_shared && !sh))))
     return HS_ERR_BAD_ARGUMENT;
-  if (!aligned16(h) || !aligned16(w) || !aligned16(x_out) || (h_out && !aligned16(h_out)) || (y && !aligned16(y)) ||
+  if (!aligned16(h) || (w && !aligned16(w)) || (x_out && !aligned16(x_out)) || (h_out && !aligned16(h_out)) || (y && !aligned16(y)) ||
       (r && !aligned16(r)) || (sh && !aligned16(sh)))
     return HS_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -156,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(const float* __restri
        j += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float o[8];
     combine8(r, sh, 8 * j, use_shared != 0, o);
-    reinterpret_cast<uint4*>(out)[j] = pack8(o);
+    reinterpret_cast<uint4*>(out)[j] = bf16x8_pack(o);
   }
 }
 

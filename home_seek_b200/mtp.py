@@ -7,8 +7,9 @@ Reference: HomeSeekInferenceEngine.generate's decode loop
 
 What runs per layer here is the part of `_forward_layer` this build owns:
 rms_norm -> router (or hash routing for layers < num_hash_layers) -> routed FP4
-experts + FP8 shared expert (one fused kernel sequence) -> residual add, the
-add fused with the next layer's norm (hs_add_rms_norm).
+experts + FP8 shared expert -> residual add. At decode sizes (T <= 8) that is
+one call, hs_moe_layer_fp4, of three launches: the norm runs in the routing
+cluster and the residual add in the down phase's epilogue.
 Attention and the MHC hyper-connections stay on the reference's PyTorch path
 and are not part of this module; the layer body is therefore
 h <- h + MoE(rms_norm(h)). The draft layer is the MTP block's projections
@@ -119,6 +120,26 @@ class MoEPathModel:
             return self.ep.partials(st, layer, x, idx, w, dup)
         return ops.moe_ffn(st.desc(layer), st.dims, x, idx, w, use_shared=True, dup_mode=dup)
 
+    def layer(self, h: torch.Tensor, layer: int, ids: torch.Tensor,
+              h_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """h + MoE(rms_norm(h, ln_w[layer])) for T <= 8 rows (into h_out when
+        given, which may be h): one hs_moe_layer_fp4 call, or under expert
+        parallelism the partials form, an all-reduce and the combine + add."""
+        s = self.shape
+        st = self.store
+        lw = st.layers[layer]
+        dup = HS_DUP_SUM if h.shape[0] == 1 else HS_DUP_LAST
+        hashed = layer < s.hash_layers and lw.tid2eid is not None
+        kw = {"ids": ids, "tid2eid": lw.tid2eid} if hashed else {}
+        gate, bias = (None, None) if hashed else (lw.gate, lw.bias)
+        args = (st.desc(layer), st.dims, h, self.ln_w[layer], gate, bias, s.top_k, s.routed_scaling)
+        if self.ep is not None:
+            buf, _, _ = ops.moe_layer(*args, dup_mode=dup, num_experts=s.num_experts,
+                                      expert_offset=st.expert_offset, partials=True, **kw)
+            self.ep.all_reduce(buf)
+            return ops.moe_combine_add_rms_norm(buf, h, None, h_out=h_out)[0]
+        return ops.moe_layer(*args, dup_mode=dup, num_experts=s.num_experts, h_out=h_out, **kw)[0]
+
     def _add_norm(self, h: torch.Tensor, y: torch.Tensor, w: torch.Tensor, in_place: bool,
                   x_out: Optional[torch.Tensor] = None):
         """Residual add of the MoE output y (bf16, or [2, T, D] f32 partials under
@@ -133,10 +154,15 @@ class MoEPathModel:
 
     def forward(self, ids: torch.Tensor):
         """All layers for tokens `ids`: returns (h, x) with h the residual stream
-        after the last layer and x = rms_norm(h, final norm). Each layer's
-        residual add is fused with the next layer's input norm (one launch)."""
+        after the last layer and x = rms_norm(h, final norm). At T <= 8 each
+        layer is one hs_moe_layer_fp4 call updating h in place; above, each
+        layer's residual add is fused with the next layer's input norm."""
         L = self.shape.num_layers
         h = self.embed[ids]
+        if ids.shape[0] <= 8:
+            for layer in range(L):
+                self.layer(h, layer, ids, h_out=h)
+            return h, ops.rms_norm(h, self.norm_w)
         x = ops.rms_norm(h, self.ln_w[0])
         for layer in range(L):
             y = self.moe(x, layer, ids)
@@ -158,8 +184,8 @@ class MoEPathModel:
         for _ in range(s.num_draft):
             e = ops.rms_norm(self.embed[t], self.enorm_w) @ self.e_proj.t()
             hc = ops.rms_norm(prev, self.hnorm_w) @ self.h_proj.t() + e
-            y = self.moe(ops.rms_norm(hc, self.ln_w[L]), L, t)
-            hm, xm = self._add_norm(hc, y, self.mtp_norm_w, in_place=False)
+            hm = self.layer(hc, L, t)
+            xm = ops.rms_norm(hm, self.mtp_norm_w)
             lg = xm @ self.lm_head.t()
             _, t = ops.accept_greedy(lg.view(1, 1, -1), torch.empty(1, 0, dtype=torch.int64, device=lg.device))
             out.append(t)

@@ -22,7 +22,7 @@ _KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_mo
             "hs_moe_unpermute": 1, "hs_accept_greedy": 1, "hs_accept_rejection": 1, "hs_fill_bytes": 1,
             "hs_rms_norm": 1, "hs_add_rms_norm": 1, "hs_moe_ffn_fp4_partials": 3, "hs_moe_combine": 1,
             "hs_moe_route_ffn_fp4": 3, "hs_moe_route_ffn_fp4_partials": 3,
-            "hs_moe_combine_add_rms_norm": 1}
+            "hs_moe_combine_add_rms_norm": 1, "hs_moe_layer_fp4": 3, "hs_moe_layer_fp4_partials": 3}
 
 
 def _launch(name: str, *args, extra: int = 0) -> None:
@@ -68,11 +68,13 @@ def workspace(device: torch.device, nbytes: int, tag: str) -> torch.Tensor:
 
 
 def status_word(device: torch.device) -> torch.Tensor:
-    """Device int32 that kernels OR HS_DEV_* bits into; read with check_status()."""
-    s = _status.get(device.index)
+    """Device int32 that kernels OR HS_DEV_* bits into; read with check_status().
+    One word per GPU: torch.device("cuda") means the current device."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    s = _status.get(idx)
     if s is None:
-        s = torch.zeros(1, dtype=torch.int32, device=device)
-        _status[device.index] = s
+        s = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = s
     return s
 
 
@@ -242,6 +244,55 @@ def moe_route_ffn(desc: ctypes.Array, dims: tuple, hidden: torch.Tensor, gate: t
     return out, idx, w
 
 
+def moe_layer(desc: ctypes.Array, dims: tuple, h: torch.Tensor, norm_w: torch.Tensor,
+              gate: Optional[torch.Tensor], bias: Optional[torch.Tensor], top_k: int, routed_scaling: float,
+              eps: float = 1e-6, use_shared: bool = True, dup_mode: int = _lib.HS_DUP_LAST,
+              num_experts: Optional[int] = None, expert_offset: int = 0, ids: Optional[torch.Tensor] = None,
+              tid2eid: Optional[torch.Tensor] = None, h_out: Optional[torch.Tensor] = None,
+              x_out: Optional[torch.Tensor] = None, partials: bool = False, out: Optional[torch.Tensor] = None):
+    """The MoE half of a decode layer for T <= 8 (hs_moe_layer_fp4):
+    h_out = h + MoE(rms_norm(h, norm_w)), routed by the router (gate, bias) or,
+    with tid2eid, by hash of ids. Returns (h_out, topk_idx, topk_w); h_out may
+    be h. With partials the first value is the [2, T, D] f32 partial sums of
+    this store's experts (expert parallelism) and h is left untouched."""
+    dev = _check_cuda(h, norm_w, gate, bias, ids, tid2eid, h_out, x_out, out)
+    h = _rows(h, "h")
+    norm_w = _rows(norm_w, "norm_w")
+    T, D = h.shape
+    E, Dd, I, I_sh = dims
+    if D != Dd:
+        raise ValueError(f"hidden dim {D} != store dim {Dd}")
+    if tid2eid is None and (gate is None or gate.dtype != torch.bfloat16):
+        raise TypeError("router mode needs a bf16 gate")
+    if tid2eid is not None and (ids is None or ids.dtype != torch.int64 or tid2eid.dtype != torch.int64):
+        raise TypeError("hash mode needs int64 ids and tid2eid")
+    n_exp = int(num_experts if num_experts is not None else (gate.shape[0] if gate is not None else E))
+    idx = torch.empty(T, top_k, dtype=torch.int64, device=dev)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws = workspace(dev, lib.hs_moe_workspace_size(T, top_k, D, I, I_sh), "moe")
+    use_shared = bool(use_shared) and bool(I_sh)
+    ids_c = ids.reshape(-1).contiguous() if ids is not None else None
+    vocab = int(tid2eid.shape[0]) if tid2eid is not None else 0
+    route = (ctypes.addressof(desc), h.data_ptr(), norm_w.data_ptr(), float(eps),
+             None if tid2eid is not None else gate.data_ptr(), None if tid2eid is not None else _ptr(bias),
+             _ptr(ids_c), _ptr(tid2eid), vocab, n_exp, int(expert_offset), T, top_k, float(routed_scaling),
+             int(use_shared), int(dup_mode), idx.data_ptr(), w.data_ptr(), _ptr(x_out))
+    if partials:
+        if out is None:
+            out = torch.empty(2, T, D, dtype=torch.float32, device=dev)
+        if not use_shared:
+            out[1].zero_()
+        _launch("hs_moe_layer_fp4_partials", *route, out[0].data_ptr(), out[1].data_ptr() if use_shared else None,
+                ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(), _stream(dev))
+        return out, idx, w
+    if h_out is None:
+        h_out = torch.empty_like(h)
+    _launch("hs_moe_layer_fp4", *route, h_out.data_ptr(), ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(),
+            _stream(dev))
+    return h_out, idx, w
+
+
 def moe_combine(partials: torch.Tensor, use_shared: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """bf16(bf16(routed) + bf16(shared)) from summed f32 partials [2, T, D]."""
     dev = _check_cuda(partials, out)
@@ -257,17 +308,19 @@ def moe_combine_add_rms_norm(partials: torch.Tensor, h: torch.Tensor, w: torch.T
                              use_shared: bool = True, h_out: Optional[torch.Tensor] = None,
                              x_out: Optional[torch.Tensor] = None):
     """Combine f32 partials [2, T, D], add to the residual stream h and normalise:
-    returns (h + combine, rms_norm(h + combine, w)). h_out may be h."""
+    returns (h + combine, rms_norm(h + combine, w)). h_out may be h. With w
+    None the norm is left out: returns (h + combine, None)."""
     dev = _check_cuda(partials, h, w, h_out, x_out)
     h = _rows(h, "h")
-    w = _rows(w, "w")
+    if w is not None:
+        w = _rows(w, "w")
     _, T, D = partials.shape
     if h_out is None:
         h_out = torch.empty_like(h)
-    if x_out is None:
+    if x_out is None and w is not None:
         x_out = torch.empty_like(h)
     _launch("hs_moe_combine_add_rms_norm", partials[0].data_ptr(), partials[1].data_ptr(), int(bool(use_shared)),
-            h.data_ptr(), w.data_ptr(), float(eps), T, D, h_out.data_ptr(), x_out.data_ptr(), _stream(dev))
+            h.data_ptr(), _ptr(w), float(eps), T, D, h_out.data_ptr(), _ptr(x_out), _stream(dev))
     return h_out, x_out
 
 

@@ -226,6 +226,7 @@ int hs_accept_rejection(const void* target_logits, const void* draft_logits,
 /* hs_add_rms_norm fuses the residual add that closes a layer                 */
 /*   (engine.py:2685, h = h + ffn_out) with the norm that opens the next:     */
 /*   h_out = bf16(h + y), x_out = rms_norm(h_out, w). h_out may alias h.       */
+/*   w and x_out both NULL: the residual add alone (h_out = bf16(h + y)).     */
 /* x, h, y, w, out: bf16, rows of D; T rows. Limits: D % 8 == 0, D <= 8192,    */
 /* 16-byte aligned pointers. The sum of squares runs in a fixed order         */
 /* (deterministic; it may differ from torch's by an ulp of the variance).     */
@@ -290,6 +291,43 @@ int hs_moe_route_ffn_fp4_partials(const void* desc, const void* hidden,
                                   float* shared_f32, void* workspace,
                                   size_t workspace_bytes, int32_t* dev_status,
                                   void* stream);
+/* ------------------------------------------------------------------------ */
+/* The MoE half of a decode layer in one call (T <= 8).                       */
+/* h_out = h + MoE(rms_norm(h, norm_w)): the norm that opens the FFN block    */
+/* (engine.py:2679, utils.py:6-9), the routing, the routed FP4 experts with   */
+/* the FP8 shared expert, and the residual add that closes the layer          */
+/* (engine.py:2685), in three launches: the norm runs inside the routing      */
+/* cluster (same summation order as hs_rms_norm, so the rows are identical)   */
+/* and the add inside the down phase's epilogue. Routing is the router        */
+/* (gate, bias, routed_scaling; as hs_moe_route_ffn_fp4) or, when tid2eid is  */
+/* not NULL, hash routing by input_ids (as hs_hash_route: weights 1/top_k,    */
+/* gate and bias ignored). x_out [T][D] receives the normed rows when not     */
+/* NULL. h_out may alias h. The partials form writes the UN-ROUNDED f32 sums  */
+/* of this rank's experts instead (expert parallelism); the caller adds them  */
+/* over ranks and calls hs_moe_combine_add_rms_norm with w = x_out = NULL for */
+/* h_out = h + combine. No reference entry point has this shape: it replaces  */
+/* the FFN block of _forward_layer (engine.py:2679-2685) as one operator.     */
+/* Limits and workspace as hs_moe_route_ffn_fp4.                              */
+/* ------------------------------------------------------------------------ */
+int hs_moe_layer_fp4(const void* desc, const void* h, const void* norm_w,
+                     float eps, const void* gate, const void* bias,
+                     const int64_t* input_ids, const int64_t* tid2eid,
+                     int64_t vocab, int64_t num_experts, int64_t expert_offset,
+                     int64_t T, int64_t top_k, float routed_scaling,
+                     int use_shared, int dup_mode, int64_t* topk_idx,
+                     float* topk_w, void* x_out, void* h_out, void* workspace,
+                     size_t workspace_bytes, int32_t* dev_status, void* stream);
+int hs_moe_layer_fp4_partials(const void* desc, const void* h,
+                              const void* norm_w, float eps, const void* gate,
+                              const void* bias, const int64_t* input_ids,
+                              const int64_t* tid2eid, int64_t vocab,
+                              int64_t num_experts, int64_t expert_offset,
+                              int64_t T, int64_t top_k, float routed_scaling,
+                              int use_shared, int dup_mode, int64_t* topk_idx,
+                              float* topk_w, void* x_out, float* routed_f32,
+                              float* shared_f32, void* workspace,
+                              size_t workspace_bytes, int32_t* dev_status,
+                              void* stream);
 int hs_moe_combine(const float* routed_f32, const float* shared_f32,
                    int use_shared, int64_t T, int64_t D, void* out,
                    void* stream);
