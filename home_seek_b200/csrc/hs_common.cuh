@@ -50,6 +50,12 @@ HS_DI void report(int32_t* status, int32_t bits) {
   if (status != nullptr) atomicOr(status, bits);
 }
 
+HS_DI uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Bounded waits give up after this many nanoseconds (about two seconds), after
 // which the kernel reports HS_DEV_TIMEOUT and returns.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
@@ -149,6 +155,13 @@ HS_DI void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(dst)),
                "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Bring [src, src + bytes) into L2 without waiting (bytes a multiple of 16,
+// src 16-byte aligned): data a later phase reads, fetched while HBM is idle.
+HS_DI void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
                : "memory");
 }
 

@@ -80,6 +80,11 @@ struct __align__(64) Desc {
   const uint8_t* s2a;   // [E][D/128][I/128][512]
   const uint8_t* sh_s13a;  // [I_sh/128][D/128][2][512]
   const uint8_t* sh_s2a;   // [D/128][I_sh/128][512]
+  // the same weights as plain bytes (L2 prefetch)
+  const uint8_t* w13;
+  const uint8_t* w2;
+  const uint8_t* sh_w13;
+  const uint8_t* sh_w2;
   int32_t E, D, I, I_sh;
   int32_t has_shared;
   uint32_t magic;
@@ -241,6 +246,15 @@ __device__ __forceinline__ int act_prescale(float wb) {
   int ex;
   frexpf(m, &ex);
   return max(-100, min(100, 1 - ex));
+}
+
+// Row prescale exponent of a token row with max |x| = mx: the row times
+// 2^e has its largest magnitude in [2^7, 2^8) for the hi/lo e4m3 split.
+__device__ __forceinline__ int row_prescale(float mx) {
+  if (!(mx > 0.f) || !isfinite(mx)) return 0;
+  int ex;
+  frexpf(mx, &ex);
+  return max(-100, min(100, 8 - ex));
 }
 
 __device__ __forceinline__ int32_t clamp_id(int64_t v, int E) {
@@ -767,7 +781,8 @@ __device__ __forceinline__ float key32_score(uint32_t k) {
   return __uint_as_float(k == 0xffffffffu ? k : k - 1u);
 }
 
-__global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs A, Plan P) {
+__global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs A, Plan P,
+                                                                      const __grid_constant__ Desc d) {
   extern __shared__ __align__(128) uint8_t rs[];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
@@ -847,31 +862,22 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   }
   ok = __syncthreads_and(ok) != 0;  // uniform over the CTA (barriers follow)
 
-  // ---- RMSNorm of every row, the standalone norm kernel's summation order ----
+  // ---- RMSNorm of every row (the standalone norm kernel's summation order),
+  // and each normed row's max |x| for its prescale exponent ----
   if (norm && ok) {
-    float ss[8];
+    for (int t = 0; t < T; ++t) {
+      const uint4* row = reinterpret_cast<const uint4*>(xs + t * RS);
+      float ss = 0.f;
+      for (int j = tid; j < nv; j += kRouteThreads) {
+        float v[8];
+        bf16x8_unpack(row[j], v);
 #pragma unroll
-    for (int t = 0; t < 8; ++t) ss[t] = 0.f;
+        for (int k = 0; k < 8; ++k) ss = __fadd_rn(ss, __fmul_rn(v[k], v[k]));
+      }
 #pragma unroll
-    for (int i = 0; i < kNormMaxVec; ++i) {
-      const int j = tid + i * kRouteThreads;
-      if (j < nv)
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-          if (t < T) {
-            float v[8];
-            bf16x8_unpack(reinterpret_cast<const uint4*>(xs + t * RS)[j], v);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) ss[t] = __fadd_rn(ss[t], __fmul_rn(v[k], v[k]));
-          }
+      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      if (lane == 0) wpart[warp * 8 + t] = ss;
     }
-#pragma unroll
-    for (int t = 0; t < 8; ++t)
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss[t] = __fadd_rn(ss[t], __shfl_xor_sync(0xffffffffu, ss[t], o));
-    if (lane == 0)
-#pragma unroll
-      for (int t = 0; t < 8; ++t) wpart[warp * 8 + t] = ss[t];
     __syncthreads();
     if (tid < T) {
       float tot = 0.f;
@@ -880,24 +886,45 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       rinv[tid] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, A.eps)));
     }
     __syncthreads();
+    const uint4* wv = reinterpret_cast<const uint4*>(nw);
+    for (int t = 0; t < T; ++t) {
+      uint4* row = reinterpret_cast<uint4*>(xs + t * RS);
+      const float ri = rinv[t];
+      float mx = 0.f;
+      for (int j = tid; j < nv; j += kRouteThreads) {
+        float wf[8], v[8];
+        bf16x8_unpack(wv[j], wf);
+        bf16x8_unpack(row[j], v);
 #pragma unroll
-    for (int i = 0; i < kNormMaxVec; ++i) {
-      const int j = tid + i * kRouteThreads;
-      if (j < nv) {
-        float wf[8];
-        bf16x8_unpack(reinterpret_cast<const uint4*>(nw)[j], wf);
-        for (int t = 0; t < T; ++t) {
-          uint4* p = reinterpret_cast<uint4*>(xs + t * RS) + j;
-          float v[8], o[8];
-          bf16x8_unpack(*p, v);
-          const float ri = rinv[t];
+        for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(wf[k], __fmul_rn(v[k], ri));
+        const uint4 p = bf16x8_pack(v);
+        row[j] = p;
+        bf16x8_unpack(p, v);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(wf[k], __fmul_rn(v[k], ri));
-          *p = bf16x8_pack(o);
-        }
+        for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[k]));
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) wpart[warp * 8 + t] = mx;
     }
     __syncthreads();
+    if (tid < T) {
+      float mx = 0.f;
+      for (int w = 0; w < kRouteThreads / 32; ++w) mx = fmaxf(mx, wpart[w * 8 + tid]);
+      rowe[tid] = row_prescale(mx);
+    }
+  } else if (warp < T) {  // rows arrive normed: the prescale from them, one warp per token
+    const uint4* row = reinterpret_cast<const uint4*>(xs + warp * RS);
+    float mx = 0.f;
+    for (int v = lane; v < nv; v += 32) {
+      float f[8];
+      bf16x8_unpack(row[v], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(f[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) rowe[warp] = row_prescale(mx);
   }
 
   // ---- logits: warp s sums the four 128-column quarters of k-split s in order ----
@@ -916,29 +943,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
 #pragma unroll
     for (int j = 0; j < 4; ++j) red[(warp * 32 + lane) * 4 + j] = s4[j];
   }
-  // row prescale of every token, one warp per token (each CTA needs it for its x8 slice)
-  if (warp < T) {
-    const uint4* row = reinterpret_cast<const uint4*>(xs + warp * RS);
-    float mx = 0.f;
-    for (int v = lane; v < nv; v += 32) {
-      float f[8];
-      bf16x8_unpack(row[v], f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(f[i]));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) {
-      int ex = 0;
-      if (mx > 0.f && isfinite(mx)) {
-        frexpf(mx, &ex);
-        ex = max(-100, min(100, 8 - ex));
-      } else {
-        ex = 0;
-      }
-      rowe[warp] = ex;
-    }
-  }
   __syncthreads();
   // (expert, token) of the 16 x 8 fragment: the logit (k-splits in order), its
   // score sqrt(softplus(bf16(bf16(l) + bias))) and selection key, to CTA 0
@@ -953,25 +957,30 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     const float sc = sqrtf(sp);
     if (t < T) cluster.map_shared_rank(keys, 0)[t * 256 + e0 + el] = score_key32(sc);
   }
-  // this CTA's columns of the normed rows and of their hi/lo e4m3 split
-  {
-    const int cols = D / ncta, c0 = rank * cols;
-    for (int i = tid; i < T * (cols / 16); i += kRouteThreads) {
-      const int t = i / (cols / 16), k16 = c0 / 16 + (i - t * (cols / 16));
-      const uint4* src = reinterpret_cast<const uint4*>(xs + t * RS);
-      uint4 hv, lv;
-      split16(src[2 * k16], src[2 * k16 + 1], exp2i(rowe[t]), hv, lv);
-      reinterpret_cast<uint4*>(P.x8 + static_cast<int64_t>(t) * D)[k16] = hv;
-      reinterpret_cast<uint4*>(P.x8 + (A.P_max + t) * D)[k16] = lv;
-      if (A.x_out) {
-        uint4* xo = reinterpret_cast<uint4*>(A.x_out + static_cast<int64_t>(t) * D);
-        xo[2 * k16] = src[2 * k16];
-        xo[2 * k16 + 1] = src[2 * k16 + 1];
+  cluster.sync();
+
+  // ---- the normed rows and their hi/lo e4m3 split, column slice by slice: off
+  // CTA 0's critical path (rank 1 also takes rank 0's slice) ----
+  if (rank != 0 || ncta == 1) {
+    const int cols = D / ncta;
+    for (int sl = (rank == 1 ? 0 : rank); sl <= rank; ++sl) {
+      const int c16 = sl * cols / 16;
+      for (int i = tid; i < T * (cols / 16); i += kRouteThreads) {
+        const int t = i / (cols / 16), k16 = c16 + (i - t * (cols / 16));
+        const uint4* src = reinterpret_cast<const uint4*>(xs + t * RS);
+        uint4 hv, lv;
+        split16(src[2 * k16], src[2 * k16 + 1], exp2i(rowe[t]), hv, lv);
+        reinterpret_cast<uint4*>(P.x8 + static_cast<int64_t>(t) * D)[k16] = hv;
+        reinterpret_cast<uint4*>(P.x8 + (A.P_max + t) * D)[k16] = lv;
+        if (A.x_out) {
+          uint4* xo = reinterpret_cast<uint4*>(A.x_out + static_cast<int64_t>(t) * D);
+          xo[2 * k16] = src[2 * k16];
+          xo[2 * k16 + 1] = src[2 * k16 + 1];
+        }
       }
     }
+    if (rank != 0) return;
   }
-  cluster.sync();
-  if (rank != 0) return;
 
   // ---- CTA 0: the router's top-k selection from the gathered keys ----
   if (!hash && warp < T) {
@@ -1092,6 +1101,12 @@ struct UnitArgs {
   uint32_t* ucount;      // [U_max] per-unit tickets, cleared by the plan kernel
   float* part;           // [(U_max + G)][slot] partial accumulators
   int64_t act_rows;      // rows per activation plane (P_max, or (1 + C_max) * 8 in token mode)
+  int ncl;               // token-mode down phase on clusters: CTAs per cluster (one cluster per tile)
+  // schedule weight of a shared-expert k-step against a routed one: 2 when
+  // both stream from HBM (FP8 is twice the bytes of FP4), 1 when the shared
+  // expert was brought into L2 beforehand (token mode) and a step costs the
+  // same MMA issue time either way
+  int w_sh;
 };
 
 template <int NT, int BOXES>
@@ -1173,7 +1188,7 @@ __device__ __forceinline__ Sched make_sched(const Desc& d, const UnitArgs& a, bo
   s.U = s.n_sh_units + s.n_rt_units;
   s.nk_sh = down ? (d.has_shared ? d.I_sh / 256 : 1) : d.D / 128;
   s.nk_rt = down ? d.I / 256 : d.D / 128;
-  s.w_sh = 2;
+  s.w_sh = a.w_sh;
   s.S_sh = s.n_sh_units * s.nk_sh;
   s.S = s.S_sh + s.n_rt_units * s.nk_rt;
   s.W_sh = s.S_sh * s.w_sh;
@@ -1250,7 +1265,8 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 // One element of the MoE output from its routed and shared f32 sums:
 // bf16(bf16(routed) + bf16(shared)) (engine.py:1530-1536), and the residual
 // add when the call carries one.
-__device__ __forceinline__ void store_out(const UnitArgs& a, int64_t o_i, float r, float h) {
+// res: the residual element a.resid[o_i] when the caller loaded it early.
+__device__ __forceinline__ void store_out(const UnitArgs& a, int64_t o_i, float r, float h, float res) {
   if (a.out_f32) a.out_f32[o_i] = r;
   if (a.partials) {
     if (a.shared_f32) a.shared_f32[o_i] = h;
@@ -1260,7 +1276,10 @@ __device__ __forceinline__ void store_out(const UnitArgs& a, int64_t o_i, float 
   if (a.use_shared) o += round_bf16(h);
   const __nv_bfloat16 y = __float2bfloat16_rn(o);
   if (a.out) a.out[o_i] = y;
-  if (a.resid_out) a.resid_out[o_i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(a.resid[o_i]), __bfloat162float(y)));
+  if (a.resid_out) a.resid_out[o_i] = __float2bfloat16_rn(__fadd_rn(res, __bfloat162float(y)));
+}
+__device__ __forceinline__ void store_out(const UnitArgs& a, int64_t o_i, float r, float h) {
+  store_out(a, o_i, r, h, a.resid_out ? __bfloat162float(a.resid[o_i]) : 0.f);
 }
 
 // Gate/up epilogue of one 128-row unit from the summed accumulators.
@@ -1329,6 +1348,44 @@ __device__ __forceinline__ void sum_slots(const SchedT& sc, int cf, int cl, int6
 #pragma unroll
         for (int t = 0; t < NV; ++t) acc[t] += v[b][t];
   }
+}
+
+// A split unit's finishing CTA: the sum, in CTA order, of the partial rows
+// the other CTAs c0..cl published in their slots (slot 2c; CTAs without steps
+// skipped), NV values of one row.
+template <int NV, typename SchedT>
+__device__ __forceinline__ void peer_sum(const SchedT& sc, int c0, int cl, const float* part, int slot_floats,
+                                         int row, float (&acc)[NV]) {
+#pragma unroll
+  for (int t = 0; t < NV; ++t) acc[t] = 0.f;
+  for (int cc = c0; cc <= cl; ++cc) {
+    if (sc.lo(cc) == sc.lo(cc + 1)) continue;
+    const float* sl = part + 2 * static_cast<int64_t>(cc) * slot_floats;
+    float v[NV];
+#pragma unroll
+    for (int t = 0; t < NV; ++t) v[t] = __ldcg(sl + t * kM + row);
+#pragma unroll
+    for (int t = 0; t < NV; ++t) acc[t] += v[t];
+  }
+}
+
+// The 128 epilogue threads wait (bounded) until a unit's ticket reaches
+// target: thread 0 polls with acquire loads, the named barrier releases the rest.
+__device__ __forceinline__ void wait_ticket(const uint32_t* ctr, uint32_t target, int etid, int32_t* status) {
+  if (etid == 0) {
+    if (ld_acquire_gpu(ctr) < target) {
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t i = 1;; ++i) {
+        if (ld_acquire_gpu(ctr) >= target) break;
+        if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          report(status, HS_DEV_TIMEOUT);
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  epi_bar();
 }
 
 // Token-mode gate/up epilogue: the accumulator columns are the (up to 8)
@@ -1433,6 +1490,26 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     prefetch_tensormap(kDown ? &d.tm_w2 : &d.tm_w13);
     prefetch_tensormap(kDown ? &d.tm_sw2 : &d.tm_sw13);
     prefetch_tensormap(kDown ? &cm.tm_act8 : &cm.tm_x8);
+    // token mode: the shared expert's gate/up and down weights do not depend on
+    // the routing; while the routing runs, the CTAs that are resident early
+    // (all but the last 40, which wait for the routing cluster's SMs) bring
+    // them into L2 in 64 KB pieces, about 90 KB per CTA
+    if (kTok && !kDown && a.use_shared && c < a.G - 40) {
+      constexpr int64_t kPiece = 65536;
+      const int64_t Dl = D, Ish = d.I_sh;
+      const uint8_t* base_r[4] = {d.sh_w13, d.sh_w2, d.sh_s13a, d.sh_s2a};
+      const int64_t len_r[4] = {2 * Ish * Dl, Dl * Ish, (Ish / kM) * (Dl / kM) * 1024, (Dl / kM) * (Ish / kM) * 512};
+      const int64_t nct = a.G - 40;
+      int64_t first = 0;  // index of the region's first piece
+      for (int r = 0; r < 4; ++r) {
+        const int64_t np = (len_r[r] + kPiece - 1) / kPiece;
+        for (int64_t i = (c - first % nct + nct) % nct; i < np; i += nct) {
+          const int64_t off = i * kPiece, left = len_r[r] - off;
+          prefetch_l2_bulk(base_r[r] + off, static_cast<uint32_t>(left < kPiece ? left : kPiece));
+        }
+        first += np;
+      }
+    }
   }
   // everything above overlaps the previous kernel; from here on the plan (and,
   // for the down phase, the gate/up phase) is complete and visible
@@ -1593,17 +1670,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     }
   } else {
     // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31) ----------------
+    // A unit split between CTAs cf..cl is finished by cf, the CTA holding its
+    // first steps (its last segment, so the latest in time); the others publish
+    // their partial rows in slot 2c (their first segment) and add their step
+    // counts to the unit's ticket. The finisher sums the published rows while
+    // its own MMAs still run, so its tail is its accumulator plus the epilogue.
     const int row = 32 * warp + lane;
     const int etid = threadIdx.x;  // 0..127
     const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+    constexpr int NV = kDown ? NP : 2 * NP;
     int seg = 0;
     for (int64_t s = s_begin; s < s_end; ++seg) {
       const int64_t u = sc.unit_of(s);
       const int64_t us = sc.ustart(u);
       const int nk = sc.unk(u);
+      const int k0 = static_cast<int>(s - us);
       const int k1 = static_cast<int>(min64(static_cast<int64_t>(nk), s_end - us));
       const UnitInfo ui = unit_info(d, a, sc, u, kDown);
       const int buf = seg & 1;
+      const int cf = sc.cta_of(us);
+      const int cl = sc.cta_of(us + nk - 1);
+      const bool split = cf != cl;
+      const bool finish = !split || c == cf;
+      float pre[NV];
+      if (split && finish) {
+        wait_ticket(&a.ucount[u], static_cast<uint32_t>(nk - (k1 - k0)), etid, a.status);
+        peer_sum<NV>(sc, cf + 1, cl, a.part, kSlot, row, pre);
+      }
       if (!mbar_wait(&bars->acc_full[buf], static_cast<uint32_t>((seg >> 1) & 1))) {
         if (etid == 0) report(a.status, HS_DEV_TIMEOUT);
         break;
@@ -1634,15 +1727,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
         g[r] = c0[r] + c0[NP + r];
         v[r] = kDown ? 0.f : c1[r] + c1[NP + r];
       }
-
-      // which CTAs share this unit
-      const int cf = sc.cta_of(us);
-      const int cl = sc.cta_of(us + nk - 1);
-      bool finish = (cf == cl);
-      const int k0 = static_cast<int>(s - us);
-      if (!finish) {
-        // a CTA splits at most its first and its last unit: slots 2c and 2c+1
-        float* slot = a.part + (2 * static_cast<int64_t>(c) + (u == sc.unit_of(s_begin) ? 0 : 1)) * kSlot;
+      if (split && finish) {
+#pragma unroll
+        for (int n = 0; n < NP; ++n) {
+          g[n] += pre[n];
+          if (!kDown) v[n] += pre[NP + n];
+        }
+      } else if (split) {
+        // publish: slot 2c, then the ticket
+        float* slot = a.part + 2 * static_cast<int64_t>(c) * kSlot;
 #pragma unroll
         for (int n = 0; n < NP; ++n) {
           __stcg(slot + n * kM + row, g[n]);
@@ -1650,29 +1743,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
         }
         __threadfence();
         epi_bar();
-        if (etid == 0) {
-          // ticket counts the unit's steps: the segment that completes them is last
-          const uint32_t mine = static_cast<uint32_t>(k1 - k0);
-          bars->flag = atomicAdd(&a.ucount[u], mine) + mine == static_cast<uint32_t>(nk);
-        }
-        epi_bar();
-        finish = bars->flag != 0;
-        epi_bar();  // every thread has read the flag before it is reused
-        if (finish) {
-          __threadfence();
-          // sum every segment's partial in CTA order (this CTA's included)
-          if constexpr (kDown) {
-            sum_slots<NP>(sc, cf, cl, us, a.part, kSlot, row, g);
-          } else {
-            float gv[2 * NP];
-            sum_slots<2 * NP>(sc, cf, cl, us, a.part, kSlot, row, gv);
-#pragma unroll
-            for (int n = 0; n < NP; ++n) {
-              g[n] = gv[n];
-              v[n] = gv[NP + n];
-            }
-          }
-        }
+        if (etid == 0) atomicAdd(&a.ucount[u], static_cast<uint32_t>(k1 - k0));
       }
       if (finish) {
         if constexpr (kTok) {
@@ -1742,7 +1813,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
 // separately as the reference's routed + shared add does. The CTA that
 // completes a unit writes the output rows; no per-pair rows, no finalize pass.
 struct TokSched {
-  int U, nsh, nrt, C, Su, G;
+  int U, nsh, nrt, C, Su, G, wsh;
   int64_t Wu, W;
 
   __device__ __forceinline__ static int64_t udiv(int64_t a, int64_t b) {
@@ -1755,13 +1826,13 @@ struct TokSched {
   __device__ __forceinline__ int64_t wpos(int64_t s) const {
     const int64_t u = unit_of(s);
     const int64_t k = s - u * Su;
-    return u * Wu + (k < nsh ? 2 * k : 2 * nsh + (k - nsh));
+    return u * Wu + (k < nsh ? wsh * k : wsh * nsh + (k - nsh));
   }
   // first step at or after weight position w
   __device__ __forceinline__ int64_t step_at(int64_t w) const {
     const int64_t u = udiv(w, Wu);
     const int64_t r = w - u * Wu;
-    return u * Su + (r <= 2 * nsh ? (r + 1) / 2 : nsh + (r - 2 * nsh));
+    return u * Su + (r <= wsh * nsh ? (r + wsh - 1) / wsh : nsh + (r - wsh * nsh));
   }
   __device__ __forceinline__ int64_t lo(int c) const {
     if (c >= G) return static_cast<int64_t>(U) * Su;
@@ -1781,7 +1852,8 @@ __device__ __forceinline__ TokSched make_tok_sched(const Desc& d, const UnitArgs
   s.nrt = d.I / 256;
   s.C = __ldcg(a.P.hdr);
   s.Su = s.nsh + s.C * s.nrt;
-  s.Wu = 2 * s.nsh + static_cast<int64_t>(s.C) * s.nrt;
+  s.wsh = a.w_sh;
+  s.Wu = s.wsh * s.nsh + static_cast<int64_t>(s.C) * s.nrt;
   s.W = s.Wu * s.U;
   s.G = a.G;
   return s;
@@ -1839,6 +1911,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     prefetch_tensormap(&d.tm_sw2);
     prefetch_tensormap(&cm.tm_act8);
   }
+
   tc5::fence_before_sync();
   __syncthreads();
   tc5::fence_after_sync();
@@ -1852,11 +1925,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   int64_t s_begin = 0, s_end = 0;
   if (any) {
     if constexpr (kCl) {
-      // cluster u = tile u; rank j takes the weight slice [Wu j/8, Wu (j+1)/8)
-      const int64_t u = c / 8, j = c % 8;
+      // cluster u = tile u; rank j takes the weight slice [Wu j/n, Wu (j+1)/n)
+      const int64_t u = c / a.ncl, j = c % a.ncl;
       auto kb = [&](int64_t jj) {
-        const int64_t w = TokSched::udiv(sc.Wu * jj, 8);
-        return w <= 2 * sc.nsh ? (w + 1) / 2 : sc.nsh + (w - 2 * sc.nsh);
+        const int64_t w = TokSched::udiv(sc.Wu * jj, a.ncl);
+        return w <= sc.wsh * sc.nsh ? (w + sc.wsh - 1) / sc.wsh : sc.nsh + (w - sc.wsh * sc.nsh);
       };
       s_begin = u * sc.Su + kb(j);
       s_end = u * sc.Su + kb(j + 1);
@@ -1953,6 +2026,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     return static_cast<uint32_t>((q.shared ? 2 * kBoxBytes : kBoxBytes) + L::kB + 1024);
   };
 
+  float res_pre = 0.f;  // cluster epilogue: the preloaded residual element
   if (warp == 4) {
     for (int64_t step = 0; step < npre; ++step) {  // stages are free: no empty waits yet
       const Step q = decode(s_begin + step);
@@ -2063,6 +2137,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     // ---------------- epilogue, cluster mode (one segment) ----------------
     const int row = 32 * warp + lane;
     const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+    // the residual element this thread adds in the reduction below, loaded now
+    // (row rpr * rank + tid / 8 of the tile, token tid % 8)
+    {
+      const int rpr = (kM + a.ncl - 1) / a.ncl;
+      const int rl = threadIdx.x >> 3, rowc = static_cast<int>(cg::this_cluster().block_rank()) * rpr + rl;
+      if (a.resid_out && (threadIdx.x & 7) < a.T && rl < rpr && rowc < kM)
+        res_pre = __bfloat162float(a.resid[(threadIdx.x & 7) * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc]);
+    }
     float r[8], h[8];
 #pragma unroll
     for (int t = 0; t < 8; ++t) r[t] = h[t] = 0.f;
@@ -2174,29 +2256,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   }
 
   if constexpr (kCl) {
-    // the tile's 8 partial accumulators, summed in rank order: rank j reduces
-    // rows 16j..16j+15, thread (row, token) reads its two values from all 8
+    // the tile's n partial accumulators, summed in rank order: rank j reduces
+    // rows rpr j .. rpr (j + 1) - 1 (rpr = ceil(128 / n)), thread (row, token)
+    // reads its two values from all n and adds the residual element it loaded
+    // before the accumulator was ready
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
-    if (warp < 4) {
-      const int rank = static_cast<int>(cluster.block_rank());
-      const int rl = threadIdx.x >> 3, t = threadIdx.x & 7;
-      const int rowc = rank * 16 + rl;
-      float* red = reinterpret_cast<float*>(base);
-      float vr[8], vh[8];
+    const int rpr = (kM + a.ncl - 1) / a.ncl;
+    const int rl = threadIdx.x >> 3, t = threadIdx.x & 7;
+    const int rowc = static_cast<int>(cluster.block_rank()) * rpr + rl;
+    if (warp < 4 && rl < rpr && rowc < kM) {
+      const float* red = reinterpret_cast<const float*>(base);
+      float vr[16], vh[16];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float* pr = cluster.map_shared_rank(red, q);
-        vr[q] = pr[t * kM + rowc];
-        vh[q] = pr[(8 + t) * kM + rowc];
-      }
+      for (int q = 0; q < 16; ++q)
+        if (q < a.ncl) {
+          const float* pr = cluster.map_shared_rank(red, q);
+          vr[q] = pr[t * kM + rowc];
+          vh[q] = pr[(8 + t) * kM + rowc];
+        }
       float rs = 0.f, hs = 0.f;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        rs += vr[q];
-        hs += vh[q];
-      }
-      if (t < a.T) store_out(a, t * static_cast<int64_t>(D) + (c / 8) * kM + rowc, rs, hs);
+      for (int q = 0; q < 16; ++q)
+        if (q < a.ncl) {
+          rs += vr[q];
+          hs += vh[q];
+        }
+      if (t < a.T) store_out(a, t * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc, rs, hs, res_pre);
     }
     cluster.sync();  // peers have read this CTA's shared memory
   }
@@ -2346,6 +2432,51 @@ static int launch_sk(const Desc& d, const CallMaps& cm, const UnitArgs& a, cudaS
   return check_launch();
 }
 
+// An empty kernel with the token-mode down kernel's launch shape (threads,
+// shared memory, two CTAs per SM): the occupancy calculator's answer for it is
+// how many clusters of a given size the GPCs can hold at once. (For the
+// tcgen05 kernels themselves it reports one CTA per SM, while two run.)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) cluster_fit_probe() {}
+
+// Cluster size for the token-mode down phase with `tiles` tiles of D: the
+// largest n in [8, 16] whose n * tiles CTAs fit the two-per-SM budget and whose
+// `tiles` clusters can all be resident at once; 0 when none (stream-K then).
+// More CTAs per tile leave fewer SMs running a single CTA, which streams at
+// twice the rate of a paired one and would idle at the end.
+static int tok_down_cluster(int tiles, int bytes) {
+  static std::mutex mu;
+  static int cached[64][65];
+  static bool have[64][65];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64 || tiles > 64) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  if (have[dev][tiles]) return cached[dev][tiles];
+  int best = 0;
+  if (cudaFuncSetAttribute(cluster_fit_probe, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
+      cudaFuncSetAttribute(cluster_fit_probe, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    for (int n = 16; n >= 8 && !best; --n) {
+      if (n * tiles > kCtasPerSm * sm_count()) continue;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(n * tiles));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = static_cast<size_t>(bytes);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = static_cast<unsigned>(n);
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int m = 0;
+      if (cudaOccupancyMaxActiveClusters(&m, cluster_fit_probe, &cfg) == cudaSuccess && m >= tiles) best = n;
+    }
+  }
+  (void)cudaGetLastError();
+  cached[dev][tiles] = best;
+  have[dev][tiles] = true;
+  return best;
+}
+
 static int launch_tok_down(const Desc& d, const CallMaps& cm, UnitArgs a, cudaStream_t st) {
   constexpr int bytes = SmemLayout<1, 2>::kBytes;
   static std::atomic<uint64_t> done{0};
@@ -2355,18 +2486,17 @@ static int launch_tok_down(const Desc& d, const CallMaps& cm, UnitArgs a, cudaSt
   if (!(done.load() & bit)) {
     HS_CUDA_CHECK(cudaFuncSetAttribute(tok_down_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
     HS_CUDA_CHECK(cudaFuncSetAttribute(tok_down_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    HS_CUDA_CHECK(cudaFuncSetAttribute(tok_down_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     done.fetch_or(bit);
   }
   const int tiles = d.D / kM;
-  // One 8-CTA cluster per tile when all tiles' clusters fit the two-CTAs-per-SM
-  // budget (D = 4096: 32 clusters, 256 CTAs). cudaOccupancyMaxActiveClusters
-  // reports one CTA per SM for these kernels, but 32 clusters do run at once on
-  // a B200 (measured); clusters never wait on one another, so a device that
-  // fits fewer runs the rest in a second wave.
-  if (8 * tiles <= kCtasPerSm * sm_count()) {
-    a.G = 8 * tiles;
+  // One cluster of n CTAs per tile (D = 4096 on a B200: 32 clusters)
+  const int n = tok_down_cluster(tiles, bytes);
+  if (n > 0) {
+    a.ncl = n;
+    a.G = n * tiles;
     HS_CUDA_CHECK(launch_pdl_cluster(tok_down_kernel<true>, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes,
-                                     st, 8u, d, cm, a));
+                                     st, static_cast<unsigned>(n), d, cm, a));
     return check_launch();
   }
   HS_CUDA_CHECK(
@@ -2438,6 +2568,8 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
     return st;
   d.s13a = static_cast<const uint8_t*>(w->s13);
   d.s2a = static_cast<const uint8_t*>(w->s2);
+  d.w13 = static_cast<const uint8_t*>(w->w13);
+  d.w2 = static_cast<const uint8_t*>(w->w2);
   if (d.has_shared) {
     if (!dim_ok(w->I_sh, 256, 256, 8192)) return HS_ERR_BAD_SHAPE;
     if (!w->sh_s13 || !w->sh_w2 || !w->sh_s2) return HS_ERR_BAD_ARGUMENT;
@@ -2452,6 +2584,8 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
       return st;
     d.sh_s13a = static_cast<const uint8_t*>(w->sh_s13);
     d.sh_s2a = static_cast<const uint8_t*>(w->sh_s2);
+    d.sh_w13 = static_cast<const uint8_t*>(w->sh_w13);
+    d.sh_w2 = static_cast<const uint8_t*>(w->sh_w2);
   }
   d.magic = kDescMagic;
   memset(desc_out, 0, desc_bytes);
@@ -2485,7 +2619,7 @@ struct RouteIn {
   int64_t vocab = 0;
 };
 
-static int launch_route(const RouteArgs& ra, const Plan& P, cudaStream_t st) {
+static int launch_route(const RouteArgs& ra, const Plan& P, const Desc& d, cudaStream_t st) {
   const int ncta = ra.E / 16;
   const size_t bytes = RouteSmem::bytes(ra.D);
   static std::atomic<uint64_t> done{0};
@@ -2499,7 +2633,7 @@ static int launch_route(const RouteArgs& ra, const Plan& P, cudaStream_t st) {
     done.fetch_or(bit);
   }
   HS_CUDA_CHECK(launch_pdl_cluster(route_plan_kernel, dim3(static_cast<unsigned>(ncta)), dim3(kRouteThreads), bytes,
-                                   st, static_cast<unsigned>(ncta), ra, P));
+                                   st, static_cast<unsigned>(ncta), ra, P, d));
   return check_launch();
 }
 
@@ -2605,7 +2739,7 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
     ra.n_ucount = pa.n_ucount;
     ra.n_ctab = g.C_max * 8;
     ra.P_max = g.P_max;
-    if ((rc = launch_route(ra, P, st))) return rc;
+    if ((rc = launch_route(ra, P, d, st))) return rc;
   } else if ((rc = launch_plan(pa, P, 1 + static_cast<int>(T), st))) {
     return rc;
   }
@@ -2616,6 +2750,8 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   }
 
   UnitArgs a;
+  a.ncl = 0;
+  a.w_sh = tok && use_shared ? 1 : 2;  // token mode prefetches the shared expert into L2
   a.P = P;
   a.T = static_cast<int>(T);
   a.K = static_cast<int>(top_k);
