@@ -863,20 +863,29 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   ok = __syncthreads_and(ok) != 0;  // uniform over the CTA (barriers follow)
 
   // ---- RMSNorm of every row (the standalone norm kernel's summation order),
-  // and each normed row's max |x| for its prescale exponent ----
+  // and each normed row's max |x| for its prescale exponent; rows in groups
+  // of four so their load, add and shuffle chains overlap ----
   if (norm && ok) {
-    for (int t = 0; t < T; ++t) {
-      const uint4* row = reinterpret_cast<const uint4*>(xs + t * RS);
-      float ss = 0.f;
+    for (int t0 = 0; t0 < T; t0 += 4) {
+      float ss[4] = {0.f, 0.f, 0.f, 0.f};
       for (int j = tid; j < nv; j += kRouteThreads) {
-        float v[8];
-        bf16x8_unpack(row[j], v);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) ss = __fadd_rn(ss, __fmul_rn(v[k], v[k]));
+        for (int q = 0; q < 4; ++q)
+          if (t0 + q < T) {
+            float v[8];
+            bf16x8_unpack(reinterpret_cast<const uint4*>(xs + (t0 + q) * RS)[j], v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ss[q] = __fadd_rn(ss[q], __fmul_rn(v[k], v[k]));
+          }
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-      if (lane == 0) wpart[warp * 8 + t] = ss;
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ss[q] = __fadd_rn(ss[q], __shfl_xor_sync(0xffffffffu, ss[q], o));
+      if (lane == 0)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (t0 + q < T) wpart[warp * 8 + t0 + q] = ss[q];
     }
     __syncthreads();
     if (tid < T) {
@@ -887,25 +896,35 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     }
     __syncthreads();
     const uint4* wv = reinterpret_cast<const uint4*>(nw);
-    for (int t = 0; t < T; ++t) {
-      uint4* row = reinterpret_cast<uint4*>(xs + t * RS);
-      const float ri = rinv[t];
-      float mx = 0.f;
+    for (int t0 = 0; t0 < T; t0 += 4) {
+      float mx[4] = {0.f, 0.f, 0.f, 0.f};
       for (int j = tid; j < nv; j += kRouteThreads) {
-        float wf[8], v[8];
+        float wf[8];
         bf16x8_unpack(wv[j], wf);
-        bf16x8_unpack(row[j], v);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(wf[k], __fmul_rn(v[k], ri));
-        const uint4 p = bf16x8_pack(v);
-        row[j] = p;
-        bf16x8_unpack(p, v);
+        for (int q = 0; q < 4; ++q)
+          if (t0 + q < T) {
+            uint4* row = reinterpret_cast<uint4*>(xs + (t0 + q) * RS);
+            const float ri = rinv[t0 + q];
+            float v[8];
+            bf16x8_unpack(row[j], v);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx = fmaxf(mx, fabsf(v[k]));
+            for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(wf[k], __fmul_rn(v[k], ri));
+            const uint4 pk = bf16x8_pack(v);
+            row[j] = pk;
+            bf16x8_unpack(pk, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx[q] = fmaxf(mx[q], fabsf(v[k]));
+          }
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if (lane == 0) wpart[warp * 8 + t] = mx;
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) mx[q] = fmaxf(mx[q], __shfl_xor_sync(0xffffffffu, mx[q], o));
+      if (lane == 0)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (t0 + q < T) wpart[warp * 8 + t0 + q] = mx[q];
     }
     __syncthreads();
     if (tid < T) {
@@ -1031,36 +1050,58 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   __syncthreads();
 
   // ---- CTA 0: the token-mode plan, one thread per (token, slot) pair ----
+  // (each thread loads its token's selections at once: no dependent loads)
   const int npairs = T * K;
   int le = -1;
   float ws = 0.f;
   if (tid < npairs) {
     const int t = tid / K, j = tid - t * K;
-    auto local = [&](int jj) {
-      const int64_t e = sI[t * K + jj] - A.offset;
-      return (e < 0 || e >= A.held) ? -1 : static_cast<int>(e);
-    };
-    le = local(j);
+    int lv[16];
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) {
+      int v = -1;
+      if (jj < K) {
+        const int64_t e = sI[t * K + jj] - A.offset;
+        v = (e < 0 || e >= A.held) ? -1 : static_cast<int>(e);
+      }
+      lv[jj] = v;
+    }
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj)
+      if (jj == j) le = lv[jj];
     if (le >= 0) {
+      bool dropped = false;
       if (A.dup_mode == HS_DUP_SUM) {  // the first slot of an expert carries the summed weight
-        for (int jj = 0; jj < j; ++jj)
-          if (local(jj) == le) le = -1;
-        if (le >= 0)
-          for (int jj = j; jj < K; ++jj)
-            if (local(jj) == le) ws += sW[t * K + jj];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj)
+          if (jj < j && lv[jj] == le) dropped = true;
+        if (!dropped)
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj)
+            if (jj >= j && jj < K && lv[jj] == le) ws += sW[t * K + jj];
       } else {  // the last slot of an expert wins
-        for (int jj = j + 1; jj < K; ++jj)
-          if (local(jj) == le) le = -1;
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj)
+          if (jj > j && jj < K && lv[jj] == le) dropped = true;
         ws = sW[t * K + j];
       }
+      if (dropped) le = -1;
     }
     if (le >= 0) atomicOr(&emask[le >> 5], 1u << (le & 31));
   }
   __syncthreads();
+  uint32_t em[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) em[w] = emask[w];
   if (tid < npairs && le >= 0) {
     const int t = tid / K;
-    int cb = __popc(emask[le >> 5] & ((1u << (le & 31)) - 1u));
-    for (int w = 0; w < (le >> 5); ++w) cb += __popc(emask[w]);
+    int cb = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t ew = em[w];
+      const uint32_t m = w < (le >> 5) ? ew : (w == (le >> 5) ? (ew & ((1u << (le & 31)) - 1u)) : 0u);
+      cb += __popc(m);
+    }
     const float wb = round_bf16(ws);
     P.ctab_wb[cb * 8 + t] = wb;
     P.ctab_sb[cb * 8 + t] = static_cast<uint8_t>(127 - act_prescale(wb));
@@ -1070,7 +1111,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   }
   if (tid == 0) {
     int C = 0;
-    for (int w = 0; w < 8; ++w) C += __popc(emask[w]);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) C += __popc(em[w]);
     P.hdr[0] = C;
     P.hdr[1] = C;
     P.hdr[2] = 0;
@@ -2171,13 +2213,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
       }
     }
     // park this CTA's partial rows in stage 0 (every stage is consumed once
-    // the accumulator is complete): [routed t][row], [shared t][row]
-    float* red = reinterpret_cast<float*>(base);
+    // the accumulator is complete): [token t][row] pairs (routed, shared)
+    float2* red = reinterpret_cast<float2*>(base);
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      red[t * kM + row] = r[t];
-      red[(8 + t) * kM + row] = h[t];
-    }
+    for (int t = 0; t < 8; ++t) red[t * kM + row] = make_float2(r[t], h[t]);
   } else {
     // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31) ----------------
     const int row = 32 * warp + lane;
@@ -2265,26 +2304,29 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     const int rpr = (kM + a.ncl - 1) / a.ncl;
     const int rl = threadIdx.x >> 3, t = threadIdx.x & 7;
     const int rowc = static_cast<int>(cluster.block_rank()) * rpr + rl;
-    if (warp < 4 && rl < rpr && rowc < kM) {
-      const float* red = reinterpret_cast<const float*>(base);
-      float vr[16], vh[16];
+    const bool mine = warp < 4 && rl < rpr && rowc < kM;
+    float rs = 0.f, hs = 0.f;
+    if (mine) {
+      // all remote loads issued before the sum (eight at a time)
+      const float2* red = reinterpret_cast<const float2*>(base);
+      for (int q0 = 0; q0 < a.ncl; q0 += 8) {
+        float2 v[8];
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        if (q < a.ncl) {
-          const float* pr = cluster.map_shared_rank(red, q);
-          vr[q] = pr[t * kM + rowc];
-          vh[q] = pr[(8 + t) * kM + rowc];
-        }
-      float rs = 0.f, hs = 0.f;
+        for (int q = 0; q < 8; ++q)
+          v[q] = q0 + q < a.ncl ? cluster.map_shared_rank(red, q0 + q)[t * kM + rowc] : make_float2(0.f, 0.f);
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        if (q < a.ncl) {
-          rs += vr[q];
-          hs += vh[q];
-        }
-      if (t < a.T) store_out(a, t * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc, rs, hs, res_pre);
+        for (int q = 0; q < 8; ++q)
+          if (q0 + q < a.ncl) {
+            rs += v[q].x;
+            hs += v[q].y;
+          }
+      }
     }
-    cluster.sync();  // peers have read this CTA's shared memory
+    // this CTA has read its peers: let them leave (the arrival orders the
+    // reads before it), store meanwhile, and wait for them before leaving
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    if (mine && t < a.T) store_out(a, t * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc, rs, hs, res_pre);
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
 
   tc5::fence_before_sync();
