@@ -50,9 +50,9 @@ HS_DI void report(int32_t* status, int32_t bits) {
   if (status != nullptr) atomicOr(status, bits);
 }
 
-HS_DI uint32_t ld_acquire_gpu(const uint32_t* p) {
+HS_DI uint32_t ld_relaxed_gpu(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -163,6 +163,19 @@ HS_DI void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
 HS_DI void prefetch_l2_bulk(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
                : "memory");
+}
+
+// Distributed shared memory: the address of this CTA's shared variable at
+// `local` in cluster rank `rank`, and an 8-byte load from it.
+HS_DI uint32_t dsmem_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+HS_DI float2 ld_dsmem_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
 }
 
 // Programmatic dependent launch. A kernel launched with launch_pdl() may start

@@ -1415,19 +1415,34 @@ __device__ __forceinline__ void peer_sum(const SchedT& sc, int c0, int cl, const
 // target: thread 0 polls with acquire loads, the named barrier releases the rest.
 __device__ __forceinline__ void wait_ticket(const uint32_t* ctr, uint32_t target, int etid, int32_t* status) {
   if (etid == 0) {
-    if (ld_acquire_gpu(ctr) < target) {
+    // relaxed polls, one acquire fence once the count is reached
+    if (ld_relaxed_gpu(ctr) < target) {
       const uint64_t t0 = globaltimer_ns();
       for (uint32_t i = 1;; ++i) {
-        if (ld_acquire_gpu(ctr) >= target) break;
+        if (ld_relaxed_gpu(ctr) >= target) break;
         if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
           report(status, HS_DEV_TIMEOUT);
           break;
         }
       }
     }
-    __threadfence();
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
   }
   epi_bar();
+}
+
+// The chunk's per-token routing weights (bf16 values) and activation prescale
+// exponents, loaded before the unit's accumulator is ready.
+__device__ __forceinline__ void tok_weights(const UnitArgs& a, const UnitInfo& ui, float (&wbv)[8], int (&qv)[8]) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    wbv[r] = 0.f;
+    qv[r] = 0;
+    if (r < a.T) {
+      wbv[r] = ui.shared ? 1.f : __ldg(a.P.ctab_wb + ui.chunk * 8 + r);
+      qv[r] = ui.shared ? 0 : 127 - static_cast<int>(__ldg(a.P.ctab_sb + ui.chunk * 8 + r));
+    }
+  }
 }
 
 // Token-mode gate/up epilogue: the accumulator columns are the (up to 8)
@@ -1436,23 +1451,13 @@ __device__ __forceinline__ void wait_ticket(const uint32_t* ctr, uint32_t target
 // run each unit over all experts with the same 8 token columns.
 template <bool kFP8>
 __device__ __forceinline__ void gateup_finish_tok(const Desc& d, const UnitArgs& a, const UnitInfo& ui, int row,
-                                                  const float (&g)[8], const float (&u)[8]) {
+                                                  const float (&g)[8], const float (&u)[8], const float (&wbv)[8],
+                                                  const int (&qv)[8]) {
   const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
   uint8_t* hi_plane = a.P.act8;
   uint8_t* lo_plane = a.P.act8 + a.act_rows * I_act;
   const int col = ui.tile * kM + row;
   const int64_t slot = kFP8 ? 0 : 1 + ui.chunk;
-  float wbv[8];
-  int qv[8];
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    wbv[r] = 0.f;
-    qv[r] = 0;
-    if (r < a.T) {
-      wbv[r] = kFP8 ? 1.f : __ldg(a.P.ctab_wb + ui.chunk * 8 + r);
-      qv[r] = kFP8 ? 0 : 127 - static_cast<int>(__ldg(a.P.ctab_sb + ui.chunk * 8 + r));
-    }
-  }
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     __nv_fp8_storage_t hb = 0, lb = 0;
@@ -1561,6 +1566,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   __syncthreads();
   tc5::fence_after_sync();
   const uint32_t tmem = bars->tmem;
+  // token mode: the producer's chunk experts (lane j: chunks j, j+32, j+64,
+  // j+96) and token B scales (lane t), loaded together with the schedule's
+  // header so the plan costs one round trip (entries past the chunk count are
+  // never used; the 512 bytes read lie inside the workspace, whose token-row
+  // planes follow the chunk table)
+  int px0 = 0, px1 = 0, px2 = 0, px3 = 0;
+  uint32_t psb = 127u;
+  if (kTok && warp == 4) {
+    const int32_t* ce = a.P.chunk_expert;
+    px0 = __ldcg(ce + lane);
+    px1 = __ldcg(ce + lane + 32);
+    px2 = __ldcg(ce + lane + 64);
+    px3 = __ldcg(ce + lane + 96);
+    if (lane < a.T) psb = __ldcg(a.P.sb1 + lane);
+  }
   const Sched sc = make_sched(d, a, kDown);
   const int64_t s_begin = sc.lo(c), s_end = sc.lo(c + 1);
 
@@ -1571,7 +1591,29 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     bool ok = true;
     for (int64_t s = s_begin; s < s_end && ok;) {
       const int64_t u = sc.unit_of(s);
-      const UnitInfo ui = unit_info(d, a, sc, u, kDown);
+      UnitInfo ui;
+      if constexpr (kTok) {
+        // unit_info with the chunk's expert from the registers above
+        const int tiles_sh = d.has_shared ? d.I_sh / kM : 1, tiles_rt = d.I / kM;
+        if (u < sc.n_sh_units) {
+          ui.shared = 1;
+          ui.chunk = static_cast<int>(u / tiles_sh);
+          ui.tile = static_cast<int>(u - static_cast<int64_t>(ui.chunk) * tiles_sh);
+          ui.e = 0;
+        } else {
+          const int64_t uu = u - sc.n_sh_units;
+          ui.shared = 0;
+          ui.chunk = static_cast<int>(uu / tiles_rt);
+          ui.tile = static_cast<int>(uu - static_cast<int64_t>(ui.chunk) * tiles_rt);
+          const int grp = ui.chunk >> 5;
+          const int sel = grp == 0 ? px0 : grp == 1 ? px1 : grp == 2 ? px2 : px3;
+          ui.e = __shfl_sync(0xffffffffu, sel, ui.chunk & 31);
+        }
+        ui.pair0 = 0;
+        ui.np = 0;
+      } else {
+        ui = unit_info(d, a, sc, u, kDown);
+      }
       const int64_t us = sc.ustart(u);
       const int k0 = static_cast<int>(s - us);
       const int k1 = static_cast<int>(min64(static_cast<int64_t>(sc.unk(u)), s_end - us));
@@ -1632,11 +1674,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
           for (int wi = lane; wi < 128; wi += 32) {
             const int m0 = wi >> 2, m1 = wi & 3;
             const int n = m0 + 32 * m1;
+            const int r = n % (8 * NT);
+            // token rows: lane r holds sb1[r] (every lane takes part in the shuffle)
+            const uint32_t tb = kTok ? __shfl_sync(0xffffffffu, psb, r & 31) : 127u;
             uint32_t b = 127u;
             if (n < N) {
-              const int r = n % (8 * NT);
               if (kTok) {
-                if (r < a.T) b = a.P.sb1[r];  // token rows: the shared rows 0..T-1
+                if (r < a.T) b = tb;
               } else if (r < ui.np) {
                 b = sbv[ui.pair0 + r];
               }
@@ -1735,6 +1779,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       const bool split = cf != cl;
       const bool finish = !split || c == cf;
       float pre[NV];
+      float wbv[8];
+      int qv[8];
+      if (kTok && finish) tok_weights(a, ui, wbv, qv);
       if (split && finish) {
         wait_ticket(&a.ucount[u], static_cast<uint32_t>(nk - (k1 - k0)), etid, a.status);
         peer_sum<NV>(sc, cf + 1, cl, a.part, kSlot, row, pre);
@@ -1790,9 +1837,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       if (finish) {
         if constexpr (kTok) {
           if (ui.shared)
-            gateup_finish_tok<true>(d, a, ui, row, g, v);
+            gateup_finish_tok<true>(d, a, ui, row, g, v, wbv, qv);
           else
-            gateup_finish_tok<false>(d, a, ui, row, g, v);
+            gateup_finish_tok<false>(d, a, ui, row, g, v, wbv, qv);
         } else if (!kDown) {
           if (ui.shared)
             gateup_finish<NT, true>(d, a, ui, row, g, v);
@@ -2313,7 +2360,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
         float2 v[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q)
-          v[q] = q0 + q < a.ncl ? cluster.map_shared_rank(red, q0 + q)[t * kM + rowc] : make_float2(0.f, 0.f);
+          v[q] = q0 + q < a.ncl ? ld_dsmem_f2(dsmem_addr(red + t * kM + rowc, static_cast<uint32_t>(q0 + q)))
+                                : make_float2(0.f, 0.f);
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           if (q0 + q < a.ncl) {
