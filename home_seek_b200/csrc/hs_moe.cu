@@ -65,6 +65,7 @@ constexpr int kLocalPairs = 4096;       // T*K up to this: token CTAs place thei
 constexpr int kFastPlanPairs = 1024;    // T*K up to this: block 0 uses the direct-count plan
 constexpr uint32_t kDescMagic = 0x48534d33u;  // "HSM3" (tiled weights)
 constexpr int kTokMax = 8;              // T <= this: token mode (activation rows per token, not per pair)
+constexpr int kInlineCombineMax = 64;   // T above this: the down phase's outputs are combined by a separate grid
 constexpr int kTokChunks = 128;         // token mode: at most T*K <= 8*16 routed chunks
 constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two independent MMA streams)
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
@@ -1149,6 +1150,10 @@ struct UnitArgs {
   // expert was brought into L2 beforehand (token mode) and a step costs the
   // same MMA issue time either way
   int w_sh;
+  // non-token mode, many tokens: the down phase only writes the per-pair rows
+  // and combine_rows_kernel sums them afterwards over the whole grid (the
+  // in-kernel per-tile finalize is one CTA per 128-row tile of D)
+  int ext_combine;
 };
 
 template <int NT, int BOXES>
@@ -1299,6 +1304,47 @@ __device__ __forceinline__ void finalize_tile(const UnitArgs& a, int D, int tile
     float o = round_bf16(r);
     if (a.use_shared) o += round_bf16(sh);
     a.out[o_i] = __float2bfloat16_rn(o);
+  }
+}
+
+// finalize_tile over the whole output, eight elements per thread and the
+// same per-element order: out[t][d] from the token's per-pair rows (positions
+// ascending) and its shared-expert row. Runs after the down phase.
+__global__ void __launch_bounds__(256) combine_rows_kernel(UnitArgs a, int D) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t nv = static_cast<int64_t>(a.T) * (D / 8);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / (D / 8));
+    const int dd = static_cast<int>(i - static_cast<int64_t>(t) * (D / 8)) * 8;
+    float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < a.K; ++j) {
+      const int p = __ldcg(a.P.tok_pos + static_cast<int64_t>(t) * a.K + j);
+      if (p < 0) continue;
+      const float4* src = reinterpret_cast<const float4*>(a.P.out_part + static_cast<int64_t>(p) * D + dd);
+      const float4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
+      r[0] += v0.x, r[1] += v0.y, r[2] += v0.z, r[3] += v0.w;
+      r[4] += v1.x, r[5] += v1.y, r[6] += v1.z, r[7] += v1.w;
+    }
+    const int64_t o_i = static_cast<int64_t>(t) * D + dd;
+    float sh[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (a.use_shared) {
+      const float4* src = reinterpret_cast<const float4*>(a.P.out_part + o_i);  // the token's shared row
+      const float4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
+      sh[0] = v0.x, sh[1] = v0.y, sh[2] = v0.z, sh[3] = v0.w, sh[4] = v1.x, sh[5] = v1.y, sh[6] = v1.z, sh[7] = v1.w;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (a.out_f32) a.out_f32[o_i + k] = r[k];
+      if (a.partials) {
+        if (a.shared_f32) a.shared_f32[o_i + k] = sh[k];
+        continue;
+      }
+      float o = round_bf16(r[k]);
+      if (a.use_shared) o += round_bf16(sh[k]);
+      a.out[o_i + k] = __float2bfloat16_rn(o);
+    }
   }
 }
 
@@ -1850,25 +1896,27 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
           for (int r = 0; r < NP; ++r)
             if (r < ui.np) a.P.out_part[static_cast<int64_t>(ui.pair0 + r) * D + ui.tile * kM + row] = g[r];
           // finalize the 128-row slice of D once every unit on it is done
-          __threadfence();
-          epi_bar();
-          if (etid == 0) {
-            const uint32_t total = static_cast<uint32_t>(a.n_sh_chunks + a.P.hdr[0]);
-            bars->flag = atomicAdd(&a.P.dcount[ui.tile], 1u) == total - 1u;
-          }
-          epi_bar();
-          const bool fin = bars->flag != 0;
-          epi_bar();
-          if (fin) {
+          if (!a.ext_combine) {
             __threadfence();
-            finalize_tile(a, D, ui.tile, etid, 128);
+            epi_bar();
+            if (etid == 0) {
+              const uint32_t total = static_cast<uint32_t>(a.n_sh_chunks + a.P.hdr[0]);
+              bars->flag = atomicAdd(&a.P.dcount[ui.tile], 1u) == total - 1u;
+            }
+            epi_bar();
+            const bool fin = bars->flag != 0;
+            epi_bar();
+            if (fin) {
+              __threadfence();
+              finalize_tile(a, D, ui.tile, etid, 128);
+            }
           }
         }
       }
       s = us + k1;
     }
     // no unit at all (every pair skipped, no shared expert): write zeros
-    if (kDown && sc.U == 0)
+    if (kDown && sc.U == 0 && !a.ext_combine)
       for (int tile = c; tile < D / kM; tile += sc.G) finalize_tile(a, D, tile, etid, 128);
   }
 
@@ -2842,6 +2890,7 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   UnitArgs a;
   a.ncl = 0;
   a.w_sh = tok && use_shared ? 1 : 2;  // token mode prefetches the shared expert into L2
+  a.ext_combine = T > kInlineCombineMax ? 1 : 0;
   a.P = P;
   a.T = static_cast<int>(T);
   a.K = static_cast<int>(top_k);
@@ -2868,7 +2917,12 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   }
   if ((rc = launch_nt<false>(NT, d, cm, a, st))) return rc;
   a.ucount = pa.ucount + g.U_gu;
-  return launch_nt<true>(NT, d, cm, a, st);
+  if ((rc = launch_nt<true>(NT, d, cm, a, st))) return rc;
+  if (!a.ext_combine) return HS_OK;
+  const int64_t nv = T * (d.D / 8);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((nv + 255) / 256, 8 * sm_count()));
+  HS_CUDA_CHECK(launch_pdl(combine_rows_kernel, dim3(grid), dim3(256), 0, st, a, d.D));
+  return check_launch();
 }
 
 extern "C" int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx, const float* topk_w,
