@@ -45,7 +45,7 @@ def _peaks():
 
 def _traffic_from_profile():
     """dram bytes per MoE FFN call from the committed ncu summary, if any."""
-    f = REPO / "profiles" / "moe_ffn_cfg0_t3.md"
+    f = REPO / "profiles" / "moe_layer_cfg0_t3.md"
     if not f.exists():
         return None
     m = re.search(r"traffic_bytes_per_call:\s*([0-9.eE+]+)", f.read_text())
