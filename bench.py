@@ -243,6 +243,11 @@ def moe_roofline(model, reps: int = 43):
             ops.moe_layer(st.desc(l), st.dims, h, model.ln_w[l], lw.gate, lw.bias, s.top_k, s.routed_scaling,
                           h_out=h_out)
             return
+        if model.ep.peers is not None:
+            ops.moe_layer_ep(st.desc(l), st.dims, h, model.ln_w[l], lw.gate, lw.bias, s.top_k, s.routed_scaling,
+                             model.ep.peers.peers, num_experts=s.num_experts, expert_offset=st.expert_offset,
+                             h_out=h_out)
+            return
         buf = ops.moe_layer(st.desc(l), st.dims, h, model.ln_w[l], lw.gate, lw.bias, s.top_k, s.routed_scaling,
                             num_experts=s.num_experts, expert_offset=st.expert_offset, partials=True)[0]
         model.ep.all_reduce(buf)
@@ -251,6 +256,9 @@ def moe_roofline(model, reps: int = 43):
     lo, hi = st.expert_offset, st.expert_offset + st.E_local
     uniq = [len({e for e in c[2].flatten().tolist() if lo <= e < hi}) for c in calls]
     per_call = _graph_time_per_call(lambda: [layer_call(l, h, ho) for (l, h, idx, ho) in calls], len(calls))
+    # the main pass's shape too (T = 1), for the record
+    calls1 = [(l, h[:1].contiguous(), idx, torch.empty_like(h[:1])) for (l, h, idx, ho) in calls]
+    per_call_t1 = _graph_time_per_call(lambda: [layer_call(l, h, ho) for (l, h, idx, ho) in calls1], len(calls1))
     ms = [per_call] * len(calls)
     shared = 3 * st.I_sh * s.hidden + 3 * (st.I_sh // 128) * (s.hidden // 128)
     # h in, normed rows (x8) and activations, h out, idx/w, norm weight, router gate and bias
@@ -258,7 +266,7 @@ def moe_roofline(model, reps: int = 43):
     bytes_ = [u * s.bytes_per_expert + shared + act for u in uniq]
     gbs = [b / (m * 1e-3) / 1e9 for b, m in zip(bytes_, ms)]
     return {"avg_ms": statistics.mean(ms), "avg_bytes": statistics.mean(bytes_), "avg_gbs": statistics.mean(gbs),
-            "avg_unique_experts": statistics.mean(uniq)}
+            "avg_unique_experts": statistics.mean(uniq), "t1_ms": per_call_t1}
 
 
 def run_moe_only(args):
@@ -344,8 +352,12 @@ def run_ours(args):
     if world > 1:
         # one decode stream over an expert-parallel group: every rank holds
         # 1/world of the routed experts and of the shared expert (ep.py)
-        from home_seek_b200.ep import ExpertParallel
+        from home_seek_b200.ep import ExpertParallel, PeerExchange
         ep = ExpertParallel(rank, world)
+        # decode-size layers exchange their partial sums through NVLink peer
+        # memory inside the layer call (HS_EP_TRANSPORT=nccl: NCCL all-reduce)
+        if os.environ.get("HS_EP_TRANSPORT", "p2p") == "p2p":
+            ep.peers = PeerExchange(rank, world, shape.hidden)
     model = MoEPathModel(shape, device=dev, seed=0, ep=ep)
     dec = MTPDecoder(model, max_tokens=(args.steps + args.warmup + 8) * (shape.num_draft + 2))
     dec.reset(token=1234)
@@ -425,6 +437,8 @@ def run_ours(args):
         dec.graph = None
         del dev_graph
         dist.barrier()
+        if ep.peers is not None:
+            ep.peers.close()
         dist.destroy_process_group()
     if rank != 0:
         return 0
@@ -440,15 +454,18 @@ def run_ours(args):
                                "accept) over the 43-layer MoE path, bs=1",
                    "model": "DeepSeek-V4-Flash-shape 43L+MTP, 256 FP4 experts top-6 + FP8 shared, random init",
                    "global_batch": 1, "seq_len": 3,
-                   "parallelism": f"expert-parallel x{world} (1/{world} of the routed and shared experts per GPU, "
-                                  f"f32 partials all-reduced over NCCL)" if world > 1 else "single GPU",
+                   "parallelism": (f"expert-parallel x{world} (1/{world} of the routed and shared experts per GPU, "
+                                   + ("f32 partials stored into every rank's buffer over NVLink by the down phase)"
+                                      if ep is not None and ep.peers is not None else
+                                      "f32 partials all-reduced over NCCL)")) if world > 1 else "single GPU",
                    "attention": "not in this build's step (reference PyTorch path)",
                    "l2": "inputs larger than L2: ~16 GB of distinct expert weights streamed per iteration",
                    "acceptance_rate": accepted / max(1, args.steps * shape.num_draft), "status_word": status},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": _traffic_from_profile(),
                      "kernel": "hs_moe_layer_fp4 at T=3 (norm+route+plan, gate/up, down+residual launches)",
-                     "peak_kind": peak_kind, "avg_ms": roof["avg_ms"], "avg_bytes": roof["avg_bytes"],
+                     "peak_kind": peak_kind, "avg_ms": roof["avg_ms"], "t1_layer_ms": roof["t1_ms"],
+                     "avg_bytes": roof["avg_bytes"],
                      "avg_unique_experts": roof["avg_unique_experts"]},
         "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_d["cores"], "kind": "port",
                          "sample": "one T=3 + one T=1 MoE layer and one lm_head GEMV at config-0 shapes, "

@@ -29,6 +29,14 @@ HS_MOE_DESC_BYTES = 1024
 HS_MOE_NOALLOC_BYTES = 16 << 20
 HS_DUP_LAST = 0
 HS_DUP_SUM = 1
+HS_EP_MAX_RANKS = 8
+HS_IPC_HANDLE_BYTES = 64
+
+
+class HsEpPeers(ctypes.Structure):
+    """hs_ep_peers: this rank, the group size, and every rank's receive buffer
+    as mapped in this process (recv[rank] is the local buffer)."""
+    _fields_ = [("rank", c_int32), ("world", c_int32), ("recv", c_void_p * HS_EP_MAX_RANKS)]
 
 
 class HsError(RuntimeError):
@@ -92,6 +100,16 @@ SIGNATURES = {
                                           c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int,
                                           c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                           c_size_t, c_void_p, c_void_p]),
+    "hs_ep_buffer_bytes": (c_size_t, [c_int64, c_int64]),
+    "hs_ep_buffer_alloc": (c_int, [c_size_t, POINTER(c_void_p)]),
+    "hs_ep_buffer_free": (c_int, [c_void_p]),
+    "hs_ipc_get_handle": (c_int, [c_void_p, c_void_p, c_size_t]),
+    "hs_ipc_open_handle": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "hs_ipc_close_handle": (c_int, [c_void_p]),
+    "hs_moe_layer_fp4_ep": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int, c_int, c_void_p,
+                                    c_void_p, c_void_p, POINTER(HsEpPeers), c_void_p, c_void_p, c_size_t, c_void_p,
+                                    c_void_p]),
     "hs_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]),
     "hs_moe_combine_add_rms_norm": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_float, c_int64, c_int64,
                                             c_void_p, c_void_p, c_void_p]),

@@ -70,6 +70,28 @@ constexpr int kTokChunks = 128;         // token mode: at most T*K <= 8*16 route
 constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two independent MMA streams)
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
 
+// Receive buffer of the peer-memory expert-parallel exchange: a 256-byte
+// header ([0] calls made, [1] combine ticket, u64) and two slots (calls
+// alternate) of [world][routed, shared][8 tokens][D] f32 rows. A rank's call k
+// writes slot k % 2 of every rank; rank q's call k+2 can only start after
+// every rank finished call k+1 and so consumed slot k % 2. An empty entry
+// holds kEmpty (a NaN bit pattern the sums never produce: their NaNs are the
+// canonical 0x7fffffff), so a row entry is its own arrival flag: the producer
+// only stores, the consumer waits for every entry it reads to be filled and
+// sets it back to kEmpty.
+namespace epx {
+constexpr int64_t kHdr = 256;
+constexpr uint32_t kEmpty = 0xffffffffu;
+constexpr int kRows = 8;
+__host__ __device__ inline float* rows(uint8_t* buf, int slot, int world, int src, int which, int D) {
+  return reinterpret_cast<float*>(buf + kHdr) +
+         ((static_cast<int64_t>(slot) * world + src) * 2 + which) * kRows * static_cast<int64_t>(D);
+}
+inline size_t bytes(int64_t world, int64_t D) {
+  return static_cast<size_t>(kHdr + 2 * world * 2 * kRows * D * static_cast<int64_t>(sizeof(float)));
+}
+}  // namespace epx
+
 struct __align__(64) Desc {
   // Weight tiles as rows of 128 values: [tiles * 128 rows][128], box 128 x 256
   // (two adjacent tiles), 128B swizzle.
@@ -1154,6 +1176,10 @@ struct UnitArgs {
   // and combine_rows_kernel sums them afterwards over the whole grid (the
   // in-kernel per-tile finalize is one CTA per 128-row tile of D)
   int ext_combine;
+  // expert parallelism over peer memory (hs_moe_layer_fp4_ep): the cluster
+  // down epilogue stores this rank's rows into every rank's receive buffer
+  int ep_rank, ep_world;  // ep_world 0: off
+  uint8_t* ep_recv[HS_EP_MAX_RANKS];
 };
 
 template <int NT, int BOXES>
@@ -1344,6 +1370,64 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(UnitArgs a, int D) {
       float o = round_bf16(r[k]);
       if (a.use_shared) o += round_bf16(sh[k]);
       a.out[o_i + k] = __float2bfloat16_rn(o);
+    }
+  }
+}
+
+// Peer-memory exchange, consumer side: per element, wait (bounded) until
+// every rank's routed and shared entries of this call have arrived in the
+// local buffer, then h_out = bf16(h + bf16(bf16(sum_q routed_q) +
+// bf16(sum_q shared_q))), ranks summed in order from 0 (identical on every
+// rank), and the entries are emptied again; the last CTA advances the local
+// call counter.
+__global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world, int T, int D, int use_shared,
+                                                         const __nv_bfloat16* h, __nv_bfloat16* h_out,
+                                                         int32_t* status) {
+  pdl_trigger();
+  pdl_wait();
+  uint64_t* hdr = reinterpret_cast<uint64_t*>(buf);
+  const uint64_t k = *reinterpret_cast<volatile const uint64_t*>(hdr);
+  const int slot = static_cast<int>(k & 1u);
+  const int64_t n = static_cast<int64_t>(T) * D;
+  bool timed_out = false;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t o = i;  // token-major [8][D] rows: entry (t, d) of this call's T x D output
+    float r = 0.f, sh = 0.f;
+    for (int q = 0; q < world && !timed_out; ++q) {
+      volatile uint32_t* pr = reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 0, D) + o);
+      volatile uint32_t* ps = reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 1, D) + o);
+      uint32_t vr = *pr, vs = *ps;
+      if (vr == epx::kEmpty || vs == epx::kEmpty) {
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t it = 1; vr == epx::kEmpty || vs == epx::kEmpty; ++it) {
+          vr = *pr;
+          vs = *ps;
+          if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+            report(status, HS_DEV_TIMEOUT);
+            timed_out = true;
+            break;
+          }
+        }
+      }
+      r += __uint_as_float(vr);
+      sh += __uint_as_float(vs);
+      *pr = epx::kEmpty;
+      *ps = epx::kEmpty;
+    }
+    if (timed_out) break;
+    float y = round_bf16(r);
+    if (use_shared) y += round_bf16(sh);
+    const float yb = __bfloat162float(__float2bfloat16_rn(y));
+    h_out[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(h[i]), yb));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(reinterpret_cast<unsigned int*>(hdr + 1), 1u) == gridDim.x - 1) {
+      *reinterpret_cast<volatile unsigned int*>(hdr + 1) = 0u;
+      *reinterpret_cast<volatile uint64_t*>(hdr) = k + 1;
+      __threadfence();
     }
   }
 }
@@ -2164,6 +2248,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   };
 
   float res_pre = 0.f;  // cluster epilogue: the preloaded residual element
+  int ep_slot = 0;      // peer-memory exchange: this call's slot
   if (warp == 4) {
     for (int64_t step = 0; step < npre; ++step) {  // stages are free: no empty waits yet
       const Step q = decode(s_begin + step);
@@ -2275,12 +2360,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     const int row = 32 * warp + lane;
     const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
     // the residual element this thread adds in the reduction below, loaded now
-    // (row rpr * rank + tid / 8 of the tile, token tid % 8)
+    // (row rpr * rank + tid % 16 of the tile, token tid / 16)
     {
       const int rpr = (kM + a.ncl - 1) / a.ncl;
-      const int rl = threadIdx.x >> 3, rowc = static_cast<int>(cg::this_cluster().block_rank()) * rpr + rl;
-      if (a.resid_out && (threadIdx.x & 7) < a.T && rl < rpr && rowc < kM)
-        res_pre = __bfloat162float(a.resid[(threadIdx.x & 7) * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc]);
+      const int rl = threadIdx.x & 15, rowc = static_cast<int>(cg::this_cluster().block_rank()) * rpr + rl;
+      if (a.resid_out && (threadIdx.x >> 4) < a.T && rl < rpr && rowc < kM)
+        res_pre = __bfloat162float(a.resid[(threadIdx.x >> 4) * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc]);
     }
     float r[8], h[8];
 #pragma unroll
@@ -2391,13 +2476,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
 
   if constexpr (kCl) {
     // the tile's n partial accumulators, summed in rank order: rank j reduces
-    // rows rpr j .. rpr (j + 1) - 1 (rpr = ceil(128 / n)), thread (row, token)
-    // reads its two values from all n and adds the residual element it loaded
-    // before the accumulator was ready
+    // rows rpr j .. rpr (j + 1) - 1 (rpr = ceil(128 / n) <= 16), thread (row,
+    // token) reads its two values from all n and adds the residual element it
+    // loaded before the accumulator was ready
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
+    if (a.ep_world > 0)  // this call's slot (the local call counter, advanced by the previous combine)
+      ep_slot = static_cast<int>(*reinterpret_cast<volatile const uint64_t*>(a.ep_recv[a.ep_rank]) & 1u);
     const int rpr = (kM + a.ncl - 1) / a.ncl;
-    const int rl = threadIdx.x >> 3, t = threadIdx.x & 7;
+    // thread (token tid / 16, row tid % 16): a warp covers 16 consecutive rows
+    // of two tokens, so its output (and peer) stores are contiguous runs
+    const int rl = threadIdx.x & 15, t = threadIdx.x >> 4;
     const int rowc = static_cast<int>(cluster.block_rank()) * rpr + rl;
     const bool mine = warp < 4 && rl < rpr && rowc < kM;
     float rs = 0.f, hs = 0.f;
@@ -2421,12 +2510,25 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     // this CTA has read its peers: let them leave (the arrival orders the
     // reads before it), store meanwhile, and wait for them before leaving
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    if (mine && t < a.T) store_out(a, t * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc, rs, hs, res_pre);
+    if (mine && t < a.T) {
+      if (a.ep_world > 0) {
+        // this rank's routed and shared sums into every rank's slot (each
+        // entry is its own arrival flag)
+        const int64_t o_i = t * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc;
+        for (int q = 0; q < a.ep_world; ++q) {
+          epx::rows(a.ep_recv[q], ep_slot, a.ep_world, a.ep_rank, 0, D)[o_i] = rs;
+          epx::rows(a.ep_recv[q], ep_slot, a.ep_world, a.ep_rank, 1, D)[o_i] = hs;
+        }
+      } else {
+        store_out(a, t * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc, rs, hs, res_pre);
+      }
+    }
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
 
   tc5::fence_before_sync();
   __syncthreads();
+
   if (threadIdx.x == 128) {
     for (int64_t k = bars->consumed; k < bars->issued; ++k)
       if (!mbar_wait(&bars->full[k % S_], static_cast<uint32_t>((k / S_) & 1))) {
@@ -2615,7 +2717,7 @@ static int tok_down_cluster(int tiles, int bytes) {
   return best;
 }
 
-static int launch_tok_down(const Desc& d, const CallMaps& cm, UnitArgs a, cudaStream_t st) {
+static int launch_tok_down(const Desc& d, const CallMaps& cm, UnitArgs a, cudaStream_t st, int* grid_out = nullptr) {
   constexpr int bytes = SmemLayout<1, 2>::kBytes;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
@@ -2633,10 +2735,12 @@ static int launch_tok_down(const Desc& d, const CallMaps& cm, UnitArgs a, cudaSt
   if (n > 0) {
     a.ncl = n;
     a.G = n * tiles;
+    if (grid_out) *grid_out = a.G;
     HS_CUDA_CHECK(launch_pdl_cluster(tok_down_kernel<true>, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes,
                                      st, static_cast<unsigned>(n), d, cm, a));
     return check_launch();
   }
+  if (a.ep_world > 0) return HS_ERR_UNSUPPORTED;  // the peer exchange runs on the cluster epilogue
   HS_CUDA_CHECK(
       launch_pdl(tok_down_kernel<false>, dim3(static_cast<unsigned>(a.G)), dim3(kThreads), bytes, st, d, cm, a));
   return check_launch();
@@ -2755,6 +2859,7 @@ struct RouteIn {
   const int64_t* ids = nullptr;      // hash routing when tid2eid is set
   const int64_t* tid2eid = nullptr;
   int64_t vocab = 0;
+  const hs_ep_peers* ep = nullptr;   // peer-memory expert parallelism (layer form)
 };
 
 static int launch_route(const RouteArgs& ra, const Plan& P, const Desc& d, cudaStream_t st) {
@@ -2802,6 +2907,14 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
         (route->x_out && !aligned16(route->x_out)))
       return HS_ERR_ALIGN;
     if (layer && !partials && !route->h_out) return HS_ERR_BAD_ARGUMENT;
+    if (route->ep) {
+      const hs_ep_peers* pe = route->ep;
+      if (!layer || partials || pe->world < 1 || pe->world > HS_EP_MAX_RANKS || pe->rank < 0 ||
+          pe->rank >= pe->world)
+        return HS_ERR_BAD_ARGUMENT;
+      for (int q = 0; q < pe->world; ++q)
+        if (!pe->recv[q] || !aligned16(pe->recv[q])) return HS_ERR_BAD_ARGUMENT;
+    }
   }
   if (partials ? !out_f32 : (!out && !(layer && route->h_out))) return HS_ERR_BAD_ARGUMENT;
   if (dup_mode != HS_DUP_LAST && dup_mode != HS_DUP_SUM) return HS_ERR_BAD_ARGUMENT;
@@ -2891,6 +3004,14 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   a.ncl = 0;
   a.w_sh = tok && use_shared ? 1 : 2;  // token mode prefetches the shared expert into L2
   a.ext_combine = T > kInlineCombineMax ? 1 : 0;
+  a.ep_rank = 0;
+  a.ep_world = 0;
+  for (int q = 0; q < HS_EP_MAX_RANKS; ++q) a.ep_recv[q] = nullptr;
+  if (route && route->ep) {
+    a.ep_rank = route->ep->rank;
+    a.ep_world = route->ep->world;
+    for (int q = 0; q < a.ep_world; ++q) a.ep_recv[q] = static_cast<uint8_t*>(route->ep->recv[q]);
+  }
   a.P = P;
   a.T = static_cast<int>(T);
   a.K = static_cast<int>(top_k);
@@ -2913,7 +3034,16 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   if (tok) {
     if ((rc = launch_sk<false, 1, true>(d, cm, a, st))) return rc;
     a.ucount = pa.ucount + g.U_gu;
-    return launch_tok_down(d, cm, a, st);
+    if (a.ep_world == 0) return launch_tok_down(d, cm, a, st);
+    int gdown = 0;
+    if ((rc = launch_tok_down(d, cm, a, st, &gdown))) return rc;
+    (void)gdown;
+    const int64_t n = T * d.D;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64));
+    HS_CUDA_CHECK(launch_pdl(ep_combine_kernel, dim3(grid), dim3(256), 0, st, a.ep_recv[a.ep_rank], a.ep_world,
+                             static_cast<int>(T), d.D, use_shared, static_cast<const __nv_bfloat16*>(hidden),
+                             static_cast<__nv_bfloat16*>(route->h_out), dev_status));
+    return check_launch();
   }
   if ((rc = launch_nt<false>(NT, d, cm, a, st))) return rc;
   a.ucount = pa.ucount + g.U_gu;
@@ -2989,6 +3119,75 @@ extern "C" int hs_moe_layer_fp4_partials(const void* desc, const void* h, const 
   r.vocab = vocab;
   return moe_ffn_impl(desc, h, nullptr, nullptr, T, top_k, use_shared, dup_mode, nullptr, routed_f32, shared_f32, 1,
                       workspace, workspace_bytes, dev_status, stream, &r);
+}
+
+extern "C" int hs_moe_layer_fp4_ep(const void* desc, const void* h, const void* norm_w, float eps, const void* gate,
+                                   const void* bias, const int64_t* input_ids, const int64_t* tid2eid, int64_t vocab,
+                                   int64_t num_experts, int64_t expert_offset, int64_t T, int64_t top_k,
+                                   float routed_scaling, int use_shared, int dup_mode, int64_t* topk_idx,
+                                   float* topk_w, void* x_out, const hs_ep_peers* peers, void* h_out,
+                                   void* workspace, size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  if (!norm_w || !h_out || !peers) return HS_ERR_BAD_ARGUMENT;
+  Desc dd;
+  if (!desc) return HS_ERR_BAD_ARGUMENT;
+  memcpy(&dd, desc, sizeof(dd));
+  if (T > epx::kRows || dd.D > 8192) return HS_ERR_UNSUPPORTED;
+  RouteIn r{gate, bias, num_experts, expert_offset, routed_scaling, topk_idx, topk_w};
+  r.norm_w = norm_w;
+  r.eps = eps;
+  r.x_out = x_out;
+  r.h_out = h_out;
+  r.ids = input_ids;
+  r.tid2eid = tid2eid;
+  r.vocab = vocab;
+  r.ep = peers;
+  return moe_ffn_impl(desc, h, nullptr, nullptr, T, top_k, use_shared, dup_mode, nullptr, nullptr, nullptr, 0,
+                      workspace, workspace_bytes, dev_status, stream, &r);
+}
+
+extern "C" size_t hs_ep_buffer_bytes(int64_t world, int64_t D) {
+  if (world < 1 || world > HS_EP_MAX_RANKS || D < 8 || D > 8192) return 0;
+  return epx::bytes(world, D);
+}
+
+extern "C" int hs_ep_buffer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return HS_ERR_BAD_ARGUMENT;
+  *ptr = nullptr;
+  HS_CUDA_CHECK(cudaMalloc(ptr, bytes));
+  HS_CUDA_CHECK(cudaMemset(*ptr, 0, static_cast<size_t>(epx::kHdr)));              // counters
+  if (bytes > static_cast<size_t>(epx::kHdr))                                        // every entry empty
+    HS_CUDA_CHECK(cudaMemset(static_cast<uint8_t*>(*ptr) + epx::kHdr, 0xff, bytes - epx::kHdr));
+  HS_CUDA_CHECK(cudaDeviceSynchronize());
+  return HS_OK;
+}
+
+extern "C" int hs_ep_buffer_free(void* ptr) {
+  if (!ptr) return HS_OK;
+  HS_CUDA_CHECK(cudaFree(ptr));
+  return HS_OK;
+}
+
+extern "C" int hs_ipc_get_handle(const void* ptr, void* handle, size_t handle_bytes) {
+  if (!ptr || !handle || handle_bytes < sizeof(cudaIpcMemHandle_t)) return HS_ERR_BAD_ARGUMENT;
+  cudaIpcMemHandle_t hnd;
+  HS_CUDA_CHECK(cudaIpcGetMemHandle(&hnd, const_cast<void*>(ptr)));
+  memcpy(handle, &hnd, sizeof(hnd));
+  return HS_OK;
+}
+
+extern "C" int hs_ipc_open_handle(const void* handle, void** ptr) {
+  if (!handle || !ptr) return HS_ERR_BAD_ARGUMENT;
+  cudaIpcMemHandle_t hnd;
+  memcpy(&hnd, handle, sizeof(hnd));
+  *ptr = nullptr;
+  HS_CUDA_CHECK(cudaIpcOpenMemHandle(ptr, hnd, cudaIpcMemLazyEnablePeerAccess));
+  return HS_OK;
+}
+
+extern "C" int hs_ipc_close_handle(void* ptr) {
+  if (!ptr) return HS_OK;
+  HS_CUDA_CHECK(cudaIpcCloseMemHandle(ptr));
+  return HS_OK;
 }
 
 extern "C" int hs_moe_ffn_fp4_partials(const void* desc, const void* hidden, const int64_t* topk_idx,

@@ -21,12 +21,13 @@ sizes: the tokens are already on every rank, so the only exchange is the
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
 
-from . import ops
+from . import _lib, ops
 from .expert_store import HBMExpertStore
 
 
@@ -55,14 +56,68 @@ def localize(topk_idx: torch.Tensor, offset: int, held: int) -> torch.Tensor:
     return torch.where(inside, topk_idx - offset, torch.full_like(topk_idx, -1))
 
 
+class PeerExchange:
+    """The receive buffers of the peer-memory exchange (hs_moe_layer_fp4_ep).
+
+    Each rank's buffer is allocated by the library, its CUDA IPC handle is
+    exchanged over the process group, and every other rank maps it, so a down
+    phase can store its rows into all ranks' buffers over NVLink. Created
+    collectively (every rank, same order); `close` is collective too and must
+    run after all GPU work that uses the buffers has finished."""
+
+    def __init__(self, rank: int, world: int, hidden: int, group=None):
+        import torch.distributed as dist
+        lib = _lib.load()
+        nbytes = lib.hs_ep_buffer_bytes(world, hidden)
+        if nbytes == 0:
+            raise ValueError(f"no peer exchange for world={world}, hidden={hidden}")
+        local = ctypes.c_void_p()
+        _lib.call("hs_ep_buffer_alloc", nbytes, ctypes.byref(local))
+        self.local = local.value
+        hnd = (ctypes.c_uint8 * _lib.HS_IPC_HANDLE_BYTES)()
+        _lib.call("hs_ipc_get_handle", self.local, hnd, _lib.HS_IPC_HANDLE_BYTES)
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(hnd), group=group)
+        self.group = group
+        self.mapped = []
+        peers = _lib.HsEpPeers()
+        peers.rank = rank
+        peers.world = world
+        for q in range(world):
+            if q == rank:
+                peers.recv[q] = self.local
+                continue
+            ptr = ctypes.c_void_p()
+            buf = (ctypes.c_uint8 * _lib.HS_IPC_HANDLE_BYTES).from_buffer_copy(handles[q])
+            _lib.call("hs_ipc_open_handle", buf, ctypes.byref(ptr))
+            peers.recv[q] = ptr.value
+            self.mapped.append(ptr.value)
+        self.peers = peers
+        dist.barrier(group=group)  # every rank has mapped every buffer before anyone stores
+
+    def close(self) -> None:
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank stores into a buffer that is going away
+        for ptr in self.mapped:
+            _lib.call("hs_ipc_close_handle", ptr)
+        self.mapped = []
+        dist.barrier(group=self.group)
+        _lib.call("hs_ep_buffer_free", self.local)
+        self.local = None
+
+
 @dataclass
 class ExpertParallel:
     """One rank's view of the expert-parallel group. `all_reduce` sums a tensor
-    over the group in place (default: torch.distributed on `group`)."""
+    over the group in place (default: torch.distributed on `group`). With
+    `peers` set (a PeerExchange), decode-size layers exchange their partial
+    sums through NVLink peer memory inside the layer call instead."""
     rank: int
     world: int
     group: Optional[object] = None
     all_reduce: Optional[Callable[[torch.Tensor], None]] = None
+    peers: Optional[PeerExchange] = None
 
     def __post_init__(self):
         if self.all_reduce is None:

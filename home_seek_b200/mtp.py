@@ -123,8 +123,10 @@ class MoEPathModel:
     def layer(self, h: torch.Tensor, layer: int, ids: torch.Tensor,
               h_out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """h + MoE(rms_norm(h, ln_w[layer])) for T <= 8 rows (into h_out when
-        given, which may be h): one hs_moe_layer_fp4 call, or under expert
-        parallelism the partials form, an all-reduce and the combine + add."""
+        given, which may be h): one hs_moe_layer_fp4 call; under expert
+        parallelism either hs_moe_layer_fp4_ep (the exchange through NVLink
+        peer memory inside the call) or the partials form, an NCCL all-reduce
+        and the combine + add."""
         s = self.shape
         st = self.store
         lw = st.layers[layer]
@@ -133,6 +135,9 @@ class MoEPathModel:
         kw = {"ids": ids, "tid2eid": lw.tid2eid} if hashed else {}
         gate, bias = (None, None) if hashed else (lw.gate, lw.bias)
         args = (st.desc(layer), st.dims, h, self.ln_w[layer], gate, bias, s.top_k, s.routed_scaling)
+        if self.ep is not None and self.ep.peers is not None:  # exchange through peer memory in the call
+            return ops.moe_layer_ep(*args, self.ep.peers.peers, dup_mode=dup, num_experts=s.num_experts,
+                                    expert_offset=st.expert_offset, h_out=h_out, **kw)[0]
         if self.ep is not None:
             buf, _, _ = ops.moe_layer(*args, dup_mode=dup, num_experts=s.num_experts,
                                       expert_offset=st.expert_offset, partials=True, **kw)

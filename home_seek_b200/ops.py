@@ -22,7 +22,8 @@ _KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_mo
             "hs_moe_unpermute": 1, "hs_accept_greedy": 1, "hs_accept_rejection": 1, "hs_fill_bytes": 1,
             "hs_rms_norm": 1, "hs_add_rms_norm": 1, "hs_moe_ffn_fp4_partials": 3, "hs_moe_combine": 1,
             "hs_moe_route_ffn_fp4": 3, "hs_moe_route_ffn_fp4_partials": 3,
-            "hs_moe_combine_add_rms_norm": 1, "hs_moe_layer_fp4": 3, "hs_moe_layer_fp4_partials": 3}
+            "hs_moe_combine_add_rms_norm": 1, "hs_moe_layer_fp4": 3, "hs_moe_layer_fp4_partials": 3,
+            "hs_moe_layer_fp4_ep": 4}
 
 
 def _launch(name: str, *args, extra: int = 0) -> None:
@@ -289,6 +290,43 @@ def moe_layer(desc: ctypes.Array, dims: tuple, h: torch.Tensor, norm_w: torch.Te
     if h_out is None:
         h_out = torch.empty_like(h)
     _launch("hs_moe_layer_fp4", *route, h_out.data_ptr(), ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(),
+            _stream(dev))
+    return h_out, idx, w
+
+
+def moe_layer_ep(desc: ctypes.Array, dims: tuple, h: torch.Tensor, norm_w: torch.Tensor,
+                 gate: Optional[torch.Tensor], bias: Optional[torch.Tensor], top_k: int, routed_scaling: float,
+                 peers: "_lib.HsEpPeers", eps: float = 1e-6, use_shared: bool = True,
+                 dup_mode: int = _lib.HS_DUP_LAST, num_experts: Optional[int] = None, expert_offset: int = 0,
+                 ids: Optional[torch.Tensor] = None, tid2eid: Optional[torch.Tensor] = None,
+                 h_out: Optional[torch.Tensor] = None, x_out: Optional[torch.Tensor] = None):
+    """moe_layer for one rank of an expert-parallel group over NVLink peer
+    memory (hs_moe_layer_fp4_ep): this rank's experts, their rows stored into
+    every rank's receive buffer by the down phase, summed in rank order into
+    h_out (identical on every rank). Every rank must make the same calls."""
+    dev = _check_cuda(h, norm_w, gate, bias, ids, tid2eid, h_out, x_out)
+    h = _rows(h, "h")
+    norm_w = _rows(norm_w, "norm_w")
+    T, D = h.shape
+    E, Dd, I, I_sh = dims
+    if D != Dd:
+        raise ValueError(f"hidden dim {D} != store dim {Dd}")
+    if tid2eid is None and (gate is None or gate.dtype != torch.bfloat16):
+        raise TypeError("router mode needs a bf16 gate")
+    n_exp = int(num_experts if num_experts is not None else (gate.shape[0] if gate is not None else E))
+    idx = torch.empty(T, top_k, dtype=torch.int64, device=dev)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws = workspace(dev, lib.hs_moe_workspace_size(T, top_k, D, I, I_sh), "moe")
+    ids_c = ids.reshape(-1).contiguous() if ids is not None else None
+    vocab = int(tid2eid.shape[0]) if tid2eid is not None else 0
+    if h_out is None:
+        h_out = torch.empty_like(h)
+    _launch("hs_moe_layer_fp4_ep", ctypes.addressof(desc), h.data_ptr(), norm_w.data_ptr(), float(eps),
+            None if tid2eid is not None else gate.data_ptr(), None if tid2eid is not None else _ptr(bias),
+            _ptr(ids_c), _ptr(tid2eid), vocab, n_exp, int(expert_offset), T, top_k, float(routed_scaling),
+            int(bool(use_shared) and bool(I_sh)), int(dup_mode), idx.data_ptr(), w.data_ptr(), _ptr(x_out),
+            ctypes.byref(peers), h_out.data_ptr(), ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(),
             _stream(dev))
     return h_out, idx, w
 

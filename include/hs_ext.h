@@ -328,6 +328,48 @@ int hs_moe_layer_fp4_partials(const void* desc, const void* h,
                               float* shared_f32, void* workspace,
                               size_t workspace_bytes, int32_t* dev_status,
                               void* stream);
+/* ------------------------------------------------------------------------ */
+/* Expert parallelism over NVLink peer memory (decode sizes, T <= 8).         */
+/* The reference's EP adds the GPUs' outputs on GPU 0 (engine.py:1575-1709,  */
+/* parallel.py:203-290); hs_moe_layer_fp4_partials + an NCCL all-reduce is    */
+/* this library's collective form of it. hs_moe_layer_fp4_ep fuses the        */
+/* exchange into the layer call instead: the down phase stores each rank's    */
+/* f32 routed/shared rows straight into every rank's receive buffer over      */
+/* NVLink (plain peer stores, no multicast; an entry is empty until stored,   */
+/* so the entries are their own arrival flags); a combine kernel waits        */
+/* (bounded) for this call's entries of all ranks, sums them in rank order    */
+/* (so every rank holds the same h), applies bf16(bf16(routed) +              */
+/* bf16(shared)) and the residual add, and empties the entries again. Setup,  */
+/* once per process and rank: hs_ep_buffer_alloc a buffer of                  */
+/* hs_ep_buffer_bytes(world, D) (zero-filled), exchange its handle from       */
+/* hs_ipc_get_handle with the other ranks, hs_ipc_open_handle theirs, and     */
+/* fill hs_ep_peers (recv[q] = rank q's buffer as mapped here, recv[rank] =   */
+/* the local one). Every rank must make the same sequence of calls. Limits:   */
+/* world <= HS_EP_MAX_RANKS, T <= 8, D <= 8192; the down phase must run on     */
+/* clusters (D = 4096 on a B200), else HS_ERR_UNSUPPORTED.                     */
+/* ------------------------------------------------------------------------ */
+#define HS_EP_MAX_RANKS 8
+#define HS_IPC_HANDLE_BYTES 64
+typedef struct hs_ep_peers {
+  int32_t rank, world;
+  void* recv[HS_EP_MAX_RANKS];
+} hs_ep_peers;
+size_t hs_ep_buffer_bytes(int64_t world, int64_t D);
+int hs_ep_buffer_alloc(size_t bytes, void** ptr);
+int hs_ep_buffer_free(void* ptr);
+int hs_ipc_get_handle(const void* ptr, void* handle, size_t handle_bytes);
+int hs_ipc_open_handle(const void* handle, void** ptr);
+int hs_ipc_close_handle(void* ptr);
+int hs_moe_layer_fp4_ep(const void* desc, const void* h, const void* norm_w,
+                        float eps, const void* gate, const void* bias,
+                        const int64_t* input_ids, const int64_t* tid2eid,
+                        int64_t vocab, int64_t num_experts,
+                        int64_t expert_offset, int64_t T, int64_t top_k,
+                        float routed_scaling, int use_shared, int dup_mode,
+                        int64_t* topk_idx, float* topk_w, void* x_out,
+                        const hs_ep_peers* peers, void* h_out, void* workspace,
+                        size_t workspace_bytes, int32_t* dev_status,
+                        void* stream);
 int hs_moe_combine(const float* routed_f32, const float* shared_f32,
                    int use_shared, int64_t T, int64_t D, void* out,
                    void* stream);

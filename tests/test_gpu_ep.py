@@ -115,3 +115,71 @@ def test_nccl_expert_parallel_matches_single_gpu():
         assert p.exitcode == 0
     for rank, rel in res:
         assert rel <= MOE_TOL, (rank, rel)
+
+
+def _p2p_rank(rank: int, world: int, port: int, q) -> None:
+    """One rank of a two-GPU group: four consecutive layer calls through the
+    peer-memory exchange (both slots used twice) against the single-GPU layer
+    call on the full store, and the ranks' results bit-identical."""
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    px = None
+    try:
+        from home_seek_b200 import ops
+        from home_seek_b200.ep import PeerExchange, shard_store
+        from home_seek_b200.expert_store import HBMExpertStore
+        full = HBMExpertStore(2, 256, 4096, 2048, 2048, device=dev)
+        full.fill_random(31)
+        sh = shard_store(full, rank, world)
+        px = PeerExchange(rank, world, 4096)
+        g = torch.Generator(device=dev).manual_seed(4)
+        h0 = (torch.randn(3, 4096, generator=g, device=dev) * 2).to(torch.bfloat16)
+        nw = (1 + 0.05 * torch.randn(2, 4096, generator=g, device=dev)).to(torch.bfloat16)
+        h_ep, h_ref = h0.clone(), h0.clone()
+        worst = 0.0
+        for call in range(4):
+            l = call % 2
+            lw = full.layers[l]
+            ops.moe_layer(full.desc(l), full.dims, h_ref, nw[l], lw.gate, lw.bias, 6, 1.5, h_out=h_ref)
+            ops.moe_layer_ep(sh.desc(l), sh.dims, h_ep, nw[l], lw.gate, lw.bias, 6, 1.5, px.peers,
+                             num_experts=256, expert_offset=sh.expert_offset, h_out=h_ep)
+            torch.cuda.synchronize()
+            d = (h_ep.float() - h_ref.float()).abs().max().item() / h_ref.float().abs().max().item()
+            worst = max(worst, d)
+            h_ep.copy_(h_ref)  # next call from the same input on both paths
+        status = ops.check_status(dev)
+        gathered = [torch.empty_like(h_ep) for _ in range(world)]
+        dist.all_gather(gathered, h_ep)
+        same = all(torch.equal(gathered[0], x) for x in gathered)
+        q.put((rank, worst, status, same))
+    finally:
+        if px is not None:
+            px.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_p2p_expert_parallel_layer_matches_single_gpu():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_p2p_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, worst, status, same in res:
+        assert status == 0, (rank, status)
+        assert same, rank
+        # bf16(h + y) against the single-GPU call: y differs by f32 summation order only
+        assert worst <= 2e-2, (rank, worst)
