@@ -2758,6 +2758,374 @@ static int launch_nt(int NT, const Desc& d, const CallMaps& cm, const UnitArgs& 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Token-major grouped GEMM for large calls (many pairs per expert)
+// ---------------------------------------------------------------------------
+// The kernels above put 128 weight rows on the MMA's M side and at most 24
+// pairs (48 hi/lo columns) on N, so each weight tile feeds few MACs and a
+// large call is bound by MMA issue. Here the roles swap: A = 128 consecutive
+// pair rows of one expert's chunk, as the hi and lo e4m3 planes (two MMAs into
+// one accumulator), and B = 128 weight rows (gate/up: the w1 and w3 tiles, one
+// N = 128 accumulator each; down: one w2 tile). A's scale factors are all 1;
+// each pair row's power-of-two prescale (2^e of the token row for gate/up,
+// 2^q of the activation for down) is undone in the epilogue, which is exact.
+// One CTA per SM: warp 4 streams TMA, warp 5 issues tcgen05 copies and MMAs,
+// warps 0-3 drain TMEM, one pair row per thread. Units (chunk x weight tile,
+// chunk-major so the CTAs on one chunk share its A rows through L2) go to the
+// CTAs round-robin and are never split. The down phase writes per-pair f32
+// rows and combine_rows_kernel sums them per token.
+constexpr int kTmCh = 128;                    // pairs per chunk (the MMA's M)
+constexpr int64_t kTmMinPairsPerExpert = 32;  // token-major once T*K >= this * E
+
+template <bool kDown>
+struct TmLayout {
+  static constexpr int kA = 2 * kBoxBytes;                // hi and lo planes of 128 pair rows
+  static constexpr int kB = (kDown ? 1 : 2) * kBoxBytes;  // the w2 tile, or the w1 and w3 tiles
+  static constexpr int kSF = (kDown ? 1 : 2) * 512;       // their scale-factor atoms
+  static constexpr int kStage = (kA + kB + kSF + 1023) / 1024 * 1024;
+  static constexpr int kStages = kDown ? 4 : 3;
+  static constexpr int kSfaOff = kStages * kStage;  // the all-ones A scale atom (512 B)
+  static constexpr int kBarOff = kSfaOff + 512;
+  static constexpr int kBytes = kBarOff + 256 + 1024;  // + slack to realign the base to 1024
+};
+
+struct TmBars {
+  uint64_t full[4];
+  uint64_t empty[4];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem;
+  int32_t issued, consumed;
+};
+
+// Down-phase weight maps with one 128-row tile (one k-step) per box.
+struct TmMaps {
+  CUtensorMap w2;
+  CUtensorMap sw2;
+};
+
+struct TmUnit {
+  int shared, e, pair0, np, tile;
+};
+
+__device__ __forceinline__ TmUnit tm_unit(const UnitArgs& a, int64_t u, int tiles_sh, int tiles_rt,
+                                          int64_t n_sh_units) {
+  TmUnit r;
+  if (u < n_sh_units) {
+    const int c = static_cast<int>(u / tiles_sh);
+    r.shared = 1;
+    r.tile = static_cast<int>(u - static_cast<int64_t>(c) * tiles_sh);
+    r.e = 0;
+    r.pair0 = c * kTmCh;  // the shared expert's rows are the token rows 0..T-1
+    r.np = min(kTmCh, a.T - r.pair0);
+  } else {
+    const int64_t uu = u - n_sh_units;
+    const int c = static_cast<int>(uu / tiles_rt);
+    r.shared = 0;
+    r.tile = static_cast<int>(uu - static_cast<int64_t>(c) * tiles_rt);
+    r.e = __ldcg(a.P.chunk_expert + c);
+    r.pair0 = __ldcg(a.P.chunk_pair0 + c);
+    r.np = __ldcg(a.P.chunk_np + c);
+  }
+  return r;
+}
+
+template <bool kDown>
+__global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__ Desc d,
+                                                         const __grid_constant__ CallMaps cm,
+                                                         const __grid_constant__ TmMaps tmm, UnitArgs a) {
+  using L = TmLayout<kDown>;
+  constexpr int S_ = L::kStages;
+  constexpr int NB = kDown ? 2 : 1;                  // accumulator buffers
+  constexpr uint32_t kAccCols = kDown ? 128u : 256u;  // gate/up: gate at +0, up at +128
+  constexpr uint32_t kSfa = 256;                      // the all-ones A scale atom
+  constexpr uint32_t kSfb = 264;                      // B scale atoms, 8 columns per stage
+  static_assert(kSfb + 8 * S_ <= 512, "TMEM columns");
+  static_assert(sizeof(TmBars) <= 256, "barrier block");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  TmBars* bars = reinterpret_cast<TmBars*>(base + L::kBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = d.D;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S_; ++i) {
+      mbar_init(&bars->full[i], 1);
+      mbar_init(&bars->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->acc_full[i], 1);
+      mbar_init(&bars->acc_empty[i], 4);
+    }
+    mbar_init(&bars->mma_done, 1);
+    bars->issued = 0;
+    bars->consumed = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    for (int i = lane; i < 128; i += 32) reinterpret_cast<uint32_t*>(base + L::kSfaOff)[i] = 0x7f7f7f7fu;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0) tc5::tmem_alloc(&bars->tmem, 512);
+  if (warp == 4 && lane == 0) {
+    prefetch_tensormap(kDown ? &tmm.w2 : &d.tm_w13);
+    prefetch_tensormap(kDown ? &tmm.sw2 : &d.tm_sw13);
+    prefetch_tensormap(kDown ? &cm.tm_act8 : &cm.tm_x8);
+  }
+  pdl_wait();
+  pdl_trigger();
+  tc5::fence_before_sync();
+  __syncthreads();
+  tc5::fence_after_sync();
+  const uint32_t tmem = bars->tmem;
+  const int tiles_sh = kDown ? D / kM : (d.has_shared ? d.I_sh / kM : 1);
+  const int tiles_rt = kDown ? D / kM : d.I / kM;
+  const int64_t n_sh_units = static_cast<int64_t>(a.n_sh_chunks) * tiles_sh;
+  const int64_t U = n_sh_units + static_cast<int64_t>(__ldcg(a.P.hdr)) * tiles_rt;
+  const int nk_sh = kDown ? d.I_sh / kM : D / kM;
+  const int nk_rt = kDown ? d.I / kM : D / kM;
+  const int64_t G = gridDim.x;
+
+  if (warp == 4) {
+    // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
+    int64_t step = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < U && ok; u += G) {
+      const TmUnit ui = tm_unit(a, u, tiles_sh, tiles_rt, n_sh_units);
+      const bool fp8 = ui.shared != 0;
+      const int nk = fp8 ? nk_sh : nk_rt;
+      const CUtensorMap* wm = kDown ? (fp8 ? &tmm.sw2 : &tmm.w2) : (fp8 ? &d.tm_sw13 : &d.tm_w13);
+      const CUtensorMap* am = kDown ? &cm.tm_act8 : &cm.tm_x8;
+      // the unit's first weight tile (gate/up: a w1, w3 tile pair per k-step)
+      int64_t t0;
+      const uint8_t* sf0;
+      if (!kDown) {
+        t0 = fp8 ? static_cast<int64_t>(ui.tile) * (D / kM)
+                 : (static_cast<int64_t>(ui.e) * (d.I / kM) + ui.tile) * (D / kM);
+        sf0 = (fp8 ? d.sh_s13a : d.s13a) + t0 * 1024;
+      } else {
+        t0 = fp8 ? static_cast<int64_t>(ui.tile) * (d.I_sh / kM)
+                 : (static_cast<int64_t>(ui.e) * (D / kM) + ui.tile) * (d.I / kM);
+        sf0 = (fp8 ? d.sh_s2a : d.s2a) + t0 * 512;
+      }
+      const int64_t y0 = t0 * (kDown ? kM : 2 * kM);
+      // transaction bytes: both A planes, the weight tiles as stored in global
+      // memory (packed e2m1 is half the shared-memory footprint), the atoms
+      const uint32_t wbytes = fp8 ? kBoxBytes : kBoxBytes / 2;
+      const uint32_t tx = 2 * kBoxBytes + (kDown ? 1u : 2u) * wbytes + L::kSF;
+      for (int k = 0; k < nk; ++k, ++step) {
+        const int st = static_cast<int>(step % S_);
+        if (step >= S_) {
+          bool w = true;
+          if (lane == 0) w = mbar_wait(&bars->empty[st], static_cast<uint32_t>(((step / S_) - 1) & 1));
+          w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+          if (!w) {
+            if (lane == 0) report(a.status, HS_DEV_TIMEOUT);
+            ok = false;
+            break;
+          }
+        }
+        if (lane == 0) {
+          uint8_t* S = base + st * L::kStage;
+          mbar_arrive_expect_tx(&bars->full[st], tx);
+          tma_load_3d(S, am, &bars->full[st], k * 128, ui.pair0, 0);
+          tma_load_2d(S + L::kA, wm, &bars->full[st], 0,
+                      static_cast<int>(y0 + static_cast<int64_t>(k) * (kDown ? kM : 2 * kM)));
+          bulk_load(S + L::kA + L::kB, sf0 + static_cast<int64_t>(k) * L::kSF, L::kSF, &bars->full[st]);
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) bars->issued = static_cast<int32_t>(step);
+  } else if (warp == 5) {
+    // ---------------- MMA issuer (lane 0) ----------------
+    if (lane == 0) {
+      tc5::cp_sf_32x128b(tmem + kSfa, tc5::sdesc_sf(smem_u32(base + L::kSfaOff)));
+      int64_t step = 0;
+      int seg = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; u < U && ok; u += G, ++seg) {
+        const bool fp8 = u < n_sh_units;
+        const int nk = fp8 ? nk_sh : nk_rt;
+        const uint32_t bfmt = fp8 ? 0u : 5u;
+        const int buf = seg % NB;
+        if (seg >= NB && !mbar_wait(&bars->acc_empty[buf], static_cast<uint32_t>(((seg / NB) - 1) & 1))) {
+          report(a.status, HS_DEV_TIMEOUT);
+          break;
+        }
+        tc5::fence_after_sync();
+        const uint32_t acc = tmem + buf * kAccCols;
+        for (int k = 0; k < nk; ++k, ++step) {
+          const int st = static_cast<int>(step % S_);
+          if (!mbar_wait(&bars->full[st], static_cast<uint32_t>((step / S_) & 1))) {
+            report(a.status, HS_DEV_TIMEOUT);
+            ok = false;
+            break;
+          }
+          tc5::fence_after_sync();
+          uint8_t* S = base + st * L::kStage;
+          const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
+          const uint32_t sfb = tmem + kSfb + st * 8;
+          tc5::cp_sf_32x128b(sfb, tc5::sdesc_sf(sSF));
+          if (!kDown) tc5::cp_sf_32x128b(sfb + 4, tc5::sdesc_sf(sSF + 512));
+#pragma unroll
+          for (int i = 0; i < (kDown ? 1 : 2); ++i) {  // gate (w1), up (w3)
+            const uint64_t bd = tc5::sdesc_sw128(sB + i * kBoxBytes);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // hi, lo planes
+              const uint64_t ad = tc5::sdesc_sw128(sA + h * kBoxBytes);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t id = tc5::idesc_mxf8f6f4_ab(0u, bfmt, 128, j, j);
+                const uint32_t accum = (k > 0 || h > 0 || j > 0) ? 1u : 0u;
+                tc5::mma_mxf8f6f4(acc + i * 128, ad + 2 * j, bd + 2 * j, id, accum,
+                                  (tmem + kSfa) | (static_cast<uint32_t>(j) << 30),
+                                  (sfb + 4 * i) | (static_cast<uint32_t>(j) << 30));
+              }
+            }
+          }
+          tc5::commit(&bars->empty[st]);
+        }
+        tc5::commit(&bars->acc_full[buf]);
+      }
+      // every tcgen05 operation of this thread done before TMEM is freed
+      bars->consumed = static_cast<int32_t>(step);
+      tc5::commit(&bars->mma_done);
+      if (!mbar_wait(&bars->mma_done, 0)) report(a.status, HS_DEV_TIMEOUT);
+    }
+  } else {
+    // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31 = pair rows) ----------------
+    const int row = 32 * warp + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+    const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
+    int seg = 0;
+    for (int64_t u = blockIdx.x; u < U; u += G, ++seg) {
+      const TmUnit ui = tm_unit(a, u, tiles_sh, tiles_rt, n_sh_units);
+      const int buf = seg % NB;
+      const bool valid = row < ui.np;
+      const int64_t p = static_cast<int64_t>(ui.pair0) + row;
+      float rs = 0.f, wb = 0.f, qs = 0.f;
+      if (valid) {
+        if (kDown) {
+          rs = exp2i(static_cast<int>(__ldcg(a.P.sb2 + p)) - 127);
+        } else {
+          rs = exp2i(static_cast<int>(__ldcg(a.P.sb1 + p)) - 127);
+          wb = __ldcg(a.P.pair_wb + p);
+          qs = exp2i(__ldcg(a.P.pair_q + p));
+        }
+      }
+      if (!mbar_wait(&bars->acc_full[buf], static_cast<uint32_t>((seg / NB) & 1))) {
+        if (threadIdx.x == 0) report(a.status, HS_DEV_TIMEOUT);
+        break;
+      }
+      tc5::fence_after_sync();
+      const uint32_t acc = tmem + lane_off + buf * kAccCols;
+      if constexpr (kDown) {
+        float* dst = a.P.out_part + p * D + ui.tile * kM;
+#pragma unroll 1
+        for (int g = 0; g < 4; ++g) {
+          float v0[16], v1[16];
+          tc5::ld_32x32b_x16(acc + g * 32, v0);
+          tc5::ld_32x32b_x16(acc + g * 32 + 16, v1);
+          tc5::wait_ld();
+          if (g == 3) {
+            tc5::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+          }
+          if (valid) {
+            float4* o = reinterpret_cast<float4*>(dst + g * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              o[i] = make_float4(v0[4 * i] * rs, v0[4 * i + 1] * rs, v0[4 * i + 2] * rs, v0[4 * i + 3] * rs);
+              o[4 + i] = make_float4(v1[4 * i] * rs, v1[4 * i + 1] * rs, v1[4 * i + 2] * rs, v1[4 * i + 3] * rs);
+            }
+          }
+        }
+      } else {
+        const bool fp8 = ui.shared != 0;
+        uint8_t* hi = a.P.act8 + p * I_act + ui.tile * kM;
+        uint8_t* lo = hi + a.act_rows * I_act;
+#pragma unroll 1
+        for (int g = 0; g < 4; ++g) {
+          float gv[32], uv[32];
+          tc5::ld_32x32b_x16(acc + g * 32, *reinterpret_cast<float(*)[16]>(gv));
+          tc5::ld_32x32b_x16(acc + g * 32 + 16, *reinterpret_cast<float(*)[16]>(gv + 16));
+          tc5::ld_32x32b_x16(acc + 128 + g * 32, *reinterpret_cast<float(*)[16]>(uv));
+          tc5::ld_32x32b_x16(acc + 128 + g * 32 + 16, *reinterpret_cast<float(*)[16]>(uv + 16));
+          tc5::wait_ld();
+          if (g == 3) {
+            tc5::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+          }
+          if (valid) {
+            uint32_t hw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, lw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              // reference roundings as in gateup_finish
+              const float gf = round_bf16(gv[i] * rs);
+              const float uf = round_bf16(uv[i] * rs);
+              const float gc = gf > 10.f ? 10.f : gf;
+              const float uc = uf > 10.f ? 10.f : (uf < -10.f ? -10.f : uf);
+              const float sig = 1.f / (1.f + expf(-gc));
+              float av = round_bf16((gc * sig) * uc);
+              if (!fp8) av = round_bf16(av * wb);
+              const float v = av * qs;
+              const __nv_fp8_storage_t hb = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+              const __half_raw hr = __nv_cvt_fp8_to_halfraw(hb, __NV_E4M3);
+              const float hf = __half2float(*reinterpret_cast<const __half*>(&hr));
+              const __nv_fp8_storage_t lb = __nv_cvt_float_to_fp8(v - hf, __NV_SATFINITE, __NV_E4M3);
+              hw[i >> 2] |= static_cast<uint32_t>(hb) << (8 * (i & 3));
+              lw[i >> 2] |= static_cast<uint32_t>(lb) << (8 * (i & 3));
+            }
+            uint4* ho = reinterpret_cast<uint4*>(hi + g * 32);
+            uint4* lo4 = reinterpret_cast<uint4*>(lo + g * 32);
+            ho[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            ho[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            lo4[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            lo4[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+          }
+        }
+      }
+    }
+  }
+
+  tc5::fence_before_sync();
+  __syncthreads();
+  // copies issued but never consumed (only after a timed-out wait): let them
+  // land before the CTA's shared memory is released
+  if (threadIdx.x == 128) {
+    for (int64_t k = bars->consumed; k < bars->issued; ++k)
+      if (!mbar_wait(&bars->full[k % S_], static_cast<uint32_t>((k / S_) & 1))) {
+        report(a.status, HS_DEV_TIMEOUT);
+        break;
+      }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc5::fence_after_sync();
+    tc5::tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool kDown>
+static int launch_tm(const Desc& d, const CallMaps& cm, const TmMaps& tmm, const UnitArgs& a, cudaStream_t st) {
+  constexpr int bytes = TmLayout<kDown>::kBytes;
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  HS_CUDA_CHECK(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(done.load() & bit)) {
+    HS_CUDA_CHECK(cudaFuncSetAttribute(tm_kernel<kDown>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.fetch_or(bit);
+  }
+  HS_CUDA_CHECK(launch_pdl(tm_kernel<kDown>, dim3(static_cast<unsigned>(sm_count())), dim3(kThreads), bytes, st, d,
+                           cm, tmm, a));
+  return check_launch();
+}
+
 
 static int plan_smem(int E, int npairs) {
   const int cached = npairs <= kLocalPairs ? 2 * npairs : 0;  // ids and post-duplicate experts
@@ -2929,16 +3297,19 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const Plan P = plan_views(g, workspace);
   const int NT = static_cast<int>(ntiles(T));
-  const int CH = 8 * NT;
   const int64_t npairs = T * top_k;
+  // many pairs per expert: the token-major kernels, chunks of 128 pairs
+  const bool tmaj = T > kTokMax && !route && npairs >= kTmMinPairsPerExpert * d.E;
+  const int CH = tmaj ? kTmCh : 8 * NT;
   const bool local_rows = npairs <= kLocalPairs;
 
   CallMaps cm;
   int rc;
   const bool tok = T <= kTokMax;
   // token mode reads the T token rows (rows T..7 of the box read as zero)
-  if ((rc = make_map_3d(&cm.tm_x8, P.x8, d.D, tok ? T : g.P_max, 2, d.D, 8 * NT, g.P_max))) return rc;
-  if ((rc = make_map_3d(&cm.tm_act8, P.act8, g.I_act, g.act_rows, 2, g.I_act, 8 * NT, g.act_rows)))
+  const uint32_t box_rows = tmaj ? kTmCh : 8 * NT;
+  if ((rc = make_map_3d(&cm.tm_x8, P.x8, d.D, tok ? T : g.P_max, 2, d.D, box_rows, g.P_max))) return rc;
+  if ((rc = make_map_3d(&cm.tm_act8, P.act8, g.I_act, g.act_rows, 2, g.I_act, box_rows, g.act_rows)))
     return rc;
 
   PlanArgs pa;
@@ -3045,9 +3416,23 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
                              static_cast<__nv_bfloat16*>(route->h_out), dev_status));
     return check_launch();
   }
-  if ((rc = launch_nt<false>(NT, d, cm, a, st))) return rc;
-  a.ucount = pa.ucount + g.U_gu;
-  if ((rc = launch_nt<true>(NT, d, cm, a, st))) return rc;
+  if (tmaj) {
+    TmMaps tmm;
+    const uint64_t E = d.E, D = d.D, I = d.I, Ish = d.I_sh;
+    if ((rc = make_map(&tmm.w2, d.w2, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 128, E * D * (I / 128), 64, 128, 128)))
+      return rc;
+    tmm.sw2 = tmm.w2;
+    if (use_shared &&
+        (rc = make_map(&tmm.sw2, d.sh_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, D * (Ish / 128), 128, 128, 128)))
+      return rc;
+    a.ext_combine = 1;
+    if ((rc = launch_tm<false>(d, cm, tmm, a, st))) return rc;
+    if ((rc = launch_tm<true>(d, cm, tmm, a, st))) return rc;
+  } else {
+    if ((rc = launch_nt<false>(NT, d, cm, a, st))) return rc;
+    a.ucount = pa.ucount + g.U_gu;
+    if ((rc = launch_nt<true>(NT, d, cm, a, st))) return rc;
+  }
   if (!a.ext_combine) return HS_OK;
   const int64_t nv = T * (d.D / 8);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((nv + 255) / 256, 8 * sm_count()));

@@ -59,6 +59,11 @@ HS_DI uint32_t idesc_mxf8f6f4(uint32_t a_fmt, uint32_t n, uint32_t a_sf_id, uint
   return d;
 }
 
+// The same descriptor with the B format given (bits 10-12): 5 = E2M1, 0 = E4M3.
+HS_DI uint32_t idesc_mxf8f6f4_ab(uint32_t a_fmt, uint32_t b_fmt, uint32_t n, uint32_t a_sf_id, uint32_t b_sf_id) {
+  return idesc_mxf8f6f4(a_fmt, n, a_sf_id, b_sf_id) | ((b_fmt & 7u) << 10);
+}
+
 HS_DI void mma_mxf8f6f4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate,
                         uint32_t tsfa, uint32_t tsfb) {
   asm volatile(
