@@ -199,7 +199,7 @@ def _graph_time_per_call(enqueue, n_calls: int, replays: int = 5) -> float:
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    with torch.cuda.graph(graph, stream=s):  # the warm-up's workspaces, no captured fill
         enqueue()
     for _ in range(2):
         graph.replay()

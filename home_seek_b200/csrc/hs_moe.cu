@@ -67,6 +67,9 @@ constexpr uint32_t kDescMagic = 0x48534d33u;  // "HSM3" (tiled weights)
 constexpr int kTokMax = 8;              // T <= this: token mode (activation rows per token, not per pair)
 constexpr int kInlineCombineMax = 64;   // T above this: the down phase's outputs are combined by a separate grid
 constexpr int kTokChunks = 128;         // token mode: at most T*K <= 8*16 routed chunks
+constexpr int kSegPairs = 1024;         // segmented plan: pairs per counting CTA
+constexpr int kSegMaxE = 256;           // segmented plan: experts per call at most
+constexpr int kSegTicket = 15;          // plan header word: the counting CTAs' ticket (left at 0)
 constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two independent MMA streams)
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
 
@@ -148,7 +151,7 @@ struct Geometry {
   int64_t slot_floats;     // floats per partial slot (gate/up, the larger)
   int64_t act_rows;        // rows per activation plane
   size_t off_hdr, off_chunk, off_pair, off_sb, off_tok, off_tokpos, off_dcount, off_x8, off_act8, off_out,
-      off_ucount, off_part, off_ctab, total;
+      off_ucount, off_part, off_ctab, off_seg, total;
 };
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -205,6 +208,9 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   o = align_up(o + 2 * static_cast<int64_t>(G) * g.slot_floats * sizeof(float), 256);
   g.off_ctab = o;
   o = align_up(o + g.C_max * 8 * (sizeof(float) + 1), 256);
+  // segmented plan: per-pair ranks, per-segment offsets, expert bases
+  g.off_seg = o;
+  o = align_up(o + (Pr + ((Pr + kSegPairs - 1) / kSegPairs) * kSegMaxE + kSegMaxE) * sizeof(int32_t), 256);
   g.total = o;
   return g;
 }
@@ -259,6 +265,12 @@ struct PlanArgs {
   int32_t* status;
   uint32_t* ucount;  // stream-K unit tickets to clear (all plan CTAs share the work)
   int64_t n_ucount;
+  // segmented plan (plan_seg_kernel ran first; nullptr: off): a pair's rank
+  // among its expert's pairs in its segment, [segment][E] offsets of the
+  // segments, [E] first position of each expert (without pos_offset)
+  const int32_t* seg_lrank;
+  const int32_t* seg_off;
+  const int32_t* seg_base;
 };
 
 // Power-of-two prescale for an activation aw = bf16(a * wb), |a| <= 100:
@@ -328,6 +340,142 @@ __device__ __forceinline__ void split16(const uint4& a, const uint4& b, float sc
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// Segmented plan for calls with many pairs (a stable counting sort of the
+// pairs by expert, the order the single-CTA plan below produces). CTA s ranks
+// the pairs of segment s (kSegPairs consecutive pairs) among the segment's
+// pairs of the same expert (warp match + per-warp counts) and publishes the
+// segment's per-expert counts; the last CTA to finish (a ticket in the plan
+// header, reset for the next call) turns the counts into per-segment offsets
+// and expert bases and writes the chunk table and the header. The token CTAs
+// of plan_kernel then place their own pairs: position = T + base[e] +
+// offset[segment][e] + rank.
+__global__ void __launch_bounds__(kSegPairs) plan_seg_kernel(PlanArgs A, Plan P, int32_t* lrank, int32_t* segoff,
+                                                            int32_t* ebase) {
+  __shared__ int32_t wc[kSegPairs / 32][kSegMaxE];
+  __shared__ int32_t hist[kSegMaxE];
+  __shared__ int32_t base[kSegMaxE + 1];
+  __shared__ int32_t cbase[kSegMaxE + 1];
+  __shared__ int32_t slots;
+  __shared__ int last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = A.K, E = A.E;
+  const int npairs = A.T * K;
+  pdl_wait();
+  pdl_trigger();
+  const int l = blockIdx.x * kSegPairs + tid;
+  int e = -1;
+  if (l < npairs) {
+    const int t = l / K, j = l - t * K;
+    int32_t row[16];
+    for (int jj = 0; jj < K; ++jj) row[jj] = clamp_id(A.topk_idx[static_cast<int64_t>(t) * K + jj], E);
+    if (row[j] == kBadId) report(A.status, HS_DEV_BAD_EXPERT);
+    e = pair_expert(row, nullptr, j, K, A.dup_mode, nullptr);
+  }
+  for (int x = lane; x < E; x += 32) wc[warp][x] = 0;
+  __syncwarp();
+  const unsigned msk = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(msk & ((1u << lane) - 1u));
+  if (e >= 0 && rank == 0) wc[warp][e] = __popc(msk);
+  __syncthreads();
+  if (tid < E) {
+    int run = 0;
+    for (int w = 0; w < kSegPairs / 32; ++w) {
+      const int c = wc[w][tid];
+      wc[w][tid] = run;
+      run += c;
+    }
+    segoff[static_cast<int64_t>(blockIdx.x) * E + tid] = run;
+  }
+  __syncthreads();
+  if (e >= 0) lrank[l] = wc[warp][e] + rank;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(reinterpret_cast<unsigned int*>(P.hdr + kSegTicket), 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // ---- last CTA: offsets of every segment per expert ----
+  // thread (part, e) scans segments [part * per, (part + 1) * per) of expert e
+  const int nseg = gridDim.x;
+  const int parts = kSegPairs / E;
+  const int per = (nseg + parts - 1) / parts;
+  const int pe = tid % E, part = tid / E;
+  int32_t* ps = &wc[0][0];  // [parts][E] partial sums
+  if (part < parts) {
+    int sum = 0;
+    for (int sg = part * per; sg < min(nseg, (part + 1) * per); ++sg) sum += __ldcg(segoff + static_cast<int64_t>(sg) * E + pe);
+    ps[part * E + pe] = sum;
+  }
+  __syncthreads();
+  if (tid < E) {
+    int run = 0;
+    for (int pp = 0; pp < parts; ++pp) {
+      const int c = ps[pp * E + tid];
+      ps[pp * E + tid] = run;
+      run += c;
+    }
+    hist[tid] = run;
+  }
+  if (tid == 0) slots = 0;
+  __syncthreads();
+  if (part < parts) {
+    int run = ps[part * E + pe];
+    for (int sg = part * per; sg < min(nseg, (part + 1) * per); ++sg) {
+      int32_t* q = segoff + static_cast<int64_t>(sg) * E + pe;
+      const int c = __ldcg(q);
+      *q = run;
+      run += c;
+    }
+  }
+  // ---- expert bases and chunk bases (exclusive scans over experts) ----
+  if (warp == 0) {
+    int run = 0, crun = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int x0 = e0 + lane;
+      const int hh = x0 < E ? hist[x0] : 0;
+      const int c = (hh + A.CH - 1) / A.CH;
+      int x = hh, y = c;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int xv = __shfl_up_sync(0xffffffffu, x, o);
+        const int yv = __shfl_up_sync(0xffffffffu, y, o);
+        if (lane >= o) {
+          x += xv;
+          y += yv;
+        }
+      }
+      if (x0 < E) {
+        base[x0] = run + x - hh;
+        cbase[x0] = crun + y - c;
+      }
+      run += __shfl_sync(0xffffffffu, x, 31);
+      crun += __shfl_sync(0xffffffffu, y, 31);
+    }
+    if (lane == 0) {
+      base[E] = run;
+      cbase[E] = crun;
+    }
+  }
+  __syncthreads();
+  if (tid < E) {
+    const int hh = hist[tid];
+    ebase[tid] = base[tid];
+    if (hh > 0) atomicAdd(&slots, 1);
+    int cb = cbase[tid];
+    for (int c = 0; c * A.CH < hh; ++c, ++cb) {
+      P.chunk_expert[cb] = tid;
+      P.chunk_pair0[cb] = A.pos_offset + base[tid] + c * A.CH;
+      P.chunk_np[cb] = min(A.CH, hh - c * A.CH);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    P.hdr[0] = cbase[E];
+    P.hdr[1] = slots;
+    P.hdr[2] = base[E];
+    P.hdr[kSegTicket] = 0;
+  }
+}
+
 // Block 0 builds the routing plan; blocks 1..T (MoE call only) convert one
 // token row each into its shared-expert row and, when local_rows is set, its
 // routed pair rows (positions recomputed locally from the same counts).
@@ -336,7 +484,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
   const int tid = threadIdx.x;
   const int T = A.T, K = A.K, E = A.E;
   const int npairs = T * K;
-  const bool cache_idx = npairs <= kLocalPairs;
+  const bool cache_idx = npairs <= kLocalPairs && !A.seg_lrank;
   pdl_trigger();  // the MoE kernels may start their prologues
   pdl_wait();     // router outputs (and everything earlier) are complete
   // token CTAs: thread k16 holds values 16*k16 .. 16*k16+15 of the row in
@@ -408,6 +556,51 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
         if (lane == 0) rows[1 + warp] = e >= 0 ? A.pos_offset + base + rank : -1;
       }
     }
+    if (A.seg_lrank) {
+      // segmented plan: lane j of warp 0 places this token's pair j from the
+      // counts plan_seg_kernel left (the expert's base, the segment's offset,
+      // the pair's rank in its segment), records the pair and the token's
+      // sorted positions; the token's rows then go to all its positions
+      nrows = 1 + K;
+      if (warp == 0) {
+        int pos = -1;
+        if (lane < K) {
+          int32_t row[16];
+          for (int jj = 0; jj < K; ++jj) row[jj] = clamp_id(A.topk_idx[static_cast<int64_t>(t) * K + jj], E);
+          const float* wrow = A.topk_w ? A.topk_w + static_cast<int64_t>(t) * K : nullptr;
+          float wsum = 0.f;
+          const int e = pair_expert(row, wrow, lane, K, A.dup_mode, &wsum);
+          if (e >= 0) {
+            const int l = t * K + lane;
+            pos = A.pos_offset + __ldcg(A.seg_base + e) +
+                  __ldcg(A.seg_off + static_cast<int64_t>(l / kSegPairs) * E + e) + __ldcg(A.seg_lrank + l);
+            const float wb = round_bf16(wsum);
+            const int q = act_prescale(wb);
+            P.pair_token[pos] = t;
+            P.pair_wb[pos] = wb;
+            P.pair_q[pos] = q;
+            P.sb2[pos] = static_cast<uint8_t>(127 - q);
+          }
+        }
+        int nvalid = 0, rank = 0;
+        for (int j = 0; j < K; ++j) {
+          const int p2 = __shfl_sync(0xffffffffu, pos, j);
+          nvalid += p2 >= 0;
+          rank += (p2 >= 0) & (pos >= 0) & (p2 < pos);
+        }
+        if (lane < K) {
+          if (pos >= 0) P.tok_pos[static_cast<int64_t>(t) * K + rank] = pos;
+          if (lane >= nvalid) P.tok_pos[static_cast<int64_t>(t) * K + lane] = -1;
+          rows[1 + lane] = pos;
+        }
+        if (lane == 0) {  // the token's shared-expert pair
+          P.pair_token[t] = t;
+          P.pair_wb[t] = 1.f;
+          P.pair_q[t] = 0;
+          P.sb2[t] = 127;
+        }
+      }
+    }
     __syncthreads();
     if (tid == 0) {
       float v = 0.f;
@@ -438,6 +631,11 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
       }
     }
     if (tid < nrows && rows[tid] >= 0) P.sb1[rows[tid]] = static_cast<uint8_t>(127 - e);
+    return;
+  }
+
+  if (A.seg_lrank) {  // plan_seg_kernel built the plan
+    for (int i = tid; i < A.n_dcount; i += blockDim.x) P.dcount[i] = 0u;
     return;
   }
 
@@ -2769,12 +2967,15 @@ static int launch_nt(int NT, const Desc& d, const CallMaps& cm, const UnitArgs& 
 // N = 128 accumulator each; down: one w2 tile). A's scale factors are all 1;
 // each pair row's power-of-two prescale (2^e of the token row for gate/up,
 // 2^q of the activation for down) is undone in the epilogue, which is exact.
-// One CTA per SM: warp 4 streams TMA, warp 5 issues tcgen05 copies and MMAs,
-// warps 0-3 drain TMEM, one pair row per thread. Units (chunk x weight tile,
+// One CTA per SM: warp 8 streams TMA, warp 9 issues tcgen05 copies and MMAs,
+// warps 0-7 drain TMEM (two warps per pair row quadrant, half the columns
+// each: the gate/up accumulator is single-buffered, so its epilogue is on the
+// MMA's critical path). Units (chunk x weight tile,
 // chunk-major so the CTAs on one chunk share its A rows through L2) go to the
 // CTAs round-robin and are never split. The down phase writes per-pair f32
 // rows and combine_rows_kernel sums them per token.
 constexpr int kTmCh = 128;                    // pairs per chunk (the MMA's M)
+constexpr int kTmThreads = 320;               // warps 0-7 epilogue, warp 8 TMA, warp 9 MMA
 constexpr int64_t kTmMinPairsPerExpert = 32;  // token-major once T*K >= this * E
 
 template <bool kDown>
@@ -2832,7 +3033,7 @@ __device__ __forceinline__ TmUnit tm_unit(const UnitArgs& a, int64_t u, int tile
 }
 
 template <bool kDown>
-__global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__ Desc d,
+__global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant__ Desc d,
                                                          const __grid_constant__ CallMaps cm,
                                                          const __grid_constant__ TmMaps tmm, UnitArgs a) {
   using L = TmLayout<kDown>;
@@ -2856,19 +3057,19 @@ __global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->acc_full[i], 1);
-      mbar_init(&bars->acc_empty[i], 4);
+      mbar_init(&bars->acc_empty[i], 8);
     }
     mbar_init(&bars->mma_done, 1);
     bars->issued = 0;
     bars->consumed = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     for (int i = lane; i < 128; i += 32) reinterpret_cast<uint32_t*>(base + L::kSfaOff)[i] = 0x7f7f7f7fu;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 0) tc5::tmem_alloc(&bars->tmem, 512);
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     prefetch_tensormap(kDown ? &tmm.w2 : &d.tm_w13);
     prefetch_tensormap(kDown ? &tmm.sw2 : &d.tm_sw13);
     prefetch_tensormap(kDown ? &cm.tm_act8 : &cm.tm_x8);
@@ -2887,7 +3088,7 @@ __global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__
   const int nk_rt = kDown ? d.I / kM : D / kM;
   const int64_t G = gridDim.x;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
     int64_t step = 0;
     bool ok = true;
@@ -2938,7 +3139,7 @@ __global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__
       }
     }
     if (lane == 0) bars->issued = static_cast<int32_t>(step);
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer (lane 0) ----------------
     if (lane == 0) {
       tc5::cp_sf_32x128b(tmem + kSfa, tc5::sdesc_sf(smem_u32(base + L::kSfaOff)));
@@ -2995,9 +3196,12 @@ __global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__
       if (!mbar_wait(&bars->mma_done, 0)) report(a.status, HS_DEV_TIMEOUT);
     }
   } else {
-    // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31 = pair rows) ----------------
-    const int row = 32 * warp + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
+    // ---------------- epilogue (warps 0-7) ----------------
+    // warp w reads TMEM lanes 32 (w % 4) .. +31 (its pair rows) and columns
+    // [64 (w / 4), +64) of each accumulator
+    const int row = 32 * (warp & 3) + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const int c0 = 64 * (warp >> 2);
     const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
     int seg = 0;
     for (int64_t u = blockIdx.x; u < U; u += G, ++seg) {
@@ -3020,16 +3224,16 @@ __global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__
         break;
       }
       tc5::fence_after_sync();
-      const uint32_t acc = tmem + lane_off + buf * kAccCols;
+      const uint32_t acc = tmem + lane_off + buf * kAccCols + c0;
       if constexpr (kDown) {
-        float* dst = a.P.out_part + p * D + ui.tile * kM;
+        float* dst = a.P.out_part + p * D + ui.tile * kM + c0;
 #pragma unroll 1
-        for (int g = 0; g < 4; ++g) {
+        for (int g = 0; g < 2; ++g) {
           float v0[16], v1[16];
           tc5::ld_32x32b_x16(acc + g * 32, v0);
           tc5::ld_32x32b_x16(acc + g * 32 + 16, v1);
           tc5::wait_ld();
-          if (g == 3) {
+          if (g == 1) {
             tc5::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
@@ -3045,17 +3249,17 @@ __global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__
         }
       } else {
         const bool fp8 = ui.shared != 0;
-        uint8_t* hi = a.P.act8 + p * I_act + ui.tile * kM;
+        uint8_t* hi = a.P.act8 + p * I_act + ui.tile * kM + c0;
         uint8_t* lo = hi + a.act_rows * I_act;
 #pragma unroll 1
-        for (int g = 0; g < 4; ++g) {
+        for (int g = 0; g < 2; ++g) {
           float gv[32], uv[32];
           tc5::ld_32x32b_x16(acc + g * 32, *reinterpret_cast<float(*)[16]>(gv));
           tc5::ld_32x32b_x16(acc + g * 32 + 16, *reinterpret_cast<float(*)[16]>(gv + 16));
           tc5::ld_32x32b_x16(acc + 128 + g * 32, *reinterpret_cast<float(*)[16]>(uv));
           tc5::ld_32x32b_x16(acc + 128 + g * 32 + 16, *reinterpret_cast<float(*)[16]>(uv + 16));
           tc5::wait_ld();
-          if (g == 3) {
+          if (g == 1) {
             tc5::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
@@ -3096,7 +3300,7 @@ __global__ void __launch_bounds__(kThreads, 1) tm_kernel(const __grid_constant__
   __syncthreads();
   // copies issued but never consumed (only after a timed-out wait): let them
   // land before the CTA's shared memory is released
-  if (threadIdx.x == 128) {
+  if (threadIdx.x == 256) {  // the producer's lane 0
     for (int64_t k = bars->consumed; k < bars->issued; ++k)
       if (!mbar_wait(&bars->full[k % S_], static_cast<uint32_t>((k / S_) & 1))) {
         report(a.status, HS_DEV_TIMEOUT);
@@ -3121,7 +3325,7 @@ static int launch_tm(const Desc& d, const CallMaps& cm, const TmMaps& tmm, const
     HS_CUDA_CHECK(cudaFuncSetAttribute(tm_kernel<kDown>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
     done.fetch_or(bit);
   }
-  HS_CUDA_CHECK(launch_pdl(tm_kernel<kDown>, dim3(static_cast<unsigned>(sm_count())), dim3(kThreads), bytes, st, d,
+  HS_CUDA_CHECK(launch_pdl(tm_kernel<kDown>, dim3(static_cast<unsigned>(sm_count())), dim3(kTmThreads), bytes, st, d,
                            cm, tmm, a));
   return check_launch();
 }
@@ -3134,8 +3338,15 @@ static int plan_smem(int E, int npairs) {
   return static_cast<int>((cached + std::max(general, fast)) * sizeof(int32_t));
 }
 
+static int launch_seg(const PlanArgs& pa, const Plan& P, int nseg, int32_t* seg_ws, cudaStream_t st) {
+  const int64_t npairs = static_cast<int64_t>(pa.T) * pa.K;
+  HS_CUDA_CHECK(launch_pdl(plan_seg_kernel, dim3(static_cast<unsigned>(nseg)), dim3(kSegPairs), 0, st, pa, P, seg_ws,
+                           seg_ws + npairs, seg_ws + npairs + static_cast<int64_t>(nseg) * kSegMaxE));
+  return check_launch();
+}
+
 static int launch_plan(const PlanArgs& pa, const Plan& P, int grid, cudaStream_t st) {
-  const int smem = plan_smem(pa.E, pa.T * pa.K);
+  const int smem = pa.seg_lrank ? 0 : plan_smem(pa.E, pa.T * pa.K);
   if (smem > 200 * 1024) return HS_ERR_BAD_SHAPE;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
@@ -3326,13 +3537,23 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   pa.sort_tok = 1;
   pa.n_dcount = d.D / kM;
   pa.P_max = g.P_max;
-  pa.local_rows = local_rows ? 1 : 0;
+  // many pairs: the segmented plan (plan_seg_kernel + token CTAs placing their pairs and rows)
+  const bool seg = !tok && !route && npairs > kFastPlanPairs && d.E <= kSegMaxE;
+  pa.local_rows = local_rows && !seg ? 1 : 0;
   pa.tok_mode = tok ? 1 : 0;
   pa.n_ctab = tok ? g.C_max * 8 : 0;
   pa.po = PermuteOut{nullptr, nullptr, nullptr};
   pa.status = dev_status;
   pa.ucount = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + g.off_ucount);
   pa.n_ucount = g.U_gu + g.U_dn;
+  pa.seg_lrank = pa.seg_off = pa.seg_base = nullptr;
+  int32_t* seg_ws = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + g.off_seg);
+  const int nseg = static_cast<int>((npairs + kSegPairs - 1) / kSegPairs);
+  if (seg) {
+    pa.seg_lrank = seg_ws;
+    pa.seg_off = seg_ws + npairs;
+    pa.seg_base = seg_ws + npairs + static_cast<int64_t>(nseg) * kSegMaxE;
+  }
   if (route) {
     RouteArgs ra;
     const bool hash = route->tid2eid != nullptr;
@@ -3362,10 +3583,12 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
     ra.n_ctab = g.C_max * 8;
     ra.P_max = g.P_max;
     if ((rc = launch_route(ra, P, d, st))) return rc;
+  } else if (seg && (rc = launch_seg(pa, P, nseg, seg_ws, st))) {
+    return rc;
   } else if ((rc = launch_plan(pa, P, 1 + static_cast<int>(T), st))) {
     return rc;
   }
-  if (!route && !local_rows && !tok) {
+  if (!route && !local_rows && !tok && !seg) {
     HS_CUDA_CHECK(launch_pdl(gather_kernel, dim3(static_cast<unsigned>(npairs)), dim3(256), 0, st, P,
                              static_cast<int>(T), g.P_max, d.D));
     if ((rc = check_launch())) return rc;
@@ -3627,6 +3850,7 @@ extern "C" int hs_moe_permute(const int64_t* topk_idx, int64_t T, int64_t top_k,
   pa.status = dev_status;
   pa.ucount = nullptr;
   pa.n_ucount = 0;
+  pa.seg_lrank = pa.seg_off = pa.seg_base = nullptr;
   int rc = launch_plan(pa, P, 1, st);
   if (rc) return rc;
   if (x_expanded) {

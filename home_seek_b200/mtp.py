@@ -250,7 +250,9 @@ class MTPDecoder:
                 self.iteration()
         torch.cuda.current_stream().wait_stream(s)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+        # capture on the warm-up stream: the per-stream workspaces it allocated
+        # (zero-filled once) are reused, so no fill is captured into the graph
+        with torch.cuda.graph(self.graph, stream=s):
             self.iteration()
 
     def replay(self) -> None:
