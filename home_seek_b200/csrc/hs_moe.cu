@@ -2963,8 +2963,9 @@ static int launch_nt(int NT, const Desc& d, const CallMaps& cm, const UnitArgs& 
 // pairs (48 hi/lo columns) on N, so each weight tile feeds few MACs and a
 // large call is bound by MMA issue. Here the roles swap: A = 128 consecutive
 // pair rows of one expert's chunk, as the hi and lo e4m3 planes (two MMAs into
-// one accumulator), and B = 128 weight rows (gate/up: the w1 and w3 tiles, one
-// N = 128 accumulator each; down: one w2 tile). A's scale factors are all 1;
+// one accumulator), and B = two 128-row weight tiles, one N = 128 accumulator
+// each (gate/up: the w1 and w3 tiles; down: the w2 tiles of two consecutive
+// 128-row slices of D, so each A tile feeds twice the MACs). A's scale factors are all 1;
 // each pair row's power-of-two prescale (2^e of the token row for gate/up,
 // 2^q of the activation for down) is undone in the epilogue, which is exact.
 // One CTA per SM: warp 8 streams TMA, warp 9 issues tcgen05 copies and MMAs,
@@ -2980,11 +2981,11 @@ constexpr int64_t kTmMinPairsPerExpert = 32;  // token-major once T*K >= this * 
 
 template <bool kDown>
 struct TmLayout {
-  static constexpr int kA = 2 * kBoxBytes;                // hi and lo planes of 128 pair rows
-  static constexpr int kB = (kDown ? 1 : 2) * kBoxBytes;  // the w2 tile, or the w1 and w3 tiles
-  static constexpr int kSF = (kDown ? 1 : 2) * 512;       // their scale-factor atoms
+  static constexpr int kA = 2 * kBoxBytes;  // hi and lo planes of 128 pair rows
+  static constexpr int kB = 2 * kBoxBytes;  // the w1 and w3 tiles, or two w2 tiles (256 rows of D)
+  static constexpr int kSF = 2 * 512;       // their scale-factor atoms
   static constexpr int kStage = (kA + kB + kSF + 1023) / 1024 * 1024;
-  static constexpr int kStages = kDown ? 4 : 3;
+  static constexpr int kStages = 3;
   static constexpr int kSfaOff = kStages * kStage;  // the all-ones A scale atom (512 B)
   static constexpr int kBarOff = kSfaOff + 512;
   static constexpr int kBytes = kBarOff + 256 + 1024;  // + slack to realign the base to 1024
@@ -3038,8 +3039,8 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
                                                          const __grid_constant__ TmMaps tmm, UnitArgs a) {
   using L = TmLayout<kDown>;
   constexpr int S_ = L::kStages;
-  constexpr int NB = kDown ? 2 : 1;                  // accumulator buffers
-  constexpr uint32_t kAccCols = kDown ? 128u : 256u;  // gate/up: gate at +0, up at +128
+  constexpr int NB = 1;                // accumulator buffers (256 columns each)
+  constexpr uint32_t kAccCols = 256u;  // gate at +0, up at +128; down: D-tiles 2j at +0, 2j+1 at +128
   constexpr uint32_t kSfa = 256;                      // the all-ones A scale atom
   constexpr uint32_t kSfb = 264;                      // B scale atoms, 8 columns per stage
   static_assert(kSfb + 8 * S_ <= 512, "TMEM columns");
@@ -3080,8 +3081,8 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
   __syncthreads();
   tc5::fence_after_sync();
   const uint32_t tmem = bars->tmem;
-  const int tiles_sh = kDown ? D / kM : (d.has_shared ? d.I_sh / kM : 1);
-  const int tiles_rt = kDown ? D / kM : d.I / kM;
+  const int tiles_sh = kDown ? D / (2 * kM) : (d.has_shared ? d.I_sh / kM : 1);
+  const int tiles_rt = kDown ? D / (2 * kM) : d.I / kM;
   const int64_t n_sh_units = static_cast<int64_t>(a.n_sh_chunks) * tiles_sh;
   const int64_t U = n_sh_units + static_cast<int64_t>(__ldcg(a.P.hdr)) * tiles_rt;
   const int nk_sh = kDown ? d.I_sh / kM : D / kM;
@@ -3098,7 +3099,8 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
       const int nk = fp8 ? nk_sh : nk_rt;
       const CUtensorMap* wm = kDown ? (fp8 ? &tmm.sw2 : &tmm.w2) : (fp8 ? &d.tm_sw13 : &d.tm_w13);
       const CUtensorMap* am = kDown ? &cm.tm_act8 : &cm.tm_x8;
-      // the unit's first weight tile (gate/up: a w1, w3 tile pair per k-step)
+      // the unit's first weight tile. gate/up: a (w1, w3) tile pair per k-step,
+      // adjacent; down: tiles 2j and 2j+1 of D, nk tiles apart
       int64_t t0;
       const uint8_t* sf0;
       if (!kDown) {
@@ -3106,15 +3108,15 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
                  : (static_cast<int64_t>(ui.e) * (d.I / kM) + ui.tile) * (D / kM);
         sf0 = (fp8 ? d.sh_s13a : d.s13a) + t0 * 1024;
       } else {
-        t0 = fp8 ? static_cast<int64_t>(ui.tile) * (d.I_sh / kM)
-                 : (static_cast<int64_t>(ui.e) * (D / kM) + ui.tile) * (d.I / kM);
+        t0 = fp8 ? static_cast<int64_t>(2 * ui.tile) * nk_sh
+                 : (static_cast<int64_t>(ui.e) * (D / kM) + 2 * ui.tile) * nk_rt;
         sf0 = (fp8 ? d.sh_s2a : d.s2a) + t0 * 512;
       }
       const int64_t y0 = t0 * (kDown ? kM : 2 * kM);
       // transaction bytes: both A planes, the weight tiles as stored in global
       // memory (packed e2m1 is half the shared-memory footprint), the atoms
       const uint32_t wbytes = fp8 ? kBoxBytes : kBoxBytes / 2;
-      const uint32_t tx = 2 * kBoxBytes + (kDown ? 1u : 2u) * wbytes + L::kSF;
+      const uint32_t tx = 2 * kBoxBytes + 2u * wbytes + L::kSF;
       for (int k = 0; k < nk; ++k, ++step) {
         const int st = static_cast<int>(step % S_);
         if (step >= S_) {
@@ -3131,9 +3133,17 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
           uint8_t* S = base + st * L::kStage;
           mbar_arrive_expect_tx(&bars->full[st], tx);
           tma_load_3d(S, am, &bars->full[st], k * 128, ui.pair0, 0);
-          tma_load_2d(S + L::kA, wm, &bars->full[st], 0,
-                      static_cast<int>(y0 + static_cast<int64_t>(k) * (kDown ? kM : 2 * kM)));
-          bulk_load(S + L::kA + L::kB, sf0 + static_cast<int64_t>(k) * L::kSF, L::kSF, &bars->full[st]);
+          if (!kDown) {
+            tma_load_2d(S + L::kA, wm, &bars->full[st], 0, static_cast<int>(y0 + static_cast<int64_t>(k) * 2 * kM));
+            bulk_load(S + L::kA + L::kB, sf0 + static_cast<int64_t>(k) * 1024, 1024, &bars->full[st]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int64_t tk = static_cast<int64_t>(i) * nk + k;  // tile 2j + i, k-step k
+              tma_load_2d(S + L::kA + i * kBoxBytes, wm, &bars->full[st], 0, static_cast<int>(y0 + tk * kM));
+              bulk_load(S + L::kA + L::kB + i * 512, sf0 + tk * 512, 512, &bars->full[st]);
+            }
+          }
         }
         __syncwarp();
       }
@@ -3169,9 +3179,9 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
           const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
           const uint32_t sfb = tmem + kSfb + st * 8;
           tc5::cp_sf_32x128b(sfb, tc5::sdesc_sf(sSF));
-          if (!kDown) tc5::cp_sf_32x128b(sfb + 4, tc5::sdesc_sf(sSF + 512));
+          tc5::cp_sf_32x128b(sfb + 4, tc5::sdesc_sf(sSF + 512));
 #pragma unroll
-          for (int i = 0; i < (kDown ? 1 : 2); ++i) {  // gate (w1), up (w3)
+          for (int i = 0; i < 2; ++i) {  // gate (w1), up (w3); or D-tiles 2j, 2j+1
             const uint64_t bd = tc5::sdesc_sw128(sB + i * kBoxBytes);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {  // hi, lo planes
@@ -3224,16 +3234,17 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
         break;
       }
       tc5::fence_after_sync();
-      const uint32_t acc = tmem + lane_off + buf * kAccCols + c0;
       if constexpr (kDown) {
-        float* dst = a.P.out_part + p * D + ui.tile * kM + c0;
+        // warp half h: columns [128 h, 128 h + 128) = D-tile 2j + h
+        const uint32_t accd = tmem + lane_off + buf * kAccCols + 128 * (warp >> 2);
+        float* dst = a.P.out_part + p * D + ui.tile * (2 * kM) + 128 * (warp >> 2);
 #pragma unroll 1
-        for (int g = 0; g < 2; ++g) {
+        for (int g = 0; g < 4; ++g) {
           float v0[16], v1[16];
-          tc5::ld_32x32b_x16(acc + g * 32, v0);
-          tc5::ld_32x32b_x16(acc + g * 32 + 16, v1);
+          tc5::ld_32x32b_x16(accd + g * 32, v0);
+          tc5::ld_32x32b_x16(accd + g * 32 + 16, v1);
           tc5::wait_ld();
-          if (g == 1) {
+          if (g == 3) {
             tc5::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
@@ -3248,6 +3259,7 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
           }
         }
       } else {
+        const uint32_t acc = tmem + lane_off + buf * kAccCols + c0;
         const bool fp8 = ui.shared != 0;
         uint8_t* hi = a.P.act8 + p * I_act + ui.tile * kM + c0;
         uint8_t* lo = hi + a.act_rows * I_act;
@@ -3356,7 +3368,10 @@ static int launch_plan(const PlanArgs& pa, const Plan& P, int grid, cudaStream_t
     HS_CUDA_CHECK(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     done.fetch_or(bit);
   }
-  HS_CUDA_CHECK(launch_pdl(plan_kernel, dim3(grid), dim3(kPlanThreads), smem, st, pa, P));
+  // segmented plan: block 0 only clears counters, so the token CTAs get the
+  // threads their row needs (16 values each) and twice as many fit per SM
+  const int threads = pa.seg_lrank ? std::max(256, (pa.D / 16 + 31) / 32 * 32) : kPlanThreads;
+  HS_CUDA_CHECK(launch_pdl(plan_kernel, dim3(grid), dim3(threads), smem, st, pa, P));
   return check_launch();
 }
 
