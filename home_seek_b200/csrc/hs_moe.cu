@@ -3180,20 +3180,20 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
           const uint32_t sfb = tmem + kSfb + st * 8;
           tc5::cp_sf_32x128b(sfb, tc5::sdesc_sf(sSF));
           tc5::cp_sf_32x128b(sfb + 4, tc5::sdesc_sf(sSF + 512));
+          // one N = 256 MMA per plane and 32-column k-block: B is the two tiles
+          // as 256 consecutive K-major rows (gate then up, or D-tile 2j then
+          // 2j+1), its scale atoms in columns sfb (rows 0-127) and sfb + 4
+          // (rows 128-255); the accumulator's columns follow B's rows
+          const uint64_t bd = tc5::sdesc_sw128(sB);
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {  // gate (w1), up (w3); or D-tiles 2j, 2j+1
-            const uint64_t bd = tc5::sdesc_sw128(sB + i * kBoxBytes);
+          for (int h = 0; h < 2; ++h) {  // hi, lo planes
+            const uint64_t ad = tc5::sdesc_sw128(sA + h * kBoxBytes);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {  // hi, lo planes
-              const uint64_t ad = tc5::sdesc_sw128(sA + h * kBoxBytes);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint32_t id = tc5::idesc_mxf8f6f4_ab(0u, bfmt, 128, j, j);
-                const uint32_t accum = (k > 0 || h > 0 || j > 0) ? 1u : 0u;
-                tc5::mma_mxf8f6f4(acc + i * 128, ad + 2 * j, bd + 2 * j, id, accum,
-                                  (tmem + kSfa) | (static_cast<uint32_t>(j) << 30),
-                                  (sfb + 4 * i) | (static_cast<uint32_t>(j) << 30));
-              }
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t id = tc5::idesc_mxf8f6f4_ab(0u, bfmt, 256, j, j);
+              const uint32_t accum = (k > 0 || h > 0 || j > 0) ? 1u : 0u;
+              tc5::mma_mxf8f6f4(acc, ad + 2 * j, bd + 2 * j, id, accum, (tmem + kSfa) | (static_cast<uint32_t>(j) << 30),
+                                sfb | (static_cast<uint32_t>(j) << 30));
             }
           }
           tc5::commit(&bars->empty[st]);
