@@ -34,7 +34,7 @@ def _full_store(device="cuda"):
     return st
 
 
-@pytest.mark.parametrize("T", [1, 3, 24])
+@pytest.mark.parametrize("T", [1, 3, 24, 1024])  # 1024: segmented plan + token-major kernels on every shard
 def test_emulated_two_rank_partials_combine_to_the_single_call(T):
     from home_seek_b200 import ops
     from home_seek_b200.ep import localize, shard_store

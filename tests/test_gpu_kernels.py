@@ -229,6 +229,34 @@ def test_moe_token_major_full_shape_rows_match_token_mode():
     assert rel(out[rows], alone) <= MOE_TOL, rel(out[rows], alone)
 
 
+@pytest.mark.parametrize("dup", ["last", "sum"])
+def test_moe_large_t_duplicates_and_skips(dup):
+    """T*K above the single-CTA plan's limit with many pairs per expert (the
+    segmented plan and the token-major kernels), with duplicated, skipped (-1)
+    and out-of-range ids, against the oracle; the out-of-range id is flagged."""
+    from home_seek_b200 import ops
+    from home_seek_b200._lib import HS_DEV_BAD_EXPERT, HS_DUP_LAST, HS_DUP_SUM
+    shape = I.SMALL
+    T = 1024
+    idx, w = I.zipf_routing(T, E=shape.E, K=shape.K, seed=41)
+    idx = idx.clone()
+    idx[::7, 1] = idx[::7, 0]   # duplicated expert within a token
+    idx[::5, 2] = -1            # skipped slot
+    bad = idx.clone()
+    bad[3, 4] = 999             # out of range: skipped and reported
+    st, load, sh = make_store(shape, [x for x in idx.flatten().tolist() if 0 <= x < shape.E], seed_shared=79)
+    h = I.hidden(T, shape.D, seed=42).cuda()
+    dev = torch.device("cuda:0")
+    ops.check_status(dev)
+    mode = HS_DUP_SUM if dup == "sum" else HS_DUP_LAST
+    out = ops.moe_ffn(st.desc(0), st.dims, h, bad.cuda(), w.cuda(), use_shared=False, dup_mode=mode)
+    assert ops.check_status(dev) & HS_DEV_BAD_EXPERT
+    ref_idx = bad.clone()
+    ref_idx[3, 4] = -1
+    ref = O.moe_routed(h.cpu(), ref_idx, w, load, dup_mode=dup)
+    assert rel(out, ref) <= MOE_TOL, rel(out, ref)
+
+
 def test_moe_empty_tokens():
     from home_seek_b200 import ops
     shape = I.SMALL
