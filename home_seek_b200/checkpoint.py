@@ -119,7 +119,8 @@ def _dequant_block128(data: torch.Tensor, scale: Optional[torch.Tensor]) -> torc
 
 
 def load_expert_store(weight_dir: str, prefixes: Optional[Sequence[str]] = None, device="cuda",
-                      rank: int = 0, world: int = 1, with_router: bool = True) -> HBMExpertStore:
+                      rank: int = 0, world: int = 1, with_router: bool = True,
+                      shared: str = "split") -> HBMExpertStore:
     """Read the MoE weights of `prefixes` (default: every `layers.{l}` with
     routed experts, in order; add "mtp.0" for the MTP layer) into a new store.
 
@@ -127,7 +128,8 @@ def load_expert_store(weight_dir: str, prefixes: Optional[Sequence[str]] = None,
     ([I, D/2] packed e2m1), I_sh from the shared expert's w1, the hash layers
     and top_k from `ffn.gate.tid2eid` [V, k]. Layer j of the store is
     prefixes[j]. With world > 1 the store holds rank's block of routed experts
-    and its rows of the shared expert (ep.expert_range / ep.shared_slice)."""
+    and its rows of the shared expert (ep.expert_range / ep.shared_slice), or
+    the whole shared expert with shared="replicated" (ep.TokenShardedEP)."""
     from .ep import expert_range, shared_slice
     ck = CheckpointIndex(weight_dir)
     try:
@@ -148,7 +150,10 @@ def load_expert_store(weight_dir: str, prefixes: Optional[Sequence[str]] = None,
             raise ValueError("hash-routed layers (ffn.gate.tid2eid) must come first")
         vocab, top_k = (int(tids[0].shape[0]), int(tids[0].shape[1])) if hash_layers else (129280, 6)
         off, held = expert_range(E, rank, world)
-        lo, hi = shared_slice(I_sh_full, rank, world) if I_sh_full else (0, 0)
+        if shared not in ("split", "replicated"):
+            raise ValueError(f"shared must be 'split' or 'replicated', not {shared!r}")
+        lo, hi = (shared_slice(I_sh_full, rank, world) if shared == "split" else (0, I_sh_full)) \
+            if I_sh_full else (0, 0)
         store = HBMExpertStore(len(prefixes), E, D, I, (hi - lo) if I_sh_full else None, device=device,
                                with_router=with_router, hash_layers=hash_layers, vocab_size=vocab, top_k=top_k,
                                expert_offset=off, experts_held=held)

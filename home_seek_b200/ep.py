@@ -147,14 +147,23 @@ class ExpertParallel:
         return ops.moe_combine(buf, use_shared=use_shared and store.I_sh > 0)
 
 
-def shard_store(full: HBMExpertStore, rank: int, world: int, device=None) -> HBMExpertStore:
-    """Rank `rank`'s slice of a full store: its routed experts, its rows of the
-    shared expert, and the replicated router (for tests and for loading one
-    set of weights onto an expert-parallel group)."""
+def shard_store(full: HBMExpertStore, rank: int, world: int, device=None, shared: str = "split") -> HBMExpertStore:
+    """Rank `rank`'s slice of a full store: its routed experts, the replicated
+    router, and its rows of the shared expert (shared="split", the decode
+    scheme) or all of them (shared="replicated", the token-sharded prefill
+    scheme of TokenShardedEP). For tests and for loading one set of weights
+    onto an expert-parallel group."""
     from .layout import untile_rows
+    if shared not in ("split", "replicated"):
+        raise ValueError(f"shared must be 'split' or 'replicated', not {shared!r}")
     dev = torch.device(device) if device is not None else full.device
     off, held = expert_range(full.E, rank, world)
-    lo, hi = shared_slice(full.I_sh, rank, world) if full.I_sh else (0, 0)
+    if not full.I_sh:
+        lo, hi = 0, 0
+    elif shared == "split":
+        lo, hi = shared_slice(full.I_sh, rank, world)
+    else:
+        lo, hi = 0, full.I_sh
     hash_layers = sum(1 for lw in full.layers if lw.tid2eid is not None)
     vocab = full.layers[0].tid2eid.shape[0] if hash_layers else 129280
     out = HBMExpertStore(full.num_layers, full.E, full.D, full.I, hi - lo if full.I_sh else None, device=dev,
@@ -183,3 +192,113 @@ def shard_store(full: HBMExpertStore, rank: int, world: int, device=None) -> HBM
             dst.tid2eid.copy_(src.tid2eid)
         dst.desc = None
     return out
+
+
+@dataclass
+class Dispatch:
+    """Where one rank's tokens went: for every destination rank the local token
+    indices sent there (ascending), and the row counts both ways."""
+    tokens: list
+    send_counts: list
+    recv_counts: list
+
+
+def dispatch_lists(topk_idx: torch.Tensor, experts_per_rank: int, world: int):
+    """For every destination rank r: the tokens with at least one expert on r
+    (ascending) and their ids localised to r (experts elsewhere -> -1). Ids
+    outside [0, world * experts_per_rank) go nowhere (skipped)."""
+    owner = torch.where(topk_idx >= 0, torch.div(topk_idx, experts_per_rank, rounding_mode="floor"),
+                        torch.full_like(topk_idx, -1))
+    toks, ids = [], []
+    for r in range(world):
+        m = owner == r
+        t_r = m.any(1).nonzero().flatten()
+        toks.append(t_r)
+        ids.append(torch.where(m, topk_idx - r * experts_per_rank, torch.full_like(topk_idx, -1)).index_select(0, t_r))
+    return toks, ids
+
+
+class TokenShardedEP:
+    """Expert parallelism for prefill-size calls with the tokens sharded over
+    the ranks (the dispatch / combine scheme; the reference's own
+    `_forward_ffn_ep`, engine.py:1575-1709, replicates the tokens instead).
+
+    Rank r holds the routed experts [r E/n, (r+1) E/n) (shard_store or
+    checkpoint.load_expert_store with rank/world) and the whole shared expert
+    (shared="replicated"), and owns a shard of the tokens with their routing.
+    `moe` sends each token's hidden row once to every rank that holds one of
+    its experts, with its ids localised to that rank and its weights (NCCL
+    all-to-all of counts, rows, ids, weights), runs the routed FP4 kernels on
+    the received rows (`hs_moe_ffn_fp4_partials`: un-rounded f32 sums), sends
+    the f32 rows back, adds them per token in rank order (deterministic), runs
+    the shared expert on its own tokens and rounds as the single-GPU call does
+    (bf16(bf16(routed) + bf16(shared)), `hs_moe_combine`). The host reads the
+    counts (one synchronisation per call), as any all-to-all with
+    data-dependent sizes does."""
+
+    def __init__(self, rank: int, world: int, group=None,
+                 all_to_all: Optional[Callable[[torch.Tensor, torch.Tensor, list, list], None]] = None):
+        self.rank = rank
+        self.world = world
+        self.group = group
+        if all_to_all is None:
+            import torch.distributed as dist
+
+            def _a2a(out, inp, out_splits, in_splits):
+                dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
+            all_to_all = _a2a
+        self._a2a = all_to_all
+
+    def dispatch(self, h: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts_per_rank: int):
+        """-> (Dispatch, received rows [N, D], their local ids [N, K], weights [N, K])."""
+        toks, ids = dispatch_lists(topk_idx, experts_per_rank, self.world)
+        send_counts = [int(t.numel()) for t in toks]
+        order = torch.cat(toks)
+        sc = torch.tensor(send_counts, dtype=torch.int64, device=h.device)
+        rc = torch.empty_like(sc)
+        self._a2a(rc, sc, [1] * self.world, [1] * self.world)
+        recv_counts = [int(c) for c in rc.tolist()]
+        n = sum(recv_counts)
+        K = topk_idx.shape[1]
+        h_recv = h.new_empty(n, h.shape[1])
+        idx_recv = topk_idx.new_empty(n, K)
+        w_recv = topk_w.new_empty(n, K)
+        self._a2a(h_recv, h.index_select(0, order).contiguous(), recv_counts, send_counts)
+        self._a2a(idx_recv, torch.cat(ids).contiguous(), recv_counts, send_counts)
+        self._a2a(w_recv, topk_w.index_select(0, order).contiguous(), recv_counts, send_counts)
+        return Dispatch(toks, send_counts, recv_counts), h_recv, idx_recv, w_recv
+
+    def combine(self, d: Dispatch, y_recv: torch.Tensor, num_tokens: int) -> torch.Tensor:
+        """The received rows' f32 results back to their tokens: [T_local, D] f32,
+        each token's rows added in rank order."""
+        D = y_recv.shape[1]
+        back = y_recv.new_empty(sum(d.send_counts), D)
+        self._a2a(back, y_recv.contiguous(), d.send_counts, d.recv_counts)
+        routed = torch.zeros(num_tokens, D, dtype=torch.float32, device=y_recv.device)
+        off = 0
+        for t_r, c in zip(d.tokens, d.send_counts):
+            if c:
+                routed.index_add_(0, t_r, back[off:off + c].float())
+            off += c
+        return routed
+
+    def moe(self, store: HBMExpertStore, layer: int, h: torch.Tensor, topk_idx: torch.Tensor,
+            topk_w: torch.Tensor, dup_mode: int = _lib.HS_DUP_LAST, use_shared: bool = True) -> torch.Tensor:
+        """The MoE output [T_local, D] bf16 for this rank's tokens (normed rows h,
+        global expert ids)."""
+        T = h.shape[0]
+        d, h_r, idx_r, w_r = self.dispatch(h, topk_idx, topk_w, store.E_local)
+        if h_r.shape[0]:
+            y_r = ops.moe_ffn_partials(store.desc(layer), store.dims, h_r, idx_r, w_r, use_shared=False,
+                                       dup_mode=dup_mode)[0]
+        else:
+            y_r = torch.empty(0, h.shape[1], dtype=torch.float32, device=h.device)
+        routed = self.combine(d, y_r, T)
+        use_shared = use_shared and store.I_sh > 0
+        parts = torch.empty(2, T, h.shape[1], dtype=torch.float32, device=h.device)
+        parts[0].copy_(routed)
+        if use_shared and T:
+            none = torch.full_like(topk_idx, -1)
+            parts[1].copy_(ops.moe_ffn_partials(store.desc(layer), store.dims, h, none, topk_w, use_shared=True,
+                                                dup_mode=dup_mode)[1])
+        return ops.moe_combine(parts, use_shared=use_shared)

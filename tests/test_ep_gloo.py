@@ -74,6 +74,70 @@ def test_two_rank_expert_parallel_layer_matches_single_process(T):
     assert rel <= 1e-2, rel
 
 
+def _sharded_rank_main(rank: int, world: int, port: int, T: int, out_q) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from home_seek_b200.ep import TokenShardedEP, expert_range
+        shape = I.SMALL
+        load = I.make_loader(shape)
+        gate, bias = I.router_weights(shape.E, shape.D, seed=1)
+        sh = I.shared_fp8(shape.D, shape.I_sh, seed=2)
+        h = I.hidden(T, shape.D, seed=30 + T)
+        idx, w = O.router(h, gate, bias)
+        lo, hi = rank * T // world, (rank + 1) * T // world     # this rank's token shard
+        hl, il, wl = h[lo:hi], idx[lo:hi], w[lo:hi]
+        off, held = expert_range(shape.E, rank, world)
+        ep = TokenShardedEP(rank, world)
+        d, hr, ir, wr = ep.dispatch(hl, il, wl, held)
+        assert int(ir.max()) < held if ir.numel() else True
+        # the received rows through this rank's experts (local ids -> global for the loader)
+        y = O.moe_routed_f32(hr, torch.where(ir >= 0, ir + off, ir), wr, load)
+        routed = ep.combine(d, y, hl.shape[0])
+        out = O.ep_combine(routed, O.shared_expert_f32(hl, sh))
+        ref = O.moe_layer(hl, il, wl, load, sh)
+        ref_routed = O.moe_routed_f32(hl, il, wl, load)
+        rr = float((routed - ref_routed).abs().max() / ref_routed.abs().max())
+        out_q.put((rank, out.float().numpy(), ref.float().numpy(), rr, sum(d.send_counts), sum(d.recv_counts)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("T", [5, 8])
+def test_token_sharded_dispatch_combine_two_ranks(T):
+    """Prefill-size expert parallelism with the tokens sharded: each rank sends
+    its tokens' rows to the ranks holding their experts (gloo all-to-all), the
+    receivers run their experts (the oracle here; the kernels on the GPU), the
+    f32 results come back and are added per token in rank order: each rank's
+    tokens come out as the single-process layer computes them."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_rank_main, args=(r, 2, port, T, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    res.sort()
+    assert sum(r[4] for r in res) == sum(r[5] for r in res)   # every row sent is received
+    for _, out, ref, rr, _, _ in res:
+        assert rr <= 1e-5, rr                                # f32 sums: only the association differs
+        rel = float(np.abs(out - ref).max() / max(np.abs(ref).max(), 1e-30))
+        assert rel <= 1e-2, rel
+
+
+def test_dispatch_lists():
+    from home_seek_b200.ep import dispatch_lists
+    idx = torch.tensor([[0, 5, -1], [6, 7, 2], [1, 1, 3], [9, -1, -1]])
+    toks, ids = dispatch_lists(idx, 4, 2)           # rank 0: experts 0-3, rank 1: 4-7; id 9 goes nowhere
+    assert [t.tolist() for t in toks] == [[0, 1, 2], [0, 1]]
+    assert ids[0].tolist() == [[0, -1, -1], [-1, -1, 2], [1, 1, 3]]
+    assert ids[1].tolist() == [[-1, 1, -1], [2, 3, -1]]
+
+
 def test_expert_and_shared_splits():
     from home_seek_b200.ep import expert_range, localize, shared_slice
     assert [expert_range(256, r, 8) for r in (0, 7)] == [(0, 32), (224, 32)]

@@ -183,3 +183,116 @@ def test_p2p_expert_parallel_layer_matches_single_gpu():
         assert same, rank
         # bf16(h + y) against the single-GPU call: y differs by f32 summation order only
         assert worst <= 2e-2, (rank, worst)
+
+
+class _ThreadExchange:
+    """In-process all-to-all between rank threads on one GPU (each rank on its
+    own stream): a rank posts its input pieces, waits for every rank, gathers
+    the pieces addressed to it, and waits again before the next exchange."""
+
+    def __init__(self, world: int):
+        import threading
+        self.world = world
+        self.bar = threading.Barrier(world, timeout=120)
+        self.box = {}
+
+    def for_rank(self, rank: int):
+        def a2a(out, inp, out_splits, in_splits):
+            torch.cuda.synchronize()
+            self.box[rank] = list(torch.split(inp, in_splits))
+            self.bar.wait()
+            pieces = [self.box[s][rank] for s in range(self.world)]
+            if out.numel():
+                out.copy_(torch.cat(pieces))
+            torch.cuda.synchronize()
+            self.bar.wait()
+        return a2a
+
+
+@pytest.mark.parametrize("T", [6, 1024])   # 1024: the token-major kernels on the received rows
+def test_emulated_token_sharded_two_ranks_match_the_single_call(T):
+    """Prefill-size expert parallelism with sharded tokens (TokenShardedEP),
+    two ranks emulated as threads on one GPU: each rank's tokens come out as
+    the single-GPU call on the full store computes them."""
+    import threading
+    from home_seek_b200 import ops
+    from home_seek_b200.ep import TokenShardedEP, shard_store
+    shape = I.SMALL
+    full = _full_store()
+    gate, bias = I.router_weights(shape.E, shape.D, seed=1)
+    h = I.hidden(T, shape.D, seed=70 + T).cuda()
+    idx, w = ops.router_topk(h, gate.cuda(), bias.cuda(), shape.K, 1.5)
+    ref = ops.moe_ffn(full.desc(0), full.dims, h, idx, w, use_shared=True)
+    shards = [shard_store(full, r, 2, shared="replicated") for r in range(2)]
+    for s in shards:
+        s.desc(0)
+    torch.cuda.synchronize()
+    ex = _ThreadExchange(2)
+    outs, errs = [None, None], []
+
+    def run(r):
+        try:
+            with torch.cuda.stream(torch.cuda.Stream()):
+                lo, hi = r * T // 2, (r + 1) * T // 2
+                ep = TokenShardedEP(r, 2, all_to_all=ex.for_rank(r))
+                outs[r] = ep.moe(shards[r], 0, h[lo:hi].contiguous(), idx[lo:hi].contiguous(), w[lo:hi].contiguous())
+                torch.cuda.synchronize()
+        except BaseException as e:  # noqa: BLE001
+            errs.append(e)
+            ex.bar.abort()
+
+    th = [threading.Thread(target=run, args=(r,)) for r in range(2)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(timeout=300)
+    assert not errs, errs
+    out = torch.cat(outs)
+    assert ops.check_status(torch.device("cuda")) == 0
+    assert _rel(out, ref) <= MOE_TOL, _rel(out, ref)
+
+
+def _sharded_nccl_rank(rank: int, world: int, port: int, q) -> None:
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from home_seek_b200 import ops
+        from home_seek_b200.ep import TokenShardedEP, shard_store
+        shape = I.SMALL
+        full = _full_store(dev)
+        gate, bias = I.router_weights(shape.E, shape.D, seed=1)
+        T = 1024
+        h = I.hidden(T, shape.D, seed=11).to(dev)
+        idx, w = ops.router_topk(h, gate.to(dev), bias.to(dev), shape.K, 1.5)
+        lo, hi = rank * T // world, (rank + 1) * T // world
+        ref = ops.moe_ffn(full.desc(0), full.dims, h[lo:hi], idx[lo:hi], w[lo:hi], use_shared=True)
+        out = TokenShardedEP(rank, world).moe(shard_store(full, rank, world, shared="replicated"), 0,
+                                              h[lo:hi].contiguous(), idx[lo:hi].contiguous(), w[lo:hi].contiguous())
+        torch.cuda.synchronize()
+        q.put((rank, _rel(out, ref)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_token_sharded_expert_parallel_matches_single_gpu():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_nccl_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, rel in res:
+        assert rel <= MOE_TOL, (rank, rel)
