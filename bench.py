@@ -333,6 +333,64 @@ def run_moe_only(args):
     return 0
 
 
+def run_moe_ep(args):
+    """Config-3 class MoE microbenchmark: T tokens (sharded T/n per rank) through
+    `args.layers` layers of the config-0 shape with TokenShardedEP over the
+    torchrun ranks (NCCL all-to-all dispatch, FP4 kernels on the received rows,
+    combine). Each rank holds its 256/n routed experts and the whole shared
+    expert, random-init. Prints ms per layer call, the max over ranks of CUDA
+    event time around `reps` calls."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from home_seek_b200 import ops
+    from home_seek_b200.ep import TokenShardedEP, expert_range
+    from home_seek_b200.expert_store import HBMExpertStore
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        off, held = expert_range(256, rank, world)
+        store = HBMExpertStore(args.layers, 256, 4096, 2048, 2048, device=dev, expert_offset=off, experts_held=held)
+        store.fill_random(7 + rank)
+        for l in range(args.layers):  # one router for the whole group
+            g = torch.Generator(device=dev).manual_seed(100 + l)
+            store.layers[l].gate.copy_((torch.randn(256, 4096, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+        Tl = args.T // world
+        g = torch.Generator(device=dev).manual_seed(5 + rank)
+        calls = []
+        for i in range(max(args.reps, 1)):
+            l = i % args.layers
+            h = torch.randn(Tl, 4096, generator=g, device=dev).to(torch.bfloat16)
+            idx, w = ops.router_topk(h, store.layers[l].gate, store.layers[l].bias, 6, 1.5)
+            calls.append((l, h, idx, w))
+        ep = TokenShardedEP(rank, world)
+        for c in calls[:3]:
+            ep.moe(store, c[0], c[1], c[2], c[3])
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for c in calls:
+            ep.moe(store, c[0], c[1], c[2], c[3])
+        b.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([a.elapsed_time(b) / len(calls)], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            print(json.dumps({"mode": "moe-ep", "T": Tl * world, "tokens_per_rank": Tl, "world": world,
+                              "layers": args.layers, "calls": len(calls), "ms_per_layer": float(ms.item()),
+                              "scheme": "token-sharded dispatch/combine (NCCL all-to-all)"}), flush=True)
+        return 0
+    finally:
+        dist.destroy_process_group()
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -486,8 +544,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=43)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--mode", default="decode", choices=["decode", "moe"],
-                    help="moe: MoE FFN microbenchmark only (profiling; not the driver's line)")
+    ap.add_argument("--mode", default="decode", choices=["decode", "moe", "moe-ep"],
+                    help="moe: MoE FFN microbenchmark only (profiling; not the driver's line); moe-ep: "
+                         "prefill-size MoE with the tokens sharded over the torchrun ranks (TokenShardedEP)")
     ap.add_argument("--T", type=int, default=3, help="tokens per MoE call in --mode moe")
     ap.add_argument("--reps", type=int, default=20, help="MoE calls timed in --mode moe")
     ap.add_argument("--fused", action="store_true", help="--mode moe: router folded into the call (T <= 8)")
@@ -500,6 +559,8 @@ def main():
         return run_reference(args)
     if args.mode == "moe":
         return run_moe_only(args)
+    if args.mode == "moe-ep":
+        return run_moe_ep(args)
     return run_ours(args)
 
 
