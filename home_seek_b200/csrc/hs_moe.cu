@@ -3235,47 +3235,45 @@ __global__ void __launch_bounds__(kTmThreads, 1) tm_kernel(const __grid_constant
       }
       tc5::fence_after_sync();
       if constexpr (kDown) {
-        // warp half h: columns [128 h, 128 h + 128) = D-tile 2j + h
+        // warp half h: columns [128 h, 128 h + 128) = D-tile 2j + h. All 128
+        // values come into registers first and the accumulator is released
+        // before the stores, which then overlap the next unit's MMAs
         const uint32_t accd = tmem + lane_off + buf * kAccCols + 128 * (warp >> 2);
         float* dst = a.P.out_part + p * D + ui.tile * (2 * kM) + 128 * (warp >> 2);
-#pragma unroll 1
-        for (int g = 0; g < 4; ++g) {
-          float v0[16], v1[16];
-          tc5::ld_32x32b_x16(accd + g * 32, v0);
-          tc5::ld_32x32b_x16(accd + g * 32 + 16, v1);
-          tc5::wait_ld();
-          if (g == 3) {
-            tc5::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
-          }
-          if (valid) {
-            float4* o = reinterpret_cast<float4*>(dst + g * 32);
+        float v[128];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              o[i] = make_float4(v0[4 * i] * rs, v0[4 * i + 1] * rs, v0[4 * i + 2] * rs, v0[4 * i + 3] * rs);
-              o[4 + i] = make_float4(v1[4 * i] * rs, v1[4 * i + 1] * rs, v1[4 * i + 2] * rs, v1[4 * i + 3] * rs);
-            }
-          }
+        for (int g = 0; g < 8; ++g) tc5::ld_32x32b_x16(accd + g * 16, *reinterpret_cast<float(*)[16]>(v + 16 * g));
+        tc5::wait_ld();
+        tc5::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+        if (valid) {
+          float4* o = reinterpret_cast<float4*>(dst);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[i] = make_float4(v[4 * i] * rs, v[4 * i + 1] * rs, v[4 * i + 2] * rs, v[4 * i + 3] * rs);
         }
       } else {
         const uint32_t acc = tmem + lane_off + buf * kAccCols + c0;
         const bool fp8 = ui.shared != 0;
         uint8_t* hi = a.P.act8 + p * I_act + ui.tile * kM + c0;
         uint8_t* lo = hi + a.act_rows * I_act;
-#pragma unroll 1
+        // the warp's 64 gate and 64 up values into registers, the accumulator
+        // released, then the epilogue math overlaps the next unit's MMAs
+        float gall[64], uall[64];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          tc5::ld_32x32b_x16(acc + g * 16, *reinterpret_cast<float(*)[16]>(gall + 16 * g));
+          tc5::ld_32x32b_x16(acc + 128 + g * 16, *reinterpret_cast<float(*)[16]>(uall + 16 * g));
+        }
+        tc5::wait_ld();
+        tc5::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+#pragma unroll
         for (int g = 0; g < 2; ++g) {
-          float gv[32], uv[32];
-          tc5::ld_32x32b_x16(acc + g * 32, *reinterpret_cast<float(*)[16]>(gv));
-          tc5::ld_32x32b_x16(acc + g * 32 + 16, *reinterpret_cast<float(*)[16]>(gv + 16));
-          tc5::ld_32x32b_x16(acc + 128 + g * 32, *reinterpret_cast<float(*)[16]>(uv));
-          tc5::ld_32x32b_x16(acc + 128 + g * 32 + 16, *reinterpret_cast<float(*)[16]>(uv + 16));
-          tc5::wait_ld();
-          if (g == 1) {
-            tc5::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
-          }
+          const float* gv = gall + 32 * g;
+          const float* uv = uall + 32 * g;
           if (valid) {
             uint32_t hw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, lw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll

@@ -294,6 +294,8 @@ class TokenShardedEP:
         else:
             y_r = torch.empty(0, h.shape[1], dtype=torch.float32, device=h.device)
         routed = self.combine(d, y_r, T)
+        if T == 0:  # no tokens of its own: the rank still took part in every exchange
+            return h.new_empty(0, h.shape[1])
         use_shared = use_shared and store.I_sh > 0
         parts = torch.empty(2, T, h.shape[1], dtype=torch.float32, device=h.device)
         parts[0].copy_(routed)
