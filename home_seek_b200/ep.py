@@ -226,15 +226,16 @@ class TokenShardedEP:
     Rank r holds the routed experts [r E/n, (r+1) E/n) (shard_store or
     checkpoint.load_expert_store with rank/world) and the whole shared expert
     (shared="replicated"), and owns a shard of the tokens with their routing.
-    `moe` sends each token's hidden row once to every rank that holds one of
-    its experts, with its ids localised to that rank and its weights (NCCL
-    all-to-all of counts, rows, ids, weights), runs the routed FP4 kernels on
-    the received rows (`hs_moe_ffn_fp4_partials`: un-rounded f32 sums), sends
-    the f32 rows back, adds them per token in rank order (deterministic), runs
-    the shared expert on its own tokens and rounds as the single-GPU call does
-    (bf16(bf16(routed) + bf16(shared)), `hs_moe_combine`). The host reads the
-    counts (one synchronisation per call), as any all-to-all with
-    data-dependent sizes does."""
+    `moe` sends each token's hidden row once to every other rank that holds
+    one of its experts, with its ids localised to that rank and its weights
+    (NCCL all-to-all of counts, rows, ids, weights); runs its own experts and
+    the shared expert on its own tokens in one call and the routed FP4 kernels
+    on the received rows (`hs_moe_ffn_fp4_partials`: un-rounded f32 sums);
+    sends the f32 rows back, adds every rank's term per token in rank order
+    (deterministic) and rounds as the single-GPU call does (bf16(bf16(routed)
+    + bf16(shared)), `hs_moe_combine`). The host reads the counts (one
+    synchronisation per call), as any all-to-all with data-dependent sizes
+    does."""
 
     def __init__(self, rank: int, world: int, group=None,
                  all_to_all: Optional[Callable[[torch.Tensor, torch.Tensor, list, list], None]] = None):
@@ -249,9 +250,14 @@ class TokenShardedEP:
             all_to_all = _a2a
         self._a2a = all_to_all
 
-    def dispatch(self, h: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts_per_rank: int):
-        """-> (Dispatch, received rows [N, D], their local ids [N, K], weights [N, K])."""
+    def dispatch(self, h: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts_per_rank: int,
+                 skip_self: bool = False):
+        """-> (Dispatch, received rows [N, D], their local ids [N, K], weights [N, K]).
+        skip_self: nothing is sent to this rank itself (its own experts run locally)."""
         toks, ids = dispatch_lists(topk_idx, experts_per_rank, self.world)
+        if skip_self:
+            toks[self.rank] = toks[self.rank][:0]
+            ids[self.rank] = ids[self.rank][:0]
         send_counts = [int(t.numel()) for t in toks]
         order = torch.cat(toks)
         sc = torch.tensor(send_counts, dtype=torch.int64, device=h.device)
@@ -268,16 +274,21 @@ class TokenShardedEP:
         self._a2a(w_recv, topk_w.index_select(0, order).contiguous(), recv_counts, send_counts)
         return Dispatch(toks, send_counts, recv_counts), h_recv, idx_recv, w_recv
 
-    def combine(self, d: Dispatch, y_recv: torch.Tensor, num_tokens: int) -> torch.Tensor:
+    def combine(self, d: Dispatch, y_recv: torch.Tensor, num_tokens: int,
+                own: Optional[torch.Tensor] = None) -> torch.Tensor:
         """The received rows' f32 results back to their tokens: [T_local, D] f32,
-        each token's rows added in rank order."""
+        each token's rows added in rank order; `own` ([T_local, D] f32, zero
+        where a token has no expert here) is this rank's term when its own
+        experts ran locally (dispatch with skip_self)."""
         D = y_recv.shape[1]
         back = y_recv.new_empty(sum(d.send_counts), D)
         self._a2a(back, y_recv.contiguous(), d.send_counts, d.recv_counts)
         routed = torch.zeros(num_tokens, D, dtype=torch.float32, device=y_recv.device)
         off = 0
-        for t_r, c in zip(d.tokens, d.send_counts):
-            if c:
+        for r, (t_r, c) in enumerate(zip(d.tokens, d.send_counts)):
+            if r == self.rank and own is not None:
+                routed += own
+            elif c:
                 routed.index_add_(0, t_r, back[off:off + c].float())
             off += c
         return routed
@@ -287,20 +298,21 @@ class TokenShardedEP:
         """The MoE output [T_local, D] bf16 for this rank's tokens (normed rows h,
         global expert ids)."""
         T = h.shape[0]
-        d, h_r, idx_r, w_r = self.dispatch(h, topk_idx, topk_w, store.E_local)
+        use_shared = use_shared and store.I_sh > 0
+        d, h_r, idx_r, w_r = self.dispatch(h, topk_idx, topk_w, store.E_local, skip_self=True)
+        # this rank's own experts and the shared expert on its own tokens: one call
+        parts = None
+        if T:
+            own = localize(topk_idx, store.expert_offset, store.E_local)
+            parts = ops.moe_ffn_partials(store.desc(layer), store.dims, h, own, topk_w, use_shared=use_shared,
+                                         dup_mode=dup_mode)
         if h_r.shape[0]:
             y_r = ops.moe_ffn_partials(store.desc(layer), store.dims, h_r, idx_r, w_r, use_shared=False,
                                        dup_mode=dup_mode)[0]
         else:
             y_r = torch.empty(0, h.shape[1], dtype=torch.float32, device=h.device)
-        routed = self.combine(d, y_r, T)
+        routed = self.combine(d, y_r, T, own=parts[0] if parts is not None else None)
         if T == 0:  # no tokens of its own: the rank still took part in every exchange
             return h.new_empty(0, h.shape[1])
-        use_shared = use_shared and store.I_sh > 0
-        parts = torch.empty(2, T, h.shape[1], dtype=torch.float32, device=h.device)
         parts[0].copy_(routed)
-        if use_shared and T:
-            none = torch.full_like(topk_idx, -1)
-            parts[1].copy_(ops.moe_ffn_partials(store.desc(layer), store.dims, h, none, topk_w, use_shared=True,
-                                                dup_mode=dup_mode)[1])
         return ops.moe_combine(parts, use_shared=use_shared)
