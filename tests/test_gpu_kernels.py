@@ -206,17 +206,18 @@ def test_moe_config2_zipf_full_shape(T):
     assert rel(out, ref) <= MOE_TOL, rel(out, ref)
 
 
-def test_moe_token_major_full_shape_rows_match_token_mode():
-    """Config-2 routing at the full shape with many pairs per expert (T=4096,
-    the token-major kernels): a token's output does not depend on the other
-    tokens in the call, so selected rows must equal (within the MoE
-    tolerance) the same tokens run alone through the token-mode kernels, which
-    the oracle pins; and two runs are bit-identical."""
+@pytest.mark.parametrize("T", [512, 4096])
+def test_moe_large_t_full_shape_rows_match_token_mode(T):
+    """Config-2 routing at the full shape with more than 1024 pairs (the
+    segmented plan), feeding the weight-major kernels (T=512, 12 pairs per
+    expert) or the token-major kernels (T=4096): a token's output does not
+    depend on the other tokens in the call, so selected rows must equal
+    (within the MoE tolerance) the same tokens run alone through the
+    token-mode kernels, which the oracle pins; and two runs are bit-identical."""
     from home_seek_b200 import ops
     from home_seek_b200.expert_store import HBMExpertStore
     st = HBMExpertStore(1, 256, 4096, 2048, 2048, device="cuda", with_router=False)
     st.fill_random(31)
-    T = 4096
     idx, w = I.zipf_routing(T, E=256, K=6, seed=7)
     h = I.hidden(T, 4096, seed=8).cuda()
     idx, w = idx.cuda(), w.cuda()
@@ -224,7 +225,8 @@ def test_moe_token_major_full_shape_rows_match_token_mode():
     again = ops.moe_ffn(st.desc(0), st.dims, h, idx, w, use_shared=True)
     assert ops.check_status(torch.device("cuda")) == 0
     assert torch.equal(out, again)
-    rows = torch.tensor([0, 1, 17, 1000, 2047, 2048, 3333, 4095], device="cuda")
+    rows = torch.tensor([0, 1, 17, 100, 256, 300, 511, T - 1], device="cuda") if T == 512 else \
+        torch.tensor([0, 1, 17, 1000, 2047, 2048, 3333, 4095], device="cuda")
     alone = ops.moe_ffn(st.desc(0), st.dims, h[rows], idx[rows], w[rows], use_shared=True)
     assert rel(out[rows], alone) <= MOE_TOL, rel(out[rows], alone)
 
