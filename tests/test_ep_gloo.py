@@ -104,8 +104,8 @@ def _sharded_rank_main(rank: int, world: int, port: int, T: int, out_q) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T", [5, 8])
-def test_token_sharded_dispatch_combine_two_ranks(T):
+@pytest.mark.parametrize("T,world", [(5, 2), (8, 2), (9, 4)])
+def test_token_sharded_dispatch_combine(T, world):
     """Prefill-size expert parallelism with the tokens sharded: each rank sends
     its tokens' rows to the ranks holding their experts (gloo all-to-all), the
     receivers run their experts (the oracle here; the kernels on the GPU), the
@@ -114,7 +114,7 @@ def test_token_sharded_dispatch_combine_two_ranks(T):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_sharded_rank_main, args=(r, 2, port, T, q)) for r in range(2)]
+    procs = [ctx.Process(target=_sharded_rank_main, args=(r, world, port, T, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
