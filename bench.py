@@ -7,7 +7,7 @@ verify forward through 43 MoE layers, lm_head and greedy acceptance. Weights
 are random-init in the reference's formats (FP4 e2m1 + UE8M0 routed experts,
 FP8 e4m3 shared experts, bf16 router/embed/head), all resident in HBM.
 Attention/MHC are the reference's PyTorch path and are not part of this
-build's step (see DESIGN.md).
+build's step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 

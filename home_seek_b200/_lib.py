@@ -36,7 +36,8 @@ HS_IPC_HANDLE_BYTES = 64
 class HsEpPeers(ctypes.Structure):
     """hs_ep_peers: this rank, the group size, and every rank's receive buffer
     as mapped in this process (recv[rank] is the local buffer)."""
-    _fields_ = [("rank", c_int32), ("world", c_int32), ("recv", c_void_p * HS_EP_MAX_RANKS)]
+    _fields_ = [("rank", c_int32), ("world", c_int32), ("recv", c_void_p * HS_EP_MAX_RANKS),
+                ("wait_limit_ns", c_int64)]
 
 
 class HsError(RuntimeError):

@@ -74,7 +74,7 @@ constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two indepen
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
 
 // Receive buffer of the peer-memory expert-parallel exchange: a 256-byte
-// header ([0] calls made, [1] combine ticket, u64) and two slots (calls
+// header ([0] calls made, [1] combine ticket, [2] poisoned, u64) and two slots (calls
 // alternate) of [world][routed, shared][8 tokens][D] f32 rows. A rank's call k
 // writes slot k % 2 of every rank; rank q's call k+2 can only start after
 // every rank finished call k+1 and so consumed slot k % 2. An empty entry
@@ -84,6 +84,7 @@ constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CT
 // sets it back to kEmpty.
 namespace epx {
 constexpr int64_t kHdr = 256;
+constexpr int kPoison = 2;  // header word set once a combine's wait ran out
 constexpr uint32_t kEmpty = 0xffffffffu;
 constexpr int kRows = 8;
 __host__ __device__ inline float* rows(uint8_t* buf, int slot, int world, int src, int which, int D) {
@@ -1572,18 +1573,25 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(UnitArgs a, int D) {
   }
 }
 
-// Peer-memory exchange, consumer side: per element, wait (bounded) until
-// every rank's routed and shared entries of this call have arrived in the
-// local buffer, then h_out = bf16(h + bf16(bf16(sum_q routed_q) +
-// bf16(sum_q shared_q))), ranks summed in order from 0 (identical on every
-// rank), and the entries are emptied again; the last CTA advances the local
-// call counter.
+// Peer-memory exchange, consumer side: per element, wait (bounded by
+// limit_ns) until every rank's routed and shared entries of this call have
+// arrived in the local buffer, then h_out = bf16(h + bf16(bf16(sum_q
+// routed_q) + bf16(sum_q shared_q))), ranks summed in order from 0 (identical
+// on every rank), and the entries are emptied again; the last CTA advances
+// the local call counter. A wait that runs out poisons the buffer instead:
+// the counter stays, so entries a late peer stores afterwards sit in a slot
+// no later call reads, and every later call reports HS_DEV_TIMEOUT at once.
 __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world, int T, int D, int use_shared,
                                                          const __nv_bfloat16* h, __nv_bfloat16* h_out,
-                                                         int32_t* status) {
+                                                         int32_t* status, uint64_t limit_ns) {
   pdl_trigger();
   pdl_wait();
   uint64_t* hdr = reinterpret_cast<uint64_t*>(buf);
+  volatile uint64_t* poison = reinterpret_cast<volatile uint64_t*>(hdr + epx::kPoison);
+  if (*poison != 0u) {  // an earlier call gave up: nothing here can be trusted
+    if (threadIdx.x == 0) report(status, HS_DEV_TIMEOUT);
+    return;
+  }
   const uint64_t k = *reinterpret_cast<volatile const uint64_t*>(hdr);
   const int slot = static_cast<int>(k & 1u);
   const int64_t n = static_cast<int64_t>(T) * D;
@@ -1601,8 +1609,10 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world
         for (uint32_t it = 1; vr == epx::kEmpty || vs == epx::kEmpty; ++it) {
           vr = *pr;
           vs = *ps;
-          if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          if ((it & 63u) == 0 && (globaltimer_ns() - t0 > limit_ns || *poison != 0u)) {
             report(status, HS_DEV_TIMEOUT);
+            *poison = 1u;
+            __threadfence();
             timed_out = true;
             break;
           }
@@ -1624,7 +1634,9 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world
     __threadfence();
     if (atomicAdd(reinterpret_cast<unsigned int*>(hdr + 1), 1u) == gridDim.x - 1) {
       *reinterpret_cast<volatile unsigned int*>(hdr + 1) = 0u;
-      *reinterpret_cast<volatile uint64_t*>(hdr) = k + 1;
+      // every CTA's poison store precedes its ticket: a poisoned call keeps the counter
+      __threadfence();
+      if (*poison == 0u) *reinterpret_cast<volatile uint64_t*>(hdr) = k + 1;
       __threadfence();
     }
   }
@@ -2679,8 +2691,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     // loaded before the accumulator was ready
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
-    if (a.ep_world > 0)  // this call's slot (the local call counter, advanced by the previous combine)
-      ep_slot = static_cast<int>(*reinterpret_cast<volatile const uint64_t*>(a.ep_recv[a.ep_rank]) & 1u);
+    bool ep_poisoned = false;
+    if (a.ep_world > 0) {  // this call's slot (the local call counter, advanced by the previous combine)
+      const volatile uint64_t* hdr = reinterpret_cast<volatile const uint64_t*>(a.ep_recv[a.ep_rank]);
+      ep_slot = static_cast<int>(hdr[0] & 1u);
+      ep_poisoned = hdr[epx::kPoison] != 0u;  // an earlier combine gave up: store nothing
+    }
     const int rpr = (kM + a.ncl - 1) / a.ncl;
     // thread (token tid / 16, row tid % 16): a warp covers 16 consecutive rows
     // of two tokens, so its output (and peer) stores are contiguous runs
@@ -2713,7 +2729,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
         // this rank's routed and shared sums into every rank's slot (each
         // entry is its own arrival flag)
         const int64_t o_i = t * static_cast<int64_t>(D) + (c / a.ncl) * kM + rowc;
-        for (int q = 0; q < a.ep_world; ++q) {
+        for (int q = 0; q < a.ep_world && !ep_poisoned; ++q) {
           epx::rows(a.ep_recv[q], ep_slot, a.ep_world, a.ep_rank, 0, D)[o_i] = rs;
           epx::rows(a.ep_recv[q], ep_slot, a.ep_world, a.ep_rank, 1, D)[o_i] = hs;
         }
@@ -3647,9 +3663,11 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
     (void)gdown;
     const int64_t n = T * d.D;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64));
+    const uint64_t limit = route->ep->wait_limit_ns > 0 ? static_cast<uint64_t>(route->ep->wait_limit_ns)
+                                                         : kWaitLimitNs;
     HS_CUDA_CHECK(launch_pdl(ep_combine_kernel, dim3(grid), dim3(256), 0, st, a.ep_recv[a.ep_rank], a.ep_world,
                              static_cast<int>(T), d.D, use_shared, static_cast<const __nv_bfloat16*>(hidden),
-                             static_cast<__nv_bfloat16*>(route->h_out), dev_status));
+                             static_cast<__nv_bfloat16*>(route->h_out), dev_status, limit));
     return check_launch();
   }
   if (tmaj) {
@@ -3904,6 +3922,9 @@ static __device__ __align__(256) uint8_t g_moe_noalloc_scratch[HS_MOE_NOALLOC_BY
 
 // Device address of the scratch array per device, looked up once per device
 // with that device current (the array's name is only a host-side stand-in).
+// The cache lives as long as the process: a cudaDeviceReset (a new primary
+// context, the module loaded again) makes the kept address stale, which the
+// header tells callers.
 static void* noalloc_scratch_ptr(int* status) {
   static std::mutex mu;
   static void* ptrs[64] = {nullptr};

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define HS_ABI_VERSION 1
+#define HS_ABI_VERSION 2
 
 typedef enum hs_status {
   HS_OK = 0,
@@ -158,7 +158,10 @@ int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx
 /* I = I_sh = 2048, top_k = 6 --- the size grows with the SM count ---       */
 /* that allows T <= 16 tokens). The first call on a device looks up the       */
 /* array's device address (cudaGetSymbolAddress): make that first call        */
-/* before any stream capture. All calls share the one array, so calls that    */
+/* before any stream capture. The address is kept for the life of the        */
+/* process: after cudaDeviceReset (or any teardown of the device's primary    */
+/* context) it is stale, so do not call this entry point on that device again */
+/* in the same process. All calls share the one array, so calls that          */
 /* overlap on the GPU (two streams, two host threads) race; the kernels clear */
 /* the counters they need at the start of every call.                         */
 #define HS_MOE_NOALLOC_BYTES (16u << 20)
@@ -347,12 +350,21 @@ int hs_moe_layer_fp4_partials(const void* desc, const void* h,
 /* the local one). Every rank must make the same sequence of calls. Limits:   */
 /* world <= HS_EP_MAX_RANKS, T <= 8, D <= 8192; the down phase must run on     */
 /* clusters (D = 4096 on a B200), else HS_ERR_UNSUPPORTED.                     */
+/* Failure: the combine waits at most wait_limit_ns (0 = two seconds) for a    */
+/* peer's entries. When a wait runs out it sets HS_DEV_TIMEOUT, marks the      */
+/* local buffer poisoned and leaves the call counter where it was, so rows a  */
+/* late peer stores afterwards are never read as a later call's data. Every   */
+/* later call on a poisoned buffer stores nothing to the peers and its        */
+/* combine reports HS_DEV_TIMEOUT at once without waiting or writing h_out;   */
+/* the group must free and re-create its buffers (hs_ep_buffer_alloc) before */
+/* exchanging again.                                                          */
 /* ------------------------------------------------------------------------ */
 #define HS_EP_MAX_RANKS 8
 #define HS_IPC_HANDLE_BYTES 64
 typedef struct hs_ep_peers {
   int32_t rank, world;
   void* recv[HS_EP_MAX_RANKS];
+  int64_t wait_limit_ns;  /* bound of the combine's wait for peers; 0 = 2 s */
 } hs_ep_peers;
 size_t hs_ep_buffer_bytes(int64_t world, int64_t D);
 int hs_ep_buffer_alloc(size_t bytes, void** ptr);

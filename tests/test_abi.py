@@ -22,7 +22,7 @@ def test_library_builds_and_loads():
     from home_seek_b200 import _lib, build
     build.build()
     lib = _lib.load()
-    assert lib.hs_abi_version() == 1
+    assert lib.hs_abi_version() == 2
     assert lib.hs_status_string(3) == b"workspace too small"
 
 

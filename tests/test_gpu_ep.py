@@ -296,3 +296,60 @@ def test_nccl_token_sharded_expert_parallel_matches_single_gpu():
         assert p.exitcode == 0
     for rank, rel in res:
         assert rel <= MOE_TOL, (rank, rel)
+
+
+class _DevView:
+    """A raw device pointer as an int64 array torch can wrap (CUDA array interface)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i8", "data": (ptr, False), "version": 3}
+
+
+def test_peer_exchange_wait_runs_out_and_poisons_the_buffer():
+    """Rank 0 of a two-rank peer-memory group whose rank 1 never runs (both
+    receive buffers live on this GPU and nothing stores rank 1's rows): the
+    combine's bounded wait runs out (a short limit), the call reports
+    HS_DEV_TIMEOUT and leaves h untouched, and the next call on the poisoned
+    buffer refuses at once with the same status instead of waiting again."""
+    import ctypes
+    import time
+    from home_seek_b200 import _lib, ops
+    from home_seek_b200.ep import shard_store
+    from home_seek_b200.expert_store import HBMExpertStore
+    dev = torch.device("cuda")
+    full = HBMExpertStore(1, 256, 4096, 2048, 2048, device=dev)
+    full.fill_random(41)
+    sh = shard_store(full, 0, 2)
+    lib = _lib.load()
+    nb = lib.hs_ep_buffer_bytes(2, 4096)
+    bufs = [ctypes.c_void_p(), ctypes.c_void_p()]
+    for b in bufs:
+        _lib.call("hs_ep_buffer_alloc", nb, ctypes.byref(b))
+    try:
+        peers = _lib.HsEpPeers()
+        peers.rank, peers.world = 0, 2
+        peers.recv[0], peers.recv[1] = bufs[0].value, bufs[1].value
+        peers.wait_limit_ns = 50_000_000  # 50 ms
+        g = torch.Generator(device=dev).manual_seed(8)
+        h = (torch.randn(3, 4096, generator=g, device=dev)).to(torch.bfloat16)
+        nw = (1 + 0.05 * torch.randn(4096, generator=g, device=dev)).to(torch.bfloat16)
+        lw = full.layers[0]
+        ops.check_status(dev)
+        for call in range(2):
+            h_out = torch.full_like(h, 7.0)
+            t0 = time.monotonic()
+            ops.moe_layer_ep(sh.desc(0), sh.dims, h, nw, lw.gate, lw.bias, 6, 1.5, peers, num_experts=256,
+                             expert_offset=0, h_out=h_out)
+            torch.cuda.synchronize()
+            dt = time.monotonic() - t0
+            st = ops.check_status(dev)
+            assert st & _lib.HS_DEV_TIMEOUT, (call, st)
+            assert bool((h_out == 7.0).all()), call  # nothing combined
+            assert dt < 1.5, (call, dt)              # bounded by the 50 ms limit (first) or refused (second)
+        # the call counter stayed at 0 and the poison word is set
+        hdr = torch.as_tensor(_DevView(bufs[0].value, 4), device=dev).cpu().tolist()
+        assert hdr[0] == 0 and hdr[2] != 0, hdr
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            _lib.call("hs_ep_buffer_free", b.value)

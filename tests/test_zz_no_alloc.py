@@ -4,9 +4,11 @@ code running inside a CUDA-graph stream capture where cudaMalloc is not
 permitted, latency-critical loops where cudaMalloc/cudaFree would synchronise
 the device). It uses a fixed scratch array inside the library instead of a
 caller workspace; this test checks it through the C ABI against the
-workspace-taking hs_moe_ffn_fp4 on two calls in a row, with the MoE tolerance
-the other parity tests use. The file name sorts last so a stop-at-first-failure
-run has already run every other test."""
+workspace-taking hs_moe_ffn_fp4 on two calls in a row. Both entry points run
+the same deterministic kernels (fixed-order reductions, the same schedule),
+so the outputs must be bit-identical, not merely within the MoE tolerance.
+The file name sorts last so a stop-at-first-failure run has already run
+every other test."""
 from __future__ import annotations
 
 import ctypes
@@ -17,8 +19,6 @@ import torch
 from oracle import inputs as I
 
 pytestmark = pytest.mark.gpu
-
-MOE_TOL = 1e-2
 
 
 def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
@@ -52,7 +52,7 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
         out = torch.empty_like(ref)
         assert _noalloc(lib, store, h, idx, w, out) == 0
         torch.cuda.synchronize()
-        assert _rel(out, ref) <= MOE_TOL, (call, _rel(out, ref))
+        assert torch.equal(out, ref), (call, _rel(out, ref))
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
