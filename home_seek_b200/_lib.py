@@ -83,6 +83,9 @@ SIGNATURES = {
                                  c_void_p, c_void_p]),
     "hs_accept_rejection": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                     c_float, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "hs_lm_head_workspace_size": (c_size_t, [c_int64]),
+    "hs_lm_head_argmax": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "hs_rms_norm": (c_int, [c_void_p, c_void_p, c_float, c_int64, c_int64, c_void_p, c_void_p]),
     "hs_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_int64, c_int64, c_void_p, c_void_p,
                                 c_void_p]),

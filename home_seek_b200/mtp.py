@@ -58,10 +58,12 @@ class MoEPathModel:
     the MTP layer at index L in the same expert store)."""
 
     def __init__(self, shape: ModelShape, device: str | torch.device = "cuda", seed: int = 0,
-                 ep: Optional["ExpertParallel"] = None):
+                 ep: Optional["ExpertParallel"] = None, weights: Optional[dict] = None):
         """ep: expert parallelism (ep.py): this rank holds its block of routed
         experts and its rows of the shared expert; everything else (router,
-        embeddings, norms, lm_head) is replicated and identical on every rank."""
+        embeddings, norms, lm_head) is replicated and identical on every rank.
+        weights: explicit tensors in the reference's formats instead of a
+        random init (see load_weights)."""
         self.shape = s = shape
         self.device = dev = torch.device(device)
         self.ep = ep
@@ -74,24 +76,54 @@ class MoEPathModel:
         self.store = HBMExpertStore(s.num_layers + 1, s.num_experts, s.hidden, s.inter, sh, device=dev,
                                     with_router=True, hash_layers=s.hash_layers, vocab_size=s.vocab,
                                     top_k=s.top_k, expert_offset=off, experts_held=held)
-        self.store.fill_random(seed)
-        g = torch.Generator(device=dev)
-        g.manual_seed(seed + 17)
+        if weights is not None:
+            self.load_weights(weights)
+        else:
+            self.store.fill_random(seed)
+            g = torch.Generator(device=dev)
+            g.manual_seed(seed + 17)
 
-        def randn(*shp, std):
-            return (torch.randn(*shp, generator=g, device=dev) * std).to(torch.bfloat16)
+            def randn(*shp, std):
+                return (torch.randn(*shp, generator=g, device=dev) * std).to(torch.bfloat16)
 
-        self.embed = randn(s.vocab, s.hidden, std=0.02)
-        self.lm_head = randn(s.vocab, s.hidden, std=0.02)
-        self.norm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
-        self.ln_w = (1.0 + randn(s.num_layers + 1, s.hidden, std=0.02).float()).to(torch.bfloat16)
-        self.e_proj = randn(s.hidden, s.hidden, std=0.02)
-        self.h_proj = randn(s.hidden, s.hidden, std=0.02)
-        self.enorm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
-        self.hnorm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
-        self.mtp_norm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
+            self.embed = randn(s.vocab, s.hidden, std=0.02)
+            self.lm_head = randn(s.vocab, s.hidden, std=0.02)
+            self.norm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
+            self.ln_w = (1.0 + randn(s.num_layers + 1, s.hidden, std=0.02).float()).to(torch.bfloat16)
+            self.e_proj = randn(s.hidden, s.hidden, std=0.02)
+            self.h_proj = randn(s.hidden, s.hidden, std=0.02)
+            self.enorm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
+            self.hnorm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
+            self.mtp_norm_w = (1.0 + randn(s.hidden, std=0.02).float()).to(torch.bfloat16)
         for layer in range(s.num_layers + 1):
             self.store.desc(layer)  # encode TMA descriptors once
+
+    def load_weights(self, w: dict) -> None:
+        """Fill the model from tensors in the reference's formats: w["experts"][l]
+        (eid -> FP4 6-tuple), w["shared"][l] (FP8 (w13, s13, w2, s2)) for the
+        main layers, w["gate"][l], w["bias"][l], w["tid2eid"][l] for the hash
+        layers, and the dense bf16 tensors embed, lm_head, norm_w, ln_w
+        [L + 1, D], e_proj, h_proj, enorm_w, hnorm_w, mtp_norm_w. Layer L is the
+        MTP layer (no shared expert is used there)."""
+        s = self.shape
+        dev = self.device
+        st = self.store
+        lo, hi = st.expert_offset, st.expert_offset + st.E_local
+        for layer in range(s.num_layers + 1):
+            load = w["experts"][layer]
+            for e in range(lo, hi):
+                st.set_expert(layer, e, *load(e))
+            if layer < s.num_layers and st.I_sh:
+                st.set_shared(layer, *w["shared"][layer])
+            st.set_router(layer, w["gate"][layer].to(dev), w["bias"][layer].to(dev))
+            tid = w["tid2eid"].get(layer)
+            if tid is not None and st.layers[layer].tid2eid is not None:
+                st.layers[layer].tid2eid.copy_(tid.to(dev))
+        bf = lambda t: t.to(device=dev, dtype=torch.bfloat16).contiguous()  # noqa: E731
+        self.embed, self.lm_head = bf(w["embed"]), bf(w["lm_head"])
+        self.norm_w, self.ln_w = bf(w["norm_w"]), bf(w["ln_w"])
+        self.e_proj, self.h_proj = bf(w["e_proj"]), bf(w["h_proj"])
+        self.enorm_w, self.hnorm_w, self.mtp_norm_w = bf(w["enorm_w"]), bf(w["hnorm_w"]), bf(w["mtp_norm_w"])
 
     # --- one MoE layer (the part of _forward_layer / _forward_ffn this build owns)
     def moe(self, x: torch.Tensor, layer: int, ids: torch.Tensor) -> torch.Tensor:
@@ -133,6 +165,8 @@ class MoEPathModel:
         dup = HS_DUP_SUM if h.shape[0] == 1 else HS_DUP_LAST
         hashed = layer < s.hash_layers and lw.tid2eid is not None
         kw = {"ids": ids, "tid2eid": lw.tid2eid} if hashed else {}
+        # the MTP block runs the routed experts only (engine.py:2087-2097)
+        kw["use_shared"] = layer < s.num_layers
         gate, bias = (None, None) if hashed else (lw.gate, lw.bias)
         args = (st.desc(layer), st.dims, h, self.ln_w[layer], gate, bias, s.top_k, s.routed_scaling)
         if self.ep is not None and self.ep.peers is not None:  # exchange through peer memory in the call
@@ -176,8 +210,15 @@ class MoEPathModel:
         return h, x
 
     def logits(self, x_normed: torch.Tensor) -> torch.Tensor:
-        """lm_head over rows that already carry the final norm (forward's x)."""
-        return x_normed @ self.lm_head.t()
+        """lm_head over rows that already carry the final norm (forward's x):
+        the bf16 logits, written out (the sampling paths need them)."""
+        return ops.lm_head_argmax(x_normed, self.lm_head, want_logits=True)[3]
+
+    def greedy(self, x_normed: torch.Tensor, draft_ids: Optional[torch.Tensor] = None):
+        """lm_head + argmax in one kernel (the logits never leave the chip):
+        returns (argmax [T], n_accept [1], next_token [1]); with draft_ids the
+        verify pass's greedy acceptance (engine.py:2485-2497)."""
+        return ops.lm_head_argmax(x_normed, self.lm_head, draft_ids=draft_ids)
 
     def draft(self, h_last: torch.Tensor, tok: torch.Tensor) -> torch.Tensor:
         """_mtp_generate_draft at t=0 (engine.py:2251-2336) on the MoE path: M steps."""
@@ -191,8 +232,7 @@ class MoEPathModel:
             hc = ops.rms_norm(prev, self.hnorm_w) @ self.h_proj.t() + e
             hm = self.layer(hc, L, t)
             xm = ops.rms_norm(hm, self.mtp_norm_w)
-            lg = xm @ self.lm_head.t()
-            _, t = ops.accept_greedy(lg.view(1, 1, -1), torch.empty(1, 0, dtype=torch.int64, device=lg.device))
+            t = self.greedy(xm)[2]
             out.append(t)
             prev = hm
         return torch.cat(out)
@@ -218,13 +258,12 @@ class MTPDecoder:
         """One generate() iteration: main T=1 step, M-token draft, fused T=1+M verify, accept."""
         m = self.m
         M = m.shape.num_draft
-        none = torch.empty(1, 0, dtype=torch.int64, device=self.next_id.device)
         h, x = m.forward(self.next_id)                                # main step, T=1
-        _, main_pred = ops.accept_greedy(m.logits(x).view(1, 1, -1), none)
+        main_pred = m.greedy(x)[2]
         d = m.draft(h, main_pred)                                     # M drafts
         ids = torch.cat([main_pred, d])                               # combined_ids
         _, xv = m.forward(ids)                                        # fused verify, T=1+M
-        n_acc, bonus = ops.accept_greedy(m.logits(xv).view(1, M + 1, -1), d.view(1, M))
+        _, n_acc, bonus = m.greedy(xv, draft_ids=d)                   # lm_head + greedy acceptance
         n = n_acc.to(torch.int64)
         # tokens of this iteration: main_pred, then d[:n], then bonus if n > 0
         cand = torch.cat([main_pred, d, bonus])                       # [M + 2]

@@ -23,7 +23,7 @@ _KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_mo
             "hs_rms_norm": 1, "hs_add_rms_norm": 1, "hs_moe_ffn_fp4_partials": 3, "hs_moe_combine": 1,
             "hs_moe_route_ffn_fp4": 3, "hs_moe_route_ffn_fp4_partials": 3,
             "hs_moe_combine_add_rms_norm": 1, "hs_moe_layer_fp4": 3, "hs_moe_layer_fp4_partials": 3,
-            "hs_moe_layer_fp4_ep": 4}
+            "hs_moe_layer_fp4_ep": 4, "hs_lm_head_argmax": 1}
 
 
 def _launch(name: str, *args, extra: int = 0) -> None:
@@ -431,6 +431,44 @@ def accept_rejection(target: torch.Tensor, draft: torch.Tensor, draft_ids: torch
     return n, nxt
 
 
+# --- lm_head + greedy decision ---------------------------------------------------
+
+def lm_head_argmax(x: torch.Tensor, head: torch.Tensor, draft_ids: Optional[torch.Tensor] = None,
+                   want_logits: bool = False, out: Optional[tuple] = None):
+    """logits = x @ head.t() (bf16, f32 accumulate) with the argmax fused in
+    (hs_lm_head_argmax): x [T, D] bf16 rows after the final norm (T <= 16),
+    head [V, D] bf16. Returns (argmax int64 [T], n_accept int32 [1],
+    next_token int64 [1]) and, with want_logits, the bf16 logits [T, V].
+    With draft_ids [T-1] the greedy acceptance of the verify pass is applied
+    (engine.py:2485-2497): n_accept leading matches, next_token =
+    argmax[n_accept]; without them next_token = argmax[0]. `out` may supply
+    the three result tensors (e.g. buffers that a CUDA graph reuses)."""
+    dev = _check_cuda(x, head, draft_ids)
+    x = _rows(x, "x")
+    head = _rows(head, "head")
+    T, D = x.shape
+    V = head.shape[0]
+    if head.shape[1] != D:
+        raise ValueError(f"head has {head.shape[1]} columns, rows have {D}")
+    ids = None
+    if draft_ids is not None:
+        ids = draft_ids.reshape(-1).to(torch.int64).contiguous()
+        if ids.numel() != T - 1:
+            raise ValueError(f"{ids.numel()} draft ids for {T} rows")
+    if out is None:
+        am = torch.empty(T, dtype=torch.int64, device=dev)
+        n = torch.empty(1, dtype=torch.int32, device=dev)
+        nxt = torch.empty(1, dtype=torch.int64, device=dev)
+    else:
+        am, n, nxt = out
+    lg = torch.empty(T, V, dtype=torch.bfloat16, device=dev) if want_logits else None
+    lib = _lib.load()
+    ws = workspace(dev, lib.hs_lm_head_workspace_size(T), "head")
+    _launch("hs_lm_head_argmax", x.data_ptr(), head.data_ptr(), T, D, V, _ptr(ids), am.data_ptr(), n.data_ptr(),
+            nxt.data_ptr(), _ptr(lg), ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(), _stream(dev))
+    return (am, n, nxt, lg) if want_logits else (am, n, nxt)
+
+
 # --- RMSNorm / residual add + RMSNorm ---------------------------------------------
 
 def _rows(x: torch.Tensor, name: str) -> torch.Tensor:
@@ -482,7 +520,7 @@ def fill_bytes(t: torch.Tensor, seed: int, lo: int = 0, hi: int = 255) -> torch.
 
 
 __all__ = ["HsError", "router_topk", "hash_route", "make_moe_desc", "moe_ffn", "moe_permute", "moe_unpermute",
-           "accept_greedy", "accept_rejection", "fill_bytes", "rms_norm", "add_rms_norm", "moe_ffn_partials",
+           "accept_greedy", "accept_rejection", "lm_head_argmax", "fill_bytes", "rms_norm", "add_rms_norm", "moe_ffn_partials",
            "moe_route_ffn",
            "moe_combine", "moe_combine_add_rms_norm", "check_status",
            "status_word", "workspace"]

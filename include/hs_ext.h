@@ -222,6 +222,33 @@ int hs_accept_rejection(const void* target_logits, const void* draft_logits,
                         int64_t* next_token, int32_t* dev_status, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* lm_head GEMV with the greedy decision fused in.                            */
+/* Replaces `logits = h_3d @ lm_head.t()` + `argmax` of the MTP draft          */
+/* (inference_engine/engine.py:2327-2333), of the fused verify with its greedy */
+/* loop (engine.py:2482-2497) and of the main decode step                     */
+/* (engine.py:2846-2853). x [T][D] bf16 (rows after the final norm), head     */
+/* [V][D] bf16. logit[t][v] = bf16(sum_k x[t][k] * head[v][k]) with f32        */
+/* accumulation; the logits stay on chip unless logits_out [T][V] bf16 is     */
+/* given. argmax_out [T] int64 (may be NULL) = first index of the maximal      */
+/* logit of row t, NaN maximal (torch.argmax). With draft_ids [T-1] (T > 1;   */
+/* may be NULL): n_accept = number of leading positions i < T-1 with          */
+/* argmax[i] == draft_ids[i], next_token = argmax[n_accept]; without draft    */
+/* ids n_accept = 0 and next_token = argmax[0]. n_accept [1] int32 and        */
+/* next_token [1] int64 may be NULL. A draft id outside [0, V) stops the      */
+/* acceptance there and sets HS_DEV_BAD_DRAFT. The workspace (size from        */
+/* hs_lm_head_workspace_size, zero-filled once) holds one key per CTA and     */
+/* token and a counter the call leaves at zero.                               */
+/* Limits: 1 <= T <= 16, D a multiple of 64 (<= 65536), V <= 2^30; x and head */
+/* 16-byte aligned; logits_out needs V % 8 == 0.                               */
+/* ------------------------------------------------------------------------ */
+size_t hs_lm_head_workspace_size(int64_t T);
+int hs_lm_head_argmax(const void* x, const void* head, int64_t T, int64_t D,
+                      int64_t V, const int64_t* draft_ids, int64_t* argmax_out,
+                      int32_t* n_accept, int64_t* next_token, void* logits_out,
+                      void* workspace, size_t workspace_bytes,
+                      int32_t* dev_status, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* RMSNorm and residual add + RMSNorm (the layer loop around the MoE FFN).    */
 /* hs_rms_norm replaces home_seek/utils.py:6-9 (rms_norm; called before every */
 /*   FFN at inference_engine/engine.py:2679 and before the logits at          */

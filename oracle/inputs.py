@@ -113,3 +113,67 @@ def accept_inputs(B: int = 64, M: int = 2, V: int = 129280, t: float = 0.7, seed
     q = torch.softmax(draft[:, :M].float() / t, dim=-1)
     ids = torch.multinomial(q.reshape(B * M, V), 1, generator=gd).reshape(B, M)
     return target, draft, ids, u
+
+
+@dataclass(frozen=True)
+class MtpShape:
+    D: int = 512
+    I: int = 512
+    E: int = 16
+    I_sh: int = 512
+    K: int = 6
+    V: int = 1024
+    L: int = 2            # main MoE layers; the MTP layer is index L
+    hash_layers: int = 1
+    M: int = 2            # draft tokens per iteration
+
+
+MTP_SMALL = MtpShape()
+
+
+def mtp_model(shape: MtpShape = MTP_SMALL, seed: int = 50) -> dict:
+    """A small seeded model for the MTP token-stream parity tests, in the
+    reference's formats (uint8 FP4/FP8 bytes, bf16 dense weights).
+
+    Built so that drafts are accepted often but not always: the MTP layer is a
+    copy of the last main layer (same experts, router and norm weight),
+    e_proj = I and h_proj = 2^-4 I (both exact in bf16 on any GEMM, so the
+    projections add no rounding of their own), enorm/hnorm weights 1 and the
+    MTP head norm equal to the final norm; embedding rows ~N(0, 1) so the
+    residual stream dominates and the MTP block sees nearly the main model's
+    input. The hash layers' tid2eid rows hold distinct experts (the reference's
+    T = 1 and T > 1 paths then agree on duplicate handling).
+
+    Returns {"experts": [loader per layer 0..L], "shared": [sh tuple per main
+    layer], "gate": [...], "bias": [...], "tid2eid": {layer: [V, K]}, "embed",
+    "lm_head", "norm_w", "ln_w" [L+1, D], "e_proj", "h_proj", "enorm_w",
+    "hnorm_w", "mtp_norm_w"}; the MTP layer (index L) has no shared expert (the
+    reference's MTP block runs the routed experts only, engine.py:2087-2097).
+    """
+    s = shape
+    g = torch.Generator().manual_seed(seed)
+    experts = [make_loader(MoeShape(D=s.D, I=s.I, E=s.E, I_sh=s.I_sh, K=s.K), seed_base=10000 + 1000 * l)
+               for l in range(s.L)]
+    experts.append(experts[s.L - 1])
+    shared = [shared_fp8(s.D, s.I_sh, seed=seed + 10 + l) for l in range(s.L)]
+    gates, biases = [], []
+    for l in range(s.L):
+        gw, bw = router_weights(s.E, s.D, seed=seed + 20 + l)
+        gates.append(gw)
+        biases.append(bw)
+    gates.append(gates[s.L - 1])
+    biases.append(biases[s.L - 1])
+    tid = {}
+    for l in range(s.hash_layers):
+        gt = torch.Generator().manual_seed(seed + 30 + l)
+        tid[l] = torch.stack([torch.randperm(s.E, generator=gt)[: s.K] for _ in range(s.V)]).to(torch.int64)
+    embed = torch.randn(s.V, s.D, generator=g).to(torch.bfloat16)
+    lm_head = (torch.randn(s.V, s.D, generator=g) * 0.02).to(torch.bfloat16)
+    norm_w = (1.0 + 0.02 * torch.randn(s.D, generator=g)).to(torch.bfloat16)
+    ln_w = (1.0 + 0.02 * torch.randn(s.L + 1, s.D, generator=g)).to(torch.bfloat16)
+    ln_w[s.L] = ln_w[s.L - 1]
+    eye = torch.eye(s.D, dtype=torch.bfloat16)
+    return {"experts": experts, "shared": shared, "gate": gates, "bias": biases, "tid2eid": tid,
+            "embed": embed, "lm_head": lm_head, "norm_w": norm_w, "ln_w": ln_w, "e_proj": eye.clone(),
+            "h_proj": (eye.float() * 2.0 ** -4).to(torch.bfloat16), "enorm_w": torch.ones(s.D, dtype=torch.bfloat16),
+            "hnorm_w": torch.ones(s.D, dtype=torch.bfloat16), "mtp_norm_w": norm_w.clone()}

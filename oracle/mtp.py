@@ -94,3 +94,65 @@ def greedy_tokens(lg: torch.Tensor) -> np.ndarray:
     """argmax per row with torch.argmax's tie rule."""
     a = lg.float().numpy()
     return np.array([A._argmax_first(r) for r in a], dtype=np.int64)
+
+
+def weights_from_inputs(model: dict, num_layers: int, hash_layers: int, top_k: int = 6,
+                        num_draft: int = 2) -> ModelWeights:
+    """ModelWeights over the tensors of oracle.inputs.mtp_model (layers 0..L-1,
+    then the MTP layer, which has no shared expert)."""
+    layers = []
+    for l in range(num_layers + 1):
+        layers.append(LayerWeights(model["experts"][l], model["shared"][l] if l < num_layers else None,
+                                   model["gate"][l], model["bias"][l], model["tid2eid"].get(l)))
+    return ModelWeights(layers, model["embed"], model["lm_head"], model["norm_w"], model["ln_w"], model["e_proj"],
+                        model["h_proj"], model["enorm_w"], model["hnorm_w"], model["mtp_norm_w"], top_k,
+                        hash_layers, 1.5, num_draft)
+
+
+def decode_loop(W: ModelWeights, first_token: int, iterations: int, num_layers: int):
+    """generate()'s MTP loop at temperature 0 (engine.py:2809-2922, no stop
+    token, no token budget reached): per iteration the main T = 1 step
+    (engine.py:2811-2853), the M-step draft (_mtp_generate_draft,
+    engine.py:2251-2336), the fused T = 1 + M verify with its greedy loop
+    (_mtp_verify_batched, engine.py:2431-2497) and the bookkeeping
+    (engine.py:2885-2916): append main_pred; if n_acc > 0 append the n_acc
+    accepted drafts and the bonus token argmax(logits[n_acc]), which becomes
+    the next input; else the next input is main_pred.
+
+    Returns (tokens, records, logits) with records rows (main input, main_pred,
+    drafts..., n_acc, next input) and logits {"main": [N, V], "draft": [N, M,
+    V], "verify": [N, M + 1, V]}, the rows every argmax was taken of.
+    """
+    M = W.num_draft
+    next_id = int(first_token)
+    tokens, recs = [], []
+    lg_main, lg_draft, lg_verify = [], [], []
+    for _ in range(iterations):
+        h, x = forward(W, torch.tensor([next_id]), num_layers)
+        lg = logits(W, x)
+        main_in, main_pred = next_id, int(greedy_tokens(lg)[0])
+        tokens.append(main_pred)
+        prev, tok = h, torch.tensor([main_pred])
+        d, rows = [], []
+        for _i in range(M):
+            prev, lgd = draft_step(W, prev, tok, num_layers)
+            t = int(greedy_tokens(lgd)[0])
+            d.append(t)
+            rows.append(lgd[0])
+            tok = torch.tensor([t])
+        _, xv = forward(W, torch.tensor([main_pred] + d), num_layers)
+        lv = logits(W, xv)
+        n_a, nxt, _ = A.greedy(lv.float().numpy()[None], np.array([d], dtype=np.int64))
+        n = int(n_a[0])
+        if n > 0:
+            tokens.extend(d[:n])
+            next_id = int(nxt[0])
+            tokens.append(next_id)
+        else:
+            next_id = main_pred
+        recs.append([main_in, main_pred] + d + [n, next_id])
+        lg_main.append(lg[0])
+        lg_draft.append(torch.stack(rows))
+        lg_verify.append(lv)
+    return (np.array(tokens, dtype=np.int64), np.array(recs, dtype=np.int64),
+            {"main": torch.stack(lg_main), "draft": torch.stack(lg_draft), "verify": torch.stack(lg_verify)})

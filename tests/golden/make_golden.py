@@ -16,6 +16,11 @@ tests/golden/*.npz. Reference entry points exercised:
                                                               weight_loader.py:22-32)
   HomeSeekInferenceEngine._mtp_verify_batched (greedy loop)  (engine.py:2431-2540)
   tests/_reference.py expand_to_fused / reduce_fused          (_reference.py:52-121)
+  the MTP decode loop (gen_mtp): generate()'s greedy loop body (engine.py:
+  2809-2922, restated in the harness) around the reference's own
+  _forward_layer / _forward_ffn (engine.py:2653-2688, 1413-1541),
+  _mtp_generate_draft / _mtp_forward_draft / _mtp_finalize (engine.py:
+  2036-2133, 2251-2338) and _mtp_verify_batched (engine.py:2431-2540)
 """
 from __future__ import annotations
 
@@ -213,6 +218,172 @@ def gen_permute(out):
     out["perm_reduced"] = _bf16_np(red)
 
 
+def _mtp_engine(shape, model):
+    """A reference engine object (no __init__: that loads a checkpoint and
+    touches CUDA) whose own layer, FFN, draft and verify code runs on the small
+    seeded model, with attention off (hc_mult = 1, no MHC weights, the
+    attention blocks return zeros) and the weight stores replaced by the
+    seeded tensors in the formats the reference's loaders return."""
+    from collections import OrderedDict
+
+    from home_seek.fused_moe import FusedMoEFFN, SharedExpertFFN
+    from home_seek.inference_engine import HomeSeekInferenceEngine
+    from home_seek.inference_engine.weight_loader import load_fp8_weight
+    from home_seek.model_config import DeepSeekV4FlashConfig
+    s = shape
+    eng = HomeSeekInferenceEngine.__new__(HomeSeekInferenceEngine)
+    eng._log = lambda m: None
+    eng.verbose = False
+    eng.config = DeepSeekV4FlashConfig(num_hidden_layers=s.L, hidden_size=s.D, moe_intermediate_size=s.I,
+                                       vocab_size=s.V, n_routed_experts=s.E, num_experts_per_tok=s.K,
+                                       num_hash_layers=s.hash_layers, shared_expert_intermediate_size=s.I_sh,
+                                       hc_mult=1)
+    eng.device = torch.device("cpu")
+    eng._is_multigpu = False
+    eng._hot_expert_set = set()
+    eng._hot_expert_set_by_layer = {}
+    eng._deq_cache = OrderedDict()
+    eng._fused_moe = FusedMoEFFN(num_experts=s.E, intermediate_size=s.I, hidden_size=s.D)
+    assert not eng._fused_moe.use_triton  # CPU: _forward_legacy
+    eng._shared_ffn = SharedExpertFFN(hidden_size=s.D, intermediate_size=s.I_sh)
+    eng.layer_states = {}
+    eng._compressors = {}
+    eng._global_pos = 0
+    eng.embed = model["embed"]
+    eng.lm_head = model["lm_head"]
+    eng.norm_weight = model["norm_w"]
+    eng.hc_head_fn = None
+    eng._mtp_weights = {"mtp.0.e_proj.weight": model["e_proj"], "mtp.0.h_proj.weight": model["h_proj"],
+                        "mtp.0.enorm.weight": model["enorm_w"], "mtp.0.hnorm.weight": model["hnorm_w"],
+                        "mtp.0.norm.weight": model["mtp_norm_w"], "mtp.0.ffn_norm.weight": model["ln_w"][s.L],
+                        "mtp.0.ffn.gate.weight": model["gate"][s.L], "mtp.0.ffn.gate.bias": model["bias"][s.L]}
+    zeros_like_rows = lambda h, *a, **k: torch.zeros_like(h)  # noqa: E731  (attention off)
+    eng._forward_attn = zeros_like_rows
+    eng._mtp_attn_1tok = zeros_like_rows
+
+    def layer_weights(i):
+        lw = {"ffn_norm.weight": model["ln_w"][i], "ffn.gate.weight": model["gate"][i],
+              "ffn.gate.bias": model["bias"][i]}
+        if i in model["tid2eid"]:
+            lw["ffn.gate.tid2eid"] = model["tid2eid"][i]
+        return lw
+    eng._get_layer_weights = layer_weights
+    fp4 = [_fp4_loader_ref(model["experts"][l]) for l in range(s.L + 1)]
+    # the routed experts of layer l as FusedMoEFFN's loader receives them (the
+    # FP4 6-tuple; it replaces _load_bf16_deq, whose cache key omits the layer)
+    eng._load_bf16_deq = lambda layer, eid: fp4[layer](layer, eid)
+
+    def shared(layer):  # what _get_shared_expert returns for a cached FP8 entry
+        w13, s13, w2, s2 = model["shared"][layer]
+        t8 = lambda a: torch.from_numpy(np.ascontiguousarray(a)).view(torch.float8_e4m3fn)  # noqa: E731
+        u8 = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+        return (load_fp8_weight(t8(w13[0]), u8(s13[0])), load_fp8_weight(t8(w13[1]), u8(s13[1])),
+                load_fp8_weight(t8(w2), u8(s2)))
+    eng._get_shared_expert = shared
+
+    def mtp_expert(eid):  # _mtp_load_expert's entry: (data, f32 scale, "fp4") triples
+        w1, s1, w3, s3, w2, s2 = fp4[s.L](s.L, eid)
+        return tuple((w, sc.to(torch.float32), "fp4") for w, sc in ((w1, s1), (w3, s3), (w2, s2)))
+    eng._mtp_load_expert = mtp_expert
+    return eng
+
+
+def gen_mtp(out, iterations: int = 16, first_token: int = 17):
+    """The greedy MTP decode loop of generate() (engine.py:2809-2922, t = 0,
+    mtp_num_draft = M, no stop token) on the small seeded model: main T = 1
+    step, _mtp_generate_draft, _mtp_verify_batched, and the loop's
+    bookkeeping. Records the token stream, every decision's inputs and
+    outcome, and every logits row an argmax was taken of."""
+    from home_seek.utils import rms_norm
+    s = I.MTP_SMALL
+    model = I.mtp_model(s)
+    eng = _mtp_engine(s, model)
+    eps = eng.config.rms_norm_eps
+    next_id = torch.tensor([[first_token]], dtype=torch.int64)
+    generated = []
+    recs, lg_main, lg_draft, lg_verify = [], [], [], []
+    for _ in range(iterations):
+        # main step (engine.py:2811-2853)
+        h = eng.embed[next_id].to(torch.bfloat16)
+        h = h.unsqueeze(2).expand(-1, -1, eng.config.hc_mult, -1)
+        for layer_idx in range(s.L):
+            h, _ = eng._forward_layer(h, eng._get_layer_weights(layer_idx), layer_idx, next_id)
+        last_h = h
+        h_3d = rms_norm(h.sum(dim=2), eng.norm_weight, eps)
+        logits = torch.matmul(h_3d.to(eng.lm_head.dtype), eng.lm_head.t())
+        main_in = int(next_id)
+        next_id = logits[:, -1].argmax(dim=-1, keepdim=True)
+        generated.append(int(next_id))
+        lg_main.append(logits[0, -1])
+        # draft (engine.py:2867-2870); the logits rows of its argmaxes are
+        # captured at the head matmul (kept for the parity tests' margins)
+        heads = []
+        draft_ids, n_draft = _draft_with_logits(eng, last_h, s.M, next_id, heads)
+        assert n_draft == s.M
+        # verify (engine.py:2885-2886)
+        n_acc, bonus_logits = _verify_with_logits(eng, draft_ids, next_id, lg_verify)
+        d = [int(v) for v in draft_ids[0]]
+        rec = [main_in, int(next_id), d[0], d[1], n_acc]
+        if n_acc > 0:  # engine.py:2893-2916
+            generated.extend(d[:n_acc])
+            next_id = bonus_logits.argmax(dim=-1, keepdim=True)
+            generated.append(int(next_id))
+        rec.append(int(next_id))
+        recs.append(rec)
+        lg_draft.append(torch.stack(heads))
+    out["mtp_tokens"] = np.array(generated, dtype=np.int64)
+    out["mtp_records"] = np.array(recs, dtype=np.int64)  # main_in, main_pred, d1, d2, n_acc, next_id
+    out["mtp_logits_main"] = _bf16_np(torch.stack(lg_main))
+    out["mtp_logits_draft"] = _bf16_np(torch.stack(lg_draft))
+    out["mtp_logits_verify"] = _bf16_np(torch.stack(lg_verify))
+    out["mtp_meta"] = np.array([s.D, s.I, s.E, s.I_sh, s.K, s.V, s.L, s.hash_layers, s.M, iterations,
+                                first_token], dtype=np.int64)
+
+
+def _draft_with_logits(eng, last_h, M, next_id, rows):
+    """eng._mtp_generate_draft(last_h, M, 0.0, last_token_id=next_id), with the
+    logits of each draft step captured at its matmul with the head."""
+    real = eng.lm_head
+
+    class _Capture:
+        dtype = real.dtype
+
+        def t(self):
+            return _CaptureT()
+
+    class _CaptureT:
+        def __rmatmul__(self, x):
+            lg = x @ real.t()
+            rows.append(lg[0, -1])
+            return lg
+    eng.lm_head = _Capture()
+    try:
+        return eng._mtp_generate_draft(last_h, M, 0.0, last_token_id=next_id)
+    finally:
+        eng.lm_head = real
+
+
+def _verify_with_logits(eng, draft_ids, main_pred, rows):
+    """eng._mtp_verify_batched(draft_ids, 0.0, main_pred_id=main_pred), with
+    the [T, V] logits of its fused forward captured at torch.matmul."""
+    real_matmul = torch.matmul
+    seen = []
+
+    def hook(a, b, *args, **kw):
+        r = real_matmul(a, b, *args, **kw)
+        if r.dim() == 3 and r.shape[-1] == eng.lm_head.shape[0]:
+            seen.append(r[0])
+        return r
+    torch.matmul = hook
+    try:
+        n, bonus = eng._mtp_verify_batched(draft_ids, 0.0, main_pred_id=main_pred)
+    finally:
+        torch.matmul = real_matmul
+    assert len(seen) == 1
+    rows.append(seen[0])
+    return n, bonus
+
+
 def main():
     sys.path.insert(0, str(_ref_path()))
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -222,6 +393,7 @@ def main():
     gen_accept(out)
     gen_permute(out)
     gen_moe(out)
+    gen_mtp(out)
     np.savez_compressed(HERE / "golden.npz", **out)
     print("wrote", HERE / "golden.npz", len(out), "arrays")
 

@@ -1,119 +1,145 @@
-"""MTP decode step on a small model shape: the GPU path (fused add+RMSNorm,
-router / hash routing, MoE kernels, lm_head, greedy acceptance, device-side
-bookkeeping) against the CPU restatement in oracle/mtp.py on the same
-weights."""
+"""MTP speculative decode on the GPU against the reference's own token stream.
+
+tests/golden/golden.npz holds generate()'s greedy MTP loop (engine.py:
+2809-2922) run by the reference's own code -- _forward_layer / _forward_ffn,
+_mtp_generate_draft / _mtp_forward_draft / _mtp_finalize and
+_mtp_verify_batched, attention off, hc_mult = 1 -- on the small seeded model
+of oracle.inputs.mtp_model: 16 iterations of the token stream, every
+iteration's (main input, main prediction, drafts, n_accept, next input) and
+every logits row an argmax was taken of (tests/golden/make_golden.py,
+gen_mtp). oracle/mtp.py reproduces all of it bit for bit on the CPU
+(tests/test_oracle_golden.py).
+
+Here the GPU path builds the same model (MoEPathModel.load_weights), and
+  * the CUDA-graph-replayed MTPDecoder (the loop bench.py times) must give the
+    reference's token stream and per-iteration decisions exactly;
+  * every decision's logits, recomputed on the GPU from the reference's inputs
+    for that decision, must lie within two bf16 ulps of the reference's row,
+    and the argmax must agree wherever the reference's top two logits are
+    more than twice that apart (rows closer than that are counted and
+    reported: exact bf16 ties are common at V = 1024, the average top-two gap
+    being about 2^7 / (2 ln V) ~ 9 ulps, and the token-stream check above
+    covers them on this seeded case).
+"""
 from __future__ import annotations
 
 import numpy as np
 import pytest
 import torch
 
-from oracle import accept as A
+from oracle import inputs as I
 from oracle import mtp as OM
 
 pytestmark = pytest.mark.gpu
 
-TOL = 3e-2  # two MoE layers at <= 1e-2 each plus norms, relative to the max magnitude
+ULPS = 2  # logits tolerance in bf16 ulps of the row's top logit
 
 
-def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
-    a, b = a.float().cpu(), b.float().cpu()
-    return float((a - b).abs().max() / b.abs().max().clamp(min=1e-30))
+def _bf16(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
 
 
-def _extract(m) -> OM.ModelWeights:
-    """The GPU model's weights in the reference layouts the oracle consumes."""
-    from home_seek_b200.layout import untile_rows
-    st = m.store
-    layers = []
-    for l in range(m.shape.num_layers + 1):
-        lw = st.layers[l]
-
-        def load(e, l=l):
-            return tuple(t.view(torch.uint8).cpu().numpy() for t in st._load_expert_fp4_raw(l, e))
-
-        sh = None
-        if lw.sh_w13 is not None:
-            w13 = torch.stack([untile_rows(lw.sh_w13[:, :, 0]), untile_rows(lw.sh_w13[:, :, 1])]).cpu().numpy()
-            s13 = lw.sh_s13[..., 0].permute(2, 0, 1).contiguous().cpu().numpy()
-            sh = (w13, s13, untile_rows(lw.sh_w2).cpu().numpy(), lw.sh_s2[..., 0].contiguous().cpu().numpy())
-        layers.append(OM.LayerWeights(load, sh,
-                                      lw.gate.cpu() if lw.gate is not None else None,
-                                      lw.bias.cpu() if lw.bias is not None else None,
-                                      lw.tid2eid.cpu() if lw.tid2eid is not None else None))
-    s = m.shape
-    return OM.ModelWeights(layers, m.embed.cpu(), m.lm_head.cpu(), m.norm_w.cpu(), m.ln_w.cpu(), m.e_proj.cpu(),
-                           m.h_proj.cpu(), m.enorm_w.cpu(), m.hnorm_w.cpu(), m.mtp_norm_w.cpu(), s.top_k,
-                           s.hash_layers, s.routed_scaling, s.num_draft)
+def _shape():
+    from home_seek_b200.mtp import ModelShape
+    s = I.MTP_SMALL
+    return ModelShape(num_layers=s.L, num_experts=s.E, hidden=s.D, inter=s.I, shared_inter=s.I_sh, vocab=s.V,
+                      top_k=s.K, hash_layers=s.hash_layers, routed_scaling=1.5, num_draft=s.M)
 
 
 @pytest.fixture(scope="module")
 def model():
-    from home_seek_b200.mtp import ModelShape, MoEPathModel
-    shape = ModelShape(num_layers=2, num_experts=16, hidden=512, inter=512, shared_inter=512, vocab=1024, top_k=6,
-                       hash_layers=1, routed_scaling=1.5, num_draft=2)
-    m = MoEPathModel(shape, device="cuda", seed=3)
-    return m, _extract(m)
+    from home_seek_b200.mtp import MoEPathModel
+    return MoEPathModel(_shape(), device="cuda", weights=I.mtp_model(I.MTP_SMALL))
 
 
-@pytest.mark.parametrize("ids", [[5], [5, 17, 300]])
-def test_forward_and_logits_match_oracle(model, ids):
-    m, W = model
-    t = torch.tensor(ids, dtype=torch.int64)
-    h, x = m.forward(t.cuda())
-    ho, xo = OM.forward(W, t, m.shape.num_layers)
-    assert _rel(h, ho) <= TOL, _rel(h, ho)
-    assert _rel(x, xo) <= TOL, _rel(x, xo)
-    lg, lgo = m.logits(x), OM.logits(W, xo)
-    assert _rel(lg, lgo) <= TOL, _rel(lg, lgo)
-
-
-def _near_argmax(lv: torch.Tensor, tok: int) -> bool:
-    lv = lv.float()
-    return float(lv[tok]) >= float(lv.max()) - TOL * float(lv.abs().max())
-
-
-def test_draft_tokens_are_oracle_argmax(model):
-    from home_seek_b200 import ops
-    m, W = model
-    h, x = m.forward(torch.tensor([5], device="cuda"))
-    none = torch.empty(1, 0, dtype=torch.int64, device="cuda")
-    _, main = ops.accept_greedy(m.logits(x).view(1, 1, -1), none)
-    d = m.draft(h, main).cpu()
-    prev, tok = h.cpu(), main.cpu()
-    for i in range(m.shape.num_draft):
-        prev, lgo = OM.draft_step(W, prev, tok, m.shape.num_layers)
-        assert _near_argmax(lgo[0], int(d[i])), (i, int(d[i]), int(lgo[0].float().argmax()))
-        tok = d[i:i + 1]
-
-
-def test_iteration_bookkeeping_matches_greedy_acceptance(model):
-    """One MTPDecoder iteration: the tokens it appends, its count, acceptance
-    and next id follow oracle.accept.greedy on the logits of the same passes."""
+def test_graph_replayed_decoder_matches_the_reference_token_stream(model, golden):
     from home_seek_b200 import ops
     from home_seek_b200.mtp import MTPDecoder
-    m, _ = model
-    dec = MTPDecoder(m, max_tokens=64)
-    dec.reset(5)
-    dec.iteration()
+    meta = golden["mtp_meta"]
+    iters, first = int(meta[9]), int(meta[10])
+    recs = golden["mtp_records"]
+    dec = MTPDecoder(model, max_tokens=8 * iters)
+    dec.reset(first)
+    dec.capture(warmup=1)
+    dec.reset(first)
     torch.cuda.synchronize()
-    # the same passes again (the kernels are deterministic) to see the logits
-    M = m.shape.num_draft
-    h, x = m.forward(torch.tensor([5], device="cuda"))
-    none = torch.empty(1, 0, dtype=torch.int64, device="cuda")
-    _, main = ops.accept_greedy(m.logits(x).view(1, 1, -1), none)
-    d = m.draft(h, main)
-    _, xv = m.forward(torch.cat([main, d]))
-    lv = m.logits(xv).view(1, M + 1, -1).float().cpu().numpy()
-    n_o, nxt_o, _ = A.greedy(lv, d.view(1, M).cpu().numpy())
-    n = int(n_o[0])
-    want = [int(main)] + ([int(v) for v in d[:n].cpu()] + [int(nxt_o[0])] if n > 0 else [])
-    cnt = int(dec.step_count)
-    assert cnt == len(want)
-    assert dec.step_tokens[:cnt].cpu().tolist() == want
-    assert dec.tokens[:cnt].cpu().tolist() == want
-    assert int(dec.accepted) == n and int(dec.count) == cnt
-    assert int(dec.next_id) == (int(nxt_o[0]) if n > 0 else int(main))
+    assert dec.graph is not None
+    for it in range(iters):
+        before = int(dec.count)
+        acc_before = int(dec.accepted)
+        dec.replay()
+        torch.cuda.synchronize()
+        main_in, main_pred, d1, d2, n_acc, nxt = (int(v) for v in recs[it])
+        cnt = int(dec.count) - before
+        got = dec.step_tokens[:cnt].cpu().tolist()
+        want = [main_pred] + ([d1, d2][:n_acc] + [nxt] if n_acc > 0 else [])
+        assert got == want, (it, got, want)
+        assert int(dec.accepted) - acc_before == n_acc, it
+        assert int(dec.next_id) == nxt, it
+    assert ops.check_status(model.device) == 0
+    n = int(dec.count)
+    assert dec.tokens[:n].cpu().numpy().tolist() == golden["mtp_tokens"].tolist()
+    # acceptances of every kind happen on this seeded case
+    assert {int(r[4]) for r in recs} == {0, 1, 2}
+
+
+def _decision_rows(model, golden, it):
+    """The GPU's logits for iteration it's decisions, from the reference's inputs
+    (main input; main prediction and drafts) -> (main [V], draft [M, V], verify [M+1, V])."""
+    main_in, main_pred, d1, d2 = (int(v) for v in golden["mtp_records"][it][:4])
+    dev = model.device
+    h, x = model.forward(torch.tensor([main_in], device=dev))
+    lm = model.logits(x)[0]
+    prev, tok, rows = h, torch.tensor([main_pred], device=dev), []
+    from home_seek_b200 import ops
+    L = model.shape.num_layers
+    for d in (d1, d2):
+        e = ops.rms_norm(model.embed[tok], model.enorm_w) @ model.e_proj.t()
+        hc = ops.rms_norm(prev, model.hnorm_w) @ model.h_proj.t() + e
+        prev = model.layer(hc, L, tok)
+        rows.append(model.logits(ops.rms_norm(prev, model.mtp_norm_w))[0])
+        tok = torch.tensor([d], device=dev)
+    _, xv = model.forward(torch.tensor([main_pred, d1, d2], device=dev))
+    return lm, torch.stack(rows), model.logits(xv)
+
+
+def test_decision_logits_match_the_reference_rows(model, golden):
+    iters = int(golden["mtp_meta"][9])
+    worst, near, checked = 0.0, 0, 0
+    for it in range(iters):
+        lm, ld, lv = _decision_rows(model, golden, it)
+        n_acc = int(golden["mtp_records"][it][4])
+        pairs = [(lm, golden["mtp_logits_main"][it])]
+        pairs += [(ld[i], golden["mtp_logits_draft"][it, i]) for i in range(ld.shape[0])]
+        pairs += [(lv[i], golden["mtp_logits_verify"][it, i]) for i in range(min(n_acc + 1, lv.shape[0]))]
+        for gpu, ref_np in pairs:
+            ref = _bf16(ref_np).float()
+            g = gpu.float().cpu()
+            ulp = float(ref.abs().max()) * 2.0 ** -7
+            dev_ulps = float((g - ref).abs().max()) / ulp
+            worst = max(worst, dev_ulps)
+            assert dev_ulps <= ULPS, (it, dev_ulps)
+            top2 = ref.topk(2).values
+            checked += 1
+            if float(top2[0] - top2[1]) > 2 * ULPS * ulp:
+                assert int(g.argmax()) == int(ref.argmax()), it
+            else:
+                near += 1
+    print(f"decision rows {checked}, worst deviation {worst:.2f} ulp, rows within {2 * ULPS} ulps of a tie {near}")
+
+
+def test_forward_matches_oracle(model):
+    """Layer-by-layer forward (hash layer, router layer, final norm) on a batch
+    of T = 3 and a single token against oracle/mtp.py."""
+    s = I.MTP_SMALL
+    W = OM.weights_from_inputs(I.mtp_model(s), s.L, s.hash_layers, s.K, s.M)
+    for ids in ([5], [5, 17, 300]):
+        t = torch.tensor(ids, dtype=torch.int64)
+        h, x = model.forward(t.cuda())
+        ho, xo = OM.forward(W, t, s.L)
+        for a, b in ((h, ho), (x, xo)):
+            rel = float((a.float().cpu() - b.float()).abs().max() / b.float().abs().max())
+            assert rel <= 2e-2, rel
 
 
 def test_rms_norm_and_add_rms_norm_match_reference_formula():

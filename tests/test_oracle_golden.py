@@ -155,3 +155,23 @@ def test_rejection_oracle_properties():
             p = A._softmax64(tl[b, n2[b]].astype(np.float32) / np.float32(0.7))
             q = A._softmax64(dl[b, n2[b]].astype(np.float32) / np.float32(0.7))
             assert p[tok2[b]] > q[tok2[b]]
+
+
+def test_mtp_decode_loop_matches_reference(golden):
+    """oracle.mtp.decode_loop against the reference's own MTP loop (its
+    _forward_layer, _mtp_generate_draft and _mtp_verify_batched on the seeded
+    small model, attention off): the token stream, every iteration's decisions
+    and every logits row an argmax was taken of, bit for bit."""
+    from oracle import inputs as I
+    from oracle import mtp as OM
+    s = I.MTP_SMALL
+    meta = golden["mtp_meta"]
+    assert list(meta[:9]) == [s.D, s.I, s.E, s.I_sh, s.K, s.V, s.L, s.hash_layers, s.M]
+    W = OM.weights_from_inputs(I.mtp_model(s), s.L, s.hash_layers, s.K, s.M)
+    tokens, recs, lg = OM.decode_loop(W, int(meta[10]), int(meta[9]), s.L)
+    assert np.array_equal(tokens, golden["mtp_tokens"])
+    assert np.array_equal(recs, golden["mtp_records"])
+    for k in ("main", "draft", "verify"):
+        assert np.array_equal(lg[k].contiguous().view(torch.int16).numpy().view(np.uint16),
+                              golden[f"mtp_logits_{k}"]), k
+    assert {int(r[4]) for r in recs} == {0, 1, 2}  # rejections, one and two acceptances
