@@ -124,39 +124,109 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU
+def _reference_modules():
+    """The reference's own modules from baseline/_ref (pip-installed there from
+    its source tree, --no-deps), or None when that install is absent."""
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "home_seek").is_dir():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    try:
+        from home_seek.fused_moe import FusedMoEFFN, SharedExpertFFN
+        from home_seek.inference_engine.weight_loader import load_fp8_weight
+        from home_seek.router import compute_expert_affinity_with_bias
+    except Exception:  # noqa: BLE001 (an unusable install falls back to the port)
+        return None
+    return FusedMoEFFN, SharedExpertFFN, load_fp8_weight, compute_expert_affinity_with_bias
+
+
 def cpu_sample(threads: int | None = None):
-    """The reference algorithm's CPU path (oracle port of fused_moe.py:458-551 +
-    the FP8 shared expert + router), timed on a bounded sample: one T=3 verify
-    MoE layer and one T=1 decode MoE layer at config-0 shapes, plus one lm_head
-    GEMV. Returns (tok_per_s, detail)."""
+    """The reference's CPU path timed on a bounded sample: one T=3 verify MoE
+    layer and one T=1 decode MoE layer at config-0 shapes (router, routed FP4
+    experts, FP8 shared expert, bf16 add) and one lm_head GEMV, extrapolated to
+    the 43-layer MTP iteration. Runs the reference's own code from baseline/_ref
+    (compute_expert_affinity_with_bias, FusedMoEFFN(use_triton=False).forward,
+    SharedExpertFFN(use_triton=False).forward + load_fp8_weight: kind
+    "reference"), else the oracle's restatement of it (kind "port"). Weights
+    come from the seeded generators of oracle/inputs.py, outside the timed
+    region. Returns (tok_per_s, detail)."""
     import torch
-    from oracle import inputs as I
-    from oracle import moe as O
     n = threads or os.cpu_count() or 1
     torch.set_num_threads(n)
-    shape = I.CONFIG0
-    gate, bias = I.router_weights(256, 4096, seed=1)
-    sh = I.shared_fp8(4096, 2048, seed=2)
-    load = I.make_loader(shape)
-    h3, h1 = I.hidden(3, 4096, seed=0), I.hidden(1, 4096, seed=5)
-    i3, w3 = O.router(h3, gate, bias)
-    i1, w1 = O.router(h1, gate, bias)
-    for e in set(i3.flatten().tolist()) | set(i1.flatten().tolist()):
-        load(int(e))  # generate the sample's weights outside the timed region
-    head = (torch.randn(129280, 4096) * 0.02).to(torch.bfloat16)
+    route, layer, h3, h1, head, kind = _cpu_setup()
     t0 = time.perf_counter()
-    O.moe_layer(h3, i3, w3, load, sh)
+    i3, w3 = route(h3)
+    layer(h3, i3, w3)
     t1 = time.perf_counter()
-    O.router(h1, gate, bias)
-    O.moe_layer(h1, i1, w1, load, sh)
+    i1, w1 = route(h1)
+    layer(h1, i1, w1)
     t2 = time.perf_counter()
-    _ = h1 @ head.t()
+    _ = torch.matmul(h1, head.t())
     t3 = time.perf_counter()
     t_verify, t_main, t_head = t1 - t0, t2 - t1, t3 - t2
     L = 43
     t_iter = L * (t_main + t_verify) + 2 * t_main + 4 * t_head
     return 1.0 / t_iter, {"t_layer_T3_s": t_verify, "t_layer_T1_s": t_main, "t_lm_head_s": t_head, "cores": n,
-                          "t_iter_s": t_iter}
+                          "t_iter_s": t_iter, "kind": kind}
+
+
+_CPU_SETUP = None
+
+
+def _cpu_setup():
+    """Inputs and callables of the CPU sample, built once per process (the
+    weight generation stays out of every timed step)."""
+    global _CPU_SETUP
+    if _CPU_SETUP is not None:
+        return _CPU_SETUP
+    import numpy as np
+    import torch
+    from oracle import inputs as I
+    shape = I.CONFIG0
+    gate, bias = I.router_weights(256, 4096, seed=1)
+    w13, s13, w2, s2 = I.shared_fp8(4096, 2048, seed=2)
+    load = I.make_loader(shape)
+    h3, h1 = I.hidden(3, 4096, seed=0), I.hidden(1, 4096, seed=5)
+    head = (torch.randn(129280, 4096, generator=torch.Generator().manual_seed(9)) * 0.02).to(torch.bfloat16)
+    mods = _reference_modules()
+    if mods is not None:
+        FusedMoEFFN, SharedExpertFFN, load_fp8_weight, router = mods
+        kind = "reference"
+        t8 = lambda a: torch.from_numpy(np.ascontiguousarray(a)).view(torch.float8_e4m3fn)  # noqa: E731
+        u8 = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+        sw = (load_fp8_weight(t8(w13[0]), u8(s13[0])), load_fp8_weight(t8(w13[1]), u8(s13[1])),
+              load_fp8_weight(t8(w2), u8(s2)))
+        ffn = FusedMoEFFN(num_experts=256, intermediate_size=2048, hidden_size=4096, use_triton=False)
+        shf = SharedExpertFFN(hidden_size=4096, intermediate_size=2048, use_triton=False)
+
+        def ref_load(layer, eid):
+            a, sa, b, sb, c, sc = load(int(eid))
+            i8 = lambda x: torch.from_numpy(x).view(torch.int8)  # noqa: E731
+            e8 = lambda x: torch.from_numpy(x).view(torch.float8_e8m0fnu)  # noqa: E731
+            return (i8(a), e8(sa), i8(b), e8(sb), i8(c), e8(sc))
+
+        def route(h):
+            return router(h, gate, bias, top_k=6, routed_scaling_factor=1.5)
+
+        def layer(h, idx, w):  # engine.py:1480-1536: routed + shared, bf16 add
+            return ffn.forward(h, idx, w, ref_load, 5) + shf.forward(h.unsqueeze(0), *sw, torch.bfloat16)[0]
+    else:
+        from oracle import moe as O
+        kind = "port"
+        sh = (w13, s13, w2, s2)
+
+        def route(h):
+            return O.router(h, gate, bias)
+
+        def layer(h, idx, w):
+            return O.moe_layer(h, idx, w, load, sh)
+    i3, w3 = route(h3)
+    i1, w1 = route(h1)
+    for e in set(i3.flatten().tolist()) | set(i1.flatten().tolist()):
+        load(int(e))  # generate the sample's weights outside the timed region
+    _CPU_SETUP = (route, layer, h3, h1, head, kind)
+    return _CPU_SETUP
 
 
 def run_reference(args):
@@ -177,7 +247,7 @@ def run_reference(args):
         "config": {"workload": "config1 MTP iteration, MoE path, extrapolated from one T=3 + one T=1 MoE layer "
                                "and one lm_head GEMV per step", "model": "DeepSeek-V4-Flash-shape 43L",
                    "global_batch": 1, "seq_len": 3, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": det["cores"], "kind": "port",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": det["cores"], "kind": det["kind"],
                          "sample": "per step: 1 verify MoE layer (T=3) + 1 decode MoE layer (T=1) + 1 lm_head "
                                    "GEMV at config-0 shapes; x43 layers + 2 draft layers + 4 heads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -391,6 +461,97 @@ def run_moe_ep(args):
         dist.destroy_process_group()
 
 
+def run_accept(args):
+    """Config 4: batched speculative acceptance on [64, 3, 129280] bf16 logits
+    (target and draft ~N(0, 3^2), t = 0.7, fp32 uniforms [64, 3] from seed 1),
+    greedy (hs_accept_greedy, reads the target: 49.6 MB) and rejection sampling
+    (hs_accept_rejection, algorithmic bytes 2 x 64 x 3 x V x 2 = 99.3 MB).
+    Inputs are smaller than L2, so a 256 MB buffer is written between timed
+    calls (outside the events). Prints one JSON line (not the driver's line)."""
+    import torch
+    from home_seek_b200 import ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, M, V, t = 64, 2, 129280, 0.7
+    # the config-4 inputs (the same seeds and draws as the parity tests' fixture)
+    g = torch.Generator().manual_seed(101)
+    target = (torch.randn(B, M + 1, V, generator=g) * 3.0).to(torch.bfloat16)
+    draft = (torch.randn(B, M + 1, V, generator=g) * 3.0).to(torch.bfloat16)
+    u = torch.rand(B, M + 1, generator=torch.Generator().manual_seed(1))
+    q = torch.softmax(draft[:, :M].float() / t, dim=-1)
+    ids = torch.multinomial(q.reshape(B * M, V), 1, generator=torch.Generator().manual_seed(2)).reshape(B, M)
+    target, draft, ids, u = target.to(dev), draft.to(dev), ids.to(dev), u.to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    peak, kind = _peaks()
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        ms = []
+        for _ in range(reps):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ms.append(a.elapsed_time(b))
+        return statistics.median(ms)
+
+    g_ms = timed(lambda: ops.accept_greedy(target, ids), args.reps)
+    r_ms = timed(lambda: ops.accept_rejection(target, draft, ids, u, t), args.reps)
+    g_bytes = B * (M + 1) * V * 2
+    r_bytes = 2 * B * (M + 1) * V * 2 + B * (M + 1) * 4
+    out = {"mode": "accept", "config": "config4: B=64, M=2, V=129280, t=0.7", "reps": args.reps,
+           "l2": "256 MB written between timed calls",
+           "greedy_us": 1000 * g_ms, "greedy_bytes": g_bytes, "greedy_gbs": g_bytes / (g_ms * 1e-3) / 1e9,
+           "rejection_us": 1000 * r_ms, "rejection_bytes": r_bytes, "rejection_gbs": r_bytes / (r_ms * 1e-3) / 1e9,
+           "peak_gbs": peak, "peak_kind": kind}
+    out["greedy_frac"] = out["greedy_gbs"] / peak
+    out["rejection_frac"] = out["rejection_gbs"] / peak
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def run_head(args):
+    """The lm_head GEMV with the fused argmax (hs_lm_head_argmax) at the model's
+    shape: x [T, 4096] bf16, head [129280, 4096] bf16 (1.06 GB, larger than L2),
+    T = args.T; against cuBLAS (torch.matmul) + torch.argmax, the path it
+    replaces. Prints one JSON line (not the driver's line)."""
+    import torch
+    from home_seek_b200 import ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    V, D, T = 129280, 4096, args.T
+    g = torch.Generator(device=dev).manual_seed(3)
+    head = (torch.randn(V, D, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    x = torch.randn(T, D, generator=g, device=dev).to(torch.bfloat16)
+    peak, kind = _peaks()
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    ours = timed(lambda: ops.lm_head_argmax(x, head), args.reps)
+    base = timed(lambda: (x @ head.t()).argmax(dim=-1), args.reps)
+    nbytes = V * D * 2 + T * D * 2
+    am = ops.lm_head_argmax(x, head)[0]
+    same = bool(torch.equal(am, (x @ head.t()).argmax(dim=-1)))
+    print(json.dumps({"mode": "head", "T": T, "reps": args.reps, "us": 1000 * ours, "bytes": nbytes,
+                      "gbs": nbytes / (ours * 1e-3) / 1e9, "frac": nbytes / (ours * 1e-3) / 1e9 / peak,
+                      "cublas_argmax_us": 1000 * base, "argmax_equal_to_cublas": same, "peak_gbs": peak,
+                      "peak_kind": kind}), flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -430,9 +591,17 @@ def run_ours(args):
     dec.count.zero_()
     dec.accepted.zero_()
 
+    def device_barrier():
+        """Every rank's next event fires when a one-element all-reduce has
+        completed on the device, i.e. at the same moment on every rank (a host
+        barrier alone leaves each rank's start at its own host wake-up time)."""
+        if world > 1:
+            dist.barrier()
+            flag = torch.ones(1, device=dev)
+            dist.all_reduce(flag)
+
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
+    device_barrier()
     torch.cuda.synchronize()
     with ClockSampler(local if not os.environ.get("CUDA_VISIBLE_DEVICES") else
                       int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
@@ -462,8 +631,7 @@ def run_ours(args):
     host_cnt = torch.empty(1, dtype=torch.int64, pin_memory=True)
     host_in.fill_(4321)
     dec.count.zero_()
-    if world > 1:
-        dist.barrier()
+    device_barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_tokens = 0
@@ -525,7 +693,7 @@ def run_ours(args):
                      "peak_kind": peak_kind, "avg_ms": roof["avg_ms"], "t1_layer_ms": roof["t1_ms"],
                      "avg_bytes": roof["avg_bytes"],
                      "avg_unique_experts": roof["avg_unique_experts"]},
-        "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_d["cores"], "kind": "port",
+        "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_d["cores"], "kind": cpu_d.get("kind", "port"),
                          "sample": "one T=3 + one T=1 MoE layer and one lm_head GEMV at config-0 shapes, "
                                    "extrapolated to 43 layers + 2 draft layers + 4 heads"},
         "e2e": e2e,
@@ -544,9 +712,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=43)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--mode", default="decode", choices=["decode", "moe", "moe-ep"],
+    ap.add_argument("--mode", default="decode", choices=["decode", "moe", "moe-ep", "accept", "head"],
                     help="moe: MoE FFN microbenchmark only (profiling; not the driver's line); moe-ep: "
-                         "prefill-size MoE with the tokens sharded over the torchrun ranks (TokenShardedEP)")
+                         "prefill-size MoE with the tokens sharded over the torchrun ranks (TokenShardedEP); "
+                         "accept: config-4 acceptance kernels; head: lm_head GEMV + fused argmax")
     ap.add_argument("--T", type=int, default=3, help="tokens per MoE call in --mode moe")
     ap.add_argument("--reps", type=int, default=20, help="MoE calls timed in --mode moe")
     ap.add_argument("--fused", action="store_true", help="--mode moe: router folded into the call (T <= 8)")
@@ -561,6 +730,10 @@ def main():
         return run_moe_only(args)
     if args.mode == "moe-ep":
         return run_moe_ep(args)
+    if args.mode == "accept":
+        return run_accept(args)
+    if args.mode == "head":
+        return run_head(args)
     return run_ours(args)
 
 

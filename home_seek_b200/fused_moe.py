@@ -11,9 +11,12 @@ output). Two loader kinds are accepted:
     synchronisation and no per-expert Python work;
   * any reference loader returning FP4 6-tuples (w1, s1, w3, s3, w2, s2): the
     touched experts are gathered once into a compact device store (like the
-    reference's torch.cat at fused_moe.py:515-517) and the same kernel runs.
-A loader returning BF16 3-tuples is not supported (the B200 path consumes the
-packed FP4 form); it raises TypeError.
+    reference's torch.cat at fused_moe.py:515-517) and the same kernel runs;
+  * a loader returning the BF16 3-tuples the reference's T >= 2 path passes
+    (`_bf16_load`, engine.py:1480-1486: FP4 experts dequantised to bf16): each
+    weight is turned back into packed e2m1 + UE8M0 losslessly
+    (layout.fp4_block_from_bf16) and gathered the same way; a bf16 weight that
+    is not an FP4 block-scaled value raises TypeError.
 """
 from __future__ import annotations
 
@@ -85,8 +88,12 @@ class FusedMoEFFN:
             v = load_expert_fn(layer_idx, e)
             if v is None:
                 continue
-            if len(v) != 6:
-                raise TypeError("load_expert_fn must return FP4 6-tuples on the B200 path")
+            if len(v) == 3:  # bf16 (w1, w3, w2) of FP4 weights: back to the packed form
+                from .layout import fp4_block_from_bf16
+                (a, sa), (b, sb), (c, sc) = (fp4_block_from_bf16(x.to(torch.bfloat16)) for x in v)
+                v = (a, sa, b, sb, c, sc)
+            elif len(v) != 6:
+                raise TypeError("load_expert_fn must return FP4 6-tuples or their BF16 3-tuples")
             tuples.append(v)
             kept.append(e)
         if not tuples:
@@ -116,10 +123,18 @@ def _localise(topk_idx: torch.Tensor, offset: int, n_local: int) -> torch.Tensor
 
 
 class SharedExpertFFN:
-    """fused_moe.py:573-598 for the FP8 shared expert held in an HBMExpertStore.
+    """fused_moe.py:573-598: the FP8 shared expert, alone (the fused MoE call
+    normally runs it in the same launches as the routed experts).
 
-    forward(hidden_states [B, T, D], store, layer_idx) runs the shared expert
-    alone (the fused MoE call normally includes it in the same launches)."""
+    forward(hidden_states [B, T, D], w1, w3, w2, dtype) takes the reference's
+    arguments (fused_moe.py:585). Each weight is either the FP8 form the
+    reference keeps before load_fp8_weight, a (e4m3 [R, C], UE8M0 128x128 block
+    scales [R/128, C/128]) pair, or the bf16 tensor load_fp8_weight returned
+    (engine.py:1451, 1469, 1534 pass those), which is turned back into the
+    FP8 form losslessly (layout.fp8_block_from_bf16; a bf16 weight that is not
+    an FP8 block-scaled value raises TypeError). The packed weights are built
+    once per weight set and kept. forward(hidden_states, store, layer_idx,
+    dtype) runs the shared expert held by an HBMExpertStore layer."""
 
     def __init__(self, hidden_size: int = 4096, intermediate_size: int = 2048, swiglu_limit: float = 10.0,
                  use_triton: bool = True, triton_blocks=(16, 32, 64), cublas_max_tokens: int = 8):
@@ -127,10 +142,42 @@ class SharedExpertFFN:
         self.intermediate_size = intermediate_size
         self.swiglu_limit = swiglu_limit
         self.use_triton = False
+        self._packed: dict = {}
 
-    def forward(self, hidden_states: torch.Tensor, store, layer_idx: int, dtype: torch.dtype = torch.bfloat16):
-        if isinstance(store, torch.Tensor):
-            raise TypeError("SharedExpertFFN on B200 consumes the FP8 store form: pass (store, layer_idx)")
+    @staticmethod
+    def _fp8(w) -> tuple:
+        from .layout import fp8_block_from_bf16
+        if isinstance(w, (tuple, list)):
+            data, scale = w
+            return data.contiguous().view(torch.uint8), _e8m0_bytes(scale)
+        if isinstance(w, torch.Tensor) and w.dtype == torch.bfloat16:
+            return fp8_block_from_bf16(w)
+        raise TypeError("shared-expert weights must be (e4m3, block scale) pairs or bf16 FP8 values")
+
+    def _store_for(self, w1, w3, w2, device):
+        """A one-layer store holding this shared expert (no routed expert is used),
+        built once per weight set."""
+        from .expert_store import HBMExpertStore
+        key = tuple((w[0] if isinstance(w, (tuple, list)) else w).data_ptr() for w in (w1, w3, w2))
+        st = self._packed.get(key)
+        if st is not None:
+            return st
+        (a, sa), (b, sb), (c, sc) = (self._fp8(w) for w in (w1, w3, w2))
+        I_sh, D = a.shape
+        st = HBMExpertStore(1, num_experts=1, hidden_size=D, intermediate_size=512, shared_intermediate_size=I_sh,
+                            device=device, with_router=False)
+        st.set_shared(0, torch.stack([a, b]).to(device), torch.stack([sa, sb]).to(device), c.to(device),
+                      sc.to(device))
+        self._packed[key] = st
+        return st
+
+    def forward(self, hidden_states: torch.Tensor, w1, w3=None, w2=None, dtype: torch.dtype = torch.bfloat16):
+        if hasattr(w1, "desc") and hasattr(w1, "layers"):  # (store, layer_idx[, dtype])
+            store, layer_idx = w1, int(w3)
+            if isinstance(w2, torch.dtype):
+                dtype = w2
+        else:
+            store, layer_idx = self._store_for(w1, w3, w2, hidden_states.device), 0
         B, T, D = hidden_states.shape
         h = hidden_states.reshape(-1, D).contiguous()
         none = torch.full((h.shape[0], 1), -1, dtype=torch.int64, device=h.device)

@@ -304,3 +304,136 @@ class MTPDecoder:
         self.next_id.fill_(token)
         self.count.zero_()
         self.accepted.zero_()
+
+
+class MTPEngine:
+    """The reference engine's MTP methods over the MoE path, with the
+    reference's names, arguments and returns (HomeSeekInferenceEngine,
+    inference_engine/engine.py): `_mtp_generate_draft` (engine.py:2251-2336),
+    `_mtp_verify_batched` (engine.py:2431-2540) and the main decode step of
+    generate() (engine.py:2811-2853). Hidden states carry hc_mult = 1 (the
+    MHC streams are on the attention path this build does not own): [1, 1, 1,
+    D] or [1, D].
+
+    Temperature: the reference draws draft and bonus tokens with
+    torch.multinomial; here they are drawn by inverse CDF from a supplied
+    uniform (ops.sample), so a run is reproducible given the uniforms (drawn
+    with torch.rand on the device when none are given). Verification compares
+    argmaxes as the reference does at any temperature;
+    `_mtp_verify_rejection` is the speculative-sampling acceptance (accept d_i
+    iff u_i < p_i(d_i) / q_i(d_i)), which the reference does not have.
+    """
+
+    def __init__(self, model: MoEPathModel):
+        self.model = model
+        self._global_pos = 0
+        self._mtp_draft_logits: Optional[torch.Tensor] = None  # [M, V] of the last sampled draft
+
+    def _ids(self, t: torch.Tensor) -> torch.Tensor:
+        return t.reshape(-1).to(device=self.model.device, dtype=torch.int64)
+
+    def main_step(self, next_id: torch.Tensor, temperature: float = 0.0, uniform: Optional[torch.Tensor] = None):
+        """One decode step of generate() (engine.py:2811-2853): forward the token,
+        final norm, lm_head, argmax (t = 0) or a sample (t > 0). Returns
+        (last hidden [1, 1, 1, D], next token [1, 1])."""
+        m = self.model
+        h, x = m.forward(self._ids(next_id)[-1:])
+        if temperature > 0:
+            u = uniform if uniform is not None else torch.rand(1, device=m.device)
+            tok = ops.sample(m.logits(x), temperature, u)
+        else:
+            tok = m.greedy(x)[2]
+        return h.view(1, 1, 1, -1), tok.view(1, 1)
+
+    def _mtp_generate_draft(self, last_hidden: torch.Tensor, num_draft: int = 3, temperature: float = 0.6,
+                            last_token_id: Optional[torch.Tensor] = None, uniform: Optional[torch.Tensor] = None):
+        """engine.py:2251-2336: num_draft autoregressive MTP steps from the main
+        model's last hidden state. Step i: e = e_proj(enorm(embed(tok_i))) (a
+        zero embedding when step 0 has no last token), h = h_proj(hnorm(prev))
+        + e, the MTP block (its routed experts, engine.py:2036-2107), its head
+        norm, lm_head, then argmax (t = 0) or a sample with uniform[i] (t > 0).
+        Returns (draft_ids [1, num_draft] int64, num_draft), or (None, 0)."""
+        m = self.model
+        if num_draft < 1:
+            return None, 0
+        s = m.shape
+        prev = last_hidden.reshape(-1, s.hidden)[-1:].to(torch.bfloat16).contiguous()
+        dev = prev.device
+        if temperature > 0 and uniform is None:
+            uniform = torch.rand(num_draft, device=dev)
+        toks, rows = [], []
+        for step in range(num_draft):
+            if step == 0 and last_token_id is not None:
+                tok = self._ids(last_token_id)[-1:]
+            elif step > 0:
+                tok = toks[-1]
+            else:
+                tok = None
+            e_in = m.embed[tok] if tok is not None else torch.zeros(1, s.hidden, dtype=torch.bfloat16, device=dev)
+            e = ops.rms_norm(e_in, m.enorm_w) @ m.e_proj.t()
+            hc = ops.rms_norm(prev, m.hnorm_w) @ m.h_proj.t() + e
+            prev = m.layer(hc, s.num_layers, tok if tok is not None else torch.zeros(1, dtype=torch.int64, device=dev))
+            xm = ops.rms_norm(prev, m.mtp_norm_w)
+            if temperature > 0:
+                lg = m.logits(xm)
+                rows.append(lg)
+                t = ops.sample(lg, temperature, uniform.reshape(-1)[step:step + 1])
+            else:
+                t = m.greedy(xm)[2]
+            toks.append(t)
+        self._mtp_draft_logits = torch.cat(rows) if rows else None
+        return torch.cat(toks).view(1, num_draft), num_draft
+
+    def _verify_forward(self, draft_ids: torch.Tensor, main_pred_id: Optional[torch.Tensor]):
+        ids = self._ids(draft_ids)
+        if main_pred_id is not None:
+            ids = torch.cat([self._ids(main_pred_id)[-1:], ids])
+        return ids, self.model.forward(ids)[1]
+
+    def _mtp_verify_batched(self, draft_ids: torch.Tensor, temperature: float = 0.6,
+                            main_pred_id: Optional[torch.Tensor] = None):
+        """engine.py:2431-2540: one fused forward over [main_pred, drafts]; logits[i]
+        predicts the token after combined[i]; accept combined[i + 1] while
+        argmax(logits[i]) equals it. Returns (n_accept: int, bonus_logits
+        [1, V] bf16 = logits[n_accept]), or (0, None) with no drafts. The
+        decision is hs_lm_head_argmax's fused greedy loop; reading n_accept is
+        the one host synchronisation the reference's int return implies."""
+        if not isinstance(draft_ids, torch.Tensor) or draft_ids.shape[-1] == 0:
+            return 0, None
+        m = self.model
+        ids, xv = self._verify_forward(draft_ids, main_pred_id)
+        _, n, _, lg = ops.lm_head_argmax(xv, m.lm_head, draft_ids=ids[1:], want_logits=True)
+        n_accept = int(n)
+        pos = self._global_pos
+        self._global_pos = pos + n_accept  # engine.py:2518
+        return n_accept, lg[n_accept:n_accept + 1]
+
+    def _mtp_verify_rejection(self, draft_ids: torch.Tensor, temperature: float, main_pred_id: torch.Tensor,
+                              uniform: Optional[torch.Tensor] = None):
+        """Speculative-sampling acceptance of the last sampled draft (Leviathan et
+        al. 2023): target p_i = softmax(verify logits[i] / t), draft q_i =
+        softmax(draft logits[i] / t); accept d_i iff u_i < p_i(d_i) / q_i(d_i);
+        at the first rejection sample from normalise(max(0, p_i - q_i)), else
+        the bonus from p_M, with u_M. Returns (n_accept: int, next token [1, 1])."""
+        m = self.model
+        q = self._mtp_draft_logits
+        M = self._ids(draft_ids).numel()
+        if q is None or q.shape[0] != M:
+            raise ValueError("_mtp_verify_rejection needs the draft logits of a sampled draft (temperature > 0)")
+        _, xv = self._verify_forward(draft_ids, main_pred_id)
+        p = m.logits(xv)
+        u = uniform if uniform is not None else torch.rand(M + 1, device=m.device)
+        n, nxt = ops.accept_rejection(p.view(1, M + 1, -1), q.view(1, M, -1), self._ids(draft_ids).view(1, M),
+                                      u.view(1, M + 1), temperature)
+        n_accept = int(n[0])
+        self._global_pos += n_accept
+        return n_accept, nxt.view(1, 1)
+
+    def bonus_token(self, bonus_logits: torch.Tensor, temperature: float = 0.0,
+                    uniform: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """generate()'s next token from the verify's bonus logits (engine.py:
+        2905-2913): argmax at t = 0, a sample from softmax(bonus / t) above."""
+        if temperature > 0:
+            u = uniform if uniform is not None else torch.rand(1, device=bonus_logits.device)
+            return ops.sample(bonus_logits.reshape(1, -1).contiguous(), temperature, u).view(1, 1)
+        return bonus_logits.reshape(1, -1).argmax(dim=-1, keepdim=True)

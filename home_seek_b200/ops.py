@@ -431,6 +431,28 @@ def accept_rejection(target: torch.Tensor, draft: torch.Tensor, draft_ids: torch
     return n, nxt
 
 
+def sample(logits: torch.Tensor, temperature: float, uniform: torch.Tensor) -> torch.Tensor:
+    """One token per row from softmax(logits / temperature) by inverse CDF in
+    ascending token order with a supplied uniform: the sampling of the draft
+    (engine.py:2327-2331) and of the bonus token (engine.py:2908-2911) with
+    torch.multinomial replaced by a given u in [0, 1). logits [B, V] bf16,
+    uniform [B] f32 -> int64 [B]. (hs_accept_rejection with no drafts.)"""
+    dev = _check_cuda(logits, uniform)
+    if logits.dtype != torch.bfloat16:
+        raise TypeError("logits must be bf16")
+    if not temperature > 0:
+        raise ValueError("sampling needs a temperature > 0 (use lm_head_argmax for t = 0)")
+    B, V = logits.shape
+    u = uniform.reshape(-1).to(torch.float32).contiguous()
+    if u.numel() != B:
+        raise ValueError(f"{u.numel()} uniforms for {B} rows")
+    n = torch.empty(B, dtype=torch.int32, device=dev)
+    nxt = torch.empty(B, dtype=torch.int64, device=dev)
+    _launch("hs_accept_rejection", logits.contiguous().data_ptr(), None, B, 0, 0, V, None, u.data_ptr(),
+            float(temperature), n.data_ptr(), nxt.data_ptr(), status_word(dev).data_ptr(), _stream(dev))
+    return nxt
+
+
 # --- lm_head + greedy decision ---------------------------------------------------
 
 def lm_head_argmax(x: torch.Tensor, head: torch.Tensor, draft_ids: Optional[torch.Tensor] = None,
@@ -520,7 +542,7 @@ def fill_bytes(t: torch.Tensor, seed: int, lo: int = 0, hi: int = 255) -> torch.
 
 
 __all__ = ["HsError", "router_topk", "hash_route", "make_moe_desc", "moe_ffn", "moe_permute", "moe_unpermute",
-           "accept_greedy", "accept_rejection", "lm_head_argmax", "fill_bytes", "rms_norm", "add_rms_norm", "moe_ffn_partials",
+           "accept_greedy", "accept_rejection", "lm_head_argmax", "sample", "fill_bytes", "rms_norm", "add_rms_norm", "moe_ffn_partials",
            "moe_route_ffn",
            "moe_combine", "moe_combine_add_rms_norm", "check_status",
            "status_word", "workspace"]

@@ -206,14 +206,31 @@ def test_moe_config2_zipf_full_shape(T):
     assert rel(out, ref) <= MOE_TOL, rel(out, ref)
 
 
-@pytest.mark.parametrize("T", [512, 4096])
-def test_moe_large_t_full_shape_rows_match_token_mode(T):
-    """Config-2 routing at the full shape with more than 1024 pairs (the
-    segmented plan), feeding the weight-major kernels (T=512, 12 pairs per
-    expert) or the token-major kernels (T=4096): a token's output does not
-    depend on the other tokens in the call, so selected rows must equal
-    (within the MoE tolerance) the same tokens run alone through the
-    token-mode kernels, which the oracle pins; and two runs are bit-identical."""
+def _store_reference_form(st, layer: int = 0):
+    """An HBMExpertStore layer's weights in the reference's formats for the
+    oracle: a loader eid -> FP4 6-tuple (uint8 numpy) and the FP8 shared tuple."""
+    from home_seek_b200.layout import untile_rows
+    lw = st.layers[layer]
+
+    def load(e):
+        return tuple(t.view(torch.uint8).cpu().numpy() for t in st._load_expert_fp4_raw(layer, e))
+
+    w13 = torch.stack([untile_rows(lw.sh_w13[:, :, 0]), untile_rows(lw.sh_w13[:, :, 1])]).cpu().numpy()
+    s13 = lw.sh_s13[..., 0].permute(2, 0, 1).contiguous().cpu().numpy()
+    sh = (w13, s13, untile_rows(lw.sh_w2).cpu().numpy(), lw.sh_s2[..., 0].contiguous().cpu().numpy())
+    return load, sh
+
+
+@pytest.mark.parametrize("T", [1024, 8192])
+def test_moe_large_t_full_shape_sampled_rows_match_oracle(T):
+    """Config-2 routing at the full shape (D = 4096, I = 2048, 256 experts)
+    with more than 1024 pairs: the segmented plan feeding the weight-major
+    kernels (T = 1024, 24 pairs per expert) or the token-major kernels
+    (T = 8192). A token's output depends only on its own experts, so sampled
+    rows are checked against oracle.moe_layer run on just those rows with
+    their own routing (the experts they touch read back from the store in
+    the reference's layout); the whole call is also deterministic and its rows
+    equal the same tokens run alone through the decode-size kernels."""
     from home_seek_b200 import ops
     from home_seek_b200.expert_store import HBMExpertStore
     st = HBMExpertStore(1, 256, 4096, 2048, 2048, device="cuda", with_router=False)
@@ -225,10 +242,13 @@ def test_moe_large_t_full_shape_rows_match_token_mode(T):
     again = ops.moe_ffn(st.desc(0), st.dims, h, idx, w, use_shared=True)
     assert ops.check_status(torch.device("cuda")) == 0
     assert torch.equal(out, again)
-    rows = torch.tensor([0, 1, 17, 100, 256, 300, 511, T - 1], device="cuda") if T == 512 else \
-        torch.tensor([0, 1, 17, 1000, 2047, 2048, 3333, 4095], device="cuda")
-    alone = ops.moe_ffn(st.desc(0), st.dims, h[rows], idx[rows], w[rows], use_shared=True)
-    assert rel(out[rows], alone) <= MOE_TOL, rel(out[rows], alone)
+    rows = sorted({0, 1, 17, T // 3, T // 2, T // 2 + 1, T - 2, T - 1})
+    r = torch.tensor(rows, device="cuda")
+    load, sh = _store_reference_form(st)
+    ref = O.moe_layer(h[r].cpu(), idx[r].cpu(), w[r].cpu(), load, sh)
+    assert rel(out[r], ref) <= MOE_TOL, rel(out[r], ref)
+    alone = ops.moe_ffn(st.desc(0), st.dims, h[r], idx[r], w[r], use_shared=True)
+    assert rel(out[r], alone) <= MOE_TOL, rel(out[r], alone)
 
 
 @pytest.mark.parametrize("dup", ["last", "sum"])

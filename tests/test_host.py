@@ -63,3 +63,28 @@ def test_scale_atom_layout_roundtrip_and_formula():
     b = torch.tensor([[121, 120]], dtype=torch.uint8)
     ab = block_scales_to_atoms(b)
     assert ab.shape == (1, 2, 512) and (ab[0, 0] == 121).all() and (ab[0, 1] == 120).all()
+
+
+def test_fp4_and_fp8_block_forms_recovered_from_bf16_losslessly():
+    """layout.fp4_block_from_bf16 / fp8_block_from_bf16 invert the reference's
+    dequantisations (fused_moe.py:672-735, weight_loader.py:22-32) exactly,
+    and refuse bf16 weights that are not such values."""
+    import pytest
+    import torch
+    from home_seek_b200.layout import fp4_block_from_bf16, fp8_block_dequant, fp8_block_from_bf16
+    from oracle import fp4 as F
+    from oracle import inputs as I
+    w1, s1, *_ = I.expert_fp4(5, 512, 512)
+    bf = F.dequant_fp4(w1, s1)
+    p, s = fp4_block_from_bf16(bf)
+    assert torch.equal(F.dequant_fp4(p.numpy(), s.numpy()), bf)
+    with pytest.raises(TypeError):
+        fp4_block_from_bf16((bf.float() * 1.1).to(torch.bfloat16))
+    w13, s13, _, _ = I.shared_fp8(512, 512, seed=2)
+    d8 = torch.from_numpy(w13[0])
+    b8 = fp8_block_dequant(d8, torch.from_numpy(s13[0]))
+    assert torch.equal(b8, F.dequant_fp8_block(w13[0], s13[0]))
+    q, k = fp8_block_from_bf16(b8)
+    assert torch.equal(fp8_block_dequant(q, k), b8)
+    with pytest.raises(TypeError):
+        fp8_block_from_bf16((b8.float() * 1.01).to(torch.bfloat16))
