@@ -44,7 +44,17 @@ __device__ __forceinline__ void slice_of(int V, int rank, int& lo, int& hi) {
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
+__device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t w) {
+  return *reinterpret_cast<const __nv_bfloat162*>(&w);
+}
+
 // Block-wide arg-max of one row slice [lo, hi). Result valid in thread 0.
+// Each thread scans its 16-byte chunks in ascending index order and keeps
+// (value, first index). A chunk's eight values are first folded with the
+// packed NaN-propagating bf16 max (three instructions); only a chunk whose
+// maximum beats the running value (greater, or NaN over a number), and the
+// thread's first chunk, are scanned element by element, so equal values keep
+// the earlier index and the first NaN wins, as torch.argmax.
 __device__ void block_argmax(const __nv_bfloat16* __restrict__ row, int lo, int hi, float& bv, int& bi) {
   float v = -INFINITY;
   int ix = 0x7fffffff;
@@ -52,19 +62,24 @@ __device__ void block_argmax(const __nv_bfloat16* __restrict__ row, int lo, int 
   const int nvec = (hi - lo) / 8;
   const uint4* p = reinterpret_cast<const uint4*>(row + lo);
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-    const uint4 q = p[i];
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    const int base = lo + 8 * i;
+    const uint4 q = __ldcs(p + i);
+    const __nv_bfloat162 m2 =
+        __hmax2_nan(__hmax2_nan(as_bf162(q.x), as_bf162(q.y)), __hmax2_nan(as_bf162(q.z), as_bf162(q.w)));
+    const float cm = __bfloat162float(__hmax_nan(m2.x, m2.y));
+    if (cm > v || (isnan(cm) && !isnan(v)) || ix == 0x7fffffff) {  // (the first chunk: a row of -inf)
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      const int base = lo + 8 * i;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = bf16lo(w[j]), b = bf16hi(w[j]);
-      if (better(a, base + 2 * j, v, ix)) {
-        v = a;
-        ix = base + 2 * j;
-      }
-      if (better(b, base + 2 * j + 1, v, ix)) {
-        v = b;
-        ix = base + 2 * j + 1;
+      for (int j = 0; j < 4; ++j) {
+        const float a = bf16lo(w[j]), b = bf16hi(w[j]);
+        if (better(a, base + 2 * j, v, ix)) {
+          v = a;
+          ix = base + 2 * j;
+        }
+        if (better(b, base + 2 * j + 1, v, ix)) {
+          v = b;
+          ix = base + 2 * j + 1;
+        }
       }
     }
   }

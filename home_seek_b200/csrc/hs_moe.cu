@@ -72,6 +72,7 @@ constexpr int kSegMaxE = 256;           // segmented plan: experts per call at m
 constexpr int kSegTicket = 15;          // plan header word: the counting CTAs' ticket (left at 0)
 constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two independent MMA streams)
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
+constexpr int kTokDownPad = 256;        // token-mode down kernel: read-only slack after its last stage
 
 // Receive buffer of the peer-memory expert-parallel exchange: a 256-byte
 // header ([0] calls made, [1] combine ticket, [2] poisoned, u64) and two slots (calls
@@ -141,7 +142,12 @@ struct Plan {
   uint8_t* act8;          // [2][P_max][I_act] e4m3 hi / lo; token mode [2][(1 + C_max) * 8][I_act]
   float* out_part;        // [P_max][D]
   float* ctab_wb;         // token mode: [C_max][8] routing weight of (chunk, token), 0 if not routed
-  uint8_t* ctab_sb;       // token mode: [C_max][8] UE8M0 down-MMA B scale 127 - q of (chunk, token)
+  // token mode: the down MMA's B scale factors of the activation rows, as
+  // scale-atom images: [1 + C_max slots][I_act / 128 k-tiles][256 bytes];
+  // byte n * 16 + j is the UE8M0 scale of B row n (hi rows 0-7 = tokens, lo
+  // rows 8-15) over the k-tile's 32-column block j, i.e. lines 0-15 of a
+  // 512-byte atom (an N = 16 MMA never reads the rows above 15)
+  uint8_t* act_img;
 };
 
 struct Geometry {
@@ -152,7 +158,7 @@ struct Geometry {
   int64_t slot_floats;     // floats per partial slot (gate/up, the larger)
   int64_t act_rows;        // rows per activation plane
   size_t off_hdr, off_chunk, off_pair, off_sb, off_tok, off_tokpos, off_dcount, off_x8, off_act8, off_out,
-      off_ucount, off_part, off_ctab, off_seg, total;
+      off_ucount, off_part, off_ctab, off_img, off_seg, total;
 };
 
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -208,7 +214,9 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   g.off_part = o;
   o = align_up(o + 2 * static_cast<int64_t>(G) * g.slot_floats * sizeof(float), 256);
   g.off_ctab = o;
-  o = align_up(o + g.C_max * 8 * (sizeof(float) + 1), 256);
+  o = align_up(o + g.C_max * 8 * sizeof(float), 256);
+  g.off_img = o;
+  if (T <= kTokMax) o = align_up(o + (1 + g.C_max) * (g.I_act / kM) * 256, 256);
   // segmented plan: per-pair ranks, per-segment offsets, expert bases
   g.off_seg = o;
   o = align_up(o + (Pr + ((Pr + kSegPairs - 1) / kSegPairs) * kSegMaxE + kSegMaxE) * sizeof(int32_t), 256);
@@ -235,7 +243,7 @@ static Plan plan_views(const Geometry& g, void* ws) {
   p.act8 = b + g.off_act8;
   p.out_part = reinterpret_cast<float*>(b + g.off_out);
   p.ctab_wb = reinterpret_cast<float*>(b + g.off_ctab);
-  p.ctab_sb = reinterpret_cast<uint8_t*>(p.ctab_wb + g.C_max * 8);
+  p.act_img = b + g.off_img;
   return p;
 }
 
@@ -651,7 +659,6 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
     for (int i = tid; i < A.n_dcount; i += blockDim.x) P.dcount[i] = 0u;
     for (int64_t i = tid; i < A.n_ctab; i += blockDim.x) {
       P.ctab_wb[i] = 0.f;
-      P.ctab_sb[i] = 127;
     }
     if (A.po.expert_count)
       for (int x = tid; x < E; x += blockDim.x) A.po.expert_count[x] = 0;
@@ -729,7 +736,6 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs A, Plan P) 
           for (int m = 0; m < npairs; ++m) cb += (scnt[m] > 0) & (sval[m] < e);
           const int t = l / K;
           P.ctab_wb[cb * 8 + t] = swb[l];
-          P.ctab_sb[cb * 8 + t] = static_cast<uint8_t>(127 - sq[l]);
         }
       }
       if (A.sort_tok) {
@@ -1054,7 +1060,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ctab;
        i += static_cast<int64_t>(ncta) * kRouteThreads) {
     P.ctab_wb[i] = 0.f;
-    P.ctab_sb[i] = 127;
   }
   if (rank == 0) {
     if (tid < 8) emask[tid] = 0u;
@@ -1326,7 +1331,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     }
     const float wb = round_bf16(ws);
     P.ctab_wb[cb * 8 + t] = wb;
-    P.ctab_sb[cb * 8 + t] = static_cast<uint8_t>(127 - act_prescale(wb));
     P.chunk_expert[cb] = le;
     P.chunk_pair0[cb] = 0;
     P.chunk_np[cb] = 0;
@@ -1381,11 +1385,11 @@ struct UnitArgs {
   uint8_t* ep_recv[HS_EP_MAX_RANKS];
 };
 
-template <int NT, int BOXES>
+template <int NT, int BOXES, int NBSF = 1>
 struct SmemLayout {
   static constexpr int kA = 2 * kBoxBytes;             // two weight boxes per stage
   static constexpr int kB = BOXES * 2 * NT * 1024;     // hi and lo atoms per k-box
-  static constexpr int kSF = 2 * 512 + 512;            // two A scale atoms + the unit's B scale atom
+  static constexpr int kSF = 2 * 512 + NBSF * 512;     // two A scale atoms + NBSF B scale atoms
   static constexpr int kStage = kA + kB + kSF;
   static constexpr int kBarBytes = 256;
   static constexpr int kFit = (kSmemPerCta - kBarBytes) / kStage;
@@ -1771,36 +1775,39 @@ __device__ __forceinline__ void wait_ticket(const uint32_t* ctr, uint32_t target
   epi_bar();
 }
 
-// The chunk's per-token routing weights (bf16 values) and activation prescale
-// exponents, loaded before the unit's accumulator is ready.
-__device__ __forceinline__ void tok_weights(const UnitArgs& a, const UnitInfo& ui, float (&wbv)[8], int (&qv)[8]) {
+// The chunk's per-token routing weights (bf16 values), loaded before the
+// unit's accumulator is ready.
+__device__ __forceinline__ void tok_weights(const UnitArgs& a, const UnitInfo& ui, float (&wbv)[8]) {
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     wbv[r] = 0.f;
-    qv[r] = 0;
-    if (r < a.T) {
-      wbv[r] = ui.shared ? 1.f : __ldg(a.P.ctab_wb + ui.chunk * 8 + r);
-      qv[r] = ui.shared ? 0 : 127 - static_cast<int>(__ldg(a.P.ctab_sb + ui.chunk * 8 + r));
-    }
+    if (r < a.T) wbv[r] = ui.shared ? 1.f : __ldg(a.P.ctab_wb + ui.chunk * 8 + r);
   }
 }
 
 // Token-mode gate/up epilogue: the accumulator columns are the (up to 8)
 // tokens; every (chunk, token) activation row is written, as zeros where the
 // token is not routed to the chunk's expert (or t >= T), so the down phase can
-// run each unit over all experts with the same 8 token columns.
+// run each unit over all experts with the same 8 token columns. Each warp
+// holds 32 consecutive values of every row (one 32-column block of the down
+// MMA's K): the block is scaled by 2^q so its largest magnitude lies in
+// [128, 256), which makes the hi/lo e4m3 split of every bf16 value exact down
+// to 2^-10 of the block maximum, and 127 - q is written as the row's UE8M0 B
+// scale of that block (the scale-atom image the down phase copies).
 template <bool kFP8>
 __device__ __forceinline__ void gateup_finish_tok(const Desc& d, const UnitArgs& a, const UnitInfo& ui, int row,
-                                                  const float (&g)[8], const float (&u)[8], const float (&wbv)[8],
-                                                  const int (&qv)[8]) {
+                                                  const float (&g)[8], const float (&u)[8], const float (&wbv)[8]) {
   const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
   uint8_t* hi_plane = a.P.act8;
   uint8_t* lo_plane = a.P.act8 + a.act_rows * I_act;
   const int col = ui.tile * kM + row;
   const int64_t slot = kFP8 ? 0 : 1 + ui.chunk;
+  const int lane = row & 31, blk = row >> 5;
+  uint8_t* img = a.P.act_img + (slot * (I_act / kM) + ui.tile) * 256;
+  float av[8];
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
-    __nv_fp8_storage_t hb = 0, lb = 0;
+    av[r] = 0.f;
     if (wbv[r] != 0.f) {
       // reference roundings as in gateup_finish
       const float gf = round_bf16(g[r]);
@@ -1808,16 +1815,27 @@ __device__ __forceinline__ void gateup_finish_tok(const Desc& d, const UnitArgs&
       const float gc = gf > 10.f ? 10.f : gf;
       const float uc = uf > 10.f ? 10.f : (uf < -10.f ? -10.f : uf);
       const float sig = 1.f / (1.f + expf(-gc));
-      float av = round_bf16((gc * sig) * uc);
-      if (!kFP8) av = round_bf16(av * wbv[r]);
-      const float v = av * exp2i(qv[r]);
-      hb = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
-      const __half_raw hr = __nv_cvt_fp8_to_halfraw(hb, __NV_E4M3);
-      const float hf = __half2float(*reinterpret_cast<const __half*>(&hr));
-      lb = __nv_cvt_float_to_fp8(v - hf, __NV_SATFINITE, __NV_E4M3);
+      av[r] = round_bf16((gc * sig) * uc);
+      if (!kFP8) av[r] = round_bf16(av[r] * wbv[r]);
     }
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    // the block's largest magnitude (non-negative float bits order as values)
+    const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(av[r])));
+    const int q = row_prescale(__uint_as_float(mb));
+    const float v = av[r] * exp2i(q);
+    const __nv_fp8_storage_t hb = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw(hb, __NV_E4M3);
+    const float hf = __half2float(*reinterpret_cast<const __half*>(&hr));
+    const __nv_fp8_storage_t lb = __nv_cvt_float_to_fp8(v - hf, __NV_SATFINITE, __NV_E4M3);
     hi_plane[(slot * 8 + r) * I_act + col] = hb;
     lo_plane[(slot * 8 + r) * I_act + col] = lb;
+    if (lane == r) {
+      const uint8_t sf = static_cast<uint8_t>(127 - q);
+      img[r * 16 + blk] = sf;        // hi row r
+      img[(8 + r) * 16 + blk] = sf;  // lo row r
+    }
   }
 }
 
@@ -2120,8 +2138,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       const bool finish = !split || c == cf;
       float pre[NV];
       float wbv[8];
-      int qv[8];
-      if (kTok && finish) tok_weights(a, ui, wbv, qv);
+      if (kTok && finish) tok_weights(a, ui, wbv);
       if (split && finish) {
         wait_ticket(&a.ucount[u], static_cast<uint32_t>(nk - (k1 - k0)), etid, a.status);
         peer_sum<NV>(sc, cf + 1, cl, a.part, kSlot, row, pre);
@@ -2177,9 +2194,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       if (finish) {
         if constexpr (kTok) {
           if (ui.shared)
-            gateup_finish_tok<true>(d, a, ui, row, g, v, wbv, qv);
+            gateup_finish_tok<true>(d, a, ui, row, g, v, wbv);
           else
-            gateup_finish_tok<false>(d, a, ui, row, g, v, wbv, qv);
+            gateup_finish_tok<false>(d, a, ui, row, g, v, wbv);
         } else if (!kDown) {
           if (ui.shared)
             gateup_finish<NT, true>(d, a, ui, row, g, v);
@@ -2304,11 +2321,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   static_assert(sizeof(Bars) <= L::kBarBytes, "barrier block");
   constexpr int N = 16;
   // TMEM (256 columns): accumulator buffers at 0 and 96 (routed at +0, shared
-  // at +48), A scales at 192 + 8*stage, B scales at 224 + 4*stage
+  // at +48), A scales at 192 + 8*stage, B scales at 224 + 8*stage (one atom
+  // per 128-column k-tile of the stage, at +0 and +4)
   constexpr uint32_t kAcc = 96;
   constexpr uint32_t kAccSh = 48;
   constexpr uint32_t kSfa = 192;
   constexpr uint32_t kSfb = 224;
+  static_assert(kSfb + 8 * S_ <= 256, "TMEM columns");
+  // The stage's scale area holds the two A atoms and the two B images (256
+  // bytes each, at +1024 and +1280); the copy of image 1 reads a whole atom
+  // (512 bytes, its lines 16-31 unused), so 256 bytes of padding follow the
+  // last stage before the barrier block.
+  static_assert(L::kSF == 1536, "scale area");
   constexpr int kSlot = 2 * kM * 8;  // routed and shared sums of 8 tokens
   extern __shared__ uint8_t smem_raw[];  // 1024-aligned at offset 0 (checked below)
   if (smem_u32(smem_raw) & 1023u) {
@@ -2317,7 +2341,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     return;
   }
   uint8_t* base = smem_raw;
-  Bars* bars = reinterpret_cast<Bars*>(base + S_ * L::kStage);
+  Bars* bars = reinterpret_cast<Bars*>(base + S_ * L::kStage + kTokDownPad);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = d.D;
   const int c = blockIdx.x;
@@ -2371,31 +2395,27 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   }
   const int64_t npre = min64(static_cast<int64_t>(S_), s_end - s_begin);
 
-  // producer state (warp 4): chunk table in registers, lane j keeps chunks j,
-  // j+32, j+64, j+96 (expert id and the 8 per-token B-scale bytes as two words)
+  // producer state (warp 4): chunk table in registers, lane j keeps the
+  // expert ids of chunks j, j+32, j+64, j+96
   static_assert(kTokChunks <= 4 * 32, "token-mode chunk table");
   uint64_t pol = 0;
   // (scalars, not arrays: the lambdas below capture them by reference)
   int ex0 = 0, ex1 = 0, ex2 = 0, ex3 = 0;
-  uint2 sb0 = make_uint2(0x7f7f7f7fu, 0x7f7f7f7fu), sb1 = sb0, sb2 = sb0, sb3 = sb0;
   if (warp == 4) {
     pol = l2_evict_first_policy();
-    auto load = [&](int cc, int& e, uint2& sb) {
-      if (cc < sc.C) {
-        e = __ldcg(a.P.chunk_expert + cc);
-        sb = __ldcg(reinterpret_cast<const uint2*>(a.P.ctab_sb + cc * 8));
-      }
+    auto load = [&](int cc, int& e) {
+      if (cc < sc.C) e = __ldcg(a.P.chunk_expert + cc);
     };
-    load(lane, ex0, sb0);
-    load(lane + 32, ex1, sb1);
-    load(lane + 64, ex2, sb2);
-    load(lane + 96, ex3, sb3);
+    load(lane, ex0);
+    load(lane + 32, ex1);
+    load(lane + 64, ex2);
+    load(lane + 96, ex3);
   }
-  // step s -> (tile, shared?, chunk, k within the expert, expert, B-scale words)
+  const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
+  // step s -> (tile, shared?, chunk, k within the expert, expert)
   struct Step {
     int tile, ch, kk, e;
     bool shared;
-    uint32_t w0, w1;
   };
   auto decode = [&](int64_t s) {
     Step r;
@@ -2408,27 +2428,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     r.kk = r.shared ? k : kr - r.ch * sc.nrt;
     const int grp = r.ch >> 5;
     const int e_sel = grp == 0 ? ex0 : grp == 1 ? ex1 : grp == 2 ? ex2 : ex3;
-    const uint2 sb = grp == 0 ? sb0 : grp == 1 ? sb1 : grp == 2 ? sb2 : sb3;
     r.e = __shfl_sync(0xffffffffu, e_sel, r.ch & 31);
-    r.w0 = __shfl_sync(0xffffffffu, sb.x, r.ch & 31);
-    r.w1 = __shfl_sync(0xffffffffu, sb.y, r.ch & 31);
     return r;
-  };
-  // whole warp: this step's B scale atom; word (m0, m1) = scale of B row
-  // n = m0 + 32*m1; rows 0..7 are the tokens' hi rows, 8..15 their lo rows
-  auto write_atom = [&](uint8_t* SF, const Step& q) {
-    for (int wi = lane; wi < 128; wi += 32) {
-      const int m0 = wi >> 2, m1 = wi & 3;
-      const int n = m0 + 32 * m1;
-      uint32_t b = 127u;
-      if (n < N && !q.shared) {
-        const int t = n & 7;
-        b = ((t < 4 ? q.w0 : q.w1) >> (8 * (t & 3))) & 0xffu;
-      }
-      *reinterpret_cast<uint32_t*>(SF + 1024 + m0 * 16 + m1 * 4) = b * 0x01010101u;
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncwarp();
   };
   // lane 0: weights and their scale atoms (independent of the gate/up phase)
   auto issue_weights = [&](int st, const Step& q) {
@@ -2446,15 +2447,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     tma_load_2d_hint(S, q.shared ? &d.tm_sw2 : &d.tm_w2, &bars->full[st], 0, static_cast<int>(ya), pol);
     bulk_load_hint(SF, sfp, 1024, &bars->full[st], pol);
   };
-  // lane 0: the activation rows (written by the gate/up phase)
+  // lane 0: the activation rows and their block scales, lines 0-15 of the
+  // stage's B scale atom (both written by the gate/up phase)
   auto issue_act = [&](int st, const Step& q) {
     uint8_t* Bs = base + st * L::kStage + L::kA;
-    const int brow = (q.shared ? 0 : 1 + q.ch) * 8;
+    const int slot = q.shared ? 0 : 1 + q.ch;
     for (int b = 0; b < 2; ++b)
-      tma_load_3d(Bs + b * 2048, &cm.tm_act8, &bars->full[st], q.kk * 256 + b * 128, brow, 0);
+      tma_load_3d(Bs + b * 2048, &cm.tm_act8, &bars->full[st], q.kk * 256 + b * 128, slot * 8, 0);
+    const uint8_t* img = a.P.act_img + (static_cast<int64_t>(slot) * (I_act / kM) + 2 * q.kk) * 256;
+    bulk_load(Bs + L::kB + 1024, img, 512, &bars->full[st]);  // both k-tiles' images (adjacent)
   };
   auto tx_of = [&](const Step& q) {
-    return static_cast<uint32_t>((q.shared ? 2 * kBoxBytes : kBoxBytes) + L::kB + 1024);
+    return static_cast<uint32_t>((q.shared ? 2 * kBoxBytes : kBoxBytes) + L::kB + 1024 + 512);
   };
 
   float res_pre = 0.f;  // cluster epilogue: the preloaded residual element
@@ -2463,7 +2467,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     for (int64_t step = 0; step < npre; ++step) {  // stages are free: no empty waits yet
       const Step q = decode(s_begin + step);
       const int st = static_cast<int>(step);
-      write_atom(base + st * L::kStage + L::kA + L::kB, q);
       if (lane == 0) {
         mbar_expect_tx(&bars->full[st], tx_of(q));  // bytes now, the arrival after the activations
         issue_weights(st, q);
@@ -2496,7 +2499,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
           break;
         }
       }
-      write_atom(base + st * L::kStage + L::kA + L::kB, q);
       if (lane == 0) {
         mbar_arrive_expect_tx(&bars->full[st], tx_of(q));
         issue_weights(st, q);
@@ -2535,8 +2537,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
           uint8_t* S = base + st * L::kStage;
           const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
           const uint32_t sfa0 = tmem + kSfa + st * 8;
-          const uint32_t sfb = tmem + kSfb + st * 4;
+          const uint32_t sfb = tmem + kSfb + st * 8;
           tc5::cp_sf_32x128b(sfb, tc5::sdesc_sf(sSF + 1024));
+          tc5::cp_sf_32x128b(sfb + 4, tc5::sdesc_sf(sSF + 1280));
           tc5::cp_sf_32x128b(sfa0, tc5::sdesc_sf(sSF));
           tc5::cp_sf_32x128b(sfa0 + 4, tc5::sdesc_sf(sSF + 512));
           const bool shared = k < sc.nsh;
@@ -2553,7 +2556,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
               const uint32_t accum = (first && i == 0 && j == 0) ? 0u : 1u;
               tc5::mma_mxf8f6f4(dcol, ad + 2 * j, bd + 2 * j, id, accum,
                                 (sfa0 + 4 * i) | (static_cast<uint32_t>(j) << 30),
-                                sfb | (static_cast<uint32_t>(j) << 30));
+                                (sfb + 4 * i) | (static_cast<uint32_t>(j) << 30));
             }
           }
           tc5::commit(&bars->empty[st]);
@@ -2932,7 +2935,8 @@ static int tok_down_cluster(int tiles, int bytes) {
 }
 
 static int launch_tok_down(const Desc& d, const CallMaps& cm, UnitArgs a, cudaStream_t st, int* grid_out = nullptr) {
-  constexpr int bytes = SmemLayout<1, 2>::kBytes;
+  constexpr int bytes = SmemLayout<1, 2>::kBytes + kTokDownPad;
+  static_assert(bytes <= kSmemPerCta, "down kernel shared memory");
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   HS_CUDA_CHECK(cudaGetDevice(&dev));

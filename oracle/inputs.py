@@ -135,7 +135,15 @@ def mtp_model(shape: MtpShape = MTP_SMALL, seed: int = 50) -> dict:
     """A small seeded model for the MTP token-stream parity tests, in the
     reference's formats (uint8 FP4/FP8 bytes, bf16 dense weights).
 
-    Built so that drafts are accepted often but not always: the MTP layer is a
+    Built so that drafts are accepted often but not always, and so that every
+    discrete decision of the loop other than the argmaxes has a wide margin:
+    the router layers' biases lift a fixed set of top_k experts by +4 and
+    lower the rest by 4 (logits from the gate are ~N(0, 0.45^2)), so the
+    top-k selection is the same for every token with a gap of ~190 bf16 ulps
+    between the k-th and (k+1)-th score, while the routing weights still
+    follow each token's scores; a random router has several selections per
+    run within one ulp of a tie, which any other summation order may flip.
+    The hash layers give each token its own expert set. The MTP layer is a
     copy of the last main layer (same experts, router and norm weight),
     e_proj = I and h_proj = 2^-4 I (both exact in bf16 on any GEMM, so the
     projections add no rounding of their own), enorm/hnorm weights 1 and the
@@ -158,9 +166,12 @@ def mtp_model(shape: MtpShape = MTP_SMALL, seed: int = 50) -> dict:
     shared = [shared_fp8(s.D, s.I_sh, seed=seed + 10 + l) for l in range(s.L)]
     gates, biases = [], []
     for l in range(s.L):
-        gw, bw = router_weights(s.E, s.D, seed=seed + 20 + l)
+        gw, _ = router_weights(s.E, s.D, seed=seed + 20 + l)
+        gb = torch.Generator().manual_seed(seed + 40 + l)
+        bw = torch.full((s.E,), -4.0)
+        bw[torch.randperm(s.E, generator=gb)[: s.K]] = 4.0
         gates.append(gw)
-        biases.append(bw)
+        biases.append(bw.to(torch.bfloat16))
     gates.append(gates[s.L - 1])
     biases.append(biases[s.L - 1])
     tid = {}

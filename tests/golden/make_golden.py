@@ -288,7 +288,7 @@ def _mtp_engine(shape, model):
     return eng
 
 
-def gen_mtp(out, iterations: int = 16, first_token: int = 17):
+def gen_mtp(out, iterations: int = 16, first_token: int = 100):
     """The greedy MTP decode loop of generate() (engine.py:2809-2922, t = 0,
     mtp_num_draft = M, no stop token) on the small seeded model: main T = 1
     step, _mtp_generate_draft, _mtp_verify_batched, and the loop's

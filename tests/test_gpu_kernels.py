@@ -369,17 +369,20 @@ def test_greedy_accept_config4():
 def test_greedy_nan_and_ties():
     from home_seek_b200 import ops
     V = 1024
-    lg = torch.zeros(2, 2, V)
+    lg = torch.zeros(3, 2, V)
     lg[0, 0, 500] = 5.0
     lg[0, 0, 700] = 5.0  # tie -> first index 500
     lg[0, 1, 3] = float("nan")
     lg[0, 1, 900] = float("nan")  # NaN is maximal, first NaN wins
     lg[1, 0, V - 1] = 1.0
+    lg[2, 0] = float("-inf")      # a row of -inf: index 0
+    lg[2, 1, :7] = -0.0           # -0 equals +0: index 0
     lg = lg.to(torch.bfloat16)
-    ids = torch.tensor([[500], [0]])
+    ids = torch.tensor([[500], [0], [5]])
     n, nxt, am = ops.accept_greedy(lg.cuda(), ids.cuda(), want_argmax=True)
-    assert am.cpu().tolist() == [[500, 3], [V - 1, 0]]
-    assert n.cpu().tolist() == [1, 0] and nxt.cpu().tolist() == [3, V - 1]
+    assert am.cpu().tolist() == [[500, 3], [V - 1, 0], [0, 0]]
+    assert am.cpu().tolist() == lg.float().argmax(dim=-1).tolist()
+    assert n.cpu().tolist() == [1, 0, 0] and nxt.cpu().tolist() == [3, V - 1, 0]
 
 
 def test_rejection_config4():
