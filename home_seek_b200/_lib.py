@@ -117,6 +117,8 @@ SIGNATURES = {
     "hs_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]),
     "hs_moe_combine_add_rms_norm": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_float, c_int64, c_int64,
                                             c_void_p, c_void_p, c_void_p]),
+    "hs_verify_state_snapshot": (c_int, [c_void_p, c_int64, c_int64, c_void_p]),
+    "hs_verify_state_commit": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int32, c_void_p]),
     "hs_fill_bytes": (c_int, [c_void_p, c_int64, c_uint64, c_int32, c_int32, c_void_p]),
 }
 

@@ -17,7 +17,7 @@ PKG_DIR = Path(__file__).resolve().parent
 CSRC = PKG_DIR / "csrc"
 INCLUDE = PKG_DIR.parent / "include"
 LIB_PATH = PKG_DIR / "libhs_ext.so"
-SOURCES = ["hs_util.cu", "hs_router.cu", "hs_moe.cu", "hs_accept.cu", "hs_norm.cu", "hs_head.cu"]
+SOURCES = ["hs_util.cu", "hs_router.cu", "hs_moe.cu", "hs_accept.cu", "hs_norm.cu", "hs_head.cu", "hs_state.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -48,42 +48,55 @@ __device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t w) {
   return *reinterpret_cast<const __nv_bfloat162*>(&w);
 }
 
-// Block-wide arg-max of one row slice [lo, hi). Result valid in thread 0.
-// Each thread scans its 16-byte chunks in ascending index order and keeps
-// (value, first index). A chunk's eight values are first folded with the
-// packed NaN-propagating bf16 max (three instructions); only a chunk whose
-// maximum beats the running value (greater, or NaN over a number), and the
-// thread's first chunk, are scanned element by element, so equal values keep
-// the earlier index and the first NaN wins, as torch.argmax.
-__device__ void block_argmax(const __nv_bfloat16* __restrict__ row, int lo, int hi, float& bv, int& bi) {
-  float v = -INFINITY;
-  int ix = 0x7fffffff;
-  // 8 bf16 per 16-byte load; lo is a multiple of 8 and rows are 16-byte aligned
-  const int nvec = (hi - lo) / 8;
-  const uint4* p = reinterpret_cast<const uint4*>(row + lo);
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-    const uint4 q = __ldcs(p + i);
-    const __nv_bfloat162 m2 =
-        __hmax2_nan(__hmax2_nan(as_bf162(q.x), as_bf162(q.y)), __hmax2_nan(as_bf162(q.z), as_bf162(q.w)));
-    const float cm = __bfloat162float(__hmax_nan(m2.x, m2.y));
-    if (cm > v || (isnan(cm) && !isnan(v)) || ix == 0x7fffffff) {  // (the first chunk: a row of -inf)
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-      const int base = lo + 8 * i;
+constexpr int kBatch = 4;  // 16-byte chunks each thread has in flight per row
+
+// One thread's chunk u of a batch: chunk index i0 + u * blockDim.x.
+__device__ __forceinline__ void argmax_chunk(const uint4& q, int base, float& v, int& ix) {
+  const __nv_bfloat162 m2 =
+      __hmax2_nan(__hmax2_nan(as_bf162(q.x), as_bf162(q.y)), __hmax2_nan(as_bf162(q.z), as_bf162(q.w)));
+  const float cm = __bfloat162float(__hmax_nan(m2.x, m2.y));
+  if (cm > v || (isnan(cm) && !isnan(v)) || ix == 0x7fffffff) {  // (the first chunk: a row of -inf)
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float a = bf16lo(w[j]), b = bf16hi(w[j]);
-        if (better(a, base + 2 * j, v, ix)) {
-          v = a;
-          ix = base + 2 * j;
-        }
-        if (better(b, base + 2 * j + 1, v, ix)) {
-          v = b;
-          ix = base + 2 * j + 1;
-        }
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16lo(w[j]), b = bf16hi(w[j]);
+      if (better(a, base + 2 * j, v, ix)) {
+        v = a;
+        ix = base + 2 * j;
+      }
+      if (better(b, base + 2 * j + 1, v, ix)) {
+        v = b;
+        ix = base + 2 * j + 1;
       }
     }
   }
-  for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += blockDim.x) {
+}
+
+// Warp-level arg-max of one row slice [lo, hi): every lane gets the warp's
+// (value, first index). Each thread scans its 16-byte chunks in ascending
+// index order, kBatch loads in flight at a time, and keeps (value, first
+// index); a chunk's eight values are first folded with the packed
+// NaN-propagating bf16 max, and only a chunk whose maximum beats the running
+// value (greater, or NaN over a number), and the thread's first chunk, are
+// scanned element by element, so equal values keep the earlier index and the
+// first NaN wins, as torch.argmax.
+__device__ void warp_argmax(const __nv_bfloat16* __restrict__ row, int lo, int hi, float& v, int& ix) {
+  v = -INFINITY;
+  ix = 0x7fffffff;
+  // 8 bf16 per 16-byte load; lo is a multiple of 8 and rows are 16-byte aligned
+  const int nvec = (hi - lo) / 8;
+  const uint4* p = reinterpret_cast<const uint4*>(row + lo);
+  const int bd = static_cast<int>(blockDim.x);
+  for (int i0 = threadIdx.x; i0 < nvec; i0 += kBatch * bd) {
+    uint4 q[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (i0 + u * bd < nvec) q[u] = __ldcs(p + i0 + u * bd);
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (i0 + u * bd < nvec) argmax_chunk(q[u], lo + 8 * (i0 + u * bd), v, ix);
+  }
+  for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += bd) {
     const float a = __bfloat162float(row[k]);
     if (better(a, k, v, ix)) {
       v = a;
@@ -98,24 +111,6 @@ __device__ void block_argmax(const __nv_bfloat16* __restrict__ row, int lo, int 
       ix = i2;
     }
   }
-  __shared__ float sv[kThreads / 32];
-  __shared__ int si[kThreads / 32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) {
-    sv[warp] = v;
-    si[warp] = ix;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w2 = 1; w2 < static_cast<int>(blockDim.x / 32); ++w2)
-      if (better(sv[w2], si[w2], v, ix)) {
-        v = sv[w2];
-        ix = si[w2];
-      }
-    bv = v;
-    bi = ix;
-  }
 }
 
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
@@ -126,16 +121,33 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   const int b = blockIdx.x / kCluster;
   __shared__ float pv[kMaxRows];
   __shared__ int pi[kMaxRows];
+  __shared__ float wv[kMaxRows][kThreads / 32];
+  __shared__ int wi[kMaxRows][kThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int lo, hi;
   slice_of(V, rank, lo, hi);
+  // every row's warp results first, then one barrier and the CTA reduction
   for (int i = 0; i < T; ++i) {
     float v;
     int ix;
-    block_argmax(logits + (static_cast<int64_t>(b) * T + i) * V, lo, hi, v, ix);
-    if (threadIdx.x == 0) {
-      pv[i] = v;
-      pi[i] = ix;
+    warp_argmax(logits + (static_cast<int64_t>(b) * T + i) * V, lo, hi, v, ix);
+    if (lane == 0) {
+      wv[i][warp] = v;
+      wi[i][warp] = ix;
     }
+  }
+  __syncthreads();
+  if (threadIdx.x < T) {
+    const int i = threadIdx.x;
+    float v = wv[i][0];
+    int ix = wi[i][0];
+    for (int w2 = 1; w2 < kThreads / 32; ++w2)
+      if (better(wv[i][w2], wi[i][w2], v, ix)) {
+        v = wv[i][w2];
+        ix = wi[i][w2];
+      }
+    pv[i] = v;
+    pi[i] = ix;
   }
   cluster.sync();
   if (rank == 0 && threadIdx.x == 0) {
@@ -176,44 +188,59 @@ __device__ __forceinline__ MS ms_combine(MS a, MS b) {
   return MS{m, a.s * expf(a.m - m) + b.s * expf(b.m - m)};
 }
 
-// (max, sum exp(z - max)) of z = x / t over a slice; result valid in thread 0.
-// Each thread keeps a running max and rescales its sum only when the max
-// grows, so every element costs one expf.
-__device__ __forceinline__ void ms_push(MS& a, float z) {
-  if (z == -INFINITY) return;  // exp(-inf) contributes nothing
-  if (z > a.m) {
-    a.s = (a.m == -INFINITY ? 0.f : a.s * expf(a.m - z)) + 1.f;
-    a.m = z;
-  } else {
-    a.s += expf(z - a.m);
-  }
-}
-
-__device__ MS block_ms(const __nv_bfloat16* __restrict__ row, int lo, int hi, float t) {
-  MS acc{-INFINITY, 0.f};
+// Warp-level (max, sum exp(z - max)) of z = x / t over a row slice; every
+// lane gets the warp's pair. Two passes over the thread's chunks (kBatch loads
+// in flight): the largest logit (packed bf16 max, NaN propagating), whose
+// z = x / t is the thread's maximum since dividing by t > 0 keeps the order,
+// then the branch-free sum of exp(x / t - z_max).
+__device__ MS warp_ms(const __nv_bfloat16* __restrict__ row, int lo, int hi, float t) {
   const int nvec = (hi - lo) / 8;
   const uint4* p = reinterpret_cast<const uint4*>(row + lo);
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-    const uint4 q = p[i];
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  const int bd = static_cast<int>(blockDim.x);
+  __nv_bfloat162 mx2 = __float2bfloat162_rn(-INFINITY);
+  for (int i0 = threadIdx.x; i0 < nvec; i0 += kBatch * bd) {
+    uint4 q[kBatch];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      ms_push(acc, bf16lo(w[j]) / t);
-      ms_push(acc, bf16hi(w[j]) / t);
-    }
+    for (int u = 0; u < kBatch; ++u)
+      if (i0 + u * bd < nvec) q[u] = __ldcg(p + i0 + u * bd);
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (i0 + u * bd < nvec)
+        mx2 = __hmax2_nan(mx2, __hmax2_nan(__hmax2_nan(as_bf162(q[u].x), as_bf162(q[u].y)),
+                                           __hmax2_nan(as_bf162(q[u].z), as_bf162(q[u].w))));
   }
-  for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += blockDim.x) ms_push(acc, __bfloat162float(row[k]) / t);
+  float mx = __bfloat162float(__hmax_nan(mx2.x, mx2.y));
+  for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += bd) {
+    const float x = __bfloat162float(row[k]);
+    mx = isnan(x) || x > mx ? x : mx;
+  }
+  MS acc{-INFINITY, 0.f};
+  if (mx != -INFINITY) {
+    const float zm = mx / t;
+    float sum = 0.f;
+    for (int i0 = threadIdx.x; i0 < nvec; i0 += kBatch * bd) {
+      uint4 q[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (i0 + u * bd < nvec) q[u] = __ldcg(p + i0 + u * bd);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (i0 + u * bd < nvec) {
+          const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            sum += expf(bf16lo(w[j]) / t - zm);
+            sum += expf(bf16hi(w[j]) / t - zm);
+          }
+        }
+    }
+    for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += bd) sum += expf(__bfloat162float(row[k]) / t - zm);
+    acc = MS{zm, sum};
+  }
   for (int o = 16; o > 0; o >>= 1) {
     MS other{__shfl_xor_sync(0xffffffffu, acc.m, o), __shfl_xor_sync(0xffffffffu, acc.s, o)};
     acc = ms_combine(acc, other);
   }
-  __shared__ MS sm[kThreads / 32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) sm[warp] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0)
-    for (int w = 1; w < static_cast<int>(blockDim.x / 32); ++w) acc = ms_combine(acc, sm[w]);
   return acc;
 }
 
@@ -224,12 +251,33 @@ struct Bcast {
   float mt, st, md, sd;
 };
 
-__device__ __forceinline__ float resid(const __nv_bfloat16* tr, const __nv_bfloat16* dr, int k, float t,
-                                       const Bcast& bc) {
-  const float p = expf(__bfloat162float(tr[k]) / t - bc.mt) / bc.st;
+__device__ __forceinline__ float resid_of(float xt, float xd, float t, const Bcast& bc) {
+  const float p = expf(xt / t - bc.mt) / bc.st;
   if (!bc.residual) return p;
-  const float q = expf(__bfloat162float(dr[k]) / t - bc.md) / bc.sd;
+  const float q = expf(xd / t - bc.md) / bc.sd;
   return fmaxf(0.f, p - q);
+}
+
+// The sampled distribution at k .. k + 7 (values past `end` are 0): p, or
+// max(0, p - q) at a rejection. k is a multiple of 8, so a whole group is
+// one 16-byte load of each row.
+__device__ __forceinline__ void resid8(const __nv_bfloat16* tr, const __nv_bfloat16* dr, int k, int end, float t,
+                                       const Bcast& bc, float (&rv)[8]) {
+  if (k + 8 <= end) {
+    const uint4 a = __ldcg(reinterpret_cast<const uint4*>(tr + k));
+    const uint4 b = bc.residual ? __ldcg(reinterpret_cast<const uint4*>(dr + k)) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      rv[2 * j] = resid_of(bf16lo(wa[j]), bf16lo(wb[j]), t, bc);
+      rv[2 * j + 1] = resid_of(bf16hi(wa[j]), bf16hi(wb[j]), t, bc);
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    rv[j] = k + j < end ? resid_of(__bfloat162float(tr[k + j]), bc.residual ? __bfloat162float(dr[k + j]) : 0.f, t, bc)
+                        : 0.f;
 }
 
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
@@ -251,13 +299,24 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   const __nv_bfloat16* trow0 = target + static_cast<int64_t>(b) * (M + 1) * V;
   const __nv_bfloat16* drow0 = draft + static_cast<int64_t>(b) * draft_rows * V;
 
-  for (int i = 0; i <= M; ++i) {
-    const MS r = block_ms(trow0 + static_cast<int64_t>(i) * V, lo, hi, t);
-    if (threadIdx.x == 0) tms[i] = r;
+  // every row's warp pairs first (target rows 0..M, then draft rows), one
+  // barrier, then thread i combines row i over the warps in warp order
+  __shared__ MS wms[2 * kMaxRows][kThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = 0; i <= 2 * M; ++i) {
+    const __nv_bfloat16* row = i <= M ? trow0 + static_cast<int64_t>(i) * V : drow0 + static_cast<int64_t>(i - M - 1) * V;
+    const MS r = warp_ms(row, lo, hi, t);
+    if (lane == 0) wms[i][warp] = r;
   }
-  for (int i = 0; i < M; ++i) {
-    const MS r = block_ms(drow0 + static_cast<int64_t>(i) * V, lo, hi, t);
-    if (threadIdx.x == 0) dms[i] = r;
+  __syncthreads();
+  if (threadIdx.x <= 2 * M) {
+    const int i = threadIdx.x;
+    MS acc = wms[i][0];
+    for (int w = 1; w < kThreads / 32; ++w) acc = ms_combine(acc, wms[i][w]);
+    if (i <= M)
+      tms[i] = acc;
+    else
+      dms[i - M - 1] = acc;
   }
   if (threadIdx.x == 0) {
     for (int i = 0; i < M; ++i) {
@@ -321,15 +380,21 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   // Thread i owns one contiguous chunk of the slice; chunk sums are combined
   // by thread 0 in thread order, so the CTA total and the exclusive prefixes
   // come from the same sequence of additions.
+  // (chunks are a multiple of 8 values, so each starts 16-byte aligned and is
+  // read with vector loads)
   const int len = hi - lo;
-  const int chunk = (len + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+  const int chunk = (len + 8 * static_cast<int>(blockDim.x) - 1) / (8 * static_cast<int>(blockDim.x)) * 8;
   const int k0 = min(hi, lo + static_cast<int>(threadIdx.x) * chunk), k1 = min(hi, k0 + chunk);
   float ts = 0.f;
   int tl = -1;
-  for (int k = k0; k < k1; ++k) {
-    const float r = resid(tr, dr, k, t, B);
-    ts += r;
-    if (r > 0.f) tl = k;
+  for (int k = k0; k < k1; k += 8) {
+    float rv[8];
+    resid8(tr, dr, k, k1, t, B, rv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      ts += rv[j];
+      if (rv[j] > 0.f) tl = k + j;
+    }
   }
   tsum[threadIdx.x] = ts;
   for (int o = 16; o > 0; o >>= 1) tl = max(tl, __shfl_xor_sync(0xffffffffu, tl, o));
@@ -362,12 +427,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   const float tau = u[static_cast<int64_t>(b) * (M + 1) + M] * tot;
   if (tau >= pre && tau < pre + csum) {
     float x = pre + tsum[threadIdx.x];
-    for (int k = k0; k < k1; ++k) {
-      const float r = resid(tr, dr, k, t, B);
-      x += r;
-      if (r > 0.f && x > tau) {
-        atomicMin(&found, k);
-        break;
+    bool done = false;
+    for (int k = k0; k < k1 && !done; k += 8) {
+      float rv[8];
+      resid8(tr, dr, k, k1, t, B, rv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        x += rv[j];
+        if (!done && rv[j] > 0.f && x > tau) {
+          atomicMin(&found, k + j);
+          done = true;
+        }
       }
     }
   }

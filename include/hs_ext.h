@@ -419,6 +419,40 @@ int hs_moe_combine_add_rms_norm(const float* routed_f32,
                                 void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Verify-state snapshot / restore on the device.                             */
+/* Replaces the state handling of _mtp_verify_batched                         */
+/* (inference_engine/engine.py:2443-2459, 2500-2538): the reference clones    */
+/* every layer's KV latent cache, compressed KV and compressor state before   */
+/* the fused verify forward and, unless every position was accepted, trims    */
+/* the KV caches to old length + n_accept and puts the rest back. Here each   */
+/* state is a region of a table in DEVICE memory (built once by the caller):  */
+/*   append region (length != NULL): a device entry count. Snapshot records   */
+/*     it in saved_length; commit sets *length = saved_length + n_accept when */
+/*     keep_accepted (KV caches, the position), else saved_length.            */
+/*   copy region (length == NULL): `bytes` at `live` (16-byte aligned, bytes  */
+/*     a multiple of 16) saved into `shadow` (same size) by the snapshot and  */
+/*     copied back by the commit (compressor states, compressed KV).          */
+/* The commit does nothing when *n_accept >= t_total (all accepted), as the   */
+/* reference. n_accept is device memory (e.g. hs_lm_head_argmax's output):    */
+/* no host synchronisation. max_bytes = the largest copy region's size (it    */
+/* sets the grid). One launch per call over all regions; n <= 65535.         */
+/* ------------------------------------------------------------------------ */
+typedef struct hs_state_region {
+  void* live;
+  void* shadow;
+  int64_t bytes;
+  int64_t* length;
+  int64_t saved_length;
+  int32_t keep_accepted;
+  int32_t reserved;
+} hs_state_region;
+int hs_verify_state_snapshot(hs_state_region* regions, int64_t n,
+                             int64_t max_bytes, void* stream);
+int hs_verify_state_commit(hs_state_region* regions, int64_t n,
+                           int64_t max_bytes, const int32_t* n_accept,
+                           int32_t t_total, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Synthetic weight fill (device-side, counter-based hash; no allocation).    */
 /* Fills n bytes at dst with lo + (hash(seed, i) % (hi - lo + 1)). Used to    */
 /* build random-init expert stores of the full model shape in seconds.        */

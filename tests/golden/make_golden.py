@@ -384,6 +384,69 @@ def _verify_with_logits(eng, draft_ids, main_pred, rows):
     return n, bonus
 
 
+def gen_verify_state(out):
+    """The state handling of the reference's _mtp_verify_batched (engine.py:
+    2443-2459, 2500-2538) on seeded layer states: a mocked forward appends KV
+    rows, a compressed row and rewrites the compressor (oracle/verify_state.py
+    forward_mutation), its logits rows are chosen so n_accept is 0, 1 or 2 of
+    T = 3 positions; the states and position after the call are recorded."""
+    from types import SimpleNamespace
+
+    from home_seek.inference_engine import HomeSeekInferenceEngine
+    from home_seek.inference_engine.layer_state import LayerState
+    from oracle import verify_state as VS
+    V = 64
+    for case, n_want in enumerate((0, 1, 2)):
+        before = VS.scenario_states(seed=7 + case)
+        eng = HomeSeekInferenceEngine.__new__(HomeSeekInferenceEngine)
+        eng._log = lambda m: None
+        eng.config = MagicMock()
+        eng.config.num_hidden_layers = len(before)
+        eng.config.hc_mult = 1
+        eng.config.rms_norm_eps = 1e-6
+        eng.layer_states, eng._compressors = {}, {}
+        for l, st in before.items():
+            ls = LayerState(device="cpu")
+            ls.kv_latent_cache = st["kv"].clone()
+            ls.compressed_kv_data = st["cdata"].clone()
+            ls.compressed_kv_idx = st["cidx"].clone()
+            eng.layer_states[l] = ls
+            acc, kvs, scs = st["comp"]
+            eng._compressors[l] = SimpleNamespace(accumulated=acc, kv_state=kvs.clone(), score_state=scs.clone())
+        eng._global_pos = 40
+        eng.embed = torch.zeros(V, V, dtype=torch.bfloat16)
+        eng.lm_head = torch.eye(V, dtype=torch.bfloat16)
+        eng.norm_weight = None
+        eng.hc_head_fn = None
+        eng._get_layer_weights = lambda i: {}
+        ids = [5, 9, 13]
+        lg = torch.zeros(3, V)
+        lg[0, 9 if n_want >= 1 else 10] = 1.0    # predicts combined[1] = 9 or not
+        lg[1, 13 if n_want >= 2 else 14] = 1.0
+        lg[2, 20] = 1.0
+
+        def fwd(h, lw, i, ids_, lg=lg):
+            ls, comp = eng.layer_states[i], eng._compressors[i]
+            st = {"kv": ls.kv_latent_cache, "cdata": ls.compressed_kv_data, "cidx": ls.compressed_kv_idx,
+                  "comp": (comp.accumulated, comp.kv_state, comp.score_state)}
+            VS.forward_mutation(st, [int(x) for x in ids_.reshape(-1)], i)
+            ls.kv_latent_cache, ls.compressed_kv_data, ls.compressed_kv_idx = st["kv"], st["cdata"], st["cidx"]
+            comp.accumulated, comp.kv_state, comp.score_state = st["comp"]
+            return lg.view(1, 3, 1, V).to(torch.bfloat16), set()
+        eng._forward_layer = fwd
+        n, _ = eng._mtp_verify_batched(torch.tensor([ids[1:]]), 0.0, main_pred_id=torch.tensor([[ids[0]]]))
+        assert n == n_want
+        out[f"vs{case}_n"] = np.array([n, eng._global_pos], dtype=np.int64)
+        for l, ls in eng.layer_states.items():
+            comp = eng._compressors[l]
+            out[f"vs{case}_kv{l}"] = _bf16_np(ls.kv_latent_cache)
+            out[f"vs{case}_cdata{l}"] = _bf16_np(ls.compressed_kv_data)
+            out[f"vs{case}_cidx{l}"] = ls.compressed_kv_idx.numpy()
+            out[f"vs{case}_acc{l}"] = np.array([comp.accumulated], dtype=np.int64)
+            out[f"vs{case}_kvs{l}"] = comp.kv_state.numpy()
+            out[f"vs{case}_scs{l}"] = comp.score_state.numpy()
+
+
 def main():
     sys.path.insert(0, str(_ref_path()))
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -394,6 +457,7 @@ def main():
     gen_permute(out)
     gen_moe(out)
     gen_mtp(out)
+    gen_verify_state(out)
     np.savez_compressed(HERE / "golden.npz", **out)
     print("wrote", HERE / "golden.npz", len(out), "arrays")
 

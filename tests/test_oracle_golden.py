@@ -175,3 +175,29 @@ def test_mtp_decode_loop_matches_reference(golden):
         assert np.array_equal(lg[k].contiguous().view(torch.int16).numpy().view(np.uint16),
                               golden[f"mtp_logits_{k}"]), k
     assert {int(r[4]) for r in recs} == {0, 1, 2}  # rejections, one and two acceptances
+
+
+def test_verify_state_oracle_matches_reference(golden):
+    """oracle/verify_state.commit against the reference's _mtp_verify_batched
+    state handling (engine.py:2443-2459, 2500-2538): KV caches trimmed to old +
+    n_accept (restored at 0), compressed data and compressor states restored,
+    position old + n_accept, for n_accept = 0, 1, 2 of 3 positions."""
+    import copy
+
+    from oracle import verify_state as VS
+    for case in range(3):
+        before = VS.scenario_states(seed=7 + case)
+        after = copy.deepcopy(before)
+        for l in after:
+            VS.forward_mutation(after[l], [5, 9, 13], l)
+        n, pos = (int(v) for v in golden[f"vs{case}_n"])
+        assert n == case
+        out, p = VS.commit(before, after, n, 3, 40)
+        assert p == pos
+        for l, st in out.items():
+            assert np.array_equal(st["kv"].view(torch.int16).numpy().view(np.uint16), golden[f"vs{case}_kv{l}"])
+            assert np.array_equal(st["cdata"].view(torch.int16).numpy().view(np.uint16), golden[f"vs{case}_cdata{l}"])
+            assert np.array_equal(st["cidx"].numpy(), golden[f"vs{case}_cidx{l}"])
+            assert st["comp"][0] == int(golden[f"vs{case}_acc{l}"][0])
+            assert np.array_equal(st["comp"][1].numpy(), golden[f"vs{case}_kvs{l}"])
+            assert np.array_equal(st["comp"][2].numpy(), golden[f"vs{case}_scs{l}"])
