@@ -8,10 +8,15 @@
 // Transformers via Speculative Decoding"; Chen et al. 2023).
 //
 // One thread-block cluster of 8 CTAs per sequence: each CTA streams one eighth
-// of every logits row of the sequence (16-byte loads, HBM-bound), reduces in
-// shared memory, and the cluster combines the 8 partial results through
-// distributed shared memory in rank order (deterministic). The only waits are
-// hardware cluster barriers.
+// of every logits row of the sequence (16-byte loads, four in flight per
+// thread, HBM-bound), each warp reduces its part of every row, one barrier
+// and a fixed-order reduction over the warps follow, and the cluster combines
+// the 8 partial results through distributed shared memory in rank order
+// (deterministic). Greedy folds each 16-byte chunk with the packed
+// NaN-propagating bf16 max and locates an index only in a chunk that beats the
+// running maximum; rejection sampling evaluates the softmax as
+// 2^((x - max) * log2(e) / t), one fused multiply-add and one ex2 per value.
+// The only waits are hardware cluster barriers.
 #include <cooperative_groups.h>
 
 #include "hs_common.cuh"
@@ -55,20 +60,19 @@ __device__ __forceinline__ void argmax_chunk(const uint4& q, int base, float& v,
   const __nv_bfloat162 m2 =
       __hmax2_nan(__hmax2_nan(as_bf162(q.x), as_bf162(q.y)), __hmax2_nan(as_bf162(q.z), as_bf162(q.w)));
   const float cm = __bfloat162float(__hmax_nan(m2.x, m2.y));
-  if (cm > v || (isnan(cm) && !isnan(v)) || ix == 0x7fffffff) {  // (the first chunk: a row of -inf)
+  const bool nan_chunk = isnan(cm);
+  if (cm > v || (nan_chunk && !isnan(v)) || ix == 0x7fffffff) {  // (the first chunk: a row of -inf)
+    // the chunk wins: its first element equal to the folded maximum (the first
+    // NaN when it holds one; -0 and +0 compare equal)
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    int j = 7;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = bf16lo(w[j]), b = bf16hi(w[j]);
-      if (better(a, base + 2 * j, v, ix)) {
-        v = a;
-        ix = base + 2 * j;
-      }
-      if (better(b, base + 2 * j + 1, v, ix)) {
-        v = b;
-        ix = base + 2 * j + 1;
-      }
+    for (int e = 7; e >= 0; --e) {
+      const float x = (e & 1) ? bf16hi(w[e >> 1]) : bf16lo(w[e >> 1]);
+      j = (nan_chunk ? isnan(x) : x == cm) ? e : j;
     }
+    v = cm;
+    ix = base + j;
   }
 }
 
@@ -150,26 +154,40 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     pi[i] = ix;
   }
   cluster.sync();
-  if (rank == 0 && threadIdx.x == 0) {
-    int am[kMaxRows];
-    for (int i = 0; i < T; ++i) {
+  if (rank == 0 && warp == 0) {
+    // lane (row i, rank r): all remote loads at once, then the 8 ranks of a
+    // row combined with shuffles (the (value, first index) order does not
+    // depend on the combining order)
+    __shared__ int am[kMaxRows];
+    for (int i0 = 0; i0 < T; i0 += 32 / kCluster) {
+      const int i = i0 + lane / kCluster, r = lane % kCluster;
       float v = -INFINITY;
       int ix = 0x7fffffff;
-      for (int r = 0; r < kCluster; ++r) {
-        const float* rv = cluster.map_shared_rank(pv, r);
-        const int* ri = cluster.map_shared_rank(pi, r);
-        if (ri[i] != 0x7fffffff && better(rv[i], ri[i], v, ix)) {
-          v = rv[i];
-          ix = ri[i];
+      if (i < T) {
+        v = cluster.map_shared_rank(pv, r)[i];
+        ix = cluster.map_shared_rank(pi, r)[i];
+      }
+#pragma unroll
+      for (int o = kCluster / 2; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, ix, o);
+        if (i2 != 0x7fffffff && (ix == 0x7fffffff || better(v2, i2, v, ix))) {
+          v = v2;
+          ix = i2;
         }
       }
-      am[i] = ix;
-      if (argmax_out) argmax_out[static_cast<int64_t>(b) * T + i] = ix;
+      if (i < T && r == 0) {
+        am[i] = ix;
+        if (argmax_out) argmax_out[static_cast<int64_t>(b) * T + i] = ix;
+      }
     }
-    int n = 0;
-    while (n < T - 1 && static_cast<int64_t>(am[n]) == draft_ids[static_cast<int64_t>(b) * (T - 1) + n]) ++n;
-    n_acc[b] = n;
-    next_tok[b] = am[n];
+    __syncwarp();
+    if (lane == 0) {
+      int n = 0;
+      while (n < T - 1 && static_cast<int64_t>(am[n]) == draft_ids[static_cast<int64_t>(b) * (T - 1) + n]) ++n;
+      n_acc[b] = n;
+      next_tok[b] = am[n];
+    }
   }
   cluster.sync();
 }
@@ -181,19 +199,27 @@ struct MS {
   float m, s;
 };
 
-__device__ __forceinline__ MS ms_combine(MS a, MS b) {
+// The softmax of x / t is evaluated as 2^((x - m) * c) with c = log2(e) / t:
+// one fused multiply-add and one ex2 per element. A pair (m, s) holds a
+// slice's largest logit m and s = sum 2^((x - m) * c).
+__device__ __forceinline__ float ex2(float y) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
+  return r;
+}
+
+__device__ __forceinline__ MS ms_combine(MS a, MS b, float c) {
   if (a.m == -INFINITY) return b;
   if (b.m == -INFINITY) return a;
   const float m = fmaxf(a.m, b.m);
-  return MS{m, a.s * expf(a.m - m) + b.s * expf(b.m - m)};
+  return MS{m, a.s * ex2((a.m - m) * c) + b.s * ex2((b.m - m) * c)};
 }
 
-// Warp-level (max, sum exp(z - max)) of z = x / t over a row slice; every
-// lane gets the warp's pair. Two passes over the thread's chunks (kBatch loads
-// in flight): the largest logit (packed bf16 max, NaN propagating), whose
-// z = x / t is the thread's maximum since dividing by t > 0 keeps the order,
-// then the branch-free sum of exp(x / t - z_max).
-__device__ MS warp_ms(const __nv_bfloat16* __restrict__ row, int lo, int hi, float t) {
+// Warp-level (m, s) of a row slice (every lane gets the warp's pair). Two
+// passes over the thread's chunks (kBatch loads in flight): the largest logit
+// (packed bf16 max, NaN propagating), then the branch-free sum of
+// 2^((x - m) * c).
+__device__ MS warp_ms(const __nv_bfloat16* __restrict__ row, int lo, int hi, float c) {
   const int nvec = (hi - lo) / 8;
   const uint4* p = reinterpret_cast<const uint4*>(row + lo);
   const int bd = static_cast<int>(blockDim.x);
@@ -216,7 +242,7 @@ __device__ MS warp_ms(const __nv_bfloat16* __restrict__ row, int lo, int hi, flo
   }
   MS acc{-INFINITY, 0.f};
   if (mx != -INFINITY) {
-    const float zm = mx / t;
+    const float mc = mx * c;
     float sum = 0.f;
     for (int i0 = threadIdx.x; i0 < nvec; i0 += kBatch * bd) {
       uint4 q[kBatch];
@@ -229,17 +255,17 @@ __device__ MS warp_ms(const __nv_bfloat16* __restrict__ row, int lo, int hi, flo
           const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            sum += expf(bf16lo(w[j]) / t - zm);
-            sum += expf(bf16hi(w[j]) / t - zm);
+            sum += ex2(fmaf(bf16lo(w[j]), c, -mc));
+            sum += ex2(fmaf(bf16hi(w[j]), c, -mc));
           }
         }
     }
-    for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += bd) sum += expf(__bfloat162float(row[k]) / t - zm);
-    acc = MS{zm, sum};
+    for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += bd) sum += ex2(fmaf(__bfloat162float(row[k]), c, -mc));
+    acc = MS{mx, sum};
   }
   for (int o = 16; o > 0; o >>= 1) {
     MS other{__shfl_xor_sync(0xffffffffu, acc.m, o), __shfl_xor_sync(0xffffffffu, acc.s, o)};
-    acc = ms_combine(acc, other);
+    acc = ms_combine(acc, other, c);
   }
   return acc;
 }
@@ -248,20 +274,20 @@ struct Bcast {
   int n_acc;
   int row;       // target row sampled from
   int residual;  // 1: max(0, p - q), 0: p
-  float mt, st, md, sd;
+  float mt, ist, md, isd;  // row maxima and 1 / row sums
 };
 
-__device__ __forceinline__ float resid_of(float xt, float xd, float t, const Bcast& bc) {
-  const float p = expf(xt / t - bc.mt) / bc.st;
+__device__ __forceinline__ float resid_of(float xt, float xd, float c, const Bcast& bc) {
+  const float p = ex2((xt - bc.mt) * c) * bc.ist;
   if (!bc.residual) return p;
-  const float q = expf(xd / t - bc.md) / bc.sd;
+  const float q = ex2((xd - bc.md) * c) * bc.isd;
   return fmaxf(0.f, p - q);
 }
 
 // The sampled distribution at k .. k + 7 (values past `end` are 0): p, or
 // max(0, p - q) at a rejection. k is a multiple of 8, so a whole group is
 // one 16-byte load of each row.
-__device__ __forceinline__ void resid8(const __nv_bfloat16* tr, const __nv_bfloat16* dr, int k, int end, float t,
+__device__ __forceinline__ void resid8(const __nv_bfloat16* tr, const __nv_bfloat16* dr, int k, int end, float c,
                                        const Bcast& bc, float (&rv)[8]) {
   if (k + 8 <= end) {
     const uint4 a = __ldcg(reinterpret_cast<const uint4*>(tr + k));
@@ -269,14 +295,14 @@ __device__ __forceinline__ void resid8(const __nv_bfloat16* tr, const __nv_bfloa
     const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      rv[2 * j] = resid_of(bf16lo(wa[j]), bf16lo(wb[j]), t, bc);
-      rv[2 * j + 1] = resid_of(bf16hi(wa[j]), bf16hi(wb[j]), t, bc);
+      rv[2 * j] = resid_of(bf16lo(wa[j]), bf16lo(wb[j]), c, bc);
+      rv[2 * j + 1] = resid_of(bf16hi(wa[j]), bf16hi(wb[j]), c, bc);
     }
     return;
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j)
-    rv[j] = k + j < end ? resid_of(__bfloat162float(tr[k + j]), bc.residual ? __bfloat162float(dr[k + j]) : 0.f, t, bc)
+    rv[j] = k + j < end ? resid_of(__bfloat162float(tr[k + j]), bc.residual ? __bfloat162float(dr[k + j]) : 0.f, c, bc)
                         : 0.f;
 }
 
@@ -296,6 +322,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   __shared__ int found;
   int lo, hi;
   slice_of(V, rank, lo, hi);
+  const float c = 1.4426950408889634f / t;  // log2(e) / t
   const __nv_bfloat16* trow0 = target + static_cast<int64_t>(b) * (M + 1) * V;
   const __nv_bfloat16* drow0 = draft + static_cast<int64_t>(b) * draft_rows * V;
 
@@ -305,14 +332,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = 0; i <= 2 * M; ++i) {
     const __nv_bfloat16* row = i <= M ? trow0 + static_cast<int64_t>(i) * V : drow0 + static_cast<int64_t>(i - M - 1) * V;
-    const MS r = warp_ms(row, lo, hi, t);
+    const MS r = warp_ms(row, lo, hi, c);
     if (lane == 0) wms[i][warp] = r;
   }
   __syncthreads();
   if (threadIdx.x <= 2 * M) {
     const int i = threadIdx.x;
     MS acc = wms[i][0];
-    for (int w = 1; w < kThreads / 32; ++w) acc = ms_combine(acc, wms[i][w]);
+    for (int w = 1; w < kThreads / 32; ++w) acc = ms_combine(acc, wms[i][w], c);
     if (i <= M)
       tms[i] = acc;
     else
@@ -324,12 +351,29 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
       tz[i] = NAN;
       dz[i] = NAN;
       if (d >= lo && d < hi) {
-        tz[i] = __bfloat162float(trow0[static_cast<int64_t>(i) * V + d]) / t;
-        dz[i] = __bfloat162float(drow0[static_cast<int64_t>(i) * V + d]) / t;
+        tz[i] = __bfloat162float(trow0[static_cast<int64_t>(i) * V + d]);
+        dz[i] = __bfloat162float(drow0[static_cast<int64_t>(i) * V + d]);
       }
     }
   }
   cluster.sync();
+  // rank 0 gathers every rank's row pairs (lane r reads rank r: the remote
+  // loads run in parallel), then thread 0 combines them in rank order
+  __shared__ MS gT[kCluster][kMaxRows], gD[kCluster][kMaxRows];
+  __shared__ float gzt[kCluster][kMaxRows], gzd[kCluster][kMaxRows];
+  if (rank == 0 && warp == 0 && lane < kCluster) {
+    const MS* rt = cluster.map_shared_rank(tms, lane);
+    const MS* rd = cluster.map_shared_rank(dms, lane);
+    const float* rtz = cluster.map_shared_rank(tz, lane);
+    const float* rdz = cluster.map_shared_rank(dz, lane);
+    for (int i = 0; i <= M; ++i) gT[lane][i] = rt[i];
+    for (int i = 0; i < M; ++i) {
+      gD[lane][i] = rd[i];
+      gzt[lane][i] = rtz[i];
+      gzd[lane][i] = rdz[i];
+    }
+  }
+  if (rank == 0) __syncwarp();
   if (rank == 0 && threadIdx.x == 0) {
     MS T_[kMaxRows], D_[kMaxRows];
     float zt[kMaxRows], zd[kMaxRows];
@@ -340,16 +384,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
       zd[i] = NAN;
     }
     for (int r = 0; r < kCluster; ++r) {
-      const MS* rt = cluster.map_shared_rank(tms, r);
-      const MS* rd = cluster.map_shared_rank(dms, r);
-      const float* rtz = cluster.map_shared_rank(tz, r);
-      const float* rdz = cluster.map_shared_rank(dz, r);
-      for (int i = 0; i <= M; ++i) T_[i] = ms_combine(T_[i], rt[i]);
+      for (int i = 0; i <= M; ++i) T_[i] = ms_combine(T_[i], gT[r][i], c);
       for (int i = 0; i < M; ++i) {
-        D_[i] = ms_combine(D_[i], rd[i]);
-        if (!isnan(rtz[i])) {
-          zt[i] = rtz[i];
-          zd[i] = rdz[i];
+        D_[i] = ms_combine(D_[i], gD[r][i], c);
+        if (!isnan(gzt[r][i])) {
+          zt[i] = gzt[r][i];
+          zd[i] = gzd[r][i];
         }
       }
     }
@@ -360,8 +400,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
         report(status, HS_DEV_BAD_DRAFT);
         break;
       }
-      const float p = expf(zt[n] - T_[n].m) / T_[n].s;
-      const float q = expf(zd[n] - D_[n].m) / D_[n].s;
+      const float p = ex2((zt[n] - T_[n].m) * c) / T_[n].s;
+      const float q = ex2((zd[n] - D_[n].m) * c) / D_[n].s;
       const float uu = u[static_cast<int64_t>(b) * (M + 1) + n];
       if (!(uu < p / q)) break;
     }
@@ -369,9 +409,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     bc.row = n;
     bc.residual = n < M ? 1 : 0;
     bc.mt = T_[n].m;
-    bc.st = T_[n].s;
+    bc.ist = 1.f / T_[n].s;
     bc.md = n < M ? D_[n].m : 0.f;
-    bc.sd = n < M ? D_[n].s : 1.f;
+    bc.isd = n < M ? 1.f / D_[n].s : 1.f;
   }
   cluster.sync();
   const Bcast B = *cluster.map_shared_rank(&bc, 0);
@@ -389,7 +429,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   int tl = -1;
   for (int k = k0; k < k1; k += 8) {
     float rv[8];
-    resid8(tr, dr, k, k1, t, B, rv);
+    resid8(tr, dr, k, k1, c, B, rv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       ts += rv[j];
@@ -415,14 +455,22 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     found = 0x7fffffff;
   }
   cluster.sync();
-  // prefix over the cluster in rank order
+  // every rank's slice mass and last positive index, read once per CTA (lane
+  // r of warp 0 reads rank r), then the prefix over the cluster in rank order
+  __shared__ float rsum[kCluster];
+  __shared__ int rlast[kCluster];
+  if (warp == 0 && lane < kCluster) {
+    rsum[lane] = *cluster.map_shared_rank(&csum, lane);
+    rlast[lane] = *cluster.map_shared_rank(&clast, lane);
+  }
+  __syncthreads();
   float pre = 0.f, tot = 0.f;
   int last = -1;
   for (int r = 0; r < kCluster; ++r) {
-    const float s = *cluster.map_shared_rank(&csum, r);
+    const float s = rsum[r];
     if (r < rank) pre += s;
     tot += s;
-    last = max(last, *cluster.map_shared_rank(&clast, r));
+    last = max(last, rlast[r]);
   }
   const float tau = u[static_cast<int64_t>(b) * (M + 1) + M] * tot;
   if (tau >= pre && tau < pre + csum) {
@@ -430,7 +478,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     bool done = false;
     for (int k = k0; k < k1 && !done; k += 8) {
       float rv[8];
-      resid8(tr, dr, k, k1, t, B, rv);
+      resid8(tr, dr, k, k1, c, B, rv);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         x += rv[j];
@@ -442,11 +490,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     }
   }
   cluster.sync();
-  if (rank == 0 && threadIdx.x == 0) {
-    int best = 0x7fffffff;
-    for (int r = 0; r < kCluster; ++r) best = min(best, *cluster.map_shared_rank(&found, r));
-    next_tok[b] = best != 0x7fffffff ? best : (last >= 0 ? last : 0);
-    n_acc[b] = B.n_acc;
+  if (rank == 0 && warp == 0) {
+    int best = lane < kCluster ? *cluster.map_shared_rank(&found, lane) : 0x7fffffff;
+    best = __reduce_min_sync(0xffffffffu, best);
+    if (lane == 0) {
+      next_tok[b] = best != 0x7fffffff ? best : (last >= 0 ? last : 0);
+      n_acc[b] = B.n_acc;
+    }
   }
   cluster.sync();
 }

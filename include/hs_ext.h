@@ -202,7 +202,8 @@ int hs_moe_unpermute(const void* x_expanded, int64_t num_expanded, int64_t D,
 /*   engine.py:2485-2497 and the t=0 bonus at engine.py:2908-2913.            */
 /*   argmax_out [B][T] int64 may be NULL.                                     */
 /* hs_accept_rejection: standard speculative sampling (Leviathan et al. 2023) */
-/*   with p = softmax(target/t), q = softmax(draft/t) in f32: accept draft i  */
+/*   with p = softmax(target/t), q = softmax(draft/t) (f32, evaluated as      */
+/*   2^((x - max) * log2(e) / t) with the hardware ex2): accept draft i       */
 /*   iff u[b][i] < p_i(d_i) / q_i(d_i); at the first rejection i sample from  */
 /*   normalise(max(0, p_i - q_i)), else (all accepted) from p_M, by inverse   */
 /*   CDF in ascending token order with u[b][M]. target [B][M+1][V],           */

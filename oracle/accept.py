@@ -9,12 +9,13 @@ rejection(): standard speculative sampling (Leviathan et al. 2023, "Fast
 Inference from Transformers via Speculative Decoding"; Chen et al. 2023). The
 reference has no rejection sampling (temperature only reaches the draft and
 the bonus multinomial), so this restatement is parity-unpinned by the
-reference. Conventions (shared with the CUDA kernel): z = f32(logit) / f32(t);
-p = softmax(z); accept draft i iff u[i] < p_i(d_i) / q_i(d_i); at the first
-rejection i sample normalise(max(0, p_i - q_i)), else sample p_M, by inverse
-CDF in ascending token order using u[M]. Probabilities are evaluated in
-float64 here (the "exact" answer); the kernel's float32 evaluation agrees
-except within ~1e-6 of a decision boundary.
+reference. Conventions (shared with the CUDA kernel): p = softmax(logit / t);
+accept draft i iff u[i] < p_i(d_i) / q_i(d_i); at the first rejection i sample
+normalise(max(0, p_i - q_i)), else sample p_M, by inverse CDF in ascending
+token order using u[M]. Probabilities are evaluated in float64 here (the
+"exact" answer, z = f32(logit) / f32(t)); the kernel evaluates the same
+softmax in float32 as 2^((logit - max) * log2(e) / t) and agrees except within
+~1e-6 of a decision boundary.
 """
 from __future__ import annotations
 
