@@ -1050,32 +1050,20 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   }
   if (tid < 16) biasv[tid] = (!hash && A.bias) ? __bfloat162float(A.bias[e0 + tid]) : 0.f;
   pdl_trigger();
-  // Two passes over the same code. Pass 0 runs before the PDL wait, while the
-  // previous kernel finishes, on whatever shared memory holds and with every
-  // global write (and every read of data the previous kernel makes) left out:
-  // it only brings the kernel's instructions into the SM's caches, so pass 1,
-  // the real one, does not pay a cold instruction fetch per section.
-  for (int pass = 0; pass < 2; ++pass) {
-  const bool real = pass == 1;
-  if (real) {
-    // pass 0's plain shared-memory writes are ordered before the copies into xs
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    pdl_wait();  // the rows (and everything earlier) are complete
-    if (tid == 0)
-      for (int t = 0; t < T; ++t) bulk_load(xs + t * RS, A.x + static_cast<int64_t>(t) * D, rowb, bar);
-    // clear this kernel's share of the tickets and token tables meanwhile
-    for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ucount;
-         i += static_cast<int64_t>(ncta) * kRouteThreads)
-      A.ucount[i] = 0u;
-    for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ctab;
-         i += static_cast<int64_t>(ncta) * kRouteThreads) {
-      P.ctab_wb[i] = 0.f;
-    }
+  pdl_wait();  // the rows (and everything earlier) are complete
+  if (tid == 0)
+    for (int t = 0; t < T; ++t) bulk_load(xs + t * RS, A.x + static_cast<int64_t>(t) * D, rowb, bar);
+  // clear this kernel's share of the tickets and token tables meanwhile
+  for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ucount;
+       i += static_cast<int64_t>(ncta) * kRouteThreads)
+    A.ucount[i] = 0u;
+  for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ctab;
+       i += static_cast<int64_t>(ncta) * kRouteThreads) {
+    P.ctab_wb[i] = 0.f;
   }
   if (rank == 0) {
     if (tid < 8) emask[tid] = 0u;
-    if (real && hash && tid < T * K) {  // hash routing: tid2eid[id], weight 1/K (engine.py:1018-1023)
+    if (hash && tid < T * K) {  // hash routing: tid2eid[id], weight 1/K (engine.py:1018-1023)
       const int t = tid / K, j = tid - t * K;
       const int64_t id = A.ids[t];
       int64_t e = -1;
@@ -1094,7 +1082,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       sW[tid] = hw;
     }
   }
-  bool ok = real ? mbar_wait(bar, 0) : true;
+  bool ok = mbar_wait(bar, 0);
   if (!ok) {  // report, and let the copies land before the shared memory is reused or released
     report(A.status, HS_DEV_TIMEOUT);
     (void)mbar_wait(bar, 0);
@@ -1228,7 +1216,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
         const uint4* src = reinterpret_cast<const uint4*>(xs + t * RS);
         uint4 hv, lv;
         split16(src[2 * k16], src[2 * k16 + 1], exp2i(rowe[t]), hv, lv);
-        if (!real) continue;
         reinterpret_cast<uint4*>(P.x8 + static_cast<int64_t>(t) * D)[k16] = hv;
         reinterpret_cast<uint4*>(P.x8 + (A.P_max + t) * D)[k16] = lv;
         if (A.x_out) {
@@ -1238,10 +1225,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
         }
       }
     }
-    if (rank != 0) {
-      if (real) return;
-      continue;
-    }
+    if (rank != 0) return;
   }
 
   // ---- CTA 0: the router's top-k selection from the gathered keys ----
@@ -1282,13 +1266,11 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       const float wv = (wsel / denom) * A.scaling;
       sI[t * K + lane] = esel;
       sW[t * K + lane] = wv;
-      if (real) {
-        A.idx_out[t * K + lane] = esel;
-        A.w_out[t * K + lane] = wv;
-      }
+      A.idx_out[t * K + lane] = esel;
+      A.w_out[t * K + lane] = wv;
     }
   }
-  if (real && tid < T) {
+  if (tid < T) {
     P.sb1[tid] = static_cast<uint8_t>(127 - rowe[tid]);
     P.tok_e[tid] = rowe[tid];
   }
@@ -1338,7 +1320,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   uint32_t em[8];
 #pragma unroll
   for (int w = 0; w < 8; ++w) em[w] = emask[w];
-  if (real && tid < npairs && le >= 0) {
+  if (tid < npairs && le >= 0) {
     const int t = tid / K;
     int cb = 0;
 #pragma unroll
@@ -1353,7 +1335,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     P.chunk_pair0[cb] = 0;
     P.chunk_np[cb] = 0;
   }
-  if (real && tid == 0) {
+  if (tid == 0) {
     int C = 0;
 #pragma unroll
     for (int w = 0; w < 8; ++w) C += __popc(em[w]);
@@ -1361,7 +1343,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     P.hdr[1] = C;
     P.hdr[2] = 0;
   }
-  }  // pass
 }
 
 // ---------------------------------------------------------------------------
@@ -1622,16 +1603,25 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t o = i;  // token-major [8][D] rows: entry (t, d) of this call's T x D output
-    float r = 0.f, sh = 0.f;
-    for (int q = 0; q < world && !timed_out; ++q) {
-      volatile uint32_t* pr = reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 0, D) + o);
-      volatile uint32_t* ps = reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 1, D) + o);
-      uint32_t vr = *pr, vs = *ps;
-      if (vr == epx::kEmpty || vs == epx::kEmpty) {
+    // every rank's two entries are read at once (one round trip when they have
+    // all arrived); only missing ones are polled again
+    uint32_t vr[HS_EP_MAX_RANKS], vs[HS_EP_MAX_RANKS];
+#pragma unroll
+    for (int q = 0; q < HS_EP_MAX_RANKS; ++q)
+      if (q < world) {
+        vr[q] = *reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 0, D) + o);
+        vs[q] = *reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 1, D) + o);
+      }
+#pragma unroll
+    for (int q = 0; q < HS_EP_MAX_RANKS; ++q) {
+      if (q >= world || timed_out) continue;
+      if (vr[q] == epx::kEmpty || vs[q] == epx::kEmpty) {
+        volatile uint32_t* pr = reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 0, D) + o);
+        volatile uint32_t* ps = reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 1, D) + o);
         const uint64_t t0 = globaltimer_ns();
-        for (uint32_t it = 1; vr == epx::kEmpty || vs == epx::kEmpty; ++it) {
-          vr = *pr;
-          vs = *ps;
+        for (uint32_t it = 1; vr[q] == epx::kEmpty || vs[q] == epx::kEmpty; ++it) {
+          vr[q] = *pr;
+          vs[q] = *ps;
           if ((it & 63u) == 0 && (globaltimer_ns() - t0 > limit_ns || *poison != 0u)) {
             report(status, HS_DEV_TIMEOUT);
             *poison = 1u;
@@ -1641,12 +1631,17 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world
           }
         }
       }
-      r += __uint_as_float(vr);
-      sh += __uint_as_float(vs);
-      *pr = epx::kEmpty;
-      *ps = epx::kEmpty;
     }
     if (timed_out) break;
+    float r = 0.f, sh = 0.f;
+#pragma unroll
+    for (int q = 0; q < HS_EP_MAX_RANKS; ++q)
+      if (q < world) {  // ranks summed in order from 0: identical bits on every rank
+        r += __uint_as_float(vr[q]);
+        sh += __uint_as_float(vs[q]);
+        *reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 0, D) + o) = epx::kEmpty;
+        *reinterpret_cast<volatile uint32_t*>(epx::rows(buf, slot, world, q, 1, D) + o) = epx::kEmpty;
+      }
     float y = round_bf16(r);
     if (use_shared) y += round_bf16(sh);
     const float yb = __bfloat162float(__float2bfloat16_rn(y));

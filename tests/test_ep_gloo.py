@@ -74,12 +74,12 @@ def test_two_rank_expert_parallel_layer_matches_single_process(T):
     assert rel <= 1e-2, rel
 
 
-def _sharded_rank_main(rank: int, world: int, port: int, T: int, out_q) -> None:
+def _sharded_rank_main(rank: int, world: int, port: int, T: int, out_q, skip_self: bool = False) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from home_seek_b200.ep import TokenShardedEP, expert_range
+        from home_seek_b200.ep import TokenShardedEP, expert_range, localize
         shape = I.SMALL
         load = I.make_loader(shape)
         gate, bias = I.router_weights(shape.E, shape.D, seed=1)
@@ -90,11 +90,18 @@ def _sharded_rank_main(rank: int, world: int, port: int, T: int, out_q) -> None:
         hl, il, wl = h[lo:hi], idx[lo:hi], w[lo:hi]
         off, held = expert_range(shape.E, rank, world)
         ep = TokenShardedEP(rank, world)
-        d, hr, ir, wr = ep.dispatch(hl, il, wl, held)
+        d, hr, ir, wr = ep.dispatch(hl, il, wl, held, skip_self=skip_self)
         assert int(ir.max()) < held if ir.numel() else True
         # the received rows through this rank's experts (local ids -> global for the loader)
         y = O.moe_routed_f32(hr, torch.where(ir >= 0, ir + off, ir), wr, load)
-        routed = ep.combine(d, y, hl.shape[0])
+        own = None
+        if skip_self:
+            # TokenShardedEP.moe's form: this rank's own experts on its own tokens,
+            # run locally and added at this rank's place in the sum
+            assert d.send_counts[rank] == 0 and d.recv_counts[rank] == 0
+            loc = localize(il, off, held)
+            own = O.moe_routed_f32(hl, torch.where(loc >= 0, loc + off, loc), wl, load)
+        routed = ep.combine(d, y, hl.shape[0], own=own)
         out = O.ep_combine(routed, O.shared_expert_f32(hl, sh))
         ref = O.moe_layer(hl, il, wl, load, sh)
         ref_routed = O.moe_routed_f32(hl, il, wl, load)
@@ -104,17 +111,20 @@ def _sharded_rank_main(rank: int, world: int, port: int, T: int, out_q) -> None:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("skip_self", [False, True])
 @pytest.mark.parametrize("T,world", [(5, 2), (8, 2), (9, 4)])
-def test_token_sharded_dispatch_combine(T, world):
+def test_token_sharded_dispatch_combine(T, world, skip_self):
     """Prefill-size expert parallelism with the tokens sharded: each rank sends
     its tokens' rows to the ranks holding their experts (gloo all-to-all), the
     receivers run their experts (the oracle here; the kernels on the GPU), the
     f32 results come back and are added per token in rank order: each rank's
-    tokens come out as the single-process layer computes them."""
+    tokens come out as the single-process layer computes them. skip_self is
+    TokenShardedEP.moe's form: nothing is sent to the rank itself, its own
+    experts' term comes in through combine(own=...)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_sharded_rank_main, args=(r, world, port, T, q)) for r in range(world)]
+    procs = [ctx.Process(target=_sharded_rank_main, args=(r, world, port, T, q, skip_self)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
