@@ -19,7 +19,7 @@ _LIB_PATH = Path(__file__).resolve().parent / "libhs_ext.so"
 
 HS_OK = 0
 STATUS_NAMES = {0: "HS_OK", 1: "HS_ERR_BAD_SHAPE", 2: "HS_ERR_BAD_ARGUMENT", 3: "HS_ERR_WORKSPACE",
-                4: "HS_ERR_ALIGN", 5: "HS_ERR_CUDA", 6: "HS_ERR_UNSUPPORTED"}
+                4: "HS_ERR_ALIGN", 5: "HS_ERR_CUDA", 6: "HS_ERR_UNSUPPORTED", 7: "HS_ERR_NCCL"}
 HS_DEV_BAD_EXPERT = 0x1
 HS_DEV_BAD_TOKEN = 0x2
 HS_DEV_TIMEOUT = 0x4
@@ -31,6 +31,7 @@ HS_DUP_LAST = 0
 HS_DUP_SUM = 1
 HS_EP_MAX_RANKS = 8
 HS_IPC_HANDLE_BYTES = 64
+HS_NCCL_UNIQUE_ID_BYTES = 128
 
 
 class HsEpPeers(ctypes.Structure):
@@ -117,6 +118,14 @@ SIGNATURES = {
     "hs_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]),
     "hs_moe_combine_add_rms_norm": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_float, c_int64, c_int64,
                                             c_void_p, c_void_p, c_void_p]),
+    "hs_ep_nccl_unique_id": (c_int, [c_void_p]),
+    "hs_ep_nccl_comm_init": (c_int, [c_void_p, c_int32, c_int32, POINTER(c_void_p)]),
+    "hs_ep_nccl_comm_destroy": (c_int, [c_void_p]),
+    "hs_ep_dispatch_plan": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int32, c_int32, c_void_p, c_void_p,
+                                    c_void_p, c_void_p]),
+    "hs_ep_dispatch_combine_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64, c_int32]),
+    "hs_ep_dispatch_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                       c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "hs_verify_state_snapshot": (c_int, [c_void_p, c_int64, c_int64, c_void_p]),
     "hs_verify_state_commit": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int32, c_void_p]),
     "hs_fill_bytes": (c_int, [c_void_p, c_int64, c_uint64, c_int32, c_int32, c_void_p]),

@@ -17,7 +17,7 @@ PKG_DIR = Path(__file__).resolve().parent
 CSRC = PKG_DIR / "csrc"
 INCLUDE = PKG_DIR.parent / "include"
 LIB_PATH = PKG_DIR / "libhs_ext.so"
-SOURCES = ["hs_util.cu", "hs_router.cu", "hs_moe.cu", "hs_accept.cu", "hs_norm.cu", "hs_head.cu", "hs_state.cu"]
+SOURCES = ["hs_util.cu", "hs_router.cu", "hs_moe.cu", "hs_accept.cu", "hs_norm.cu", "hs_head.cu", "hs_state.cu", "hs_ep.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -61,7 +61,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             raise RuntimeError(f"nvcc failed on {s}")
         objs.append(str(obj))
     tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [nvcc, "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ARCH_FLAGS + ["-Xcompiler", "-fPIC"]
+    cmd = [nvcc, "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ARCH_FLAGS + ["-Xcompiler", "-fPIC", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)

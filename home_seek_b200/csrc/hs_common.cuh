@@ -35,6 +35,9 @@ void set_last_cuda_error(int e);
 // Returns HS_ERR_CUDA if the most recent launch on this thread failed.
 int check_launch();
 
+// The dimensions an hs_moe_make_desc descriptor was built for (hs_moe.cu).
+int moe_desc_dims(const void* desc, int64_t* E, int64_t* D, int64_t* I, int64_t* I_sh);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------------------

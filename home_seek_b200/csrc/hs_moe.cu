@@ -1752,20 +1752,37 @@ __device__ __forceinline__ void sum_slots(const SchedT& sc, int cf, int cl, int6
 
 // A split unit's finishing CTA: the sum, in CTA order, of the partial rows
 // the other CTAs c0..cl published in their slots (slot 2c; CTAs without steps
-// skipped), NV values of one row.
+// skipped), NV values of one row. Up to NB peers' rows are loaded at once
+// (one L2 round trip per NB peers), then added in CTA order.
 template <int NV, typename SchedT>
 __device__ __forceinline__ void peer_sum(const SchedT& sc, int c0, int cl, const float* part, int slot_floats,
                                          int row, float (&acc)[NV]) {
+  constexpr int NB = NV <= 16 ? 4 : (NV <= 32 ? 2 : 1);  // peers in flight (register budget)
 #pragma unroll
   for (int t = 0; t < NV; ++t) acc[t] = 0.f;
-  for (int cc = c0; cc <= cl; ++cc) {
-    if (sc.lo(cc) == sc.lo(cc + 1)) continue;
-    const float* sl = part + 2 * static_cast<int64_t>(cc) * slot_floats;
-    float v[NV];
+  int64_t lc = sc.lo(c0);
+  for (int cb = c0; cb <= cl; cb += NB) {
+    const float* sl[NB];
 #pragma unroll
-    for (int t = 0; t < NV; ++t) v[t] = __ldcg(sl + t * kM + row);
+    for (int b = 0; b < NB; ++b) {
+      const int cc = cb + b;
+      sl[b] = nullptr;
+      if (cc <= cl) {
+        const int64_t ln = sc.lo(cc + 1);
+        if (lc < ln) sl[b] = part + 2 * static_cast<int64_t>(cc) * slot_floats;
+        lc = ln;
+      }
+    }
+    float v[NB][NV];
 #pragma unroll
-    for (int t = 0; t < NV; ++t) acc[t] += v[t];
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < NV; ++t) v[b][t] = sl[b] ? __ldcg(sl[b] + t * kM + row) : 0.f;
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if (sl[b])
+#pragma unroll
+        for (int t = 0; t < NV; ++t) acc[t] += v[b][t];
   }
 }
 
@@ -3458,6 +3475,19 @@ extern "C" int hs_moe_make_desc(const hs_moe_weights* w, void* desc_out, size_t 
   d.magic = kDescMagic;
   memset(desc_out, 0, desc_bytes);
   memcpy(desc_out, &d, sizeof(d));
+  return HS_OK;
+}
+
+// The dimensions a descriptor was built for (E = the experts its store holds).
+int hs::moe_desc_dims(const void* desc, int64_t* E, int64_t* D, int64_t* I, int64_t* I_sh) {
+  if (!desc) return HS_ERR_BAD_ARGUMENT;
+  Desc d;
+  memcpy(&d, desc, sizeof(d));
+  if (d.magic != kDescMagic) return HS_ERR_BAD_ARGUMENT;
+  *E = d.E;
+  *D = d.D;
+  *I = d.I;
+  *I_sh = d.has_shared ? d.I_sh : 0;
   return HS_OK;
 }
 

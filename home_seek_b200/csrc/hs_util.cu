@@ -71,6 +71,8 @@ extern "C" const char* hs_status_string(int status) {
       return "CUDA error";
     case HS_ERR_UNSUPPORTED:
       return "unsupported device or driver";
+    case HS_ERR_NCCL:
+      return "NCCL error";
     default:
       return "unknown status";
   }

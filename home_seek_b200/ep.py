@@ -316,3 +316,80 @@ class TokenShardedEP:
             return h.new_empty(0, h.shape[1])
         parts[0].copy_(routed)
         return ops.moe_combine(parts, use_shared=use_shared)
+
+
+def dispatch_plan(topk_idx: torch.Tensor, experts_per_rank: int, world: int, rank: int):
+    """hs_ep_dispatch_plan on the device: (counts [world] int32, pos [T, world]
+    int32, own_ids [T, K] int64) — rank q's list of this rank's tokens with an
+    expert on q (ascending; empty for this rank), each token's place in it (or
+    -1), and this rank's own ids localised (others -1). The same lists as
+    dispatch_lists with skip_self."""
+    dev = ops._check_cuda(topk_idx)
+    topk_idx = topk_idx.to(torch.int64).contiguous()
+    T, K = topk_idx.shape
+    counts = torch.empty(world, dtype=torch.int32, device=dev)
+    pos = torch.empty(T, world, dtype=torch.int32, device=dev)
+    own = torch.empty(T, K, dtype=torch.int64, device=dev)
+    ops._launch("hs_ep_dispatch_plan", topk_idx.data_ptr(), T, K, experts_per_rank, world, rank,
+                counts.data_ptr(), pos.data_ptr(), own.data_ptr(), ops._stream(dev), extra=1 if T else 0)
+    return counts, pos, own
+
+
+class NcclTokenShardedEP:
+    """TokenShardedEP as one C-ABI call (hs_ep_dispatch_combine): the plan,
+    pack and combine are kernels, the exchanges NCCL send/recv on the caller's
+    stream through a communicator of the library's own (created from a unique
+    id that rank 0 makes and the torch process group hands round). Same
+    arithmetic as TokenShardedEP.moe, so the outputs are identical; T_max
+    (>= every rank's token count, the same on all ranks) sizes the workspace."""
+
+    def __init__(self, rank: int, world: int, T_max: int, group=None, device: Optional[torch.device] = None):
+        import torch.distributed as dist
+        self.rank, self.world, self.T_max = rank, world, int(T_max)
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        uid = (ctypes.c_uint8 * _lib.HS_NCCL_UNIQUE_ID_BYTES)()
+        if world > 1:
+            if rank == 0:
+                _lib.call("hs_ep_nccl_unique_id", ctypes.addressof(uid))
+            obj = [bytes(uid)]
+            dist.broadcast_object_list(obj, src=0, group=group)
+            ctypes.memmove(uid, obj[0], len(obj[0]))
+        elif world == 1:
+            _lib.call("hs_ep_nccl_unique_id", ctypes.addressof(uid))
+        self._comm = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            st = lib.hs_ep_nccl_comm_init(ctypes.addressof(uid), world, rank, ctypes.byref(self._comm))
+        if st != 0:
+            raise _lib.HsError("hs_ep_nccl_comm_init", st)
+
+    def close(self) -> None:
+        if self._comm:
+            _lib.call("hs_ep_nccl_comm_destroy", self._comm)
+            self._comm = ctypes.c_void_p()
+
+    def moe(self, store: HBMExpertStore, layer: int, h: torch.Tensor, topk_idx: torch.Tensor,
+            topk_w: torch.Tensor, dup_mode: int = _lib.HS_DUP_LAST, use_shared: bool = True,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The MoE output [T, D] bf16 of this rank's tokens (normed rows h,
+        global expert ids), as TokenShardedEP.moe."""
+        dev = self.device
+        T, D = h.shape
+        if T:
+            ops._check_cuda(h, topk_idx, topk_w, out)
+            if h.dtype != torch.bfloat16:
+                raise TypeError("h must be bf16")
+        topk_idx = topk_idx.to(torch.int64).contiguous()
+        topk_w = topk_w.to(torch.float32).contiguous()
+        K = topk_idx.shape[1] if topk_idx.dim() == 2 else 6
+        _, Dd, I, I_sh = store.dims
+        if out is None:
+            out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+        lib = _lib.load()
+        nb = lib.hs_ep_dispatch_combine_workspace_size(self.T_max, K, Dd, I, I_sh, self.world)
+        ws = ops.workspace(dev, nb, "ep_nccl")
+        ops._launch("hs_ep_dispatch_combine", self._comm, ctypes.addressof(store.desc(layer)), h.data_ptr(),
+                    topk_idx.data_ptr(), topk_w.data_ptr(), T, self.T_max, K, int(use_shared and I_sh > 0),
+                    int(dup_mode), out.data_ptr(), ws.data_ptr(), ws.numel(), ops.status_word(dev).data_ptr(),
+                    ops._stream(dev), extra=4 if T else 1)
+        return out

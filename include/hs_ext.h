@@ -42,7 +42,8 @@ typedef enum hs_status {
   HS_ERR_WORKSPACE = 3,      /* workspace smaller than *_workspace_size() */
   HS_ERR_ALIGN = 4,          /* pointer or stride not 16-byte aligned as required */
   HS_ERR_CUDA = 5,           /* a CUDA runtime/driver call failed */
-  HS_ERR_UNSUPPORTED = 6     /* device is not sm_100 or a driver entry point is missing */
+  HS_ERR_UNSUPPORTED = 6,    /* device is not sm_100 or a driver entry point is missing */
+  HS_ERR_NCCL = 7            /* an NCCL call failed (hs_ep_* over NCCL) */
 } hs_status;
 
 /* Bits OR-ed into the optional device status word. */
@@ -418,6 +419,58 @@ int hs_moe_combine_add_rms_norm(const float* routed_f32,
                                 const void* h, const void* w, float eps,
                                 int64_t T, int64_t D, void* h_out, void* x_out,
                                 void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Expert parallelism with the tokens sharded over the ranks (prefill), one  */
+/* call over NCCL. Replaces the reference's _forward_ffn_ep                  */
+/* (inference_engine/engine.py:1575-1709: every token on every GPU, the GPUs' */
+/* bf16 expert outputs added) and the dispatch/combine of                     */
+/* inference_engine/parallel.py:189-384. Rank r owns a shard of the tokens,  */
+/* its routing (global expert ids), and a store with the routed experts       */
+/* [r E_l, (r+1) E_l) (E_l = the descriptor's E) and the whole shared expert. */
+/* hs_ep_dispatch_combine, on the caller's stream:                            */
+/*   - sends each token's row once to every other rank holding one of its     */
+/*     experts, with its ids localised there and its weights (NCCL send/recv, */
+/*     after a count exchange read on the host: the call's one sync);         */
+/*   - runs hs_moe_ffn_fp4_partials on the own tokens (own experts + shared)  */
+/*     and on the received rows (routed only);                                */
+/*   - returns the received rows' f32 sums, adds every token's terms in rank  */
+/*     order (the own term at this rank's place) and writes                   */
+/*     out = bf16(bf16(routed) + bf16(shared)) [T][D].                        */
+/* Every rank of the communicator calls it with the same T_max (>= every     */
+/* rank's T), top_k, use_shared and dup_mode and a workspace of at least      */
+/* hs_ep_dispatch_combine_workspace_size(T_max, top_k, D, I, I_sh, world)     */
+/* bytes (zero-filled once). A rank whose own arguments are bad (T > T_max,   */
+/* NULL or unaligned pointers) takes part with no tokens and returns the      */
+/* error afterwards, so its peers' calls complete. T may be 0. With world 1  */
+/* the call makes no NCCL call and no host synchronisation. NCCL is loaded at */
+/* run time (libnccl.so.2); without it these return HS_ERR_UNSUPPORTED.       */
+/* T, T_max <= 65535; world <= HS_EP_MAX_RANKS.                                */
+/* hs_ep_nccl_unique_id: on one rank; the caller hands the                    */
+/* HS_NCCL_UNIQUE_ID_BYTES to the others. hs_ep_nccl_comm_init: on every rank */
+/* with the current CUDA device set.                                          */
+/* hs_ep_dispatch_plan: the call's first step alone (for tests and callers   */
+/* with their own transport): counts[world] (rows to each rank; 0 for this   */
+/* rank), pos[T][world] (the token's place in each rank's list, or -1),      */
+/* own_ids[T][top_k] (this rank's ids localised, others -1; may be NULL).     */
+/* ------------------------------------------------------------------------ */
+#define HS_NCCL_UNIQUE_ID_BYTES 128
+int hs_ep_nccl_unique_id(void* id_out);
+int hs_ep_nccl_comm_init(const void* id, int32_t world, int32_t rank, void** comm);
+int hs_ep_nccl_comm_destroy(void* comm);
+int hs_ep_dispatch_plan(const int64_t* topk_idx, int64_t T, int64_t top_k,
+                        int64_t experts_per_rank, int32_t world, int32_t rank,
+                        int32_t* counts, int32_t* pos, int64_t* own_ids,
+                        void* stream);
+size_t hs_ep_dispatch_combine_workspace_size(int64_t T_max, int64_t top_k,
+                                             int64_t D, int64_t I, int64_t I_sh,
+                                             int32_t world);
+int hs_ep_dispatch_combine(void* comm, const void* desc, const void* hidden,
+                           const int64_t* topk_idx, const float* topk_w,
+                           int64_t T, int64_t T_max, int64_t top_k,
+                           int use_shared, int dup_mode, void* out,
+                           void* workspace, size_t workspace_bytes,
+                           int32_t* dev_status, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Verify-state snapshot / restore on the device.                             */

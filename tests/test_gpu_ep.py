@@ -298,6 +298,114 @@ def test_nccl_token_sharded_expert_parallel_matches_single_gpu():
         assert rel <= MOE_TOL, (rank, rel)
 
 
+def _sharded_c_rank(rank: int, world: int, port: int, q) -> None:
+    """hs_ep_dispatch_combine (NcclTokenShardedEP) against TokenShardedEP on the
+    same shards (identical bits) and the single-GPU call; uneven token shards."""
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    ep = None
+    try:
+        from home_seek_b200 import ops
+        from home_seek_b200.ep import NcclTokenShardedEP, TokenShardedEP, shard_store
+        shape = I.SMALL
+        full = _full_store(dev)
+        gate, bias = I.router_weights(shape.E, shape.D, seed=1)
+        T = 1000
+        h = I.hidden(T, shape.D, seed=13).to(dev)
+        idx, w = ops.router_topk(h, gate.to(dev), bias.to(dev), shape.K, 1.5)
+        cuts = {2: [0, 563, 1000], 4: [0, 250, 463, 750, 1000]}[world]  # uneven token shards
+        lo, hi = cuts[rank], cuts[rank + 1]
+        T_max = max(cuts[r + 1] - cuts[r] for r in range(world))
+        st = shard_store(full, rank, world, shared="replicated")
+        hl, il, wl = h[lo:hi].contiguous(), idx[lo:hi].contiguous(), w[lo:hi].contiguous()
+        ref = ops.moe_ffn(full.desc(0), full.dims, hl, il, wl, use_shared=True)
+        py = TokenShardedEP(rank, world).moe(st, 0, hl, il, wl)
+        ep = NcclTokenShardedEP(rank, world, T_max)
+        c1 = ep.moe(st, 0, hl, il, wl)
+        c2 = ep.moe(st, 0, hl, il, wl)   # the workspace's second use
+        torch.cuda.synchronize()
+        q.put((rank, hi - lo, bool(torch.equal(c1, py)), bool(torch.equal(c2, py)), _rel(c1, ref)))
+    finally:
+        if ep is not None:
+            ep.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_nccl_dispatch_combine_c_abi_matches_token_sharded_ep(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_c_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert sum(r[1] for r in res) == 1000
+    for rank, _, eq1, eq2, rel in res:
+        assert eq1 and eq2, rank
+        assert rel <= MOE_TOL, (rank, rel)
+
+
+def test_dispatch_plan_matches_dispatch_lists():
+    """hs_ep_dispatch_plan's lists (kernel) are dispatch_lists' with this rank's
+    own list empty, and its own ids are localize's, on ids with -1 and ids past
+    the group's experts."""
+    from home_seek_b200.ep import dispatch_lists, dispatch_plan, localize
+    g = torch.Generator().manual_seed(3)
+    for T, world, epr in [(1, 2, 8), (37, 4, 8), (1500, 8, 32), (0, 2, 8)]:
+        idx = torch.randint(-1, world * epr + 3, (T, 6), generator=g)
+        for rank in range(world):
+            counts, pos, own = dispatch_plan(idx.cuda(), epr, world, rank)
+            counts, pos, own = counts.cpu(), pos.cpu(), own.cpu()
+            toks, _ = dispatch_lists(idx, epr, world)
+            for q in range(world):
+                want = toks[q].tolist() if q != rank else []
+                assert int(counts[q]) == len(want), (T, world, rank, q)
+                got = [t for t in range(T) if int(pos[t, q]) >= 0]
+                assert got == want
+                assert [int(pos[t, q]) for t in got] == list(range(len(want)))
+            if T:
+                assert torch.equal(own, localize(idx, rank * epr, epr))
+
+
+def test_nccl_dispatch_combine_single_rank_is_the_partials_call():
+    """world = 1 (no exchange, no host synchronisation): the C-ABI call is
+    hs_moe_ffn_fp4_partials on the tokens plus hs_moe_combine, bit for bit."""
+    from home_seek_b200 import ops
+    from home_seek_b200.ep import NcclTokenShardedEP
+    shape = I.SMALL
+    st = _full_store()
+    gate, bias = I.router_weights(shape.E, shape.D, seed=1)
+    ep = NcclTokenShardedEP(0, 1, 300)
+    try:
+        for T in (0, 1, 7, 300):
+            h = I.hidden(max(T, 1), shape.D, seed=17)[:T].cuda().contiguous()
+            if T:
+                idx, w = ops.router_topk(h, gate.cuda(), bias.cuda(), shape.K, 1.5)
+            else:
+                idx = torch.zeros(0, shape.K, dtype=torch.int64, device="cuda")
+                w = torch.zeros(0, shape.K, dtype=torch.float32, device="cuda")
+            out = ep.moe(st, 0, h, idx, w)
+            if T:
+                parts = ops.moe_ffn_partials(st.desc(0), st.dims, h, idx, w, use_shared=True)
+                assert torch.equal(out, ops.moe_combine(parts, use_shared=True)), T
+    finally:
+        ep.close()
+
+
 class _DevView:
     """A raw device pointer as an int64 array torch can wrap (CUDA array interface)."""
 
