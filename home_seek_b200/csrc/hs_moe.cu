@@ -148,11 +148,20 @@ struct Plan {
   // rows 8-15) over the k-tile's 32-column block j, i.e. lines 0-15 of a
   // 512-byte atom (an N = 16 MMA never reads the rows above 15)
   uint8_t* act_img;
+  // token mode, a call with its routing in the route kernel: the kernels of
+  // one call hand over through counters instead of grid completion. ready:
+  // route CTAs done (each adds 1 after its writes; the down phase resets it);
+  // done: [1 + C_max slots][I_act / 256 k-steps] gate/up units finished
+  // (each k-step of the down phase reads two 128-column units; cleared by the
+  // route kernel with the tickets)
+  uint32_t* done;
+  uint32_t* ready;
 };
 
 struct Geometry {
   int64_t T, K, D, I, I_sh, I_act, P_max, C_max;
   int64_t U_gu, U_dn;      // upper bounds on gate/up and down units
+  int64_t n_done;          // token mode: gate/up unit counters of the down phase's k-steps
   int G;                   // persistent CTAs
   int aligned;             // unit-aligned schedule (no partial slots)
   int64_t slot_floats;     // floats per partial slot (gate/up, the larger)
@@ -209,8 +218,9 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   g.G = G;
   g.aligned = 0;
   g.slot_floats = 2 * kM * 8 * ntiles(T);
-  g.off_ucount = o;
-  o = align_up(o + (g.U_gu + g.U_dn) * sizeof(uint32_t), 256);
+  g.n_done = T <= kTokMax ? (1 + g.C_max) * (g.I_act / 256) : 0;
+  g.off_ucount = o;  // tickets, then the done counters, then the ready counter
+  o = align_up(o + (g.U_gu + g.U_dn + g.n_done + 1) * sizeof(uint32_t), 256);
   g.off_part = o;
   o = align_up(o + 2 * static_cast<int64_t>(G) * g.slot_floats * sizeof(float), 256);
   g.off_ctab = o;
@@ -244,6 +254,8 @@ static Plan plan_views(const Geometry& g, void* ws) {
   p.out_part = reinterpret_cast<float*>(b + g.off_out);
   p.ctab_wb = reinterpret_cast<float*>(b + g.off_ctab);
   p.act_img = b + g.off_img;
+  p.done = reinterpret_cast<uint32_t*>(b + g.off_ucount) + g.U_gu + g.U_dn;
+  p.ready = p.done + g.n_done;
   return p;
 }
 
@@ -994,7 +1006,7 @@ struct RouteSmem {
   static constexpr size_t red(int D) { return nw(D) + static_cast<size_t>(D) * 2; }  // [split <= 8][lane][4] f32
   static constexpr size_t keys(int D) { return red(D) + 8 * 32 * 4 * 4; }            // CTA 0: [token][expert] u32
   static constexpr size_t top(int D) { return keys(D) + 8 * 256 * 4; }
-  static constexpr size_t bar(int D) { return top(D) + 8 * 16 * (8 + 4) + 32 + 32 + 64 + 32 + 256; }
+  static constexpr size_t bar(int D) { return top(D) + 8 * 16 * (8 + 4) + 32 + 32 + 64 + 32 + 256 + 256; }
   static constexpr size_t bytes(int D) { return bar(D) + 16; }
 };
 static_assert(RouteSmem::bytes(kRouteMaxD) <= 232448, "route kernel shared memory");
@@ -1007,6 +1019,16 @@ __device__ __forceinline__ uint32_t score_key32(float s) {
 }
 __device__ __forceinline__ float key32_score(uint32_t k) {
   return __uint_as_float(k == 0xffffffffu ? k : k - 1u);
+}
+
+// A route CTA's writes are complete: every thread's writes, then one release
+// increment of the ready counter the gate/up phase waits for.
+__device__ __forceinline__ void release_ready(uint32_t* ready) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(ready, 1u);
+  }
 }
 
 __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs A, Plan P,
@@ -1032,10 +1054,14 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   float* biasv = reinterpret_cast<float*>(rowe + 8);                  // [16] this CTA's biases
   float* rinv = biasv + 16;                                           // [8] 1 / rms of each row
   float* wpart = rinv + 8;                                            // [8 warps][8 rows] sums of squares
+  float* wmax = wpart + 64;                                           // [8 warps][8 rows] max |x|
   uint64_t* bar = reinterpret_cast<uint64_t*>(rs + RouteSmem::bar(D));
   const int e0 = rank * 16;
   const uint32_t rowb = static_cast<uint32_t>(D) * 2;
   const int nv = D / 8;  // 16-byte vectors per row
+  // CTAs that write the hi/lo split of the rows (and need each row's prescale
+  // exponent): every rank but 0 (rank 1 also takes rank 0's slice)
+  const bool split_rows = rank != 0 || ncta == 1;
 
   if (tid == 0) {
     mbar_init(bar, 1);
@@ -1115,16 +1141,20 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
           if (t0 + q < T) wpart[warp * 8 + t0 + q] = ss[q];
     }
     __syncthreads();
-    if (tid < T) {
+    // 1 / rms of row t in lane t of every warp: each warp adds the warps'
+    // partials itself, so no second barrier
+    float ri_l = 0.f;
+    if (lane < T) {
       float tot = 0.f;
-      for (int w = 0; w < kRouteThreads / 32; ++w) tot = __fadd_rn(tot, wpart[w * 8 + tid]);
+      for (int w = 0; w < kRouteThreads / 32; ++w) tot = __fadd_rn(tot, wpart[w * 8 + lane]);
       const float var = __fdiv_rn(tot, static_cast<float>(D));
-      rinv[tid] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, A.eps)));
+      ri_l = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, A.eps)));
     }
-    __syncthreads();
     const uint4* wv = reinterpret_cast<const uint4*>(nw);
     for (int t0 = 0; t0 < T; t0 += 4) {
-      float mx[4] = {0.f, 0.f, 0.f, 0.f};
+      float mx[4] = {0.f, 0.f, 0.f, 0.f}, rq[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) rq[q] = __shfl_sync(0xffffffffu, ri_l, (t0 + q) & 31);
       for (int j = tid; j < nv; j += kRouteThreads) {
         float wf[8];
         bf16x8_unpack(wv[j], wf);
@@ -1132,34 +1162,37 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
         for (int q = 0; q < 4; ++q)
           if (t0 + q < T) {
             uint4* row = reinterpret_cast<uint4*>(xs + (t0 + q) * RS);
-            const float ri = rinv[t0 + q];
             float v[8];
             bf16x8_unpack(row[j], v);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(wf[k], __fmul_rn(v[k], ri));
+            for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(wf[k], __fmul_rn(v[k], rq[q]));
             const uint4 pk = bf16x8_pack(v);
             row[j] = pk;
-            bf16x8_unpack(pk, v);
+            if (split_rows) {
+              bf16x8_unpack(pk, v);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) mx[q] = fmaxf(mx[q], fabsf(v[k]));
+              for (int k = 0; k < 8; ++k) mx[q] = fmaxf(mx[q], fabsf(v[k]));
+            }
           }
       }
+      if (split_rows) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
+        for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) mx[q] = fmaxf(mx[q], __shfl_xor_sync(0xffffffffu, mx[q], o));
-      if (lane == 0)
+          for (int q = 0; q < 4; ++q) mx[q] = fmaxf(mx[q], __shfl_xor_sync(0xffffffffu, mx[q], o));
+        if (lane == 0)
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (t0 + q < T) wpart[warp * 8 + t0 + q] = mx[q];
+          for (int q = 0; q < 4; ++q)
+            if (t0 + q < T) wmax[warp * 8 + t0 + q] = mx[q];
+      }
     }
     __syncthreads();
-    if (tid < T) {
+    if (split_rows && tid < T) {
       float mx = 0.f;
-      for (int w = 0; w < kRouteThreads / 32; ++w) mx = fmaxf(mx, wpart[w * 8 + tid]);
+      for (int w = 0; w < kRouteThreads / 32; ++w) mx = fmaxf(mx, wmax[w * 8 + tid]);
       rowe[tid] = row_prescale(mx);
     }
-  } else if (warp < T) {  // rows arrive normed: the prescale from them, one warp per token
+  } else if (split_rows && warp < T) {  // rows arrive normed: the prescale from them, one warp per token
     const uint4* row = reinterpret_cast<const uint4*>(xs + warp * RS);
     float mx = 0.f;
     for (int v = lane; v < nv; v += 32) {
@@ -1177,15 +1210,11 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   const int nsplit = D / router::kKSplitCols;
   if (!hash && ok && warp < nsplit) {
     const int g = lane >> 2;
-    float s4[4];
+    float acc[4][4], s4[4];
+    router::logit_chunk4(gw + g * RS, gw + (g + 8) * RS, xs + (g < T ? g : 0) * RS, g < T,
+                         warp * router::kKSplitCols, acc);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float acc[4];
-      router::logit_chunk(gw + g * RS, gw + (g + 8) * RS, xs + (g < T ? g : 0) * RS, g < T,
-                          warp * router::kKSplitCols + q * 128, acc);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) s4[j] = q == 0 ? acc[j] : s4[j] + acc[j];
-    }
+    for (int j = 0; j < 4; ++j) s4[j] = ((acc[0][j] + acc[1][j]) + acc[2][j]) + acc[3][j];
 #pragma unroll
     for (int j = 0; j < 4; ++j) red[(warp * 32 + lane) * 4 + j] = s4[j];
   }
@@ -1207,7 +1236,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
 
   // ---- the normed rows and their hi/lo e4m3 split, column slice by slice: off
   // CTA 0's critical path (rank 1 also takes rank 0's slice) ----
-  if (rank != 0 || ncta == 1) {
+  if (split_rows) {
     const int cols = D / ncta;
     for (int sl = (rank == 1 ? 0 : rank); sl <= rank; ++sl) {
       const int c16 = sl * cols / 16;
@@ -1225,7 +1254,14 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
         }
       }
     }
-    if (rank != 0) return;
+    if ((rank == 1 || ncta == 1) && tid < T) {
+      P.sb1[tid] = static_cast<uint8_t>(127 - rowe[tid]);
+      P.tok_e[tid] = rowe[tid];
+    }
+    if (rank != 0) {
+      release_ready(P.ready);
+      return;
+    }
   }
 
   // ---- CTA 0: the router's top-k selection from the gathered keys ----
@@ -1269,10 +1305,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       A.idx_out[t * K + lane] = esel;
       A.w_out[t * K + lane] = wv;
     }
-  }
-  if (tid < T) {
-    P.sb1[tid] = static_cast<uint8_t>(127 - rowe[tid]);
-    P.tok_e[tid] = rowe[tid];
   }
   __syncthreads();
 
@@ -1343,6 +1375,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     P.hdr[1] = C;
     P.hdr[2] = 0;
   }
+  release_ready(P.ready);
 }
 
 // ---------------------------------------------------------------------------
@@ -1383,6 +1416,10 @@ struct UnitArgs {
   // down epilogue stores this rank's rows into every rank's receive buffer
   int ep_rank, ep_world;  // ep_world 0: off
   uint8_t* ep_recv[HS_EP_MAX_RANKS];
+  // token mode after the route kernel: its CTA count; the gate/up phase waits
+  // for P.ready to reach it and the down phase for each k-step's two units
+  // (P.done) instead of for the previous grid's completion. 0: grid waits.
+  int ready_target;
 };
 
 template <int NT, int BOXES, int NBSF = 1>
@@ -1460,7 +1497,7 @@ __device__ __forceinline__ Sched make_sched(const Desc& d, const UnitArgs& a, bo
   const int tiles_sh = down ? d.D / kM : (d.has_shared ? d.I_sh / kM : 0);
   const int tiles_rt = down ? d.D / kM : d.I / kM;
   s.n_sh_units = static_cast<int64_t>(a.n_sh_chunks) * tiles_sh;
-  s.n_rt_units = static_cast<int64_t>(a.P.hdr[0]) * tiles_rt;
+  s.n_rt_units = static_cast<int64_t>(__ldcg(a.P.hdr)) * tiles_rt;
   s.U = s.n_sh_units + s.n_rt_units;
   s.nk_sh = down ? (d.has_shared ? d.I_sh / 256 : 1) : d.D / 128;
   s.nk_rt = down ? d.I / 256 : d.D / 128;
@@ -1496,9 +1533,11 @@ __device__ __forceinline__ UnitInfo unit_info(const Desc& d, const UnitArgs& a, 
     r.shared = 0;
     r.chunk = c;
     r.tile = static_cast<int>(uu - static_cast<int64_t>(c) * tiles_rt);
-    r.e = a.P.chunk_expert[c];
-    r.pair0 = a.P.chunk_pair0[c];
-    r.np = a.P.chunk_np[c];
+    // through L2: after the route kernel the plan may come from a grid that is
+    // still running (a counter hand-off, not grid completion)
+    r.e = __ldcg(a.P.chunk_expert + c);
+    r.pair0 = __ldcg(a.P.chunk_pair0 + c);
+    r.np = __ldcg(a.P.chunk_np + c);
   }
   return r;
 }
@@ -1786,6 +1825,28 @@ __device__ __forceinline__ void peer_sum(const SchedT& sc, int c0, int cl, const
   }
 }
 
+// Bounded wait (one thread) until *ctr >= target, then an acquire fence and a
+// proxy fence, so this thread's later generic and async-proxy (TMA, bulk copy)
+// reads see what the writers released before their increments. False if the
+// wait gave up (HS_DEV_TIMEOUT reported).
+__device__ __forceinline__ bool wait_count(const uint32_t* ctr, uint32_t target, int32_t* status) {
+  bool ok = true;
+  if (ld_relaxed_gpu(ctr) < target) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+      if (ld_relaxed_gpu(ctr) >= target) break;
+      if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+        report(status, HS_DEV_TIMEOUT);
+        ok = false;
+        break;
+      }
+    }
+  }
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return ok;
+}
+
 // The 128 epilogue threads wait (bounded) until a unit's ticket reaches
 // target: thread 0 polls with acquire loads, the named barrier releases the rest.
 __device__ __forceinline__ void wait_ticket(const uint32_t* ctr, uint32_t target, int etid, int32_t* status) {
@@ -1812,7 +1873,7 @@ __device__ __forceinline__ void tok_weights(const UnitArgs& a, const UnitInfo& u
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     wbv[r] = 0.f;
-    if (r < a.T) wbv[r] = ui.shared ? 1.f : __ldg(a.P.ctab_wb + ui.chunk * 8 + r);
+    if (r < a.T) wbv[r] = ui.shared ? 1.f : __ldcg(a.P.ctab_wb + ui.chunk * 8 + r);
   }
 }
 
@@ -1948,8 +2009,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     }
   }
   // everything above overlaps the previous kernel; from here on the plan (and,
-  // for the down phase, the gate/up phase) is complete and visible
-  pdl_wait();
+  // for the down phase, the gate/up phase) is complete and visible: after the
+  // route kernel's CTAs have released their writes (token mode after the route
+  // kernel), else after the previous grid
+  if (kTok && !kDown && a.ready_target > 0) {
+    if (threadIdx.x == 0) (void)wait_count(a.P.ready, static_cast<uint32_t>(a.ready_target), a.status);
+  } else {
+    pdl_wait();
+  }
   pdl_trigger();
   tc5::fence_before_sync();
   __syncthreads();
@@ -1975,6 +2042,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
 
   if (warp == 4) {
     // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
+    if (kTok && a.ready_target > 0) asm volatile("fence.proxy.async.global;" ::: "memory");
     const uint64_t pol = l2_evict_first_policy();
     int64_t step = 0;
     bool ok = true;
@@ -2228,6 +2296,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
             gateup_finish_tok<true>(d, a, ui, row, g, v, wbv);
           else
             gateup_finish_tok<false>(d, a, ui, row, g, v, wbv);
+          if (a.ready_target > 0) {  // the unit's activations are complete: count them for the down phase
+            epi_bar();
+            if (etid == 0) {
+              const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
+              __threadfence();
+              atomicAdd(a.P.done + (ui.shared ? 0 : 1 + ui.chunk) * (I_act / 256) + ui.tile / 2, 1u);
+            }
+          }
         } else if (!kDown) {
           if (ui.shared)
             gateup_finish<NT, true>(d, a, ui, row, g, v);
@@ -2504,8 +2580,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
       }
     }
   }
-  pdl_wait();  // the gate/up phase's activations are complete
+  // the gate/up phase's activations: after its whole grid, or (token mode
+  // after the route kernel) per k-step, once both units it reads are counted
+  const bool per_step = a.ready_target > 0;
+  if (!per_step) pdl_wait();
+  // every gate/up CTA saw the ready count before this grid could start: reset
+  // it for the next call, before this CTA lets the next kernel launch (the
+  // next call's gate/up phase starts after the next route kernel, which starts
+  // after every CTA here has triggered)
+  if (per_step && c == 0 && threadIdx.x == 0) {
+    *reinterpret_cast<volatile uint32_t*>(a.P.ready) = 0u;
+    __threadfence();
+  }
   pdl_trigger();
+  auto act_ready = [&](const Step& q) {  // lane 0 of the producer
+    if (!per_step) return true;
+    const int slot = q.shared ? 0 : 1 + q.ch;
+    return wait_count(a.P.done + slot * (I_act / 256) + q.kk, 2u, a.status);
+  };
 
   if (warp == 4) {
     // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
@@ -2513,6 +2605,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     for (; step < npre; ++step) {
       const Step q = decode(s_begin + step);
       if (lane == 0) {
+        (void)act_ready(q);
         issue_act(static_cast<int>(step), q);
         mbar_arrive(&bars->full[step]);
       }
@@ -2533,6 +2626,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
       if (lane == 0) {
         mbar_arrive_expect_tx(&bars->full[st], tx_of(q));
         issue_weights(st, q);
+        (void)act_ready(q);
         issue_act(st, q);
       }
       __syncwarp();
@@ -3622,7 +3716,7 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   pa.po = PermuteOut{nullptr, nullptr, nullptr};
   pa.status = dev_status;
   pa.ucount = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + g.off_ucount);
-  pa.n_ucount = g.U_gu + g.U_dn;
+  pa.n_ucount = g.U_gu + g.U_dn + g.n_done;  // the ready counter is the down phase's to reset
   pa.seg_lrank = pa.seg_off = pa.seg_base = nullptr;
   int32_t* seg_ws = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + g.off_seg);
   const int nseg = static_cast<int>((npairs + kSegPairs - 1) / kSegPairs);
@@ -3673,6 +3767,9 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
 
   UnitArgs a;
   a.ncl = 0;
+  // after the route kernel (token mode), the kernels hand over through the
+  // plan's counters: the gate/up phase waits for the route kernel's CTAs
+  a.ready_target = route && tok ? static_cast<int>(route->num_experts / 16) : 0;
   a.w_sh = tok && use_shared ? 1 : 2;  // token mode prefetches the shared expert into L2
   a.ext_combine = T > kInlineCombineMax ? 1 : 0;
   a.ep_rank = 0;
@@ -3703,11 +3800,17 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   a.act_rows = g.act_rows;
   a.ucount = pa.ucount;
   if (tok) {
-    if ((rc = launch_sk<false, 1, true>(d, cm, a, st))) return rc;
+    // a launch that fails after the route kernel leaves its ready count set:
+    // clear it, or the next call's gate/up phase would not wait
+    auto clear_ready = [&](int r) {
+      if (r && a.ready_target > 0) (void)cudaMemsetAsync(P.ready, 0, sizeof(uint32_t), st);
+      return r;
+    };
+    if ((rc = launch_sk<false, 1, true>(d, cm, a, st))) return clear_ready(rc);
     a.ucount = pa.ucount + g.U_gu;
-    if (a.ep_world == 0) return launch_tok_down(d, cm, a, st);
+    if (a.ep_world == 0) return clear_ready(launch_tok_down(d, cm, a, st));
     int gdown = 0;
-    if ((rc = launch_tok_down(d, cm, a, st, &gdown))) return rc;
+    if ((rc = launch_tok_down(d, cm, a, st, &gdown))) return clear_ready(rc);
     (void)gdown;
     const int64_t n = T * d.D;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64));

@@ -34,6 +34,34 @@ __device__ __forceinline__ void logit_chunk(const __nv_bfloat16* alo, const __nv
   }
 }
 
+// The four 128-column quarters [kw + 128 q, kw + 128 q + 128) of one k-split
+// at once: quarter q's accumulator gets exactly logit_chunk's MMAs in
+// logit_chunk's order, but the four quarters' MMAs alternate, so four
+// independent accumulator chains are in flight instead of one.
+__device__ __forceinline__ void logit_chunk4(const __nv_bfloat16* alo, const __nv_bfloat16* ahi,
+                                             const __nv_bfloat16* brow, bool tv, int kw, float (&acc)[4][4]) {
+  const int c = threadIdx.x & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[q][j] = 0.f;
+#pragma unroll
+  for (int k = 0; k < kKSplitCols / kWarps; k += 32) {
+    uint4 al[4], ah[4], bv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int kk = kw + q * (kKSplitCols / kWarps) + k + 8 * c;
+      al[q] = *reinterpret_cast<const uint4*>(alo + kk);
+      ah[q] = *reinterpret_cast<const uint4*>(ahi + kk);
+      bv[q] = tv ? *reinterpret_cast<const uint4*>(brow + kk) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mma_bf16(acc[q], al[q].x, ah[q].x, al[q].y, ah[q].y, bv[q].x, bv[q].y);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mma_bf16(acc[q], al[q].z, ah[q].z, al[q].w, ah[q].w, bv[q].z, bv[q].w);
+  }
+}
+
 __device__ __forceinline__ uint64_t score_key(float s, int e) {
   const uint32_t hi = isnan(s) ? 0xffffffffu : __float_as_uint(s);  // s >= 0 (or NaN)
   return (static_cast<uint64_t>(hi) << 32) | static_cast<uint64_t>(0xffffffffu - static_cast<uint32_t>(e));
