@@ -404,12 +404,16 @@ def run_moe_only(args):
 
 
 def run_moe_ep(args):
-    """Config-3 class MoE microbenchmark: T tokens (sharded T/n per rank) through
-    `args.layers` layers of the config-0 shape with TokenShardedEP over the
-    torchrun ranks (NCCL all-to-all dispatch, FP4 kernels on the received rows,
-    combine). Each rank holds its 256/n routed experts and the whole shared
-    expert, random-init. Prints ms per layer call, the max over ranks of CUDA
-    event time around `reps` calls."""
+    """Config 3, the MoE half: an 8192-token prompt (T tokens, sharded T/n per
+    rank) through `args.layers` layers of the config-0 shape (43 = the model)
+    with token-sharded expert parallelism over the torchrun ranks: each rank
+    holds its 256/n routed experts of every layer and the whole shared expert
+    (random init), and every layer call dispatches rows to the experts' ranks
+    and combines the results (--ep-impl torch: TokenShardedEP, torch.distributed
+    all-to-all; c: hs_ep_dispatch_combine, one C-ABI call over NCCL). One pass
+    calls every layer once; `reps` passes are timed (after one untimed pass).
+    Prints the ms per layer call and per pass, the max over ranks of CUDA event
+    time. Attention is not in this build's step."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -434,28 +438,42 @@ def run_moe_ep(args):
         Tl = args.T // world
         g = torch.Generator(device=dev).manual_seed(5 + rank)
         calls = []
-        for i in range(max(args.reps, 1)):
-            l = i % args.layers
+        for l in range(args.layers):  # one pass: every layer once, its own rows and routing
             h = torch.randn(Tl, 4096, generator=g, device=dev).to(torch.bfloat16)
             idx, w = ops.router_topk(h, store.layers[l].gate, store.layers[l].bias, 6, 1.5)
             calls.append((l, h, idx, w))
-        ep = TokenShardedEP(rank, world)
-        for c in calls[:3]:
+        if args.ep_impl == "c":
+            from home_seek_b200.ep import NcclTokenShardedEP
+            ep = NcclTokenShardedEP(rank, world, Tl)
+        else:
+            ep = TokenShardedEP(rank, world)
+        for c in calls:  # untimed pass
             ep.moe(store, c[0], c[1], c[2], c[3])
         torch.cuda.synchronize()
         dist.barrier()
+        flag = torch.ones(1, device=dev)
+        dist.all_reduce(flag)  # a common start on the device
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        passes = max(args.reps // max(args.layers, 1), 1)
         a.record()
-        for c in calls:
-            ep.moe(store, c[0], c[1], c[2], c[3])
+        for _ in range(passes):
+            for c in calls:
+                ep.moe(store, c[0], c[1], c[2], c[3])
         b.record()
         torch.cuda.synchronize()
-        ms = torch.tensor([a.elapsed_time(b) / len(calls)], device=dev)
+        ms = torch.tensor([a.elapsed_time(b) / passes], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        if args.ep_impl == "c":
+            ep.close()
         if rank == 0:
             print(json.dumps({"mode": "moe-ep", "T": Tl * world, "tokens_per_rank": Tl, "world": world,
-                              "layers": args.layers, "calls": len(calls), "ms_per_layer": float(ms.item()),
-                              "scheme": "token-sharded dispatch/combine (NCCL all-to-all)"}), flush=True)
+                              "layers": args.layers, "passes": passes, "ms_per_pass": float(ms.item()),
+                              "ms_per_layer": float(ms.item()) / args.layers,
+                              "tokens_per_s": Tl * world / (float(ms.item()) * 1e-3),
+                              "ep_impl": args.ep_impl,
+                              "scheme": "token-sharded dispatch/combine (" + (
+                                  "hs_ep_dispatch_combine: NCCL send/recv inside the C-ABI call)"
+                                  if args.ep_impl == "c" else "torch.distributed all-to-all)")}), flush=True)
         return 0
     finally:
         dist.destroy_process_group()
@@ -717,6 +735,8 @@ def main():
                          "prefill-size MoE with the tokens sharded over the torchrun ranks (TokenShardedEP); "
                          "accept: config-4 acceptance kernels; head: lm_head GEMV + fused argmax")
     ap.add_argument("--T", type=int, default=3, help="tokens per MoE call in --mode moe")
+    ap.add_argument("--ep-impl", default="torch", choices=["torch", "c"],
+                    help="--mode moe-ep: TokenShardedEP (torch) or hs_ep_dispatch_combine (c)")
     ap.add_argument("--reps", type=int, default=20, help="MoE calls timed in --mode moe")
     ap.add_argument("--fused", action="store_true", help="--mode moe: router folded into the call (T <= 8)")
     ap.add_argument("--layer", action="store_true",

@@ -2014,6 +2014,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   // kernel), else after the previous grid
   if (kTok && !kDown && a.ready_target > 0) {
     if (threadIdx.x == 0) (void)wait_count(a.P.ready, static_cast<uint32_t>(a.ready_target), a.status);
+    __syncthreads();  // no thread lets the down phase launch before the route kernel's writes are seen
   } else {
     pdl_wait();
   }
@@ -2588,9 +2589,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   // it for the next call, before this CTA lets the next kernel launch (the
   // next call's gate/up phase starts after the next route kernel, which starts
   // after every CTA here has triggered)
-  if (per_step && c == 0 && threadIdx.x == 0) {
-    *reinterpret_cast<volatile uint32_t*>(a.P.ready) = 0u;
-    __threadfence();
+  if (per_step && c == 0) {
+    if (threadIdx.x == 0) {
+      *reinterpret_cast<volatile uint32_t*>(a.P.ready) = 0u;
+      __threadfence();
+    }
+    __syncthreads();  // the reset precedes every trigger of this CTA
   }
   pdl_trigger();
   auto act_ready = [&](const Step& q) {  // lane 0 of the producer
