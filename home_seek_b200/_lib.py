@@ -115,6 +115,9 @@ SIGNATURES = {
                                     c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int, c_int, c_void_p,
                                     c_void_p, c_void_p, POINTER(HsEpPeers), c_void_p, c_void_p, c_size_t, c_void_p,
                                     c_void_p]),
+    "hs_lm_head_argmax_ep": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                                     c_void_p, c_void_p, c_void_p, POINTER(HsEpPeers), c_void_p, c_size_t, c_void_p,
+                                     c_void_p]),
     "hs_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p]),
     "hs_moe_combine_add_rms_norm": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_float, c_int64, c_int64,
                                             c_void_p, c_void_p, c_void_p]),

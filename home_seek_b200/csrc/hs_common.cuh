@@ -63,6 +63,44 @@ HS_DI uint32_t ld_relaxed_gpu(const uint32_t* p) {
 // which the kernel reports HS_DEV_TIMEOUT and returns.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Receive buffer of the peer-memory expert-parallel exchange (one per rank,
+// every rank's mapped in every process): a 256-byte header of u64 words ([0]
+// MoE calls made, [1] MoE combine ticket, [2] MoE exchange poisoned, [3]
+// lm_head calls made, [4] lm_head exchange poisoned), then two slots (calls
+// alternate) of [world][routed, shared][8 tokens][D] f32 MoE rows, then two
+// slots of [HS_EP_MAX_RANKS][16 tokens] u64 lm_head keys. A rank's call k
+// writes slot k % 2 of every rank; rank q's call k+2 can only start after
+// every rank finished call k+1 and so consumed slot k % 2. An empty entry
+// holds all ones (for the rows a NaN bit pattern the sums never produce: their
+// NaNs are the canonical 0x7fffffff; no key is all ones), so an entry is its
+// own arrival flag: the producer only stores, the consumer waits for every
+// entry it reads to be filled and sets it back to empty.
+namespace epx {
+constexpr int64_t kHdr = 256;
+constexpr int kPoison = 2;      // header word set once a MoE combine's wait ran out
+constexpr int kHeadCalls = 3;   // header word: lm_head exchanges made
+constexpr int kHeadPoison = 4;  // header word set once an lm_head exchange's wait ran out
+constexpr uint32_t kEmpty = 0xffffffffu;
+constexpr unsigned long long kEmptyKey = 0xffffffffffffffffull;
+constexpr int kRows = 8;
+constexpr int kHeadTokens = 16;
+__host__ __device__ inline float* rows(uint8_t* buf, int slot, int world, int src, int which, int D) {
+  return reinterpret_cast<float*>(buf + kHdr) +
+         ((static_cast<int64_t>(slot) * world + src) * 2 + which) * kRows * static_cast<int64_t>(D);
+}
+__host__ __device__ inline int64_t rows_bytes(int64_t world, int64_t D) {
+  return 2 * world * 2 * kRows * D * static_cast<int64_t>(sizeof(float));
+}
+__host__ __device__ inline unsigned long long* head_keys(uint8_t* buf, int slot, int world, int src, int D) {
+  return reinterpret_cast<unsigned long long*>(buf + kHdr + rows_bytes(world, D)) +
+         (static_cast<int64_t>(slot) * HS_EP_MAX_RANKS + src) * kHeadTokens;
+}
+inline size_t bytes(int64_t world, int64_t D) {
+  return static_cast<size_t>(kHdr + rows_bytes(world, D) +
+                             2 * HS_EP_MAX_RANKS * kHeadTokens * static_cast<int64_t>(sizeof(unsigned long long)));
+}
+}  // namespace epx
+
 // ---------------------------------------------------------------------------
 // Device: mbarrier
 // ---------------------------------------------------------------------------

@@ -56,6 +56,7 @@ static_assert(sizeof(Bars) <= kBarBytes, "barrier block");
 
 struct Args {
   int T, D, V, ntiles;
+  int row0, rows;                  // the head rows streamed: [row0, row0 + rows) of the V (keys carry the global index)
   const int64_t* draft_ids;        // [T - 1] or nullptr
   int64_t* argmax_out;             // [T] or nullptr
   int32_t* n_accept;               // [1] or nullptr
@@ -64,6 +65,12 @@ struct Args {
   unsigned long long* part;        // [gridDim.x][kPartStride] per-CTA best keys
   uint32_t* ticket;                // left at zero by every call
   int32_t* status;
+  // vocab split over an expert-parallel group (ep_world 0: one GPU): every
+  // rank's exchange buffer as mapped here, this rank, the hidden size that
+  // places the key region, the bound of the wait for the peers' keys
+  uint8_t* ep_buf[HS_EP_MAX_RANKS];
+  int ep_rank, ep_world, ep_D;
+  uint64_t wait_ns;
 };
 
 // Ordered key of a bf16 logit at vocab index v: larger key = larger value,
@@ -114,6 +121,61 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t tmem_d, uint64_t adesc, uin
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Vocab split over an expert-parallel group, in the last CTA's 128 epilogue
+// threads: thread t < T stores this rank's best key of token t into slot
+// (calls & 1) of every rank's exchange buffer, waits (bounded) until every
+// rank's key of token t has arrived in its own buffer, keeps the best (the
+// same on every rank: the key order is total) and empties the entries; then
+// thread 0 advances the call counter. A wait that runs out poisons the local
+// buffer (every later exchange on it reports HS_DEV_TIMEOUT at once and stores
+// nothing) and leaves the counter, so late keys land in a slot no later call
+// reads.
+__device__ __forceinline__ void exchange_keys(const Args& a, unsigned long long* key, int T) {
+  uint8_t* mine = a.ep_buf[a.ep_rank];
+  volatile unsigned long long* hdr = reinterpret_cast<volatile unsigned long long*>(mine);
+  const unsigned long long calls = hdr[epx::kHeadCalls];
+  const int slot = static_cast<int>(calls & 1ull);
+  const bool poisoned = hdr[epx::kHeadPoison] != 0ull;
+  const int t = threadIdx.x;
+  bool ok = !poisoned;
+  unsigned long long best = 0ull;
+  if (t < T && ok) {
+    const unsigned long long k = key[t];
+    for (int q = 0; q < a.ep_world; ++q)
+      reinterpret_cast<volatile unsigned long long*>(epx::head_keys(a.ep_buf[q], slot, a.ep_world, a.ep_rank,
+                                                                    a.ep_D))[t] = k;
+    for (int q = 0; q < a.ep_world && ok; ++q) {
+      volatile unsigned long long* e = epx::head_keys(mine, slot, a.ep_world, q, a.ep_D) + t;
+      unsigned long long v = *e;
+      if (v == epx::kEmptyKey) {
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t it = 1; v == epx::kEmptyKey; ++it) {
+          v = *e;
+          if ((it & 63u) == 0 && (globaltimer_ns() - t0 > a.wait_ns || hdr[epx::kHeadPoison] != 0ull)) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      if (ok) {
+        best = v > best ? v : best;
+        *e = epx::kEmptyKey;
+      }
+    }
+  }
+  if (t < T) {
+    key[t] = ok ? best : 0ull;
+    if (!ok) {
+      report(a.status, HS_DEV_TIMEOUT);
+      hdr[epx::kHeadPoison] = 1ull;
+    }
+  }
+  __threadfence();
+  epi_bar();
+  if (t == 0 && hdr[epx::kHeadPoison] == 0ull) hdr[epx::kHeadCalls] = calls + 1ull;
+  epi_bar();
+}
+
 __global__ void __launch_bounds__(kThreads, 1) head_argmax_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                                   const __grid_constant__ CUtensorMap tm_x, Args a) {
   extern __shared__ uint8_t smem_raw[];
@@ -122,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) head_argmax_kernel(const __grid_c
   __shared__ unsigned long long wbest[4][kN];
   __shared__ int s_last;
   __shared__ int s_am[kN];
+  __shared__ unsigned long long s_key[kN];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x, G = gridDim.x;
   const int nk = a.D / kKBox;
@@ -243,14 +306,14 @@ __global__ void __launch_bounds__(kThreads, 1) head_argmax_kernel(const __grid_c
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
       const int row = tile * kM + 32 * warp + lane;
-      const bool inside = row < a.V;
+      const bool inside = row < a.rows;
 #pragma unroll
       for (int t = 0; t < kN; ++t) {
         if (t < T) {
           const __nv_bfloat16 lb = __float2bfloat16_rn(v[t]);
           const uint32_t b16 = __bfloat16_as_ushort(lb);
           if (inside && a.logits) a.logits[static_cast<int64_t>(t) * a.V + row] = lb;
-          const unsigned long long k = inside ? logit_key(b16, row) : 0ull;
+          const unsigned long long k = inside ? logit_key(b16, a.row0 + row) : 0ull;
           const unsigned long long wk = warp_max_key(k);
           best[t] = wk > best[t] ? wk : best[t];
         }
@@ -280,11 +343,15 @@ __global__ void __launch_bounds__(kThreads, 1) head_argmax_kernel(const __grid_c
           k = q > k ? q : k;
         }
         k = warp_max_key(k);
-        if (lane == 0) {
-          const int am = k ? key_index(k) : 0;
-          s_am[t] = am;
-          if (a.argmax_out) a.argmax_out[t] = am;
-        }
+        if (lane == 0) s_key[t] = k;
+      }
+      epi_bar();
+      if (a.ep_world > 0) exchange_keys(a, s_key, T);  // every rank's best of its rows
+      if (threadIdx.x < T) {
+        const unsigned long long k = s_key[threadIdx.x];
+        const int am = k ? key_index(k) : 0;
+        s_am[threadIdx.x] = am;
+        if (a.argmax_out) a.argmax_out[threadIdx.x] = am;
       }
       epi_bar();
       if (threadIdx.x == 0) {
@@ -386,20 +453,28 @@ extern "C" size_t hs_lm_head_workspace_size(int64_t T) {
   return static_cast<size_t>(256 + static_cast<int64_t>(sm_count()) * kPartStride * 8);
 }
 
-extern "C" int hs_lm_head_argmax(const void* x, const void* head, int64_t T, int64_t D, int64_t V,
-                                 const int64_t* draft_ids, int64_t* argmax_out, int32_t* n_accept,
-                                 int64_t* next_token, void* logits_out, void* workspace, size_t workspace_bytes,
-                                 int32_t* dev_status, void* stream) {
+static int head_impl(const void* x, const void* head, int64_t T, int64_t D, int64_t V, int64_t row0, int64_t rows,
+                     const int64_t* draft_ids, int64_t* argmax_out, int32_t* n_accept, int64_t* next_token,
+                     void* logits_out, const hs_ep_peers* peers, void* workspace, size_t workspace_bytes,
+                     int32_t* dev_status, void* stream) {
   if (!x || !head || !workspace) return HS_ERR_BAD_ARGUMENT;
   if (T < 1 || T > kN || D < kKBox || D % kKBox || D > 65536 || V < 1 || V > (int64_t{1} << 30))
     return HS_ERR_BAD_SHAPE;
+  if (row0 < 0 || rows < 1 || row0 + rows > V) return HS_ERR_BAD_SHAPE;
   if (!argmax_out && !n_accept && !next_token && !logits_out) return HS_ERR_BAD_ARGUMENT;
   if (!aligned16(x) || !aligned16(head) || !aligned16(workspace) || (logits_out && (V % 8 || !aligned16(logits_out))))
     return HS_ERR_ALIGN;
   if (workspace_bytes < hs_lm_head_workspace_size(T)) return HS_ERR_WORKSPACE;
+  if (peers) {
+    if (logits_out || peers->world < 1 || peers->world > HS_EP_MAX_RANKS || peers->rank < 0 ||
+        peers->rank >= peers->world || D > 8192)
+      return HS_ERR_BAD_ARGUMENT;
+    for (int q = 0; q < peers->world; ++q)
+      if (!peers->recv[q] || !aligned16(peers->recv[q])) return HS_ERR_BAD_ARGUMENT;
+  }
   CUtensorMap tm_w, tm_x;
   int rc;
-  if ((rc = bf16_map(&tm_w, head, static_cast<uint64_t>(D), static_cast<uint64_t>(V), kM))) return rc;
+  if ((rc = bf16_map(&tm_w, head, static_cast<uint64_t>(D), static_cast<uint64_t>(rows), kM))) return rc;
   if ((rc = bf16_map(&tm_x, x, static_cast<uint64_t>(D), static_cast<uint64_t>(T), kN))) return rc;
   static std::atomic<uint64_t> done{0};
   int dev = 0;
@@ -413,7 +488,9 @@ extern "C" int hs_lm_head_argmax(const void* x, const void* head, int64_t T, int
   a.T = static_cast<int>(T);
   a.D = static_cast<int>(D);
   a.V = static_cast<int>(V);
-  a.ntiles = static_cast<int>((V + kM - 1) / kM);
+  a.row0 = static_cast<int>(row0);
+  a.rows = static_cast<int>(rows);
+  a.ntiles = static_cast<int>((rows + kM - 1) / kM);
   a.draft_ids = T > 1 ? draft_ids : nullptr;
   a.argmax_out = argmax_out;
   a.n_accept = n_accept;
@@ -422,8 +499,31 @@ extern "C" int hs_lm_head_argmax(const void* x, const void* head, int64_t T, int
   a.ticket = static_cast<uint32_t*>(workspace);
   a.part = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) + 256);
   a.status = dev_status;
+  a.ep_rank = peers ? peers->rank : 0;
+  a.ep_world = peers ? peers->world : 0;
+  a.ep_D = static_cast<int>(D);
+  a.wait_ns = peers && peers->wait_limit_ns > 0 ? static_cast<uint64_t>(peers->wait_limit_ns) : kWaitLimitNs;
+  for (int q = 0; q < HS_EP_MAX_RANKS; ++q)
+    a.ep_buf[q] = peers && q < peers->world ? static_cast<uint8_t*>(peers->recv[q]) : nullptr;
   const int G = std::min(sm_count(), a.ntiles);
   HS_CUDA_CHECK(launch_pdl(head_argmax_kernel, dim3(static_cast<unsigned>(G)), dim3(kThreads), kSmemBytes,
                            static_cast<cudaStream_t>(stream), tm_w, tm_x, a));
   return check_launch();
+}
+
+extern "C" int hs_lm_head_argmax(const void* x, const void* head, int64_t T, int64_t D, int64_t V,
+                                 const int64_t* draft_ids, int64_t* argmax_out, int32_t* n_accept,
+                                 int64_t* next_token, void* logits_out, void* workspace, size_t workspace_bytes,
+                                 int32_t* dev_status, void* stream) {
+  return head_impl(x, head, T, D, V, 0, V, draft_ids, argmax_out, n_accept, next_token, logits_out, nullptr,
+                   workspace, workspace_bytes, dev_status, stream);
+}
+
+extern "C" int hs_lm_head_argmax_ep(const void* x, const void* head_rows, int64_t T, int64_t D, int64_t V,
+                                    int64_t row0, int64_t rows, const int64_t* draft_ids, int64_t* argmax_out,
+                                    int32_t* n_accept, int64_t* next_token, const hs_ep_peers* peers,
+                                    void* workspace, size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  if (!peers) return HS_ERR_BAD_ARGUMENT;
+  return head_impl(x, head_rows, T, D, V, row0, rows, draft_ids, argmax_out, n_accept, next_token, nullptr, peers,
+                   workspace, workspace_bytes, dev_status, stream);
 }

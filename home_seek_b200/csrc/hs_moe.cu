@@ -74,28 +74,6 @@ constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two indepen
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
 constexpr int kTokDownPad = 256;        // token-mode down kernel: read-only slack after its last stage
 
-// Receive buffer of the peer-memory expert-parallel exchange: a 256-byte
-// header ([0] calls made, [1] combine ticket, [2] poisoned, u64) and two slots (calls
-// alternate) of [world][routed, shared][8 tokens][D] f32 rows. A rank's call k
-// writes slot k % 2 of every rank; rank q's call k+2 can only start after
-// every rank finished call k+1 and so consumed slot k % 2. An empty entry
-// holds kEmpty (a NaN bit pattern the sums never produce: their NaNs are the
-// canonical 0x7fffffff), so a row entry is its own arrival flag: the producer
-// only stores, the consumer waits for every entry it reads to be filled and
-// sets it back to kEmpty.
-namespace epx {
-constexpr int64_t kHdr = 256;
-constexpr int kPoison = 2;  // header word set once a combine's wait ran out
-constexpr uint32_t kEmpty = 0xffffffffu;
-constexpr int kRows = 8;
-__host__ __device__ inline float* rows(uint8_t* buf, int slot, int world, int src, int which, int D) {
-  return reinterpret_cast<float*>(buf + kHdr) +
-         ((static_cast<int64_t>(slot) * world + src) * 2 + which) * kRows * static_cast<int64_t>(D);
-}
-inline size_t bytes(int64_t world, int64_t D) {
-  return static_cast<size_t>(kHdr + 2 * world * 2 * kRows * D * static_cast<int64_t>(sizeof(float)));
-}
-}  // namespace epx
 
 struct __align__(64) Desc {
   // Weight tiles as rows of 128 values: [tiles * 128 rows][128], box 128 x 256

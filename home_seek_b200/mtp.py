@@ -217,7 +217,11 @@ class MoEPathModel:
     def greedy(self, x_normed: torch.Tensor, draft_ids: Optional[torch.Tensor] = None):
         """lm_head + argmax in one kernel (the logits never leave the chip):
         returns (argmax [T], n_accept [1], next_token [1]); with draft_ids the
-        verify pass's greedy acceptance (engine.py:2485-2497)."""
+        verify pass's greedy acceptance (engine.py:2485-2497). Under expert
+        parallelism over peer memory the vocabulary is split over the group
+        as well (every rank streams 1/n of the head; the same results)."""
+        if self.ep is not None and self.ep.peers is not None:
+            return ops.lm_head_argmax_ep(x_normed, self.lm_head, self.ep.peers.peers, draft_ids=draft_ids)
         return ops.lm_head_argmax(x_normed, self.lm_head, draft_ids=draft_ids)
 
     def draft(self, h_last: torch.Tensor, tok: torch.Tensor) -> torch.Tensor:

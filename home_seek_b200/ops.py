@@ -23,7 +23,8 @@ _KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_mo
             "hs_rms_norm": 1, "hs_add_rms_norm": 1, "hs_moe_ffn_fp4_partials": 3, "hs_moe_combine": 1,
             "hs_moe_route_ffn_fp4": 3, "hs_moe_route_ffn_fp4_partials": 3,
             "hs_moe_combine_add_rms_norm": 1, "hs_moe_layer_fp4": 3, "hs_moe_layer_fp4_partials": 3,
-            "hs_moe_layer_fp4_ep": 4, "hs_lm_head_argmax": 1}
+            "hs_moe_layer_fp4_ep": 4, "hs_lm_head_argmax": 1,
+            "hs_lm_head_argmax_ep": 1}
 
 
 def _launch(name: str, *args, extra: int = 0) -> None:
@@ -489,6 +490,48 @@ def lm_head_argmax(x: torch.Tensor, head: torch.Tensor, draft_ids: Optional[torc
     _launch("hs_lm_head_argmax", x.data_ptr(), head.data_ptr(), T, D, V, _ptr(ids), am.data_ptr(), n.data_ptr(),
             nxt.data_ptr(), _ptr(lg), ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(), _stream(dev))
     return (am, n, nxt, lg) if want_logits else (am, n, nxt)
+
+
+def vocab_rows(V: int, rank: int, world: int) -> tuple[int, int]:
+    """(row0, rows) of the head that rank `rank` of `world` streams in
+    lm_head_argmax_ep: whole 128-row tiles, split as evenly as they go."""
+    tiles = (V + 127) // 128
+    lo, hi = tiles * rank // world * 128, tiles * (rank + 1) // world * 128
+    return lo, min(hi, V) - lo
+
+
+def lm_head_argmax_ep(x: torch.Tensor, head: torch.Tensor, peers: "_lib.HsEpPeers",
+                      draft_ids: Optional[torch.Tensor] = None, out: Optional[tuple] = None):
+    """lm_head_argmax with the vocabulary split over an expert-parallel group
+    (hs_lm_head_argmax_ep): head is the whole [V, D] head (every rank holds
+    it); this rank streams its rows (vocab_rows) and the ranks exchange their
+    best keys through the peer buffers, so every rank returns the results of
+    lm_head_argmax on the whole head. Every rank must make the same calls."""
+    dev = _check_cuda(x, head, draft_ids)
+    x = _rows(x, "x")
+    head = _rows(head, "head")
+    T, D = x.shape
+    V = head.shape[0]
+    if head.shape[1] != D:
+        raise ValueError(f"head has {head.shape[1]} columns, rows have {D}")
+    row0, rows = vocab_rows(V, peers.rank, peers.world)
+    ids = None
+    if draft_ids is not None:
+        ids = draft_ids.reshape(-1).to(torch.int64).contiguous()
+        if ids.numel() != T - 1:
+            raise ValueError(f"{ids.numel()} draft ids for {T} rows")
+    if out is None:
+        am = torch.empty(T, dtype=torch.int64, device=dev)
+        n = torch.empty(1, dtype=torch.int32, device=dev)
+        nxt = torch.empty(1, dtype=torch.int64, device=dev)
+    else:
+        am, n, nxt = out
+    lib = _lib.load()
+    ws = workspace(dev, lib.hs_lm_head_workspace_size(T), "head")
+    _launch("hs_lm_head_argmax_ep", x.data_ptr(), head[row0:].data_ptr(), T, D, V, row0, rows, _ptr(ids),
+            am.data_ptr(), n.data_ptr(), nxt.data_ptr(), ctypes.byref(peers), ws.data_ptr(), ws.numel(),
+            status_word(dev).data_ptr(), _stream(dev))
+    return am, n, nxt
 
 
 # --- RMSNorm / residual add + RMSNorm ---------------------------------------------

@@ -411,6 +411,23 @@ int hs_moe_layer_fp4_ep(const void* desc, const void* h, const void* norm_w,
                         const hs_ep_peers* peers, void* h_out, void* workspace,
                         size_t workspace_bytes, int32_t* dev_status,
                         void* stream);
+/* hs_lm_head_argmax_ep: hs_lm_head_argmax with the vocabulary split over the */
+/* same group (no counterpart in the reference, whose lm_head runs on one      */
+/* GPU). head_rows points at rows [row0, row0 + rows) of the [V][D] head: this */
+/* rank streams only those, finds each token's best (bf16 logit, first index) */
+/* over them (global indices), stores those T keys into every rank's exchange */
+/* buffer and waits (bounded, as the MoE combine: HS_DEV_TIMEOUT and a poison */
+/* word on expiry) for every rank's, so argmax_out, n_accept and next_token   */
+/* are those of hs_lm_head_argmax on the whole head, on every rank. Every     */
+/* rank makes the same calls; the rows of the ranks tile [0, V). No logits    */
+/* output; T <= 16, D <= 8192.                                                 */
+int hs_lm_head_argmax_ep(const void* x, const void* head_rows, int64_t T,
+                         int64_t D, int64_t V, int64_t row0, int64_t rows,
+                         const int64_t* draft_ids, int64_t* argmax_out,
+                         int32_t* n_accept, int64_t* next_token,
+                         const hs_ep_peers* peers, void* workspace,
+                         size_t workspace_bytes, int32_t* dev_status,
+                         void* stream);
 int hs_moe_combine(const float* routed_f32, const float* shared_f32,
                    int use_shared, int64_t T, int64_t D, void* out,
                    void* stream);
