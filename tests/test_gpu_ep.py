@@ -154,11 +154,27 @@ def _p2p_rank(rank: int, world: int, port: int, q) -> None:
             d = (h_ep.float() - h_ref.float()).abs().max().item() / h_ref.float().abs().max().item()
             worst = max(worst, d)
             h_ep.copy_(h_ref)  # next call from the same input on both paths
+        # the vocabulary split lm_head over the same buffers: three calls (both
+        # key slots used, one twice), each equal to the whole-head call
+        head_same = True
+        w = (torch.randn(129280, 4096, generator=torch.Generator(device=dev).manual_seed(8), device=dev)
+             * 0.02).to(torch.bfloat16)
+        for T in (3, 1, 3):
+            x = torch.randn(T, 4096, generator=g, device=dev).to(torch.bfloat16)
+            dist.broadcast(x, src=0)
+            drafts = None
+            if T == 3:
+                am = ops.lm_head_argmax(x, w)[0]
+                drafts = torch.stack([am[0], (am[1] + 1) % 129280])
+            ref = ops.lm_head_argmax(x, w, draft_ids=drafts)
+            got = ops.lm_head_argmax_ep(x, w, px.peers, draft_ids=drafts)
+            torch.cuda.synchronize()
+            head_same = head_same and all(torch.equal(a, b) for a, b in zip(got, ref))
         status = ops.check_status(dev)
         gathered = [torch.empty_like(h_ep) for _ in range(world)]
         dist.all_gather(gathered, h_ep)
         same = all(torch.equal(gathered[0], x) for x in gathered)
-        q.put((rank, worst, status, same))
+        q.put((rank, worst, status, same and head_same))
     finally:
         if px is not None:
             px.close()
