@@ -1812,6 +1812,7 @@ __device__ __forceinline__ bool wait_count(const uint32_t* ctr, uint32_t target,
   if (ld_relaxed_gpu(ctr) < target) {
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
+      __nanosleep(64);  // hundreds of CTAs poll one word: spare its L2 line
       if (ld_relaxed_gpu(ctr) >= target) break;
       if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
         report(status, HS_DEV_TIMEOUT);
