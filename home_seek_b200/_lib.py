@@ -15,7 +15,8 @@ import os
 from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
-_LIB_PATH = Path(__file__).resolve().parent / "libhs_ext.so"
+_LIB_PATH = Path(__file__).resolve().parent / (
+    "libhs_ext_trace.so" if os.environ.get("HS_TRACE") == "1" else "libhs_ext.so")
 
 HS_OK = 0
 STATUS_NAMES = {0: "HS_OK", 1: "HS_ERR_BAD_SHAPE", 2: "HS_ERR_BAD_ARGUMENT", 3: "HS_ERR_WORKSPACE",
@@ -132,6 +133,7 @@ SIGNATURES = {
     "hs_verify_state_snapshot": (c_int, [c_void_p, c_int64, c_int64, c_void_p]),
     "hs_verify_state_commit": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int32, c_void_p]),
     "hs_fill_bytes": (c_int, [c_void_p, c_int64, c_uint64, c_int32, c_int32, c_void_p]),
+    "hs_trace_buffer": (c_void_p, [c_int]),
 }
 
 _lib = None

@@ -17,6 +17,7 @@ PKG_DIR = Path(__file__).resolve().parent
 CSRC = PKG_DIR / "csrc"
 INCLUDE = PKG_DIR.parent / "include"
 LIB_PATH = PKG_DIR / "libhs_ext.so"
+TRACE_LIB_PATH = PKG_DIR / "libhs_ext_trace.so"  # the same sources with -DHS_TRACE (trace.py)
 SOURCES = ["hs_util.cu", "hs_router.cu", "hs_moe.cu", "hs_accept.cu", "hs_norm.cu", "hs_head.cu", "hs_state.cu", "hs_ep.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -32,22 +33,25 @@ def _inputs() -> list[Path]:
     return [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + [INCLUDE / "hs_ext.h"]
 
 
-def is_stale() -> bool:
-    if not LIB_PATH.exists():
+def is_stale(lib: Path = LIB_PATH) -> bool:
+    if not lib.exists():
         return True
-    t = LIB_PATH.stat().st_mtime
+    t = lib.stat().st_mtime
     return any(p.stat().st_mtime > t for p in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile every CUDA source into one shared library (idempotent)."""
-    if not force and not is_stale():
-        return LIB_PATH
-    out_dir = PKG_DIR / "_build"
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Path:
+    """Compile every CUDA source into one shared library (idempotent). trace:
+    the tracing build (-DHS_TRACE: the layer call's kernels stamp their phase
+    boundaries, read by home_seek_b200/trace.py) into libhs_ext_trace.so."""
+    lib = TRACE_LIB_PATH if trace else LIB_PATH
+    if not force and not is_stale(lib):
+        return lib
+    out_dir = PKG_DIR / ("_build_trace" if trace else "_build")
     out_dir.mkdir(exist_ok=True)
     nvcc = _nvcc()
     common = ARCH_FLAGS + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", str(INCLUDE),
-                           "--expt-relaxed-constexpr"]
+                           "--expt-relaxed-constexpr"] + (["-DHS_TRACE"] if trace else [])
     if verbose:
         common += ["-Xptxas", "-v"]
     objs = []
@@ -60,16 +64,15 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {s}")
         objs.append(str(obj))
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = lib.with_suffix(".so.tmp")
     cmd = [nvcc, "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ARCH_FLAGS + ["-Xcompiler", "-fPIC", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("nvcc link failed")
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose="-v" in sys.argv)
-    print(LIB_PATH)
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv, trace="--trace" in sys.argv))

@@ -49,6 +49,7 @@
 #include "hs_common.cuh"
 #include "hs_tcgen05.cuh"
 #include "hs_topk.cuh"
+#include "hs_trace.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -1046,6 +1047,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     fence_mbar_init();
   }
   __syncthreads();
+  HS_TRACE_SLOT_ROUTE(hs_tslot);
+  if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 0);
   if (tid == 0) {  // parameters do not depend on the previous kernel: start them now
     mbar_arrive_expect_tx(bar, rowb * ((hash ? 0 : 16) + (norm ? 1 : 0) + T));
     if (!hash)
@@ -1055,6 +1058,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   if (tid < 16) biasv[tid] = (!hash && A.bias) ? __bfloat162float(A.bias[e0 + tid]) : 0.f;
   pdl_trigger();
   pdl_wait();  // the rows (and everything earlier) are complete
+  if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 1);
   if (tid == 0)
     for (int t = 0; t < T; ++t) bulk_load(xs + t * RS, A.x + static_cast<int64_t>(t) * D, rowb, bar);
   // clear this kernel's share of the tickets and token tables meanwhile
@@ -1092,6 +1096,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     (void)mbar_wait(bar, 0);
   }
   ok = __syncthreads_and(ok) != 0;  // uniform over the CTA (barriers follow)
+  if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 2);
 
   // ---- RMSNorm of every row (the standalone norm kernel's summation order),
   // and each normed row's max |x| for its prescale exponent; rows in groups
@@ -1184,6 +1189,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     if (lane == 0) rowe[warp] = row_prescale(mx);
   }
 
+  if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 3);
   // ---- logits: warp s sums the four 128-column quarters of k-split s in order ----
   const int nsplit = D / router::kKSplitCols;
   if (!hash && ok && warp < nsplit) {
@@ -1211,6 +1217,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     if (t < T) cluster.map_shared_rank(keys, 0)[t * 256 + e0 + el] = score_key32(sc);
   }
   cluster.sync();
+  if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 4);
 
   // ---- the normed rows and their hi/lo e4m3 split, column slice by slice: off
   // CTA 0's critical path (rank 1 also takes rank 0's slice) ----
@@ -1237,6 +1244,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
       P.tok_e[tid] = rowe[tid];
     }
     if (rank != 0) {
+      if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 5);
       release_ready(P.ready);
       return;
     }
@@ -1352,6 +1360,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     P.hdr[0] = C;
     P.hdr[1] = C;
     P.hdr[2] = 0;
+    HS_STAMP(hs_tslot, ::hs::trace::kRoute, 0, 5);
+    HS_TRACE_NEXT_CALL();
   }
   release_ready(P.ready);
 }
@@ -1606,7 +1616,13 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world
                                                          const __nv_bfloat16* h, __nv_bfloat16* h_out,
                                                          int32_t* status, uint64_t limit_ns) {
   pdl_trigger();
+  HS_TRACE_T(hs_t0);
   pdl_wait();
+  HS_TRACE_SLOT(hs_tslot);
+  if (threadIdx.x == 0) {
+    HS_STAMP_AT(hs_tslot, ::hs::trace::kCombine, blockIdx.x, 0, hs_t0);
+    HS_STAMP(hs_tslot, ::hs::trace::kCombine, blockIdx.x, 1);
+  }
   uint64_t* hdr = reinterpret_cast<uint64_t*>(buf);
   volatile uint64_t* poison = reinterpret_cast<volatile uint64_t*>(hdr + epx::kPoison);
   if (*poison != 0u) {  // an earlier call gave up: nothing here can be trusted
@@ -1664,6 +1680,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world
     const float yb = __bfloat162float(__float2bfloat16_rn(y));
     h_out[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(h[i]), yb));
   }
+  if (threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kCombine, blockIdx.x, 2);
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -1674,6 +1691,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world
       if (*poison == 0u) *reinterpret_cast<volatile uint64_t*>(hdr) = k + 1;
       __threadfence();
     }
+    HS_STAMP(hs_tslot, ::hs::trace::kCombine, blockIdx.x, 3);
   }
 }
 
@@ -1946,6 +1964,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = d.D;
   const int c = blockIdx.x;
+  HS_TRACE_T(hs_t0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S_; ++i) {
@@ -2002,6 +2021,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   __syncthreads();
   tc5::fence_after_sync();
   const uint32_t tmem = bars->tmem;
+  HS_TRACE_SLOT(hs_tslot);
+  if (kTok && !kDown && threadIdx.x == 0) {
+    HS_STAMP_AT(hs_tslot, ::hs::trace::kGateUp, c, 0, hs_t0);
+    HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 1);
+  }
   // token mode: the producer's chunk experts (lane j: chunks j, j+32, j+64,
   // j+96) and token B scales (lane t), loaded together with the schedule's
   // header so the plan costs one round trip (entries past the chunk count are
@@ -2101,6 +2125,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
           else
             mbar_arrive_expect_tx(&bars->full[st], tx);
           const int xa = kDown ? k * 256 : k * 128;
+          if (kTok && !kDown && step == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 2);
           tma_load_2d_hint(S, wm, &bars->full[st], 0, static_cast<int>(y0 + static_cast<int64_t>(k) * 256), pol);
           for (int b = 0; b < BOXES; ++b)
             tma_load_3d(Bs + b * 2 * NT * 1024, bm, &bars->full[st], xa + b * 128, kTok ? 0 : ui.pair0, 0);
@@ -2163,6 +2188,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
           tc5::fence_after_sync();
           uint8_t* S = base + st * L::kStage;
           const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
+          if (kTok && !kDown && step == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 3);
           if (k == k0) tc5::cp_sf_32x128b(sfb, tc5::sdesc_sf(sSF + 1024));
           const uint32_t sfa0 = tmem + kSfa + st * 8;
           tc5::cp_sf_32x128b(sfa0, tc5::sdesc_sf(sSF));
@@ -2187,6 +2213,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
         s = us + k1;
       }
       // every tcgen05 operation of this thread done before TMEM is freed
+      if (kTok && !kDown) HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 4);
       bars->consumed = static_cast<int32_t>(step);
       tc5::commit(&bars->mma_done);
       if (!mbar_wait(&bars->mma_done, 0)) report(a.status, HS_DEV_TIMEOUT);
@@ -2221,11 +2248,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       if (split && finish) {
         wait_ticket(&a.ucount[u], static_cast<uint32_t>(nk - (k1 - k0)), etid, a.status);
         peer_sum<NV>(sc, cf + 1, cl, a.part, kSlot, row, pre);
+        if (kTok && !kDown && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 7);
       }
       if (!mbar_wait(&bars->acc_full[buf], static_cast<uint32_t>((seg >> 1) & 1))) {
         if (etid == 0) report(a.status, HS_DEV_TIMEOUT);
         break;
       }
+      if (kTok && !kDown && seg == 0 && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 6);
       tc5::fence_after_sync();
       float c0[N], c1[N];
       const uint32_t acc = tmem + lane_off + buf * kAcc;
@@ -2331,6 +2360,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
   }
   __syncthreads();
   if (warp == 0) {
+  if (kTok && !kDown && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 5);
     tc5::fence_after_sync();
     tc5::tmem_dealloc(tmem, 256);
   }
@@ -2432,6 +2462,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = d.D;
   const int c = blockIdx.x;
+  HS_TRACE_T(hs_t0);
+  HS_TRACE_VAR(hs_t2);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S_; ++i) {
@@ -2556,6 +2588,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
       const int st = static_cast<int>(step);
       if (lane == 0) {
         mbar_expect_tx(&bars->full[st], tx_of(q));  // bytes now, the arrival after the activations
+        if (step == 0) HS_TRACE_SET(hs_t2);
         issue_weights(st, q);
       }
     }
@@ -2576,6 +2609,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     __syncthreads();  // the reset precedes every trigger of this CTA
   }
   pdl_trigger();
+  HS_TRACE_SLOT(hs_tslot);
+  if (kCl && threadIdx.x == 0) {
+    HS_STAMP_AT(hs_tslot, ::hs::trace::kDown, c, 0, hs_t0);
+    HS_STAMP(hs_tslot, ::hs::trace::kDown, c, 1);
+  }
+  if (kCl && threadIdx.x == 128) HS_STAMP_AT(hs_tslot, ::hs::trace::kDown, c, 2, hs_t2);
   auto act_ready = [&](const Step& q) {  // lane 0 of the producer
     if (!per_step) return true;
     const int slot = q.shared ? 0 : 1 + q.ch;
@@ -2646,6 +2685,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
           const uint32_t sA = smem_u32(S), sB = smem_u32(S + L::kA), sSF = smem_u32(S + L::kA + L::kB);
           const uint32_t sfa0 = tmem + kSfa + st * 8;
           const uint32_t sfb = tmem + kSfb + st * 8;
+          if (kCl && step == 0) HS_STAMP(hs_tslot, ::hs::trace::kDown, c, 3);
           tc5::cp_sf_32x128b(sfb, tc5::sdesc_sf(sSF + 1024));
           tc5::cp_sf_32x128b(sfb + 4, tc5::sdesc_sf(sSF + 1280));
           tc5::cp_sf_32x128b(sfa0, tc5::sdesc_sf(sSF));
@@ -2672,6 +2712,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
         tc5::commit(&bars->acc_full[buf]);
         s = us + k1;
       }
+      if (kCl) HS_STAMP(hs_tslot, ::hs::trace::kDown, c, 4);
       bars->consumed = static_cast<int32_t>(step);
       tc5::commit(&bars->mma_done);
       if (!mbar_wait(&bars->mma_done, 0)) report(a.status, HS_DEV_TIMEOUT);
@@ -2695,6 +2736,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
       const int64_t us = sc.ustart(sc.unit_of(s_begin));
       const int k0 = static_cast<int>(s_begin - us), k1 = static_cast<int>(s_end - us);
       if (mbar_wait(&bars->acc_full[0], 0)) {
+        if (threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kDown, c, 6);
         tc5::fence_after_sync();
         float c0[16], c1[16];
         tc5::ld_32x32b_x16(tmem + lane_off, c0);
@@ -2802,6 +2844,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     // loaded before the accumulator was ready
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
+    if (threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kDown, c, 7);
     bool ep_poisoned = false;
     if (a.ep_world > 0) {  // this call's slot (the local call counter, advanced by the previous combine)
       const volatile uint64_t* hdr = reinterpret_cast<volatile const uint64_t*>(a.ep_recv[a.ep_rank]);
@@ -2863,6 +2906,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
   }
   __syncthreads();
   if (warp == 0) {
+  if (kCl && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kDown, c, 5);
     tc5::fence_after_sync();
     tc5::tmem_dealloc(tmem, 256);
   }
@@ -4099,4 +4143,19 @@ extern "C" int hs_moe_ffn_fp4_noalloc(const void* desc, const void* hidden, cons
   if (st != HS_OK) return st;
   return hs_moe_ffn_fp4(desc, hidden, topk_idx, topk_w, T, top_k, use_shared, dup_mode, out, out_f32, scratch,
                         HS_MOE_NOALLOC_BYTES, dev_status, stream);
+}
+
+// The tracing build's stamp array ([slot][kernel][CTA][event] u64, which = 0)
+// and layer-call counter (u32, which = 1), or NULL in the normal build.
+extern "C" void* hs_trace_buffer(int which) {
+#ifdef HS_TRACE
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, which == 0 ? static_cast<const void*>(&hs::trace::g_stamp)
+                                          : static_cast<const void*>(&hs::trace::g_calls)) != cudaSuccess)
+    return nullptr;
+  return p;
+#else
+  (void)which;
+  return nullptr;
+#endif
 }

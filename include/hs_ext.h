@@ -54,6 +54,11 @@ typedef enum hs_status {
 #define HS_DEV_SMEM_ALIGN 0x10 /* dynamic shared memory not 1024-byte aligned; the MoE kernel did nothing */
 
 int hs_abi_version(void);
+/* Tracing builds (-DHS_TRACE, libhs_ext_trace.so): the device address of the  */
+/* phase-stamp array (which = 0: [32 slots][5 kernels][296 CTAs][8 events]     */
+/* u64 %globaltimer values) or of the layer-call counter (which = 1, u32);    */
+/* NULL in the normal build.                                                   */
+void* hs_trace_buffer(int which);
 const char* hs_status_string(int status);
 /* Last CUDA error code seen by the library on this thread (0 if none). */
 int hs_last_cuda_error(void);
