@@ -24,6 +24,7 @@ def test_library_builds_and_loads():
     lib = _lib.load()
     assert lib.hs_abi_version() == 2
     assert lib.hs_status_string(3) == b"workspace too small"
+    assert lib.hs_trace_buffer(0) is None  # the normal build carries no phase stamps
 
 
 def test_every_declared_symbol_is_exported_and_bound():
