@@ -15,8 +15,10 @@ import os
 from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
-_LIB_PATH = Path(__file__).resolve().parent / (
-    "libhs_ext_trace.so" if os.environ.get("HS_TRACE") == "1" else "libhs_ext.so")
+# HS_LIB_PATH: another build of the library (a tracing or a modified build);
+# HS_TRACE=1: the tracing build next to this file
+_LIB_PATH = Path(os.environ["HS_LIB_PATH"]).resolve() if os.environ.get("HS_LIB_PATH") else \
+    Path(__file__).resolve().parent / ("libhs_ext_trace.so" if os.environ.get("HS_TRACE") == "1" else "libhs_ext.so")
 
 HS_OK = 0
 STATUS_NAMES = {0: "HS_OK", 1: "HS_ERR_BAD_SHAPE", 2: "HS_ERR_BAD_ARGUMENT", 3: "HS_ERR_WORKSPACE",

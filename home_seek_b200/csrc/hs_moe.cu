@@ -71,6 +71,11 @@ constexpr int kTokChunks = 128;         // token mode: at most T*K <= 8*16 route
 constexpr int kSegPairs = 1024;         // segmented plan: pairs per counting CTA
 constexpr int kSegMaxE = 256;           // segmented plan: experts per call at most
 constexpr int kSegTicket = 15;          // plan header word: the counting CTAs' ticket (left at 0)
+// plan header word: the route kernel's ready count (token mode). At the
+// workspace's start for every T, unlike the regions after the header, whose
+// offsets depend on T: a counter that is not cleared at each call's start must
+// not lie where a call with another T keeps other data.
+constexpr int kReadyWord = 14;
 constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two independent MMA streams)
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
 constexpr int kTokDownPad = 256;        // token-mode down kernel: read-only slack after its last stage
@@ -128,11 +133,11 @@ struct Plan {
   // 512-byte atom (an N = 16 MMA never reads the rows above 15)
   uint8_t* act_img;
   // token mode, a call with its routing in the route kernel: the kernels of
-  // one call hand over through counters instead of grid completion. ready:
-  // route CTAs done (each adds 1 after its writes; the down phase resets it);
-  // done: [1 + C_max slots][I_act / 256 k-steps] gate/up units finished
-  // (each k-step of the down phase reads two 128-column units; cleared by the
-  // route kernel with the tickets)
+  // one call hand over through counters instead of grid completion. ready
+  // (plan header word kReadyWord): route CTAs done (each adds 1 after its
+  // writes; the down phase resets it); done: [1 + C_max slots][I_act / 256
+  // k-steps] gate/up units finished (each k-step of the down phase reads two
+  // 128-column units; cleared by the route kernel with the tickets)
   uint32_t* done;
   uint32_t* ready;
 };
@@ -198,8 +203,8 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   g.aligned = 0;
   g.slot_floats = 2 * kM * 8 * ntiles(T);
   g.n_done = T <= kTokMax ? (1 + g.C_max) * (g.I_act / 256) : 0;
-  g.off_ucount = o;  // tickets, then the done counters, then the ready counter
-  o = align_up(o + (g.U_gu + g.U_dn + g.n_done + 1) * sizeof(uint32_t), 256);
+  g.off_ucount = o;  // tickets, then the done counters (all cleared at each call's start)
+  o = align_up(o + (g.U_gu + g.U_dn + g.n_done) * sizeof(uint32_t), 256);
   g.off_part = o;
   o = align_up(o + 2 * static_cast<int64_t>(G) * g.slot_floats * sizeof(float), 256);
   g.off_ctab = o;
@@ -234,7 +239,7 @@ static Plan plan_views(const Geometry& g, void* ws) {
   p.ctab_wb = reinterpret_cast<float*>(b + g.off_ctab);
   p.act_img = b + g.off_img;
   p.done = reinterpret_cast<uint32_t*>(b + g.off_ucount) + g.U_gu + g.U_dn;
-  p.ready = p.done + g.n_done;
+  p.ready = reinterpret_cast<uint32_t*>(p.hdr + kReadyWord);
   return p;
 }
 
