@@ -88,3 +88,59 @@ def test_fp4_and_fp8_block_forms_recovered_from_bf16_losslessly():
     assert torch.equal(fp8_block_dequant(q, k), b8)
     with pytest.raises(TypeError):
         fp8_block_from_bf16((b8.float() * 1.01).to(torch.bfloat16))
+
+
+def test_vocab_rows_tile_the_vocabulary():
+    """ops.vocab_rows: the ranks' head rows are disjoint, cover [0, V) in rank
+    order, start on 128-row tiles and differ by at most one tile."""
+    from home_seek_b200 import ops
+    for V in (129280, 1000, 128, 5000, 257):
+        for world in (1, 2, 3, 4, 8):
+            parts = [ops.vocab_rows(V, r, world) for r in range(world)]
+            pos = 0
+            for row0, rows in parts:
+                assert row0 == pos and row0 % 128 == 0
+                pos += rows
+            assert pos == V
+            tiles = [(r + 127) // 128 for _, r in parts]
+            assert max(tiles) - min(tiles) <= 1
+
+
+def test_ep_dispatch_combine_workspace_sizes():
+    """The C-ABI exchange's workspace: grows with T_max and the group, and bad
+    arguments give 0 (the call then refuses with HS_ERR_BAD_SHAPE)."""
+    from home_seek_b200 import _lib
+    lib = _lib.load()
+    size = lib.hs_ep_dispatch_combine_workspace_size
+    s1 = size(1024, 6, 4096, 2048, 2048, 2)
+    assert s1 > 2 * 1024 * 4096 * 2           # the rows sent and received
+    assert size(2048, 6, 4096, 2048, 2048, 2) > s1
+    assert size(1024, 6, 4096, 2048, 2048, 8) > s1
+    assert size(1024, 6, 4096, 2048, 2048, 1) > 0
+    assert size(-1, 6, 4096, 2048, 2048, 2) == 0
+    assert size(70000, 6, 4096, 2048, 2048, 2) == 0
+    assert size(1024, 6, 4096, 2048, 2048, 9) == 0
+    assert lib.hs_ep_dispatch_plan(None, 3, 6, 32, 9, 0, None, None, None, None) == 1   # world 9: bad shape
+    assert lib.hs_ep_dispatch_plan(None, 3, 6, 32, 2, 0, None, None, None, None) == 2   # NULL outputs
+
+
+def test_trace_phases_from_stamps():
+    """home_seek_b200.trace.phases on a synthetic stamp array: times are per
+    call relative to the route kernel's wait (kernel 0, CTA 0, event 1), CTAs
+    without a stamp are ignored, and the first and last calls are left out."""
+    import torch
+    from home_seek_b200 import trace
+    X = torch.zeros(5, trace.KERNELS, trace.CTAS, trace.EVENTS, dtype=torch.int64)
+    for i in range(5):
+        base = 1_000_000 * (i + 1)
+        X[i, 0, 0, 1] = base                            # route wait over
+        X[i, 0, :16, 0] = base - 1500                   # route entry
+        X[i, 1, :10, 1] = base + torch.arange(10) * 100 + 9000   # gate/up wait: 9.0 .. 9.9 us
+        X[i, 2, :256, 5] = base + 60_000                # down done at 60 us
+    ph = trace.phases(X, 5)
+    assert ph["route entry"] == (-1.5, -1.5, -1.5)
+    lo, med, hi = ph["gate/up wait over"]
+    assert abs(lo - 9.0) < 1e-9 and abs(hi - 9.9) < 1e-9 and abs(med - 9.45) < 1e-9
+    assert ph["down done"] == (60.0, 60.0, 60.0)
+    assert ph["next call's route wait over"][0] == 1000.0
+    assert "combine done" not in ph                     # no stamps, no phase
