@@ -1036,8 +1036,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   uint32_t* emask = reinterpret_cast<uint32_t*>(sW + 8 * 16);         // 256-bit expert bitmap (CTA 0)
   int* rowe = reinterpret_cast<int*>(emask + 8);                      // [8] row prescale exponents
   float* biasv = reinterpret_cast<float*>(rowe + 8);                  // [16] this CTA's biases
-  float* rinv = biasv + 16;                                           // [8] 1 / rms of each row
-  float* wpart = rinv + 8;                                            // [8 warps][8 rows] sums of squares
+  float* wpart = biasv + 16 + 8;                                      // [8 warps][8 rows] sums of squares
   float* wmax = wpart + 64;                                           // [8 warps][8 rows] max |x|
   uint64_t* bar = reinterpret_cast<uint64_t*>(rs + RouteSmem::bar(D));
   const int e0 = rank * 16;
