@@ -71,11 +71,6 @@ constexpr int kTokChunks = 128;         // token mode: at most T*K <= 8*16 route
 constexpr int kSegPairs = 1024;         // segmented plan: pairs per counting CTA
 constexpr int kSegMaxE = 256;           // segmented plan: experts per call at most
 constexpr int kSegTicket = 15;          // plan header word: the counting CTAs' ticket (left at 0)
-// plan header word: the route kernel's ready count (token mode). At the
-// workspace's start for every T, unlike the regions after the header, whose
-// offsets depend on T: a counter that is not cleared at each call's start must
-// not lie where a call with another T keeps other data.
-constexpr int kReadyWord = 14;
 constexpr int kCtasPerSm = 2;           // MoE CTAs resident per SM (two independent MMA streams)
 constexpr int kSmemPerCta = 115712;     // (228 KB per SM - 1 KB reserved per CTA) / 2
 constexpr int kTokDownPad = 256;        // token-mode down kernel: read-only slack after its last stage
@@ -132,20 +127,11 @@ struct Plan {
   // rows 8-15) over the k-tile's 32-column block j, i.e. lines 0-15 of a
   // 512-byte atom (an N = 16 MMA never reads the rows above 15)
   uint8_t* act_img;
-  // token mode, a call with its routing in the route kernel: the kernels of
-  // one call hand over through counters instead of grid completion. ready
-  // (plan header word kReadyWord): route CTAs done (each adds 1 after its
-  // writes; the down phase resets it); done: [1 + C_max slots][I_act / 256
-  // k-steps] gate/up units finished (each k-step of the down phase reads two
-  // 128-column units; cleared by the route kernel with the tickets)
-  uint32_t* done;
-  uint32_t* ready;
 };
 
 struct Geometry {
   int64_t T, K, D, I, I_sh, I_act, P_max, C_max;
   int64_t U_gu, U_dn;      // upper bounds on gate/up and down units
-  int64_t n_done;          // token mode: gate/up unit counters of the down phase's k-steps
   int G;                   // persistent CTAs
   int aligned;             // unit-aligned schedule (no partial slots)
   int64_t slot_floats;     // floats per partial slot (gate/up, the larger)
@@ -202,9 +188,8 @@ static Geometry geometry(int64_t T, int64_t K, int64_t D, int64_t I, int64_t I_s
   g.G = G;
   g.aligned = 0;
   g.slot_floats = 2 * kM * 8 * ntiles(T);
-  g.n_done = T <= kTokMax ? (1 + g.C_max) * (g.I_act / 256) : 0;
-  g.off_ucount = o;  // tickets, then the done counters (all cleared at each call's start)
-  o = align_up(o + (g.U_gu + g.U_dn + g.n_done) * sizeof(uint32_t), 256);
+  g.off_ucount = o;
+  o = align_up(o + (g.U_gu + g.U_dn) * sizeof(uint32_t), 256);
   g.off_part = o;
   o = align_up(o + 2 * static_cast<int64_t>(G) * g.slot_floats * sizeof(float), 256);
   g.off_ctab = o;
@@ -238,8 +223,6 @@ static Plan plan_views(const Geometry& g, void* ws) {
   p.out_part = reinterpret_cast<float*>(b + g.off_out);
   p.ctab_wb = reinterpret_cast<float*>(b + g.off_ctab);
   p.act_img = b + g.off_img;
-  p.done = reinterpret_cast<uint32_t*>(b + g.off_ucount) + g.U_gu + g.U_dn;
-  p.ready = reinterpret_cast<uint32_t*>(p.hdr + kReadyWord);
   return p;
 }
 
@@ -1005,16 +988,6 @@ __device__ __forceinline__ float key32_score(uint32_t k) {
   return __uint_as_float(k == 0xffffffffu ? k : k - 1u);
 }
 
-// A route CTA's writes are complete: every thread's writes, then one release
-// increment of the ready counter the gate/up phase waits for.
-__device__ __forceinline__ void release_ready(uint32_t* ready) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(ready, 1u);
-  }
-}
-
 __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs A, Plan P,
                                                                       const __grid_constant__ Desc d) {
   extern __shared__ __align__(128) uint8_t rs[];
@@ -1249,7 +1222,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     }
     if (rank != 0) {
       if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 5);
-      release_ready(P.ready);
       return;
     }
   }
@@ -1367,7 +1339,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     HS_STAMP(hs_tslot, ::hs::trace::kRoute, 0, 5);
     HS_TRACE_NEXT_CALL();
   }
-  release_ready(P.ready);
 }
 
 // ---------------------------------------------------------------------------
@@ -1408,10 +1379,6 @@ struct UnitArgs {
   // down epilogue stores this rank's rows into every rank's receive buffer
   int ep_rank, ep_world;  // ep_world 0: off
   uint8_t* ep_recv[HS_EP_MAX_RANKS];
-  // token mode after the route kernel: its CTA count; the gate/up phase waits
-  // for P.ready to reach it and the down phase for each k-step's two units
-  // (P.done) instead of for the previous grid's completion. 0: grid waits.
-  int ready_target;
 };
 
 template <int NT, int BOXES, int NBSF = 1>
@@ -1825,29 +1792,6 @@ __device__ __forceinline__ void peer_sum(const SchedT& sc, int c0, int cl, const
   }
 }
 
-// Bounded wait (one thread) until *ctr >= target, then an acquire fence and a
-// proxy fence, so this thread's later generic and async-proxy (TMA, bulk copy)
-// reads see what the writers released before their increments. False if the
-// wait gave up (HS_DEV_TIMEOUT reported).
-__device__ __forceinline__ bool wait_count(const uint32_t* ctr, uint32_t target, int32_t* status) {
-  bool ok = true;
-  if (ld_relaxed_gpu(ctr) < target) {
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 1;; ++i) {
-      __nanosleep(64);  // hundreds of CTAs poll one word: spare its L2 line
-      if (ld_relaxed_gpu(ctr) >= target) break;
-      if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-        report(status, HS_DEV_TIMEOUT);
-        ok = false;
-        break;
-      }
-    }
-  }
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-  return ok;
-}
-
 // The 128 epilogue threads wait (bounded) until a unit's ticket reaches
 // target: thread 0 polls with acquire loads, the named barrier releases the rest.
 __device__ __forceinline__ void wait_ticket(const uint32_t* ctr, uint32_t target, int etid, int32_t* status) {
@@ -2011,15 +1955,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     }
   }
   // everything above overlaps the previous kernel; from here on the plan (and,
-  // for the down phase, the gate/up phase) is complete and visible: after the
-  // route kernel's CTAs have released their writes (token mode after the route
-  // kernel), else after the previous grid
-  if (kTok && !kDown && a.ready_target > 0) {
-    if (threadIdx.x == 0) (void)wait_count(a.P.ready, static_cast<uint32_t>(a.ready_target), a.status);
-    __syncthreads();  // no thread lets the down phase launch before the route kernel's writes are seen
-  } else {
-    pdl_wait();
-  }
+  // for the down phase, the gate/up phase) is complete and visible
+  pdl_wait();
   pdl_trigger();
   tc5::fence_before_sync();
   __syncthreads();
@@ -2050,7 +1987,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
 
   if (warp == 4) {
     // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
-    if (kTok && a.ready_target > 0) asm volatile("fence.proxy.async.global;" ::: "memory");
     const uint64_t pol = l2_evict_first_policy();
     int64_t step = 0;
     bool ok = true;
@@ -2309,14 +2245,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
             gateup_finish_tok<true>(d, a, ui, row, g, v, wbv);
           else
             gateup_finish_tok<false>(d, a, ui, row, g, v, wbv);
-          if (a.ready_target > 0) {  // the unit's activations are complete: count them for the down phase
-            epi_bar();
-            if (etid == 0) {
-              const int64_t I_act = max(d.I, d.has_shared ? d.I_sh : 0);
-              __threadfence();
-              atomicAdd(a.P.done + (ui.shared ? 0 : 1 + ui.chunk) * (I_act / 256) + ui.tile / 2, 1u);
-            }
-          }
         } else if (!kDown) {
           if (ui.shared)
             gateup_finish<NT, true>(d, a, ui, row, g, v);
@@ -2597,21 +2525,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
       }
     }
   }
-  // the gate/up phase's activations: after its whole grid, or (token mode
-  // after the route kernel) per k-step, once both units it reads are counted
-  const bool per_step = a.ready_target > 0;
-  if (!per_step) pdl_wait();
-  // every gate/up CTA saw the ready count before this grid could start: reset
-  // it for the next call, before this CTA lets the next kernel launch (the
-  // next call's gate/up phase starts after the next route kernel, which starts
-  // after every CTA here has triggered)
-  if (per_step && c == 0) {
-    if (threadIdx.x == 0) {
-      *reinterpret_cast<volatile uint32_t*>(a.P.ready) = 0u;
-      __threadfence();
-    }
-    __syncthreads();  // the reset precedes every trigger of this CTA
-  }
+  pdl_wait();  // the gate/up phase's activations are complete
   pdl_trigger();
   HS_TRACE_SLOT(hs_tslot);
   if (kCl && threadIdx.x == 0) {
@@ -2619,11 +2533,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     HS_STAMP(hs_tslot, ::hs::trace::kDown, c, 1);
   }
   if (kCl && threadIdx.x == 128) HS_STAMP_AT(hs_tslot, ::hs::trace::kDown, c, 2, hs_t2);
-  auto act_ready = [&](const Step& q) {  // lane 0 of the producer
-    if (!per_step) return true;
-    const int slot = q.shared ? 0 : 1 + q.ch;
-    return wait_count(a.P.done + slot * (I_act / 256) + q.kk, 2u, a.status);
-  };
 
   if (warp == 4) {
     // ---------------- TMA producer (whole warp; lane 0 issues) ----------------
@@ -2631,7 +2540,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
     for (; step < npre; ++step) {
       const Step q = decode(s_begin + step);
       if (lane == 0) {
-        (void)act_ready(q);
         issue_act(static_cast<int>(step), q);
         mbar_arrive(&bars->full[step]);
       }
@@ -2652,7 +2560,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) tok_down_kernel(const __
       if (lane == 0) {
         mbar_arrive_expect_tx(&bars->full[st], tx_of(q));
         issue_weights(st, q);
-        (void)act_ready(q);
         issue_act(st, q);
       }
       __syncwarp();
@@ -3747,7 +3654,7 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   pa.po = PermuteOut{nullptr, nullptr, nullptr};
   pa.status = dev_status;
   pa.ucount = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + g.off_ucount);
-  pa.n_ucount = g.U_gu + g.U_dn + g.n_done;  // the ready counter is the down phase's to reset
+  pa.n_ucount = g.U_gu + g.U_dn;
   pa.seg_lrank = pa.seg_off = pa.seg_base = nullptr;
   int32_t* seg_ws = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + g.off_seg);
   const int nseg = static_cast<int>((npairs + kSegPairs - 1) / kSegPairs);
@@ -3798,9 +3705,6 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
 
   UnitArgs a;
   a.ncl = 0;
-  // after the route kernel (token mode), the kernels hand over through the
-  // plan's counters: the gate/up phase waits for the route kernel's CTAs
-  a.ready_target = route && tok ? static_cast<int>(route->num_experts / 16) : 0;
   a.w_sh = tok && use_shared ? 1 : 2;  // token mode prefetches the shared expert into L2
   a.ext_combine = T > kInlineCombineMax ? 1 : 0;
   a.ep_rank = 0;
@@ -3831,17 +3735,11 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   a.act_rows = g.act_rows;
   a.ucount = pa.ucount;
   if (tok) {
-    // a launch that fails after the route kernel leaves its ready count set:
-    // clear it, or the next call's gate/up phase would not wait
-    auto clear_ready = [&](int r) {
-      if (r && a.ready_target > 0) (void)cudaMemsetAsync(P.ready, 0, sizeof(uint32_t), st);
-      return r;
-    };
-    if ((rc = launch_sk<false, 1, true>(d, cm, a, st))) return clear_ready(rc);
+    if ((rc = launch_sk<false, 1, true>(d, cm, a, st))) return rc;
     a.ucount = pa.ucount + g.U_gu;
-    if (a.ep_world == 0) return clear_ready(launch_tok_down(d, cm, a, st));
+    if (a.ep_world == 0) return launch_tok_down(d, cm, a, st);
     int gdown = 0;
-    if ((rc = launch_tok_down(d, cm, a, st, &gdown))) return clear_ready(rc);
+    if ((rc = launch_tok_down(d, cm, a, st, &gdown))) return rc;
     (void)gdown;
     const int64_t n = T * d.D;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64));
