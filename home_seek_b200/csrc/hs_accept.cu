@@ -117,54 +117,6 @@ __device__ void warp_argmax(const __nv_bfloat16* __restrict__ row, int lo, int h
   }
 }
 
-// Warp arg-max of up to kGroup rows at once, when the slice has at most
-// kChunks 16-byte chunks per thread: every chunk of every row of the group is
-// loaded before any is folded (one memory round trip for the group instead of
-// one per kBatch chunks of each row), then each row is folded exactly as
-// warp_argmax folds it (chunks in ascending order, the same tail and shuffle
-// tree), so the results are the same.
-constexpr int kGroup = 3;
-constexpr int kChunks = 8;
-__device__ void warp_argmax_rows(const __nv_bfloat16* __restrict__ rows, int64_t row_stride, int nrows, int lo,
-                                 int hi, float (&v)[kGroup], int (&ix)[kGroup]) {
-  const int nvec = (hi - lo) / 8;
-  const int bd = static_cast<int>(blockDim.x);
-  uint4 q[kGroup][kChunks];
-#pragma unroll
-  for (int r = 0; r < kGroup; ++r)
-#pragma unroll
-    for (int u = 0; u < kChunks; ++u)
-      if (r < nrows && threadIdx.x + u * bd < nvec)
-        q[r][u] = __ldcs(reinterpret_cast<const uint4*>(rows + r * row_stride + lo) + threadIdx.x + u * bd);
-#pragma unroll
-  for (int r = 0; r < kGroup; ++r) {
-    v[r] = -INFINITY;
-    ix[r] = 0x7fffffff;
-    if (r >= nrows) continue;
-#pragma unroll
-    for (int u = 0; u < kChunks; ++u)
-      if (threadIdx.x + u * bd < nvec) argmax_chunk(q[r][u], lo + 8 * (threadIdx.x + u * bd), v[r], ix[r]);
-    const __nv_bfloat16* row = rows + r * row_stride;
-    for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += bd) {
-      const float a = __bfloat162float(row[k]);
-      if (better(a, k, v[r], ix[r])) {
-        v[r] = a;
-        ix[r] = k;
-      }
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < kGroup; ++r)
-    for (int o = 16; o > 0; o >>= 1) {
-      const float v2 = __shfl_xor_sync(0xffffffffu, v[r], o);
-      const int i2 = __shfl_xor_sync(0xffffffffu, ix[r], o);
-      if (better(v2, i2, v[r], ix[r])) {
-        v[r] = v2;
-        ix[r] = i2;
-      }
-    }
-}
-
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
     greedy_kernel(const __nv_bfloat16* __restrict__ logits, int T, int V, const int64_t* __restrict__ draft_ids,
                   int32_t* __restrict__ n_acc, int64_t* __restrict__ next_tok, int64_t* __restrict__ argmax_out) {
@@ -179,28 +131,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   int lo, hi;
   slice_of(V, rank, lo, hi);
   // every row's warp results first, then one barrier and the CTA reduction
-  if ((hi - lo) / 8 <= kChunks * kThreads) {  // the slice fits one round of loads per row group
-    for (int i0 = 0; i0 < T; i0 += kGroup) {
-      float v[kGroup];
-      int ix[kGroup];
-      warp_argmax_rows(logits + (static_cast<int64_t>(b) * T + i0) * V, V, min(kGroup, T - i0), lo, hi, v, ix);
-      if (lane == 0)
-#pragma unroll
-        for (int r = 0; r < kGroup; ++r)
-          if (i0 + r < T) {
-            wv[i0 + r][warp] = v[r];
-            wi[i0 + r][warp] = ix[r];
-          }
-    }
-  } else {
-    for (int i = 0; i < T; ++i) {
-      float v;
-      int ix;
-      warp_argmax(logits + (static_cast<int64_t>(b) * T + i) * V, lo, hi, v, ix);
-      if (lane == 0) {
-        wv[i][warp] = v;
-        wi[i][warp] = ix;
-      }
+  for (int i = 0; i < T; ++i) {
+    float v;
+    int ix;
+    warp_argmax(logits + (static_cast<int64_t>(b) * T + i) * V, lo, hi, v, ix);
+    if (lane == 0) {
+      wv[i][warp] = v;
+      wi[i][warp] = ix;
     }
   }
   __syncthreads();
@@ -333,66 +270,6 @@ __device__ MS warp_ms(const __nv_bfloat16* __restrict__ row, int lo, int hi, flo
   return acc;
 }
 
-// warp_ms of up to G rows at once, when the slice has at most kChunks
-// 16-byte chunks per thread: every chunk of every row of the group is loaded
-// once, before any is used, and both passes (the maximum, then the sum) run
-// on the registers, in warp_ms's order (chunks ascending, then the tail), so
-// the pairs are the same.
-template <int G>
-__device__ void warp_ms_rows(const __nv_bfloat16* const (&rows)[G], int nrows, int lo, int hi, float c,
-                             MS (&out)[G]) {
-  const int nvec = (hi - lo) / 8;
-  const int bd = static_cast<int>(blockDim.x);
-  uint4 q[G][kChunks];
-#pragma unroll
-  for (int r = 0; r < G; ++r)
-#pragma unroll
-    for (int u = 0; u < kChunks; ++u)
-      if (r < nrows && threadIdx.x + u * bd < nvec)
-        q[r][u] = __ldcg(reinterpret_cast<const uint4*>(rows[r] + lo) + threadIdx.x + u * bd);
-#pragma unroll
-  for (int r = 0; r < G; ++r) {
-    MS acc{-INFINITY, 0.f};
-    if (r < nrows) {
-      __nv_bfloat162 mx2 = __float2bfloat162_rn(-INFINITY);
-#pragma unroll
-      for (int u = 0; u < kChunks; ++u)
-        if (threadIdx.x + u * bd < nvec)
-          mx2 = __hmax2_nan(mx2, __hmax2_nan(__hmax2_nan(as_bf162(q[r][u].x), as_bf162(q[r][u].y)),
-                                             __hmax2_nan(as_bf162(q[r][u].z), as_bf162(q[r][u].w))));
-      float mx = __bfloat162float(__hmax_nan(mx2.x, mx2.y));
-      for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += bd) {
-        const float x = __bfloat162float(rows[r][k]);
-        mx = isnan(x) || x > mx ? x : mx;
-      }
-      if (mx != -INFINITY) {
-        const float mc = mx * c;
-        float sum = 0.f;
-#pragma unroll
-        for (int u = 0; u < kChunks; ++u)
-          if (threadIdx.x + u * bd < nvec) {
-            const uint32_t w[4] = {q[r][u].x, q[r][u].y, q[r][u].z, q[r][u].w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              sum += ex2(fmaf(bf16lo(w[j]), c, -mc));
-              sum += ex2(fmaf(bf16hi(w[j]), c, -mc));
-            }
-          }
-        for (int k = lo + nvec * 8 + threadIdx.x; k < hi; k += bd)
-          sum += ex2(fmaf(__bfloat162float(rows[r][k]), c, -mc));
-        acc = MS{mx, sum};
-      }
-    }
-    out[r] = acc;
-  }
-#pragma unroll
-  for (int r = 0; r < G; ++r)
-    for (int o = 16; o > 0; o >>= 1) {
-      MS other{__shfl_xor_sync(0xffffffffu, out[r].m, o), __shfl_xor_sync(0xffffffffu, out[r].s, o)};
-      out[r] = ms_combine(out[r], other, c);
-    }
-}
-
 struct Bcast {
   int n_acc;
   int row;       // target row sampled from
@@ -453,27 +330,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   // barrier, then thread i combines row i over the warps in warp order
   __shared__ MS wms[2 * kMaxRows][kThreads / 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  auto row_of = [&](int i) {
-    return i <= M ? trow0 + static_cast<int64_t>(i) * V : drow0 + static_cast<int64_t>(i - M - 1) * V;
-  };
-  if ((hi - lo) / 8 <= kChunks * kThreads) {  // one round of loads per group of rows
-    constexpr int G = 2;  // two rows' chunks stay in registers (three spill to the stack)
-    for (int i0 = 0; i0 <= 2 * M; i0 += G) {
-      const __nv_bfloat16* rows[G];
-#pragma unroll
-      for (int r = 0; r < G; ++r) rows[r] = i0 + r <= 2 * M ? row_of(i0 + r) : trow0;
-      MS ms[G];
-      warp_ms_rows<G>(rows, min(G, 2 * M + 1 - i0), lo, hi, c, ms);
-      if (lane == 0)
-#pragma unroll
-        for (int r = 0; r < G; ++r)
-          if (i0 + r <= 2 * M) wms[i0 + r][warp] = ms[r];
-    }
-  } else {
-    for (int i = 0; i <= 2 * M; ++i) {
-      const MS r = warp_ms(row_of(i), lo, hi, c);
-      if (lane == 0) wms[i][warp] = r;
-    }
+  for (int i = 0; i <= 2 * M; ++i) {
+    const __nv_bfloat16* row = i <= M ? trow0 + static_cast<int64_t>(i) * V : drow0 + static_cast<int64_t>(i - M - 1) * V;
+    const MS r = warp_ms(row, lo, hi, c);
+    if (lane == 0) wms[i][warp] = r;
   }
   __syncthreads();
   if (threadIdx.x <= 2 * M) {
