@@ -1652,15 +1652,18 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(uint8_t* buf, int world
     h_out[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(h[i]), yb));
   }
   if (threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kCombine, blockIdx.x, 2);
-  __syncthreads();
+  // The last CTA advances the call counter unless a wait ran out. Only the
+  // poison word needs ordering here: a CTA that poisoned fences before its
+  // ticket, the last CTA fences after its own (acquire) before it reads the
+  // word. Everything else this call wrote is seen by the next call through
+  // grid completion (its kernels wait for this one).
+  const bool poisoned_here = __syncthreads_or(timed_out) != 0;
   if (threadIdx.x == 0) {
-    __threadfence();
+    if (poisoned_here) __threadfence();
     if (atomicAdd(reinterpret_cast<unsigned int*>(hdr + 1), 1u) == gridDim.x - 1) {
       *reinterpret_cast<volatile unsigned int*>(hdr + 1) = 0u;
-      // every CTA's poison store precedes its ticket: a poisoned call keeps the counter
       __threadfence();
       if (*poison == 0u) *reinterpret_cast<volatile uint64_t*>(hdr) = k + 1;
-      __threadfence();
     }
     HS_STAMP(hs_tslot, ::hs::trace::kCombine, blockIdx.x, 3);
   }
