@@ -596,6 +596,9 @@ def run_ours(args):
         if os.environ.get("HS_EP_TRANSPORT", "p2p") == "p2p":
             ep.peers = PeerExchange(rank, world, shape.hidden)
     model = MoEPathModel(shape, device=dev, seed=0, ep=ep)
+    # HS_EP_CHAIN=0: each peer-memory layer call completes its own exchange
+    # (a combine kernel per call) instead of the next call's route kernel
+    model.chain_ep = os.environ.get("HS_EP_CHAIN", "1") != "0"
     dec = MTPDecoder(model, max_tokens=(args.steps + args.warmup + 8) * (shape.num_draft + 2))
     dec.reset(token=1234)
     before = ops.launches
@@ -699,7 +702,9 @@ def run_ours(args):
                    "model": "DeepSeek-V4-Flash-shape 43L+MTP, 256 FP4 experts top-6 + FP8 shared, random init",
                    "global_batch": 1, "seq_len": 3,
                    "parallelism": (f"expert-parallel x{world} (1/{world} of the routed and shared experts per GPU, "
-                                   + ("f32 partials stored into every rank's buffer over NVLink by the down phase)"
+                                   + ("f32 partials stored into every rank's buffer over NVLink by the down phase"
+                                      + (", summed by the next layer call's route kernel)" if model.chain_ep
+                                         else ", summed by a combine kernel)")
                                       if ep is not None and ep.peers is not None else
                                       "f32 partials all-reduced over NCCL)")) if world > 1 else "single GPU",
                    "attention": "not in this build's step (reference PyTorch path)",

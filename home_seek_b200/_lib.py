@@ -118,6 +118,11 @@ SIGNATURES = {
                                     c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int, c_int, c_void_p,
                                     c_void_p, c_void_p, POINTER(HsEpPeers), c_void_p, c_void_p, c_size_t, c_void_p,
                                     c_void_p]),
+    "hs_moe_layer_fp4_ep_chained": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
+                                            c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int,
+                                            c_int, c_void_p, c_void_p, c_void_p, POINTER(HsEpPeers), c_int, c_int,
+                                            c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hs_ep_combine_pending": (c_int, [POINTER(HsEpPeers), c_void_p, c_int64, c_int64, c_int, c_void_p, c_void_p]),
     "hs_lm_head_argmax_ep": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p,
                                      c_void_p, c_void_p, c_void_p, POINTER(HsEpPeers), c_void_p, c_size_t, c_void_p,
                                      c_void_p]),

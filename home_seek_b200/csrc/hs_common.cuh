@@ -59,6 +59,22 @@ HS_DI uint32_t ld_relaxed_gpu(const uint32_t* p) {
   return v;
 }
 
+// 16-byte volatile load / store (each 4-byte word is single-copy atomic; a
+// reader that sees a torn vector polls again for the words still missing)
+HS_DI uint4 ld_volatile_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+HS_DI void st_volatile_u4(void* p, uint4 v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // Bounded waits give up after this many nanoseconds (about two seconds), after
 // which the kernel reports HS_DEV_TIMEOUT and returns.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;

@@ -959,6 +959,13 @@ struct RouteArgs {
   int64_t n_ctab;               // token tables to clear (C_max * 8)
   int64_t P_max;                // x8 plane stride in rows
   int32_t* status;
+  // chained expert parallelism: before routing, complete the previous call's
+  // peer-memory exchange into the rows (h <- h + bf16(bf16(routed) [+
+  // bf16(shared)]), in place in h_chain and in every CTA's row buffer)
+  uint8_t* ep_buf;              // this rank's exchange buffer, or nullptr (no chain)
+  __nv_bfloat16* h_chain;       // [T][D] the residual rows (x, written in place)
+  int ep_world, chain_shared;
+  uint64_t wait_ns;
 };
 
 // Shared memory of the route kernel. Gate and token rows are stored with a
@@ -1026,8 +1033,12 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   __syncthreads();
   HS_TRACE_SLOT_ROUTE(hs_tslot);
   if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 0);
+  const bool chain = A.ep_buf != nullptr;
+  // the chained exchange stores into every CTA's row buffer: each CTA arrives
+  // once it runs and waits for the others before the first such store
+  if (chain) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   if (tid == 0) {  // parameters do not depend on the previous kernel: start them now
-    mbar_arrive_expect_tx(bar, rowb * ((hash ? 0 : 16) + (norm ? 1 : 0) + T));
+    mbar_arrive_expect_tx(bar, rowb * ((hash ? 0 : 16) + (norm ? 1 : 0) + (chain ? 0 : T)));
     if (!hash)
       for (int r = 0; r < 16; ++r) bulk_load(gw + r * RS, A.gate + static_cast<int64_t>(e0 + r) * D, rowb, bar);
     if (norm) bulk_load(nw, A.norm_w, rowb, bar);
@@ -1036,8 +1047,102 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   pdl_trigger();
   pdl_wait();  // the rows (and everything earlier) are complete
   if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, rank, 1);
-  if (tid == 0)
+  if (chain) {
+    // The previous call's exchange: this CTA sums every rank's routed and
+    // shared rows of its column slice (ranks in order from 0: identical bits
+    // on every rank, the same as ep_combine_kernel), adds the residual, writes
+    // the rows in place and into every cluster CTA's row buffer, and empties
+    // the entries. Each entry is its own arrival flag; the wait is bounded and
+    // a wait that runs out poisons the buffer, as in ep_combine_kernel.
+    volatile uint64_t* hdr = reinterpret_cast<volatile uint64_t*>(A.ep_buf);
+    const int slot = static_cast<int>(hdr[0] & 1u);
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    bool bad = hdr[epx::kPoison] != 0u;
+    if (bad && tid == 0) report(A.status, HS_DEV_TIMEOUT);
+    const int cols = D / ncta, c0 = rank * cols, n4 = cols / 4;
+    for (int u = tid; u < T * n4; u += kRouteThreads) {
+      const int t = u / n4, c = c0 + 4 * (u - t * n4);
+      const int64_t o = static_cast<int64_t>(t) * D + c;
+      if (bad) {  // the call failed: zero rows (finite, routed like any rows) instead of stale shared memory
+        for (int q = 0; q < ncta; ++q)
+          *reinterpret_cast<uint2*>(cluster.map_shared_rank(xs, q) + t * RS + c) = make_uint2(0u, 0u);
+        continue;
+      }
+      uint4 vr[HS_EP_MAX_RANKS], vs[HS_EP_MAX_RANKS];
+#pragma unroll
+      for (int q = 0; q < HS_EP_MAX_RANKS; ++q)
+        if (q < A.ep_world) {
+          vr[q] = ld_volatile_u4(epx::rows(A.ep_buf, slot, A.ep_world, q, 0, D) + o);
+          vs[q] = ld_volatile_u4(epx::rows(A.ep_buf, slot, A.ep_world, q, 1, D) + o);
+        }
+      auto empty = [](const uint4& v) {
+        return v.x == epx::kEmpty || v.y == epx::kEmpty || v.z == epx::kEmpty || v.w == epx::kEmpty;
+      };
+#pragma unroll
+      for (int q = 0; q < HS_EP_MAX_RANKS; ++q) {
+        if (q >= A.ep_world || bad) continue;
+        if (empty(vr[q]) || empty(vs[q])) {
+          const float* pr = epx::rows(A.ep_buf, slot, A.ep_world, q, 0, D) + o;
+          const float* ps = epx::rows(A.ep_buf, slot, A.ep_world, q, 1, D) + o;
+          const uint64_t w0 = globaltimer_ns();
+          for (uint32_t it = 1; empty(vr[q]) || empty(vs[q]); ++it) {
+            vr[q] = ld_volatile_u4(pr);
+            vs[q] = ld_volatile_u4(ps);
+            if ((it & 63u) == 0 && (globaltimer_ns() - w0 > A.wait_ns || hdr[epx::kPoison] != 0u)) {
+              report(A.status, HS_DEV_TIMEOUT);
+              hdr[epx::kPoison] = 1u;
+              __threadfence();
+              bad = true;
+              break;
+            }
+          }
+        }
+      }
+      if (bad) {
+        for (int q = 0; q < ncta; ++q)
+          *reinterpret_cast<uint2*>(cluster.map_shared_rank(xs, q) + t * RS + c) = make_uint2(0u, 0u);
+        continue;
+      }
+      float r[4] = {0.f, 0.f, 0.f, 0.f}, sh[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < HS_EP_MAX_RANKS; ++q)
+        if (q < A.ep_world) {
+          const uint32_t a4[4] = {vr[q].x, vr[q].y, vr[q].z, vr[q].w}, b4[4] = {vs[q].x, vs[q].y, vs[q].z, vs[q].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            r[j] += __uint_as_float(a4[j]);
+            sh[j] += __uint_as_float(b4[j]);
+          }
+          const uint4 e = make_uint4(epx::kEmpty, epx::kEmpty, epx::kEmpty, epx::kEmpty);
+          st_volatile_u4(epx::rows(A.ep_buf, slot, A.ep_world, q, 0, D) + o, e);
+          st_volatile_u4(epx::rows(A.ep_buf, slot, A.ep_world, q, 1, D) + o, e);
+        }
+      const uint2 hv = *reinterpret_cast<const uint2*>(A.h_chain + o);
+      const uint32_t hw[2] = {hv.x, hv.y};
+      uint32_t ow[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float y0 = round_bf16(r[2 * j]), y1 = round_bf16(r[2 * j + 1]);
+        if (A.chain_shared) {
+          y0 += round_bf16(sh[2 * j]);
+          y1 += round_bf16(sh[2 * j + 1]);
+        }
+        const float b0 = __bfloat162float(__float2bfloat16_rn(y0)), b1 = __bfloat162float(__float2bfloat16_rn(y1));
+        const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(__fadd_rn(__uint_as_float(hw[j] << 16), b0)));
+        const uint32_t hi =
+            __bfloat16_as_ushort(__float2bfloat16_rn(__fadd_rn(__uint_as_float(hw[j] & 0xffff0000u), b1)));
+        ow[j] = lo | (hi << 16);
+      }
+      const uint2 out = make_uint2(ow[0], ow[1]);
+      *reinterpret_cast<uint2*>(A.h_chain + o) = out;
+      for (int q = 0; q < ncta; ++q)
+        *reinterpret_cast<uint2*>(cluster.map_shared_rank(xs, q) + t * RS + c) = out;
+    }
+    cluster.sync();  // every CTA's rows complete (and every poison store seen)
+    if (rank == 0 && tid == 0 && hdr[epx::kPoison] == 0u) hdr[0] = hdr[0] + 1u;
+  } else if (tid == 0) {
     for (int t = 0; t < T; ++t) bulk_load(xs + t * RS, A.x + static_cast<int64_t>(t) * D, rowb, bar);
+  }
   // clear this kernel's share of the tickets and token tables meanwhile
   for (int64_t i = static_cast<int64_t>(rank) * kRouteThreads + tid; i < A.n_ucount;
        i += static_cast<int64_t>(ncta) * kRouteThreads)
@@ -1404,6 +1509,8 @@ struct Bars {
   int32_t issued, consumed;  // TMA stages issued by the producer / consumed by the MMA issuer
 };
 
+constexpr int64_t kMinW = 4;  // least weight per CTA of a stream-K phase (above: fewer CTAs)
+
 // Stream-K schedule over one phase. Units (chunk x 128-row tile) are laid end
 // to end as k-steps, shared-expert units first; a step of an FP8 unit weighs
 // 2 (twice the bytes of an FP4 step). CTA c owns steps [lo(c), lo(c+1)).
@@ -1465,7 +1572,14 @@ __device__ __forceinline__ Sched make_sched(const Desc& d, const UnitArgs& a, bo
   s.S = s.S_sh + s.n_rt_units * s.nk_rt;
   s.W_sh = s.S_sh * s.w_sh;
   s.W = s.W_sh + s.n_rt_units * s.nk_rt;
+  // A unit's finisher sums the partial rows of every other CTA on it, one L2
+  // round trip per few CTAs; with little work in the phase (an expert-parallel
+  // rank whose only unit is its slice of the shared expert) spreading it over
+  // all CTAs would split a 32-step unit over ~70 CTAs. The steps go to the
+  // first W / kMinW CTAs instead (at least kMinW weight each), the rest idle.
   s.G = a.G;
+  if (!a.aligned && s.W < static_cast<int64_t>(a.G) * kMinW)
+    s.G = static_cast<int>(s.W / kMinW > 1 ? s.W / kMinW : 1);
   s.aligned = a.aligned;
   return s;
 }
@@ -2279,7 +2393,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     }
     // no unit at all (every pair skipped, no shared expert): write zeros
     if (kDown && sc.U == 0 && !a.ext_combine)
-      for (int tile = c; tile < D / kM; tile += sc.G) finalize_tile(a, D, tile, etid, 128);
+      for (int tile = c; tile < D / kM; tile += a.G) finalize_tile(a, D, tile, etid, 128);
   }
 
   tc5::fence_before_sync();
@@ -3551,7 +3665,16 @@ struct RouteIn {
   const int64_t* tid2eid = nullptr;
   int64_t vocab = 0;
   const hs_ep_peers* ep = nullptr;   // peer-memory expert parallelism (layer form)
+  // chained expert parallelism: the route kernel first completes the previous
+  // call's exchange into the rows (in place), and this call's exchange is left
+  // pending for the next call (or hs_ep_combine_pending)
+  int chain_prev = 0, chain_prev_shared = 0;
+  bool defer = false;
 };
+
+static uint64_t ep_wait_limit(const hs_ep_peers* pe) {
+  return pe->wait_limit_ns > 0 ? static_cast<uint64_t>(pe->wait_limit_ns) : kWaitLimitNs;
+}
 
 static int launch_route(const RouteArgs& ra, const Plan& P, const Desc& d, cudaStream_t st) {
   const int ncta = ra.E / 16;
@@ -3568,6 +3691,15 @@ static int launch_route(const RouteArgs& ra, const Plan& P, const Desc& d, cudaS
   }
   HS_CUDA_CHECK(launch_pdl_cluster(route_plan_kernel, dim3(static_cast<unsigned>(ncta)), dim3(kRouteThreads), bytes,
                                    st, static_cast<unsigned>(ncta), ra, P, d));
+  return check_launch();
+}
+
+static int launch_ep_combine(uint8_t* buf, int world, int64_t T, int D, int use_shared, const __nv_bfloat16* h,
+                             __nv_bfloat16* h_out, int32_t* status, uint64_t limit, cudaStream_t st) {
+  const int64_t n = T * D;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64));
+  HS_CUDA_CHECK(launch_pdl(ep_combine_kernel, dim3(grid), dim3(256), 0, st, buf, world, static_cast<int>(T), D,
+                           use_shared, h, h_out, status, limit));
   return check_launch();
 }
 
@@ -3694,6 +3826,18 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
     ra.n_ucount = pa.n_ucount;
     ra.n_ctab = g.C_max * 8;
     ra.P_max = g.P_max;
+    ra.ep_buf = nullptr;
+    ra.h_chain = nullptr;
+    ra.ep_world = 0;
+    ra.chain_shared = 0;
+    ra.wait_ns = 0;
+    if (route->ep && route->chain_prev) {
+      ra.ep_buf = static_cast<uint8_t*>(route->ep->recv[route->ep->rank]);
+      ra.h_chain = static_cast<__nv_bfloat16*>(route->h_out);  // the rows themselves
+      ra.ep_world = route->ep->world;
+      ra.chain_shared = route->chain_prev_shared;
+      ra.wait_ns = ep_wait_limit(route->ep);
+    }
     if ((rc = launch_route(ra, P, d, st))) return rc;
   } else if (seg && (rc = launch_seg(pa, P, nseg, seg_ws, st))) {
     return rc;
@@ -3729,8 +3873,9 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
   a.out_f32 = out_f32;
   a.shared_f32 = partials && use_shared ? shared_f32 : nullptr;
   a.partials = partials;
-  a.resid = layer && !partials ? static_cast<const __nv_bfloat16*>(hidden) : nullptr;
-  a.resid_out = layer && !partials ? static_cast<__nv_bfloat16*>(route->h_out) : nullptr;
+  // (expert parallelism: the residual add happens in the exchange's combine)
+  a.resid = layer && !partials && a.ep_world == 0 ? static_cast<const __nv_bfloat16*>(hidden) : nullptr;
+  a.resid_out = layer && !partials && a.ep_world == 0 ? static_cast<__nv_bfloat16*>(route->h_out) : nullptr;
   a.status = dev_status;
   a.G = g.G;
   a.aligned = g.aligned;
@@ -3744,14 +3889,10 @@ static int moe_ffn_impl(const void* desc, const void* hidden, const int64_t* top
     int gdown = 0;
     if ((rc = launch_tok_down(d, cm, a, st, &gdown))) return rc;
     (void)gdown;
-    const int64_t n = T * d.D;
-    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64));
-    const uint64_t limit = route->ep->wait_limit_ns > 0 ? static_cast<uint64_t>(route->ep->wait_limit_ns)
-                                                         : kWaitLimitNs;
-    HS_CUDA_CHECK(launch_pdl(ep_combine_kernel, dim3(grid), dim3(256), 0, st, a.ep_recv[a.ep_rank], a.ep_world,
-                             static_cast<int>(T), d.D, use_shared, static_cast<const __nv_bfloat16*>(hidden),
-                             static_cast<__nv_bfloat16*>(route->h_out), dev_status, limit));
-    return check_launch();
+    if (route->defer) return HS_OK;  // the next chained call (or hs_ep_combine_pending) completes it
+    return launch_ep_combine(a.ep_recv[a.ep_rank], a.ep_world, T, d.D, use_shared,
+                             static_cast<const __nv_bfloat16*>(hidden), static_cast<__nv_bfloat16*>(route->h_out),
+                             dev_status, ep_wait_limit(route->ep), st);
   }
   if (tmaj) {
     TmMaps tmm;
@@ -3865,6 +4006,46 @@ extern "C" int hs_moe_layer_fp4_ep(const void* desc, const void* h, const void* 
   r.ep = peers;
   return moe_ffn_impl(desc, h, nullptr, nullptr, T, top_k, use_shared, dup_mode, nullptr, nullptr, nullptr, 0,
                       workspace, workspace_bytes, dev_status, stream, &r);
+}
+
+extern "C" int hs_moe_layer_fp4_ep_chained(const void* desc, void* h, const void* norm_w, float eps, const void* gate,
+                                           const void* bias, const int64_t* input_ids, const int64_t* tid2eid,
+                                           int64_t vocab, int64_t num_experts, int64_t expert_offset, int64_t T,
+                                           int64_t top_k, float routed_scaling, int use_shared, int dup_mode,
+                                           int64_t* topk_idx, float* topk_w, void* x_out, const hs_ep_peers* peers,
+                                           int prev_pending, int prev_use_shared, void* workspace,
+                                           size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  if (!norm_w || !h || !peers) return HS_ERR_BAD_ARGUMENT;
+  Desc dd;
+  if (!desc) return HS_ERR_BAD_ARGUMENT;
+  memcpy(&dd, desc, sizeof(dd));
+  if (T > epx::kRows || dd.D > 8192) return HS_ERR_UNSUPPORTED;
+  RouteIn r{gate, bias, num_experts, expert_offset, routed_scaling, topk_idx, topk_w};
+  r.norm_w = norm_w;
+  r.eps = eps;
+  r.x_out = x_out;
+  r.h_out = h;
+  r.ids = input_ids;
+  r.tid2eid = tid2eid;
+  r.vocab = vocab;
+  r.ep = peers;
+  r.chain_prev = prev_pending ? 1 : 0;
+  r.chain_prev_shared = prev_use_shared ? 1 : 0;
+  r.defer = true;
+  return moe_ffn_impl(desc, h, nullptr, nullptr, T, top_k, use_shared, dup_mode, nullptr, nullptr, nullptr, 0,
+                      workspace, workspace_bytes, dev_status, stream, &r);
+}
+
+extern "C" int hs_ep_combine_pending(const hs_ep_peers* peers, void* h, int64_t T, int64_t D, int use_shared,
+                                     int32_t* dev_status, void* stream) {
+  if (!peers || !h || peers->world < 1 || peers->world > HS_EP_MAX_RANKS || peers->rank < 0 ||
+      peers->rank >= peers->world || !peers->recv[peers->rank])
+    return HS_ERR_BAD_ARGUMENT;
+  if (T < 0 || T > epx::kRows || D < 8 || D > 8192 || D % 8) return HS_ERR_BAD_SHAPE;
+  if (T == 0) return HS_OK;
+  return launch_ep_combine(static_cast<uint8_t*>(peers->recv[peers->rank]), peers->world, T, static_cast<int>(D),
+                           use_shared, static_cast<const __nv_bfloat16*>(h), static_cast<__nv_bfloat16*>(h),
+                           dev_status, ep_wait_limit(peers), static_cast<cudaStream_t>(stream));
 }
 
 extern "C" size_t hs_ep_buffer_bytes(int64_t world, int64_t D) {

@@ -67,6 +67,9 @@ class MoEPathModel:
         self.shape = s = shape
         self.device = dev = torch.device(device)
         self.ep = ep
+        # under peer-memory expert parallelism, forward chains its layer calls
+        # (each call's exchange completed by the next call's route kernel)
+        self.chain_ep = True
         off, held, sh = 0, None, s.shared_inter
         if ep is not None:
             from .ep import expert_range, shared_slice
@@ -152,13 +155,7 @@ class MoEPathModel:
             return self.ep.partials(st, layer, x, idx, w, dup)
         return ops.moe_ffn(st.desc(layer), st.dims, x, idx, w, use_shared=True, dup_mode=dup)
 
-    def layer(self, h: torch.Tensor, layer: int, ids: torch.Tensor,
-              h_out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """h + MoE(rms_norm(h, ln_w[layer])) for T <= 8 rows (into h_out when
-        given, which may be h): one hs_moe_layer_fp4 call; under expert
-        parallelism either hs_moe_layer_fp4_ep (the exchange through NVLink
-        peer memory inside the call) or the partials form, an NCCL all-reduce
-        and the combine + add."""
+    def _layer_args(self, h: torch.Tensor, layer: int, ids: torch.Tensor):
         s = self.shape
         st = self.store
         lw = st.layers[layer]
@@ -169,6 +166,29 @@ class MoEPathModel:
         kw["use_shared"] = layer < s.num_layers
         gate, bias = (None, None) if hashed else (lw.gate, lw.bias)
         args = (st.desc(layer), st.dims, h, self.ln_w[layer], gate, bias, s.top_k, s.routed_scaling)
+        return args, dup, kw
+
+    def layer_chained(self, h: torch.Tensor, layer: int, ids: torch.Tensor, prev_shared: Optional[bool]) -> bool:
+        """The layer call in the chained peer-memory form: h first receives the
+        previous chained call's output (prev_shared: its use_shared, None when
+        nothing is pending), then this layer's output is left pending. Returns
+        this call's use_shared, for the next call or ep_combine_pending."""
+        args, dup, kw = self._layer_args(h, layer, ids)
+        ops.moe_layer_ep_chained(*args, self.ep.peers.peers, prev_pending=prev_shared is not None,
+                                 prev_use_shared=bool(prev_shared), dup_mode=dup,
+                                 num_experts=self.shape.num_experts, expert_offset=self.store.expert_offset, **kw)
+        return bool(kw["use_shared"])
+
+    def layer(self, h: torch.Tensor, layer: int, ids: torch.Tensor,
+              h_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """h + MoE(rms_norm(h, ln_w[layer])) for T <= 8 rows (into h_out when
+        given, which may be h): one hs_moe_layer_fp4 call; under expert
+        parallelism either hs_moe_layer_fp4_ep (the exchange through NVLink
+        peer memory inside the call) or the partials form, an NCCL all-reduce
+        and the combine + add."""
+        s = self.shape
+        st = self.store
+        args, dup, kw = self._layer_args(h, layer, ids)
         if self.ep is not None and self.ep.peers is not None:  # exchange through peer memory in the call
             return ops.moe_layer_ep(*args, self.ep.peers.peers, dup_mode=dup, num_experts=s.num_experts,
                                     expert_offset=st.expert_offset, h_out=h_out, **kw)[0]
@@ -194,10 +214,19 @@ class MoEPathModel:
     def forward(self, ids: torch.Tensor):
         """All layers for tokens `ids`: returns (h, x) with h the residual stream
         after the last layer and x = rms_norm(h, final norm). At T <= 8 each
-        layer is one hs_moe_layer_fp4 call updating h in place; above, each
-        layer's residual add is fused with the next layer's input norm."""
+        layer is one hs_moe_layer_fp4 call updating h in place (under
+        peer-memory expert parallelism chained: each call's exchange completed
+        by the next call); above, each layer's residual add is fused with the
+        next layer's input norm."""
         L = self.shape.num_layers
         h = self.embed[ids]
+        if ids.shape[0] <= 8 and self.chain_ep and self.ep is not None and self.ep.peers is not None:
+            pending = None
+            for layer in range(L):
+                pending = self.layer_chained(h, layer, ids, pending)
+            if pending is not None:
+                ops.ep_combine_pending(self.ep.peers.peers, h, use_shared=pending)
+            return h, ops.rms_norm(h, self.norm_w)
         if ids.shape[0] <= 8:
             for layer in range(L):
                 self.layer(h, layer, ids, h_out=h)

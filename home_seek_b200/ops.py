@@ -23,7 +23,8 @@ _KERNELS = {"hs_router_topk": 1, "hs_hash_route": 1, "hs_moe_ffn_fp4": 3, "hs_mo
             "hs_rms_norm": 1, "hs_add_rms_norm": 1, "hs_moe_ffn_fp4_partials": 3, "hs_moe_combine": 1,
             "hs_moe_route_ffn_fp4": 3, "hs_moe_route_ffn_fp4_partials": 3,
             "hs_moe_combine_add_rms_norm": 1, "hs_moe_layer_fp4": 3, "hs_moe_layer_fp4_partials": 3,
-            "hs_moe_layer_fp4_ep": 4, "hs_lm_head_argmax": 1,
+            "hs_moe_layer_fp4_ep": 4, "hs_moe_layer_fp4_ep_chained": 3, "hs_ep_combine_pending": 1,
+            "hs_lm_head_argmax": 1,
             "hs_lm_head_argmax_ep": 1}
 
 
@@ -330,6 +331,57 @@ def moe_layer_ep(desc: ctypes.Array, dims: tuple, h: torch.Tensor, norm_w: torch
             ctypes.byref(peers), h_out.data_ptr(), ws.data_ptr(), ws.numel(), status_word(dev).data_ptr(),
             _stream(dev))
     return h_out, idx, w
+
+
+def moe_layer_ep_chained(desc: ctypes.Array, dims: tuple, h: torch.Tensor, norm_w: torch.Tensor,
+                         gate: Optional[torch.Tensor], bias: Optional[torch.Tensor], top_k: int,
+                         routed_scaling: float, peers: "_lib.HsEpPeers", prev_pending: bool,
+                         prev_use_shared: bool = True, eps: float = 1e-6, use_shared: bool = True,
+                         dup_mode: int = _lib.HS_DUP_LAST, num_experts: Optional[int] = None,
+                         expert_offset: int = 0, ids: Optional[torch.Tensor] = None,
+                         tid2eid: Optional[torch.Tensor] = None, x_out: Optional[torch.Tensor] = None):
+    """moe_layer_ep for a stack of layers, each call's exchange completed at
+    the start of the next (hs_moe_layer_fp4_ep_chained): with prev_pending the
+    previous chained call's output is first added to h in place, then this
+    layer runs on it and leaves its own output pending. ep_combine_pending
+    completes the last one. Consecutive calls take the same h. Returns
+    (idx, w)."""
+    dev = _check_cuda(h, norm_w, gate, bias, ids, tid2eid, x_out)
+    if not h.is_contiguous() or h.dtype != torch.bfloat16 or h.dim() != 2:
+        raise ValueError("h must be contiguous bf16 [T, D] (it is updated in place)")
+    norm_w = _rows(norm_w, "norm_w")
+    T, D = h.shape
+    E, Dd, I, I_sh = dims
+    if D != Dd:
+        raise ValueError(f"hidden dim {D} != store dim {Dd}")
+    if tid2eid is None and (gate is None or gate.dtype != torch.bfloat16):
+        raise TypeError("router mode needs a bf16 gate")
+    n_exp = int(num_experts if num_experts is not None else (gate.shape[0] if gate is not None else E))
+    idx = torch.empty(T, top_k, dtype=torch.int64, device=dev)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws = workspace(dev, lib.hs_moe_workspace_size(T, top_k, D, I, I_sh), "moe")
+    ids_c = ids.reshape(-1).contiguous() if ids is not None else None
+    vocab = int(tid2eid.shape[0]) if tid2eid is not None else 0
+    _launch("hs_moe_layer_fp4_ep_chained", ctypes.addressof(desc), h.data_ptr(), norm_w.data_ptr(), float(eps),
+            None if tid2eid is not None else gate.data_ptr(), None if tid2eid is not None else _ptr(bias),
+            _ptr(ids_c), _ptr(tid2eid), vocab, n_exp, int(expert_offset), T, top_k, float(routed_scaling),
+            int(bool(use_shared) and bool(I_sh)), int(dup_mode), idx.data_ptr(), w.data_ptr(), _ptr(x_out),
+            ctypes.byref(peers), int(bool(prev_pending)), int(bool(prev_use_shared)), ws.data_ptr(), ws.numel(),
+            status_word(dev).data_ptr(), _stream(dev))
+    return idx, w
+
+
+def ep_combine_pending(peers: "_lib.HsEpPeers", h: torch.Tensor, use_shared: bool = True) -> torch.Tensor:
+    """Completes the last moe_layer_ep_chained call: h += its MoE output, in
+    place (hs_ep_combine_pending)."""
+    dev = _check_cuda(h)
+    if not h.is_contiguous() or h.dtype != torch.bfloat16 or h.dim() != 2:
+        raise ValueError("h must be contiguous bf16 [T, D] (it is updated in place)")
+    T, D = h.shape
+    _launch("hs_ep_combine_pending", ctypes.byref(peers), h.data_ptr(), T, D, int(bool(use_shared)),
+            status_word(dev).data_ptr(), _stream(dev))
+    return h
 
 
 def moe_combine(partials: torch.Tensor, use_shared: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -416,6 +416,31 @@ int hs_moe_layer_fp4_ep(const void* desc, const void* h, const void* norm_w,
                         const hs_ep_peers* peers, void* h_out, void* workspace,
                         size_t workspace_bytes, int32_t* dev_status,
                         void* stream);
+/* hs_moe_layer_fp4_ep_chained: hs_moe_layer_fp4_ep for a stack of layers    */
+/* with the exchange of one call completed at the start of the next. The      */
+/* rows h are read and written in place: with prev_pending set, the route     */
+/* kernel first adds the previous chained call's MoE output (prev_use_shared  */
+/* its use_shared) to h exactly as hs_moe_layer_fp4_ep's combine does, then   */
+/* routes on the result; this call's own output stays pending in the receive  */
+/* buffers. hs_ep_combine_pending(peers, h, T, D, use_shared) completes the   */
+/* last pending call (its combine kernel alone, h_out = h). Consecutive       */
+/* chained calls take the same h, T and D, and every rank makes the same      */
+/* sequence of calls; failure behaves as in hs_moe_layer_fp4_ep.              */
+int hs_moe_layer_fp4_ep_chained(const void* desc, void* h, const void* norm_w,
+                                float eps, const void* gate, const void* bias,
+                                const int64_t* input_ids,
+                                const int64_t* tid2eid, int64_t vocab,
+                                int64_t num_experts, int64_t expert_offset,
+                                int64_t T, int64_t top_k, float routed_scaling,
+                                int use_shared, int dup_mode, int64_t* topk_idx,
+                                float* topk_w, void* x_out,
+                                const hs_ep_peers* peers, int prev_pending,
+                                int prev_use_shared, void* workspace,
+                                size_t workspace_bytes, int32_t* dev_status,
+                                void* stream);
+int hs_ep_combine_pending(const hs_ep_peers* peers, void* h, int64_t T,
+                          int64_t D, int use_shared, int32_t* dev_status,
+                          void* stream);
 /* hs_lm_head_argmax_ep: hs_lm_head_argmax with the vocabulary split over the */
 /* same group (no counterpart in the reference, whose lm_head runs on one      */
 /* GPU). head_rows points at rows [row0, row0 + rows) of the [V][D] head: this */

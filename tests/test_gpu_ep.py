@@ -154,6 +154,7 @@ def _p2p_rank(rank: int, world: int, port: int, q) -> None:
             d = (h_ep.float() - h_ref.float()).abs().max().item() / h_ref.float().abs().max().item()
             worst = max(worst, d)
             h_ep.copy_(h_ref)  # next call from the same input on both paths
+        chain_same = _chained_equals_unchained(sh, nw, px.peers, h0)
         # the vocabulary split lm_head over the same buffers: three calls (both
         # key slots used, one twice), each equal to the whole-head call
         head_same = True
@@ -174,11 +175,71 @@ def _p2p_rank(rank: int, world: int, port: int, q) -> None:
         gathered = [torch.empty_like(h_ep) for _ in range(world)]
         dist.all_gather(gathered, h_ep)
         same = all(torch.equal(gathered[0], x) for x in gathered)
-        q.put((rank, worst, status, same and head_same))
+        q.put((rank, worst, status, same and head_same and chain_same))
     finally:
         if px is not None:
             px.close()
         dist.destroy_process_group()
+
+
+def _chained_equals_unchained(sh, nw, peers, h0) -> bool:
+    """Five layer calls chained (each exchange completed by the next call's
+    route kernel, the last by ep_combine_pending) against the same five
+    unchained calls, for T = 3, 1 and 8 (T rows of h0 repeated), use_shared
+    alternating so the pending call's flag matters: bit-identical rows."""
+    from home_seek_b200 import ops
+    same = True
+    for T in (3, 1, 8):
+        hx = h0.repeat((T + h0.shape[0] - 1) // h0.shape[0], 1)[:T].contiguous()
+        hu, hc = hx.clone(), hx.clone()
+        plan = [(call % 2, call % 3 != 1) for call in range(5)]
+        for l, us in plan:
+            lw = sh.layers[l]
+            ops.moe_layer_ep(sh.desc(l), sh.dims, hu, nw[l], lw.gate, lw.bias, 6, 1.5, peers, use_shared=us,
+                             num_experts=256, expert_offset=sh.expert_offset, h_out=hu)
+        pending = None
+        for l, us in plan:
+            lw = sh.layers[l]
+            ops.moe_layer_ep_chained(sh.desc(l), sh.dims, hc, nw[l], lw.gate, lw.bias, 6, 1.5, peers,
+                                     prev_pending=pending is not None, prev_use_shared=bool(pending),
+                                     use_shared=us, num_experts=256, expert_offset=sh.expert_offset)
+            pending = us
+        ops.ep_combine_pending(peers, hc, use_shared=pending)
+        torch.cuda.synchronize()
+        same = same and torch.equal(hu, hc)
+    return same
+
+
+def test_chained_peer_exchange_single_rank_matches_unchained():
+    """A one-rank peer-memory group: the chained layer calls (the exchange
+    completed inside the next call's route kernel) give the unchained calls'
+    rows bit for bit, and the call counter ends where the unchained calls
+    leave it."""
+    import ctypes
+    from home_seek_b200 import _lib, ops
+    from home_seek_b200.ep import shard_store
+    from home_seek_b200.expert_store import HBMExpertStore
+    dev = torch.device("cuda")
+    full = HBMExpertStore(2, 256, 4096, 2048, 2048, device=dev)
+    full.fill_random(37)
+    sh = shard_store(full, 0, 1)
+    buf = ctypes.c_void_p()
+    _lib.call("hs_ep_buffer_alloc", _lib.load().hs_ep_buffer_bytes(1, 4096), ctypes.byref(buf))
+    try:
+        peers = _lib.HsEpPeers()
+        peers.rank, peers.world = 0, 1
+        peers.recv[0] = buf.value
+        g = torch.Generator(device=dev).manual_seed(5)
+        h0 = (torch.randn(3, 4096, generator=g, device=dev) * 2).to(torch.bfloat16)
+        nw = (1 + 0.05 * torch.randn(2, 4096, generator=g, device=dev)).to(torch.bfloat16)
+        ops.check_status(dev)
+        assert _chained_equals_unchained(sh, nw, peers, h0)
+        assert ops.check_status(dev) == 0
+        hdr = torch.as_tensor(_DevView(buf.value, 4), device=dev).cpu().tolist()
+        assert hdr[0] == 30 and hdr[2] == 0, hdr  # 3 T x (5 unchained + 5 chained) calls
+    finally:
+        torch.cuda.synchronize()
+        _lib.call("hs_ep_buffer_free", buf.value)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
@@ -476,6 +537,60 @@ def test_peer_exchange_wait_runs_out_and_poisons_the_buffer():
             assert bool((h_out == 7.0).all()), call  # nothing combined
             assert dt < 1.5, (call, dt)              # bounded by the 50 ms limit (first) or refused (second)
         # the call counter stayed at 0 and the poison word is set
+        hdr = torch.as_tensor(_DevView(bufs[0].value, 4), device=dev).cpu().tolist()
+        assert hdr[0] == 0 and hdr[2] != 0, hdr
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            _lib.call("hs_ep_buffer_free", b.value)
+
+
+def test_chained_peer_exchange_wait_runs_out_and_poisons_the_buffer():
+    """The chained form of the check above: the first chained call leaves its
+    exchange pending; the second call's route kernel waits for rank 1's rows
+    (a 50 ms limit), reports HS_DEV_TIMEOUT, leaves h untouched and poisons the
+    buffer; ep_combine_pending on it then refuses at once."""
+    import ctypes
+    import time
+    from home_seek_b200 import _lib, ops
+    from home_seek_b200.ep import shard_store
+    from home_seek_b200.expert_store import HBMExpertStore
+    dev = torch.device("cuda")
+    full = HBMExpertStore(1, 256, 4096, 2048, 2048, device=dev)
+    full.fill_random(43)
+    sh = shard_store(full, 0, 2)
+    lib = _lib.load()
+    nb = lib.hs_ep_buffer_bytes(2, 4096)
+    bufs = [ctypes.c_void_p(), ctypes.c_void_p()]
+    for b in bufs:
+        _lib.call("hs_ep_buffer_alloc", nb, ctypes.byref(b))
+    try:
+        peers = _lib.HsEpPeers()
+        peers.rank, peers.world = 0, 2
+        peers.recv[0], peers.recv[1] = bufs[0].value, bufs[1].value
+        peers.wait_limit_ns = 50_000_000  # 50 ms
+        g = torch.Generator(device=dev).manual_seed(9)
+        h = (torch.randn(3, 4096, generator=g, device=dev)).to(torch.bfloat16)
+        nw = (1 + 0.05 * torch.randn(4096, generator=g, device=dev)).to(torch.bfloat16)
+        lw = full.layers[0]
+        ops.check_status(dev)
+        h_before = h.clone()
+        for prev in (False, True):
+            t0 = time.monotonic()
+            ops.moe_layer_ep_chained(sh.desc(0), sh.dims, h, nw, lw.gate, lw.bias, 6, 1.5, peers,
+                                     prev_pending=prev, num_experts=256, expert_offset=0)
+            torch.cuda.synchronize()
+            dt = time.monotonic() - t0
+            st = ops.check_status(dev)
+            assert bool(st & _lib.HS_DEV_TIMEOUT) == prev, (prev, st)
+            assert dt < 1.5, (prev, dt)
+            assert torch.equal(h, h_before), prev
+        t0 = time.monotonic()
+        ops.ep_combine_pending(peers, h)
+        torch.cuda.synchronize()
+        assert ops.check_status(dev) & _lib.HS_DEV_TIMEOUT
+        assert time.monotonic() - t0 < 1.5
+        assert torch.equal(h, h_before)
         hdr = torch.as_tensor(_DevView(bufs[0].value, 4), device=dev).cpu().tolist()
         assert hdr[0] == 0 and hdr[2] != 0, hdr
     finally:
