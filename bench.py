@@ -615,18 +615,22 @@ def run_ours(args):
     def device_barrier():
         """Every rank's next event fires when a one-element all-reduce has
         completed on the device, i.e. at the same moment on every rank (a host
-        barrier alone leaves each rank's start at its own host wake-up time)."""
+        barrier alone leaves each rank's start at its own host wake-up time).
+        The caller records its start event right after this, with no host
+        synchronisation in between."""
+        torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
             flag = torch.ones(1, device=dev)
             dist.all_reduce(flag)
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    device_barrier()
-    torch.cuda.synchronize()
+    # the sampler is started (its first sample read) before the barrier: its
+    # start-up time differs between ranks and must not end up inside a window
     with ClockSampler(local if not os.environ.get("CUDA_VISIBLE_DEVICES") else
                       int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
                       if os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local].isdigit() else local) as clk:
+        device_barrier()
         start.record()
         for _ in range(args.steps):
             dec.replay()
@@ -652,10 +656,9 @@ def run_ours(args):
     host_cnt = torch.empty(1, dtype=torch.int64, pin_memory=True)
     host_in.fill_(4321)
     dec.count.zero_()
-    device_barrier()
-    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_tokens = 0
+    device_barrier()
     e0.record()
     for _ in range(args.steps):
         dec.next_id.copy_(host_in, non_blocking=True)

@@ -2215,6 +2215,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       s = us + k1;
     }
     if (lane == 0) bars->issued = static_cast<int32_t>(step);
+    if (kTok && !kDown && lane == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 4);
   } else if (warp == 5) {
     // ---------------- MMA issuer (lane 0) ----------------
     if (lane == 0) {
@@ -2274,6 +2275,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       bars->consumed = static_cast<int32_t>(step);
       tc5::commit(&bars->mma_done);
       if (!mbar_wait(&bars->mma_done, 0)) report(a.status, HS_DEV_TIMEOUT);
+      if (kTok && !kDown) HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 3);
     }
   } else {
     // ---------------- epilogue (warps 0-3, TMEM lanes 32w..32w+31) ----------------
@@ -2304,6 +2306,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       if (kTok && finish) tok_weights(a, ui, wbv);
       if (split && finish) {
         wait_ticket(&a.ucount[u], static_cast<uint32_t>(nk - (k1 - k0)), etid, a.status);
+        if (kTok && !kDown && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 0);
         peer_sum<NV>(sc, cf + 1, cl, a.part, kSlot, row, pre);
         if (kTok && !kDown && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 7);
       }
@@ -2312,6 +2315,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
         break;
       }
       if (kTok && !kDown && seg == 0 && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUp, c, 6);
+      if (kTok && !kDown && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 1);
       tc5::fence_after_sync();
       float c0[N], c1[N];
       const uint32_t acc = tmem + lane_off + buf * kAcc;
@@ -2390,6 +2394,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
         }
       }
       s = us + k1;
+    }
+    if (kTok && !kDown && threadIdx.x == 0) {
+      HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 2);
+      HS_STAMP_AT(hs_tslot, ::hs::trace::kGateUpTail, c, 5, static_cast<unsigned long long>(seg));
     }
     // no unit at all (every pair skipped, no shared expert): write zeros
     if (kDown && sc.U == 0 && !a.ext_combine)

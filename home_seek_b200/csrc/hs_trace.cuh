@@ -15,10 +15,13 @@
 namespace hs {
 namespace trace {
 constexpr int kSlots = 32;
-constexpr int kKernels = 5;  // route, gate/up, down, expert-parallel combine, (spare)
+constexpr int kKernels = 5;  // route, gate/up, down, gate/up tail events, expert-parallel combine
 constexpr int kCtas = 296;
 constexpr int kEvents = 8;
-enum Kernel { kRoute = 0, kGateUp = 1, kDown = 2, kCombine = 4 };
+// kGateUpTail (gate/up CTAs): 0 last ticket wait over, 1 last accumulator
+// ready, 2 epilogue done, 3 MMA warp done, 4 last copy issued, 5 the number of
+// epilogue segments (a count, not a time)
+enum Kernel { kRoute = 0, kGateUp = 1, kDown = 2, kGateUpTail = 3, kCombine = 4 };
 }  // namespace trace
 }  // namespace hs
 

@@ -25,8 +25,9 @@ PHASES = [
     ("route entry", 0, 0, "route"), ("route rows in", 0, 2, "route"), ("route norm done", 0, 3, "route"),
     ("route keys gathered", 0, 4, "route"), ("route others done", 0, 5, "others"), ("route CTA 0 done", 0, 5, "rank0"),
     ("gate/up wait over", 1, 1, None), ("gate/up first TMA", 1, 2, None), ("gate/up first MMA", 1, 3, None),
-    ("gate/up first acc", 1, 6, None), ("gate/up last MMA", 1, 4, None), ("gate/up peer sums", 1, 7, None),
-    ("gate/up done", 1, 5, None), ("down entry", 2, 0, None), ("down first weights", 2, 2, None),
+    ("gate/up first acc", 1, 6, None), ("gate/up last copy issued", 3, 4, None), ("gate/up last MMA", 1, 4, None),
+    ("gate/up MMA warp done", 3, 3, None), ("gate/up last ticket", 3, 0, None), ("gate/up peer sums", 1, 7, None),
+    ("gate/up last acc", 3, 1, None), ("gate/up epilogue done", 3, 2, None), ("gate/up done", 1, 5, None), ("down entry", 2, 0, None), ("down first weights", 2, 2, None),
     ("down started", 2, 1, None), ("down first MMA", 2, 3, None), ("down last MMA", 2, 4, None),
     ("down cluster sync", 2, 7, None), ("down done", 2, 5, None),
     ("combine started", 4, 1, None), ("combine rows in", 4, 2, None), ("combine done", 4, 3, None),
@@ -119,7 +120,8 @@ def run(T_values, layers: int = 8, device: Optional[torch.device] = None) -> dic
         b.record()
         torch.cuda.synchronize()
         n = min(int(calls.item()), SLOTS)
-        res[T] = {"us_per_call": a.elapsed_time(b) * 1000 / layers, "phases": phases(stamps[:n].cpu(), n)}
+        raw = stamps[:n].cpu()
+        res[T] = {"us_per_call": a.elapsed_time(b) * 1000 / layers, "phases": phases(raw, n), "stamps": raw}
     return res
 
 
