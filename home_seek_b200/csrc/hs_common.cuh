@@ -53,6 +53,12 @@ HS_DI void report(int32_t* status, int32_t bits) {
   if (status != nullptr) atomicOr(status, bits);
 }
 
+HS_DI uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 HS_DI uint32_t ld_relaxed_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

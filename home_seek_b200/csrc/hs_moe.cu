@@ -1504,6 +1504,7 @@ struct Bars {
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t mma_done;
+  uint64_t pub;  // stream-K: the epilogue's partial rows of a split unit are stored (128 arrivals)
   uint32_t tmem;
   int32_t flag;
   int32_t issued, consumed;  // TMA stages issued by the producer / consumed by the MMA issuer
@@ -1913,18 +1914,18 @@ __device__ __forceinline__ void peer_sum(const SchedT& sc, int c0, int cl, const
 // target: thread 0 polls with acquire loads, the named barrier releases the rest.
 __device__ __forceinline__ void wait_ticket(const uint32_t* ctr, uint32_t target, int etid, int32_t* status) {
   if (etid == 0) {
-    // relaxed polls, one acquire fence once the count is reached
-    if (ld_relaxed_gpu(ctr) < target) {
+    // acquire polls: no fence, which would also wait for this thread's own
+    // partial rows just stored for another unit
+    if (ld_acquire_gpu(ctr) < target) {
       const uint64_t t0 = globaltimer_ns();
       for (uint32_t i = 1;; ++i) {
-        if (ld_relaxed_gpu(ctr) >= target) break;
+        if (ld_acquire_gpu(ctr) >= target) break;
         if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
           report(status, HS_DEV_TIMEOUT);
           break;
         }
       }
     }
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
   }
   epi_bar();
 }
@@ -1940,9 +1941,12 @@ __device__ __forceinline__ void tok_weights(const UnitArgs& a, const UnitInfo& u
 }
 
 // Token-mode gate/up epilogue: the accumulator columns are the (up to 8)
-// tokens; every (chunk, token) activation row is written, as zeros where the
-// token is not routed to the chunk's expert (or t >= T), so the down phase can
-// run each unit over all experts with the same 8 token columns. Each warp
+// tokens; every (chunk, token < T) activation row is written, as zeros where
+// the token is not routed to the chunk's expert, so the down phase can run
+// each unit over all experts with the same 8 token columns. Rows t >= T are
+// left as they are: they only feed the down MMA's columns t >= T, which no
+// epilogue stores (their values, even non-finite ones, stay in their own
+// columns). Each warp
 // holds 32 consecutive values of every row (one 32-column block of the down
 // MMA's K): the block is scaled by 2^q so its largest magnitude lies in
 // [128, 256), which makes the hi/lo e4m3 split of every bf16 value exact down
@@ -1975,6 +1979,7 @@ __device__ __forceinline__ void gateup_finish_tok(const Desc& d, const UnitArgs&
   }
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
+    if (r >= a.T) break;  // uniform over the warp
     // the block's largest magnitude (non-negative float bits order as values)
     const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(av[r])));
     const int q = row_prescale(__uint_as_float(mb));
@@ -2041,6 +2046,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       mbar_init(&bars->acc_empty[i], 4);
     }
     mbar_init(&bars->mma_done, 1);
+    mbar_init(&bars->pub, 128);
     bars->issued = 0;
     bars->consumed = 0;
     fence_mbar_init();
@@ -2216,6 +2222,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     }
     if (lane == 0) bars->issued = static_cast<int32_t>(step);
     if (kTok && !kDown && lane == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 4);
+    // Only this CTA's first segment can be a non-finishing part of a split
+    // unit (every later segment starts a unit here). Its partial rows are
+    // stored by the epilogue threads, which arrive on `pub` and go on; this
+    // warp adds the step count to the unit's ticket after a gpu-scope fence,
+    // cumulative over their stores through the barrier.
+    if (lane == 0 && s_begin < s_end) {
+      const int64_t u0 = sc.unit_of(s_begin), us0 = sc.ustart(u0);
+      if (sc.cta_of(us0) != c) {
+        const int64_t k1 = min64(static_cast<int64_t>(sc.unk(u0)), s_end - us0);
+        if (mbar_wait(&bars->pub, 0)) {
+          __threadfence();
+          atomicAdd(&a.ucount[u0], static_cast<uint32_t>(k1 - (s_begin - us0)));
+          if (kTok && !kDown) HS_STAMP(hs_tslot, ::hs::trace::kCombine, c, 6);
+        } else {
+          report(a.status, HS_DEV_TIMEOUT);
+        }
+      }
+    }
   } else if (warp == 5) {
     // ---------------- MMA issuer (lane 0) ----------------
     if (lane == 0) {
@@ -2288,23 +2312,49 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
     const int etid = threadIdx.x;  // 0..127
     const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
     constexpr int NV = kDown ? NP : 2 * NP;
+    // A segment's unit parameters and routing weights come from L2 (a round
+    // trip of a microsecond or more while the phase streams): token mode
+    // loads them one segment ahead, while the epilogue waits for the previous
+    // accumulator.
+    struct SegP {
+      int64_t u, us;
+      int nk, k0, k1, cf, cl;
+      UnitInfo ui;
+      float wbv[8];
+    };
+    auto seg_params = [&](int64_t s0, SegP& p) {
+      p.u = sc.unit_of(s0);
+      p.us = sc.ustart(p.u);
+      p.nk = sc.unk(p.u);
+      p.k0 = static_cast<int>(s0 - p.us);
+      p.k1 = static_cast<int>(min64(static_cast<int64_t>(p.nk), s_end - p.us));
+      p.ui = unit_info(d, a, sc, p.u, kDown);
+      p.cf = sc.cta_of(p.us);
+      p.cl = sc.cta_of(p.us + p.nk - 1);
+      if (kTok && (p.cf == p.cl || c == p.cf)) tok_weights(a, p.ui, p.wbv);
+    };
+    SegP nxt;
+    if (kTok && s_begin < s_end) seg_params(s_begin, nxt);
     int seg = 0;
     for (int64_t s = s_begin; s < s_end; ++seg) {
-      const int64_t u = sc.unit_of(s);
-      const int64_t us = sc.ustart(u);
-      const int nk = sc.unk(u);
-      const int k0 = static_cast<int>(s - us);
-      const int k1 = static_cast<int>(min64(static_cast<int64_t>(nk), s_end - us));
-      const UnitInfo ui = unit_info(d, a, sc, u, kDown);
+      SegP cur;
+      if constexpr (kTok)
+        cur = nxt;
+      else
+        seg_params(s, cur);
+      const int64_t s_next = cur.us + cur.k1;
+      if (kTok && s_next < s_end) seg_params(s_next, nxt);
+      const int64_t u = cur.u;
+      const int nk = cur.nk, k0 = cur.k0, k1 = cur.k1;
+      const UnitInfo& ui = cur.ui;
       const int buf = seg & 1;
-      const int cf = sc.cta_of(us);
-      const int cl = sc.cta_of(us + nk - 1);
+      const int cf = cur.cf, cl = cur.cl;
       const bool split = cf != cl;
       const bool finish = !split || c == cf;
       float pre[NV];
-      float wbv[8];
-      if (kTok && finish) tok_weights(a, ui, wbv);
+      const float(&wbv)[8] = cur.wbv;
       if (split && finish) {
+        if (kTok && !kDown && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 7);
         wait_ticket(&a.ucount[u], static_cast<uint32_t>(nk - (k1 - k0)), etid, a.status);
         if (kTok && !kDown && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 0);
         peer_sum<NV>(sc, cf + 1, cl, a.part, kSlot, row, pre);
@@ -2349,16 +2399,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
           if (!kDown) v[n] += pre[NP + n];
         }
       } else if (split) {
-        // publish: slot 2c, then the ticket
+        // publish: slot 2c; the producer warp adds the ticket (above), so the
+        // epilogue goes straight on to its next segment
         float* slot = a.part + 2 * static_cast<int64_t>(c) * kSlot;
 #pragma unroll
         for (int n = 0; n < NP; ++n) {
           __stcg(slot + n * kM + row, g[n]);
           if (!kDown) __stcg(slot + (NP + n) * kM + row, v[n]);
         }
-        __threadfence();
-        epi_bar();
-        if (etid == 0) atomicAdd(&a.ucount[u], static_cast<uint32_t>(k1 - k0));
+        mbar_arrive(&bars->pub);
+        if (kTok && !kDown && threadIdx.x == 0) HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 6);
       }
       if (finish) {
         if constexpr (kTok) {
@@ -2393,7 +2443,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
           }
         }
       }
-      s = us + k1;
+      s = s_next;
     }
     if (kTok && !kDown && threadIdx.x == 0) {
       HS_STAMP(hs_tslot, ::hs::trace::kGateUpTail, c, 2);

@@ -20,7 +20,9 @@ constexpr int kCtas = 296;
 constexpr int kEvents = 8;
 // kGateUpTail (gate/up CTAs): 0 last ticket wait over, 1 last accumulator
 // ready, 2 epilogue done, 3 MMA warp done, 4 last copy issued, 5 the number of
-// epilogue segments (a count, not a time)
+// epilogue segments (a count, not a time), 6 partial rows stored, 7 ticket
+// wait begins; kCombine event 6 (gate/up CTAs): the producer warp added the
+// published segment's ticket
 enum Kernel { kRoute = 0, kGateUp = 1, kDown = 2, kGateUpTail = 3, kCombine = 4 };
 }  // namespace trace
 }  // namespace hs
