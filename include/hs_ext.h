@@ -154,9 +154,8 @@ int hs_moe_ffn_fp4(const void* desc, const void* hidden, const int64_t* topk_idx
 /* hs_moe_ffn_fp4_noalloc: hs_moe_ffn_fp4 without the workspace argument.     */
 /* No counterpart in the reference. It is for callers that cannot allocate    */
 /* device memory at the moment they call: plugin hosts whose enqueue path     */
-/* forbids allocation, code running while a stream is being captured into a  */
-/* CUDA graph (where cudaMalloc is not permitted), and latency-critical loops  */
-/* in which cudaMalloc/cudaFree would synchronise the device. The scratch is  */
+/* forbids allocation, and latency-critical loops in which cudaMalloc or      */
+/* cudaFree would synchronise the device. The scratch is                      */
 /* a fixed array of HS_MOE_NOALLOC_BYTES inside the library; every GPU that   */
 /* loads the library holds it until the process exits. A call whose          */
 /* hs_moe_workspace_size(T, top_k, D, I, I_sh) exceeds it returns             */

@@ -1,8 +1,7 @@
 """hs_moe_ffn_fp4_noalloc: the MoE call for callers that cannot allocate device
 memory when they call (plugin hosts whose enqueue path forbids allocation,
-code running inside a CUDA-graph stream capture where cudaMalloc is not
-permitted, latency-critical loops where cudaMalloc/cudaFree would synchronise
-the device). It uses a fixed scratch array inside the library instead of a
+latency-critical loops where cudaMalloc/cudaFree would synchronise the
+device). It uses a fixed scratch array inside the library instead of a
 caller workspace; this test checks it through the C ABI against the
 workspace-taking hs_moe_ffn_fp4 on two calls in a row. Both entry points run
 the same deterministic kernels (fixed-order reductions, the same schedule),
