@@ -1374,6 +1374,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     }
   }
   __syncthreads();
+  if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, 0, 6);
 
   // ---- CTA 0: the token-mode plan, one thread per (token, slot) pair ----
   // (each thread loads its token's selections at once: no dependent loads)
@@ -1416,6 +1417,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     if (le >= 0) atomicOr(&emask[le >> 5], 1u << (le & 31));
   }
   __syncthreads();
+  if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, 0, 7);
   uint32_t em[8];
 #pragma unroll
   for (int w = 0; w < 8; ++w) em[w] = emask[w];

@@ -23,7 +23,9 @@ import torch
 # (name, kernel, event, CTAs or None = all) of every printed phase
 PHASES = [
     ("route entry", 0, 0, "route"), ("route rows in", 0, 2, "route"), ("route norm done", 0, 3, "route"),
-    ("route keys gathered", 0, 4, "route"), ("route others done", 0, 5, "others"), ("route CTA 0 done", 0, 5, "rank0"),
+    ("route keys gathered", 0, 4, "route"), ("route others done", 0, 5, "others"),
+    ("route CTA 0 top-k done", 0, 6, "rank0"), ("route CTA 0 plan counted", 0, 7, "rank0"),
+    ("route CTA 0 done", 0, 5, "rank0"),
     ("gate/up wait over", 1, 1, None), ("gate/up first TMA", 1, 2, None), ("gate/up first MMA", 1, 3, None),
     ("gate/up first acc", 1, 6, None), ("gate/up last copy issued", 3, 4, None), ("gate/up last MMA", 1, 4, None),
     ("gate/up MMA warp done", 3, 3, None), ("gate/up last ticket", 3, 0, None), ("gate/up peer sums", 1, 7, None),
