@@ -1342,6 +1342,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
     }
     float wsum = 0.f, wsel = 0.f;
     int esel = 0;
+#pragma unroll 1
     for (int r = 0; r < K; ++r) {
       // this lane's best (the lowest id among equal keys), then the warp's
       uint32_t best = 0u;
@@ -1377,39 +1378,32 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_plan_kernel(RouteArgs 
   if (tid == 0) HS_STAMP(hs_tslot, ::hs::trace::kRoute, 0, 6);
 
   // ---- CTA 0: the token-mode plan, one thread per (token, slot) pair ----
-  // (each thread loads its token's selections at once: no dependent loads)
+  // (compact loops: this code runs once per call on one SM, so its
+  // instructions are fetched cold; fewer of them beat unrolled selections)
   const int npairs = T * K;
   int le = -1;
   float ws = 0.f;
   if (tid < npairs) {
     const int t = tid / K, j = tid - t * K;
-    int lv[16];
-#pragma unroll
-    for (int jj = 0; jj < 16; ++jj) {
-      int v = -1;
-      if (jj < K) {
-        const int64_t e = sI[t * K + jj] - A.offset;
-        v = (e < 0 || e >= A.held) ? -1 : static_cast<int>(e);
-      }
-      lv[jj] = v;
-    }
-#pragma unroll
-    for (int jj = 0; jj < 16; ++jj)
-      if (jj == j) le = lv[jj];
+    auto local = [&](int jj) {
+      const int64_t e = sI[t * K + jj] - A.offset;
+      return (e < 0 || e >= A.held) ? -1 : static_cast<int>(e);
+    };
+    le = local(j);
     if (le >= 0) {
       bool dropped = false;
       if (A.dup_mode == HS_DUP_SUM) {  // the first slot of an expert carries the summed weight
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj)
-          if (jj < j && lv[jj] == le) dropped = true;
+#pragma unroll 1
+        for (int jj = 0; jj < j; ++jj)
+          if (local(jj) == le) dropped = true;
         if (!dropped)
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj)
-            if (jj >= j && jj < K && lv[jj] == le) ws += sW[t * K + jj];
+#pragma unroll 1
+          for (int jj = j; jj < K; ++jj)
+            if (local(jj) == le) ws += sW[t * K + jj];
       } else {  // the last slot of an expert wins
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj)
-          if (jj > j && jj < K && lv[jj] == le) dropped = true;
+#pragma unroll 1
+        for (int jj = j + 1; jj < K; ++jj)
+          if (local(jj) == le) dropped = true;
         ws = sW[t * K + j];
       }
       if (dropped) le = -1;
