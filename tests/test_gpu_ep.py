@@ -67,6 +67,45 @@ def test_emulated_two_rank_partials_combine_to_the_single_call(T):
     assert _rel(x2, OM.rms_norm((res.cpu() + out.cpu()), nw.cpu())) <= 2e-2
 
 
+@pytest.mark.parametrize("T", [1, 3])
+def test_emulated_eight_shards_full_shape_combine_to_the_single_call(T):
+    """Eight expert-parallel shards of the full config-0 shape on one GPU:
+    at T = 1 and 3 most shards hold few or none of the tokens' experts, so
+    their gate/up phase is little more than their eighth of the shared
+    expert and runs on fewer stream-K CTAs (at least four steps each). The
+    shards' f32 partials, summed and combined, equal the single call within
+    the MoE tolerance, and the routed sums within f32 association error."""
+    from home_seek_b200 import ops
+    from home_seek_b200.ep import localize, shard_store
+    from home_seek_b200.expert_store import HBMExpertStore
+    dev = torch.device("cuda")
+    full = HBMExpertStore(1, 256, 4096, 2048, 2048, device=dev)
+    full.fill_random(47)
+    g = torch.Generator(device=dev).manual_seed(11 + T)
+    h = (torch.randn(T, 4096, generator=g, device=dev) * 2).to(torch.bfloat16)
+    gate = (torch.randn(256, 4096, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(256, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    idx, w = ops.router_topk(h, gate, bias, 6, 1.5)
+    dup = 1 if T == 1 else 0
+    ref = ops.moe_ffn(full.desc(0), full.dims, h, idx, w, use_shared=True, dup_mode=dup)
+    ref_f32 = torch.empty(T, 4096, dtype=torch.float32, device=dev)
+    ops.moe_ffn(full.desc(0), full.dims, h, idx, w, use_shared=False, dup_mode=dup, out_f32=ref_f32)
+    total = torch.zeros(2, T, 4096, dtype=torch.float32, device=dev)
+    held = []
+    for r in range(8):
+        sh = shard_store(full, r, 8)
+        loc = localize(idx, sh.expert_offset, sh.E_local)
+        held.append(int((loc >= 0).sum()))
+        total += ops.moe_ffn_partials(sh.desc(0), sh.dims, h, loc, w, use_shared=True, dup_mode=dup)
+        del sh
+    out = ops.moe_combine(total)
+    assert ops.check_status(dev) == 0
+    if T == 1:
+        assert min(held) == 0, held  # some shard's phase is the shared slice alone
+    assert _rel(out, ref) <= MOE_TOL, _rel(out, ref)
+    assert _rel(total[0], ref_f32) <= 1e-3, _rel(total[0], ref_f32)
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
