@@ -1507,6 +1507,7 @@ struct Bars {
 };
 
 constexpr int64_t kMinW = 4;  // least weight per CTA of a stream-K phase (above: fewer CTAs)
+constexpr int kFinishNlMaxT = 4;  // token mode: T up to this takes the warmed, non-inlined activation epilogue
 
 // Stream-K schedule over one phase. Units (chunk x 128-row tile) are laid end
 // to end as k-steps, shared-expert units first; a step of an FP8 unit weighs
@@ -1994,6 +1995,61 @@ __device__ __forceinline__ void gateup_finish_tok(const Desc& d, const UnitArgs&
   }
 }
 
+struct F8 {
+  float v[8];
+};
+
+// The same for T <= 4, not inlined, so that every call runs the same
+// instructions: the epilogue warps run it once with dry set (no stores) while
+// the CTA waits for the routing, and the first real call then finds its code
+// in the instruction cache instead of fetching it line by line from L2 on the
+// phase's tail. (At T = 8 the call costs more than the fetch it saves.)
+__device__ __noinline__ void gateup_finish_tok_nl(uint8_t* act8, int64_t act_rows, uint8_t* act_img, int64_t I_act,
+                                                  int T, int fp8, int tile, int chunk, int row, F8 g, F8 u, F8 wbv,
+                                                  int dry) {
+  uint8_t* hi_plane = act8;
+  uint8_t* lo_plane = act8 + act_rows * I_act;
+  const int col = tile * kM + row;
+  const int64_t slot = fp8 ? 0 : 1 + chunk;
+  const int lane = row & 31, blk = row >> 5;
+  uint8_t* img = act_img + (slot * (I_act / kM) + tile) * 256;
+  float av[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    av[r] = 0.f;
+    if (wbv.v[r] != 0.f) {
+      // reference roundings as in gateup_finish
+      const float gf = round_bf16(g.v[r]);
+      const float uf = round_bf16(u.v[r]);
+      const float gc = gf > 10.f ? 10.f : gf;
+      const float uc = uf > 10.f ? 10.f : (uf < -10.f ? -10.f : uf);
+      const float sig = 1.f / (1.f + expf(-gc));
+      av[r] = round_bf16((gc * sig) * uc);
+      if (!fp8) av[r] = round_bf16(av[r] * wbv.v[r]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    if (r >= T) break;  // uniform over the warp
+    // the block's largest magnitude (non-negative float bits order as values)
+    const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(av[r])));
+    const int q = row_prescale(__uint_as_float(mb));
+    const float v = av[r] * exp2i(q);
+    const __nv_fp8_storage_t hb = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw(hb, __NV_E4M3);
+    const float hf = __half2float(*reinterpret_cast<const __half*>(&hr));
+    const __nv_fp8_storage_t lb = __nv_cvt_float_to_fp8(v - hf, __NV_SATFINITE, __NV_E4M3);
+    if (dry) continue;
+    hi_plane[(slot * 8 + r) * I_act + col] = hb;
+    lo_plane[(slot * 8 + r) * I_act + col] = lb;
+    if (lane == r) {
+      const uint8_t sf = static_cast<uint8_t>(127 - q);
+      img[r * 16 + blk] = sf;        // hi row r
+      img[(8 + r) * 16 + blk] = sf;  // lo row r
+    }
+  }
+}
+
 // Persistent stream-K kernel for one phase. kDown = false: gate/up (A boxes =
 // w1 and w3 tiles of one 128-column k-step); kDown = true: down (A boxes = two
 // k-boxes of w2). One CTA per SM: warp 4 streams TMA, warp 5 issues tcgen05
@@ -2072,6 +2128,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
         first += np;
       }
     }
+  }
+  if (kTok && !kDown && warp < 4 && a.T <= kFinishNlMaxT) {  // the activation epilogue's code into the instruction cache
+    F8 z, one;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      z.v[r] = 0.f;
+      one.v[r] = 1.f;
+    }
+    gateup_finish_tok_nl(a.P.act8, a.act_rows, a.P.act_img, d.I, a.T, 0, 0, 0, threadIdx.x, z, z, one, 1);
   }
   // everything above overlaps the previous kernel; from here on the plan (and,
   // for the down phase, the gate/up phase) is complete and visible
@@ -2408,10 +2473,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sk_kernel(const __grid_c
       }
       if (finish) {
         if constexpr (kTok) {
-          if (ui.shared)
+          if (a.T <= kFinishNlMaxT) {
+            F8 gg, vv, ww;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              gg.v[r] = g[r];
+              vv.v[r] = v[r];
+              ww.v[r] = wbv[r];
+            }
+            gateup_finish_tok_nl(a.P.act8, a.act_rows, a.P.act_img, max(d.I, d.has_shared ? d.I_sh : 0), a.T,
+                                 ui.shared, ui.tile, ui.chunk, row, gg, vv, ww, 0);
+          } else if (ui.shared) {
             gateup_finish_tok<true>(d, a, ui, row, g, v, wbv);
-          else
+          } else {
             gateup_finish_tok<false>(d, a, ui, row, g, v, wbv);
+          }
         } else if (!kDown) {
           if (ui.shared)
             gateup_finish<NT, true>(d, a, ui, row, g, v);
